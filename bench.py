@@ -1,0 +1,582 @@
+#!/usr/bin/env python3
+"""BW++ B200 benchmark.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload gemm|attention|attention_causal|rmsnorm_fwd|
+                                rmsnorm_bwd|layernorm_fwd|layernorm_bwd|
+                                reduce_max_fwd|reduce_max_bwd]
+
+Default workload (the headline): fused matmul + bias +
+SiLU, X[8192x4096] bf16 * W[4096x11008] bf16 + b[11008], fp32 out, rows of X
+split over the N ranks (one process per GPU, torchrun), no collective on the
+data path.  The other workloads are BASELINE configs[2] / configs[3] kernels.
+
+One JSON line on rank 0:
+  value         whole-job throughput, inputs resident in HBM, CUDA events on
+                the launching stream around each step, max over ranks
+  e2e           the same metric through the reference-facing C ABI mirror
+                (bwpp_cuda_*_f32 with pinned HOST buffers: host->device copies,
+                the kernel and the device->host copy of the result are timed)
+  roofline      the dominant kernel against MEASURED_PEAKS.json
+  cpu_baseline  the reference's own CPU code (oracle/_ref, built from the
+                reference sources) on a bounded row sample, rank 0 at N=1
+  clocks        NVML samples taken while the timed steps execute
+
+--impl reference times the reference's own CPU implementation on the host
+cores (rank 0 only; other ranks exit 0), same metric / unit / config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (os.path.join(ROOT, "bluewolf-plus-plus_b200"), os.path.join(ROOT, "oracle")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+METRIC = "TFLOP/s (GEMM, attention) & HBM GB/s (norms) per B200 at 1/2/4/8 GPUs"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+L2_FLUSH_BYTES = 256 << 20
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+def profile_traffic(name):
+    """dram bytes per launch recorded in profiles/<name>.md (from an ncu capture)."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def split_rows(total, rank, world):
+    base, rem = divmod(total, world)
+    start = rank * base + min(rank, rem)
+    return start, start + base + (1 if rank < rem else 0)
+
+
+class ClockSampler:
+    """NVML SM clock / throttle-reason samples; poll() while the timed work runs."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+
+    def __init__(self, device):
+        self.samples, self.reasons, self.max_mhz, self.h = [], set(), None, None
+        try:
+            import pynvml as N
+            import torch
+            N.nvmlInit()
+            self.N = N
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            try:
+                self.h = N.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+            except Exception:
+                self.h = N.nvmlDeviceGetHandleByUUID("GPU-" + uuid)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+        except Exception:
+            self.h = None
+        self.last = 0.0
+
+    def poll(self, force=False):
+        if self.h is None:
+            return
+        now = time.perf_counter()
+        if not force and now - self.last < 0.004:
+            return
+        self.last = now
+        N = self.N
+        try:
+            self.samples.append(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
+            try:
+                bits = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except AttributeError:
+                bits = N.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+            for b, name in self.REASONS.items():
+                if bits & b and b != 0x1:
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+
+class Workload:
+    """One step = one pass of the hot path over this rank's shard."""
+    unit = "TFLOP/s"
+    bound = "tensor"
+    dtype = "bf16"
+
+    def __init__(self, rank, world, torch, bwpp, ctx):
+        self.rank, self.world, self.torch, self.bwpp, self.ctx = rank, world, torch, bwpp, ctx
+
+    def work_per_step(self):           # algorithmic FLOP or bytes of this rank per step
+        raise NotImplementedError
+
+    def total_work_per_step(self):     # all ranks
+        raise NotImplementedError
+
+    def scale(self, work, seconds):
+        return work / seconds / (1e12 if self.unit == "TFLOP/s" else 1e9)
+
+
+class GemmWorkload(Workload):
+    """X[8192x4096] W[4096x11008] + b, SiLU, fp32 out."""
+    M, K, N = 8192, 4096, 11008
+    kernel = "gemm_tc_kernel"
+    profile = "gemm_tc_kernel_config2"
+
+    def setup(self):
+        t = self.torch
+        self.r0, self.r1 = split_rows(self.M, self.rank, self.world)
+        self.m = self.r1 - self.r0
+        g = t.Generator(device="cuda").manual_seed(2000)
+        x = t.randn(self.M, self.K, device="cuda", generator=g) * 0.02
+        self.x = x[self.r0:self.r1].to(t.bfloat16).contiguous()
+        del x
+        self.w = (t.randn(self.K, self.N, device="cuda", generator=g) * 0.02).to(t.bfloat16)
+        self.b = t.rand(self.N, device="cuda", generator=g) * 0.2 - 0.1
+        self.c = t.empty(self.m, self.N, device="cuda")
+
+    def step(self):
+        self.ctx.matmul_bf16(self.x, self.w, self.c, self.m, self.N, self.K, self.K, self.N, self.N,
+                             self.b, 1, 1)
+        return 1
+
+    def work_per_step(self):
+        return 2.0 * self.m * self.N * self.K
+
+    def total_work_per_step(self):
+        return 2.0 * self.M * self.N * self.K
+
+    def config(self):
+        return {"workload": "fused matmul+bias+SiLU (BASELINE configs[1], examples/matmul_add_silu)",
+                "M": self.M, "K": self.K, "N": self.N, "rows_per_gpu": self.m,
+                "inputs": "X,W ~ N(0,0.02) bf16, b ~ U(-0.1,0.1) fp32, out fp32",
+                "parallelism": f"rows of X over {self.world} GPU(s), W replicated, no collective",
+                "l2": "256 MiB written between timed steps (flush)"}
+
+    # e2e through the CPU-signature mirror with pinned host buffers
+    def setup_e2e(self):
+        t = self.torch
+        self.ha = self.x.float().cpu().pin_memory()
+        self.hb = self.w.float().cpu().pin_memory()
+        self.hbias = self.b.cpu().pin_memory()
+        self.hc = t.empty(self.m, self.N, dtype=t.float32).pin_memory()
+        self.h2d = (self.m * self.K + self.K * self.N + self.N) * 4
+        self.d2h = self.m * self.N * 4
+
+    def step_e2e(self):
+        self.bwpp.matmul_f32(self.ha, self.hb, self.hc, self.m, self.N, self.K, self.K, self.N, self.N,
+                             self.hbias, 1, 1)
+
+    # reference CPU code on a bounded row sample
+    def cpu_sample(self, lib, threads):
+        import oracle as O
+        rows = max(threads, 4)
+        if not hasattr(self, "cpu_a"):
+            rng = np.random.default_rng(2000)
+            self.cpu_a = (0.02 * rng.standard_normal((rows, self.K))).astype(np.float32)
+            self.cpu_b = (0.02 * rng.standard_normal((self.K, self.N))).astype(np.float32)
+            self.cpu_bias = rng.uniform(-0.1, 0.1, self.N).astype(np.float32)
+            self.cpu_c = np.zeros((rows, self.N), np.float32)
+        t0 = time.perf_counter()
+        O.run_rows_threaded(lambda r0, r1: O.ref_matmul_rows(lib, self.cpu_a, self.cpu_b, self.cpu_c,
+                                                             self.cpu_bias, 1, 1, r0, r1), rows, threads)
+        dt = time.perf_counter() - t0
+        return 2.0 * rows * self.N * self.K, dt, f"{rows} of 8192 rows x all 11008 columns, K=4096, fp32, row-split over {threads} threads"
+
+
+class AttentionWorkload(Workload):
+    """B=8 H=32 S=4096 d=128, bf16 in, fp32 out; heads over ranks."""
+    B, H, S, D = 8, 32, 4096, 128
+    kernel = "attention"
+    profile = "attention_config4"
+
+    def __init__(self, *a, causal=False):
+        super().__init__(*a)
+        self.causal = causal
+
+    def setup(self):
+        t = self.torch
+        self.h0, self.h1 = split_rows(self.B * self.H, self.rank, self.world)
+        self.nh = self.h1 - self.h0
+        g = t.Generator(device="cuda").manual_seed(4000 + self.h0)
+        self.q, self.k, self.v = (t.randn(self.nh, self.S, self.D, device="cuda", generator=g).to(t.bfloat16)
+                                  for _ in range(3))
+        self.o = t.empty(self.nh, self.S, self.D, device="cuda")
+
+    def step(self):
+        self.ctx.attention_bf16(self.q, self.k, self.v, self.o, 1, self.nh, self.S, self.S, self.D,
+                                self.D ** -0.5, int(self.causal))
+        return 1
+
+    def flops_per_head(self):
+        S, D = self.S, self.D
+        return 4.0 * D * S * (S + 1) / 2 if self.causal else 4.0 * S * S * D
+
+    def work_per_step(self):
+        return self.nh * self.flops_per_head()
+
+    def total_work_per_step(self):
+        return self.B * self.H * self.flops_per_head()
+
+    def config(self):
+        return {"workload": f"attention {'causal' if self.causal else 'non-causal'} (BASELINE configs[3])",
+                "B": self.B, "H": self.H, "S": self.S, "D": self.D, "heads_per_gpu": self.nh,
+                "parallelism": f"batch x head over {self.world} GPU(s), no collective",
+                "l2": "256 MiB written between timed steps (flush)"}
+
+    def setup_e2e(self):
+        self.hq, self.hk, self.hv = (t.float().cpu().pin_memory() for t in (self.q, self.k, self.v))
+        self.ho = self.torch.empty(self.nh, self.S, self.D).pin_memory()
+        self.h2d = 3 * self.nh * self.S * self.D * 4
+        self.d2h = self.nh * self.S * self.D * 4
+
+    def step_e2e(self):
+        if self.causal:
+            raise NotImplementedError
+        for h in range(self.nh):  # the reference's 2-D entry point is one head at a time
+            self.bwpp.attention_f32(self.hq[h], self.hk[h], self.hv[h], self.ho[h], self.S, self.S,
+                                    self.D, self.D, self.D, self.D, self.D, self.D)
+
+    def cpu_sample(self, lib, threads):
+        import oracle as O
+        rows = max(threads, 4)
+        rng = np.random.default_rng(4000)
+        q = rng.standard_normal((rows, self.D)).astype(np.float32) * np.float32(self.D ** -0.5)
+        k = rng.standard_normal((self.S, self.D)).astype(np.float32)
+        v = rng.standard_normal((self.S, self.D)).astype(np.float32)
+        o = np.zeros((rows, self.D), np.float32)
+        import ctypes as C
+        fp = C.POINTER(C.c_float)
+
+        def part(r0, r1):
+            for r in range(r0, r1):
+                n = (r * (self.S // rows) + 1) if self.causal else self.S
+                lib.attention_f32(C.cast(C.c_void_p(q.ctypes.data + r * self.D * 4), fp),
+                                  k.ctypes.data_as(fp), v.ctypes.data_as(fp),
+                                  C.cast(C.c_void_p(o.ctypes.data + r * self.D * 4), fp),
+                                  1, n, self.D, self.D, self.D, self.D, self.D, self.D)
+        t0 = time.perf_counter()
+        O.run_rows_threaded(part, rows, threads)
+        dt = time.perf_counter() - t0
+        flops = sum(4.0 * self.D * ((r * (self.S // rows) + 1) if self.causal else self.S) for r in range(rows))
+        return flops, dt, f"{rows} query rows of one (b,h), S={self.S}, d={self.D}, fp32, {threads} threads"
+
+
+class RowWorkload(Workload):
+    """x[65536x4096] fp32, rows over ranks."""
+    R, Cc = 65536, 4096
+    unit = "GB/s"
+    bound = "hbm"
+    dtype = "f32"
+
+    def __init__(self, *a, op="rmsnorm_fwd"):
+        super().__init__(*a)
+        self.op = op
+        self.kernel = op
+        self.profile = f"{op}_config3"
+
+    def setup(self):
+        t = self.torch
+        self.r0, self.r1 = split_rows(self.R, self.rank, self.world)
+        self.m = self.r1 - self.r0
+        g = t.Generator(device="cuda").manual_seed(3000 + self.r0)
+        self.x = t.randn(self.m, self.Cc, device="cuda", generator=g)
+        self.dy = t.randn(self.m, self.Cc, device="cuda", generator=g)
+        self.g = 1 + 0.1 * t.randn(self.Cc, device="cuda", generator=g)
+        self.bt = 0.1 * t.randn(self.Cc, device="cuda", generator=g)
+        self.y = t.empty_like(self.x)
+        self.dg = t.empty(self.Cc, device="cuda")
+        self.db = t.empty(self.Cc, device="cuda")
+        self.mx = t.empty(self.m, device="cuda")
+        self.am = t.zeros(self.m, dtype=t.int32, device="cuda")
+        self.dyr = self.dy[:, 0].contiguous()
+        if self.op == "reduce_max_bwd":
+            self.ctx.reduce_max_fwd(self.x, self.mx, self.am, self.m, self.Cc, self.Cc)
+
+    def step(self):
+        c, m, C_ = self.ctx, self.m, self.Cc
+        if self.op == "rmsnorm_fwd":
+            c.rmsnorm_fwd(self.x, self.y, self.g, self.bt, m, C_, C_, 1e-5); return 1
+        if self.op == "layernorm_fwd":
+            c.layernorm_fwd(self.x, self.y, self.g, self.bt, m, C_, C_, 1e-5); return 1
+        if self.op == "rmsnorm_bwd":
+            c.rmsnorm_bwd(self.x, self.g, self.dy, self.y, self.dg, self.db, m, C_, C_, 1e-5); return 3
+        if self.op == "layernorm_bwd":
+            c.layernorm_bwd(self.x, self.g, self.dy, self.y, self.dg, self.db, m, C_, C_, 1e-5); return 3
+        if self.op == "reduce_max_fwd":
+            c.reduce_max_fwd(self.x, self.mx, self.am, m, C_, C_); return 1
+        if self.op == "reduce_max_bwd":
+            c.reduce_max_bwd(self.am, self.dyr, self.y, m, C_, C_); return 1
+        raise ValueError(self.op)
+
+    def bytes_for(self, rows):
+        n = rows * self.Cc * 4
+        return {"rmsnorm_fwd": 2 * n, "layernorm_fwd": 2 * n, "rmsnorm_bwd": 3 * n,
+                "layernorm_bwd": 3 * n, "reduce_max_fwd": n + 8 * rows,
+                "reduce_max_bwd": n + 8 * rows}[self.op]
+
+    def work_per_step(self):
+        return float(self.bytes_for(self.m))
+
+    def total_work_per_step(self):
+        return float(self.bytes_for(self.R))
+
+    def config(self):
+        return {"workload": f"{self.op} (BASELINE configs[2], examples/norms)", "rows": self.R,
+                "cols": self.Cc, "rows_per_gpu": self.m, "eps": 1e-5,
+                "parallelism": f"rows over {self.world} GPU(s), no collective",
+                "l2": "inputs (>= 1 GiB) larger than L2 and 256 MiB flush between steps"}
+
+    def setup_e2e(self):
+        self.hx = self.x.cpu().pin_memory()
+        self.hy = self.torch.empty_like(self.hx).pin_memory()
+        self.hg, self.hbt = self.g.cpu().pin_memory(), self.bt.cpu().pin_memory()
+        self.h2d = (self.m * self.Cc + 2 * self.Cc) * 4
+        self.d2h = self.m * self.Cc * 4
+
+    def step_e2e(self):
+        if self.op != "rmsnorm_fwd":
+            raise NotImplementedError
+        self.bwpp.rmsnorm_f32(self.hx, self.hy, self.hg, self.hbt, self.m, self.Cc, self.Cc, 1e-5)
+
+    def cpu_sample(self, lib, threads):
+        import oracle as O
+        if self.op != "rmsnorm_fwd":
+            return None
+        rows = 4096
+        rng = np.random.default_rng(3000)
+        x = rng.standard_normal((rows, self.Cc), dtype=np.float32)
+        y = np.zeros_like(x)
+        g = (1 + 0.1 * rng.standard_normal(self.Cc)).astype(np.float32)
+        import ctypes as C
+        fp = C.POINTER(C.c_float)
+
+        def part(r0, r1):
+            lib.rmsnorm_f32(C.cast(C.c_void_p(x.ctypes.data + r0 * self.Cc * 4), fp),
+                            C.cast(C.c_void_p(y.ctypes.data + r0 * self.Cc * 4), fp),
+                            g.ctypes.data_as(fp), None, r1 - r0, self.Cc, self.Cc, 1e-5)
+        t0 = time.perf_counter()
+        O.run_rows_threaded(part, rows, threads)
+        dt = time.perf_counter() - t0
+        return 2.0 * rows * self.Cc * 4, dt, f"{rows} of 65536 rows, fp32, {threads} threads"
+
+
+def make_workload(name, *a):
+    if name == "gemm":
+        return GemmWorkload(*a)
+    if name in ("attention", "attention_causal"):
+        return AttentionWorkload(*a, causal=name.endswith("causal"))
+    return RowWorkload(*a, op=name)
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's own CPU code on the host cores
+# ---------------------------------------------------------------------------
+
+def run_reference(args, world):
+    import oracle as O
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    lib = O.ref_lib()
+    kind = "reference"
+    if lib is None:
+        lib, kind = O.oracle_lib(), "port"
+    threads = O.cpu_threads()
+    wl = make_workload(args.workload, 0, 1, None, None, None)
+    for _ in range(args.warmup):
+        wl.cpu_sample(lib, threads)
+    work, secs = 0.0, 0.0
+    sample = ""
+    for _ in range(args.steps):
+        w, dt, sample = wl.cpu_sample(lib, threads)
+        work += w
+        secs += dt
+    value = wl.scale(work, secs)
+    cfg = {"workload": args.workload}
+    line = {"metric": METRIC, "value": value, "unit": wl.unit, "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / max(args.steps, 1),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded), fp32 copies of the benchmark inputs", "config": cfg,
+            "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="gemm")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        run_reference(args, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import bwpp
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    ctx = bwpp.Ctx(local)
+    wl = make_workload(args.workload, rank, world, torch, bwpp, ctx)
+    wl.setup()
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    for _ in range(max(args.warmup, 0)):
+        wl.step()
+    ctx.sync()
+
+    # ---- timed region: K steps, events around each step on the launch stream
+    clocks = ClockSampler(local)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches = 0
+    barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        starts[i].record(stream)
+        launches += wl.step()
+        ends[i].record(stream)
+        clocks.poll()
+    while not ends[-1].query():
+        clocks.poll()
+        time.sleep(0.001)
+    torch.cuda.synchronize()
+    clocks.poll(force=True)
+    barrier()
+    wall = time.perf_counter() - wall0
+    ctx.sync()
+    per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    dev_s = torch.tensor([sum(per_step_ms) / 1e3], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(dev_s, op=dist.ReduceOp.MAX)
+    total_s = float(dev_s.item())
+    value = wl.scale(wl.total_work_per_step() * args.steps, total_s)
+    ms_per_step = 1e3 * total_s / args.steps
+    my_launch_s = sum(per_step_ms) / 1e3 / args.steps
+
+    # ---- roofline of the dominant kernel (this rank's launches)
+    hbm, tflops, tflops_sus, src = peaks()
+    achieved = wl.scale(wl.work_per_step(), my_launch_s)
+    peak = tflops if wl.unit == "TFLOP/s" else hbm
+    # ncu dram bytes of one full-size (N = 1) launch, scaled to this rank's share
+    traffic = profile_traffic(wl.profile)
+    if traffic is not None:
+        traffic = traffic * wl.work_per_step() / wl.total_work_per_step()
+    roofline = {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": wl.unit,
+                "frac": achieved / peak, "traffic": traffic, "peak_source": f"{src} (MEASURED_PEAKS.json)"
+                if src == "measured" else "fallback", "kernel": wl.kernel}
+
+    # ---- e2e through the C ABI mirror with host buffers
+    e2e = None
+    if not args.no_e2e:
+        try:
+            wl.setup_e2e()
+            for _ in range(max(1, min(args.warmup, 2))):
+                wl.step_e2e()
+            n_e2e = max(3, min(args.steps, 10))
+            barrier()
+            t0 = time.perf_counter()
+            for _ in range(n_e2e):
+                wl.step_e2e()
+            dt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device="cuda")
+            if world > 1:
+                dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+            e2e = {"value": wl.scale(wl.total_work_per_step() * n_e2e, float(dt.item())), "unit": wl.unit,
+                   "h2d_bytes_per_step": int(wl.h2d), "d2h_bytes_per_step": int(wl.d2h), "steps": n_e2e,
+                   "api": "bwpp_cuda_*_f32 CPU-signature mirror, pinned host buffers"}
+        except NotImplementedError:
+            e2e = None
+
+    # ---- CPU baseline: the reference's own code on this host (rank 0, N = 1)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        import oracle as O
+        lib, kind = O.ref_lib(), "reference"
+        if lib is None:
+            lib, kind = O.oracle_lib(), "port"
+        threads = O.cpu_threads()
+        r = wl.cpu_sample(lib, threads)
+        if r is not None:
+            w, dt, sample = r
+            cpu = {"value": wl.scale(w, dt), "unit": wl.unit, "cores": threads, "kind": kind,
+                   "sample": sample, "seconds": dt}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype,
+                "data": "synthetic (seeded torch generators), shapes and distributions of the BASELINE config",
+                "config": wl.config(), "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": launches, "clocks": clocks.summary(), "wall_s_timed_region": wall}
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,277 @@
+"""Python view of the BW++ B200 runtime (lib/libbwpp_cuda.so) through its C ABI.
+
+This module is a thin ctypes layer over include/bwpp_cuda.h, used by the test
+suite, bench.py and __graft_entry__.  It adds no compute of its own: every op
+below is one call into the CUDA library, and importing it fails loudly when the
+library has not been built (there is no CPU fallback).
+
+Argument order and meaning follow the reference's runtime/cpu/bwpp_cpu_ref.h
+and runtime/metal/dispatch_stub.h (see the C header for citations).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+PKG_ROOT = os.path.dirname(_HERE)
+REPO_ROOT = os.path.dirname(PKG_ROOT)
+LIB_PATH = os.path.join(PKG_ROOT, "lib", "libbwpp_cuda.so")
+HEADER_PATH = os.path.join(REPO_ROOT, "include", "bwpp_cuda.h")
+
+OK = 0
+ERR = 1
+ERR_ARG = 2
+ERR_CUDA = 3
+ERR_TIMEOUT = 4
+ERR_NOMEM = 5
+ERR_UNSUPPORTED = 6
+
+_u32, _u64, _i32, _f32, _vp, _sz = C.c_uint32, C.c_uint64, C.c_int, C.c_float, C.c_void_p, C.c_size_t
+_cp = C.c_char_p
+
+
+class BwppError(RuntimeError):
+    def __init__(self, status, message=""):
+        super().__init__(f"bwpp status {status}: {message}")
+        self.status = status
+
+
+class MatmulParams(C.Structure):
+    _fields_ = [(n, _u32) for n in ("M", "N", "K", "lda", "ldb", "ldc")]
+
+
+class SoftmaxParams(C.Structure):
+    _fields_ = [(n, _u32) for n in ("rows", "cols", "ld")]
+
+
+class RmsnormParams(C.Structure):
+    _fields_ = [("rows", _u32), ("cols", _u32), ("ld", _u32), ("eps", _f32)]
+
+
+class AttentionParams(C.Structure):
+    _fields_ = [(n, _u32) for n in ("M", "N", "K", "D", "ldq", "ldk", "ldv", "ldo")]
+
+
+class Arena(C.Structure):
+    _fields_ = [("buffer", _vp), ("capacity", _sz), ("offset", _sz)]
+
+
+# name -> (restype, argtypes)
+_SIGS = {
+    "bwpp_cuda_arena_init": (_i32, [C.POINTER(Arena), _sz, _i32]),
+    "bwpp_cuda_arena_alloc": (_vp, [C.POINTER(Arena), _sz, _sz]),
+    "bwpp_cuda_arena_reset": (None, [C.POINTER(Arena)]),
+    "bwpp_cuda_arena_destroy": (None, [C.POINTER(Arena)]),
+    "bwpp_cuda_ctx_create": (_i32, [C.POINTER(_vp), _i32, _vp]),
+    "bwpp_cuda_ctx_destroy": (_i32, [_vp]),
+    "bwpp_cuda_ctx_set_stream": (_i32, [_vp, _vp]),
+    "bwpp_cuda_ctx_set_workspace": (_i32, [_vp, _vp, _sz]),
+    "bwpp_cuda_norm_bwd_workspace_size": (_sz, [_vp, _u32, _u32]),
+    "bwpp_cuda_sync": (_i32, [_vp]),
+    "bwpp_cuda_status_string": (_cp, [_i32]),
+    "bwpp_cuda_ctx_last_error": (_cp, [_vp]),
+    "bwpp_cuda_device_count": (_i32, []),
+    "bwpp_cuda_selftest_wait_timeout": (_i32, [_vp, _u32]),
+    "bwpp_cuda_matmul_bf16": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _i32, _i32]),
+    "bwpp_cuda_attention_bf16": (_i32, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _i32]),
+    "bwpp_cuda_rmsnorm_fwd_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
+    "bwpp_cuda_rmsnorm_bwd_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
+    "bwpp_cuda_layernorm_fwd_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
+    "bwpp_cuda_layernorm_bwd_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
+    "bwpp_cuda_reduce_max_fwd_f32": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32]),
+    "bwpp_cuda_reduce_max_bwd_f32": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32]),
+    "bwpp_cuda_reduce_max_mask_ex": (_i32, [_vp, _vp, _vp, _u32, _u32, _i32]),
+    "bwpp_cuda_reduce_max_grad_ex": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _i32]),
+    "bwpp_cuda_softmax_fwd_f32": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32]),
+    "bwpp_cuda_cast_f32_bf16": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32]),
+    "bwpp_cuda_matmul_f32": (None, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _i32, _i32]),
+    "bwpp_cuda_softmax_f32": (None, [_vp, _vp, _u32, _u32, _u32]),
+    "bwpp_cuda_rmsnorm_f32": (None, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
+    "bwpp_cuda_attention_f32": (None, [_vp, _vp, _vp, _vp] + [_u32] * 8),
+    "bwpp_cuda_reduce_max_mask_f32": (None, [_vp, _vp, _u32, _u32, _i32]),
+    "bwpp_cuda_reduce_max_grad_f32": (None, [_vp, _vp, _vp, _u32, _u32, _i32]),
+    "bwpp_cuda_last_status": (_i32, []),
+    "bwpp_cuda_dispatch_matmul": (_i32, [_vp, _vp, _vp, _vp, _vp, MatmulParams, _cp]),
+    "bwpp_cuda_dispatch_softmax": (_i32, [_vp, _vp, _vp, SoftmaxParams, _cp]),
+    "bwpp_cuda_dispatch_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _vp, RmsnormParams, _cp]),
+    "bwpp_cuda_dispatch_attention": (_i32, [_vp, _vp, _vp, _vp, _vp, AttentionParams, _cp]),
+}
+
+_lib = None
+
+
+def header_symbols(path: str = HEADER_PATH) -> list[str]:
+    """Function names declared in include/bwpp_cuda.h."""
+    text = open(path).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(bwpp_cuda_\w+)\s*\(", text)))
+
+
+def load(path: str = LIB_PATH) -> C.CDLL:
+    """Loads the CUDA runtime library; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(
+            f"{path} is missing: build it with `make -C bluewolf-plus-plus_b200` "
+            "(or __graft_entry__.build()); there is no CPU fallback")
+    lib = C.CDLL(path)
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def status_string(status: int) -> str:
+    return load().bwpp_cuda_status_string(status).decode()
+
+
+def _ptr(t):
+    """Device / host address of a torch tensor, numpy array or int (None -> NULL)."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if hasattr(t, "data_ptr"):
+        return t.data_ptr()
+    if hasattr(t, "ctypes"):
+        return t.ctypes.data
+    raise TypeError(type(t))
+
+
+class Ctx:
+    """A BwppCudaCtx bound to one device and stream (torch's current stream by default)."""
+
+    def __init__(self, device: int = 0, stream=None):
+        self.lib = load()
+        if stream is None:
+            import torch
+            stream = torch.cuda.current_stream(device).cuda_stream
+        handle = C.c_void_p()
+        rc = self.lib.bwpp_cuda_ctx_create(C.byref(handle), device, stream)
+        if rc != OK:
+            raise BwppError(rc, f"ctx_create(device={device}) failed: {status_string(rc)}")
+        self.handle = handle
+        self.device = device
+
+    def close(self):
+        if self.handle:
+            self.lib.bwpp_cuda_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, rc: int, what: str = ""):
+        if rc != OK:
+            msg = self.lib.bwpp_cuda_ctx_last_error(self.handle).decode()
+            raise BwppError(rc, f"{what}: {msg}")
+
+    def sync(self):
+        self.check(self.lib.bwpp_cuda_sync(self.handle), "sync")
+
+    def set_stream(self, stream):
+        self.check(self.lib.bwpp_cuda_ctx_set_stream(self.handle, stream), "set_stream")
+
+    def set_workspace(self, ptr, nbytes):
+        self.check(self.lib.bwpp_cuda_ctx_set_workspace(self.handle, _ptr(ptr), nbytes), "set_workspace")
+
+    # ---- ops (device tensors) -----------------------------------------
+    def matmul_bf16(self, a, b, c, M, N, K, lda, ldb, ldc, bias=None, silu=0, add=0):
+        self.check(self.lib.bwpp_cuda_matmul_bf16(self.handle, _ptr(a), _ptr(b), _ptr(c), M, N, K,
+                                                  lda, ldb, ldc, _ptr(bias), int(silu), int(add)),
+                   "matmul_bf16")
+
+    def attention_bf16(self, q, k, v, o, B, H, Sq, Skv, D, scale, causal):
+        self.check(self.lib.bwpp_cuda_attention_bf16(self.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(o),
+                                                     B, H, Sq, Skv, D, float(scale), int(causal)),
+                   "attention_bf16")
+
+    def rmsnorm_fwd(self, x, y, gamma, beta, rows, cols, ld, eps):
+        self.check(self.lib.bwpp_cuda_rmsnorm_fwd_f32(self.handle, _ptr(x), _ptr(y), _ptr(gamma),
+                                                      _ptr(beta), rows, cols, ld, eps), "rmsnorm_fwd")
+
+    def layernorm_fwd(self, x, y, gamma, beta, rows, cols, ld, eps):
+        self.check(self.lib.bwpp_cuda_layernorm_fwd_f32(self.handle, _ptr(x), _ptr(y), _ptr(gamma),
+                                                        _ptr(beta), rows, cols, ld, eps), "layernorm_fwd")
+
+    def rmsnorm_bwd(self, x, gamma, dy, dx, dgamma, dbeta, rows, cols, ld, eps):
+        self.check(self.lib.bwpp_cuda_rmsnorm_bwd_f32(self.handle, _ptr(x), _ptr(gamma), _ptr(dy), _ptr(dx),
+                                                      _ptr(dgamma), _ptr(dbeta), rows, cols, ld, eps),
+                   "rmsnorm_bwd")
+
+    def layernorm_bwd(self, x, gamma, dy, dx, dgamma, dbeta, rows, cols, ld, eps):
+        self.check(self.lib.bwpp_cuda_layernorm_bwd_f32(self.handle, _ptr(x), _ptr(gamma), _ptr(dy), _ptr(dx),
+                                                        _ptr(dgamma), _ptr(dbeta), rows, cols, ld, eps),
+                   "layernorm_bwd")
+
+    def reduce_max_fwd(self, x, maxv, argmax, rows, cols, ld):
+        self.check(self.lib.bwpp_cuda_reduce_max_fwd_f32(self.handle, _ptr(x), _ptr(maxv), _ptr(argmax),
+                                                         rows, cols, ld), "reduce_max_fwd")
+
+    def reduce_max_bwd(self, argmax, dy, dx, rows, cols, ld):
+        self.check(self.lib.bwpp_cuda_reduce_max_bwd_f32(self.handle, _ptr(argmax), _ptr(dy), _ptr(dx),
+                                                         rows, cols, ld), "reduce_max_bwd")
+
+    def reduce_max_mask(self, x, mask, rows, cols, axis):
+        self.check(self.lib.bwpp_cuda_reduce_max_mask_ex(self.handle, _ptr(x), _ptr(mask), rows, cols, axis),
+                   "reduce_max_mask")
+
+    def reduce_max_grad(self, mask, dy, dx, rows, cols, axis):
+        self.check(self.lib.bwpp_cuda_reduce_max_grad_ex(self.handle, _ptr(mask), _ptr(dy), _ptr(dx),
+                                                         rows, cols, axis), "reduce_max_grad")
+
+    def softmax_fwd(self, x, y, rows, cols, ld):
+        self.check(self.lib.bwpp_cuda_softmax_fwd_f32(self.handle, _ptr(x), _ptr(y), rows, cols, ld),
+                   "softmax_fwd")
+
+    def cast_f32_bf16(self, src, dst, rows, cols, ld_src):
+        self.check(self.lib.bwpp_cuda_cast_f32_bf16(self.handle, _ptr(src), _ptr(dst), rows, cols, ld_src),
+                   "cast_f32_bf16")
+
+
+# ---- CPU-signature mirrors (host or device pointers, synchronous) ---------
+
+def _mirror_check(what):
+    rc = load().bwpp_cuda_last_status()
+    if rc != OK:
+        raise BwppError(rc, f"{what}: {status_string(rc)}")
+
+
+def matmul_f32(a, b, c, M, N, K, lda, ldb, ldc, bias, apply_silu, apply_bias):
+    load().bwpp_cuda_matmul_f32(_ptr(a), _ptr(b), _ptr(c), M, N, K, lda, ldb, ldc, _ptr(bias),
+                                int(apply_silu), int(apply_bias))
+    _mirror_check("bwpp_cuda_matmul_f32")
+
+
+def softmax_f32(x, y, rows, cols, ld):
+    load().bwpp_cuda_softmax_f32(_ptr(x), _ptr(y), rows, cols, ld)
+    _mirror_check("bwpp_cuda_softmax_f32")
+
+
+def rmsnorm_f32(x, y, gamma, beta, rows, cols, ld, eps):
+    load().bwpp_cuda_rmsnorm_f32(_ptr(x), _ptr(y), _ptr(gamma), _ptr(beta), rows, cols, ld, eps)
+    _mirror_check("bwpp_cuda_rmsnorm_f32")
+
+
+def attention_f32(q, k, v, o, M, N, K, D, ldq, ldk, ldv, ldo):
+    load().bwpp_cuda_attention_f32(_ptr(q), _ptr(k), _ptr(v), _ptr(o), M, N, K, D, ldq, ldk, ldv, ldo)
+    _mirror_check("bwpp_cuda_attention_f32")
+
+
+def reduce_max_mask_f32(x, mask, rows, cols, axis):
+    load().bwpp_cuda_reduce_max_mask_f32(_ptr(x), _ptr(mask), rows, cols, axis)
+    _mirror_check("bwpp_cuda_reduce_max_mask_f32")
+
+
+def reduce_max_grad_f32(mask, dy, dx, rows, cols, axis):
+    load().bwpp_cuda_reduce_max_grad_f32(_ptr(mask), _ptr(dy), _ptr(dx), rows, cols, axis)
+    _mirror_check("bwpp_cuda_reduce_max_grad_f32")

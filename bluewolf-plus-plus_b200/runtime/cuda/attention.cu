@@ -1,0 +1,40 @@
+// Attention entry point: O = softmax(scale * Q K^T [causal]) V on [B,H,S,D].
+#include "bwpp_cuda_internal.cuh"
+
+int bwpp_attention_simt_launch(BwppCudaCtx *ctx, const uint16_t *q,
+                               const uint16_t *k, const uint16_t *v, float *o,
+                               uint32_t BH, uint32_t Sq, uint32_t Skv,
+                               uint32_t Kd, uint32_t Dv, uint64_t q_bh,
+                               uint64_t k_bh, uint64_t v_bh, uint64_t o_bh,
+                               uint32_t ldq, uint32_t ldk, uint32_t ldv,
+                               uint32_t ldo, float scale, int causal);
+
+// Chooses the kernel for a batch of BH independent (Sq x Kd, Skv x Kd,
+// Skv x Dv) problems with the given strides.
+int bwpp_attention_launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                          const uint16_t *v, float *o, uint32_t BH, uint32_t Sq,
+                          uint32_t Skv, uint32_t Kd, uint32_t Dv, uint64_t q_bh,
+                          uint64_t k_bh, uint64_t v_bh, uint64_t o_bh,
+                          uint32_t ldq, uint32_t ldk, uint32_t ldv, uint32_t ldo,
+                          float scale, int causal) {
+  return bwpp_attention_simt_launch(ctx, q, k, v, o, BH, Sq, Skv, Kd, Dv, q_bh,
+                                    k_bh, v_bh, o_bh, ldq, ldk, ldv, ldo, scale,
+                                    causal);
+}
+
+extern "C" int bwpp_cuda_attention_bf16(BwppCudaCtx *ctx, const uint16_t *q,
+                                        const uint16_t *k, const uint16_t *v,
+                                        float *o, uint32_t B, uint32_t H,
+                                        uint32_t Sq, uint32_t Skv, uint32_t D,
+                                        float scale, int causal) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (!q || !k || !v || !o) return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "attention: NULL buffer");
+  const uint64_t BH = (uint64_t)B * H;
+  if (BH == 0 || Sq == 0 || D == 0) return BWPP_CUDA_OK;
+  if (BH > 0xFFFFFFFFull) return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "attention: B*H too large");
+  return bwpp_attention_launch(ctx, q, k, v, o, (uint32_t)BH, Sq, Skv, D, D,
+                               (uint64_t)Sq * D, (uint64_t)Skv * D,
+                               (uint64_t)Skv * D, (uint64_t)Sq * D, D, D, D, D,
+                               scale, causal);
+}

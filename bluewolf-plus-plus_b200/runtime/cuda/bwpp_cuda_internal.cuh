@@ -1,0 +1,329 @@
+// Internal helpers of the BW++ CUDA runtime (sm_100a only).
+//
+//  * BwppCudaCtx: device, stream, device status word, workspace.
+//  * Bounded device waits: every spin in a kernel gives up after
+//    BWPP_WAIT_LIMIT_NS of %globaltimer, records BWPP_CUDA_ERR_TIMEOUT in the
+//    ctx's status word and lets the kernel unwind; nothing traps.
+//  * Thin inline-PTX wrappers for mbarrier, TMA (cp.async.bulk.tensor, no
+//    multicast anywhere) and tcgen05 (alloc / mma / commit / ld).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "bwpp_cuda.h"
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+struct BwppCudaCtx {
+  int device;
+  cudaStream_t stream;
+  int *status_word;        // device int, 0 = ok, else a BWPP_CUDA_ERR_* code
+  void *workspace;         // device scratch (owned unless user_workspace)
+  size_t workspace_bytes;
+  int user_workspace;      // 1: set by bwpp_cuda_ctx_set_workspace, not freed
+  int num_sms;
+  char last_error[256];
+};
+
+// Records a message in ctx->last_error (if ctx) and returns `code`.
+int bwpp_set_error(BwppCudaCtx *ctx, int code, const char *fmt, ...);
+
+// Checks a CUDA runtime return code; on failure records it and returns
+// BWPP_CUDA_ERR_CUDA.
+int bwpp_check_cuda(BwppCudaCtx *ctx, cudaError_t err, const char *what);
+
+// Makes ctx's device current; returns BWPP_CUDA_OK or an error.
+int bwpp_ctx_enter(BwppCudaCtx *ctx);
+
+// Returns a device pointer to at least `bytes` of scratch owned by ctx,
+// growing the ctx-owned buffer if needed (a user-provided workspace is never
+// grown: a too-small one is an error).  NULL on failure (error recorded).
+void *bwpp_ctx_workspace(BwppCudaCtx *ctx, size_t bytes);
+
+// Launch-error check after a kernel launch.
+#define BWPP_LAUNCH_CHECK(ctx, name)                                        \
+  do {                                                                     \
+    cudaError_t e_ = cudaGetLastError();                                   \
+    if (e_ != cudaSuccess) return bwpp_check_cuda((ctx), e_, (name));      \
+  } while (0)
+
+// TMA descriptor encoding through the driver entry point (no -lcuda link).
+typedef CUresult (*bwpp_encode_tiled_fn)(
+    CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+    CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+    CUtensorMapFloatOOBfill);
+bwpp_encode_tiled_fn bwpp_get_encode_tiled(void);
+
+// 2-D tensor map: dims {inner, outer}, row pitch in bytes, box {bi, bo}.
+int bwpp_make_tmap_2d(BwppCudaCtx *ctx, CUtensorMap *map, const void *base,
+                      CUtensorMapDataType dtype, uint64_t inner,
+                      uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner,
+                      uint32_t box_outer, CUtensorMapSwizzle swz);
+
+// ---------------------------------------------------------------------------
+// device side
+// ---------------------------------------------------------------------------
+
+#define BWPP_WAIT_LIMIT_NS (2ull * 1000ull * 1000ull * 1000ull)  // 2 s
+
+__device__ __forceinline__ uint64_t bwpp_globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void bwpp_report(int *status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// ---- mbarrier ---------------------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar,
+                                                      uint32_t bytes) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with `parity` to complete.  Gives up after `limit_ns`
+// (default BWPP_WAIT_LIMIT_NS), reports BWPP_CUDA_ERR_TIMEOUT and returns
+// false; the caller then unwinds instead of waiting on.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          int *status,
+                                          uint64_t limit_ns = BWPP_WAIT_LIMIT_NS) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = bwpp_globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (bwpp_globaltimer() - t0 > limit_ns) {
+      bwpp_report(status, BWPP_CUDA_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// ---- TMA (no multicast) ---------------------------------------------------
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,
+                                            uint64_t *bar, int32_t x,
+                                            int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::"
+      "bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map,
+                                             const void *src, int32_t x,
+                                             int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], "
+      "[%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void tma_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map))
+               : "memory");
+}
+
+// ---- tcgen05 ----------------------------------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile(
+      "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+          smem_u32(dst_smem)),
+      "r"(ncols)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::
+                   : "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(
+                   taddr),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D(tmem) (+)= A(smem desc) * B(smem desc), kind::f16, one CTA.
+__device__ __forceinline__ void tc_mma_f16_ss(uint32_t d_tmem, uint64_t adesc,
+                                              uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D(tmem) (+)= A(tmem) * B(smem desc), kind::f16, one CTA.
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem,
+                                              uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 op issued so far by this thread is done.
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+      "[%0];" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 32 lanes x 32 columns of 32-bit: thread t gets lane (base lane + t),
+// columns [col, col+32).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr,
+                                                   uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+        "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// 32 lanes x 16 columns of 32-bit, from registers into TMEM.
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr,
+                                                   const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
+      "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]),
+      "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// Shared-memory matrix descriptor for tcgen05 (sm_100 layout: start >> 4 in
+// bits 0-13, leading byte offset >> 4 in 16-29, stride byte offset >> 4 in
+// 32-45, version 1 in 46-47, swizzle mode in 61-63).
+__device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr,
+                                                   uint32_t lbo_bytes,
+                                                   uint32_t sbo_bytes,
+                                                   uint32_t swizzle_mode) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)(swizzle_mode & 7u) << 61;
+  return d;
+}
+
+#define BWPP_SWIZZLE_128B 2u
+
+// Instruction descriptor, kind::f16 with bf16 A/B and fp32 D.
+__host__ __device__ constexpr uint32_t make_idesc_bf16_f32(uint32_t M,
+                                                           uint32_t N,
+                                                           uint32_t a_mn_major,
+                                                           uint32_t b_mn_major) {
+  return (1u << 4)                // D format: f32
+         | (1u << 7)              // A format: bf16
+         | (1u << 10)             // B format: bf16
+         | (a_mn_major << 15)     // A major: 0 = K-major
+         | (b_mn_major << 16)     // B major: 1 = MN-major
+         | ((N >> 3) << 17)       // N / 8
+         | ((M >> 4) << 24);      // M / 16
+}
+
+__device__ __forceinline__ float bwpp_silu_f(float x) {
+  return x / (1.0f + __expf(-x));
+}

@@ -1,0 +1,397 @@
+// Fused matmul (+bias, +SiLU) on sm_100a tensor cores.
+//
+// C[M,N] (fp32) = epilogue(A[M,K] (bf16, K contiguous) * B[K,N] (bf16, N
+// contiguous)), epilogue = +bias[N] then SiLU, each optional, in the order of
+// runtime/cpu/bwpp_cpu_ref.c:26-31 and compiler/codegen_metal.c:426-431.
+//
+// Persistent, warp-specialised kernel, one CTA per SM (192 threads):
+//   warp 0       TMA producer: A box 128(M) x 64(K), B as four 64(N) x 64(K)
+//                boxes, 128-byte swizzle, 4-stage smem ring (48 KB/stage)
+//   warp 1       TMEM allocator + single-thread tcgen05.mma issuer
+//                (M=128, N=256, K=16, A K-major, B MN-major), commits free the
+//                smem stage / publish the accumulator
+//   warps 2..5   epilogue: tcgen05.ld 32 lanes x 32 columns, +bias, SiLU,
+//                swizzled smem staging, TMA store (double-buffered per warp)
+// Two 256-column fp32 accumulators in TMEM (512 columns): the epilogue of
+// tile i overlaps the main loop of tile i+1.  Tiles are rasterised in groups
+// of 8 M-blocks so CTAs running together share B panels in L2.
+//
+// Every wait is bounded (BWPP_WAIT_LIMIT_NS); an expired wait records
+// BWPP_CUDA_ERR_TIMEOUT, all roles unwind, TMEM is freed and the kernel ends.
+//
+// Shapes the TMA path cannot describe (row pitch not a multiple of 16 bytes,
+// unaligned pointers, K == 0) run on a CUDA-core kernel instead.
+#include "bwpp_cuda_internal.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_STAGE = BM * BK * 2;   // 16 KB
+constexpr int B_SUB = 64 * BK * 2;     // 8 KB: 64 N-columns x 64 K-rows
+constexpr int B_STAGE = BN * BK * 2;   // 32 KB
+constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int EPI_WARPS = 4;
+constexpr int EPI_COLS = 32;                   // columns per TMEM load / store
+constexpr int EPI_BUF = 32 * EPI_COLS * 4;     // 4 KB: 32 rows x 128 B
+constexpr int OFF_B = STAGES * A_STAGE;
+constexpr int OFF_C = OFF_B + STAGES * B_STAGE;
+constexpr int OFF_BAR = OFF_C + EPI_WARPS * 2 * EPI_BUF;
+constexpr int SMEM_USED = OFF_BAR + 128;
+constexpr int SMEM_ALLOC = SMEM_USED + 1024;  // slack for 1024-B alignment
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
+constexpr uint32_t TMEM_COLS = 2 * BN;
+constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN, 0, 1);
+constexpr uint32_t GROUP_M = 8;
+
+static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in limit");
+
+__device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m,
+                                            uint32_t tiles_n, uint32_t &mb,
+                                            uint32_t &nb) {
+  const uint32_t per_group = GROUP_M * tiles_n;
+  const uint32_t g = t / per_group;
+  const uint32_t first_m = g * GROUP_M;
+  const uint32_t gm = min(GROUP_M, tiles_m - first_m);
+  const uint32_t r = t - g * per_group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                   const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC,
+                   const float *__restrict__ bias, uint32_t M, uint32_t N,
+                   uint32_t K, int apply_bias, int apply_silu, int *status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tfull = empty + STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *drain = tempty + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
+  const uint32_t num_tiles = tiles_m * tiles_n;
+  const uint32_t num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      for (uint32_t t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        uint32_t mb, nb;
+        tile_coords(t, tiles_m, tiles_n, mb, nb);
+        for (uint32_t kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, status)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          uint8_t *sa = smem + stage * A_STAGE;
+          uint8_t *sb = smem + OFF_B + stage * B_STAGE;
+          tma_load_2d(sa, &tmA, &full[stage], (int32_t)(kb * BK), (int32_t)(mb * BM));
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(sb + j * B_SUB, &tmB, &full[stage],
+                        (int32_t)(nb * BN + j * 64), (int32_t)(kb * BK));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      for (uint32_t t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, status)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (uint32_t kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, status)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + stage * A_STAGE);
+          const uint32_t b0 = smem_u32(smem + OFF_B + stage * B_STAGE);
+#pragma unroll
+          for (int ks = 0; ks < BK / 16; ++ks) {
+            // A: K-major, 128-B swizzle; a K step of 16 bf16 = 32 bytes.
+            const uint64_t ad = make_smem_desc(a0 + ks * 32, 16, 1024, BWPP_SWIZZLE_128B);
+            // B: MN-major, 128-B swizzle; 64-column atoms 8 KB apart (LBO),
+            // 8-row K groups 1 KB apart (SBO); a K step of 16 rows = 2 KB.
+            const uint64_t bd = make_smem_desc(b0 + ks * 2048, B_SUB, 1024, BWPP_SWIZZLE_128B);
+            tc_mma_f16_ss(d_tmem, ad, bd, IDESC, (kb | ks) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // every MMA issued by this thread has finished before TMEM is freed
+      tc_commit(drain);
+      mbar_wait(drain, 0, status);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;
+    uint8_t *stage_c = smem + OFF_C + ew * 2 * EPI_BUF;
+    uint32_t acc = 0, acc_phase = 0, buf = 0;
+    for (uint32_t t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      uint32_t mb, nb;
+      tile_coords(t, tiles_m, tiles_n, mb, nb);
+      if (!mbar_wait(&tfull[acc], acc_phase, status)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t row0 = mb * BM + q * 32;
+      for (int c = 0; c < BN / EPI_COLS; ++c) {
+        const uint32_t col0 = nb * BN + c * EPI_COLS;
+        if (col0 >= N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c * EPI_COLS, r);
+        tc_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (apply_bias) {
+          if (col0 + 32 <= N) {
+            const float4 *b4 = reinterpret_cast<const float4 *>(bias + col0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 bb = __ldg(b4 + j);
+              v[4 * j] += bb.x;
+              v[4 * j + 1] += bb.y;
+              v[4 * j + 2] += bb.z;
+              v[4 * j + 3] += bb.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) v[j] += __ldg(bias + col0 + j);
+          }
+        }
+        if (apply_silu) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = bwpp_silu_f(v[j]);
+        }
+        // the store that last used this buffer has finished reading it
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+        uint8_t *sc = stage_c + buf * EPI_BUF;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4 *>(sc + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+              make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < M) {
+          tma_store_2d(&tmC, sc, (int32_t)col0, (int32_t)row0);
+          tma_store_commit();
+        }
+        buf ^= 1;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    if (lane == 0) tma_store_wait_all<0>();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core fallback for shapes TMA cannot describe (and K == 0)
+// ---------------------------------------------------------------------------
+constexpr int ST = 16;
+
+__global__ void gemm_simt_kernel(const uint16_t *__restrict__ a,
+                                 const uint16_t *__restrict__ b,
+                                 float *__restrict__ c, uint32_t M, uint32_t N,
+                                 uint32_t K, uint32_t lda, uint32_t ldb,
+                                 uint32_t ldc, const float *__restrict__ bias,
+                                 int apply_silu, int apply_bias) {
+  __shared__ float As[ST][ST + 1], Bs[ST][ST + 1];
+  const uint32_t row = blockIdx.y * ST + threadIdx.y;
+  const uint32_t col = blockIdx.x * ST + threadIdx.x;
+  float acc = 0.0f;
+  for (uint32_t k0 = 0; k0 < K; k0 += ST) {
+    const uint32_t ka = k0 + threadIdx.x, kb = k0 + threadIdx.y;
+    As[threadIdx.y][threadIdx.x] =
+        (row < M && ka < K) ? __uint_as_float((uint32_t)a[(size_t)row * lda + ka] << 16) : 0.0f;
+    Bs[threadIdx.y][threadIdx.x] =
+        (kb < K && col < N) ? __uint_as_float((uint32_t)b[(size_t)kb * ldb + col] << 16) : 0.0f;
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < ST; ++kk) acc += As[threadIdx.y][kk] * Bs[kk][threadIdx.x];
+    __syncthreads();
+  }
+  if (row < M && col < N) {
+    if (apply_bias && bias) acc += bias[col];
+    if (apply_silu) acc = acc / (1.0f + expf(-acc));
+    c[(size_t)row * ldc + col] = acc;
+  }
+}
+
+__global__ void cast_f32_bf16_kernel(const float *__restrict__ src,
+                                     uint16_t *__restrict__ dst, uint32_t rows,
+                                     uint32_t cols, uint32_t ld_src,
+                                     uint32_t ld_dst) {
+  const size_t n = (size_t)rows * cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / cols, cc = i % cols;
+    const float x = src[r * ld_src + cc];
+    uint32_t u = __float_as_uint(x);
+    uint16_t h;
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu))
+      h = (uint16_t)((u >> 16) | 0x0040u);  // quiet NaN
+    else
+      h = (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);  // nearest even
+    dst[r * ld_dst + cc] = h;
+  }
+}
+
+bool g_attr_set[64] = {};
+
+inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+// Kernel-only entry used by the public API and by composite paths.
+int bwpp_gemm_launch(BwppCudaCtx *ctx, const uint16_t *a, const uint16_t *b,
+                     float *c, uint32_t M, uint32_t N, uint32_t K, uint32_t lda,
+                     uint32_t ldb, uint32_t ldc, const float *bias,
+                     int apply_silu, int apply_bias, int force_simt) {
+  if (M == 0 || N == 0) return BWPP_CUDA_OK;
+  const int use_bias = (apply_bias && bias) ? 1 : 0;
+  const bool tc_ok = !force_simt && K > 0 && al16(a) && al16(b) && al16(c) &&
+                     (lda % 8) == 0 && (ldb % 8) == 0 && (ldc % 4) == 0 &&
+                     (!use_bias || al16(bias));
+  cudaStream_t s = ctx->stream;
+  if (!tc_ok) {
+    dim3 grid((N + ST - 1) / ST, (M + ST - 1) / ST);
+    gemm_simt_kernel<<<grid, dim3(ST, ST), 0, s>>>(a, b, c, M, N, K, lda, ldb, ldc,
+                                                   bias, apply_silu, use_bias);
+    BWPP_LAUNCH_CHECK(ctx, "gemm simt");
+    return BWPP_CUDA_OK;
+  }
+  CUtensorMap ta, tb, tcm;
+  int rc = bwpp_make_tmap_2d(ctx, &ta, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M,
+                             (uint64_t)lda * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc)
+    rc = bwpp_make_tmap_2d(ctx, &tb, b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, K,
+                           (uint64_t)ldb * 2, 64, BK, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc)
+    rc = bwpp_make_tmap_2d(ctx, &tcm, c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M,
+                           (uint64_t)ldc * 4, EPI_COLS, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (ctx->device < 64 && !g_attr_set[ctx->device]) {
+    rc = bwpp_check_cuda(ctx,
+                         cudaFuncSetAttribute(gemm_tc_kernel,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              SMEM_ALLOC),
+                         "gemm smem attribute");
+    if (rc) return rc;
+    g_attr_set[ctx->device] = true;
+  }
+  const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const uint32_t grid = tiles < (uint32_t)ctx->num_sms ? tiles : (uint32_t)ctx->num_sms;
+  gemm_tc_kernel<<<grid, THREADS, SMEM_ALLOC, s>>>(ta, tb, tcm, bias, M, N, K, use_bias,
+                                                   apply_silu, ctx->status_word);
+  BWPP_LAUNCH_CHECK(ctx, "gemm tcgen05");
+  return BWPP_CUDA_OK;
+}
+
+int bwpp_cast_launch(BwppCudaCtx *ctx, const float *src, uint16_t *dst,
+                     uint32_t rows, uint32_t cols, uint32_t ld_src,
+                     uint32_t ld_dst) {
+  const size_t n = (size_t)rows * cols;
+  if (n == 0) return BWPP_CUDA_OK;
+  size_t blocks = (n + 255) / 256;
+  const size_t cap = (size_t)ctx->num_sms * 16;
+  if (blocks > cap) blocks = cap;
+  cast_f32_bf16_kernel<<<(unsigned)blocks, 256, 0, ctx->stream>>>(src, dst, rows, cols, ld_src,
+                                                                   ld_dst);
+  BWPP_LAUNCH_CHECK(ctx, "cast f32->bf16");
+  return BWPP_CUDA_OK;
+}
+
+extern "C" {
+
+int bwpp_cuda_matmul_bf16(BwppCudaCtx *ctx, const uint16_t *a,
+                          const uint16_t *b, float *c, uint32_t M, uint32_t N,
+                          uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
+                          const float *bias, int apply_silu, int apply_bias) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (!a || !b || !c) return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "matmul: NULL buffer");
+  if (lda < K || ldb < N || ldc < N)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "matmul: leading dim smaller than row");
+  return bwpp_gemm_launch(ctx, a, b, c, M, N, K, lda, ldb, ldc, bias, apply_silu,
+                          apply_bias, 0);
+}
+
+int bwpp_cuda_cast_f32_bf16(BwppCudaCtx *ctx, const float *src, uint16_t *dst,
+                            uint32_t rows, uint32_t cols, uint32_t ld_src) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (!src || !dst || ld_src < cols) return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "cast: bad args");
+  return bwpp_cast_launch(ctx, src, dst, rows, cols, ld_src, cols);
+}
+
+}  // extern "C"

@@ -1,0 +1,428 @@
+// Drop-in mirrors of the reference's runtime/cpu and runtime/metal entry
+// points on top of the ctx API.
+//
+// CPU mirrors (runtime/cpu/bwpp_cpu_ref.h:6-58): same argument lists, void,
+// synchronous.  Each buffer may be host or device memory: device buffers are
+// used in place, host buffers are staged through the calling thread's
+// per-device context scratch.  fp32 matmul / attention operands are rounded
+// to bf16 on the device before the tensor-core kernels run.  Like the
+// reference, NULL required buffers make a call a silent no-op.
+//
+// Metal mirrors (runtime/metal/dispatch_stub.h:42-74): same param structs; a
+// call only runs when `source` carries the kernel's bwpp.meta tag, as in
+// runtime/metal/dispatch_stub.m:74-79.
+#include <string.h>
+
+#include "bwpp_cuda_internal.cuh"
+
+int bwpp_gemm_launch(BwppCudaCtx *ctx, const uint16_t *a, const uint16_t *b,
+                     float *c, uint32_t M, uint32_t N, uint32_t K, uint32_t lda,
+                     uint32_t ldb, uint32_t ldc, const float *bias,
+                     int apply_silu, int apply_bias, int force_simt);
+int bwpp_cast_launch(BwppCudaCtx *ctx, const float *src, uint16_t *dst,
+                     uint32_t rows, uint32_t cols, uint32_t ld_src,
+                     uint32_t ld_dst);
+int bwpp_attention_launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                          const uint16_t *v, float *o, uint32_t BH, uint32_t Sq,
+                          uint32_t Skv, uint32_t Kd, uint32_t Dv, uint64_t q_bh,
+                          uint64_t k_bh, uint64_t v_bh, uint64_t o_bh,
+                          uint32_t ldq, uint32_t ldk, uint32_t ldv, uint32_t ldo,
+                          float scale, int causal);
+
+namespace {
+
+thread_local BwppCudaCtx *tl_ctx[64];
+thread_local int tl_status = BWPP_CUDA_OK;
+
+BwppCudaCtx *mirror_ctx() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (!tl_ctx[dev] && bwpp_cuda_ctx_create(&tl_ctx[dev], dev, nullptr) != BWPP_CUDA_OK)
+    tl_ctx[dev] = nullptr;
+  return tl_ctx[dev];
+}
+
+bool is_device_ptr(const void *p) {
+  if (!p) return false;
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+inline uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
+
+// Carves 256-byte-aligned pieces out of one workspace request.
+struct Carver {
+  size_t total = 0;
+  size_t take(size_t bytes) {
+    size_t off = total;
+    total += (bytes + 255) & ~(size_t)255;
+    return off;
+  }
+};
+
+// A fp32 matrix view (rows x cols, leading dim ld) made device-resident:
+// device buffers are used as they are, host buffers copied densely.
+struct DevF32 {
+  const float *src;
+  uint32_t rows, cols, ld;
+  bool dev;
+  size_t off;
+  const float *ptr;
+  uint32_t dld;
+};
+
+void plan_f32(Carver &cv, DevF32 &m, const float *src, uint32_t rows,
+              uint32_t cols, uint32_t ld) {
+  m.src = src;
+  m.rows = rows;
+  m.cols = cols;
+  m.ld = ld;
+  m.dev = is_device_ptr(src);
+  m.off = m.dev ? 0 : cv.take(sizeof(float) * (size_t)rows * cols);
+  m.ptr = m.dev ? src : nullptr;
+  m.dld = m.dev ? ld : cols;
+}
+
+int upload_f32(BwppCudaCtx *ctx, uint8_t *ws, DevF32 &m) {
+  if (m.dev || !m.src) return BWPP_CUDA_OK;
+  float *d = reinterpret_cast<float *>(ws + m.off);
+  m.ptr = d;
+  if ((size_t)m.rows * m.cols == 0) return BWPP_CUDA_OK;
+  return bwpp_check_cuda(ctx,
+                         cudaMemcpy2DAsync(d, sizeof(float) * m.cols, m.src,
+                                           sizeof(float) * m.ld,
+                                           sizeof(float) * m.cols, m.rows,
+                                           cudaMemcpyHostToDevice, ctx->stream),
+                         "mirror upload");
+}
+
+// Output view: written in place when it is device memory with a usable
+// layout, else into dense scratch and copied back with the caller's ld.
+struct OutF32 {
+  float *dst;
+  uint32_t rows, cols, ld;
+  bool direct;
+  size_t off;
+  float *ptr;
+  uint32_t dld;
+};
+
+void plan_out(Carver &cv, OutF32 &m, float *dst, uint32_t rows, uint32_t cols,
+              uint32_t ld, uint32_t need_ld_mult) {
+  m.dst = dst;
+  m.rows = rows;
+  m.cols = cols;
+  m.ld = ld;
+  m.direct = is_device_ptr(dst) && ld % need_ld_mult == 0 &&
+             (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+  m.dld = m.direct ? ld : round_up(cols ? cols : 1, need_ld_mult);
+  m.off = m.direct ? 0 : cv.take(sizeof(float) * (size_t)rows * m.dld);
+  m.ptr = m.direct ? dst : nullptr;
+}
+
+void bind_out(uint8_t *ws, OutF32 &m) {
+  if (!m.direct) m.ptr = reinterpret_cast<float *>(ws + m.off);
+}
+
+int download(BwppCudaCtx *ctx, OutF32 &m) {
+  if (m.direct || (size_t)m.rows * m.cols == 0) return BWPP_CUDA_OK;
+  return bwpp_check_cuda(ctx,
+                         cudaMemcpy2DAsync(m.dst, sizeof(float) * m.ld, m.ptr,
+                                           sizeof(float) * m.dld,
+                                           sizeof(float) * m.cols, m.rows,
+                                           cudaMemcpyDefault, ctx->stream),
+                         "mirror download");
+}
+
+int finish(BwppCudaCtx *ctx, int rc) {
+  if (rc == BWPP_CUDA_OK) rc = bwpp_cuda_sync(ctx);
+  else bwpp_cuda_sync(ctx);
+  tl_status = rc;
+  return rc;
+}
+
+bool has_tag(const char *src, const char *tag) {
+  return src && tag && strstr(src, tag) != nullptr;
+}
+
+void parse_epilogue(const char *src, int *ep_add, int *ep_silu) {
+  // Same vocabulary as runtime/cpu/test_metal_parity.c:48-76.
+  *ep_add = has_tag(src, "#define BWPP_EPILOGUE_ADD 1");
+  *ep_silu = has_tag(src, "#define BWPP_EPILOGUE_SILU 1");
+  if (*ep_add || *ep_silu) return;
+  const char *p = src ? strstr(src, "bwpp.meta: epilogue=") : nullptr;
+  if (!p) return;
+  p += strlen("bwpp.meta: epilogue=");
+  if (strncmp(p, "add_silu", 8) == 0) {
+    *ep_add = 1;
+    *ep_silu = 1;
+  } else if (strncmp(p, "add", 3) == 0) {
+    *ep_add = 1;
+  } else if (strncmp(p, "silu", 4) == 0) {
+    *ep_silu = 1;
+  }
+}
+
+int bwpp_cuda_last_status_impl() { return tl_status; }
+
+// Row-wise ops (softmax, rmsnorm) read x and write y with one leading dim.
+// Device x and y that share ld run in place; otherwise both go through dense
+// scratch (ld = cols).
+struct RowOp {
+  const float *x;
+  float *y;
+  uint32_t ld;
+  bool staged;
+  size_t off_x, off_y;
+};
+
+void plan_rowop(Carver &cv, RowOp &r, const float *x, float *y, uint32_t rows,
+                uint32_t cols, uint32_t ld) {
+  r.staged = !(is_device_ptr(x) && is_device_ptr(y));
+  r.x = x;
+  r.y = y;
+  r.ld = r.staged ? cols : ld;
+  r.off_x = r.staged ? cv.take(sizeof(float) * (size_t)rows * cols) : 0;
+  r.off_y = r.staged ? cv.take(sizeof(float) * (size_t)rows * cols) : 0;
+}
+
+int rowop_upload(BwppCudaCtx *ctx, uint8_t *ws, RowOp &r, const float *x,
+                 uint32_t rows, uint32_t cols, uint32_t ld) {
+  if (!r.staged) return BWPP_CUDA_OK;
+  float *dx = reinterpret_cast<float *>(ws + r.off_x);
+  r.x = dx;
+  r.y = reinterpret_cast<float *>(ws + r.off_y);
+  if ((size_t)rows * cols == 0) return BWPP_CUDA_OK;
+  return bwpp_check_cuda(ctx,
+                         cudaMemcpy2DAsync(dx, sizeof(float) * cols, x, sizeof(float) * ld,
+                                           sizeof(float) * cols, rows, cudaMemcpyDefault,
+                                           ctx->stream),
+                         "row op upload");
+}
+
+int rowop_download(BwppCudaCtx *ctx, RowOp &r, float *y, uint32_t rows,
+                   uint32_t cols, uint32_t ld) {
+  if (!r.staged || (size_t)rows * cols == 0) return BWPP_CUDA_OK;
+  return bwpp_check_cuda(ctx,
+                         cudaMemcpy2DAsync(y, sizeof(float) * ld, r.y, sizeof(float) * cols,
+                                           sizeof(float) * cols, rows, cudaMemcpyDefault,
+                                           ctx->stream),
+                         "row op download");
+}
+
+}  // namespace
+
+extern "C" {
+
+int bwpp_cuda_last_status(void) { return bwpp_cuda_last_status_impl(); }
+
+void bwpp_cuda_matmul_f32(const float *a, const float *b, float *c, uint32_t M,
+                          uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                          uint32_t ldc, const float *bias, int apply_silu,
+                          int apply_bias) {
+  tl_status = BWPP_CUDA_OK;
+  if (!a || !b || !c) return;
+  BwppCudaCtx *ctx = mirror_ctx();
+  if (!ctx) { tl_status = BWPP_CUDA_ERR_CUDA; return; }
+  const bool use_bias = apply_bias && bias;
+  const uint32_t K8 = round_up(K ? K : 1, 8), N8 = round_up(N ? N : 1, 8);
+  Carver cv;
+  DevF32 da, db, dbias;
+  plan_f32(cv, da, a, M, K, lda);
+  plan_f32(cv, db, b, K, N, ldb);
+  plan_f32(cv, dbias, use_bias ? bias : nullptr, 1, use_bias ? N : 0, N);
+  const size_t off_a16 = cv.take(2 * (size_t)M * K8);
+  const size_t off_b16 = cv.take(2 * (size_t)K * N8);
+  OutF32 oc;
+  plan_out(cv, oc, c, M, N, ldc, 4);
+  uint8_t *ws = (uint8_t *)bwpp_ctx_workspace(ctx, cv.total);
+  if (!ws) { tl_status = BWPP_CUDA_ERR_NOMEM; return; }
+  bind_out(ws, oc);
+  uint16_t *a16 = reinterpret_cast<uint16_t *>(ws + off_a16);
+  uint16_t *b16 = reinterpret_cast<uint16_t *>(ws + off_b16);
+  int rc = upload_f32(ctx, ws, da);
+  if (!rc) rc = upload_f32(ctx, ws, db);
+  if (!rc && use_bias) rc = upload_f32(ctx, ws, dbias);
+  if (!rc) rc = bwpp_cast_launch(ctx, da.ptr, a16, M, K, da.dld, K8);
+  if (!rc) rc = bwpp_cast_launch(ctx, db.ptr, b16, K, N, db.dld, N8);
+  if (!rc)
+    rc = bwpp_gemm_launch(ctx, a16, b16, oc.ptr, M, N, K, K8, N8, oc.dld,
+                          use_bias ? dbias.ptr : nullptr, apply_silu, use_bias, 0);
+  if (!rc) rc = download(ctx, oc);
+  finish(ctx, rc);
+}
+
+void bwpp_cuda_softmax_f32(const float *x, float *y, uint32_t rows,
+                           uint32_t cols, uint32_t ld) {
+  tl_status = BWPP_CUDA_OK;
+  if (!x || !y) return;
+  BwppCudaCtx *ctx = mirror_ctx();
+  if (!ctx) { tl_status = BWPP_CUDA_ERR_CUDA; return; }
+  Carver cv;
+  RowOp r;
+  plan_rowop(cv, r, x, y, rows, cols, ld);
+  uint8_t *ws = (uint8_t *)bwpp_ctx_workspace(ctx, cv.total);
+  if (!ws) { tl_status = BWPP_CUDA_ERR_NOMEM; return; }
+  int rc = rowop_upload(ctx, ws, r, x, rows, cols, ld);
+  if (!rc) rc = bwpp_cuda_softmax_fwd_f32(ctx, r.x, r.y, rows, cols, r.ld);
+  if (!rc) rc = rowop_download(ctx, r, y, rows, cols, ld);
+  finish(ctx, rc);
+}
+
+void bwpp_cuda_rmsnorm_f32(const float *x, float *y, const float *gamma,
+                           const float *beta, uint32_t rows, uint32_t cols,
+                           uint32_t ld, float eps) {
+  tl_status = BWPP_CUDA_OK;
+  if (!x || !y) return;
+  BwppCudaCtx *ctx = mirror_ctx();
+  if (!ctx) { tl_status = BWPP_CUDA_ERR_CUDA; return; }
+  Carver cv;
+  RowOp r;
+  plan_rowop(cv, r, x, y, rows, cols, ld);
+  DevF32 dg, db;
+  plan_f32(cv, dg, gamma, 1, gamma ? cols : 0, cols);
+  plan_f32(cv, db, beta, 1, beta ? cols : 0, cols);
+  uint8_t *ws = (uint8_t *)bwpp_ctx_workspace(ctx, cv.total);
+  if (!ws) { tl_status = BWPP_CUDA_ERR_NOMEM; return; }
+  int rc = rowop_upload(ctx, ws, r, x, rows, cols, ld);
+  if (!rc && gamma) rc = upload_f32(ctx, ws, dg);
+  if (!rc && beta) rc = upload_f32(ctx, ws, db);
+  if (!rc)
+    rc = bwpp_cuda_rmsnorm_fwd_f32(ctx, r.x, r.y, gamma ? dg.ptr : nullptr,
+                                   beta ? db.ptr : nullptr, rows, cols, r.ld, eps);
+  if (!rc) rc = rowop_download(ctx, r, y, rows, cols, ld);
+  finish(ctx, rc);
+}
+
+void bwpp_cuda_attention_f32(const float *q, const float *k, const float *v,
+                             float *o, uint32_t M, uint32_t N, uint32_t K,
+                             uint32_t D, uint32_t ldq, uint32_t ldk,
+                             uint32_t ldv, uint32_t ldo) {
+  tl_status = BWPP_CUDA_OK;
+  if (!q || !k || !v || !o) return;
+  BwppCudaCtx *ctx = mirror_ctx();
+  if (!ctx) { tl_status = BWPP_CUDA_ERR_CUDA; return; }
+  Carver cv;
+  DevF32 dq, dk, dv;
+  plan_f32(cv, dq, q, M, K, ldq);
+  plan_f32(cv, dk, k, N, K, ldk);
+  plan_f32(cv, dv, v, N, D, ldv);
+  const size_t oq = cv.take(2 * (size_t)M * K), ok_ = cv.take(2 * (size_t)N * K),
+               ov = cv.take(2 * (size_t)N * D);
+  OutF32 oo;
+  plan_out(cv, oo, o, M, D, ldo, 1);
+  uint8_t *ws = (uint8_t *)bwpp_ctx_workspace(ctx, cv.total);
+  if (!ws) { tl_status = BWPP_CUDA_ERR_NOMEM; return; }
+  bind_out(ws, oo);
+  uint16_t *q16 = reinterpret_cast<uint16_t *>(ws + oq);
+  uint16_t *k16 = reinterpret_cast<uint16_t *>(ws + ok_);
+  uint16_t *v16 = reinterpret_cast<uint16_t *>(ws + ov);
+  int rc = upload_f32(ctx, ws, dq);
+  if (!rc) rc = upload_f32(ctx, ws, dk);
+  if (!rc) rc = upload_f32(ctx, ws, dv);
+  if (!rc) rc = bwpp_cast_launch(ctx, dq.ptr, q16, M, K, dq.dld, K);
+  if (!rc) rc = bwpp_cast_launch(ctx, dk.ptr, k16, N, K, dk.dld, K);
+  if (!rc) rc = bwpp_cast_launch(ctx, dv.ptr, v16, N, D, dv.dld, D);
+  if (!rc)
+    rc = bwpp_attention_launch(ctx, q16, k16, v16, oo.ptr, 1, M, N, K, D,
+                               (uint64_t)M * K, (uint64_t)N * K, (uint64_t)N * D,
+                               (uint64_t)M * oo.dld, K, K, D, oo.dld, 1.0f, 0);
+  if (!rc) rc = download(ctx, oo);
+  finish(ctx, rc);
+}
+
+void bwpp_cuda_reduce_max_mask_f32(const float *x, float *mask, uint32_t rows,
+                                   uint32_t cols, int axis) {
+  tl_status = BWPP_CUDA_OK;
+  if (!x || !mask) return;
+  BwppCudaCtx *ctx = mirror_ctx();
+  if (!ctx) { tl_status = BWPP_CUDA_ERR_CUDA; return; }
+  Carver cv;
+  DevF32 dx;
+  plan_f32(cv, dx, x, rows, cols, cols);
+  OutF32 om;
+  plan_out(cv, om, mask, rows, cols, cols, 1);
+  uint8_t *ws = (uint8_t *)bwpp_ctx_workspace(ctx, cv.total);
+  if (!ws) { tl_status = BWPP_CUDA_ERR_NOMEM; return; }
+  bind_out(ws, om);
+  int rc = upload_f32(ctx, ws, dx);
+  if (!rc) rc = bwpp_cuda_reduce_max_mask_ex(ctx, dx.ptr, om.ptr, rows, cols, axis);
+  if (!rc) rc = download(ctx, om);
+  finish(ctx, rc);
+}
+
+void bwpp_cuda_reduce_max_grad_f32(const float *mask, const float *dy,
+                                   float *dx, uint32_t rows, uint32_t cols,
+                                   int axis) {
+  tl_status = BWPP_CUDA_OK;
+  if (!mask || !dy || !dx) return;
+  BwppCudaCtx *ctx = mirror_ctx();
+  if (!ctx) { tl_status = BWPP_CUDA_ERR_CUDA; return; }
+  Carver cv;
+  DevF32 dm, dd;
+  plan_f32(cv, dm, mask, rows, cols, cols);
+  plan_f32(cv, dd, dy, 1, axis == 0 ? cols : rows, axis == 0 ? cols : rows);
+  OutF32 od;
+  plan_out(cv, od, dx, rows, cols, cols, 1);
+  uint8_t *ws = (uint8_t *)bwpp_ctx_workspace(ctx, cv.total);
+  if (!ws) { tl_status = BWPP_CUDA_ERR_NOMEM; return; }
+  bind_out(ws, od);
+  int rc = upload_f32(ctx, ws, dm);
+  if (!rc) rc = upload_f32(ctx, ws, dd);
+  if (!rc) rc = bwpp_cuda_reduce_max_grad_ex(ctx, dm.ptr, dd.ptr, od.ptr, rows, cols, axis);
+  if (!rc) rc = download(ctx, od);
+  finish(ctx, rc);
+}
+
+// ---- Metal dispatch mirrors ----------------------------------------------
+
+int bwpp_cuda_dispatch_matmul(BwppCudaCtx *ctx, const uint16_t *a,
+                              const uint16_t *b, float *c, const float *bias,
+                              BwppCudaMatmulParams p, const char *source) {
+  if (!ctx || !a || !b || !c || !source) return BWPP_CUDA_ERR_ARG;
+  if (has_tag(source, "bwpp.meta: kernel=none") ||
+      !has_tag(source, "bwpp.meta: kernel=matmul_f16"))
+    return BWPP_CUDA_OK;
+  int ep_add = 0, ep_silu = 0;
+  parse_epilogue(source, &ep_add, &ep_silu);
+  return bwpp_cuda_matmul_bf16(ctx, a, b, c, p.M, p.N, p.K, p.lda, p.ldb, p.ldc,
+                               bias, ep_silu, ep_add);
+}
+
+int bwpp_cuda_dispatch_softmax(BwppCudaCtx *ctx, const float *x, float *y,
+                               BwppCudaSoftmaxParams p, const char *source) {
+  if (!ctx || !x || !y || !source) return BWPP_CUDA_ERR_ARG;
+  if (!has_tag(source, "softmax_f16")) return BWPP_CUDA_OK;
+  return bwpp_cuda_softmax_fwd_f32(ctx, x, y, p.rows, p.cols, p.ld);
+}
+
+int bwpp_cuda_dispatch_rmsnorm(BwppCudaCtx *ctx, const float *x,
+                               const float *gamma, const float *beta, float *y,
+                               BwppCudaRmsnormParams p, const char *source) {
+  if (!ctx || !x || !y || !source) return BWPP_CUDA_ERR_ARG;
+  if (!has_tag(source, "rmsnorm_f16")) return BWPP_CUDA_OK;
+  // A missing gamma / beta acts as ones / zeros (dispatch_stub.m:225-243).
+  return bwpp_cuda_rmsnorm_fwd_f32(ctx, x, y, gamma, beta, p.rows, p.cols, p.ld,
+                                   p.eps);
+}
+
+int bwpp_cuda_dispatch_attention(BwppCudaCtx *ctx, const uint16_t *q,
+                                 const uint16_t *k, const uint16_t *v, float *o,
+                                 BwppCudaAttentionParams p,
+                                 const char *source) {
+  if (!ctx || !q || !k || !v || !o || !source) return BWPP_CUDA_ERR_ARG;
+  if (!has_tag(source, "bwpp.meta: kernel=attention_f16")) return BWPP_CUDA_OK;
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  return bwpp_attention_launch(ctx, q, k, v, o, 1, p.M, p.N, p.K, p.D, 0, 0, 0, 0,
+                               p.ldq, p.ldk, p.ldv, p.ldo, 1.0f, 0);
+}
+
+}  // extern "C"

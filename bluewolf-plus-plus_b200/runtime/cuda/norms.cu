@@ -1,0 +1,527 @@
+// RMSNorm / LayerNorm forward and backward, fp32, HBM-bound.
+//
+// Row kernels: one CTA per row (grid-stride), the row held in registers as
+// 128-bit vectors (thread t owns vectors t, t+T, t+2T, ...: every load and
+// store instruction of a warp touches 512 contiguous bytes), warp-shuffle +
+// shared-memory block reductions.  Rows wider than the register budget use a
+// looped variant that re-reads the row (from L2) instead.
+//
+// Backward: a persistent grid; each CTA walks rows blockIdx.x, +gridDim.x, ...
+// and accumulates its dgamma / dbeta partial for the columns its threads own
+// in registers, then writes one partial row to scratch.  A second kernel sums
+// the partials over CTAs in a fixed order, so results are deterministic.
+//
+// Reference: runtime/cpu/bwpp_cpu_ref.c:63-90 (rmsnorm fwd); backward rule
+// compiler/graph_ir.c:1735-1789; layernorm has no reference counterpart.
+#include "bwpp_cuda_internal.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxVecFwd = 16;  // fwd: up to 256*16 vectors in registers
+constexpr int kMaxVecBwd = 8;   // bwd: x and dy both resident
+
+template <bool V4>
+struct Vec;
+template <>
+struct Vec<true> {
+  static constexpr int W = 4;
+  __device__ static void load(const float *p, uint32_t i, float (&o)[4]) {
+    float4 t = __ldg(reinterpret_cast<const float4 *>(p) + i);
+    o[0] = t.x; o[1] = t.y; o[2] = t.z; o[3] = t.w;
+  }
+  __device__ static void load_stream(const float *p, uint32_t i,
+                                     float (&o)[4]) {
+    float4 t = __ldcs(reinterpret_cast<const float4 *>(p) + i);
+    o[0] = t.x; o[1] = t.y; o[2] = t.z; o[3] = t.w;
+  }
+  __device__ static void store(float *p, uint32_t i, const float (&v)[4]) {
+    __stcs(reinterpret_cast<float4 *>(p) + i,
+           make_float4(v[0], v[1], v[2], v[3]));
+  }
+};
+template <>
+struct Vec<false> {
+  static constexpr int W = 1;
+  __device__ static void load(const float *p, uint32_t i, float (&o)[1]) {
+    o[0] = __ldg(p + i);
+  }
+  __device__ static void load_stream(const float *p, uint32_t i,
+                                     float (&o)[1]) {
+    o[0] = __ldcs(p + i);
+  }
+  __device__ static void store(float *p, uint32_t i, const float (&v)[1]) {
+    __stcs(p + i, v[0]);
+  }
+};
+
+// Sums NV values over the block; every thread gets the totals.
+template <int NV>
+__device__ __forceinline__ void block_sum(float (&v)[NV], float *red) {
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  __syncthreads();  // `red` may still be read from the previous row
+  if (lane == 0)
+#pragma unroll
+    for (int j = 0; j < NV; ++j) red[j * 32 + warp] = v[j];
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    float t = lane < nwarps ? red[j * 32 + lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    v[j] = t;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// forward, row held in registers
+// ---------------------------------------------------------------------------
+template <int MAXV, bool V4, bool CENTERED>
+__global__ void __launch_bounds__(kThreads)
+    norm_fwd_kernel(const float *__restrict__ x, float *__restrict__ y,
+                    const float *__restrict__ gamma,
+                    const float *__restrict__ beta, uint32_t rows,
+                    uint32_t cols, uint32_t ld, float eps) {
+  using V = Vec<V4>;
+  constexpr int W = V::W;
+  __shared__ float red[3 * 32];
+  const uint32_t nv = cols / W;
+  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float *xr = x + (size_t)r * ld;
+    float *yr = y + (size_t)r * ld;
+    float xv[MAXV][W];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv) V::load_stream(xr, idx, xv[i]);
+      else
+#pragma unroll
+        for (int w = 0; w < W; ++w) xv[i][w] = 0.0f;
+    }
+    float mean = 0.0f;
+    if (CENTERED) {
+      float s[1] = {0.0f};
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i)
+#pragma unroll
+        for (int w = 0; w < W; ++w) s[0] += xv[i][w];
+      block_sum<1>(s, red);
+      mean = s[0] / (float)cols;
+    }
+    float ss[1] = {0.0f};
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv)
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          const float d = xv[i][w] - mean;
+          ss[0] += d * d;
+        }
+    }
+    block_sum<1>(ss, red);
+    const float inv = 1.0f / sqrtf(ss[0] / (float)cols + eps);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx >= nv) continue;
+      float g[W], b[W], o[W];
+      if (gamma) V::load(gamma, idx, g);
+      if (beta) V::load(beta, idx, b);
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        float v = (xv[i][w] - mean) * inv;
+        if (gamma) v *= g[w];
+        if (beta) v += b[w];
+        o[w] = v;
+      }
+      V::store(yr, idx, o);
+    }
+  }
+}
+
+// forward, any width: re-reads the row
+template <bool CENTERED>
+__global__ void __launch_bounds__(kThreads)
+    norm_fwd_looped_kernel(const float *__restrict__ x, float *__restrict__ y,
+                           const float *__restrict__ gamma,
+                           const float *__restrict__ beta, uint32_t rows,
+                           uint32_t cols, uint32_t ld, float eps) {
+  __shared__ float red[3 * 32];
+  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float *xr = x + (size_t)r * ld;
+    float *yr = y + (size_t)r * ld;
+    float mean = 0.0f;
+    if (CENTERED) {
+      float s[1] = {0.0f};
+      for (uint32_t c = threadIdx.x; c < cols; c += kThreads) s[0] += xr[c];
+      block_sum<1>(s, red);
+      mean = s[0] / (float)cols;
+    }
+    float ss[1] = {0.0f};
+    for (uint32_t c = threadIdx.x; c < cols; c += kThreads) {
+      const float d = xr[c] - mean;
+      ss[0] += d * d;
+    }
+    block_sum<1>(ss, red);
+    const float inv = 1.0f / sqrtf(ss[0] / (float)cols + eps);
+    for (uint32_t c = threadIdx.x; c < cols; c += kThreads) {
+      float v = (xr[c] - mean) * inv;
+      if (gamma) v *= gamma[c];
+      if (beta) v += beta[c];
+      yr[c] = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------
+// Per row (CENTERED = layernorm, else rmsnorm), with g = gamma * dy:
+//   mu = CENTERED ? mean(x) : 0;  r = 1/sqrt(mean((x-mu)^2) + eps)
+//   xhat = (x - mu) r;  dx = r (g - CENTERED*mean(g) - xhat mean(g xhat))
+//   dgamma += dy xhat;  dbeta += dy
+template <int MAXV, bool V4, bool CENTERED>
+__global__ void __launch_bounds__(kThreads)
+    norm_bwd_kernel(const float *__restrict__ x, const float *__restrict__ gamma,
+                    const float *__restrict__ dy, float *__restrict__ dx,
+                    float *__restrict__ part_g, float *__restrict__ part_b,
+                    uint32_t rows, uint32_t cols, uint32_t ld, float eps) {
+  using V = Vec<V4>;
+  constexpr int W = V::W;
+  __shared__ float red[3 * 32];
+  const uint32_t nv = cols / W;
+  float acc_g[MAXV][W], acc_b[MAXV][W], gm[MAXV][W];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const uint32_t idx = threadIdx.x + i * kThreads;
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      acc_g[i][w] = 0.0f;
+      acc_b[i][w] = 0.0f;
+      gm[i][w] = 1.0f;
+    }
+    if (gamma && idx < nv) V::load(gamma, idx, gm[i]);
+  }
+  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float *xr = x + (size_t)r * ld;
+    const float *gr = dy + (size_t)r * ld;
+    float xv[MAXV][W], dv[MAXV][W];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv) {
+        V::load_stream(xr, idx, xv[i]);
+        V::load_stream(gr, idx, dv[i]);
+      } else {
+#pragma unroll
+        for (int w = 0; w < W; ++w) xv[i][w] = dv[i][w] = 0.0f;
+      }
+    }
+    float mean = 0.0f;
+    if (CENTERED) {
+      float s[1] = {0.0f};
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i)
+#pragma unroll
+        for (int w = 0; w < W; ++w) s[0] += xv[i][w];
+      block_sum<1>(s, red);
+      mean = s[0] / (float)cols;
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const uint32_t idx = threadIdx.x + i * kThreads;
+        if (idx < nv)
+#pragma unroll
+          for (int w = 0; w < W; ++w) xv[i][w] -= mean;
+      }
+    }
+    // t = {sum (x-mu)^2, sum g, sum g (x-mu)}
+    float t[3] = {0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        const float g = gm[i][w] * dv[i][w];
+        t[0] += xv[i][w] * xv[i][w];
+        t[1] += g;
+        t[2] += g * xv[i][w];
+      }
+    block_sum<3>(t, red);
+    const float rs = 1.0f / sqrtf(t[0] / (float)cols + eps);
+    const float mg = CENTERED ? t[1] / (float)cols : 0.0f;
+    const float mgx = t[2] * rs / (float)cols;  // mean(g * xhat)
+    float *dxr = dx + (size_t)r * ld;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx >= nv) continue;
+      float o[W];
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        const float xh = xv[i][w] * rs;
+        const float g = gm[i][w] * dv[i][w];
+        o[w] = rs * (g - mg - xh * mgx);
+        acc_g[i][w] += dv[i][w] * xh;
+        acc_b[i][w] += dv[i][w];
+      }
+      V::store(dxr, idx, o);
+    }
+  }
+  if (part_g) {
+    float *pg = part_g + (size_t)blockIdx.x * cols;
+    float *pb = part_b + (size_t)blockIdx.x * cols;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv) {
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          pg[idx * W + w] = acc_g[i][w];
+          pb[idx * W + w] = acc_b[i][w];
+        }
+      }
+    }
+  }
+}
+
+// backward, any width (re-reads x and dy)
+template <bool CENTERED>
+__global__ void __launch_bounds__(kThreads)
+    norm_bwd_looped_kernel(const float *__restrict__ x,
+                           const float *__restrict__ gamma,
+                           const float *__restrict__ dy, float *__restrict__ dx,
+                           float *__restrict__ part_g, float *__restrict__ part_b,
+                           uint32_t rows, uint32_t cols, uint32_t ld,
+                           float eps) {
+  __shared__ float red[3 * 32];
+  float *pg = part_g ? part_g + (size_t)blockIdx.x * cols : nullptr;
+  float *pb = part_b ? part_b + (size_t)blockIdx.x * cols : nullptr;
+  if (pg)
+    for (uint32_t c = threadIdx.x; c < cols; c += kThreads) pg[c] = pb[c] = 0.0f;
+  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float *xr = x + (size_t)r * ld;
+    const float *gr = dy + (size_t)r * ld;
+    float mean = 0.0f;
+    if (CENTERED) {
+      float s[1] = {0.0f};
+      for (uint32_t c = threadIdx.x; c < cols; c += kThreads) s[0] += xr[c];
+      block_sum<1>(s, red);
+      mean = s[0] / (float)cols;
+    }
+    float t[3] = {0.0f, 0.0f, 0.0f};
+    for (uint32_t c = threadIdx.x; c < cols; c += kThreads) {
+      const float d = xr[c] - mean;
+      const float g = (gamma ? gamma[c] : 1.0f) * gr[c];
+      t[0] += d * d;
+      t[1] += g;
+      t[2] += g * d;
+    }
+    block_sum<3>(t, red);
+    const float rs = 1.0f / sqrtf(t[0] / (float)cols + eps);
+    const float mg = CENTERED ? t[1] / (float)cols : 0.0f;
+    const float mgx = t[2] * rs / (float)cols;
+    float *dxr = dx + (size_t)r * ld;
+    for (uint32_t c = threadIdx.x; c < cols; c += kThreads) {
+      const float xh = (xr[c] - mean) * rs;
+      const float g = (gamma ? gamma[c] : 1.0f) * gr[c];
+      dxr[c] = rs * (g - mg - xh * mgx);
+      if (pg) {
+        pg[c] += gr[c] * xh;
+        pb[c] += gr[c];
+      }
+    }
+  }
+}
+
+// out[c] = sum_{p < nparts} part[p * cols + c], fixed order
+__global__ void column_sum_kernel(const float *__restrict__ part,
+                                  float *__restrict__ out, uint32_t nparts,
+                                  uint32_t cols) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols || !out) return;
+  float s = 0.0f;
+  for (uint32_t p = 0; p < nparts; ++p) s += part[(size_t)p * cols + c];
+  out[c] = s;
+}
+
+inline bool aligned16(const void *p) {
+  return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+int pick_maxv(uint32_t nv, int limit) {
+  uint32_t per = (nv + kThreads - 1) / kThreads;
+  int m = 1;
+  while ((uint32_t)m < per) m <<= 1;
+  return m <= limit ? m : 0;  // 0: use the looped kernel
+}
+
+uint32_t row_grid(BwppCudaCtx *ctx, uint32_t rows, int ctas_per_sm) {
+  uint32_t g = (uint32_t)ctx->num_sms * (uint32_t)ctas_per_sm;
+  return rows < g ? (rows ? rows : 1) : g;
+}
+
+template <bool CENTERED>
+int norm_fwd(BwppCudaCtx *ctx, const float *x, float *y, const float *gamma,
+             const float *beta, uint32_t rows, uint32_t cols, uint32_t ld,
+             float eps) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (!x || !y || ld < cols) return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "norm fwd: bad args");
+  if (rows == 0 || cols == 0) return BWPP_CUDA_OK;
+  const bool v4 = cols % 4 == 0 && ld % 4 == 0 && aligned16(x) && aligned16(y) &&
+                  aligned16(gamma) && aligned16(beta);
+  const uint32_t nv = v4 ? cols / 4 : cols;
+  const int mv = pick_maxv(nv, kMaxVecFwd);
+  const uint32_t grid = row_grid(ctx, rows, mv > 8 ? 4 : 8);
+  cudaStream_t s = ctx->stream;
+#define BWPP_FWD(MV, V4)                                                         \
+  norm_fwd_kernel<MV, V4, CENTERED><<<grid, kThreads, 0, s>>>(x, y, gamma, beta, \
+                                                              rows, cols, ld, eps)
+  if (mv == 0) {
+    norm_fwd_looped_kernel<CENTERED><<<grid, kThreads, 0, s>>>(x, y, gamma, beta,
+                                                               rows, cols, ld, eps);
+  } else if (v4) {
+    switch (mv) {
+      case 1: BWPP_FWD(1, true); break;
+      case 2: BWPP_FWD(2, true); break;
+      case 4: BWPP_FWD(4, true); break;
+      case 8: BWPP_FWD(8, true); break;
+      default: BWPP_FWD(16, true); break;
+    }
+  } else {
+    switch (mv) {
+      case 1: BWPP_FWD(1, false); break;
+      case 2: BWPP_FWD(2, false); break;
+      case 4: BWPP_FWD(4, false); break;
+      case 8: BWPP_FWD(8, false); break;
+      default: BWPP_FWD(16, false); break;
+    }
+  }
+#undef BWPP_FWD
+  BWPP_LAUNCH_CHECK(ctx, "norm fwd");
+  return BWPP_CUDA_OK;
+}
+
+uint32_t bwd_grid(BwppCudaCtx *ctx, uint32_t rows) { return row_grid(ctx, rows, 4); }
+
+template <bool CENTERED>
+int norm_bwd(BwppCudaCtx *ctx, const float *x, const float *gamma,
+             const float *dy, float *dx, float *dgamma, float *dbeta,
+             uint32_t rows, uint32_t cols, uint32_t ld, float eps,
+             float *scratch /* may be NULL: ctx workspace */) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (!x || !dy || !dx || ld < cols)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "norm bwd: bad args");
+  if (cols == 0) return BWPP_CUDA_OK;
+  cudaStream_t s = ctx->stream;
+  if (rows == 0) {
+    if (dgamma) cudaMemsetAsync(dgamma, 0, sizeof(float) * cols, s);
+    if (dbeta) cudaMemsetAsync(dbeta, 0, sizeof(float) * cols, s);
+    return BWPP_CUDA_OK;
+  }
+  const uint32_t grid = bwd_grid(ctx, rows);
+  float *pg = nullptr, *pb = nullptr;
+  if (dgamma || dbeta) {
+    if (!scratch) {
+      scratch = (float *)bwpp_ctx_workspace(ctx, sizeof(float) * 2 * (size_t)grid * cols);
+      if (!scratch) return BWPP_CUDA_ERR_NOMEM;
+    }
+    pg = scratch;
+    pb = scratch + (size_t)grid * cols;
+  }
+  const bool v4 = cols % 4 == 0 && ld % 4 == 0 && aligned16(x) && aligned16(dy) &&
+                  aligned16(dx) && aligned16(gamma);
+  const uint32_t nv = v4 ? cols / 4 : cols;
+  const int mv = pick_maxv(nv, kMaxVecBwd);
+#define BWPP_BWD(MV, V4)                                                     \
+  norm_bwd_kernel<MV, V4, CENTERED><<<grid, kThreads, 0, s>>>(               \
+      x, gamma, dy, dx, pg, pb, rows, cols, ld, eps)
+  if (mv == 0) {
+    norm_bwd_looped_kernel<CENTERED><<<grid, kThreads, 0, s>>>(
+        x, gamma, dy, dx, pg, pb, rows, cols, ld, eps);
+  } else if (v4) {
+    switch (mv) {
+      case 1: BWPP_BWD(1, true); break;
+      case 2: BWPP_BWD(2, true); break;
+      case 4: BWPP_BWD(4, true); break;
+      default: BWPP_BWD(8, true); break;
+    }
+  } else {
+    switch (mv) {
+      case 1: BWPP_BWD(1, false); break;
+      case 2: BWPP_BWD(2, false); break;
+      case 4: BWPP_BWD(4, false); break;
+      default: BWPP_BWD(8, false); break;
+    }
+  }
+#undef BWPP_BWD
+  BWPP_LAUNCH_CHECK(ctx, "norm bwd");
+  if (pg) {
+    const uint32_t cb = (cols + 255) / 256;
+    column_sum_kernel<<<cb, 256, 0, s>>>(pg, dgamma, grid, cols);
+    column_sum_kernel<<<cb, 256, 0, s>>>(pb, dbeta, grid, cols);
+    BWPP_LAUNCH_CHECK(ctx, "norm bwd column sum");
+  }
+  return BWPP_CUDA_OK;
+}
+
+}  // namespace
+
+// Backward with caller-provided scratch (2 * grid * cols floats); used by the
+// tiny_model step to keep scratch inside its arena.
+int bwpp_norm_bwd_with_scratch(BwppCudaCtx *ctx, int centered, const float *x,
+                               const float *gamma, const float *dy, float *dx,
+                               float *dgamma, float *dbeta, uint32_t rows,
+                               uint32_t cols, uint32_t ld, float eps,
+                               float *scratch) {
+  return centered ? norm_bwd<true>(ctx, x, gamma, dy, dx, dgamma, dbeta, rows,
+                                   cols, ld, eps, scratch)
+                  : norm_bwd<false>(ctx, x, gamma, dy, dx, dgamma, dbeta, rows,
+                                    cols, ld, eps, scratch);
+}
+
+extern "C" {
+
+size_t bwpp_cuda_norm_bwd_workspace_size(BwppCudaCtx *ctx, uint32_t rows,
+                                         uint32_t cols) {
+  if (!ctx) return 0;
+  return sizeof(float) * 2 * (size_t)bwd_grid(ctx, rows) * cols;
+}
+
+int bwpp_cuda_rmsnorm_fwd_f32(BwppCudaCtx *ctx, const float *x, float *y,
+                              const float *gamma, const float *beta,
+                              uint32_t rows, uint32_t cols, uint32_t ld,
+                              float eps) {
+  return norm_fwd<false>(ctx, x, y, gamma, beta, rows, cols, ld, eps);
+}
+
+int bwpp_cuda_layernorm_fwd_f32(BwppCudaCtx *ctx, const float *x, float *y,
+                                const float *gamma, const float *beta,
+                                uint32_t rows, uint32_t cols, uint32_t ld,
+                                float eps) {
+  return norm_fwd<true>(ctx, x, y, gamma, beta, rows, cols, ld, eps);
+}
+
+int bwpp_cuda_rmsnorm_bwd_f32(BwppCudaCtx *ctx, const float *x,
+                              const float *gamma, const float *dy, float *dx,
+                              float *dgamma, float *dbeta, uint32_t rows,
+                              uint32_t cols, uint32_t ld, float eps) {
+  return norm_bwd<false>(ctx, x, gamma, dy, dx, dgamma, dbeta, rows, cols, ld,
+                         eps, nullptr);
+}
+
+int bwpp_cuda_layernorm_bwd_f32(BwppCudaCtx *ctx, const float *x,
+                                const float *gamma, const float *dy, float *dx,
+                                float *dgamma, float *dbeta, uint32_t rows,
+                                uint32_t cols, uint32_t ld, float eps) {
+  return norm_bwd<true>(ctx, x, gamma, dy, dx, dgamma, dbeta, rows, cols, ld,
+                        eps, nullptr);
+}
+
+}  // extern "C"

@@ -1,0 +1,292 @@
+/*
+ * bwpp_cuda.h -- C ABI of the BW++ B200 (sm_100a) runtime, runtime/cuda.
+ *
+ * Drop-in boundary for the reference project's kernel runtimes:
+ *   - runtime/cpu/bwpp_cpu_ref.h:6-58     (bwpp_cpu_*_f32 entry points)
+ *   - runtime/metal/dispatch_stub.h:9-74  (param structs + dispatch calls)
+ *   - runtime/core/arena.h:6-15, tensor.h:7-25 (arena / tensor metadata)
+ *   - compiler/include/bwpp.h:8-11        (BwppStatus: 0 ok, 1 error)
+ *
+ * Plain C, no CUDA or torch types in any signature: streams are passed as
+ * `void *` (a cudaStream_t), every buffer is a plain pointer.
+ *
+ * Three families of entry points:
+ *   1. ctx entry points (bwpp_cuda_*(BwppCudaCtx *ctx, ...)): device
+ *      pointers, asynchronous on the ctx's stream, return a status code.
+ *      bwpp_cuda_sync(ctx) waits and reports device-side errors (a bounded
+ *      wait that expired inside a kernel comes back as
+ *      BWPP_CUDA_ERR_TIMEOUT).
+ *   2. exact mirrors of the CPU reference signatures (void, synchronous).
+ *      Pointers may be host or device memory; host buffers are staged through
+ *      the device.  bwpp_cuda_last_status() gives the status of the calling
+ *      thread's last mirror call (the reference returns nothing and silently
+ *      ignores NULL inputs; so do these).
+ *   3. mirrors of the Metal dispatch calls with the same param structs.
+ *
+ * Numerics: contractions (matmul, attention) run on tcgen05 tensor cores with
+ * bf16 operands and fp32 accumulation; fp32 inputs of the mirrors are rounded
+ * to bf16 (nearest even) on the device first.  Norms, softmax and reduce_max
+ * run in fp32.
+ */
+#ifndef BWPP_CUDA_H
+#define BWPP_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---- status codes (0 / 1 agree with BwppStatus, compiler/include/bwpp.h:8-11) */
+#define BWPP_CUDA_OK 0
+#define BWPP_CUDA_ERR 1             /* generic failure */
+#define BWPP_CUDA_ERR_ARG 2         /* invalid argument (NULL, size, alignment) */
+#define BWPP_CUDA_ERR_CUDA 3        /* CUDA runtime / launch error */
+#define BWPP_CUDA_ERR_TIMEOUT 4     /* a bounded device-side wait expired */
+#define BWPP_CUDA_ERR_NOMEM 5       /* device allocation failed */
+#define BWPP_CUDA_ERR_UNSUPPORTED 6 /* shape / option not supported */
+
+/* ---- arena + tensor metadata ------------------------------------------- */
+
+/* Same layout as BwppArena (runtime/core/arena.h:6-10); a BwppArena* may be
+ * passed where a BwppCudaArena* is expected.  `buffer` is device memory. */
+typedef struct {
+  unsigned char *buffer;
+  size_t capacity;
+  size_t offset;
+} BwppCudaArena;
+
+/* Same enumerators / layout as runtime/core/tensor.h:7-25; `buffer` holds a
+ * device pointer (typically from bwpp_cuda_arena_alloc). */
+typedef enum {
+  BWPP_CUDA_DTYPE_F16 = 0,
+  BWPP_CUDA_DTYPE_BF16 = 1,
+  BWPP_CUDA_DTYPE_F32 = 2
+} BwppCudaDType;
+
+typedef enum {
+  BWPP_CUDA_LAYOUT_ROW_MAJOR = 0,
+  BWPP_CUDA_LAYOUT_COL_MAJOR = 1
+} BwppCudaLayout;
+
+typedef struct {
+  BwppCudaDType dtype;
+  BwppCudaLayout layout;
+  uint32_t rank;
+  uint64_t shape[4];
+  uint64_t stride[4];
+  void *buffer;
+} BwppCudaTensor;
+
+/* Replaces bwpp_arena_init (runtime/core/arena.c:9-17): ONE cudaMalloc of
+ * `capacity` bytes on `device`.  Returns 1 on success, 0 on failure (the
+ * reference's convention). */
+int bwpp_cuda_arena_init(BwppCudaArena *arena, size_t capacity, int device);
+/* Same bump semantics as bwpp_arena_alloc (runtime/core/arena.c:23-31):
+ * `align` a power of two (0 means 1), NULL when the arena is full. */
+void *bwpp_cuda_arena_alloc(BwppCudaArena *arena, size_t size, size_t align);
+/* runtime/core/arena.c:19-21 */
+void bwpp_cuda_arena_reset(BwppCudaArena *arena);
+/* runtime/core/arena.c:33-38, with cudaFree */
+void bwpp_cuda_arena_destroy(BwppCudaArena *arena);
+
+/* ---- context ------------------------------------------------------------ */
+
+typedef struct BwppCudaCtx BwppCudaCtx;
+
+/* New context on `device`, launching on `stream` (a cudaStream_t; NULL means
+ * the legacy default stream).  One context per host thread per GPU. */
+int bwpp_cuda_ctx_create(BwppCudaCtx **out, int device, void *stream);
+int bwpp_cuda_ctx_destroy(BwppCudaCtx *ctx);
+int bwpp_cuda_ctx_set_stream(BwppCudaCtx *ctx, void *stream);
+/* Hands the context caller-owned device scratch (e.g. an arena slice).  With
+ * a workspace set the context never allocates; a call that needs more than
+ * `bytes` fails with BWPP_CUDA_ERR_NOMEM.  NULL / 0 returns to ctx-owned
+ * scratch. */
+int bwpp_cuda_ctx_set_workspace(BwppCudaCtx *ctx, void *device_ptr,
+                                size_t bytes);
+/* Scratch bytes the norm backward passes need for `rows` x `cols`. */
+size_t bwpp_cuda_norm_bwd_workspace_size(BwppCudaCtx *ctx, uint32_t rows,
+                                         uint32_t cols);
+/* Waits for the ctx's stream; returns the first device-side error recorded
+ * since the previous sync (then clears it), or a CUDA error. */
+int bwpp_cuda_sync(BwppCudaCtx *ctx);
+const char *bwpp_cuda_status_string(int status);
+const char *bwpp_cuda_ctx_last_error(const BwppCudaCtx *ctx);
+int bwpp_cuda_device_count(void);
+/* Failure-path self test (no reference counterpart): launches a kernel whose
+ * bounded device wait never completes and expires after `limit_ms` (1..2000);
+ * the next bwpp_cuda_sync returns BWPP_CUDA_ERR_TIMEOUT and the context stays
+ * usable.  Nothing faults or traps. */
+int bwpp_cuda_selftest_wait_timeout(BwppCudaCtx *ctx, uint32_t limit_ms);
+
+/* ---- 1. ctx entry points (device pointers, async) ---------------------- */
+
+/* C[M,N] = A[M,K] * B[K,N] (+ bias[N] if apply_bias && bias) (then SiLU if
+ * apply_silu), row-major with leading dims; A, B bf16 bits, bias / C fp32.
+ * The fused matmul+bias+SiLU and matmul+bias(+reshape) epilogues of
+ * runtime/cpu/bwpp_cpu_ref.c:8-35 and compiler/codegen_metal.c:392-434
+ * (bias before SiLU).  tcgen05 path when lda, ldb are multiples of 8, ldc of
+ * 4 and the pointers 16-byte aligned; otherwise a CUDA-core kernel. */
+int bwpp_cuda_matmul_bf16(BwppCudaCtx *ctx, const uint16_t *a,
+                          const uint16_t *b, float *c, uint32_t M, uint32_t N,
+                          uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
+                          const float *bias, int apply_silu, int apply_bias);
+
+/* O = softmax(scale * Q K^T [+ causal mask]) V on contiguous [B,H,S,D]
+ * tensors: Q [B,H,Sq,D], K and V [B,H,Skv,D] bf16 bits, O [B,H,Sq,D] fp32.
+ * causal: key n visible to query m iff n <= m.  Single-pass online softmax
+ * (compiler/codegen_metal.c:534-548); the reference's 2-D, unscaled, unmasked
+ * form (runtime/cpu/bwpp_cpu_ref.c:92-144) is B=H=1, scale=1, causal=0.
+ * tcgen05 path for D in {64, 128}; other D up to 256 on CUDA cores. */
+int bwpp_cuda_attention_bf16(BwppCudaCtx *ctx, const uint16_t *q,
+                             const uint16_t *k, const uint16_t *v, float *o,
+                             uint32_t B, uint32_t H, uint32_t Sq, uint32_t Skv,
+                             uint32_t D, float scale, int causal);
+
+/* RMSNorm forward, runtime/cpu/bwpp_cpu_ref.c:63-90: y = x / sqrt(mean(x^2) +
+ * eps) * gamma + beta; gamma / beta may be NULL. */
+int bwpp_cuda_rmsnorm_fwd_f32(BwppCudaCtx *ctx, const float *x, float *y,
+                              const float *gamma, const float *beta,
+                              uint32_t rows, uint32_t cols, uint32_t ld,
+                              float eps);
+
+/* RMSNorm backward (rule of compiler/graph_ir.c:1735-1789):
+ * dx = r*(g - xhat*mean(g*xhat)), g = gamma*dy, r = 1/sqrt(mean(x^2)+eps),
+ * dgamma = sum_rows dy*xhat, dbeta = sum_rows dy.  dgamma / dbeta may be
+ * NULL (not computed); gamma NULL means 1.  Uses ctx scratch
+ * (bwpp_cuda_norm_bwd_workspace_size). */
+int bwpp_cuda_rmsnorm_bwd_f32(BwppCudaCtx *ctx, const float *x,
+                              const float *gamma, const float *dy, float *dx,
+                              float *dgamma, float *dbeta, uint32_t rows,
+                              uint32_t cols, uint32_t ld, float eps);
+
+/* LayerNorm forward (no reference counterpart; signature follows
+ * bwpp_cpu_rmsnorm_f32): y = (x - mean) * rstd * gamma + beta. */
+int bwpp_cuda_layernorm_fwd_f32(BwppCudaCtx *ctx, const float *x, float *y,
+                                const float *gamma, const float *beta,
+                                uint32_t rows, uint32_t cols, uint32_t ld,
+                                float eps);
+
+/* LayerNorm backward: dx = rstd*(g - mean(g) - xhat*mean(g*xhat)),
+ * dgamma = sum_rows dy*xhat, dbeta = sum_rows dy. */
+int bwpp_cuda_layernorm_bwd_f32(BwppCudaCtx *ctx, const float *x,
+                                const float *gamma, const float *dy, float *dx,
+                                float *dgamma, float *dbeta, uint32_t rows,
+                                uint32_t cols, uint32_t ld, float eps);
+
+/* Row max over the last dim and the FIRST index attaining it (strict '>'
+ * scan from -INF as in runtime/cpu/bwpp_cpu_ref.c:174-181; index 0 when no
+ * element exceeds -INF).  maxv or argmax may be NULL. */
+int bwpp_cuda_reduce_max_fwd_f32(BwppCudaCtx *ctx, const float *x, float *maxv,
+                                 uint32_t *argmax, uint32_t rows,
+                                 uint32_t cols, uint32_t ld);
+
+/* Argmax-routed gradient: dx[r, argmax[r]] = dy[r], 0 elsewhere (the
+ * reduce_max rule of compiler/graph_ir.c:1798-1821 with first-index ties). */
+int bwpp_cuda_reduce_max_bwd_f32(BwppCudaCtx *ctx, const uint32_t *argmax,
+                                 const float *dy, float *dx, uint32_t rows,
+                                 uint32_t cols, uint32_t ld);
+
+/* runtime/cpu/bwpp_cpu_ref.c:146-190: mask = 1 at EVERY position equal to the
+ * max along `axis` (0: down columns, else along rows), dense rows x cols. */
+int bwpp_cuda_reduce_max_mask_ex(BwppCudaCtx *ctx, const float *x, float *mask,
+                                 uint32_t rows, uint32_t cols, int axis);
+
+/* runtime/cpu/bwpp_cpu_ref.c:192-219: dx = mask * dy[axis == 0 ? c : r]. */
+int bwpp_cuda_reduce_max_grad_ex(BwppCudaCtx *ctx, const float *mask,
+                                 const float *dy, float *dx, uint32_t rows,
+                                 uint32_t cols, int axis);
+
+/* runtime/cpu/bwpp_cpu_ref.c:37-61: row softmax, 1/sum guarded at 0. */
+int bwpp_cuda_softmax_fwd_f32(BwppCudaCtx *ctx, const float *x, float *y,
+                              uint32_t rows, uint32_t cols, uint32_t ld);
+
+/* fp32 -> bf16 bits, round to nearest even (dst dense rows x cols, src with
+ * leading dim ld_src). */
+int bwpp_cuda_cast_f32_bf16(BwppCudaCtx *ctx, const float *src, uint16_t *dst,
+                            uint32_t rows, uint32_t cols, uint32_t ld_src);
+
+/* ---- 2. mirrors of runtime/cpu/bwpp_cpu_ref.h:6-58 ---------------------- */
+/* Same argument lists; host or device pointers; synchronous; the calling
+ * thread's context on the current device is created on first use. */
+
+void bwpp_cuda_matmul_f32(const float *a, const float *b, float *c, uint32_t M,
+                          uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                          uint32_t ldc, const float *bias, int apply_silu,
+                          int apply_bias);
+void bwpp_cuda_softmax_f32(const float *x, float *y, uint32_t rows,
+                           uint32_t cols, uint32_t ld);
+void bwpp_cuda_rmsnorm_f32(const float *x, float *y, const float *gamma,
+                           const float *beta, uint32_t rows, uint32_t cols,
+                           uint32_t ld, float eps);
+void bwpp_cuda_attention_f32(const float *q, const float *k, const float *v,
+                             float *o, uint32_t M, uint32_t N, uint32_t K,
+                             uint32_t D, uint32_t ldq, uint32_t ldk,
+                             uint32_t ldv, uint32_t ldo);
+void bwpp_cuda_reduce_max_mask_f32(const float *x, float *mask, uint32_t rows,
+                                   uint32_t cols, int axis);
+void bwpp_cuda_reduce_max_grad_f32(const float *mask, const float *dy,
+                                   float *dx, uint32_t rows, uint32_t cols,
+                                   int axis);
+/* Status of the calling thread's last mirror call (BWPP_CUDA_OK when none). */
+int bwpp_cuda_last_status(void);
+
+/* ---- 3. mirrors of runtime/metal/dispatch_stub.h:9-74 -------------------- */
+/* Param structs with the Metal layouts.  Buffers are device pointers; A/B/Q/
+ * K/V are bf16 (the Metal kernels take half: an f16 variant is not built),
+ * C/O/bias/x/y/gamma/beta fp32.  `source` is the compiler output text: like
+ * the Metal shim (dispatch_stub.m:74-79) a call is a no-op returning
+ * BWPP_CUDA_OK unless `source` carries the matching `bwpp.meta:` kernel tag;
+ * `bwpp.meta: epilogue=add|silu|add_silu` selects the matmul epilogue. */
+
+typedef struct {
+  uint32_t M, N, K, lda, ldb, ldc;
+} BwppCudaMatmulParams;
+
+typedef struct {
+  uint32_t rows, cols, ld;
+} BwppCudaSoftmaxParams;
+
+typedef struct {
+  uint32_t rows, cols, ld;
+  float eps;
+} BwppCudaRmsnormParams;
+
+typedef struct {
+  uint32_t M, N, K, D, ldq, ldk, ldv, ldo;
+} BwppCudaAttentionParams;
+
+/* runtime/metal/dispatch_stub.h:42-49 */
+int bwpp_cuda_dispatch_matmul(BwppCudaCtx *ctx, const uint16_t *a,
+                              const uint16_t *b, float *c, const float *bias,
+                              BwppCudaMatmulParams params, const char *source);
+/* runtime/metal/dispatch_stub.h:51-56 */
+int bwpp_cuda_dispatch_softmax(BwppCudaCtx *ctx, const float *x, float *y,
+                               BwppCudaSoftmaxParams params,
+                               const char *source);
+/* runtime/metal/dispatch_stub.h:58-65 */
+int bwpp_cuda_dispatch_rmsnorm(BwppCudaCtx *ctx, const float *x,
+                               const float *gamma, const float *beta, float *y,
+                               BwppCudaRmsnormParams params,
+                               const char *source);
+/* runtime/metal/dispatch_stub.h:67-74 (2-D, unscaled, unmasked; ld strides) */
+int bwpp_cuda_dispatch_attention(BwppCudaCtx *ctx, const uint16_t *q,
+                                 const uint16_t *k, const uint16_t *v, float *o,
+                                 BwppCudaAttentionParams params,
+                                 const char *source);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BWPP_CUDA_H */

@@ -1,0 +1,119 @@
+"""Fused matmul (+bias, +SiLU) on the GPU vs the CPU oracle.
+
+The oracle runs on the fp32 upcast of the exact bf16 operands the kernel sees.
+Tolerance (north star): relative Frobenius error <= 1e-2 against the fp32
+reference.  fp32 accumulation of exact bf16 products lands near 1e-6, so a
+second, tighter bound (2e-4) is asserted as a bug detector.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from conftest import dev, empty_f32, host, rel_fro
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+TIGHT = 2e-4
+
+
+def operands(rng, M, N, K, lda, ldb, scale=1.0):
+    a = (scale * rng.standard_normal((M, lda))).astype(np.float32)
+    b = (scale * rng.standard_normal((K, ldb))).astype(np.float32)
+    a16, b16 = O.f32_to_bf16(a), O.f32_to_bf16(b)
+    af = np.ascontiguousarray(O.bf16_to_f32(a16)[:, :K])
+    bf = np.ascontiguousarray(O.bf16_to_f32(b16)[:, :N])
+    return a16, b16, af, bf
+
+
+def run(ctx, a16, b16, M, N, K, lda, ldb, ldc, bias, silu, add):
+    cd = empty_f32(M, ldc)
+    ctx.matmul_bf16(dev(a16), dev(b16), cd, M, N, K, lda, ldb, ldc,
+                    None if bias is None else dev(bias), silu, add)
+    ctx.sync()
+    return host(cd)
+
+
+# tensor-core path: lda, ldb multiples of 8, ldc of 4
+TC_SHAPES = [(128, 256, 64), (1, 8, 8), (3, 40, 24), (129, 264, 72), (300, 520, 1000),
+             (256, 512, 4096), (1000, 1024, 200), (17, 11008, 256), (1024, 1024, 4096)]
+
+
+@pytest.mark.parametrize("M,N,K", TC_SHAPES)
+@pytest.mark.parametrize("silu,add", [(0, 0), (1, 1), (0, 1), (1, 0)])
+def test_matmul_tcgen05(ctx, M, N, K, silu, add):
+    rng = np.random.default_rng(M * 31 + N * 7 + K)
+    a16, b16, af, bf = operands(rng, M, N, K, K, N)
+    bias = rng.uniform(-0.1, 0.1, N).astype(np.float32)
+    ref = O.matmul(af, bf, bias, silu, add)
+    out = run(ctx, a16, b16, M, N, K, K, N, N, bias, silu, add)
+    err = rel_fro(out, ref)
+    assert err <= TOL and err <= TIGHT, err
+
+
+def test_matmul_tcgen05_leading_dims(ctx):
+    # padded rows: lda > K, ldb > N, ldc > N; the padding of C stays untouched
+    M, N, K, lda, ldb, ldc = 130, 200, 136, 144, 208, 204
+    rng = np.random.default_rng(5)
+    a16, b16, af, bf = operands(rng, M, N, K, lda, ldb)
+    bias = rng.uniform(-0.1, 0.1, N).astype(np.float32)
+    out = run(ctx, a16, b16, M, N, K, lda, ldb, ldc, bias, 1, 1)
+    assert rel_fro(out[:, :N], O.matmul(af, bf, bias, 1, 1)) <= TIGHT
+    assert np.isnan(out[:, N:]).all()
+
+
+@pytest.mark.parametrize("M,N,K,lda", [(4, 4, 4, 4), (7, 9, 5, 5), (33, 17, 0, 1)])
+def test_matmul_cuda_core_fallback(ctx, M, N, K, lda):
+    # shapes TMA cannot describe (pitch not a multiple of 16 B, K == 0)
+    rng = np.random.default_rng(M + N + K)
+    a16, b16, af, bf = operands(rng, M, N, K, max(lda, 1), N)
+    bias = rng.uniform(-0.1, 0.1, N).astype(np.float32)
+    out = run(ctx, a16, b16, M, N, K, max(lda, 1), N, N, bias, 1, 1)
+    assert rel_fro(out, O.matmul(af, bf, bias, 1, 1)) <= TIGHT
+
+
+def test_matmul_reference_case(ctx):
+    # runtime/cpu/test_metal_parity.c:86-131: 4x4x4 ramp, bias 0.01*(i+1)
+    a = ((np.arange(16) + 1) * np.float32(0.1)).astype(np.float32).reshape(4, 4)
+    b = ((np.arange(16) + 1) * np.float32(0.05)).astype(np.float32).reshape(4, 4)
+    bias = (0.01 * np.arange(1, 5)).astype(np.float32)
+    a16, b16 = O.f32_to_bf16(a), O.f32_to_bf16(b)
+    ref = O.matmul(O.bf16_to_f32(a16), O.bf16_to_f32(b16), bias, 1, 1)
+    out = run(ctx, a16, b16, 4, 4, 4, 4, 4, 4, bias, 1, 1)
+    assert np.max(np.abs(out - ref)) <= 1e-4
+
+
+def test_matmul_repeated_calls_are_deterministic(ctx):
+    rng = np.random.default_rng(9)
+    a16, b16, _, _ = operands(rng, 512, 768, 1024, 1024, 768)
+    outs = [run(ctx, a16, b16, 512, 768, 1024, 1024, 768, 768, None, 0, 0) for _ in range(3)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+
+
+def test_config2_full_size_sampled_rows(ctx):
+    """X[8192x4096] W[4096x11008] + b, SiLU: 64 sampled rows against the oracle,
+    plus size-independent properties on the full problem."""
+    M, K, N = 8192, 4096, 11008
+    g = torch.Generator(device="cuda").manual_seed(2000)
+    x = (torch.randn(M, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    w = (torch.randn(K, N, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.rand(N, device="cuda", generator=g) * 0.2 - 0.1)
+    c = torch.empty(M, N, device="cuda")
+    ctx.matmul_bf16(x, w, c, M, N, K, K, N, N, b, 1, 1)
+    ctx.sync()
+    rows = np.unique(np.concatenate([[0, 1, 127, 128, M - 1],
+                                     np.random.default_rng(1).integers(0, M, 59)]))
+    xs = x[rows].float().cpu().numpy()
+    wf = w.float().cpu().numpy()
+    ref = O.matmul(np.ascontiguousarray(xs), np.ascontiguousarray(wf), b.cpu().numpy(), 1, 1)
+    assert rel_fro(c[rows].cpu().numpy(), ref) <= TIGHT
+    # size-independent properties on the full shape, no epilogue:
+    # homogeneity C(2X) == 2 C(X) and row permutation C(PX) == P C(X), bit-exact
+    perm = torch.randperm(M, device="cuda", generator=g)
+    c1, c2, c3 = (torch.empty(M, N, device="cuda") for _ in range(3))
+    ctx.matmul_bf16(x, w, c1, M, N, K, K, N, N, None, 0, 0)
+    ctx.matmul_bf16((x.float() * 2).to(torch.bfloat16), w, c2, M, N, K, K, N, N, None, 0, 0)
+    ctx.matmul_bf16(x[perm].contiguous(), w, c3, M, N, K, K, N, N, None, 0, 0)
+    ctx.sync()
+    assert torch.equal(c2, 2 * c1)
+    assert torch.equal(c3, c1[perm])
