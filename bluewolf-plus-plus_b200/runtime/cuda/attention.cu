@@ -1,4 +1,6 @@
-// Attention entry point: O = softmax(scale * Q K^T [causal]) V on [B,H,S,D].
+// Attention entry point: O = softmax(scale * Q K^T [causal]) V on [B,H,S,D]:
+// dispatch between the tcgen05 kernel (attention_tc.cu) and the CUDA-core
+// kernel (attention_simt.cu).
 #include "bwpp_cuda_internal.cuh"
 
 int bwpp_attention_simt_launch(BwppCudaCtx *ctx, const uint16_t *q,
@@ -9,14 +11,27 @@ int bwpp_attention_simt_launch(BwppCudaCtx *ctx, const uint16_t *q,
                                uint32_t ldq, uint32_t ldk, uint32_t ldv,
                                uint32_t ldo, float scale, int causal);
 
+int bwpp_attention_tc_launch(BwppCudaCtx *ctx, const uint16_t *q,
+                             const uint16_t *k, const uint16_t *v, float *o,
+                             uint32_t BH, uint32_t Sq, uint32_t Skv, uint32_t D,
+                             float scale, int causal);
+
 // Chooses the kernel for a batch of BH independent (Sq x Kd, Skv x Kd,
-// Skv x Dv) problems with the given strides.
+// Skv x Dv) problems with the given strides: the tcgen05 kernel for dense
+// [BH, S, D] tensors with D in {64, 128}, the CUDA-core kernel otherwise.
 int bwpp_attention_launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
                           const uint16_t *v, float *o, uint32_t BH, uint32_t Sq,
                           uint32_t Skv, uint32_t Kd, uint32_t Dv, uint64_t q_bh,
                           uint64_t k_bh, uint64_t v_bh, uint64_t o_bh,
                           uint32_t ldq, uint32_t ldk, uint32_t ldv, uint32_t ldo,
                           float scale, int causal) {
+  const bool dense = Kd == Dv && ldq == Kd && ldk == Kd && ldv == Dv && ldo == Dv &&
+                     q_bh == (uint64_t)Sq * Kd && k_bh == (uint64_t)Skv * Kd &&
+                     v_bh == (uint64_t)Skv * Dv && o_bh == (uint64_t)Sq * Dv;
+  if (dense && (Kd == 64 || Kd == 128) && Skv > 0) {
+    int rc = bwpp_attention_tc_launch(ctx, q, k, v, o, BH, Sq, Skv, Kd, scale, causal);
+    if (rc != BWPP_CUDA_ERR_UNSUPPORTED) return rc;
+  }
   return bwpp_attention_simt_launch(ctx, q, k, v, o, BH, Sq, Skv, Kd, Dv, q_bh,
                                     k_bh, v_bh, o_bh, ldq, ldk, ldv, ldo, scale,
                                     causal);

@@ -1,0 +1,460 @@
+// Attention forward on sm_100a tensor cores, single pass with online softmax.
+//
+//   O[bh, m, :] = sum_n softmax_n(scale * q_m . k_n [n <= m if causal]) v_n
+//
+// One CTA owns 256 query rows of one (batch, head) as two 128-row tiles A and
+// B that ping-pong: while the softmax warps of one tile turn its S into P, the
+// tensor core works on the other tile.  Per 128-key block j:
+//   S_X = Q_X K_j^T          tcgen05 M=128 N=128 K=16 (Q, K K-major, bf16)
+//   P_X = exp2(S_X*c - m)    softmax warps, one thread per row, P -> smem bf16
+//   O_X += P_X V_j           tcgen05 M=128 N=D K=16 (P K-major, V MN-major)
+// S_A, S_B, O_A, O_B live in TMEM (4 x 128 columns for D = 128).  The running
+// max only moves when it grows by more than 2^8 (log2 domain), so O is
+// rescaled (tcgen05.ld / st) rarely; P <= 256 stays exact enough in bf16.
+//
+// Warp roles (320 threads): warp 0 TMA producer (Q once; K double-buffered,
+// V single-buffered, 3-D tensor maps so ragged S zero-fills per head),
+// warp 1 TMEM allocator + single-thread MMA issuer, warps 2-5 softmax of
+// tile A, warps 6-9 softmax of tile B (warp w reads TMEM lanes 32*(w%4)..).
+// MMA issue order per block: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1), so one
+// tile's softmax always overlaps the other tile's MMAs.
+//
+// Every wait is bounded (BWPP_WAIT_LIMIT_NS); on expiry the kernel records
+// BWPP_CUDA_ERR_TIMEOUT, unwinds, frees TMEM and returns.
+#include "bwpp_cuda_internal.cuh"
+
+namespace {
+
+constexpr int BM = 128;  // rows per Q tile (two tiles per CTA)
+constexpr int BN = 128;  // keys per K/V block
+constexpr int BOX = 128 * 64 * 2;  // one TMA box: 128 rows x 64 bf16 (16 KB)
+constexpr int P_TILE = BM * BN * 2;  // 32 KB
+constexpr int THREADS = 320;
+
+template <int D>
+struct Cfg {
+  static constexpr int BOXES = D / 64;
+  static constexpr int TILE = BOXES * BOX;  // Q / K / V tile bytes
+  static constexpr int OFF_Q = 0;           // 2 tiles
+  static constexpr int OFF_K = 2 * TILE;    // 2 stages
+  static constexpr int OFF_V = 4 * TILE;    // 1 stage
+  static constexpr int OFF_P = 5 * TILE;    // 2 tiles
+  static constexpr int OFF_BAR = OFF_P + 2 * P_TILE;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr uint32_t TMEM_S = 0;        // S_A at 0, S_B at 128
+  static constexpr uint32_t TMEM_O = 2 * BN;   // O_A at 256, O_B at 256 + D
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t IDESC_S = make_idesc_bf16_f32(BM, BN, 0, 0);
+  static constexpr uint32_t IDESC_PV = make_idesc_bf16_f32(BM, D, 0, 1);
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[2], k_empty[2];
+  uint64_t v_full, v_empty;
+  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  uint64_t drain;
+  uint32_t tmem;
+  int abort_flag;
+};
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map,
+                                            uint64_t *bar, int32_t x, int32_t y,
+                                            int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::"
+      "bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Number of 128-key blocks tile X (first row r0) needs.
+__device__ __forceinline__ int blocks_for(uint32_t r0, uint32_t Sq, uint32_t Skv,
+                                          int causal) {
+  if (r0 >= Sq) return 0;
+  int n = (int)((Skv + BN - 1) / BN);
+  if (causal) {
+    const uint32_t last = min(r0 + BM - 1, Sq - 1);
+    n = min(n, (int)(last / BN) + 1);
+  }
+  return n;
+}
+
+template <int D>
+__global__ void __maxnreg__(200)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                        const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV,
+                        float *__restrict__ out, uint32_t BH, uint32_t Sq,
+                        uint32_t Skv, float scale_log2, int causal,
+                        uint32_t pairs, int *status) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  Bars *bar = reinterpret_cast<Bars *>(smem + C::OFF_BAR);
+  volatile int *abort_flag = &bar->abort_flag;
+
+  // heaviest (latest) query blocks first: better tail for causal masks
+  const uint32_t lin = blockIdx.x;
+  const uint32_t pair = pairs - 1 - lin / BH;
+  const uint32_t bh = lin % BH;
+  const uint32_t q0 = pair * 2 * BM;
+  const int nblk[2] = {blocks_for(q0, Sq, Skv, causal),
+                       blocks_for(q0 + BM, Sq, Skv, causal)};
+  const int n = max(nblk[0], nblk[1]);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->k_full[s], 1);
+      mbar_init(&bar->k_empty[s], 1);
+      mbar_init(&bar->s_full[s], 1);
+      mbar_init(&bar->s_free[s], 4);
+      mbar_init(&bar->p_full[s], 4);
+      mbar_init(&bar->pv_done[s], 1);
+    }
+    mbar_init(&bar->v_full, 1);
+    mbar_init(&bar->v_empty, 1);
+    mbar_init(&bar->drain, 1);
+    bar->abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bar->tmem, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem;
+
+  if (warp == 0) {
+    // ----------------------------------------------------------- producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bar->q_full, 2 * C::TILE);
+      for (int X = 0; X < 2; ++X)
+        for (int b = 0; b < C::BOXES; ++b)
+          tma_load_3d(smem + C::OFF_Q + X * C::TILE + b * BOX, &tmQ, &bar->q_full,
+                      b * 64, (int32_t)(q0 + X * BM), (int32_t)bh);
+      auto load_k = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&bar->k_empty[s], ((j >> 1) & 1) ^ 1, status)) return false;
+        mbar_arrive_expect_tx(&bar->k_full[s], C::TILE);
+        for (int b = 0; b < C::BOXES; ++b)
+          tma_load_3d(smem + C::OFF_K + s * C::TILE + b * BOX, &tmK, &bar->k_full[s],
+                      b * 64, j * BN, (int32_t)bh);
+        return true;
+      };
+      bool ok = n > 0 ? load_k(0) : true;
+      for (int j = 0; j < n && ok && !*abort_flag; ++j) {
+        if (j + 1 < n && !load_k(j + 1)) { ok = false; break; }
+        if (!mbar_wait(&bar->v_empty, (j & 1) ^ 1, status)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bar->v_full, C::TILE);
+        for (int b = 0; b < C::BOXES; ++b)
+          tma_load_3d(smem + C::OFF_V + b * BOX, &tmV, &bar->v_full, b * 64, j * BN,
+                      (int32_t)bh);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(&bar->q_full, 0, status);
+      const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
+      const uint32_t k_addr = smem_u32(smem + C::OFF_K);
+      const uint32_t v_addr = smem_u32(smem + C::OFF_V);
+      const uint32_t p_addr = smem_u32(smem + C::OFF_P);
+      // S_X = Q_X K_j^T into TMEM columns X * 128
+      auto issue_s = [&](int X, int j) {
+        const uint32_t qa = q_addr + X * C::TILE, ka = k_addr + (j & 1) * C::TILE;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * BOX + (ks & 3) * 32;
+          tc_mma_f16_ss(tmem + C::TMEM_S + X * BN,
+                        make_smem_desc(qa + off, 16, 1024, BWPP_SWIZZLE_128B),
+                        make_smem_desc(ka + off, 16, 1024, BWPP_SWIZZLE_128B), C::IDESC_S,
+                        ks > 0 ? 1u : 0u);
+        }
+        tc_commit(&bar->s_full[X]);
+      };
+      // O_X += P_X V_j
+      auto issue_pv = [&](int X, int j) {
+        const uint32_t pa = p_addr + X * P_TILE;
+#pragma unroll
+        for (int ks = 0; ks < BN / 16; ++ks) {
+          const uint32_t aoff = (ks >> 2) * BOX + (ks & 3) * 32;
+          tc_mma_f16_ss(tmem + C::TMEM_O + X * D,
+                        make_smem_desc(pa + aoff, 16, 1024, BWPP_SWIZZLE_128B),
+                        make_smem_desc(v_addr + ks * 2048, BOX, 1024, BWPP_SWIZZLE_128B),
+                        C::IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc_commit(&bar->pv_done[X]);
+      };
+      // block 0: S_A(0), S_B(0)
+      if (ok && n > 0) {
+        ok = mbar_wait(&bar->k_full[0], 0, status);
+        if (ok) {
+          tc_fence_after();
+          for (int X = 0; X < 2; ++X)
+            if (nblk[X] > 0) issue_s(X, 0);
+          tc_commit(&bar->k_empty[0]);
+        }
+      }
+      for (int j = 0; j < n && ok && !*abort_flag; ++j) {
+        bool v_ready = false, k_ready = false;
+        for (int X = 0; X < 2 && ok; ++X) {
+          if (j < nblk[X]) {
+            ok = mbar_wait(&bar->p_full[X], j & 1, status);
+            if (ok && !v_ready) v_ready = ok = mbar_wait(&bar->v_full, j & 1, status);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv(X, j);
+          }
+          if (X == 1) tc_commit(&bar->v_empty);  // V_j free after PV_B(j)
+          if (j + 1 < nblk[X]) {
+            if (!k_ready)
+              k_ready = ok = mbar_wait(&bar->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, status);
+            if (ok) ok = mbar_wait(&bar->s_free[X], j & 1, status);
+            if (!ok) break;
+            tc_fence_after();
+            issue_s(X, j + 1);
+          }
+        }
+        if (ok && j + 1 < n) tc_commit(&bar->k_empty[(j + 1) & 1]);
+      }
+      if (!ok) *abort_flag = 1;
+      tc_commit(&bar->drain);
+      mbar_wait(&bar->drain, 0, status);
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int X = (warp - 2) >> 2;    // query tile
+    const int quarter = warp & 3;     // TMEM lanes 32*quarter ..
+    const int row = quarter * 32 + lane;
+    const uint32_t m_row = q0 + X * BM + row;  // query index
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_col = tmem + lane_base + C::TMEM_S + X * BN;
+    const uint32_t o_col = tmem + lane_base + C::TMEM_O + X * D;
+    uint8_t *p_tile = smem + C::OFF_P + X * P_TILE;
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool ok = true;
+    const int nb = nblk[X];
+    for (int j = 0; j < nb && ok; ++j) {
+      if (*abort_flag || !mbar_wait(&bar->s_full[X], j & 1, status)) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // Two passes over S in TMEM (row max, then exp2 + pack) keep the
+      // 128-float row out of registers.  S_X(j+1) is only issued after
+      // PV_X(j), i.e. after this tile's P is published, so re-reading S here
+      // does not delay the tensor core.
+      const uint32_t n0 = (uint32_t)j * BN;
+      const bool need_mask = n0 + BN > Skv || (causal && n0 + BN - 1 > m_row);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(s_col + c * 32, r);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const uint32_t key = n0 + c * 32 + i;
+          const bool dead = need_mask && (key >= Skv || (causal && key > m_row));
+          mx = fmaxf(mx, dead ? -INFINITY : __uint_as_float(r[i]));
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      // move the reference max only when it grows by more than 2^8
+      const bool move = (m_new - m_run) * scale_log2 > 8.0f;
+      const float m_use = move ? m_new : m_run;
+      const float alpha = move ? fast_exp2((m_run - m_new) * scale_log2) : 1.0f;
+      const float mb = m_use * scale_log2;
+      if (j > 0) {
+        // PV_X(j-1) is done (its completion precedes S_X(j)'s, so this wait
+        // is immediate): O_X is stable and P_X's smem may be overwritten.
+        if (!mbar_wait(&bar->pv_done[X], (j - 1) & 1, status)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, move)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(o_col + c * 32, r);
+            tc_wait_ld();
+            uint32_t w0[16], w1[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              w0[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+              w1[i] = __float_as_uint(__uint_as_float(r[16 + i]) * alpha);
+            }
+            tmem_st_32x32b_x16(o_col + c * 32, w0);
+            tmem_st_32x32b_x16(o_col + c * 32 + 16, w1);
+          }
+          tc_wait_st();
+        }
+      }
+      // pass 2: P = exp2(S*c - m) as bf16, streamed into smem per 32 keys in
+      // the K-major 128-byte-swizzle layout (two 64-key atoms of 16 KB)
+      float psum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(s_col + c * 32, r);
+        tc_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float v0 = __uint_as_float(r[2 * i]), v1 = __uint_as_float(r[2 * i + 1]);
+          if (need_mask) {
+            const uint32_t key = n0 + c * 32 + 2 * i;
+            if (key >= Skv || (causal && key > m_row)) v0 = -INFINITY;
+            if (key + 1 >= Skv || (causal && key + 1 > m_row)) v1 = -INFINITY;
+          }
+          const uint32_t w = pack_bf16(fast_exp2(fmaf(v0, scale_log2, -mb)),
+                                       fast_exp2(fmaf(v1, scale_log2, -mb)));
+          pk[i] = w;
+          // sum the bf16-rounded values the PV product sees
+          psum += __uint_as_float(w << 16) + __uint_as_float(w & 0xFFFF0000u);
+        }
+        uint8_t *atom = p_tile + (c >> 1) * BOX + row * 128;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int q = (c & 1) * 4 + q4;  // 16-byte chunk within the 128-byte row
+          *reinterpret_cast<uint4 *>(atom + ((q ^ (row & 7)) << 4)) =
+              make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+        }
+      }
+      l_run = l_run * alpha + psum;
+      m_run = m_use;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bar->s_free[X]);  // S_X may be overwritten
+        mbar_arrive(&bar->p_full[X]);  // P_X ready for PV_X(j)
+      }
+    }
+    // epilogue: O / l -> global (fp32)
+    if (ok && nb > 0) {
+      if (mbar_wait(&bar->pv_done[X], (nb - 1) & 1, status)) {
+        tc_fence_after();
+        const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+        float *orow = out + ((size_t)bh * Sq + m_row) * D;
+        const bool valid = m_row < Sq;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(o_col + c * 32, r);
+          tc_wait_ld();
+          if (valid) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              __stcs(reinterpret_cast<float4 *>(orow + c * 32) + i,
+                     make_float4(__uint_as_float(r[4 * i]) * inv, __uint_as_float(r[4 * i + 1]) * inv,
+                                 __uint_as_float(r[4 * i + 2]) * inv,
+                                 __uint_as_float(r[4 * i + 3]) * inv));
+          }
+        }
+      } else {
+        *abort_flag = 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+int make_tmap_3d(BwppCudaCtx *ctx, CUtensorMap *map, const void *base,
+                 uint32_t D, uint32_t S, uint32_t BH) {
+  bwpp_encode_tiled_fn enc = bwpp_get_encode_tiled();
+  if (!enc) return bwpp_set_error(ctx, BWPP_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {D, S, BH};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_CUDA, "attention tensor map failed (%d)", (int)r);
+  return BWPP_CUDA_OK;
+}
+
+bool g_attr_set[2][64] = {};
+
+template <int D>
+int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *v,
+           float *o, uint32_t BH, uint32_t Sq, uint32_t Skv, float scale, int causal) {
+  CUtensorMap tq, tk, tv;
+  int rc = make_tmap_3d(ctx, &tq, q, D, Sq, BH);
+  if (!rc) rc = make_tmap_3d(ctx, &tk, k, D, Skv, BH);
+  if (!rc) rc = make_tmap_3d(ctx, &tv, v, D, Skv, BH);
+  if (rc) return rc;
+  const int di = D == 128 ? 1 : 0;
+  if (ctx->device < 64 && !g_attr_set[di][ctx->device]) {
+    rc = bwpp_check_cuda(ctx,
+                         cudaFuncSetAttribute(attention_tc_kernel<D>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              Cfg<D>::SMEM),
+                         "attention smem attribute");
+    if (rc) return rc;
+    g_attr_set[di][ctx->device] = true;
+  }
+  const uint32_t pairs = (Sq + 2 * BM - 1) / (2 * BM);
+  const uint64_t grid = (uint64_t)pairs * BH;
+  if (grid > 0x7fffffffull)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "attention: grid too large");
+  attention_tc_kernel<D><<<(unsigned)grid, THREADS, Cfg<D>::SMEM, ctx->stream>>>(
+      tq, tk, tv, o, BH, Sq, Skv, scale * 1.4426950408889634f, causal, pairs,
+      ctx->status_word);
+  BWPP_LAUNCH_CHECK(ctx, "attention tcgen05");
+  return BWPP_CUDA_OK;
+}
+
+}  // namespace
+
+// Contiguous [BH, S, D] bf16 inputs with D in {64, 128}: tensor-core path.
+// Returns BWPP_CUDA_ERR_UNSUPPORTED for anything else (the caller then uses
+// the CUDA-core kernel).
+int bwpp_attention_tc_launch(BwppCudaCtx *ctx, const uint16_t *q,
+                             const uint16_t *k, const uint16_t *v, float *o,
+                             uint32_t BH, uint32_t Sq, uint32_t Skv, uint32_t D,
+                             float scale, int causal) {
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  // the lazy running max assumes a positive softmax scale
+  if (!al(q) || !al(k) || !al(v) || !al(o) || Skv == 0 || !(scale > 0.0f))
+    return BWPP_CUDA_ERR_UNSUPPORTED;
+  if (D == 128) return launch<128>(ctx, q, k, v, o, BH, Sq, Skv, scale, causal);
+  if (D == 64) return launch<64>(ctx, q, k, v, o, BH, Sq, Skv, scale, causal);
+  return BWPP_CUDA_ERR_UNSUPPORTED;
+}

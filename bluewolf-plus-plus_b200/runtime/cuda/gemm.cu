@@ -379,7 +379,10 @@ int bwpp_cuda_matmul_bf16(BwppCudaCtx *ctx, const uint16_t *a,
                           const float *bias, int apply_silu, int apply_bias) {
   int rc = bwpp_ctx_enter(ctx);
   if (rc) return rc;
-  if (!a || !b || !c) return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "matmul: NULL buffer");
+  // A and B are not read when K == 0 (C = epilogue(0)); nothing is touched
+  // when M or N is 0.
+  if (M && N && (!c || (K && (!a || !b))))
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "matmul: NULL buffer");
   if (lda < K || ldb < N || ldc < N)
     return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "matmul: leading dim smaller than row");
   return bwpp_gemm_launch(ctx, a, b, c, M, N, K, lda, ldb, ldc, bias, apply_silu,

@@ -8,8 +8,8 @@
 //
 // Backward: a persistent grid; each CTA walks rows blockIdx.x, +gridDim.x, ...
 // and accumulates its dgamma / dbeta partial for the columns its threads own
-// in registers, then writes one partial row to scratch.  A second kernel sums
-// the partials over CTAs in a fixed order, so results are deterministic.
+// in shared memory, then writes one partial row to scratch.  A second kernel
+// sums the partials over CTAs in a fixed order, so results are deterministic.
 //
 // Reference: runtime/cpu/bwpp_cpu_ref.c:63-90 (rmsnorm fwd); backward rule
 // compiler/graph_ir.c:1735-1789; layernorm has no reference counterpart.
@@ -186,6 +186,13 @@ __global__ void __launch_bounds__(kThreads)
 //   mu = CENTERED ? mean(x) : 0;  r = 1/sqrt(mean((x-mu)^2) + eps)
 //   xhat = (x - mu) r;  dx = r (g - CENTERED*mean(g) - xhat mean(g xhat))
 //   dgamma += dy xhat;  dbeta += dy
+// One block reduction per row.  For layernorm the statistics come from sums
+// shifted by the row's first element k (broadcast load):
+//   s1 = sum(x-k), s2 = sum((x-k)^2), sg = sum g, sgx = sum g (x-k)
+//   mean = k + s1/C, var = s2/C - (s1/C)^2, sum g xhat = r (sgx - (s1/C) sg)
+// which keeps var well conditioned when |mean| >> std.  The CTA's dgamma /
+// dbeta partials live in shared memory (each thread owns fixed columns, so
+// there are no conflicts), leaving registers for more resident CTAs.
 template <int MAXV, bool V4, bool CENTERED>
 __global__ void __launch_bounds__(kThreads)
     norm_bwd_kernel(const float *__restrict__ x, const float *__restrict__ gamma,
@@ -194,20 +201,13 @@ __global__ void __launch_bounds__(kThreads)
                     uint32_t rows, uint32_t cols, uint32_t ld, float eps) {
   using V = Vec<V4>;
   constexpr int W = V::W;
-  __shared__ float red[3 * 32];
+  __shared__ float red[4 * 32];
+  extern __shared__ float sacc[];  // [2][cols] when part_g != nullptr
+  float *acc_g = sacc, *acc_b = sacc + cols;
   const uint32_t nv = cols / W;
-  float acc_g[MAXV][W], acc_b[MAXV][W], gm[MAXV][W];
-#pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const uint32_t idx = threadIdx.x + i * kThreads;
-#pragma unroll
-    for (int w = 0; w < W; ++w) {
-      acc_g[i][w] = 0.0f;
-      acc_b[i][w] = 0.0f;
-      gm[i][w] = 1.0f;
-    }
-    if (gamma && idx < nv) V::load(gamma, idx, gm[i]);
-  }
+  if (part_g)
+    for (uint32_t c = threadIdx.x; c < 2 * cols; c += kThreads) sacc[c] = 0.0f;
+  // (each thread only ever touches its own columns of sacc: no barrier needed)
   for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float *xr = x + (size_t)r * ld;
     const float *gr = dy + (size_t)r * ld;
@@ -223,68 +223,61 @@ __global__ void __launch_bounds__(kThreads)
         for (int w = 0; w < W; ++w) xv[i][w] = dv[i][w] = 0.0f;
       }
     }
-    float mean = 0.0f;
-    if (CENTERED) {
-      float s[1] = {0.0f};
+    const float k = CENTERED ? __ldg(xr) : 0.0f;
+    // t = {sum (x-k)^2, sum g, sum g (x-k), sum (x-k)}
+    float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int i = 0; i < MAXV; ++i)
-#pragma unroll
-        for (int w = 0; w < W; ++w) s[0] += xv[i][w];
-      block_sum<1>(s, red);
-      mean = s[0] / (float)cols;
-#pragma unroll
-      for (int i = 0; i < MAXV; ++i) {
-        const uint32_t idx = threadIdx.x + i * kThreads;
-        if (idx < nv)
-#pragma unroll
-          for (int w = 0; w < W; ++w) xv[i][w] -= mean;
-      }
-    }
-    // t = {sum (x-mu)^2, sum g, sum g (x-mu)}
-    float t[3] = {0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int i = 0; i < MAXV; ++i)
+    for (int i = 0; i < MAXV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx >= nv) continue;
+      float gm[W];
+      if (gamma) V::load(gamma, idx, gm);
 #pragma unroll
       for (int w = 0; w < W; ++w) {
-        const float g = gm[i][w] * dv[i][w];
-        t[0] += xv[i][w] * xv[i][w];
+        const float d = xv[i][w] - k;
+        const float g = (gamma ? gm[w] : 1.0f) * dv[i][w];
+        t[0] += d * d;
         t[1] += g;
-        t[2] += g * xv[i][w];
+        t[2] += g * d;
+        t[3] += d;
       }
-    block_sum<3>(t, red);
-    const float rs = 1.0f / sqrtf(t[0] / (float)cols + eps);
-    const float mg = CENTERED ? t[1] / (float)cols : 0.0f;
-    const float mgx = t[2] * rs / (float)cols;  // mean(g * xhat)
+    }
+    block_sum<4>(t, red);
+    const float inv_c = 1.0f / (float)cols;
+    const float m1 = CENTERED ? t[3] * inv_c : 0.0f;            // mean - k
+    const float var = CENTERED ? fmaxf(t[0] * inv_c - m1 * m1, 0.0f) : t[0] * inv_c;
+    const float rs = 1.0f / sqrtf(var + eps);
+    const float mg = CENTERED ? t[1] * inv_c : 0.0f;
+    const float mgx = rs * (t[2] - m1 * t[1]) * inv_c;           // mean(g * xhat)
+    const float mu = k + m1;
     float *dxr = dx + (size_t)r * ld;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
       const uint32_t idx = threadIdx.x + i * kThreads;
       if (idx >= nv) continue;
-      float o[W];
+      float gm[W], o[W];
+      if (gamma) V::load(gamma, idx, gm);
 #pragma unroll
       for (int w = 0; w < W; ++w) {
-        const float xh = xv[i][w] * rs;
-        const float g = gm[i][w] * dv[i][w];
+        const float xh = (xv[i][w] - mu) * rs;
+        const float g = (gamma ? gm[w] : 1.0f) * dv[i][w];
         o[w] = rs * (g - mg - xh * mgx);
-        acc_g[i][w] += dv[i][w] * xh;
-        acc_b[i][w] += dv[i][w];
+        if (part_g) {
+          acc_g[idx * W + w] += dv[i][w] * xh;
+          acc_b[idx * W + w] += dv[i][w];
+        }
       }
       V::store(dxr, idx, o);
     }
   }
   if (part_g) {
+    __syncthreads();
     float *pg = part_g + (size_t)blockIdx.x * cols;
     float *pb = part_b + (size_t)blockIdx.x * cols;
-#pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const uint32_t idx = threadIdx.x + i * kThreads;
-      if (idx < nv) {
-#pragma unroll
-        for (int w = 0; w < W; ++w) {
-          pg[idx * W + w] = acc_g[i][w];
-          pb[idx * W + w] = acc_b[i][w];
-        }
-      }
+    for (uint32_t c = threadIdx.x; c < cols; c += kThreads) {
+      // column c was accumulated by the thread that owns vector c / W
+      pg[c] = acc_g[c];
+      pb[c] = acc_b[c];
     }
   }
 }
@@ -438,9 +431,12 @@ int norm_bwd(BwppCudaCtx *ctx, const float *x, const float *gamma,
   const bool v4 = cols % 4 == 0 && ld % 4 == 0 && aligned16(x) && aligned16(dy) &&
                   aligned16(dx) && aligned16(gamma);
   const uint32_t nv = v4 ? cols / 4 : cols;
-  const int mv = pick_maxv(nv, kMaxVecBwd);
+  int mv = pick_maxv(nv, kMaxVecBwd);
+  // partials in shared memory: 2 * cols floats per CTA
+  const size_t acc_bytes = pg ? sizeof(float) * 2 * (size_t)cols : 0;
+  if (acc_bytes > 48 * 1024) mv = 0;  // wide rows: looped kernel (global partials)
 #define BWPP_BWD(MV, V4)                                                     \
-  norm_bwd_kernel<MV, V4, CENTERED><<<grid, kThreads, 0, s>>>(               \
+  norm_bwd_kernel<MV, V4, CENTERED><<<grid, kThreads, acc_bytes, s>>>(       \
       x, gamma, dy, dx, pg, pb, rows, cols, ld, eps)
   if (mv == 0) {
     norm_bwd_looped_kernel<CENTERED><<<grid, kThreads, 0, s>>>(

@@ -107,31 +107,34 @@ def test_metal_dispatch_mirrors(ctx):
     b = rng.standard_normal((K, N)).astype(np.float32)
     bias = rng.uniform(-0.1, 0.1, N).astype(np.float32)
     a16, b16 = O.f32_to_bf16(a), O.f32_to_bf16(b)
+    ta, tb, tbias = dev(a16), dev(b16), dev(bias)  # kept alive while the kernels run
     cd = empty_f32(M, N)
     p = bwpp.MatmulParams(M, N, K, K, N, N)
-    rc = lib.bwpp_cuda_dispatch_matmul(ctx.handle, dev(a16).data_ptr(), dev(b16).data_ptr(),
-                                       cd.data_ptr(), dev(bias).data_ptr(), p, META_MM.encode())
+    rc = lib.bwpp_cuda_dispatch_matmul(ctx.handle, ta.data_ptr(), tb.data_ptr(),
+                                       cd.data_ptr(), tbias.data_ptr(), p, META_MM.encode())
     assert rc == 0
     ctx.sync()
     ref = O.matmul(O.bf16_to_f32(a16), O.bf16_to_f32(b16), bias, 1, 1)
     assert rel_fro(host(cd), ref) <= 2e-4
     # kernel=none: the call is a no-op (runtime/metal/dispatch_stub.m:74-76)
     cd2 = empty_f32(M, N)
-    rc = lib.bwpp_cuda_dispatch_matmul(ctx.handle, dev(a16).data_ptr(), dev(b16).data_ptr(),
+    rc = lib.bwpp_cuda_dispatch_matmul(ctx.handle, ta.data_ptr(), tb.data_ptr(),
                                        cd2.data_ptr(), None, p, b"// bwpp.meta: kernel=none\n")
     ctx.sync()
     assert rc == 0 and torch.isnan(cd2).all()
     # rmsnorm with NULL gamma / beta acts as ones / zeros
     x = rng.standard_normal((8, 64)).astype(np.float32)
+    tx = dev(x)
     yd = empty_f32(8, 64)
-    rc = lib.bwpp_cuda_dispatch_rmsnorm(ctx.handle, dev(x).data_ptr(), None, None, yd.data_ptr(),
+    rc = lib.bwpp_cuda_dispatch_rmsnorm(ctx.handle, tx.data_ptr(), None, None, yd.data_ptr(),
                                         bwpp.RmsnormParams(8, 64, 64, 1e-5),
                                         b"// bwpp.meta: aux_kernel=rmsnorm_f16\n")
     ctx.sync()
     assert rc == 0 and rel_fro(host(yd), O.rmsnorm(x)) <= 1e-5
     xs = rng.standard_normal((4, 33)).astype(np.float32)
+    txs = dev(xs)
     yd = empty_f32(4, 33)
-    rc = lib.bwpp_cuda_dispatch_softmax(ctx.handle, dev(xs).data_ptr(), yd.data_ptr(),
+    rc = lib.bwpp_cuda_dispatch_softmax(ctx.handle, txs.data_ptr(), yd.data_ptr(),
                                         bwpp.SoftmaxParams(4, 33, 33),
                                         b"// bwpp.meta: aux_kernel=softmax_f16\n")
     ctx.sync()
@@ -141,9 +144,10 @@ def test_metal_dispatch_mirrors(ctx):
     k = rng.standard_normal((7, 24)).astype(np.float32)
     v = rng.standard_normal((7, 10)).astype(np.float32)
     q16, k16, v16 = (O.f32_to_bf16(t) for t in (q, k, v))
+    tq, tk, tv = dev(q16), dev(k16), dev(v16)
     od = empty_f32(5, 10)
-    rc = lib.bwpp_cuda_dispatch_attention(ctx.handle, dev(q16).data_ptr(), dev(k16).data_ptr(),
-                                          dev(v16).data_ptr(), od.data_ptr(),
+    rc = lib.bwpp_cuda_dispatch_attention(ctx.handle, tq.data_ptr(), tk.data_ptr(),
+                                          tv.data_ptr(), od.data_ptr(),
                                           bwpp.AttentionParams(5, 7, 24, 10, 24, 24, 10, 10),
                                           b"// bwpp.meta: kernel=attention_f16\n")
     ctx.sync()

@@ -85,7 +85,13 @@ def test_norm_bwd(ctx, rows, cols, ld, centered):
     fn = ctx.layernorm_bwd if centered else ctx.rmsnorm_bwd
     fn(dev(x), dev(g), dev(dy), dxd, dgd, dbd, rows, cols, ld, 1e-5)
     ctx.sync()
-    assert rel_fro(host(dxd)[:, :cols], rdx) <= TOL
+    if cols == 1:
+        # one column: dx = r g (1 - xhat^2) is eps-sized, a cancellation of
+        # O(r g) terms in fp32; measure the error against that term scale
+        scale = np.abs(g[0] * dyc[:, 0] / np.sqrt(xc[:, 0] ** 2 + 1e-5)).max()
+        assert np.abs(host(dxd)[:, :1] - rdx).max() <= TOL * scale
+    else:
+        assert rel_fro(host(dxd)[:, :cols], rdx) <= TOL
     assert rel_fro(host(dgd), rdg) <= TOL
     assert rel_fro(host(dbd), rdb) <= TOL
 
