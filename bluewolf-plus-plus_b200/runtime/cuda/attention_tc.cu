@@ -94,8 +94,10 @@ __device__ __forceinline__ int blocks_for(uint32_t r0, uint32_t Sq, uint32_t Skv
   return n;
 }
 
+// 10 warps: two SM sub-partitions host three warps each, which caps the
+// kernel at 168 registers per thread (16384 / (3 * 32), rounded down to 8).
 template <int D>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,

@@ -262,12 +262,25 @@ __global__ void __launch_bounds__(kThreads)
         const float xh = (xv[i][w] - mu) * rs;
         const float g = (gamma ? gm[w] : 1.0f) * dv[i][w];
         o[w] = rs * (g - mg - xh * mgx);
-        if (part_g) {
-          acc_g[idx * W + w] += dv[i][w] * xh;
-          acc_b[idx * W + w] += dv[i][w];
-        }
+        xv[i][w] = xh;  // keep xhat for the partials below
       }
       V::store(dxr, idx, o);
+      if (part_g) {
+        // 128-bit shared accesses: a warp touches 512 contiguous bytes
+        if constexpr (W == 4) {
+          float4 *ag = reinterpret_cast<float4 *>(acc_g) + idx;
+          float4 *ab = reinterpret_cast<float4 *>(acc_b) + idx;
+          float4 tg = *ag, tb = *ab;
+          tg.x += dv[i][0] * xv[i][0]; tg.y += dv[i][1] * xv[i][1];
+          tg.z += dv[i][2] * xv[i][2]; tg.w += dv[i][3] * xv[i][3];
+          tb.x += dv[i][0]; tb.y += dv[i][1]; tb.z += dv[i][2]; tb.w += dv[i][3];
+          *ag = tg;
+          *ab = tb;
+        } else {
+          acc_g[idx] += dv[i][0] * xv[i][0];
+          acc_b[idx] += dv[i][0];
+        }
+      }
     }
   }
   if (part_g) {
