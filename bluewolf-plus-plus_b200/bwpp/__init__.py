@@ -78,6 +78,7 @@ _SIGS = {
     "bwpp_cuda_attention_bf16": (_i32, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _i32]),
     "bwpp_cuda_rmsnorm_fwd_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
     "bwpp_cuda_rmsnorm_bwd_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
+    "bwpp_cuda_rmsnorm_bwd_f32_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32, _vp]),
     "bwpp_cuda_layernorm_fwd_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
     "bwpp_cuda_layernorm_bwd_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
     "bwpp_cuda_reduce_max_fwd_f32": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32]),

@@ -534,3 +534,122 @@ int bwpp_cuda_layernorm_bwd_f32(BwppCudaCtx *ctx, const float *x,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// RMSNorm backward without any allocation
+// ---------------------------------------------------------------------------
+// For callers that cannot allocate device memory themselves: code embedded in
+// a host framework that owns the whole device-memory budget through its own
+// pool and forbids allocations outside it, or latency-critical loops where a
+// cudaMalloc / cudaFree (which can synchronize the device) is not acceptable.
+// The dgamma / dbeta partials of this variant live in the fixed array below
+// instead of a context workspace; it needs no BwppCudaCtx (creating one
+// allocates).  Limits and sharing rules are stated at the declaration in
+// include/bwpp_cuda.h.
+
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = (size_t)1 << 20;  // 4 MiB
+
+// Lives in the module of this file on every GPU that loads it, until exit.
+// Host code must not pass this name to a kernel (on the host it is only a
+// stand-in symbol); the device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) float g_norm_bwd_scratch[kNoAllocScratchFloats];
+
+float *g_noalloc_scratch[64];
+int g_noalloc_sms[64];
+int g_noalloc_ready[64];
+
+// Once per device, with that device current.
+int noalloc_setup(int dev) {
+  if (dev < 0 || dev >= 64) return BWPP_CUDA_ERR_ARG;
+  if (__atomic_load_n(&g_noalloc_ready[dev], __ATOMIC_ACQUIRE)) return BWPP_CUDA_OK;
+  float *p = nullptr;
+  if (cudaGetSymbolAddress((void **)&p, g_norm_bwd_scratch) != cudaSuccess || !p) {
+    cudaGetLastError();
+    return BWPP_CUDA_ERR_CUDA;
+  }
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms <= 0) {
+    cudaGetLastError();
+    return BWPP_CUDA_ERR_CUDA;
+  }
+  g_noalloc_scratch[dev] = p;
+  g_noalloc_sms[dev] = sms;
+  __atomic_store_n(&g_noalloc_ready[dev], 1, __ATOMIC_RELEASE);
+  return BWPP_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" int bwpp_cuda_rmsnorm_bwd_f32_noalloc(
+    const float *x, const float *gamma, const float *dy, float *dx, float *dgamma,
+    float *dbeta, uint32_t rows, uint32_t cols, uint32_t ld, float eps, void *stream) {
+  if (!x || !dy || !dx || ld < cols) return BWPP_CUDA_ERR_ARG;
+  if (cols == 0) return BWPP_CUDA_OK;
+  const bool partials = dgamma || dbeta;
+  // One CTA needs 2 * cols floats of partials: wider rows are rejected.
+  if (partials && 2 * (size_t)cols > kNoAllocScratchFloats) return BWPP_CUDA_ERR_ARG;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return BWPP_CUDA_ERR_CUDA;
+  }
+  int rc = noalloc_setup(dev);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (rows == 0) {
+    // dgamma = dbeta = 0 without a memset allocation: one tiny kernel
+    if (partials) {
+      column_sum_kernel<<<(cols + 255) / 256, 256, 0, s>>>(g_noalloc_scratch[dev], dgamma, 0, cols);
+      column_sum_kernel<<<(cols + 255) / 256, 256, 0, s>>>(g_noalloc_scratch[dev], dbeta, 0, cols);
+    }
+    return cudaGetLastError() == cudaSuccess ? BWPP_CUDA_OK : BWPP_CUDA_ERR_CUDA;
+  }
+  uint32_t grid = (uint32_t)g_noalloc_sms[dev] * 4;
+  if (rows < grid) grid = rows;
+  float *pg = nullptr, *pb = nullptr;
+  if (partials) {
+    const size_t fit = kNoAllocScratchFloats / (2 * (size_t)cols);  // CTAs whose partials fit
+    if (grid > fit) grid = (uint32_t)fit;
+    // Each CTA overwrites its whole partial row before it is read, so nothing
+    // left over from an earlier call leaks into this one.
+    pg = g_noalloc_scratch[dev];
+    pb = pg + (size_t)grid * cols;
+  }
+  const bool v4 = cols % 4 == 0 && ld % 4 == 0 && aligned16(x) && aligned16(dy) &&
+                  aligned16(dx) && aligned16(gamma);
+  const uint32_t nv = v4 ? cols / 4 : cols;
+  int mv = pick_maxv(nv, kMaxVecBwd);
+  const size_t acc_bytes = pg ? sizeof(float) * 2 * (size_t)cols : 0;
+  if (acc_bytes > 48 * 1024) mv = 0;
+#define BWPP_NA_BWD(MV, V4)                                                     \
+  norm_bwd_kernel<MV, V4, false><<<grid, kThreads, acc_bytes, s>>>(             \
+      x, gamma, dy, dx, pg, pb, rows, cols, ld, eps)
+  if (mv == 0) {
+    norm_bwd_looped_kernel<false><<<grid, kThreads, 0, s>>>(x, gamma, dy, dx, pg, pb, rows,
+                                                            cols, ld, eps);
+  } else if (v4) {
+    switch (mv) {
+      case 1: BWPP_NA_BWD(1, true); break;
+      case 2: BWPP_NA_BWD(2, true); break;
+      case 4: BWPP_NA_BWD(4, true); break;
+      default: BWPP_NA_BWD(8, true); break;
+    }
+  } else {
+    switch (mv) {
+      case 1: BWPP_NA_BWD(1, false); break;
+      case 2: BWPP_NA_BWD(2, false); break;
+      case 4: BWPP_NA_BWD(4, false); break;
+      default: BWPP_NA_BWD(8, false); break;
+    }
+  }
+#undef BWPP_NA_BWD
+  if (pg) {
+    const uint32_t cb = (cols + 255) / 256;
+    column_sum_kernel<<<cb, 256, 0, s>>>(pg, dgamma, grid, cols);
+    column_sum_kernel<<<cb, 256, 0, s>>>(pb, dbeta, grid, cols);
+  }
+  return cudaGetLastError() == cudaSuccess ? BWPP_CUDA_OK : BWPP_CUDA_ERR_CUDA;
+}

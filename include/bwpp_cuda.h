@@ -166,6 +166,34 @@ int bwpp_cuda_rmsnorm_bwd_f32(BwppCudaCtx *ctx, const float *x,
                               float *dgamma, float *dbeta, uint32_t rows,
                               uint32_t cols, uint32_t ld, float eps);
 
+/* RMSNorm backward that allocates nothing (no counterpart in the reference):
+ * same math and outputs as bwpp_cuda_rmsnorm_bwd_f32, for callers that cannot
+ * allocate device memory themselves -- code inside a host framework that owns
+ * the whole device-memory budget and forbids allocations outside its pool, or
+ * latency-critical loops where cudaMalloc / cudaFree (which may synchronize
+ * the device) is not acceptable.  It takes no BwppCudaCtx (creating one
+ * allocates) and runs on `stream` (a cudaStream_t, NULL = default stream) of
+ * the current device.
+ *   - Scratch: the dgamma / dbeta partials live in a fixed 4 MiB array
+ *     (1,048,576 floats) inside the library, held on every GPU that loads it
+ *     until the process exits.  The first call on a device does the set-up:
+ *     it looks up that array's device address (once per device, with the
+ *     device current).  Make that first call before any stream capture.
+ *   - Limit: with dgamma or dbeta requested, cols may be at most 524,288
+ *     (2 * cols floats per CTA); larger cols return BWPP_CUDA_ERR_ARG.  Wide
+ *     rows run on fewer CTAs (the partials of all CTAs must fit).
+ *   - Sharing: every call uses the same array.  Calls whose work overlaps on
+ *     the GPU (different streams, or other host threads) race on it and give
+ *     wrong dgamma / dbeta; serialize them.  Each call overwrites the part of
+ *     the array it reads, so leftovers of earlier calls do not matter.
+ *   - Calls no cudaMalloc, cudaFree or other allocating routine.  Returns a
+ *     status code (BWPP_CUDA_ERR_CUDA on a launch error); device-side errors
+ *     surface at the caller's next synchronization. */
+int bwpp_cuda_rmsnorm_bwd_f32_noalloc(const float *x, const float *gamma,
+                                      const float *dy, float *dx, float *dgamma,
+                                      float *dbeta, uint32_t rows, uint32_t cols,
+                                      uint32_t ld, float eps, void *stream);
+
 /* LayerNorm forward (no reference counterpart; signature follows
  * bwpp_cpu_rmsnorm_f32): y = (x - mean) * rstd * gamma + beta. */
 int bwpp_cuda_layernorm_fwd_f32(BwppCudaCtx *ctx, const float *x, float *y,
