@@ -11,6 +11,9 @@
 // S_A, S_B, O_A, O_B live in TMEM (4 x 128 columns for D = 128).  The running
 // max only moves when it grows by more than 2^8 (log2 domain), so O is
 // rescaled (tcgen05.ld / st) rarely; P <= 256 stays exact enough in bf16.
+// The softmax arithmetic uses paired fp32 lanes (fma/add .f32x2) and 3-input
+// max to halve its instruction count; CTAs are ordered head-major so one
+// head's K / V is read from DRAM once and shared through L2.
 //
 // Warp roles (320 threads): warp 0 TMA producer (Q once; K double-buffered,
 // V single-buffered, 3-D tensor maps so ragged S zero-fills per head),
@@ -76,6 +79,36 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Two fp32 lanes in one 64-bit register: Blackwell issues one FMA / ADD for
+// both (fma.rn.f32x2 / add.rn.f32x2).
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f2unpack(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -111,10 +144,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   Bars *bar = reinterpret_cast<Bars *>(smem + C::OFF_BAR);
   volatile int *abort_flag = &bar->abort_flag;
 
-  // heaviest (latest) query blocks first: better tail for causal masks
+  // Head-major order: the CTAs of one (b,h) run together and share its K / V
+  // through L2.  Within a head the heaviest (latest) query blocks go first,
+  // which evens out the causal tail.
   const uint32_t lin = blockIdx.x;
-  const uint32_t pair = pairs - 1 - lin / BH;
-  const uint32_t bh = lin % BH;
+  const uint32_t bh = lin / pairs;
+  const uint32_t pair = pairs - 1 - lin % pairs;
   const uint32_t q0 = pair * 2 * BM;
   const int nblk[2] = {blocks_for(q0, Sq, Skv, causal),
                        blocks_for(q0 + BM, Sq, Skv, causal)};
@@ -270,21 +305,39 @@ __global__ void __launch_bounds__(THREADS, 1)
       // Two passes over S in TMEM (row max, then exp2 + pack) keep the
       // 128-float row out of registers.  S_X(j+1) is only issued after
       // PV_X(j), i.e. after this tile's P is published, so re-reading S here
-      // does not delay the tensor core.
+      // does not delay the tensor core.  Blocks that need no mask take a
+      // branch-free path; masked blocks compare each key with one limit.
       const uint32_t n0 = (uint32_t)j * BN;
-      const bool need_mask = n0 + BN > Skv || (causal && n0 + BN - 1 > m_row);
-      float mx = -INFINITY;
+      uint32_t lim = Skv - 1;                       // last visible key
+      if (causal && m_row < lim) lim = m_row;
+      const bool need_mask = n0 + BN - 1 > lim;
+      const int lim_rel = (int)lim - (int)n0;       // visible iff index <= lim_rel
+      // pass 1: all four 32-column loads in flight behind one wait, then a
+      // max over 8 independent chains
+      float mx;
+      {
+        uint32_t r[BN];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(s_col + c * 32, r);
-        tc_wait_ld();
+        for (int c = 0; c < BN / 32; ++c)
+          tmem_ld_32x32b_x32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const uint32_t key = n0 + c * 32 + i;
-          const bool dead = need_mask && (key >= Skv || (causal && key > m_row));
-          mx = fmaxf(mx, dead ? -INFINITY : __uint_as_float(r[i]));
+        for (int c = 0; c < BN / 32; ++c)
+          tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < BN; ++i)
+            if (i > lim_rel) r[i] = __float_as_uint(-INFINITY);
         }
+        float m8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(r[k]);
+#pragma unroll
+        for (int i = 8; i < BN; i += 16)
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            m8[k] = max3(m8[k], __uint_as_float(r[i + k]), __uint_as_float(r[i + 8 + k]));
+        mx = fmaxf(fmaxf(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5])),
+                   fmaxf(m8[6], m8[7]));
       }
       const float m_new = fmaxf(m_run, mx);
       // move the reference max only when it grows by more than 2^8
@@ -306,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int c = 0; c < D / 32; ++c) {
             uint32_t r[32];
             tmem_ld_32x32b_x32(o_col + c * 32, r);
-            tc_wait_ld();
+            tc_wait_ld(r);
             uint32_t w0[16], w1[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -320,27 +373,35 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       // pass 2: P = exp2(S*c - m) as bf16, streamed into smem per 32 keys in
-      // the K-major 128-byte-swizzle layout (two 64-key atoms of 16 KB)
-      float psum = 0.0f;
+      // the K-major 128-byte-swizzle layout (two 64-key atoms of 16 KB).  The
+      // row sum adds the fp32 values (paired lanes), the PV product sees them
+      // rounded to bf16.
+      const uint64_t sc2 = f2pack(scale_log2, scale_log2);
+      const uint64_t nb2 = f2pack(-mb, -mb);
+      uint64_t acc2 = f2pack(0.0f, 0.0f);
+      // double-buffered: the load of chunk c+1 is in flight while chunk c is
+      // turned into P
+      uint32_t rbuf[2][32];
+      tmem_ld_32x32b_x32(s_col, rbuf[0]);
+      tc_wait_ld(rbuf[0]);
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(s_col + c * 32, r);
-        tc_wait_ld();
+        uint32_t (&r)[32] = rbuf[c & 1];
+        if (c + 1 < BN / 32) tmem_ld_32x32b_x32(s_col + (c + 1) * 32, rbuf[(c + 1) & 1]);
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i > lim_rel) r[i] = __float_as_uint(-INFINITY);
+        }
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float v0 = __uint_as_float(r[2 * i]), v1 = __uint_as_float(r[2 * i + 1]);
-          if (need_mask) {
-            const uint32_t key = n0 + c * 32 + 2 * i;
-            if (key >= Skv || (causal && key > m_row)) v0 = -INFINITY;
-            if (key + 1 >= Skv || (causal && key + 1 > m_row)) v1 = -INFINITY;
-          }
-          const uint32_t w = pack_bf16(fast_exp2(fmaf(v0, scale_log2, -mb)),
-                                       fast_exp2(fmaf(v1, scale_log2, -mb)));
-          pk[i] = w;
-          // sum the bf16-rounded values the PV product sees
-          psum += __uint_as_float(w << 16) + __uint_as_float(w & 0xFFFF0000u);
+          float y0, y1;
+          f2unpack(f2fma(f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nb2),
+                   y0, y1);
+          const float p0 = fast_exp2(y0), p1 = fast_exp2(y1);
+          pk[i] = pack_bf16(p0, p1);
+          acc2 = f2add(acc2, f2pack(p0, p1));
         }
         uint8_t *atom = p_tile + (c >> 1) * BOX + row * 128;
 #pragma unroll
@@ -349,7 +410,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           *reinterpret_cast<uint4 *>(atom + ((q ^ (row & 7)) << 4)) =
               make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
         }
+        if (c + 1 < BN / 32) tc_wait_ld(rbuf[(c + 1) & 1]);
       }
+      float psum_lo, psum_hi;
+      f2unpack(acc2, psum_lo, psum_hi);
+      const float psum = psum_lo + psum_hi;
       l_run = l_run * alpha + psum;
       m_run = m_use;
       fence_proxy_async_smem();
@@ -371,7 +436,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int c = 0; c < D / 32; ++c) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(o_col + c * 32, r);
-          tc_wait_ld();
+          tc_wait_ld(r);
           if (valid) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
