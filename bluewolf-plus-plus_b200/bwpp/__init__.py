@@ -54,6 +54,12 @@ class AttentionParams(C.Structure):
     _fields_ = [(n, _u32) for n in ("M", "N", "K", "D", "ldq", "ldk", "ldv", "ldo")]
 
 
+class GemmParams(C.Structure):
+    _fields_ = [(n, _u32) for n in ("M", "N", "K", "lda", "ldb", "ldc", "ldr")] + \
+               [(n, _i32) for n in ("a_mn_major", "b_mn_major", "out_bf16", "apply_silu")] + \
+               [("bias", _vp), ("residual", _vp)]
+
+
 class Arena(C.Structure):
     _fields_ = [("buffer", _vp), ("capacity", _sz), ("offset", _sz)]
 
@@ -75,6 +81,7 @@ _SIGS = {
     "bwpp_cuda_device_count": (_i32, []),
     "bwpp_cuda_selftest_wait_timeout": (_i32, [_vp, _u32]),
     "bwpp_cuda_matmul_bf16": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _i32, _i32]),
+    "bwpp_cuda_gemm_bf16_ex": (_i32, [_vp, _vp, _vp, _vp, C.POINTER(GemmParams)]),
     "bwpp_cuda_attention_bf16": (_i32, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _i32]),
     "bwpp_cuda_rmsnorm_fwd_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
     "bwpp_cuda_rmsnorm_bwd_f32": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
@@ -190,6 +197,13 @@ class Ctx:
         self.check(self.lib.bwpp_cuda_matmul_bf16(self.handle, _ptr(a), _ptr(b), _ptr(c), M, N, K,
                                                   lda, ldb, ldc, _ptr(bias), int(silu), int(add)),
                    "matmul_bf16")
+
+    def gemm_ex(self, a, b, c, M, N, K, lda, ldb, ldc, a_mn=0, b_mn=1, out_bf16=0, silu=0,
+                bias=None, residual=None, ldr=0):
+        p = GemmParams(M, N, K, lda, ldb, ldc, ldr, int(a_mn), int(b_mn), int(out_bf16), int(silu),
+                       _ptr(bias), _ptr(residual))
+        self.check(self.lib.bwpp_cuda_gemm_bf16_ex(self.handle, _ptr(a), _ptr(b), _ptr(c), C.byref(p)),
+                   "gemm_bf16_ex")
 
     def attention_bf16(self, q, k, v, o, B, H, Sq, Skv, D, scale, causal):
         self.check(self.lib.bwpp_cuda_attention_bf16(self.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(o),

@@ -1,8 +1,13 @@
-// Fused matmul (+bias, +SiLU) on sm_100a tensor cores.
+// Fused matmul (+bias, +SiLU, +residual) on sm_100a tensor cores.
 //
-// C[M,N] (fp32) = epilogue(A[M,K] (bf16, K contiguous) * B[K,N] (bf16, N
-// contiguous)), epilogue = +bias[N] then SiLU, each optional, in the order of
-// runtime/cpu/bwpp_cpu_ref.c:26-31 and compiler/codegen_metal.c:426-431.
+// C[M,N] = epilogue(A[M,K] * B[K,N]), A and B bf16, fp32 accumulation.
+// epilogue: +bias[N], then SiLU, then +residual[M,N] (fp32), each optional
+// (bias before SiLU as in runtime/cpu/bwpp_cpu_ref.c:26-31 and
+// compiler/codegen_metal.c:426-431); C is written as fp32 or bf16.
+// Operand layouts (template): A K-major (a[m*lda+k]) or MN-major (a[k*lda+m]),
+// B MN-major (b[k*ldb+n], the reference's row-major B) or K-major
+// (b[n*ldb+k], i.e. a transposed weight).  The MN-major forms let the
+// autodiff products (dX = dY W^T, dW = X^T dY) run without transposes.
 //
 // Persistent, warp-specialised kernel, one CTA per SM (192 threads):
 //   warp 0       TMA producer: A box 128(M) x 64(K), B as four 64(N) x 64(K)
@@ -40,8 +45,15 @@ constexpr int SMEM_USED = OFF_BAR + 128;
 constexpr int SMEM_ALLOC = SMEM_USED + 1024;  // slack for 1024-B alignment
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr uint32_t TMEM_COLS = 2 * BN;
-constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN, 0, 1);
 constexpr uint32_t GROUP_M = 8;
+
+struct GemmEpi {
+  const float *bias;      // [N] or nullptr
+  const float *residual;  // fp32 [M, ldr] added last, or nullptr
+  uint32_t ldr;
+  int silu;
+  int out_bf16;
+};
 
 static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in limit");
 
@@ -57,12 +69,13 @@ __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m,
   nb = r / gm;
 }
 
+template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC,
-                   const float *__restrict__ bias, uint32_t M, uint32_t N,
-                   uint32_t K, int apply_bias, int apply_silu, int *status) {
+                   const __grid_constant__ CUtensorMap tmC, const GemmEpi epi,
+                   uint32_t M, uint32_t N, uint32_t K, int *status) {
+  constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN, A_MN ? 1u : 0u, B_MN ? 1u : 0u);
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -119,11 +132,25 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           uint8_t *sa = smem + stage * A_STAGE;
           uint8_t *sb = smem + OFF_B + stage * B_STAGE;
-          tma_load_2d(sa, &tmA, &full[stage], (int32_t)(kb * BK), (int32_t)(mb * BM));
+          if (!A_MN) {
+            // [128 rows of M] x [64 K]: one 16 KB box
+            tma_load_2d(sa, &tmA, &full[stage], (int32_t)(kb * BK), (int32_t)(mb * BM));
+          } else {
+            // [64 K rows] x [64 M] boxes, two of them for 128 M
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(sb + j * B_SUB, &tmB, &full[stage],
-                        (int32_t)(nb * BN + j * 64), (int32_t)(kb * BK));
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d(sa + j * B_SUB, &tmA, &full[stage], (int32_t)(mb * BM + j * 64),
+                          (int32_t)(kb * BK));
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * B_SUB, &tmB, &full[stage],
+                          (int32_t)(nb * BN + j * 64), (int32_t)(kb * BK));
+          } else {
+            // [256 rows of N] x [64 K]: one 32 KB box
+            tma_load_2d(sb, &tmB, &full[stage], (int32_t)(kb * BK), (int32_t)(nb * BN));
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -154,11 +181,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t b0 = smem_u32(smem + OFF_B + stage * B_STAGE);
 #pragma unroll
           for (int ks = 0; ks < BK / 16; ++ks) {
-            // A: K-major, 128-B swizzle; a K step of 16 bf16 = 32 bytes.
-            const uint64_t ad = make_smem_desc(a0 + ks * 32, 16, 1024, BWPP_SWIZZLE_128B);
-            // B: MN-major, 128-B swizzle; 64-column atoms 8 KB apart (LBO),
-            // 8-row K groups 1 KB apart (SBO); a K step of 16 rows = 2 KB.
-            const uint64_t bd = make_smem_desc(b0 + ks * 2048, B_SUB, 1024, BWPP_SWIZZLE_128B);
+            // K-major, 128-B swizzle: a K step of 16 bf16 is 32 bytes inside
+            // the swizzle atom; 8-row groups 1 KB apart (SBO).
+            // MN-major, 128-B swizzle: 64-element MN atoms 8 KB apart (LBO),
+            // 8-row K groups 1 KB apart (SBO); a K step of 16 rows is 2 KB.
+            const uint64_t ad = A_MN ? make_smem_desc(a0 + ks * 2048, B_SUB, 1024, BWPP_SWIZZLE_128B)
+                                     : make_smem_desc(a0 + ks * 32, 16, 1024, BWPP_SWIZZLE_128B);
+            const uint64_t bd = B_MN ? make_smem_desc(b0 + ks * 2048, B_SUB, 1024, BWPP_SWIZZLE_128B)
+                                     : make_smem_desc(b0 + ks * 32, 16, 1024, BWPP_SWIZZLE_128B);
             tc_mma_f16_ss(d_tmem, ad, bd, IDESC, (kb | ks) != 0 ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
@@ -191,35 +221,74 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_after();
       const uint32_t row0 = mb * BM + q * 32;
-      for (int c = 0; c < BN / EPI_COLS; ++c) {
-        const uint32_t col0 = nb * BN + c * EPI_COLS;
+      const uint32_t my_row = row0 + lane;
+      // fp32 out: 32-column chunks; bf16 out: 64-column chunks (two TMEM
+      // loads).  Either way a chunk is 32 rows x 128 bytes in smem.
+      const int cw = epi.out_bf16 ? 64 : 32;
+      for (int c = 0; c < BN / cw; ++c) {
+        const uint32_t col0 = nb * BN + c * cw;
         if (col0 >= N) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c * EPI_COLS, r);
-        tc_wait_ld();
-        float v[32];
+        uint32_t outw[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (apply_bias) {
-          if (col0 + 32 <= N) {
-            const float4 *b4 = reinterpret_cast<const float4 *>(bias + col0);
+        for (int h = 0; h < 2; ++h) {
+          if (h == 1 && !epi.out_bf16) break;
+          const uint32_t cs = col0 + h * 32;  // first column of this 32-wide part
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + (cs - nb * BN), r);
+          tc_wait_ld(r);
+          float v[32];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 bb = __ldg(b4 + j);
-              v[4 * j] += bb.x;
-              v[4 * j + 1] += bb.y;
-              v[4 * j + 2] += bb.z;
-              v[4 * j + 3] += bb.w;
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (epi.bias) {
+            if (cs + 32 <= N) {
+              const float4 *b4 = reinterpret_cast<const float4 *>(epi.bias + cs);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 bb = __ldg(b4 + j);
+                v[4 * j] += bb.x;
+                v[4 * j + 1] += bb.y;
+                v[4 * j + 2] += bb.z;
+                v[4 * j + 3] += bb.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (cs + j < N) v[j] += __ldg(epi.bias + cs + j);
+            }
+          }
+          if (epi.silu) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = bwpp_silu_f(v[j]);
+          }
+          if (epi.residual && my_row < M) {
+            const float *rr = epi.residual + (size_t)my_row * epi.ldr + cs;
+            if (cs + 32 <= N && (epi.ldr & 3) == 0 &&
+                (reinterpret_cast<uintptr_t>(epi.residual) & 15) == 0) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 t = *reinterpret_cast<const float4 *>(rr + 4 * j);
+                v[4 * j] += t.x;
+                v[4 * j + 1] += t.y;
+                v[4 * j + 2] += t.z;
+                v[4 * j + 3] += t.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (cs + j < N) v[j] += rr[j];
+            }
+          }
+          if (epi.out_bf16) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              uint32_t w;
+              asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(v[2 * j + 1]), "f"(v[2 * j]));
+              outw[h * 16 + j] = w;
             }
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < N) v[j] += __ldg(bias + col0 + j);
+            for (int j = 0; j < 32; ++j) outw[j] = __float_as_uint(v[j]);
           }
-        }
-        if (apply_silu) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = bwpp_silu_f(v[j]);
         }
         // the store that last used this buffer has finished reading it
         if (lane == 0) tma_store_wait_read<1>();
@@ -227,8 +296,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint8_t *sc = stage_c + buf * EPI_BUF;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<float4 *>(sc + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-              make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          *reinterpret_cast<uint4 *>(sc + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+              make_uint4(outw[4 * j], outw[4 * j + 1], outw[4 * j + 2], outw[4 * j + 3]);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && row0 < M) {
@@ -260,30 +329,37 @@ __global__ void __launch_bounds__(THREADS, 1)
 constexpr int ST = 16;
 
 __global__ void gemm_simt_kernel(const uint16_t *__restrict__ a,
-                                 const uint16_t *__restrict__ b,
-                                 float *__restrict__ c, uint32_t M, uint32_t N,
-                                 uint32_t K, uint32_t lda, uint32_t ldb,
-                                 uint32_t ldc, const float *__restrict__ bias,
-                                 int apply_silu, int apply_bias) {
+                                 const uint16_t *__restrict__ b, void *c,
+                                 uint32_t M, uint32_t N, uint32_t K, uint32_t lda,
+                                 uint32_t ldb, uint32_t ldc, int a_mn, int b_mn,
+                                 const GemmEpi epi) {
   __shared__ float As[ST][ST + 1], Bs[ST][ST + 1];
   const uint32_t row = blockIdx.y * ST + threadIdx.y;
   const uint32_t col = blockIdx.x * ST + threadIdx.x;
+  auto bf = [](uint16_t h) { return __uint_as_float((uint32_t)h << 16); };
   float acc = 0.0f;
   for (uint32_t k0 = 0; k0 < K; k0 += ST) {
     const uint32_t ka = k0 + threadIdx.x, kb = k0 + threadIdx.y;
     As[threadIdx.y][threadIdx.x] =
-        (row < M && ka < K) ? __uint_as_float((uint32_t)a[(size_t)row * lda + ka] << 16) : 0.0f;
+        (row < M && ka < K) ? bf(a_mn ? a[(size_t)ka * lda + row] : a[(size_t)row * lda + ka]) : 0.0f;
     Bs[threadIdx.y][threadIdx.x] =
-        (kb < K && col < N) ? __uint_as_float((uint32_t)b[(size_t)kb * ldb + col] << 16) : 0.0f;
+        (kb < K && col < N) ? bf(b_mn ? b[(size_t)kb * ldb + col] : b[(size_t)col * ldb + kb]) : 0.0f;
     __syncthreads();
 #pragma unroll
     for (int kk = 0; kk < ST; ++kk) acc += As[threadIdx.y][kk] * Bs[kk][threadIdx.x];
     __syncthreads();
   }
   if (row < M && col < N) {
-    if (apply_bias && bias) acc += bias[col];
-    if (apply_silu) acc = acc / (1.0f + expf(-acc));
-    c[(size_t)row * ldc + col] = acc;
+    if (epi.bias) acc += epi.bias[col];
+    if (epi.silu) acc = acc / (1.0f + expf(-acc));
+    if (epi.residual) acc += epi.residual[(size_t)row * epi.ldr + col];
+    if (epi.out_bf16) {
+      uint32_t w;
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(0.0f), "f"(acc));
+      reinterpret_cast<uint16_t *>(c)[(size_t)row * ldc + col] = (uint16_t)(w & 0xFFFFu);
+    } else {
+      reinterpret_cast<float *>(c)[(size_t)row * ldc + col] = acc;
+    }
   }
 }
 
@@ -306,55 +382,83 @@ __global__ void cast_f32_bf16_kernel(const float *__restrict__ src,
   }
 }
 
-bool g_attr_set[64] = {};
+bool g_attr_set[4][64] = {};
 
 inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+template <bool A_MN, bool B_MN>
+int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
+              const CUtensorMap &tcm, const GemmEpi &epi, uint32_t M, uint32_t N,
+              uint32_t K) {
+  const int v = (A_MN ? 2 : 0) + (B_MN ? 1 : 0);
+  if (ctx->device < 64 && !g_attr_set[v][ctx->device]) {
+    int rc = bwpp_check_cuda(ctx,
+                             cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  SMEM_ALLOC),
+                             "gemm smem attribute");
+    if (rc) return rc;
+    g_attr_set[v][ctx->device] = true;
+  }
+  const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const uint32_t grid = tiles < (uint32_t)ctx->num_sms ? tiles : (uint32_t)ctx->num_sms;
+  gemm_tc_kernel<A_MN, B_MN><<<grid, THREADS, SMEM_ALLOC, ctx->stream>>>(ta, tb, tcm, epi, M, N, K,
+                                                                        ctx->status_word);
+  BWPP_LAUNCH_CHECK(ctx, "gemm tcgen05");
+  return BWPP_CUDA_OK;
+}
+
 }  // namespace
 
-// Kernel-only entry used by the public API and by composite paths.
-int bwpp_gemm_launch(BwppCudaCtx *ctx, const uint16_t *a, const uint16_t *b,
-                     float *c, uint32_t M, uint32_t N, uint32_t K, uint32_t lda,
-                     uint32_t ldb, uint32_t ldc, const float *bias,
-                     int apply_silu, int apply_bias, int force_simt) {
+// General entry used by the public API and by composite paths (the training
+// step).  a_mn / b_mn select the operand layouts described at the top.
+int bwpp_gemm_launch_ex(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,
+                        const uint16_t *b, int b_mn, uint32_t ldb, void *c,
+                        uint32_t ldc, uint32_t M, uint32_t N, uint32_t K,
+                        const float *bias, int silu, const float *residual,
+                        uint32_t ldr, int out_bf16, int force_simt) {
   if (M == 0 || N == 0) return BWPP_CUDA_OK;
-  const int use_bias = (apply_bias && bias) ? 1 : 0;
+  GemmEpi epi{bias, residual, ldr, silu ? 1 : 0, out_bf16 ? 1 : 0};
+  const uint32_t out_es = out_bf16 ? 2 : 4;
   const bool tc_ok = !force_simt && K > 0 && al16(a) && al16(b) && al16(c) &&
-                     (lda % 8) == 0 && (ldb % 8) == 0 && (ldc % 4) == 0 &&
-                     (!use_bias || al16(bias));
+                     (lda % 8) == 0 && (ldb % 8) == 0 && ((ldc * out_es) % 16) == 0 &&
+                     (!bias || al16(bias));
   cudaStream_t s = ctx->stream;
   if (!tc_ok) {
     dim3 grid((N + ST - 1) / ST, (M + ST - 1) / ST);
-    gemm_simt_kernel<<<grid, dim3(ST, ST), 0, s>>>(a, b, c, M, N, K, lda, ldb, ldc,
-                                                   bias, apply_silu, use_bias);
+    gemm_simt_kernel<<<grid, dim3(ST, ST), 0, s>>>(a, b, c, M, N, K, lda, ldb, ldc, a_mn, b_mn, epi);
     BWPP_LAUNCH_CHECK(ctx, "gemm simt");
     return BWPP_CUDA_OK;
   }
   CUtensorMap ta, tb, tcm;
-  int rc = bwpp_make_tmap_2d(ctx, &ta, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M,
-                             (uint64_t)lda * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  int rc = a_mn ? bwpp_make_tmap_2d(ctx, &ta, a, BF, M, K, (uint64_t)lda * 2, 64, BK, SW)
+                : bwpp_make_tmap_2d(ctx, &ta, a, BF, K, M, (uint64_t)lda * 2, BK, BM, SW);
   if (!rc)
-    rc = bwpp_make_tmap_2d(ctx, &tb, b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, K,
-                           (uint64_t)ldb * 2, 64, BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = b_mn ? bwpp_make_tmap_2d(ctx, &tb, b, BF, N, K, (uint64_t)ldb * 2, 64, BK, SW)
+              : bwpp_make_tmap_2d(ctx, &tb, b, BF, K, N, (uint64_t)ldb * 2, BK, BN, SW);
   if (!rc)
-    rc = bwpp_make_tmap_2d(ctx, &tcm, c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M,
-                           (uint64_t)ldc * 4, EPI_COLS, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = out_bf16 ? bwpp_make_tmap_2d(ctx, &tcm, c, BF, N, M, (uint64_t)ldc * 2, 64, 32, SW)
+                  : bwpp_make_tmap_2d(ctx, &tcm, c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M,
+                                      (uint64_t)ldc * 4, EPI_COLS, 32, SW);
   if (rc) return rc;
-  if (ctx->device < 64 && !g_attr_set[ctx->device]) {
-    rc = bwpp_check_cuda(ctx,
-                         cudaFuncSetAttribute(gemm_tc_kernel,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              SMEM_ALLOC),
-                         "gemm smem attribute");
-    if (rc) return rc;
-    g_attr_set[ctx->device] = true;
+  if (a_mn) {
+    return b_mn ? launch_tc<true, true>(ctx, ta, tb, tcm, epi, M, N, K)
+                : launch_tc<true, false>(ctx, ta, tb, tcm, epi, M, N, K);
   }
-  const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const uint32_t grid = tiles < (uint32_t)ctx->num_sms ? tiles : (uint32_t)ctx->num_sms;
-  gemm_tc_kernel<<<grid, THREADS, SMEM_ALLOC, s>>>(ta, tb, tcm, bias, M, N, K, use_bias,
-                                                   apply_silu, ctx->status_word);
-  BWPP_LAUNCH_CHECK(ctx, "gemm tcgen05");
-  return BWPP_CUDA_OK;
+  return b_mn ? launch_tc<false, true>(ctx, ta, tb, tcm, epi, M, N, K)
+              : launch_tc<false, false>(ctx, ta, tb, tcm, epi, M, N, K);
+}
+
+// The reference-shaped matmul: A K-major, B MN-major, fp32 out.
+int bwpp_gemm_launch(BwppCudaCtx *ctx, const uint16_t *a, const uint16_t *b,
+                     float *c, uint32_t M, uint32_t N, uint32_t K, uint32_t lda,
+                     uint32_t ldb, uint32_t ldc, const float *bias,
+                     int apply_silu, int apply_bias, int force_simt) {
+  return bwpp_gemm_launch_ex(ctx, a, 0, lda, b, 1, ldb, c, ldc, M, N, K,
+                             (apply_bias && bias) ? bias : nullptr, apply_silu, nullptr, 0,
+                             0, force_simt);
 }
 
 int bwpp_cast_launch(BwppCudaCtx *ctx, const float *src, uint16_t *dst,
@@ -387,6 +491,21 @@ int bwpp_cuda_matmul_bf16(BwppCudaCtx *ctx, const uint16_t *a,
     return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "matmul: leading dim smaller than row");
   return bwpp_gemm_launch(ctx, a, b, c, M, N, K, lda, ldb, ldc, bias, apply_silu,
                           apply_bias, 0);
+}
+
+int bwpp_cuda_gemm_bf16_ex(BwppCudaCtx *ctx, const uint16_t *a, const uint16_t *b,
+                           void *c, const BwppCudaGemmParams *p) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (!p) return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "gemm_ex: NULL params");
+  if (p->M && p->N && (!c || (p->K && (!a || !b))))
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "gemm_ex: NULL buffer");
+  if (p->lda < (p->a_mn_major ? p->M : p->K) || p->ldb < (p->b_mn_major ? p->N : p->K) ||
+      p->ldc < p->N || (p->residual && p->ldr < p->N))
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "gemm_ex: leading dim smaller than row");
+  return bwpp_gemm_launch_ex(ctx, a, p->a_mn_major, p->lda, b, p->b_mn_major, p->ldb, c,
+                             p->ldc, p->M, p->N, p->K, p->bias, p->apply_silu, p->residual,
+                             p->ldr, p->out_bf16, 0);
 }
 
 int bwpp_cuda_cast_f32_bf16(BwppCudaCtx *ctx, const float *src, uint16_t *dst,

@@ -138,6 +138,29 @@ int bwpp_cuda_matmul_bf16(BwppCudaCtx *ctx, const uint16_t *a,
                           uint32_t K, uint32_t lda, uint32_t ldb, uint32_t ldc,
                           const float *bias, int apply_silu, int apply_bias);
 
+/* General form of the matmul above (no single reference counterpart: it
+ * covers the transposed products of the autodiff rule for matmul,
+ * compiler/graph_ir.c:1529-1583, dA = dY B^T and dB = A^T dY, plus the
+ * residual add of a decoder block).
+ *   A[m,k] = a_mn_major ? a[k*lda + m] : a[m*lda + k]
+ *   B[k,n] = b_mn_major ? b[k*ldb + n] : b[n*ldb + k]
+ *   v = A*B (+ bias[n]) (SiLU) (+ residual[m*ldr + n]); C = v as fp32 or bf16
+ * residual may alias C when C is fp32 (C += A*B). */
+typedef struct {
+  uint32_t M, N, K;
+  uint32_t lda, ldb, ldc, ldr;
+  int a_mn_major;
+  int b_mn_major;
+  int out_bf16;
+  int apply_silu;
+  const float *bias;
+  const float *residual;
+} BwppCudaGemmParams;
+
+int bwpp_cuda_gemm_bf16_ex(BwppCudaCtx *ctx, const uint16_t *a,
+                           const uint16_t *b, void *c,
+                           const BwppCudaGemmParams *params);
+
 /* O = softmax(scale * Q K^T [+ causal mask]) V on contiguous [B,H,S,D]
  * tensors: Q [B,H,Sq,D], K and V [B,H,Skv,D] bf16 bits, O [B,H,Sq,D] fp32.
  * causal: key n visible to query m iff n <= m.  Single-pass online softmax

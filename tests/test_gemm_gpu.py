@@ -117,3 +117,83 @@ def test_config2_full_size_sampled_rows(ctx):
     ctx.sync()
     assert torch.equal(c2, 2 * c1)
     assert torch.equal(c3, c1[perm])
+
+
+# ---- general form: operand layouts, bf16 output, residual ---------------------
+
+def logical(storage16, mn_major, rows, cols):
+    """A operand: logical [rows=M, cols=K]; MN-major storage is [K, lda] (transposed)."""
+    f = O.bf16_to_f32(storage16)
+    return np.ascontiguousarray(f.T[:rows, :cols] if mn_major else f[:rows, :cols])
+
+
+def logical_b(storage16, mn_major, K, N):
+    """B operand: logical [K, N]; MN-major storage is [K, ldb], K-major is [N, ldb]."""
+    f = O.bf16_to_f32(storage16)
+    return np.ascontiguousarray(f[:K, :N] if mn_major else f[:N, :K].T)
+
+
+@pytest.mark.parametrize("a_mn", [0, 1])
+@pytest.mark.parametrize("b_mn", [0, 1])
+@pytest.mark.parametrize("out_bf16", [0, 1])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 320), (129, 264, 72), (520, 130, 1000)])
+def test_gemm_ex_layouts(ctx, a_mn, b_mn, out_bf16, M, N, K):
+    rng = np.random.default_rng(M + 3 * N + 7 * K + 11 * a_mn + 13 * b_mn)
+    pad = lambda n: (n + 7) // 8 * 8 + 8  # leading dims > the row, multiple of 8
+    # storage: A K-major [M, lda>=K] or MN-major [K, lda>=M]; B MN-major [K, ldb>=N]
+    # or K-major [N, ldb>=K]
+    lda = pad(M if a_mn else K)
+    ldb = pad(N if b_mn else K)
+    a16 = O.f32_to_bf16(rng.standard_normal((K if a_mn else M, lda)).astype(np.float32))
+    b16 = O.f32_to_bf16(rng.standard_normal((K if b_mn else N, ldb)).astype(np.float32))
+    A = logical(a16, a_mn, M, K)
+    B = logical_b(b16, b_mn, K, N)
+    bias = rng.uniform(-0.5, 0.5, N).astype(np.float32)
+    resid = rng.standard_normal((M, N)).astype(np.float32)
+    ref = O.matmul(A, B, bias, 1, 1) + resid
+    ldc = N + 8
+    if out_bf16:
+        cd = torch.zeros(M, ldc, dtype=torch.int16, device="cuda")
+    else:
+        cd = empty_f32(M, ldc)
+    ctx.gemm_ex(dev(a16), dev(b16), cd, M, N, K, lda, ldb, ldc, a_mn=a_mn, b_mn=b_mn,
+                out_bf16=out_bf16, silu=1, bias=dev(bias), residual=dev(resid), ldr=N)
+    ctx.sync()
+    if out_bf16:
+        got = O.bf16_to_f32(host(cd).view(np.uint16))[:, :N]
+        err = rel_fro(got, ref)
+        assert err <= TOL and err <= 5e-3, err   # bf16 output rounding ~ 2^-9
+    else:
+        err = rel_fro(host(cd)[:, :N], ref)
+        assert err <= TOL and err <= TIGHT, err
+
+
+def test_gemm_ex_accumulate_in_place(ctx):
+    # residual aliasing C: C += A B (the residual add of a decoder block)
+    M, N, K = 384, 768, 512
+    rng = np.random.default_rng(77)
+    a16 = O.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    b16 = O.f32_to_bf16(rng.standard_normal((K, N)).astype(np.float32))
+    c0 = rng.standard_normal((M, N)).astype(np.float32)
+    cd = dev(c0)
+    ctx.gemm_ex(dev(a16), dev(b16), cd, M, N, K, K, N, N, residual=cd, ldr=N)
+    ctx.sync()
+    ref = O.matmul(O.bf16_to_f32(a16), O.bf16_to_f32(b16)) + c0
+    assert rel_fro(host(cd), ref) <= TIGHT
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (1, 1), (1, 0)])
+def test_gemm_ex_cuda_core_layouts(ctx, a_mn, b_mn):
+    # odd leading dims force the CUDA-core path; same layout semantics
+    M, N, K = 37, 29, 45
+    rng = np.random.default_rng(5 + a_mn + 2 * b_mn)
+    lda = (M if a_mn else K) + 1
+    ldb = (N if b_mn else K) + 3
+    a16 = O.f32_to_bf16(rng.standard_normal((K if a_mn else M, lda)).astype(np.float32))
+    b16 = O.f32_to_bf16(rng.standard_normal((K if b_mn else N, ldb)).astype(np.float32))
+    A = logical(a16, a_mn, M, K)
+    B = logical_b(b16, b_mn, K, N)
+    cd = empty_f32(M, N)
+    ctx.gemm_ex(dev(a16), dev(b16), cd, M, N, K, lda, ldb, N, a_mn=a_mn, b_mn=b_mn)
+    ctx.sync()
+    assert rel_fro(host(cd), O.matmul(A, B)) <= TIGHT
