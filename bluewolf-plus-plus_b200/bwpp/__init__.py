@@ -60,6 +60,11 @@ class GemmParams(C.Structure):
                [("bias", _vp), ("residual", _vp)]
 
 
+class TinyModelConfig(C.Structure):
+    _fields_ = [(n, _u32) for n in ("layers", "d_model", "heads", "head_dim", "ffn", "batch", "seq")] + \
+               [("eps", _f32)]
+
+
 class Arena(C.Structure):
     _fields_ = [("buffer", _vp), ("capacity", _sz), ("offset", _sz)]
 
@@ -94,6 +99,20 @@ _SIGS = {
     "bwpp_cuda_reduce_max_grad_ex": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _i32]),
     "bwpp_cuda_softmax_fwd_f32": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32]),
     "bwpp_cuda_cast_f32_bf16": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32]),
+    "bwpp_cuda_comm_unique_id": (_i32, [_vp]),
+    "bwpp_cuda_comm_create": (_i32, [C.POINTER(_vp), _vp, _i32, _i32, _i32]),
+    "bwpp_cuda_comm_allreduce_sum_f32": (_i32, [_vp, _vp, _sz, _vp]),
+    "bwpp_cuda_comm_destroy": (_i32, [_vp]),
+    "bwpp_cuda_tiny_model_create": (_i32, [_vp, C.POINTER(TinyModelConfig), _u64, C.POINTER(_vp)]),
+    "bwpp_cuda_tiny_model_destroy": (_i32, [_vp]),
+    "bwpp_cuda_tiny_model_param_count": (_sz, [_vp]),
+    "bwpp_cuda_tiny_model_get": (_i32, [_vp, _vp, _vp]),
+    "bwpp_cuda_tiny_model_set_params": (_i32, [_vp, _vp]),
+    "bwpp_cuda_attention_fwd_lse_bf16": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _f32, _i32,
+                                                _vp, _u32, _vp]),
+    "bwpp_cuda_attention_bwd_bf16": (_i32, [_vp, _vp, _vp, _vp, _u32, _vp, _u32, _vp, _u32, _vp,
+                                            _u32, _u32, _u32, _f32, _i32, _vp, _vp, _vp, _u32]),
+    "bwpp_cuda_tiny_model_step": (_i32, [_vp, _vp, _vp, _f32, _vp, _vp]),
     "bwpp_cuda_matmul_f32": (None, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _i32, _i32]),
     "bwpp_cuda_softmax_f32": (None, [_vp, _vp, _u32, _u32, _u32]),
     "bwpp_cuda_rmsnorm_f32": (None, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
@@ -251,6 +270,36 @@ class Ctx:
     def cast_f32_bf16(self, src, dst, rows, cols, ld_src):
         self.check(self.lib.bwpp_cuda_cast_f32_bf16(self.handle, _ptr(src), _ptr(dst), rows, cols, ld_src),
                    "cast_f32_bf16")
+
+
+class TinyModel:
+    """The tiny_model training step (bwpp_cuda_tiny_model_*) on one Ctx."""
+
+    def __init__(self, ctx: "Ctx", layers, d_model, heads, ffn, batch, seq, eps=1e-5, seed=1):
+        self.ctx, self.lib = ctx, ctx.lib
+        self.cfg = TinyModelConfig(layers, d_model, heads, 128, ffn, batch, seq, eps)
+        h = C.c_void_p()
+        ctx.check(self.lib.bwpp_cuda_tiny_model_create(ctx.handle, C.byref(self.cfg), seed, C.byref(h)),
+                  "tiny_model_create")
+        self.handle = h
+        self.count = self.lib.bwpp_cuda_tiny_model_param_count(h)
+
+    def step(self, x, target, lr=0.0, comm=None, loss_out=None):
+        self.ctx.check(self.lib.bwpp_cuda_tiny_model_step(self.handle, _ptr(x), _ptr(target), float(lr),
+                                                          comm, _ptr(loss_out)), "tiny_model_step")
+
+    def get(self, params_out=None, grads_out=None):
+        self.ctx.check(self.lib.bwpp_cuda_tiny_model_get(self.handle, _ptr(params_out), _ptr(grads_out)),
+                       "tiny_model_get")
+
+    def set_params(self, params):
+        self.ctx.check(self.lib.bwpp_cuda_tiny_model_set_params(self.handle, _ptr(params)),
+                       "tiny_model_set_params")
+
+    def close(self):
+        if self.handle:
+            self.lib.bwpp_cuda_tiny_model_destroy(self.handle)
+            self.handle = None
 
 
 # ---- CPU-signature mirrors (host or device pointers, synchronous) ---------

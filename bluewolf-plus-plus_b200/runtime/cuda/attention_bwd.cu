@@ -1,0 +1,562 @@
+// Attention backward on sm_100a tensor cores (training step of the tiny_model
+// config).  With s = scale * q.k, P = softmax(s) recomputed from the forward's
+// base-2 log-sum-exp (P = exp2(q.k * scale*log2e - lse2)), dO the upstream
+// gradient and delta = rowsum(dO * O):
+//   dP = dO V^T,  dS = P * (dP - delta),
+//   dQ = scale * dS K,  dK = scale * dS^T Q,  dV = P^T dO
+// Two kernels, no atomics:
+//   bwd_dq_kernel    one CTA per (head, 128 query rows); loops over 128-key
+//                    blocks: S = Q K^T and dP = dO V^T into TMEM, the softmax
+//                    warps (one query row per thread) form dS -> smem bf16,
+//                    dQ += dS K accumulates in TMEM.
+//   bwd_dkdv_kernel  one CTA per (head, 128 keys); loops over 128-row query
+//                    tiles: S^T = K Q^T and dP^T = V dO^T into TMEM, the
+//                    softmax warps (one key per thread) form P^T and dS^T ->
+//                    smem bf16, dV += P^T dO and dK += dS^T Q accumulate in
+//                    TMEM.
+// Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer, 2-5 softmax.  All
+// waits are bounded (BWPP_WAIT_LIMIT_NS) as in the forward kernel.
+// Operands reuse the forward's smem layouts: a 128-row tile is two 64-column
+// 128-byte-swizzle boxes; read K-major for S-type products and MN-major when
+// it is the B of dQ / dK / dV.
+#include "attention_common.cuh"
+
+namespace {
+
+using namespace bwpp_attn;
+
+constexpr int D = 128;
+constexpr int TILE = 2 * BOX;  // 128 rows x 128 bf16
+constexpr int THREADS = 192;
+constexpr uint32_t IDESC_KK = make_idesc_bf16_f32(128, 128, 0, 0);  // S-type
+constexpr uint32_t IDESC_KM = make_idesc_bf16_f32(128, D, 0, 1);    // dQ / dK / dV
+
+struct BwdIO {
+  uint16_t *d0, *d1;  // dq kernel: dQ; dkdv kernel: dK (d0), dV (d1)
+  uint32_t ldd;       // token-major pitch of the outputs
+  const float *lse;   // [B*H, Sq]
+  const float *delta; // [B*H, Sq]
+  AttnIO in;          // input layout (tok / H)
+};
+
+__device__ __forceinline__ void mma_kk(uint32_t d, uint32_t a, uint32_t b) {
+  // D(128 x 128) = A(128 x D) B(128 x D)^T, both K-major
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks) {
+    const uint32_t off = (ks >> 2) * BOX + (ks & 3) * 32;
+    tc_mma_f16_ss(d, make_smem_desc(a + off, 16, 1024, BWPP_SWIZZLE_128B),
+                  make_smem_desc(b + off, 16, 1024, BWPP_SWIZZLE_128B), IDESC_KK,
+                  ks > 0 ? 1u : 0u);
+  }
+}
+
+__device__ __forceinline__ void mma_km(uint32_t d, uint32_t a, uint32_t b, bool acc) {
+  // D(128 x D) += A(128 x 128, K-major) B(128 x D, MN-major)
+#pragma unroll
+  for (int ks = 0; ks < 128 / 16; ++ks) {
+    const uint32_t aoff = (ks >> 2) * BOX + (ks & 3) * 32;
+    tc_mma_f16_ss(d, make_smem_desc(a + aoff, 16, 1024, BWPP_SWIZZLE_128B),
+                  make_smem_desc(b + ks * 2048, BOX, 1024, BWPP_SWIZZLE_128B), IDESC_KM,
+                  (acc || ks > 0) ? 1u : 0u);
+  }
+}
+
+// Writes a row of 128 fp32 TMEM values (x scale) as bf16 to global memory.
+__device__ __forceinline__ void store_row_bf16(uint32_t taddr, uint16_t *dst, float scale,
+                                               bool valid) {
+#pragma unroll 1
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr + c * 32, r);
+    tc_wait_ld(r);
+    if (valid) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<uint4 *>(dst + c * 32 + 8 * i) = make_uint4(
+            pack_bf16(__uint_as_float(r[8 * i]) * scale, __uint_as_float(r[8 * i + 1]) * scale),
+            pack_bf16(__uint_as_float(r[8 * i + 2]) * scale, __uint_as_float(r[8 * i + 3]) * scale),
+            pack_bf16(__uint_as_float(r[8 * i + 4]) * scale, __uint_as_float(r[8 * i + 5]) * scale),
+            pack_bf16(__uint_as_float(r[8 * i + 6]) * scale, __uint_as_float(r[8 * i + 7]) * scale));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dQ
+// ---------------------------------------------------------------------------
+constexpr int Q_OFF_Q = 0, Q_OFF_DO = TILE, Q_OFF_K = 2 * TILE, Q_OFF_V = 4 * TILE,
+              Q_OFF_DS = 6 * TILE, Q_OFF_BAR = 7 * TILE;
+constexpr int Q_SMEM = Q_OFF_BAR + 256 + 1024;
+static_assert(Q_SMEM <= 232448, "dq smem");
+
+struct QBars {
+  uint64_t qd_full, kv_full[2], kv_empty[2], s_full, s_free, ds_full, dq_done, drain;
+  uint32_t tmem;
+  int abort_flag;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+    bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                  const BwdIO io, uint32_t BH, uint32_t Sq, uint32_t Skv, float scale,
+                  float scale_log2, int causal, uint32_t qtiles, int *status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  QBars *bar = reinterpret_cast<QBars *>(smem + Q_OFF_BAR);
+  volatile int *abort_flag = &bar->abort_flag;
+  const uint32_t bh = blockIdx.x / qtiles;
+  const uint32_t q0 = (qtiles - 1 - blockIdx.x % qtiles) * BM;  // heavy first
+  const int n = blocks_for(q0, Sq, Skv, causal);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->qd_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->kv_full[s], 1);
+      mbar_init(&bar->kv_empty[s], 1);
+    }
+    mbar_init(&bar->s_full, 1);
+    mbar_init(&bar->s_free, 4);
+    mbar_init(&bar->ds_full, 4);
+    mbar_init(&bar->dq_done, 1);
+    mbar_init(&bar->drain, 1);
+    bar->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bar->tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem;  // S at 0, dP at 128, dQ at 256
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bar->qd_full, 2 * TILE);
+      load_rows<2>(smem + Q_OFF_Q, &tmQ, &bar->qd_full, io.in, bh, Sq, q0);
+      load_rows<2>(smem + Q_OFF_DO, &tmDO, &bar->qd_full, io.in, bh, Sq, q0);
+      for (int j = 0; j < n && !*abort_flag; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&bar->kv_empty[s], ((j >> 1) & 1) ^ 1, status)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&bar->kv_full[s], 2 * TILE);
+        load_rows<2>(smem + Q_OFF_K + s * TILE, &tmK, &bar->kv_full[s], io.in, bh, Skv, j * BN);
+        load_rows<2>(smem + Q_OFF_V + s * TILE, &tmV, &bar->kv_full[s], io.in, bh, Skv, j * BN);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(&bar->qd_full, 0, status);
+      const uint32_t qa = smem_u32(smem + Q_OFF_Q), da = smem_u32(smem + Q_OFF_DO);
+      const uint32_t dsa = smem_u32(smem + Q_OFF_DS);
+      for (int j = 0; j < n && ok && !*abort_flag; ++j) {
+        const int s = j & 1;
+        const uint32_t ka = smem_u32(smem + Q_OFF_K + s * TILE);
+        const uint32_t va = smem_u32(smem + Q_OFF_V + s * TILE);
+        ok = mbar_wait(&bar->kv_full[s], (j >> 1) & 1, status);
+        if (ok && j > 0) ok = mbar_wait(&bar->s_free, (j - 1) & 1, status);
+        if (!ok) break;
+        tc_fence_after();
+        mma_kk(tmem + 0, qa, ka);    // S  = Q  K_j^T
+        mma_kk(tmem + 128, da, va);  // dP = dO V_j^T
+        tc_commit(&bar->s_full);
+        ok = mbar_wait(&bar->ds_full, j & 1, status);
+        if (!ok) break;
+        tc_fence_after();
+        mma_km(tmem + 256, dsa, ka, j > 0);  // dQ += dS K_j
+        tc_commit(&bar->dq_done);
+        tc_commit(&bar->kv_empty[s]);
+      }
+      if (!ok) *abort_flag = 1;
+      tc_commit(&bar->drain);
+      mbar_wait(&bar->drain, 0, status);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t m = q0 + row;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const bool valid = m < Sq;
+    const float lse = valid ? io.lse[(size_t)bh * Sq + m] : INFINITY;
+    const float dl = valid ? io.delta[(size_t)bh * Sq + m] : 0.0f;
+    uint8_t *ds_tile = smem + Q_OFF_DS;
+    bool ok = true;
+    for (int j = 0; j < n && ok; ++j) {
+      if (*abort_flag || !mbar_wait(&bar->s_full, j & 1, status)) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // dS smem is free once dQ(j-1) is done (it completed before S(j))
+      if (j > 0 && !mbar_wait(&bar->dq_done, (j - 1) & 1, status)) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      const uint32_t n0 = (uint32_t)j * BN;
+      uint32_t lim = Skv - 1;
+      if (causal && m < lim) lim = m;
+      const int lim_rel = (int)lim - (int)n0;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t rs[32], rp[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + c * 32, rs);
+        tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, rp);
+        tc_wait_ld(rs);
+        tc_wait_ld(rp);
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float ds[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int col = c * 32 + 2 * i + e;
+            const float p = (col <= lim_rel)
+                                ? fast_exp2(fmaf(__uint_as_float(rs[2 * i + e]), scale_log2, -lse))
+                                : 0.0f;
+            ds[e] = p * (__uint_as_float(rp[2 * i + e]) - dl);
+          }
+          pk[i] = pack_bf16(ds[0], ds[1]);
+        }
+        store_swizzled_chunk(ds_tile, row, c, pk);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bar->s_free);
+        mbar_arrive(&bar->ds_full);
+      }
+    }
+    if (ok && n > 0) {
+      if (mbar_wait(&bar->dq_done, (n - 1) & 1, status)) {
+        tc_fence_after();
+        uint16_t *dst = io.d0 + ((size_t)(bh / io.in.H) * Sq + m) * io.ldd +
+                        (size_t)(bh % io.in.H) * D;
+        store_row_bf16(tmem + lane_base + 256, dst, scale, valid);
+      } else {
+        *abort_flag = 1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dK, dV
+// ---------------------------------------------------------------------------
+constexpr int K_OFF_K = 0, K_OFF_V = TILE, K_OFF_Q = 2 * TILE, K_OFF_DO = 3 * TILE,
+              K_OFF_PT = 4 * TILE, K_OFF_DST = 5 * TILE, K_OFF_LSE = 6 * TILE,
+              K_OFF_BAR = K_OFF_LSE + 2 * 2 * 128 * 4;
+constexpr int K_SMEM = K_OFF_BAR + 256 + 1024;
+static_assert(K_SMEM <= 232448, "dkdv smem");
+
+struct KBars {
+  uint64_t kv_full, qd_full, qd_empty, s_full, s_free, p_full, pdone, staged, drain;
+  uint32_t tmem;
+  int abort_flag;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+    bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const BwdIO io, uint32_t BH, uint32_t Sq, uint32_t Skv, float scale,
+                    float scale_log2, int causal, uint32_t kblocks, int *status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  KBars *bar = reinterpret_cast<KBars *>(smem + K_OFF_BAR);
+  volatile int *abort_flag = &bar->abort_flag;
+  float *lse_s = reinterpret_cast<float *>(smem + K_OFF_LSE);  // [2][128]
+  float *del_s = lse_s + 2 * 128;                              // [2][128]
+  const uint32_t bh = blockIdx.x / kblocks;
+  const uint32_t k0 = (blockIdx.x % kblocks) * BN;
+  const uint32_t qtiles = (Sq + BM - 1) / BM;
+  const uint32_t i0 = causal ? min(k0 / BM, qtiles) : 0;  // first query tile that sees k0
+  const int n = (int)(qtiles - i0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->kv_full, 1);
+    mbar_init(&bar->qd_full, 1);
+    mbar_init(&bar->qd_empty, 1);
+    mbar_init(&bar->s_full, 1);
+    mbar_init(&bar->s_free, 4);
+    mbar_init(&bar->p_full, 4);
+    mbar_init(&bar->pdone, 1);
+    mbar_init(&bar->staged, 128);
+    mbar_init(&bar->drain, 1);
+    bar->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bar->tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem;  // S^T 0, dP^T 128, dV 256, dK 384
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bar->kv_full, 2 * TILE);
+      load_rows<2>(smem + K_OFF_K, &tmK, &bar->kv_full, io.in, bh, Skv, k0);
+      load_rows<2>(smem + K_OFF_V, &tmV, &bar->kv_full, io.in, bh, Skv, k0);
+      for (int it = 0; it < n && !*abort_flag; ++it) {
+        if (!mbar_wait(&bar->qd_empty, (it & 1) ^ 1, status)) {
+          *abort_flag = 1;
+          break;
+        }
+        const uint32_t qs = (i0 + it) * BM;
+        mbar_arrive_expect_tx(&bar->qd_full, 2 * TILE);
+        load_rows<2>(smem + K_OFF_Q, &tmQ, &bar->qd_full, io.in, bh, Sq, qs);
+        load_rows<2>(smem + K_OFF_DO, &tmDO, &bar->qd_full, io.in, bh, Sq, qs);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(&bar->kv_full, 0, status);
+      const uint32_t ka = smem_u32(smem + K_OFF_K), va = smem_u32(smem + K_OFF_V);
+      const uint32_t qa = smem_u32(smem + K_OFF_Q), da = smem_u32(smem + K_OFF_DO);
+      const uint32_t pa = smem_u32(smem + K_OFF_PT), dsa = smem_u32(smem + K_OFF_DST);
+      for (int it = 0; it < n && ok && !*abort_flag; ++it) {
+        ok = mbar_wait(&bar->qd_full, it & 1, status);
+        if (ok && it > 0) ok = mbar_wait(&bar->s_free, (it - 1) & 1, status);
+        if (!ok) break;
+        tc_fence_after();
+        mma_kk(tmem + 0, ka, qa);    // S^T  = K  Q_i^T
+        mma_kk(tmem + 128, va, da);  // dP^T = V dO_i^T
+        tc_commit(&bar->s_full);
+        ok = mbar_wait(&bar->p_full, it & 1, status);
+        if (!ok) break;
+        tc_fence_after();
+        mma_km(tmem + 256, pa, da, it > 0);   // dV += P^T  dO_i
+        mma_km(tmem + 384, dsa, qa, it > 0);  // dK += dS^T Q_i
+        tc_commit(&bar->pdone);
+        tc_commit(&bar->qd_empty);
+      }
+      if (!ok) *abort_flag = 1;
+      tc_commit(&bar->drain);
+      mbar_wait(&bar->drain, 0, status);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // key within the block
+    const int tid = threadIdx.x - 64;     // 0..127 over the softmax warps
+    const uint32_t key = k0 + row;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    uint8_t *pt_tile = smem + K_OFF_PT;
+    uint8_t *dst_tile = smem + K_OFF_DST;
+    bool ok = true;
+    for (int it = 0; it < n && ok; ++it) {
+      const uint32_t qs = (i0 + it) * BM;
+      // stage this tile's lse / delta (one query per thread) in buffer it & 1;
+      // every thread passed phase it-1 only after all had finished tile it-2,
+      // so the buffer is free.  Bounded wait, like every other.
+      {
+        const uint32_t q = qs + tid;
+        lse_s[(it & 1) * 128 + tid] = q < Sq ? io.lse[(size_t)bh * Sq + q] : INFINITY;
+        del_s[(it & 1) * 128 + tid] = q < Sq ? io.delta[(size_t)bh * Sq + q] : 0.0f;
+        mbar_arrive(&bar->staged);
+      }
+      if (*abort_flag || !mbar_wait(&bar->staged, it & 1, status) ||
+          !mbar_wait(&bar->s_full, it & 1, status)) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // P^T / dS^T smem free once dV / dK of the previous tile are done
+      if (it > 0 && !mbar_wait(&bar->pdone, (it - 1) & 1, status)) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      // query q = qs + col is visible to this key iff q >= key (causal),
+      // q < Sq and key < Skv
+      int first_rel = causal ? (int)key - (int)qs : 0;  // first visible col
+      if (first_rel < 0) first_rel = 0;
+      const int last_rel = key < Skv ? (int)min(Sq - 1 - qs, (uint32_t)127) : -1;
+      const float *ls = lse_s + (it & 1) * 128;
+      const float *dd = del_s + (it & 1) * 128;
+#pragma unroll 1
+      for (int c = 0; c < BM / 32; ++c) {
+        uint32_t rs[32], rp[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + c * 32, rs);
+        tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, rp);
+        tc_wait_ld(rs);
+        tc_wait_ld(rp);
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float p[2], ds[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int col = c * 32 + 2 * i + e;
+            const bool vis = col >= first_rel && col <= last_rel;
+            p[e] = vis ? fast_exp2(fmaf(__uint_as_float(rs[2 * i + e]), scale_log2, -ls[col])) : 0.0f;
+            ds[e] = p[e] * (__uint_as_float(rp[2 * i + e]) - dd[col]);
+          }
+          pk[i] = pack_bf16(p[0], p[1]);
+          dk[i] = pack_bf16(ds[0], ds[1]);
+        }
+        store_swizzled_chunk(pt_tile, row, c, pk);
+        store_swizzled_chunk(dst_tile, row, c, dk);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bar->s_free);
+        mbar_arrive(&bar->p_full);
+      }
+    }
+    const bool valid = key < Skv;
+    uint16_t *dk_dst = io.d0 + ((size_t)(bh / io.in.H) * Skv + key) * io.ldd + (size_t)(bh % io.in.H) * D;
+    uint16_t *dv_dst = io.d1 + ((size_t)(bh / io.in.H) * Skv + key) * io.ldd + (size_t)(bh % io.in.H) * D;
+    if (ok && n > 0) {
+      if (mbar_wait(&bar->pdone, (n - 1) & 1, status)) {
+        tc_fence_after();
+        store_row_bf16(tmem + lane_base + 256, dv_dst, 1.0f, valid);
+        store_row_bf16(tmem + lane_base + 384, dk_dst, scale, valid);
+      } else {
+        *abort_flag = 1;
+      }
+    } else if (ok && valid) {
+      // no query sees these keys: zero gradients
+      for (int c = 0; c < D; c += 8) {
+        *reinterpret_cast<uint4 *>(dk_dst + c) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4 *>(dv_dst + c) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+int make_map(BwppCudaCtx *ctx, CUtensorMap *map, const void *base, uint32_t S, uint32_t BH,
+             uint32_t H, uint32_t ld) {
+  bwpp_encode_tiled_fn enc = bwpp_get_encode_tiled();
+  if (!enc) return bwpp_set_error(ctx, BWPP_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {D, H, (cuuint64_t)(BH / H) * S};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)ld * 2};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_CUDA, "attention bwd tensor map failed (%d)", (int)r);
+  return BWPP_CUDA_OK;
+}
+
+bool g_attr[64] = {};
+
+}  // namespace
+
+// Token-major bf16 inputs (q/k/v with pitch ld_in, dO with pitch ld_do, head h
+// at column h*128), lse / delta [B*H, S]; writes dQ, dK, dV token-major bf16
+// with pitch ldd.  Sq == Skv == S, head dim 128.
+int bwpp_attention_bwd_train(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                             const uint16_t *v, uint32_t ld_in, const uint16_t *dout,
+                             uint32_t ld_do, const float *lse, const float *delta,
+                             uint32_t B, uint32_t H, uint32_t S, float scale, int causal,
+                             uint16_t *dq, uint16_t *dk, uint16_t *dv, uint32_t ldd) {
+  if (S == 0 || !(scale > 0.0f) || (ld_in % 8) || (ld_do % 8) || (ldd % 8))
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "attention bwd: layout");
+  const uint32_t BH = B * H;
+  CUtensorMap tq, tk, tv, tdo;
+  int rc = make_map(ctx, &tq, q, S, BH, H, ld_in);
+  if (!rc) rc = make_map(ctx, &tk, k, S, BH, H, ld_in);
+  if (!rc) rc = make_map(ctx, &tv, v, S, BH, H, ld_in);
+  if (!rc) rc = make_map(ctx, &tdo, dout, S, BH, H, ld_do);
+  if (rc) return rc;
+  if (ctx->device < 64 && !g_attr[ctx->device]) {
+    rc = bwpp_check_cuda(ctx,
+                         cudaFuncSetAttribute(bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              Q_SMEM),
+                         "bwd dq smem");
+    if (!rc)
+      rc = bwpp_check_cuda(ctx,
+                           cudaFuncSetAttribute(bwd_dkdv_kernel,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, K_SMEM),
+                           "bwd dkdv smem");
+    if (rc) return rc;
+    g_attr[ctx->device] = true;
+  }
+  const float sl2 = scale * 1.4426950408889634f;
+  const uint32_t tiles = (S + 127) / 128;
+  BwdIO io{dq, nullptr, ldd, lse, delta, AttnIO{nullptr, nullptr, 0, nullptr, 1, H}};
+  bwd_dq_kernel<<<tiles * BH, THREADS, Q_SMEM, ctx->stream>>>(tq, tk, tv, tdo, io, BH, S, S, scale,
+                                                              sl2, causal, tiles, ctx->status_word);
+  BWPP_LAUNCH_CHECK(ctx, "attention bwd dq");
+  BwdIO io2{dk, dv, ldd, lse, delta, AttnIO{nullptr, nullptr, 0, nullptr, 1, H}};
+  bwd_dkdv_kernel<<<tiles * BH, THREADS, K_SMEM, ctx->stream>>>(tq, tk, tv, tdo, io2, BH, S, S, scale,
+                                                                sl2, causal, tiles, ctx->status_word);
+  BWPP_LAUNCH_CHECK(ctx, "attention bwd dkdv");
+  return BWPP_CUDA_OK;
+}
+
+int bwpp_attention_fwd_train(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                             const uint16_t *v, uint32_t ld_in, uint32_t B, uint32_t H,
+                             uint32_t S, uint32_t D, float scale, int causal, uint16_t *o,
+                             uint32_t ldo, float *lse);
+int bwpp_attn_delta(BwppCudaCtx *ctx, const uint16_t *dO, const uint16_t *O, float *delta,
+                    uint32_t B, uint32_t S, uint32_t H, uint32_t Dh);
+
+extern "C" {
+
+int bwpp_cuda_attention_fwd_lse_bf16(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                                     const uint16_t *v, uint32_t ld_qkv, uint32_t B, uint32_t H,
+                                     uint32_t S, float scale, int causal, uint16_t *o,
+                                     uint32_t ldo, float *lse) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (!q || !k || !v || !o || !lse || ld_qkv < H * D || ldo < H * D)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "attention fwd_lse: bad args");
+  if (B == 0 || H == 0 || S == 0) return BWPP_CUDA_OK;
+  return bwpp_attention_fwd_train(ctx, q, k, v, ld_qkv, B, H, S, D, scale, causal, o, ldo, lse);
+}
+
+int bwpp_cuda_attention_bwd_bf16(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                                 const uint16_t *v, uint32_t ld_qkv, const uint16_t *o,
+                                 uint32_t ldo, const uint16_t *dout, uint32_t ld_do,
+                                 const float *lse, uint32_t B, uint32_t H, uint32_t S,
+                                 float scale, int causal, uint16_t *dq, uint16_t *dk,
+                                 uint16_t *dv, uint32_t ldd) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv || ld_qkv < H * D ||
+      ldo < H * D || ld_do < H * D || ldd < H * D)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "attention bwd: bad args");
+  if (B == 0 || H == 0 || S == 0) return BWPP_CUDA_OK;
+  if (ldo != H * D)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "attention bwd: O must be dense");
+  float *delta = (float *)bwpp_ctx_workspace(ctx, sizeof(float) * (size_t)B * H * S);
+  if (!delta) return BWPP_CUDA_ERR_NOMEM;
+  if (ld_do != H * D)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "attention bwd: dO must be dense");
+  rc = bwpp_attn_delta(ctx, dout, o, delta, B, S, H, D);
+  if (rc) return rc;
+  return bwpp_attention_bwd_train(ctx, q, k, v, ld_qkv, dout, ld_do, lse, delta, B, H, S, scale,
+                                  causal, dq, dk, dv, ldd);
+}
+
+}  // extern "C"

@@ -24,14 +24,11 @@
 //
 // Every wait is bounded (BWPP_WAIT_LIMIT_NS); on expiry the kernel records
 // BWPP_CUDA_ERR_TIMEOUT, unwinds, frees TMEM and returns.
-#include "bwpp_cuda_internal.cuh"
+#include "attention_common.cuh"
 
 namespace {
 
-constexpr int BM = 128;  // rows per Q tile (two tiles per CTA)
-constexpr int BN = 128;  // keys per K/V block
-constexpr int BOX = 128 * 64 * 2;  // one TMA box: 128 rows x 64 bf16 (16 KB)
-constexpr int P_TILE = BM * BN * 2;  // 32 KB
+using namespace bwpp_attn;
 constexpr int THREADS = 320;
 
 template <int D>
@@ -62,79 +59,12 @@ struct Bars {
   int abort_flag;
 };
 
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map,
-                                            uint64_t *bar, int32_t x, int32_t y,
-                                            int32_t z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::"
-      "bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z),
-      "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// Two fp32 lanes in one 64-bit register: Blackwell issues one FMA / ADD for
-// both (fma.rn.f32x2 / add.rn.f32x2).
-__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-
-__device__ __forceinline__ void f2unpack(uint64_t v, float &lo, float &hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-
-__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-
-__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-
-// Number of 128-key blocks tile X (first row r0) needs.
-__device__ __forceinline__ int blocks_for(uint32_t r0, uint32_t Sq, uint32_t Skv,
-                                          int causal) {
-  if (r0 >= Sq) return 0;
-  int n = (int)((Skv + BN - 1) / BN);
-  if (causal) {
-    const uint32_t last = min(r0 + BM - 1, Sq - 1);
-    n = min(n, (int)(last / BN) + 1);
-  }
-  return n;
-}
-
-// 10 warps: two SM sub-partitions host three warps each, which caps the
-// kernel at 168 registers per thread (16384 / (3 * 32), rounded down to 8).
 template <int D>
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
-                        float *__restrict__ out, uint32_t BH, uint32_t Sq,
+                        const AttnIO io, uint32_t BH, uint32_t Sq,
                         uint32_t Skv, float scale_log2, int causal,
                         uint32_t pairs, int *status) {
   using C = Cfg<D>;
@@ -189,16 +119,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       mbar_arrive_expect_tx(&bar->q_full, 2 * C::TILE);
       for (int X = 0; X < 2; ++X)
-        for (int b = 0; b < C::BOXES; ++b)
-          tma_load_3d(smem + C::OFF_Q + X * C::TILE + b * BOX, &tmQ, &bar->q_full,
-                      b * 64, (int32_t)(q0 + X * BM), (int32_t)bh);
+        load_rows<C::BOXES>(smem + C::OFF_Q + X * C::TILE, &tmQ, &bar->q_full, io, bh, Sq,
+                            q0 + X * BM);
       auto load_k = [&](int j) -> bool {
         const int s = j & 1;
         if (!mbar_wait(&bar->k_empty[s], ((j >> 1) & 1) ^ 1, status)) return false;
         mbar_arrive_expect_tx(&bar->k_full[s], C::TILE);
-        for (int b = 0; b < C::BOXES; ++b)
-          tma_load_3d(smem + C::OFF_K + s * C::TILE + b * BOX, &tmK, &bar->k_full[s],
-                      b * 64, j * BN, (int32_t)bh);
+        load_rows<C::BOXES>(smem + C::OFF_K + s * C::TILE, &tmK, &bar->k_full[s], io, bh, Skv,
+                            j * BN);
         return true;
       };
       bool ok = n > 0 ? load_k(0) : true;
@@ -206,9 +134,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (j + 1 < n && !load_k(j + 1)) { ok = false; break; }
         if (!mbar_wait(&bar->v_empty, (j & 1) ^ 1, status)) { ok = false; break; }
         mbar_arrive_expect_tx(&bar->v_full, C::TILE);
-        for (int b = 0; b < C::BOXES; ++b)
-          tma_load_3d(smem + C::OFF_V + b * BOX, &tmV, &bar->v_full, b * 64, j * BN,
-                      (int32_t)bh);
+        load_rows<C::BOXES>(smem + C::OFF_V, &tmV, &bar->v_full, io, bh, Skv, j * BN);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -430,20 +356,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (mbar_wait(&bar->pv_done[X], (nb - 1) & 1, status)) {
         tc_fence_after();
         const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-        float *orow = out + ((size_t)bh * Sq + m_row) * D;
         const bool valid = m_row < Sq;
+        if (valid && io.lse)
+          io.lse[(size_t)bh * Sq + m_row] =
+              l_run > 0.0f ? m_run * scale_log2 + __log2f(l_run) : -INFINITY;
+        float *orow = io.out_f32 ? io.out_f32 + ((size_t)bh * Sq + m_row) * D : nullptr;
+        uint16_t *brow = io.out_bf16 ? io.out_bf16 + ((size_t)(bh / io.H) * Sq + m_row) * io.ldo +
+                                           (size_t)(bh % io.H) * D
+                                     : nullptr;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(o_col + c * 32, r);
           tc_wait_ld(r);
-          if (valid) {
+          if (valid && orow) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               __stcs(reinterpret_cast<float4 *>(orow + c * 32) + i,
                      make_float4(__uint_as_float(r[4 * i]) * inv, __uint_as_float(r[4 * i + 1]) * inv,
                                  __uint_as_float(r[4 * i + 2]) * inv,
                                  __uint_as_float(r[4 * i + 3]) * inv));
+          }
+          if (valid && brow) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              *reinterpret_cast<uint4 *>(brow + c * 32 + 8 * i) = make_uint4(
+                  pack_bf16(__uint_as_float(r[8 * i]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
+                  pack_bf16(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
+                  pack_bf16(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
+                  pack_bf16(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
           }
         }
       } else {
@@ -460,13 +401,22 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-int make_tmap_3d(BwppCudaCtx *ctx, CUtensorMap *map, const void *base,
-                 uint32_t D, uint32_t S, uint32_t BH) {
+// head-major: dims {D, S, BH}; token-major (ld > 0): dims {D, H, B*S}, row pitch ld
+int make_tmap_3d(BwppCudaCtx *ctx, CUtensorMap *map, const void *base, uint32_t D,
+                 uint32_t S, uint32_t BH, uint32_t H, uint32_t ld) {
   bwpp_encode_tiled_fn enc = bwpp_get_encode_tiled();
   if (!enc) return bwpp_set_error(ctx, BWPP_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[3] = {D, S, BH};
-  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+  if (ld == 0) {
+    dims[0] = D; dims[1] = S; dims[2] = BH;
+    strides[0] = (cuuint64_t)D * 2; strides[1] = (cuuint64_t)S * D * 2;
+    box[0] = 64; box[1] = 128; box[2] = 1;
+  } else {
+    dims[0] = D; dims[1] = H; dims[2] = (cuuint64_t)(BH / H) * S;
+    strides[0] = (cuuint64_t)D * 2; strides[1] = (cuuint64_t)ld * 2;
+    box[0] = 64; box[1] = 1; box[2] = 128;
+  }
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -481,11 +431,12 @@ bool g_attr_set[2][64] = {};
 
 template <int D>
 int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *v,
-           float *o, uint32_t BH, uint32_t Sq, uint32_t Skv, float scale, int causal) {
+           uint32_t ld_in, uint32_t BH, uint32_t H, uint32_t Sq, uint32_t Skv, float scale,
+           int causal, const AttnIO &io) {
   CUtensorMap tq, tk, tv;
-  int rc = make_tmap_3d(ctx, &tq, q, D, Sq, BH);
-  if (!rc) rc = make_tmap_3d(ctx, &tk, k, D, Skv, BH);
-  if (!rc) rc = make_tmap_3d(ctx, &tv, v, D, Skv, BH);
+  int rc = make_tmap_3d(ctx, &tq, q, D, Sq, BH, H, ld_in);
+  if (!rc) rc = make_tmap_3d(ctx, &tk, k, D, Skv, BH, H, ld_in);
+  if (!rc) rc = make_tmap_3d(ctx, &tv, v, D, Skv, BH, H, ld_in);
   if (rc) return rc;
   const int di = D == 128 ? 1 : 0;
   if (ctx->device < 64 && !g_attr_set[di][ctx->device]) {
@@ -502,7 +453,7 @@ int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_
   if (grid > 0x7fffffffull)
     return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "attention: grid too large");
   attention_tc_kernel<D><<<(unsigned)grid, THREADS, Cfg<D>::SMEM, ctx->stream>>>(
-      tq, tk, tv, o, BH, Sq, Skv, scale * 1.4426950408889634f, causal, pairs,
+      tq, tk, tv, io, BH, Sq, Skv, scale * 1.4426950408889634f, causal, pairs,
       ctx->status_word);
   BWPP_LAUNCH_CHECK(ctx, "attention tcgen05");
   return BWPP_CUDA_OK;
@@ -521,7 +472,21 @@ int bwpp_attention_tc_launch(BwppCudaCtx *ctx, const uint16_t *q,
   // the lazy running max assumes a positive softmax scale
   if (!al(q) || !al(k) || !al(v) || !al(o) || Skv == 0 || !(scale > 0.0f))
     return BWPP_CUDA_ERR_UNSUPPORTED;
-  if (D == 128) return launch<128>(ctx, q, k, v, o, BH, Sq, Skv, scale, causal);
-  if (D == 64) return launch<64>(ctx, q, k, v, o, BH, Sq, Skv, scale, causal);
+  AttnIO io{o, nullptr, 0, nullptr, 0, 1};
+  if (D == 128) return launch<128>(ctx, q, k, v, 0, BH, 1, Sq, Skv, scale, causal, io);
+  if (D == 64) return launch<64>(ctx, q, k, v, 0, BH, 1, Sq, Skv, scale, causal, io);
   return BWPP_CUDA_ERR_UNSUPPORTED;
+}
+
+// Training-step form: token-major bf16 inputs (row pitch ld_in, head h at
+// column h*D), bf16 token-major output (pitch ldo) and the per-query base-2
+// log-sum-exp [B*H, S] the backward pass needs.  Sq == Skv == S.
+int bwpp_attention_fwd_train(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                             const uint16_t *v, uint32_t ld_in, uint32_t B, uint32_t H,
+                             uint32_t S, uint32_t D, float scale, int causal, uint16_t *o,
+                             uint32_t ldo, float *lse) {
+  if (D != 128 || !(scale > 0.0f) || S == 0 || (ld_in % 8) || (ldo % 8))
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "attention train: D=128 only");
+  AttnIO io{nullptr, o, ldo, lse, 1, H};
+  return launch<128>(ctx, q, k, v, ld_in, B * H, H, S, S, scale, causal, io);
 }

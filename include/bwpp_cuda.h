@@ -172,6 +172,27 @@ int bwpp_cuda_attention_bf16(BwppCudaCtx *ctx, const uint16_t *q,
                              uint32_t B, uint32_t H, uint32_t Sq, uint32_t Skv,
                              uint32_t D, float scale, int causal);
 
+/* Attention for training (no reference counterpart: the reference has no
+ * attention backward).  Token-major bf16 tensors: row b*S + s, head h at
+ * column h*128 (row pitches ld_*), head dim 128, Sq == Skv == S.
+ * Forward writes O (bf16, pitch ldo) and the base-2 log-sum-exp of the
+ * scaled scores per query, lse [B*H, S] fp32.  Backward takes O, dO and lse
+ * and writes dQ, dK, dV (bf16, pitch ldd); it uses ctx scratch
+ * (4 * B*H*S bytes). */
+int bwpp_cuda_attention_fwd_lse_bf16(BwppCudaCtx *ctx, const uint16_t *q,
+                                     const uint16_t *k, const uint16_t *v,
+                                     uint32_t ld_qkv, uint32_t B, uint32_t H,
+                                     uint32_t S, float scale, int causal,
+                                     uint16_t *o, uint32_t ldo, float *lse);
+int bwpp_cuda_attention_bwd_bf16(BwppCudaCtx *ctx, const uint16_t *q,
+                                 const uint16_t *k, const uint16_t *v,
+                                 uint32_t ld_qkv, const uint16_t *o,
+                                 uint32_t ldo, const uint16_t *dout,
+                                 uint32_t ld_do, const float *lse, uint32_t B,
+                                 uint32_t H, uint32_t S, float scale,
+                                 int causal, uint16_t *dq, uint16_t *dk,
+                                 uint16_t *dv, uint32_t ldd);
+
 /* RMSNorm forward, runtime/cpu/bwpp_cpu_ref.c:63-90: y = x / sqrt(mean(x^2) +
  * eps) * gamma + beta; gamma / beta may be NULL. */
 int bwpp_cuda_rmsnorm_fwd_f32(BwppCudaCtx *ctx, const float *x, float *y,
@@ -262,6 +283,60 @@ int bwpp_cuda_softmax_fwd_f32(BwppCudaCtx *ctx, const float *x, float *y,
  * leading dim ld_src). */
 int bwpp_cuda_cast_f32_bf16(BwppCudaCtx *ctx, const float *src, uint16_t *dst,
                             uint32_t rows, uint32_t cols, uint32_t ld_src);
+
+/* ---- data-parallel communicator (NCCL) ----------------------------------- */
+/* The gradient allreduce of the tiny_model training step (no reference
+ * counterpart: the reference has no multi-device code).  NCCL is loaded at
+ * run time (libnccl.so.2), sharing a copy the process already has. */
+typedef struct BwppCudaComm BwppCudaComm;
+/* Rank 0 creates the 128-byte id and hands it to every rank. */
+int bwpp_cuda_comm_unique_id(unsigned char *id128);
+int bwpp_cuda_comm_create(BwppCudaComm **out, const unsigned char *id128,
+                          int rank, int nranks, int device);
+/* In-place sum over ranks, asynchronous on `stream`. */
+int bwpp_cuda_comm_allreduce_sum_f32(BwppCudaComm *comm, float *buf,
+                                     size_t count, void *stream);
+int bwpp_cuda_comm_destroy(BwppCudaComm *comm);
+
+/* ---- tiny_model training step ------------------------------------------- */
+/* The decoder block of examples/tiny_model.bwpp:4-58 in the shape of the
+ * benchmark config: `layers` pre-RMSNorm blocks, causal attention with
+ * `heads` x 128, SiLU-gated MLP of width `ffn`, MSE loss.  Forward and
+ * backward follow the autodiff rules of compiler/graph_ir.c:1485-1839
+ * (matmul, silu, rmsnorm) plus the attention backward; weights are fp32
+ * masters with bf16 compute copies, initialised N(0, 0.02) (norm gains 1)
+ * from `seed`. */
+typedef struct {
+  uint32_t layers, d_model, heads, head_dim, ffn, batch, seq;
+  float eps;
+} BwppCudaTinyModelConfig;
+
+typedef struct BwppCudaTinyModel BwppCudaTinyModel;
+
+int bwpp_cuda_tiny_model_create(BwppCudaCtx *ctx,
+                                const BwppCudaTinyModelConfig *cfg,
+                                uint64_t seed, BwppCudaTinyModel **out);
+int bwpp_cuda_tiny_model_destroy(BwppCudaTinyModel *model);
+/* Parameters form one flat fp32 vector; per layer the order is g1 [D],
+ * Wqkv [D,3D], Wo [D,D], g2 [D], W13 [D,2F] (gate | up), W2 [F,D]. */
+size_t bwpp_cuda_tiny_model_param_count(const BwppCudaTinyModel *model);
+/* Copies the fp32 parameters and / or the gradients of the last step out
+ * (host or device destinations; NULL skips).  Synchronous. */
+int bwpp_cuda_tiny_model_get(BwppCudaTinyModel *model, float *params_out,
+                             float *grads_out);
+/* Replaces the fp32 parameters (host or device source) and re-derives the
+ * bf16 compute copies.  Synchronous. */
+int bwpp_cuda_tiny_model_set_params(BwppCudaTinyModel *model,
+                                    const float *params_in);
+/* One training step on inputs x, target [batch*seq, d_model] fp32 (host or
+ * device memory; both are staged into the model's arena):
+ * forward, loss, backward into the gradient buffer, then (comm != NULL) the
+ * gradient sum over ranks and (lr != 0) w -= lr * mean gradient.  The loss
+ * is copied to *loss_out (host or device) when loss_out != NULL.
+ * Asynchronous on the ctx stream. */
+int bwpp_cuda_tiny_model_step(BwppCudaTinyModel *model, const float *x,
+                              const float *target, float lr,
+                              BwppCudaComm *comm, float *loss_out);
 
 /* ---- 2. mirrors of runtime/cpu/bwpp_cpu_ref.h:6-58 ---------------------- */
 /* Same argument lists; host or device pointers; synchronous; the calling

@@ -1,0 +1,154 @@
+"""Training path on the GPU: attention forward with log-sum-exp and attention
+backward, then the whole tiny_model step (BASELINE configs[4] at reduced
+size), against float64 torch autograd on the CPU.
+
+The reference has no backward kernels and no model step (parity unpinned by
+the reference); the checker is a float64 restatement of the same math.  For
+the model step the restatement rounds to bf16 at the points where the GPU
+stores bf16 (straight-through in the backward), so the comparison isolates
+kernel error from the chosen storage precision.
+Tolerances: relative Frobenius <= 1e-2 for attention (north star bound for
+contractions); <= 3e-2 for the composed gradients of the whole step (every
+layer's backward rounds its activation gradients to bf16 once more).
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import bwpp
+import oracle as O
+from conftest import rel_fro
+
+pytestmark = pytest.mark.gpu
+
+
+def bf16(t):
+    return t.to(torch.bfloat16)
+
+
+def ref_attention(q, k, v, scale, causal):
+    s = (q @ k.transpose(-1, -2)) * scale
+    if causal:
+        S = s.shape[-1]
+        s = s.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool), 1), float("-inf"))
+    return torch.softmax(s, -1) @ v, torch.logsumexp(s, -1) / math.log(2.0)
+
+
+def heads(t, B, S, H, D=128):  # token-major [B*S, H*D] -> [B, H, S, D]
+    return t.reshape(B, S, H, D).permute(0, 2, 1, 3)
+
+
+@pytest.mark.parametrize("B,H,S", [(2, 2, 256), (1, 3, 384), (2, 1, 128)])
+@pytest.mark.parametrize("causal", [1, 0])
+def test_attention_fwd_lse_and_bwd(ctx, B, H, S, causal):
+    D, lib = 128, bwpp.load()
+    g = torch.Generator(device="cuda").manual_seed(B * 100 + S + causal)
+    T, HD = B * S, H * 128
+    q, k, v, do = (bf16(torch.randn(T, HD, device="cuda", generator=g)) for _ in range(4))
+    o = torch.empty(T, HD, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(B * H * S, device="cuda")
+    scale = 1.0 / math.sqrt(D)
+    ctx.check(lib.bwpp_cuda_attention_fwd_lse_bf16(ctx.handle, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                                   HD, B, H, S, scale, causal, o.data_ptr(), HD,
+                                                   lse.data_ptr()), "fwd_lse")
+    dq, dk, dv = (torch.empty(T, HD, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+    ctx.check(lib.bwpp_cuda_attention_bwd_bf16(ctx.handle, q.data_ptr(), k.data_ptr(), v.data_ptr(), HD,
+                                               o.data_ptr(), HD, do.data_ptr(), HD, lse.data_ptr(), B, H,
+                                               S, scale, causal, dq.data_ptr(), dk.data_ptr(),
+                                               dv.data_ptr(), HD), "bwd")
+    ctx.sync()
+    qf, kf, vf, dof = (heads(t.double().cpu(), B, S, H).requires_grad_(True) for t in (q, k, v, do))
+    ro, rlse = ref_attention(qf, kf, vf, scale, causal)
+    ro.backward(dof.detach())
+    got_o = heads(o.double().cpu(), B, S, H)
+    assert rel_fro(got_o.numpy(), ro.detach().numpy()) <= 1e-2
+    assert np.abs(lse.cpu().numpy().reshape(B, H, S) - rlse.detach().numpy()).max() <= 2e-2
+    for got, ref in ((dq, qf.grad), (dk, kf.grad), (dv, vf.grad)):
+        err = rel_fro(heads(got.double().cpu(), B, S, H).numpy(), ref.numpy())
+        assert err <= 1e-2, err
+
+
+# ---- tiny_model step -----------------------------------------------------------
+
+def split_params(flat, L, D, F):
+    out, off = [], 0
+    for _ in range(L):
+        layer = {}
+        for name, n, shape in (("g1", D, (D,)), ("wqkv", 3 * D * D, (D, 3 * D)), ("wo", D * D, (D, D)),
+                               ("g2", D, (D,)), ("w13", 2 * F * D, (D, 2 * F)), ("w2", F * D, (F, D))):
+            layer[name] = flat[off:off + n].reshape(shape)
+            off += n
+        out.append(layer)
+    return out
+
+
+def st_bf16(t):
+    """Round to bf16 in the forward, identity in the backward."""
+    return t + (t.to(torch.bfloat16).to(t.dtype) - t).detach()
+
+
+def ref_model_step(flat, x, tgt, L, D, H, F, B, S, eps):
+    params = flat.clone().requires_grad_(True)
+    P = split_params(params, L, D, F)
+    h = x.clone()
+    scale = 1.0 / math.sqrt(128)
+
+    def rms(u, gam):
+        return u * torch.rsqrt((u * u).mean(-1, keepdim=True) + eps) * gam
+
+    for p in P:
+        w = {k_: st_bf16(v_) if v_.dim() == 2 else v_ for k_, v_ in p.items()}
+        n1 = st_bf16(rms(h, w["g1"]))
+        qkv = st_bf16(n1 @ w["wqkv"])
+        q, k, v = (heads(qkv[:, i * D:(i + 1) * D], B, S, H) for i in range(3))
+        o, _ = ref_attention(q, k, v, scale, True)
+        o = st_bf16(o.permute(0, 2, 1, 3).reshape(B * S, D))
+        h = h + o @ w["wo"]
+        n2 = st_bf16(rms(h, w["g2"]))
+        gu = st_bf16(n2 @ w["w13"])
+        a = st_bf16(torch.nn.functional.silu(gu[:, :F]) * gu[:, F:])
+        h = h + a @ w["w2"]
+    loss = ((h - tgt) ** 2).mean()
+    loss.backward()
+    return float(loss.detach()), params.grad
+
+
+def test_tiny_model_step_vs_float64():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    L, D, H, F, B, S, eps = 2, 256, 2, 512, 2, 256, 1e-5
+    ctx = bwpp.Ctx(0)
+    model = bwpp.TinyModel(ctx, L, D, H, F, B, S, eps, seed=3)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(B * S, D, device="cuda", generator=g)
+    tgt = torch.randn(B * S, D, device="cuda", generator=g)
+    params = torch.empty(model.count, device="cuda")
+    grads = torch.empty(model.count, device="cuda")
+    model.get(params, None)
+    loss = torch.empty(1, device="cuda")
+    model.step(x, tgt, lr=0.0, loss_out=loss)
+    model.get(None, grads)
+    rloss, rgrad = ref_model_step(params.double().cpu(), x.double().cpu(), tgt.double().cpu(),
+                                  L, D, H, F, B, S, eps)
+    assert abs(float(loss) - rloss) <= 2e-3 * abs(rloss)
+    gp = split_params(grads.double().cpu(), L, D, F)
+    rp = split_params(rgrad, L, D, F)
+    for l in range(L):
+        for name in gp[l]:
+            err = rel_fro(gp[l][name].numpy(), rp[l][name].numpy())
+            assert err <= 3e-2, (l, name, err)
+    # SGD: params' = params - lr * grads (one GPU: the mean is the gradient)
+    before = params.clone()
+    model.step(x, tgt, lr=0.1, loss_out=loss)
+    model.get(params, grads)
+    assert torch.allclose(params, before - 0.1 * grads, rtol=0, atol=1e-6)
+    # the step is deterministic
+    g1 = grads.clone()
+    model.set_params(before)
+    model.step(x, tgt, lr=0.0, loss_out=loss)
+    model.get(None, grads)
+    assert torch.equal(grads, g1)
+    model.close()
+    ctx.close()
