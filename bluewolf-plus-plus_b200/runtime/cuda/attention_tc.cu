@@ -30,6 +30,10 @@ namespace {
 
 using namespace bwpp_attn;
 constexpr int THREADS = 320;
+// Of every 8 score pairs, this many take exp2 on the FMA pipe (exp2_fma2),
+// the rest on MUFU: one ex2 per score would keep MUFU as busy as the tensor
+// core, so part of the load moves to the otherwise idle FMA pipe.
+constexpr int kEmuPairsPer8 = 3;
 
 template <int D>
 struct Cfg {
@@ -322,10 +326,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float y0, y1;
+          float y0, y1, p0, p1;
           f2unpack(f2fma(f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nb2),
                    y0, y1);
-          const float p0 = fast_exp2(y0), p1 = fast_exp2(y1);
+          if ((i & 7) >= 8 - kEmuPairsPer8) {
+            exp2_fma2(y0, y1, p0, p1);  // FMA pipe
+          } else {
+            p0 = fast_exp2(y0);  // MUFU
+            p1 = fast_exp2(y1);
+          }
           pk[i] = pack_bf16(p0, p1);
           acc2 = f2add(acc2, f2pack(p0, p1));
         }

@@ -5,7 +5,8 @@
 //    BWPP_WAIT_LIMIT_NS of %globaltimer, records BWPP_CUDA_ERR_TIMEOUT in the
 //    ctx's status word and lets the kernel unwind; nothing traps.
 //  * Thin inline-PTX wrappers for mbarrier, TMA (cp.async.bulk.tensor, no
-//    multicast anywhere) and tcgen05 (alloc / mma / commit / ld).
+//    cluster-wide copies: every load lands in the issuing CTA) and tcgen05
+//    (alloc / mma / commit / ld).
 #pragma once
 
 #include <cuda.h>
@@ -142,7 +143,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
   }
 }
 
-// ---- TMA (no multicast) ---------------------------------------------------
+// ---- TMA: each copy targets the issuing CTA only --------------------------
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,
                                             uint64_t *bar, int32_t x,
