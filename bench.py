@@ -517,6 +517,8 @@ def main():
     ap.add_argument("--workload", default="gemm")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="row-workload rows (default 65536; smaller only for profiler captures)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
@@ -541,6 +543,8 @@ def main():
 
     ctx = bwpp.Ctx(local)
     wl = make_workload(args.workload, rank, world, torch, bwpp, ctx)
+    if args.rows and isinstance(wl, RowWorkload):
+        wl.R = args.rows
     wl.setup()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     stream = torch.cuda.current_stream()

@@ -81,6 +81,7 @@ _SIGS = {
     "bwpp_cuda_ctx_set_workspace": (_i32, [_vp, _vp, _sz]),
     "bwpp_cuda_norm_bwd_workspace_size": (_sz, [_vp, _u32, _u32]),
     "bwpp_cuda_sync": (_i32, [_vp]),
+    "bwpp_cuda_copy": (_i32, [_vp, _vp, _vp, _sz]),
     "bwpp_cuda_status_string": (_cp, [_i32]),
     "bwpp_cuda_ctx_last_error": (_cp, [_vp]),
     "bwpp_cuda_device_count": (_i32, []),

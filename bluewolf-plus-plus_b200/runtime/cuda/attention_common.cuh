@@ -95,13 +95,15 @@ __device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
 // round(x) in the low mantissa bits), f in [-0.5, 0.5]; 2^f from a cubic
 // fitted for relative error on that interval by weighted least squares on
 // Chebyshev nodes (max relative error 1.4e-4, far below the 2^-9 of the bf16
-// P it feeds); 2^n is added to the exponent bits.  x is clamped at -127, so
-// -inf (a masked score) gives a value below 2^-126, i.e. 0 for all purposes.
+// P it feeds); 2^n is added to the exponent bits.  x is clamped at -126 (the
+// cubic may return just under 1, whose exponent field 126 must stay >= 126
+// after adding n), so -inf (a masked score) gives about 2^-126, i.e. 0 for
+// all purposes.
 __device__ __forceinline__ void exp2_fma2(float x0, float x1, float &y0, float &y1) {
   const uint64_t magic = f2pack(12582912.0f, 12582912.0f);
   const uint64_t nmagic = f2pack(-12582912.0f, -12582912.0f);
   const uint64_t neg1 = f2pack(-1.0f, -1.0f);
-  const uint64_t x = f2pack(fmaxf(x0, -127.0f), fmaxf(x1, -127.0f));
+  const uint64_t x = f2pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
   const uint64_t j = f2add(x, magic);
   const uint64_t n = f2add(j, nmagic);
   const uint64_t f = f2fma(n, neg1, x);  // x - n

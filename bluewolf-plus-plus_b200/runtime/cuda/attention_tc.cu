@@ -6,8 +6,10 @@
 // B that ping-pong: while the softmax warps of one tile turn its S into P, the
 // tensor core works on the other tile.  Per 128-key block j:
 //   S_X = Q_X K_j^T          tcgen05 M=128 N=128 K=16 (Q, K K-major, bf16)
-//   P_X = exp2(S_X*c - m)    softmax warps, one thread per row, P -> smem bf16
-//   O_X += P_X V_j           tcgen05 M=128 N=D K=16 (P K-major, V MN-major)
+//   P_X = exp2(S_X*c - m)    softmax warps, one thread per row; P as bf16
+//                            pairs written back into S_X's TMEM columns
+//   O_X += P_X V_j           tcgen05 M=128 N=D K=16, A = P from TMEM,
+//                            B = V MN-major from smem
 // S_A, S_B, O_A, O_B live in TMEM (4 x 128 columns for D = 128).  The running
 // max only moves when it grows by more than 2^8 (log2 domain), so O is
 // rescaled (tcgen05.ld / st) rarely; P <= 256 stays exact enough in bf16.
@@ -15,8 +17,8 @@
 // max to halve its instruction count; CTAs are ordered head-major so one
 // head's K / V is read from DRAM once and shared through L2.
 //
-// Warp roles (320 threads): warp 0 TMA producer (Q once; K double-buffered,
-// V single-buffered, 3-D tensor maps so ragged S zero-fills per head),
+// Warp roles (320 threads): warp 0 TMA producer (Q once; K and V
+// double-buffered, 3-D tensor maps so ragged S zero-fills per head),
 // warp 1 TMEM allocator + single-thread MMA issuer, warps 2-5 softmax of
 // tile A, warps 6-9 softmax of tile B (warp w reads TMEM lanes 32*(w%4)..).
 // MMA issue order per block: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1), so one
@@ -33,7 +35,7 @@ constexpr int THREADS = 320;
 // Of every 8 score pairs, this many take exp2 on the FMA pipe (exp2_fma2),
 // the rest on MUFU: one ex2 per score would keep MUFU as busy as the tensor
 // core, so part of the load moves to the otherwise idle FMA pipe.
-constexpr int kEmuPairsPer8 = 3;
+constexpr int kEmuPairsPer8 = 0;
 
 template <int D>
 struct Cfg {
@@ -41,9 +43,8 @@ struct Cfg {
   static constexpr int TILE = BOXES * BOX;  // Q / K / V tile bytes
   static constexpr int OFF_Q = 0;           // 2 tiles
   static constexpr int OFF_K = 2 * TILE;    // 2 stages
-  static constexpr int OFF_V = 4 * TILE;    // 1 stage
-  static constexpr int OFF_P = 5 * TILE;    // 2 tiles
-  static constexpr int OFF_BAR = OFF_P + 2 * P_TILE;
+  static constexpr int OFF_V = 4 * TILE;    // 2 stages
+  static constexpr int OFF_BAR = 6 * TILE;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
   static constexpr uint32_t TMEM_S = 0;        // S_A at 0, S_B at 128
   static constexpr uint32_t TMEM_O = 2 * BN;   // O_A at 256, O_B at 256 + D
@@ -56,7 +57,7 @@ struct Cfg {
 struct Bars {
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2];
-  uint64_t v_full, v_empty;
+  uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
   uint64_t drain;
   uint32_t tmem;
@@ -100,8 +101,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&bar->p_full[s], 4);
       mbar_init(&bar->pv_done[s], 1);
     }
-    mbar_init(&bar->v_full, 1);
-    mbar_init(&bar->v_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->v_full[s], 1);
+      mbar_init(&bar->v_empty[s], 1);
+    }
     mbar_init(&bar->drain, 1);
     bar->abort_flag = 0;
     fence_mbar_init();
@@ -136,9 +139,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = n > 0 ? load_k(0) : true;
       for (int j = 0; j < n && ok && !*abort_flag; ++j) {
         if (j + 1 < n && !load_k(j + 1)) { ok = false; break; }
-        if (!mbar_wait(&bar->v_empty, (j & 1) ^ 1, status)) { ok = false; break; }
-        mbar_arrive_expect_tx(&bar->v_full, C::TILE);
-        load_rows<C::BOXES>(smem + C::OFF_V, &tmV, &bar->v_full, io, bh, Skv, j * BN);
+        const int vs = j & 1;
+        if (!mbar_wait(&bar->v_empty[vs], ((j >> 1) & 1) ^ 1, status)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bar->v_full[vs], C::TILE);
+        load_rows<C::BOXES>(smem + C::OFF_V + vs * C::TILE, &tmV, &bar->v_full[vs], io, bh, Skv,
+                            j * BN);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -149,7 +154,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
       const uint32_t k_addr = smem_u32(smem + C::OFF_K);
       const uint32_t v_addr = smem_u32(smem + C::OFF_V);
-      const uint32_t p_addr = smem_u32(smem + C::OFF_P);
       // S_X = Q_X K_j^T into TMEM columns X * 128
       auto issue_s = [&](int X, int j) {
         const uint32_t qa = q_addr + X * C::TILE, ka = k_addr + (j & 1) * C::TILE;
@@ -163,17 +167,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_commit(&bar->s_full[X]);
       };
-      // O_X += P_X V_j
+      // O_X += P_X V_j with P_X read from TMEM (bf16 pairs in the first 64
+      // columns of S_X: 16 keys = 8 columns per MMA) and V_j from smem
       auto issue_pv = [&](int X, int j) {
-        const uint32_t pa = p_addr + X * P_TILE;
+        const uint32_t va = v_addr + (j & 1) * C::TILE;
+        const uint32_t pt = tmem + C::TMEM_S + X * BN;
 #pragma unroll
-        for (int ks = 0; ks < BN / 16; ++ks) {
-          const uint32_t aoff = (ks >> 2) * BOX + (ks & 3) * 32;
-          tc_mma_f16_ss(tmem + C::TMEM_O + X * D,
-                        make_smem_desc(pa + aoff, 16, 1024, BWPP_SWIZZLE_128B),
-                        make_smem_desc(v_addr + ks * 2048, BOX, 1024, BWPP_SWIZZLE_128B),
+        for (int ks = 0; ks < BN / 16; ++ks)
+          tc_mma_f16_ts(tmem + C::TMEM_O + X * D, pt + ks * 8,
+                        make_smem_desc(va + ks * 2048, BOX, 1024, BWPP_SWIZZLE_128B),
                         C::IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
-        }
         tc_commit(&bar->pv_done[X]);
       };
       // block 0: S_A(0), S_B(0)
@@ -191,12 +194,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int X = 0; X < 2 && ok; ++X) {
           if (j < nblk[X]) {
             ok = mbar_wait(&bar->p_full[X], j & 1, status);
-            if (ok && !v_ready) v_ready = ok = mbar_wait(&bar->v_full, j & 1, status);
+            if (ok && !v_ready)
+              v_ready = ok = mbar_wait(&bar->v_full[j & 1], (j >> 1) & 1, status);
             if (!ok) break;
             tc_fence_after();
             issue_pv(X, j);
           }
-          if (X == 1) tc_commit(&bar->v_empty);  // V_j free after PV_B(j)
+          if (X == 1) tc_commit(&bar->v_empty[j & 1]);  // V_j free after PV_B(j)
           if (j + 1 < nblk[X]) {
             if (!k_ready)
               k_ready = ok = mbar_wait(&bar->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, status);
@@ -221,7 +225,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_col = tmem + lane_base + C::TMEM_S + X * BN;
     const uint32_t o_col = tmem + lane_base + C::TMEM_O + X * D;
-    uint8_t *p_tile = smem + C::OFF_P + X * P_TILE;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     const int nb = nblk[X];
@@ -276,8 +279,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float alpha = move ? fast_exp2((m_run - m_new) * scale_log2) : 1.0f;
       const float mb = m_use * scale_log2;
       if (j > 0) {
-        // PV_X(j-1) is done (its completion precedes S_X(j)'s, so this wait
-        // is immediate): O_X is stable and P_X's smem may be overwritten.
+        // PV_X(j-1), which read P_X(j-1) from these TMEM columns, is done (its
+        // completion precedes S_X(j)'s, so this wait is immediate); O_X is
+        // stable for the rescale
         if (!mbar_wait(&bar->pv_done[X], (j - 1) & 1, status)) {
           *abort_flag = 1;
           ok = false;
@@ -287,30 +291,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (__any_sync(0xffffffffu, move)) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(o_col + c * 32, r);
-            tc_wait_ld(r);
+            uint32_t ro[32];
+            tmem_ld_32x32b_x32(o_col + c * 32, ro);
+            tc_wait_ld(ro);
             uint32_t w0[16], w1[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              w0[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-              w1[i] = __float_as_uint(__uint_as_float(r[16 + i]) * alpha);
+              w0[i] = __float_as_uint(__uint_as_float(ro[i]) * alpha);
+              w1[i] = __float_as_uint(__uint_as_float(ro[16 + i]) * alpha);
             }
             tmem_st_32x32b_x16(o_col + c * 32, w0);
             tmem_st_32x32b_x16(o_col + c * 32 + 16, w1);
           }
-          tc_wait_st();
         }
       }
-      // pass 2: P = exp2(S*c - m) as bf16, streamed into smem per 32 keys in
-      // the K-major 128-byte-swizzle layout (two 64-key atoms of 16 KB).  The
-      // row sum adds the fp32 values (paired lanes), the PV product sees them
-      // rounded to bf16.
+      // pass 2 (double-buffered loads): P = exp2(S*c - m) as bf16 pairs into
+      // TMEM columns [0, 64) of S_X, i.e. over S columns already read.  The
+      // row sum adds the fp32 values (paired lanes), the PV product sees bf16.
       const uint64_t sc2 = f2pack(scale_log2, scale_log2);
       const uint64_t nb2 = f2pack(-mb, -mb);
       uint64_t acc2 = f2pack(0.0f, 0.0f);
-      // double-buffered: the load of chunk c+1 is in flight while chunk c is
-      // turned into P
       uint32_t rbuf[2][32];
       tmem_ld_32x32b_x32(s_col, rbuf[0]);
       tc_wait_ld(rbuf[0]);
@@ -338,21 +338,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           pk[i] = pack_bf16(p0, p1);
           acc2 = f2add(acc2, f2pack(p0, p1));
         }
-        uint8_t *atom = p_tile + (c >> 1) * BOX + row * 128;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int q = (c & 1) * 4 + q4;  // 16-byte chunk within the 128-byte row
-          *reinterpret_cast<uint4 *>(atom + ((q ^ (row & 7)) << 4)) =
-              make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-        }
+        tmem_st_32x32b_x16(s_col + c * 16, pk);
         if (c + 1 < BN / 32) tc_wait_ld(rbuf[(c + 1) & 1]);
       }
       float psum_lo, psum_hi;
       f2unpack(acc2, psum_lo, psum_hi);
-      const float psum = psum_lo + psum_hi;
-      l_run = l_run * alpha + psum;
+      l_run = l_run * alpha + psum_lo + psum_hi;
       m_run = m_use;
-      fence_proxy_async_smem();
+      tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {

@@ -205,6 +205,17 @@ int bwpp_cuda_sync(BwppCudaCtx *ctx) {
   return BWPP_CUDA_OK;
 }
 
+int bwpp_cuda_copy(BwppCudaCtx *ctx, void *dst, const void *src, size_t bytes) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (bytes == 0) return BWPP_CUDA_OK;
+  if (!dst || !src) return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "copy: NULL");
+  rc = bwpp_check_cuda(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, ctx->stream),
+                       "copy");
+  if (rc) return rc;
+  return bwpp_check_cuda(ctx, cudaStreamSynchronize(ctx->stream), "copy sync");
+}
+
 const char *bwpp_cuda_ctx_last_error(const BwppCudaCtx *ctx) {
   return ctx ? ctx->last_error : "no context";
 }

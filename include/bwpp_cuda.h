@@ -110,6 +110,9 @@ int bwpp_cuda_ctx_set_stream(BwppCudaCtx *ctx, void *stream);
  * scratch. */
 int bwpp_cuda_ctx_set_workspace(BwppCudaCtx *ctx, void *device_ptr,
                                 size_t bytes);
+/* Copies `bytes` between any two host / device buffers (e.g. filling arena
+ * buffers from a plain C caller), ordered on the ctx stream; synchronous. */
+int bwpp_cuda_copy(BwppCudaCtx *ctx, void *dst, const void *src, size_t bytes);
 /* Scratch bytes the norm backward passes need for `rows` x `cols`. */
 size_t bwpp_cuda_norm_bwd_workspace_size(BwppCudaCtx *ctx, uint32_t rows,
                                          uint32_t cols);

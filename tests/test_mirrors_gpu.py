@@ -183,3 +183,20 @@ def test_device_timeout_status_is_reported(ctx):
     ctx.rmsnorm_fwd(dev(x), yd, None, None, 2, 8, 8, 0.0)
     ctx.sync()
     assert np.allclose(host(yd), 1.0)
+
+
+@pytest.mark.parametrize("mode", [["--cuda"], []])
+def test_c_bench_twin_schema(tmp_path, mode):
+    """bwpp_bench_cuda keeps the reference bench's CLI and JSON keys
+    (bench/bench_cpu.c:45-63,142-158), so bench/bench_regress.py can read it."""
+    import json
+    import subprocess
+    exe = bwpp.PKG_ROOT + "/bench/bwpp_bench_cuda"
+    out = tmp_path / "b.json"
+    r = subprocess.run([exe, "--iters", "3", "--m", "128", "--n", "256", "--k", "64", "--rows", "64",
+                        "--cols", "512", "--json", str(out)] + mode, capture_output=True, text=True,
+                       timeout=120)
+    assert r.returncode == 0, r.stderr
+    d = json.loads(out.read_text())
+    assert set(d["matmul"]) == {"M", "N", "K", "iters", "time_s", "gflops"}
+    assert d["matmul"]["gflops"] > 0 and d["softmax"]["time_s"] > 0 and d["rmsnorm"]["rows"] == 64
