@@ -6,7 +6,7 @@
 //    ctx's status word and lets the kernel unwind; nothing traps.
 //  * Thin inline-PTX wrappers for mbarrier, TMA (cp.async.bulk.tensor, no
 //    cluster-wide copies: every load lands in the issuing CTA) and tcgen05
-//    (alloc / mma / commit / ld).
+//    (alloc / mma / commit / ld), in one-CTA and CTA-pair forms.
 #pragma once
 
 #include <cuda.h>
@@ -341,6 +341,104 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16_f32(uint32_t M,
          | ((M >> 4) << 24);      // M / 16
 }
 
+// ---- CTA pairs (cluster of 2, tcgen05 cta_group::2) -------------------------
+// A kernel that uses these must use cta_group::2 for every tcgen05 alloc /
+// dealloc / mma / commit.  Rank 0 of the pair issues the MMAs; each CTA
+// holds half of A (M/2 rows), half of B (N/2 columns) and its M/2 x N slice
+// of the accumulator.  Every copy still lands in the issuing CTA's shared
+// memory; only the mbarrier that counts its bytes may be the peer's.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the object at `p` in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// All threads of both CTAs; orders prior shared-memory work cluster-wide.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (may be the peer's).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
+// 2-D tile load into this CTA's shared memory whose completed bytes are
+// counted on `cluster_bar`, an mbarrier of either CTA of the pair.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map,
+                                                 uint32_t cluster_bar, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::"
+      "bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(cluster_bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// D (both CTAs' TMEM) (+)= A (both CTAs' smem) * B (both CTAs' smem); the
+// descriptors hold this CTA's addresses, the peer's halves sit at the same
+// offsets in its shared memory.
+__device__ __forceinline__ void tc_mma_f16_ss_pair(uint32_t d_tmem, uint64_t adesc,
+                                                   uint64_t bdesc, uint32_t idesc,
+                                                   uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the mbarrier at shared::cluster address `cluster_bar` once the
+// pair MMAs issued so far by this thread are done.
+__device__ __forceinline__ void tc_commit_pair(uint32_t cluster_bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          cluster_bar)
+      : "memory");
+}
+
+// x * sigmoid(x).  __fdividef (2 ulp, no special-case branch) instead of the
+// IEEE divide: the divide's slow-path branch serialises the 32 independent
+// columns an epilogue thread holds.  Limits are kept: for x -> -inf the
+// denominator overflows to inf (or exceeds 2^126) and the result is -0 / 0.
 __device__ __forceinline__ float bwpp_silu_f(float x) {
-  return x / (1.0f + __expf(-x));
+  return __fdividef(x, 1.0f + __expf(-x));
 }

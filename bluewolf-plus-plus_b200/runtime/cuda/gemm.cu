@@ -9,14 +9,22 @@
 // (b[n*ldb+k], i.e. a transposed weight).  The MN-major forms let the
 // autodiff products (dX = dY W^T, dW = X^T dY) run without transposes.
 //
-// Persistent, warp-specialised kernel, one CTA per SM (192 threads):
-//   warp 0       TMA producer: A box 128(M) x 64(K), B as four 64(N) x 64(K)
-//                boxes, 128-byte swizzle, 4-stage smem ring (48 KB/stage)
-//   warp 1       TMEM allocator + single-thread tcgen05.mma issuer
-//                (M=128, N=256, K=16, A K-major, B MN-major), commits free the
-//                smem stage / publish the accumulator
+// Persistent, warp-specialised kernel (192 threads per CTA), in two forms:
+//   CTA pair (cluster of 2, tcgen05 cta_group::2), used when M > 128: the
+//     pair computes a 256 x 256 tile; each CTA loads 128 rows of A and 128
+//     columns of B per K step (32 KB, 6-stage ring) into its own shared
+//     memory, so operand traffic per SM is 2/3 of the single-CTA form.  The
+//     TMA bytes of both CTAs count on rank 0's "full" barrier; rank 0's single
+//     MMA thread issues M=256 N=256 K=16 MMAs and commits to the barriers of
+//     both CTAs; each CTA's epilogue drains its own 128 TMEM lanes and
+//     arrives on rank 0's "accumulator empty" barrier.
+//   single CTA: 128 x 256 tiles, 48 KB per K step, 4-stage ring.
+// Roles:
+//   warp 0       TMA producer, 128-byte swizzle
+//   warp 1       TMEM allocator + single-thread tcgen05.mma issuer; commits
+//                free the smem stage / publish the accumulator
 //   warps 2..5   epilogue: tcgen05.ld 32 lanes x 32 columns, +bias, SiLU,
-//                swizzled smem staging, TMA store (double-buffered per warp)
+//                +residual, swizzled smem staging, TMA store (double-buffered)
 // Two 256-column fp32 accumulators in TMEM (512 columns): the epilogue of
 // tile i overlaps the main loop of tile i+1.  Tiles are rasterised in groups
 // of 8 M-blocks so CTAs running together share B panels in L2.
@@ -26,26 +34,40 @@
 //
 // Shapes the TMA path cannot describe (row pitch not a multiple of 16 bytes,
 // unaligned pointers, K == 0) run on a CUDA-core kernel instead.
+#include <stdlib.h>
+
 #include "bwpp_cuda_internal.cuh"
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int A_STAGE = BM * BK * 2;   // 16 KB
-constexpr int B_SUB = 64 * BK * 2;     // 8 KB: 64 N-columns x 64 K-rows
-constexpr int B_STAGE = BN * BK * 2;   // 32 KB
-constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int BM = 128, BN = 256, BK = 64;  // BM: rows per CTA; BN: accumulator width
+constexpr int A_STAGE = BM * BK * 2;        // 16 KB
+constexpr int B_SUB = 64 * BK * 2;          // 8 KB: 64 MN-columns x 64 K-rows
 constexpr int EPI_WARPS = 4;
-constexpr int EPI_COLS = 32;                   // columns per TMEM load / store
-constexpr int EPI_BUF = 32 * EPI_COLS * 4;     // 4 KB: 32 rows x 128 B
-constexpr int OFF_B = STAGES * A_STAGE;
-constexpr int OFF_C = OFF_B + STAGES * B_STAGE;
-constexpr int OFF_BAR = OFF_C + EPI_WARPS * 2 * EPI_BUF;
-constexpr int SMEM_USED = OFF_BAR + 128;
-constexpr int SMEM_ALLOC = SMEM_USED + 1024;  // slack for 1024-B alignment
+constexpr int EPI_COLS = 32;                // columns per TMEM load / store
+constexpr int EPI_BUF = 32 * EPI_COLS * 4;  // 4 KB: 32 rows x 128 B
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr uint32_t GROUP_M = 8;
+
+// PAIR: a cluster of two CTAs computes a 256 x 256 tile with cta_group::2
+// MMAs; each CTA loads 128 rows of A and 128 columns of B per K step (32 KB,
+// six stages).  Single CTA: 128 x 256 tiles, 128 rows of A and 256 columns of
+// B per K step (48 KB, four stages).
+template <bool PAIR>
+struct GemmCfg {
+  static constexpr int BN_LOAD = PAIR ? 128 : 256;  // B columns this CTA loads
+  static constexpr int STAGES = PAIR ? 6 : 4;
+  static constexpr int B_STAGE = BN_LOAD * BK * 2;
+  static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+  static constexpr int OFF_B = STAGES * A_STAGE;
+  static constexpr int OFF_C = OFF_B + STAGES * B_STAGE;
+  static constexpr int OFF_BAR = OFF_C + EPI_WARPS * 2 * EPI_BUF;
+  static constexpr int SMEM_ALLOC = OFF_BAR + 256 + 1024;  // + slack for 1024-B alignment
+  static constexpr uint32_t TILE_M = PAIR ? 2 * BM : BM;
+  static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in limit");
+  static_assert((2 * STAGES + 5) * 8 + 8 <= 256, "barrier block");
+};
 
 struct GemmEpi {
   const float *bias;      // [N] or nullptr
@@ -54,8 +76,6 @@ struct GemmEpi {
   int silu;
   int out_bf16;
 };
-
-static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in limit");
 
 __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m,
                                             uint32_t tiles_n, uint32_t &mb,
@@ -69,17 +89,20 @@ __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m,
   nb = r / gm;
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmEpi epi,
                    uint32_t M, uint32_t N, uint32_t K, int *status) {
-  constexpr uint32_t IDESC = make_idesc_bf16_f32(BM, BN, A_MN ? 1u : 0u, B_MN ? 1u : 0u);
+  using Cfg = GemmCfg<PAIR>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC =
+      make_idesc_bf16_f32(Cfg::TILE_M, BN, A_MN ? 1u : 0u, B_MN ? 1u : 0u);
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + Cfg::OFF_BAR);
   uint64_t *empty = full + STAGES;
   uint64_t *tfull = empty + STAGES;
   uint64_t *tempty = tfull + 2;
@@ -88,7 +111,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
+  // rank 0 of a pair issues the MMAs and owns the barriers both CTAs feed
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const uint32_t first_tile = PAIR ? cluster_id_x() : blockIdx.x;
+  const uint32_t tile_step = PAIR ? cluster_count_x() : gridDim.x;
+  const uint32_t tiles_m = (M + Cfg::TILE_M - 1) / Cfg::TILE_M, tiles_n = (N + BN - 1) / BN;
   const uint32_t num_tiles = tiles_m * tiles_n;
   const uint32_t num_kb = (K + BK - 1) / BK;
 
@@ -99,7 +126,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], EPI_WARPS);
+      mbar_init(&tempty[a], PAIR ? 2 * EPI_WARPS : EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -109,11 +136,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tmap(&tmC);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_holder, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync_all(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
@@ -121,35 +153,41 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
-      for (uint32_t t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      for (uint32_t t = first_tile; t < num_tiles && !*abort_flag; t += tile_step) {
         uint32_t mb, nb;
         tile_coords(t, tiles_m, tiles_n, mb, nb);
+        const int32_t row0 = (int32_t)(mb * Cfg::TILE_M + rank * BM);
+        const int32_t col0 = (int32_t)(nb * BN + rank * Cfg::BN_LOAD);
         for (uint32_t kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, status)) {
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          // the pair's bytes all count on rank 0's barrier
+          if (rank == 0)
+            mbar_arrive_expect_tx(&full[stage], (PAIR ? 2 : 1) * Cfg::STAGE_BYTES);
+          uint32_t fbar = 0;
+          if constexpr (PAIR) fbar = cluster_addr(&full[stage], 0);
+          auto load = [&](void *dst, const CUtensorMap *map, int32_t x, int32_t y) {
+            if constexpr (PAIR) tma_load_2d_pair(dst, map, fbar, x, y);
+            else tma_load_2d(dst, map, &full[stage], x, y);
+          };
           uint8_t *sa = smem + stage * A_STAGE;
-          uint8_t *sb = smem + OFF_B + stage * B_STAGE;
+          uint8_t *sb = smem + Cfg::OFF_B + stage * Cfg::B_STAGE;
+          const int32_t k0 = (int32_t)(kb * BK);
           if (!A_MN) {
-            // [128 rows of M] x [64 K]: one 16 KB box
-            tma_load_2d(sa, &tmA, &full[stage], (int32_t)(kb * BK), (int32_t)(mb * BM));
+            load(sa, &tmA, k0, row0);  // [128 rows of M] x [64 K]: one 16 KB box
           } else {
-            // [64 K rows] x [64 M] boxes, two of them for 128 M
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j)
-              tma_load_2d(sa + j * B_SUB, &tmA, &full[stage], (int32_t)(mb * BM + j * 64),
-                          (int32_t)(kb * BK));
+            for (int j = 0; j < BM / 64; ++j)  // [64 K rows] x [64 M] boxes
+              load(sa + j * B_SUB, &tmA, row0 + j * 64, k0);
           }
           if (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sb + j * B_SUB, &tmB, &full[stage],
-                          (int32_t)(nb * BN + j * 64), (int32_t)(kb * BK));
+            for (int j = 0; j < Cfg::BN_LOAD / 64; ++j)
+              load(sb + j * B_SUB, &tmB, col0 + j * 64, k0);
           } else {
-            // [256 rows of N] x [64 K]: one 32 KB box
-            tma_load_2d(sb, &tmB, &full[stage], (int32_t)(kb * BK), (int32_t)(nb * BN));
+            load(sb, &tmB, k0, col0);  // [BN_LOAD rows of N] x [64 K]: one box
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -160,9 +198,18 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
+      // commit: arrive on this CTA's barrier and, for a pair, the peer's copy
+      auto commit = [&](uint64_t *bar) {
+        if constexpr (PAIR) {
+          tc_commit_pair(smem_u32(bar));
+          tc_commit_pair(cluster_addr(bar, 1));
+        } else {
+          tc_commit(bar);
+        }
+      };
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
-      for (uint32_t t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      for (uint32_t t = first_tile; t < num_tiles && !*abort_flag; t += tile_step) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, status)) {
           *abort_flag = 1;
           break;
@@ -178,7 +225,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tc_fence_after();
           const uint32_t a0 = smem_u32(smem + stage * A_STAGE);
-          const uint32_t b0 = smem_u32(smem + OFF_B + stage * B_STAGE);
+          const uint32_t b0 = smem_u32(smem + Cfg::OFF_B + stage * Cfg::B_STAGE);
 #pragma unroll
           for (int ks = 0; ks < BK / 16; ++ks) {
             // K-major, 128-B swizzle: a K step of 16 bf16 is 32 bytes inside
@@ -189,30 +236,31 @@ __global__ void __launch_bounds__(THREADS, 1)
                                      : make_smem_desc(a0 + ks * 32, 16, 1024, BWPP_SWIZZLE_128B);
             const uint64_t bd = B_MN ? make_smem_desc(b0 + ks * 2048, B_SUB, 1024, BWPP_SWIZZLE_128B)
                                      : make_smem_desc(b0 + ks * 32, 16, 1024, BWPP_SWIZZLE_128B);
-            tc_mma_f16_ss(d_tmem, ad, bd, IDESC, (kb | ks) != 0 ? 1u : 0u);
+            if constexpr (PAIR) tc_mma_f16_ss_pair(d_tmem, ad, bd, IDESC, (kb | ks) != 0 ? 1u : 0u);
+            else tc_mma_f16_ss(d_tmem, ad, bd, IDESC, (kb | ks) != 0 ? 1u : 0u);
           }
-          tc_commit(&empty[stage]);
+          commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit(&tfull[acc]);
+        commit(&tfull[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
       // every MMA issued by this thread has finished before TMEM is freed
-      tc_commit(drain);
+      if constexpr (PAIR) tc_commit_pair(smem_u32(drain)); else tc_commit(drain);
       mbar_wait(drain, 0, status);
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int ew = warp - 2;
-    uint8_t *stage_c = smem + OFF_C + ew * 2 * EPI_BUF;
+    uint8_t *stage_c = smem + Cfg::OFF_C + ew * 2 * EPI_BUF;
     uint32_t acc = 0, acc_phase = 0, buf = 0;
-    for (uint32_t t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+    for (uint32_t t = first_tile; t < num_tiles && !*abort_flag; t += tile_step) {
       uint32_t mb, nb;
       tile_coords(t, tiles_m, tiles_n, mb, nb);
       if (!mbar_wait(&tfull[acc], acc_phase, status)) {
@@ -220,7 +268,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t row0 = mb * BM + q * 32;
+      const uint32_t row0 = mb * Cfg::TILE_M + rank * BM + q * 32;
       const uint32_t my_row = row0 + lane;
       // fp32 out: 32-column chunks; bf16 out: 64-column chunks (two TMEM
       // loads).  Either way a chunk is 32 rows x 128 bytes in smem.
@@ -308,18 +356,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if constexpr (PAIR) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
+        else mbar_arrive(&tempty[acc]);
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
     if (lane == 0) tma_store_wait_all<0>();
   }
 
+  // Neither CTA of a pair leaves (or frees TMEM) while the other may still
+  // touch its barriers: every wait above is bounded, so both arrive here.
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync_all(); else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -382,30 +436,89 @@ __global__ void cast_f32_bf16_kernel(const float *__restrict__ src,
   }
 }
 
-bool g_attr_set[4][64] = {};
+bool g_attr_set[8][64] = {};
+int g_pair_clusters[4][64] = {};  // resident CTA pairs per device (0: not queried)
 
 inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <bool A_MN, bool B_MN>
+// CTA pairs are used unless BWPP_GEMM_CTA_PAIR=0 (then every GEMM runs the
+// single-CTA kernel).
+bool pairs_enabled() {
+  static const int on = [] {
+    const char *e = getenv("BWPP_GEMM_CTA_PAIR");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return on != 0;
+}
+
+// Launches the tensor-core kernel.  Returns BWPP_CUDA_ERR_UNSUPPORTED (with
+// nothing launched) when a CTA pair cannot be made resident, so the caller
+// can take the single-CTA kernel.
+template <bool A_MN, bool B_MN, bool PAIR>
 int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
               const CUtensorMap &tcm, const GemmEpi &epi, uint32_t M, uint32_t N,
               uint32_t K) {
+  using Cfg = GemmCfg<PAIR>;
+  auto kern = gemm_tc_kernel<A_MN, B_MN, PAIR>;
   const int v = (A_MN ? 2 : 0) + (B_MN ? 1 : 0);
-  if (ctx->device < 64 && !g_attr_set[v][ctx->device]) {
+  const int dev = ctx->device;
+  if (dev >= 64) return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "gemm: device index >= 64");
+  if (!g_attr_set[v + (PAIR ? 4 : 0)][dev]) {
     int rc = bwpp_check_cuda(ctx,
-                             cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN>,
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  SMEM_ALLOC),
+                             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  Cfg::SMEM_ALLOC),
                              "gemm smem attribute");
     if (rc) return rc;
-    g_attr_set[v][ctx->device] = true;
+    g_attr_set[v + (PAIR ? 4 : 0)][dev] = true;
   }
-  const uint32_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const uint32_t grid = tiles < (uint32_t)ctx->num_sms ? tiles : (uint32_t)ctx->num_sms;
-  gemm_tc_kernel<A_MN, B_MN><<<grid, THREADS, SMEM_ALLOC, ctx->stream>>>(ta, tb, tcm, epi, M, N, K,
-                                                                        ctx->status_word);
-  BWPP_LAUNCH_CHECK(ctx, "gemm tcgen05");
-  return BWPP_CUDA_OK;
+  const uint32_t tiles = ((M + Cfg::TILE_M - 1) / Cfg::TILE_M) * ((N + BN - 1) / BN);
+  if constexpr (!PAIR) {
+    const uint32_t grid = tiles < (uint32_t)ctx->num_sms ? tiles : (uint32_t)ctx->num_sms;
+    kern<<<grid, THREADS, Cfg::SMEM_ALLOC, ctx->stream>>>(ta, tb, tcm, epi, M, N, K,
+                                                          ctx->status_word);
+    BWPP_LAUNCH_CHECK(ctx, "gemm tcgen05");
+    return BWPP_CUDA_OK;
+  } else {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(ctx->num_sms & ~1), 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM_ALLOC;
+    cfg.stream = ctx->stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int &pairs = g_pair_clusters[v][dev];
+    if (pairs == 0) {
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        pairs = -1;
+      } else {
+        pairs = n;
+      }
+    }
+    if (pairs < 0) return BWPP_CUDA_ERR_UNSUPPORTED;
+    const uint32_t clusters = tiles < (uint32_t)pairs ? tiles : (uint32_t)pairs;
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    int *status = ctx->status_word;
+    return bwpp_check_cuda(ctx, cudaLaunchKernelEx(&cfg, kern, ta, tb, tcm, epi, M, N, K, status),
+                           "gemm tcgen05 pair");
+  }
+}
+
+template <bool A_MN, bool B_MN>
+int launch_tc_any(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
+                  const CUtensorMap &tb_pair, const CUtensorMap &tcm, const GemmEpi &epi,
+                  uint32_t M, uint32_t N, uint32_t K, bool pair) {
+  if (pair) {
+    const int rc = launch_tc<A_MN, B_MN, true>(ctx, ta, tb_pair, tcm, epi, M, N, K);
+    if (rc != BWPP_CUDA_ERR_UNSUPPORTED) return rc;
+  }
+  return launch_tc<A_MN, B_MN, false>(ctx, ta, tb, tcm, epi, M, N, K);
 }
 
 }  // namespace
@@ -430,25 +543,34 @@ int bwpp_gemm_launch_ex(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t 
     BWPP_LAUNCH_CHECK(ctx, "gemm simt");
     return BWPP_CUDA_OK;
   }
-  CUtensorMap ta, tb, tcm;
+  // CTA pairs take GEMMs with more than one 128-row block (the second CTA
+  // of a pair would otherwise compute rows past M only).
+  const bool pair = pairs_enabled() && M > (uint32_t)BM;
+  CUtensorMap ta, tb, tb_pair, tcm;
   const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
   int rc = a_mn ? bwpp_make_tmap_2d(ctx, &ta, a, BF, M, K, (uint64_t)lda * 2, 64, BK, SW)
                 : bwpp_make_tmap_2d(ctx, &ta, a, BF, K, M, (uint64_t)lda * 2, BK, BM, SW);
+  // B boxes: MN-major 64 columns x 64 K rows; K-major 64 K x (256 or, for a
+  // pair, 128) rows of N
   if (!rc)
     rc = b_mn ? bwpp_make_tmap_2d(ctx, &tb, b, BF, N, K, (uint64_t)ldb * 2, 64, BK, SW)
               : bwpp_make_tmap_2d(ctx, &tb, b, BF, K, N, (uint64_t)ldb * 2, BK, BN, SW);
+  if (!rc)
+    rc = (b_mn || !pair) ? (tb_pair = tb, 0)
+                         : bwpp_make_tmap_2d(ctx, &tb_pair, b, BF, K, N, (uint64_t)ldb * 2, BK,
+                                             GemmCfg<true>::BN_LOAD, SW);
   if (!rc)
     rc = out_bf16 ? bwpp_make_tmap_2d(ctx, &tcm, c, BF, N, M, (uint64_t)ldc * 2, 64, 32, SW)
                   : bwpp_make_tmap_2d(ctx, &tcm, c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M,
                                       (uint64_t)ldc * 4, EPI_COLS, 32, SW);
   if (rc) return rc;
   if (a_mn) {
-    return b_mn ? launch_tc<true, true>(ctx, ta, tb, tcm, epi, M, N, K)
-                : launch_tc<true, false>(ctx, ta, tb, tcm, epi, M, N, K);
+    return b_mn ? launch_tc_any<true, true>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair)
+                : launch_tc_any<true, false>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair);
   }
-  return b_mn ? launch_tc<false, true>(ctx, ta, tb, tcm, epi, M, N, K)
-              : launch_tc<false, false>(ctx, ta, tb, tcm, epi, M, N, K);
+  return b_mn ? launch_tc_any<false, true>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair)
+              : launch_tc_any<false, false>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair);
 }
 
 // The reference-shaped matmul: A K-major, B MN-major, fp32 out.

@@ -17,7 +17,7 @@ __device__ __forceinline__ uint32_t f2bf2(float lo, float hi) {
   return r;
 }
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 template <int NV>
 __device__ __forceinline__ void block_sum_n(float (&v)[NV], float *red) {

@@ -197,3 +197,42 @@ def test_gemm_ex_cuda_core_layouts(ctx, a_mn, b_mn):
     ctx.gemm_ex(dev(a16), dev(b16), cd, M, N, K, lda, ldb, N, a_mn=a_mn, b_mn=b_mn)
     ctx.sync()
     assert rel_fro(host(cd), O.matmul(A, B)) <= TIGHT
+
+
+_SINGLE_CTA_SCRIPT = r"""
+import sys
+import numpy as np
+sys.path[:0] = sys.argv[1:]
+import bwpp, oracle as O, torch
+ctx = bwpp.Ctx(0)
+worst = 0.0
+for (M, N, K, a_mn, b_mn) in ((300, 520, 1000, 0, 1), (1000, 1024, 200, 1, 0), (520, 130, 264, 1, 1)):
+    rng = np.random.default_rng(M + N + K)
+    a16 = O.f32_to_bf16(rng.standard_normal((K, M) if a_mn else (M, K)).astype(np.float32))
+    b16 = O.f32_to_bf16(rng.standard_normal((K, N) if b_mn else (N, K)).astype(np.float32))
+    A = O.bf16_to_f32(a16).T if a_mn else O.bf16_to_f32(a16)
+    B = O.bf16_to_f32(b16) if b_mn else O.bf16_to_f32(b16).T
+    c = torch.empty(M, N, device="cuda")
+    ctx.gemm_ex(torch.from_numpy(a16.view(np.int16)).cuda(), torch.from_numpy(b16.view(np.int16)).cuda(), c, M, N, K,
+                M if a_mn else K, N if b_mn else K, N, a_mn=a_mn, b_mn=b_mn)
+    ctx.sync()
+    ref = O.matmul(np.ascontiguousarray(A), np.ascontiguousarray(B))
+    worst = max(worst, float(np.linalg.norm(c.cpu().numpy() - ref) / np.linalg.norm(ref)))
+print("WORST", worst)
+"""
+
+
+def test_single_cta_kernel_with_pairs_disabled(ctx):
+    """BWPP_GEMM_CTA_PAIR=0 routes every GEMM to the single-CTA kernel (the
+    switch is read once per process, so this runs in a child process)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    paths = [os.path.join(root, "bluewolf-plus-plus_b200"), os.path.join(root, "oracle")]
+    env = dict(os.environ, BWPP_GEMM_CTA_PAIR="0")
+    out = subprocess.run([sys.executable, "-c", _SINGLE_CTA_SCRIPT] + paths, env=env,
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    worst = float(out.stdout.split("WORST")[-1])
+    assert worst <= TIGHT, worst
