@@ -4,7 +4,9 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload gemm|attention|attention_causal|rmsnorm_fwd|
                                 rmsnorm_bwd|layernorm_fwd|layernorm_bwd|
-                                reduce_max_fwd|reduce_max_bwd]
+                                reduce_max_fwd|reduce_max_bwd|softmax_fwd|
+                                softmax_grad|silu_grad|reduce_sum_rows|
+                                reduce_sum_cols|broadcast_rows|tiny_model]
 
 Default workload (the headline): fused matmul + bias +
 SiLU, X[8192x4096] bf16 * W[4096x11008] bf16 + b[11008], fp32 out, rows of X
@@ -340,13 +342,27 @@ class RowWorkload(Workload):
             c.reduce_max_fwd(self.x, self.mx, self.am, m, C_, C_); return 1
         if self.op == "reduce_max_bwd":
             c.reduce_max_bwd(self.am, self.dyr, self.y, m, C_, C_); return 1
+        if self.op == "softmax_fwd":
+            c.softmax_fwd(self.x, self.y, m, C_, C_); return 1
+        if self.op == "softmax_grad":
+            c.softmax_grad(self.x, self.dy, self.y, m, C_, C_); return 1
+        if self.op == "silu_grad":
+            c.silu_grad(self.x, self.dy, self.y, m * C_); return 1
+        if self.op == "reduce_sum_rows":
+            c.reduce_sum(self.x, self.mx, m, C_, C_, 1); return 1
+        if self.op == "reduce_sum_cols":
+            c.reduce_sum(self.x, self.dg, m, C_, C_, 0); return 2
+        if self.op == "broadcast_rows":
+            c.broadcast(self.dyr, self.y, m, C_, C_, 1); return 1
         raise ValueError(self.op)
 
     def bytes_for(self, rows):
         n = rows * self.Cc * 4
         return {"rmsnorm_fwd": 2 * n, "layernorm_fwd": 2 * n, "rmsnorm_bwd": 3 * n,
                 "layernorm_bwd": 3 * n, "reduce_max_fwd": n + 8 * rows,
-                "reduce_max_bwd": n + 8 * rows}[self.op]
+                "reduce_max_bwd": n + 8 * rows, "softmax_fwd": 2 * n, "softmax_grad": 3 * n,
+                "silu_grad": 3 * n, "reduce_sum_rows": n + 4 * rows,
+                "reduce_sum_cols": n + 4 * self.Cc, "broadcast_rows": n + 4 * rows}[self.op]
 
     def work_per_step(self):
         return float(self.bytes_for(self.m))
@@ -355,7 +371,9 @@ class RowWorkload(Workload):
         return float(self.bytes_for(self.R))
 
     def config(self):
-        return {"workload": f"{self.op} (BASELINE configs[2], examples/norms)", "rows": self.R,
+        src = ("BASELINE configs[2], examples/norms" if "norm" in self.op or "max" in self.op
+               else "autodiff graph op at the BASELINE configs[2] shape")
+        return {"workload": f"{self.op} ({src})", "rows": self.R,
                 "cols": self.Cc, "rows_per_gpu": self.m, "eps": 1e-5,
                 "parallelism": f"rows over {self.world} GPU(s), no collective",
                 "l2": "inputs (>= 1 GiB) larger than L2 and 256 MiB flush between steps"}

@@ -99,6 +99,10 @@ _SIGS = {
     "bwpp_cuda_reduce_max_mask_ex": (_i32, [_vp, _vp, _vp, _u32, _u32, _i32]),
     "bwpp_cuda_reduce_max_grad_ex": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _i32]),
     "bwpp_cuda_softmax_fwd_f32": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32]),
+    "bwpp_cuda_silu_grad_f32": (_i32, [_vp, _vp, _vp, _vp, C.c_size_t]),
+    "bwpp_cuda_softmax_grad_f32": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32]),
+    "bwpp_cuda_reduce_sum_f32": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32, C.c_int]),
+    "bwpp_cuda_broadcast_f32": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32, C.c_int]),
     "bwpp_cuda_cast_f32_bf16": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32]),
     "bwpp_cuda_comm_unique_id": (_i32, [_vp]),
     "bwpp_cuda_comm_create": (_i32, [C.POINTER(_vp), _vp, _i32, _i32, _i32]),
@@ -267,6 +271,23 @@ class Ctx:
     def softmax_fwd(self, x, y, rows, cols, ld):
         self.check(self.lib.bwpp_cuda_softmax_fwd_f32(self.handle, _ptr(x), _ptr(y), rows, cols, ld),
                    "softmax_fwd")
+
+    # autodiff-internal ops (fp32)
+    def silu_grad(self, x, dy, dx, n):
+        self.check(self.lib.bwpp_cuda_silu_grad_f32(self.handle, _ptr(x), _ptr(dy), _ptr(dx), n),
+                   "silu_grad")
+
+    def softmax_grad(self, y, dy, dx, rows, cols, ld):
+        self.check(self.lib.bwpp_cuda_softmax_grad_f32(self.handle, _ptr(y), _ptr(dy), _ptr(dx), rows,
+                                                       cols, ld), "softmax_grad")
+
+    def reduce_sum(self, x, out, rows, cols, ld, axis):
+        self.check(self.lib.bwpp_cuda_reduce_sum_f32(self.handle, _ptr(x), _ptr(out), rows, cols, ld,
+                                                     axis), "reduce_sum")
+
+    def broadcast(self, src, dst, rows, cols, ld, axis):
+        self.check(self.lib.bwpp_cuda_broadcast_f32(self.handle, _ptr(src), _ptr(dst), rows, cols, ld,
+                                                    axis), "broadcast")
 
     def cast_f32_bf16(self, src, dst, rows, cols, ld_src):
         self.check(self.lib.bwpp_cuda_cast_f32_bf16(self.handle, _ptr(src), _ptr(dst), rows, cols, ld_src),

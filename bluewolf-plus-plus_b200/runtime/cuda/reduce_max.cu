@@ -8,6 +8,7 @@
 #include <math.h>
 
 #include "bwpp_cuda_internal.cuh"
+#include "rowwise.cuh"
 
 namespace {
 
@@ -210,8 +211,59 @@ __global__ void mask_grad_kernel(const float *__restrict__ mask,
   }
 }
 
-// row softmax, three passes as runtime/cpu/bwpp_cpu_ref.c:37-61 (the row is
-// re-read from L2 for the second and third pass)
+// Row softmax with the row held in registers (one HBM read, one write):
+// max by strict '>' from -INF (NaN never wins, as the serial scan of
+// runtime/cpu/bwpp_cpu_ref.c:43-49), e = expf(x - max) kept in registers,
+// sum, inv = sum > 0 ? 1/sum : 0 (line 56), y = e * inv.
+template <int MAXV, bool V4>
+__global__ void __launch_bounds__(kThreads)
+    softmax_rows_kernel(const float *__restrict__ x, float *__restrict__ y, uint32_t rows,
+                        uint32_t cols, uint32_t ld) {
+  using V = bwpp_row::Vec<V4>;
+  constexpr int W = V::W;
+  __shared__ float sv[32];
+  const uint32_t nv = cols / W;
+  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float *xr = x + (size_t)r * ld;
+    float xv[MAXV][W];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv) V::load_stream(xr, idx, xv[i]);
+#pragma unroll
+      for (int w = 0; w < W; ++w)
+        if (idx < nv && xv[i][w] > m) m = xv[i][w];
+    }
+    m = block_max(m, sv);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv)
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          xv[i][w] = expf(xv[i][w] - m);
+          s += xv[i][w];
+        }
+    }
+    s = block_sum1(s, sv);
+    const float inv = s > 0.0f ? 1.0f / s : 0.0f;
+    float *yr = y + (size_t)r * ld;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv) {
+#pragma unroll
+        for (int w = 0; w < W; ++w) xv[i][w] *= inv;
+        V::store(yr, idx, xv[i]);
+      }
+    }
+  }
+}
+
+// Row softmax for rows wider than the register budget: three passes as
+// runtime/cpu/bwpp_cpu_ref.c:37-61 (the second and third from L2).
 __global__ void __launch_bounds__(kThreads)
     softmax_kernel(const float *__restrict__ x, float *__restrict__ y,
                    uint32_t rows, uint32_t cols, uint32_t ld) {
@@ -311,7 +363,20 @@ int bwpp_cuda_softmax_fwd_f32(BwppCudaCtx *ctx, const float *x, float *y,
   if (rc) return rc;
   if (!x || !y || ld < cols) return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "softmax: bad args");
   if (rows == 0 || cols == 0) return BWPP_CUDA_OK;
-  softmax_kernel<<<grid_for(ctx, rows, 8), kThreads, 0, ctx->stream>>>(x, y, rows, cols, ld);
+  const bool v4 = cols % 4 == 0 && ld % 4 == 0 && aligned16(x) && aligned16(y);
+  const uint32_t per = ((v4 ? cols / 4 : cols) + kThreads - 1) / kThreads;
+  const uint32_t grid = grid_for(ctx, rows, 8);
+  cudaStream_t s = ctx->stream;
+#define BWPP_SMX(MV)                                                                   \
+  (v4 ? softmax_rows_kernel<MV, true><<<grid, kThreads, 0, s>>>(x, y, rows, cols, ld)  \
+      : softmax_rows_kernel<MV, false><<<grid, kThreads, 0, s>>>(x, y, rows, cols, ld))
+  if (per <= 1) BWPP_SMX(1);
+  else if (per <= 2) BWPP_SMX(2);
+  else if (per <= 4) BWPP_SMX(4);
+  else if (per <= 8) BWPP_SMX(8);
+  else if (per <= 16) BWPP_SMX(16);
+  else softmax_kernel<<<grid, kThreads, 0, s>>>(x, y, rows, cols, ld);
+#undef BWPP_SMX
   BWPP_LAUNCH_CHECK(ctx, "softmax");
   return BWPP_CUDA_OK;
 }

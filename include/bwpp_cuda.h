@@ -282,6 +282,31 @@ int bwpp_cuda_reduce_max_grad_ex(BwppCudaCtx *ctx, const float *mask,
 int bwpp_cuda_softmax_fwd_f32(BwppCudaCtx *ctx, const float *x, float *y,
                               uint32_t rows, uint32_t cols, uint32_t ld);
 
+/* Autodiff-internal ops of the gradient graph (compiler/include/graph_ir.h:
+ * 42-55).  The reference emits them from its backward rules but has no
+ * kernel for them; fp32, stream-async. */
+
+/* compiler/graph_ir.c:1709-1720 SILU_GRAD: dx = dy * s * (1 + x * (1 - s)),
+ * s = sigmoid(x), over n dense elements (dx may alias dy). */
+int bwpp_cuda_silu_grad_f32(BwppCudaCtx *ctx, const float *x, const float *dy,
+                            float *dx, size_t n);
+
+/* compiler/graph_ir.c:1722-1733 SOFTMAX_GRAD over the last axis:
+ * dx[r, c] = y[r, c] * (dy[r, c] - sum_j dy[r, j] * y[r, j]) (dx may alias dy). */
+int bwpp_cuda_softmax_grad_f32(BwppCudaCtx *ctx, const float *y, const float *dy,
+                               float *dx, uint32_t rows, uint32_t cols, uint32_t ld);
+
+/* compiler/graph_ir.c:1414-1443 REDUCE_SUM: axis 1 -> out[rows] row sums,
+ * axis 0 -> out[cols] column sums (deterministic; column sums use ctx
+ * scratch).  An empty reduction writes zeros. */
+int bwpp_cuda_reduce_sum_f32(BwppCudaCtx *ctx, const float *x, float *out,
+                             uint32_t rows, uint32_t cols, uint32_t ld, int axis);
+
+/* compiler/graph_ir.c:1457-1470 BROADCAST (the reduce_sum gradient,
+ * 1791-1796): dst[r, c] = src[axis == 1 ? r : c]. */
+int bwpp_cuda_broadcast_f32(BwppCudaCtx *ctx, const float *src, float *dst,
+                            uint32_t rows, uint32_t cols, uint32_t ld, int axis);
+
 /* fp32 -> bf16 bits, round to nearest even (dst dense rows x cols, src with
  * leading dim ld_src). */
 int bwpp_cuda_cast_f32_bf16(BwppCudaCtx *ctx, const float *src, uint16_t *dst,

@@ -359,3 +359,50 @@ void bwpp_oracle_bf16_to_f32(const uint16_t *src, float *dst, size_t n) {
     memcpy(&dst[i], &u, 4);
   }
 }
+
+/* ---- autodiff-internal graph ops ----------------------------------------- */
+
+void bwpp_oracle_silu_grad_f32(const float *x, const float *dy, float *dx, size_t n) {
+  if (!x || !dy || !dx) return;
+  for (size_t i = 0; i < n; ++i) {
+    const double s = 1.0 / (1.0 + exp(-(double)x[i]));
+    dx[i] = (float)((double)dy[i] * s * (1.0 + (double)x[i] * (1.0 - s)));
+  }
+}
+
+void bwpp_oracle_softmax_grad_f32(const float *y, const float *dy, float *dx,
+                                  uint32_t rows, uint32_t cols, uint32_t ld) {
+  if (!y || !dy || !dx) return;
+  for (uint32_t r = 0; r < rows; ++r) {
+    const float *yr = y + (size_t)r * ld, *gr = dy + (size_t)r * ld;
+    double dot = 0.0;
+    for (uint32_t c = 0; c < cols; ++c) dot += (double)yr[c] * (double)gr[c];
+    float *dr = dx + (size_t)r * ld;
+    for (uint32_t c = 0; c < cols; ++c) dr[c] = (float)((double)yr[c] * ((double)gr[c] - dot));
+  }
+}
+
+void bwpp_oracle_reduce_sum_f32(const float *x, float *out, uint32_t rows,
+                                uint32_t cols, uint32_t ld, int axis) {
+  if (!out) return;
+  if (axis == 1) {
+    for (uint32_t r = 0; r < rows; ++r) {
+      double s = 0.0;
+      for (uint32_t c = 0; c < cols; ++c) s += x[(size_t)r * ld + c];
+      out[r] = (float)s;
+    }
+  } else {
+    for (uint32_t c = 0; c < cols; ++c) {
+      double s = 0.0;
+      for (uint32_t r = 0; r < rows; ++r) s += x[(size_t)r * ld + c];
+      out[c] = (float)s;
+    }
+  }
+}
+
+void bwpp_oracle_broadcast_f32(const float *src, float *dst, uint32_t rows,
+                               uint32_t cols, uint32_t ld, int axis) {
+  if (!src || !dst) return;
+  for (uint32_t r = 0; r < rows; ++r)
+    for (uint32_t c = 0; c < cols; ++c) dst[(size_t)r * ld + c] = axis == 1 ? src[r] : src[c];
+}

@@ -120,6 +120,25 @@ void bwpp_oracle_attention_bhsd_fast_f32(const float *q, const float *k,
                                          uint32_t D, float scale, int causal,
                                          uint32_t row_begin, uint32_t row_end);
 
+/* Autodiff-internal graph ops (compiler/include/graph_ir.h:42-55; the
+ * reference has rules, compiler/graph_ir.c:1414-1470,1709-1733,1791-1796,
+ * but no kernels).  float64 arithmetic, rounded to fp32 once. */
+
+/* dx = dy * s * (1 + x * (1 - s)), s = 1 / (1 + exp(-x)) over n elements. */
+void bwpp_oracle_silu_grad_f32(const float *x, const float *dy, float *dx, size_t n);
+
+/* dx[r, c] = y[r, c] * (dy[r, c] - sum_j dy[r, j] * y[r, j]). */
+void bwpp_oracle_softmax_grad_f32(const float *y, const float *dy, float *dx,
+                                  uint32_t rows, uint32_t cols, uint32_t ld);
+
+/* axis 1: out[r] = sum_c x[r, c]; axis 0: out[c] = sum_r x[r, c]. */
+void bwpp_oracle_reduce_sum_f32(const float *x, float *out, uint32_t rows,
+                                uint32_t cols, uint32_t ld, int axis);
+
+/* dst[r, c] = src[axis == 1 ? r : c]. */
+void bwpp_oracle_broadcast_f32(const float *src, float *dst, uint32_t rows,
+                               uint32_t cols, uint32_t ld, int axis);
+
 /* Host float -> bf16 bits, round to nearest even (NaN kept quiet). */
 void bwpp_oracle_f32_to_bf16(const float *src, uint16_t *dst, size_t n);
 /* bf16 bits -> float (exact). */

@@ -52,6 +52,10 @@ _EXT_SIGS = {
     "attention_bhsd_fast_f32": [_f, _f, _f, _f, _u32, _u32, _u32, _u32, _u32, _f32, _i32, _u32, _u32],
     "f32_to_bf16": [_f, _u16, _sz],
     "bf16_to_f32": [_u16, _f, _sz],
+    "silu_grad_f32": [_f, _f, _f, _sz],
+    "softmax_grad_f32": [_f, _f, _f, _u32, _u32, _u32],
+    "reduce_sum_f32": [_f, _f, _u32, _u32, _u32, _i32],
+    "broadcast_f32": [_f, _f, _u32, _u32, _u32, _i32],
 }
 
 
@@ -191,6 +195,34 @@ def attention_bhsd(q, k, v, scale, causal, rows=None, fast=True):
     fn = oracle_lib().attention_bhsd_fast_f32 if fast else oracle_lib().attention_bhsd_f32
     fn(_fp(q), _fp(k), _fp(v), _fp(o), B, H, Sq, Skv, D, scale, int(causal), r0, r1)
     return o
+
+
+def silu_grad(x, dy):
+    x, dy = (np.ascontiguousarray(t, np.float32) for t in (x, dy))
+    dx = np.zeros_like(x)
+    oracle_lib().silu_grad_f32(_fp(x), _fp(dy), _fp(dx), x.size)
+    return dx
+
+
+def softmax_grad(y, dy):
+    rows, cols = y.shape
+    dx = np.zeros_like(y)
+    oracle_lib().softmax_grad_f32(_fp(y), _fp(dy), _fp(dx), rows, cols, cols)
+    return dx
+
+
+def reduce_sum(x, axis):
+    rows, cols = x.shape
+    out = np.zeros(rows if axis == 1 else cols, np.float32)
+    oracle_lib().reduce_sum_f32(_fp(x), _fp(out), rows, cols, cols, int(axis))
+    return out
+
+
+def broadcast(src, rows, cols, axis):
+    dst = np.zeros((rows, cols), np.float32)
+    oracle_lib().broadcast_f32(_fp(np.ascontiguousarray(src, np.float32)), _fp(dst), rows, cols,
+                               cols, int(axis))
+    return dst
 
 
 def f32_to_bf16(x):

@@ -225,3 +225,27 @@ def test_bf16_round_trip():
     assert h[0] == 0x3F80 and h[1] == 0x3F80 and h[2] == 0x3F82
     assert O.bf16_to_f32(h)[3] == -2.5 and np.isinf(O.bf16_to_f32(h)[4])
     assert np.isnan(O.round_bf16(np.array([np.nan], np.float32)))[0]
+
+
+def test_autodiff_ops_vs_torch_autograd():
+    """silu_grad / softmax_grad against float64 torch autograd; reduce_sum and
+    broadcast against numpy (the reference has rules, no kernels, for these)."""
+    import torch
+    rng = np.random.default_rng(17)
+    x = (3 * rng.standard_normal((37, 53))).astype(np.float32)
+    dy = rng.standard_normal((37, 53)).astype(np.float32)
+    xt = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    torch.nn.functional.silu(xt).backward(torch.tensor(dy, dtype=torch.float64))
+    np.testing.assert_allclose(O.silu_grad(x, dy), xt.grad.numpy(), rtol=1e-6, atol=1e-7)
+    xt = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    yt = torch.softmax(xt, -1)
+    yt.backward(torch.tensor(dy, dtype=torch.float64))
+    y = yt.detach().numpy().astype(np.float32)
+    np.testing.assert_allclose(O.softmax_grad(y, dy), xt.grad.numpy(), rtol=1e-5, atol=1e-7)
+    for axis in (0, 1):
+        np.testing.assert_allclose(O.reduce_sum(x, axis), x.astype(np.float64).sum(axis),
+                                   rtol=1e-6, atol=1e-6)
+    col = rng.standard_normal(53).astype(np.float32)
+    row = rng.standard_normal(37).astype(np.float32)
+    assert np.array_equal(O.broadcast(col, 37, 53, 0), np.broadcast_to(col, (37, 53)))
+    assert np.array_equal(O.broadcast(row, 37, 53, 1), np.broadcast_to(row[:, None], (37, 53)))
