@@ -129,6 +129,17 @@ _SIGS = {
     "bwpp_cuda_dispatch_softmax": (_i32, [_vp, _vp, _vp, SoftmaxParams, _cp]),
     "bwpp_cuda_dispatch_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _vp, RmsnormParams, _cp]),
     "bwpp_cuda_dispatch_attention": (_i32, [_vp, _vp, _vp, _vp, _vp, AttentionParams, _cp]),
+    # f16 variants (half ABI)
+    "bwpp_cuda_matmul_f16": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _i32, _i32]),
+    "bwpp_cuda_attention_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _i32]),
+    "bwpp_cuda_softmax_f16": (_i32, [_vp, _vp, _vp, _u32, _u32, _u32]),
+    "bwpp_cuda_rmsnorm_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _f32]),
+    "bwpp_cuda_cast_f16_f32": (_i32, [_vp, _vp, _vp, C.c_size_t]),
+    "bwpp_cuda_cast_f32_f16": (_i32, [_vp, _vp, _vp, C.c_size_t]),
+    "bwpp_cuda_dispatch_matmul_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, MatmulParams, _cp]),
+    "bwpp_cuda_dispatch_softmax_f16": (_i32, [_vp, _vp, _vp, SoftmaxParams, _cp]),
+    "bwpp_cuda_dispatch_rmsnorm_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, RmsnormParams, _cp]),
+    "bwpp_cuda_dispatch_attention_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, AttentionParams, _cp]),
 }
 
 _lib = None
@@ -271,6 +282,25 @@ class Ctx:
     def softmax_fwd(self, x, y, rows, cols, ld):
         self.check(self.lib.bwpp_cuda_softmax_fwd_f32(self.handle, _ptr(x), _ptr(y), rows, cols, ld),
                    "softmax_fwd")
+
+    # f16 variants (half ABI): tensors hold IEEE half (torch.float16)
+    def matmul_f16(self, a, b, c, M, N, K, lda, ldb, ldc, bias=None, silu=0, add=0):
+        self.check(self.lib.bwpp_cuda_matmul_f16(self.handle, _ptr(a), _ptr(b), _ptr(c), M, N, K, lda,
+                                                 ldb, ldc, _ptr(bias), int(silu), int(add)),
+                   "matmul_f16")
+
+    def attention_f16(self, q, k, v, o, B, H, Sq, Skv, D, scale, causal):
+        self.check(self.lib.bwpp_cuda_attention_f16(self.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(o),
+                                                    B, H, Sq, Skv, D, float(scale), int(causal)),
+                   "attention_f16")
+
+    def softmax_f16(self, x, y, rows, cols, ld):
+        self.check(self.lib.bwpp_cuda_softmax_f16(self.handle, _ptr(x), _ptr(y), rows, cols, ld),
+                   "softmax_f16")
+
+    def rmsnorm_f16(self, x, y, gamma, beta, rows, cols, ld, eps):
+        self.check(self.lib.bwpp_cuda_rmsnorm_f16(self.handle, _ptr(x), _ptr(y), _ptr(gamma), _ptr(beta),
+                                                  rows, cols, ld, float(eps)), "rmsnorm_f16")
 
     # autodiff-internal ops (fp32)
     def silu_grad(self, x, dy, dx, n):

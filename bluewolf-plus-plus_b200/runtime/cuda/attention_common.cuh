@@ -17,7 +17,8 @@ constexpr int P_TILE = BM * BN * 2;  // a 128 x 128 bf16 tile (32 KB)
 //   tok = 1: token-major rows t = b*S + s with head h at column h*D
 //            (tensor maps {D, H, B*S}; e.g. straight out of a QKV projection)
 //   out_f32: head-major fp32 [B*H, Sq, D]   (either or both outputs)
-//   out_bf16: token-major bf16, row b*Sq + m, column h*D, pitch ldo
+//   out_bf16: token-major 16-bit (bf16, or f16 in the f16 kernels), row
+//             b*Sq + m, column h*D, pitch ldo (H = 1: head-major, pitch D)
 //   lse: base-2 log-sum-exp of the scaled scores per query, [B*H, Sq]
 struct AttnIO {
   float *out_f32;

@@ -11,10 +11,13 @@ namespace {
 
 constexpr int kMaxPerLane = 8;  // head dims up to 256
 
+// F16 = false: bf16 Q/K/V, fp32 O.  F16 = true (the half ABI): f16 Q/K/V and
+// f16 O (rounded to nearest even once, at the end).
+template <bool F16>
 __global__ void __launch_bounds__(128)
     attention_simt_kernel(const uint16_t *__restrict__ q,
                           const uint16_t *__restrict__ k,
-                          const uint16_t *__restrict__ v, float *__restrict__ o,
+                          const uint16_t *__restrict__ v, void *__restrict__ o,
                           uint32_t BH, uint32_t Sq, uint32_t Skv, uint32_t Kd,
                           uint32_t Dv, uint64_t q_bh, uint64_t k_bh,
                           uint64_t v_bh, uint64_t o_bh, uint32_t ldq,
@@ -31,7 +34,7 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
   for (int i = 0; i < kMaxPerLane; ++i) {
     const uint32_t d = lane + 32 * i;
-    qv[i] = d < Kd ? __uint_as_float((uint32_t)qr[d] << 16) : 0.0f;
+    qv[i] = d < Kd ? load16<F16>(qr[d]) : 0.0f;
     acc[i] = 0.0f;
   }
   uint32_t nk = Skv;
@@ -43,7 +46,7 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int i = 0; i < kMaxPerLane; ++i) {
       const uint32_t d = lane + 32 * i;
-      if (d < Kd) s += qv[i] * __uint_as_float((uint32_t)kr[d] << 16);
+      if (d < Kd) s += qv[i] * load16<F16>(kr[d]);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
@@ -56,29 +59,33 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int i = 0; i < kMaxPerLane; ++i) {
       const uint32_t d = lane + 32 * i;
-      const float vv = d < Dv ? __uint_as_float((uint32_t)vr[d] << 16) : 0.0f;
+      const float vv = d < Dv ? load16<F16>(vr[d]) : 0.0f;
       acc[i] = acc[i] * corr + p * vv;
     }
     mx = mn;
   }
   const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-  float *orow = o + bh * o_bh + (uint64_t)m * ldo;
+  const uint64_t ob = bh * o_bh + (uint64_t)m * ldo;
 #pragma unroll
   for (int i = 0; i < kMaxPerLane; ++i) {
     const uint32_t d = lane + 32 * i;
-    if (d < Dv) orow[d] = acc[i] * inv;
+    if (d < Dv) {
+      if (F16) static_cast<uint16_t *>(o)[ob + d] = (uint16_t)pack2_16<true>(acc[i] * inv, 0.0f);
+      else static_cast<float *>(o)[ob + d] = acc[i] * inv;
+    }
   }
 }
 
 }  // namespace
 
+// o: fp32 (f16 == 0, bf16 inputs) or f16 (f16 == 1, f16 inputs)
 int bwpp_attention_simt_launch(BwppCudaCtx *ctx, const uint16_t *q,
-                               const uint16_t *k, const uint16_t *v, float *o,
+                               const uint16_t *k, const uint16_t *v, void *o,
                                uint32_t BH, uint32_t Sq, uint32_t Skv,
                                uint32_t Kd, uint32_t Dv, uint64_t q_bh,
                                uint64_t k_bh, uint64_t v_bh, uint64_t o_bh,
                                uint32_t ldq, uint32_t ldk, uint32_t ldv,
-                               uint32_t ldo, float scale, int causal) {
+                               uint32_t ldo, float scale, int causal, int f16) {
   if (Kd > 32 * kMaxPerLane || Dv > 32 * kMaxPerLane)
     return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED,
                           "attention: head dims above 256 are not supported");
@@ -87,9 +94,12 @@ int bwpp_attention_simt_launch(BwppCudaCtx *ctx, const uint16_t *q,
   const uint64_t blocks = (rows + 3) / 4;
   if (blocks > 0x7fffffffull)
     return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "attention: too many rows");
-  attention_simt_kernel<<<(unsigned)blocks, 128, 0, ctx->stream>>>(
-      q, k, v, o, BH, Sq, Skv, Kd, Dv, q_bh, k_bh, v_bh, o_bh, ldq, ldk, ldv, ldo,
-      scale, causal);
+  if (f16)
+    attention_simt_kernel<true><<<(unsigned)blocks, 128, 0, ctx->stream>>>(
+        q, k, v, o, BH, Sq, Skv, Kd, Dv, q_bh, k_bh, v_bh, o_bh, ldq, ldk, ldv, ldo, scale, causal);
+  else
+    attention_simt_kernel<false><<<(unsigned)blocks, 128, 0, ctx->stream>>>(
+        q, k, v, o, BH, Sq, Skv, Kd, Dv, q_bh, k_bh, v_bh, o_bh, ldq, ldk, ldv, ldo, scale, causal);
   BWPP_LAUNCH_CHECK(ctx, "attention simt");
   return BWPP_CUDA_OK;
 }

@@ -37,7 +37,7 @@ constexpr int THREADS = 320;
 // core, so part of the load moves to the otherwise idle FMA pipe.
 constexpr int kEmuPairsPer8 = 0;
 
-template <int D>
+template <int D, bool F16 = false>
 struct Cfg {
   static constexpr int BOXES = D / 64;
   static constexpr int TILE = BOXES * BOX;  // Q / K / V tile bytes
@@ -49,8 +49,9 @@ struct Cfg {
   static constexpr uint32_t TMEM_S = 0;        // S_A at 0, S_B at 128
   static constexpr uint32_t TMEM_O = 2 * BN;   // O_A at 256, O_B at 256 + D
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t IDESC_S = make_idesc_bf16_f32(BM, BN, 0, 0);
-  static constexpr uint32_t IDESC_PV = make_idesc_bf16_f32(BM, D, 0, 1);
+  // Q, K, V and P are all bf16, or all f16 (the half ABI)
+  static constexpr uint32_t IDESC_S = make_idesc_f32acc(BM, BN, 0, 0, F16 ? 1u : 0u);
+  static constexpr uint32_t IDESC_PV = make_idesc_f32acc(BM, D, 0, 1, F16 ? 1u : 0u);
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -64,7 +65,7 @@ struct Bars {
   int abort_flag;
 };
 
-template <int D>
+template <int D, bool F16>
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
@@ -72,7 +73,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const AttnIO io, uint32_t BH, uint32_t Sq,
                         uint32_t Skv, float scale_log2, int causal,
                         uint32_t pairs, int *status) {
-  using C = Cfg<D>;
+  using C = Cfg<D, F16>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -335,7 +336,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             p0 = fast_exp2(y0);  // MUFU
             p1 = fast_exp2(y1);
           }
-          pk[i] = pack_bf16(p0, p1);
+          pk[i] = pack2_16<F16>(p0, p1);
           acc2 = f2add(acc2, f2pack(p0, p1));
         }
         tmem_st_32x32b_x16(s_col + c * 16, pk);
@@ -383,10 +384,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 4; ++i)
               *reinterpret_cast<uint4 *>(brow + c * 32 + 8 * i) = make_uint4(
-                  pack_bf16(__uint_as_float(r[8 * i]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
-                  pack_bf16(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
-                  pack_bf16(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
-                  pack_bf16(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
+                  pack2_16<F16>(__uint_as_float(r[8 * i]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
+                  pack2_16<F16>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
+                  pack2_16<F16>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
+                  pack2_16<F16>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
           }
         }
       } else {
@@ -405,7 +406,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // head-major: dims {D, S, BH}; token-major (ld > 0): dims {D, H, B*S}, row pitch ld
 int make_tmap_3d(BwppCudaCtx *ctx, CUtensorMap *map, const void *base, uint32_t D,
-                 uint32_t S, uint32_t BH, uint32_t H, uint32_t ld) {
+                 uint32_t S, uint32_t BH, uint32_t H, uint32_t ld, bool f16 = false) {
   bwpp_encode_tiled_fn enc = bwpp_get_encode_tiled();
   if (!enc) return bwpp_set_error(ctx, BWPP_CUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3], strides[2];
@@ -420,7 +421,8 @@ int make_tmap_3d(BwppCudaCtx *ctx, CUtensorMap *map, const void *base, uint32_t 
     box[0] = 64; box[1] = 1; box[2] = 128;
   }
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
+  CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                   const_cast<void *>(base), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -429,23 +431,23 @@ int make_tmap_3d(BwppCudaCtx *ctx, CUtensorMap *map, const void *base, uint32_t 
   return BWPP_CUDA_OK;
 }
 
-bool g_attr_set[2][64] = {};
+bool g_attr_set[4][64] = {};
 
-template <int D>
+template <int D, bool F16 = false>
 int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *v,
            uint32_t ld_in, uint32_t BH, uint32_t H, uint32_t Sq, uint32_t Skv, float scale,
            int causal, const AttnIO &io) {
   CUtensorMap tq, tk, tv;
-  int rc = make_tmap_3d(ctx, &tq, q, D, Sq, BH, H, ld_in);
-  if (!rc) rc = make_tmap_3d(ctx, &tk, k, D, Skv, BH, H, ld_in);
-  if (!rc) rc = make_tmap_3d(ctx, &tv, v, D, Skv, BH, H, ld_in);
+  int rc = make_tmap_3d(ctx, &tq, q, D, Sq, BH, H, ld_in, F16);
+  if (!rc) rc = make_tmap_3d(ctx, &tk, k, D, Skv, BH, H, ld_in, F16);
+  if (!rc) rc = make_tmap_3d(ctx, &tv, v, D, Skv, BH, H, ld_in, F16);
   if (rc) return rc;
-  const int di = D == 128 ? 1 : 0;
+  const int di = (D == 128 ? 1 : 0) + (F16 ? 2 : 0);
   if (ctx->device < 64 && !g_attr_set[di][ctx->device]) {
     rc = bwpp_check_cuda(ctx,
-                         cudaFuncSetAttribute(attention_tc_kernel<D>,
+                         cudaFuncSetAttribute(attention_tc_kernel<D, F16>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              Cfg<D>::SMEM),
+                                              Cfg<D, F16>::SMEM),
                          "attention smem attribute");
     if (rc) return rc;
     g_attr_set[di][ctx->device] = true;
@@ -454,7 +456,7 @@ int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_
   const uint64_t grid = (uint64_t)pairs * BH;
   if (grid > 0x7fffffffull)
     return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "attention: grid too large");
-  attention_tc_kernel<D><<<(unsigned)grid, THREADS, Cfg<D>::SMEM, ctx->stream>>>(
+  attention_tc_kernel<D, F16><<<(unsigned)grid, THREADS, Cfg<D, F16>::SMEM, ctx->stream>>>(
       tq, tk, tv, io, BH, Sq, Skv, scale * 1.4426950408889634f, causal, pairs,
       ctx->status_word);
   BWPP_LAUNCH_CHECK(ctx, "attention tcgen05");
@@ -477,6 +479,22 @@ int bwpp_attention_tc_launch(BwppCudaCtx *ctx, const uint16_t *q,
   AttnIO io{o, nullptr, 0, nullptr, 0, 1};
   if (D == 128) return launch<128>(ctx, q, k, v, 0, BH, 1, Sq, Skv, scale, causal, io);
   if (D == 64) return launch<64>(ctx, q, k, v, 0, BH, 1, Sq, Skv, scale, causal, io);
+  return BWPP_CUDA_ERR_UNSUPPORTED;
+}
+
+// The half ABI: contiguous [BH, S, D] f16 inputs, D in {64, 128}, f16
+// head-major output [BH, Sq, D].  Returns BWPP_CUDA_ERR_UNSUPPORTED for
+// anything else.
+int bwpp_attention_tc_launch_f16(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                                 const uint16_t *v, uint16_t *o, uint32_t BH, uint32_t Sq,
+                                 uint32_t Skv, uint32_t D, float scale, int causal) {
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al(q) || !al(k) || !al(v) || !al(o) || Skv == 0 || !(scale > 0.0f))
+    return BWPP_CUDA_ERR_UNSUPPORTED;
+  // head-major 16-bit output: row bh * Sq + m (H = 1 in the output map), pitch D
+  AttnIO io{nullptr, o, D, nullptr, 0, 1};
+  if (D == 128) return launch<128, true>(ctx, q, k, v, 0, BH, 1, Sq, Skv, scale, causal, io);
+  if (D == 64) return launch<64, true>(ctx, q, k, v, 0, BH, 1, Sq, Skv, scale, causal, io);
   return BWPP_CUDA_ERR_UNSUPPORTED;
 }
 

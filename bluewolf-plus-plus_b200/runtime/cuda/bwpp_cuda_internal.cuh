@@ -327,18 +327,46 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr,
 
 #define BWPP_SWIZZLE_128B 2u
 
-// Instruction descriptor, kind::f16 with bf16 A/B and fp32 D.
-__host__ __device__ constexpr uint32_t make_idesc_bf16_f32(uint32_t M,
-                                                           uint32_t N,
+// Instruction descriptor, kind::f16 with fp32 D and A/B both bf16 (ab_f16 =
+// 0) or both f16 (ab_f16 = 1): A/B format fields 0 = f16, 1 = bf16.
+__host__ __device__ constexpr uint32_t make_idesc_f32acc(uint32_t M, uint32_t N,
+                                                         uint32_t a_mn_major,
+                                                         uint32_t b_mn_major,
+                                                         uint32_t ab_f16) {
+  return (1u << 4)                          // D format: f32
+         | ((ab_f16 ? 0u : 1u) << 7)        // A format
+         | ((ab_f16 ? 0u : 1u) << 10)       // B format
+         | (a_mn_major << 15)               // A major: 0 = K-major
+         | (b_mn_major << 16)               // B major: 1 = MN-major
+         | ((N >> 3) << 17)                 // N / 8
+         | ((M >> 4) << 24);                // M / 16
+}
+
+__host__ __device__ constexpr uint32_t make_idesc_bf16_f32(uint32_t M, uint32_t N,
                                                            uint32_t a_mn_major,
                                                            uint32_t b_mn_major) {
-  return (1u << 4)                // D format: f32
-         | (1u << 7)              // A format: bf16
-         | (1u << 10)             // B format: bf16
-         | (a_mn_major << 15)     // A major: 0 = K-major
-         | (b_mn_major << 16)     // B major: 1 = MN-major
-         | ((N >> 3) << 17)       // N / 8
-         | ((M >> 4) << 24);      // M / 16
+  return make_idesc_f32acc(M, N, a_mn_major, b_mn_major, 0u);
+}
+
+// Two fp32 values to a packed pair of 16-bit floats (lo in the low half),
+// round to nearest even: bf16 or, with F16, IEEE half.
+template <bool F16>
+__device__ __forceinline__ uint32_t pack2_16(float lo, float hi) {
+  uint32_t r;
+  if (F16) asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  else asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// One 16-bit float (bf16 or, with F16, IEEE half bits) to fp32, exact.
+template <bool F16>
+__device__ __forceinline__ float load16(uint16_t h) {
+  if (F16) {
+    float f;
+    asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+    return f;
+  }
+  return __uint_as_float((uint32_t)h << 16);
 }
 
 // ---- CTA pairs (cluster of 2, tcgen05 cta_group::2) -------------------------

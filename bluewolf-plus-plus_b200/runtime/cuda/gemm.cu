@@ -74,7 +74,8 @@ struct GemmEpi {
   const float *residual;  // fp32 [M, ldr] added last, or nullptr
   uint32_t ldr;
   int silu;
-  int out_bf16;
+  int out_bf16;           // 16-bit output (bf16, or f16 when out_f16)
+  int out_f16;
 };
 
 __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m,
@@ -94,11 +95,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmEpi epi,
-                   uint32_t M, uint32_t N, uint32_t K, int *status) {
+                   uint32_t M, uint32_t N, uint32_t K, uint32_t ab_f16, int *status) {
   using Cfg = GemmCfg<PAIR>;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr uint32_t IDESC =
-      make_idesc_bf16_f32(Cfg::TILE_M, BN, A_MN ? 1u : 0u, B_MN ? 1u : 0u);
+  // A and B both bf16, or both f16 (the half ABI)
+  const uint32_t IDESC =
+      make_idesc_f32acc(Cfg::TILE_M, BN, A_MN ? 1u : 0u, B_MN ? 1u : 0u, ab_f16);
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -328,11 +330,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           if (epi.out_bf16) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              uint32_t w;
-              asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(v[2 * j + 1]), "f"(v[2 * j]));
-              outw[h * 16 + j] = w;
-            }
+            for (int j = 0; j < 16; ++j)
+              outw[h * 16 + j] = epi.out_f16 ? pack2_16<true>(v[2 * j], v[2 * j + 1])
+                                             : pack2_16<false>(v[2 * j], v[2 * j + 1]);
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j) outw[j] = __float_as_uint(v[j]);
@@ -386,11 +386,11 @@ __global__ void gemm_simt_kernel(const uint16_t *__restrict__ a,
                                  const uint16_t *__restrict__ b, void *c,
                                  uint32_t M, uint32_t N, uint32_t K, uint32_t lda,
                                  uint32_t ldb, uint32_t ldc, int a_mn, int b_mn,
-                                 const GemmEpi epi) {
+                                 const GemmEpi epi, int ab_f16) {
   __shared__ float As[ST][ST + 1], Bs[ST][ST + 1];
   const uint32_t row = blockIdx.y * ST + threadIdx.y;
   const uint32_t col = blockIdx.x * ST + threadIdx.x;
-  auto bf = [](uint16_t h) { return __uint_as_float((uint32_t)h << 16); };
+  auto bf = [ab_f16](uint16_t h) { return ab_f16 ? load16<true>(h) : load16<false>(h); };
   float acc = 0.0f;
   for (uint32_t k0 = 0; k0 < K; k0 += ST) {
     const uint32_t ka = k0 + threadIdx.x, kb = k0 + threadIdx.y;
@@ -408,8 +408,7 @@ __global__ void gemm_simt_kernel(const uint16_t *__restrict__ a,
     if (epi.silu) acc = acc / (1.0f + expf(-acc));
     if (epi.residual) acc += epi.residual[(size_t)row * epi.ldr + col];
     if (epi.out_bf16) {
-      uint32_t w;
-      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(0.0f), "f"(acc));
+      const uint32_t w = epi.out_f16 ? pack2_16<true>(acc, 0.0f) : pack2_16<false>(acc, 0.0f);
       reinterpret_cast<uint16_t *>(c)[(size_t)row * ldc + col] = (uint16_t)(w & 0xFFFFu);
     } else {
       reinterpret_cast<float *>(c)[(size_t)row * ldc + col] = acc;
@@ -457,7 +456,7 @@ bool pairs_enabled() {
 template <bool A_MN, bool B_MN, bool PAIR>
 int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
               const CUtensorMap &tcm, const GemmEpi &epi, uint32_t M, uint32_t N,
-              uint32_t K) {
+              uint32_t K, uint32_t ab_f16) {
   using Cfg = GemmCfg<PAIR>;
   auto kern = gemm_tc_kernel<A_MN, B_MN, PAIR>;
   const int v = (A_MN ? 2 : 0) + (B_MN ? 1 : 0);
@@ -474,7 +473,7 @@ int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
   const uint32_t tiles = ((M + Cfg::TILE_M - 1) / Cfg::TILE_M) * ((N + BN - 1) / BN);
   if constexpr (!PAIR) {
     const uint32_t grid = tiles < (uint32_t)ctx->num_sms ? tiles : (uint32_t)ctx->num_sms;
-    kern<<<grid, THREADS, Cfg::SMEM_ALLOC, ctx->stream>>>(ta, tb, tcm, epi, M, N, K,
+    kern<<<grid, THREADS, Cfg::SMEM_ALLOC, ctx->stream>>>(ta, tb, tcm, epi, M, N, K, ab_f16,
                                                           ctx->status_word);
     BWPP_LAUNCH_CHECK(ctx, "gemm tcgen05");
     return BWPP_CUDA_OK;
@@ -505,7 +504,8 @@ int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
     const uint32_t clusters = tiles < (uint32_t)pairs ? tiles : (uint32_t)pairs;
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     int *status = ctx->status_word;
-    return bwpp_check_cuda(ctx, cudaLaunchKernelEx(&cfg, kern, ta, tb, tcm, epi, M, N, K, status),
+    return bwpp_check_cuda(ctx,
+                           cudaLaunchKernelEx(&cfg, kern, ta, tb, tcm, epi, M, N, K, ab_f16, status),
                            "gemm tcgen05 pair");
   }
 }
@@ -513,25 +513,28 @@ int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
 template <bool A_MN, bool B_MN>
 int launch_tc_any(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
                   const CUtensorMap &tb_pair, const CUtensorMap &tcm, const GemmEpi &epi,
-                  uint32_t M, uint32_t N, uint32_t K, bool pair) {
+                  uint32_t M, uint32_t N, uint32_t K, bool pair, uint32_t ab_f16) {
   if (pair) {
-    const int rc = launch_tc<A_MN, B_MN, true>(ctx, ta, tb_pair, tcm, epi, M, N, K);
+    const int rc = launch_tc<A_MN, B_MN, true>(ctx, ta, tb_pair, tcm, epi, M, N, K, ab_f16);
     if (rc != BWPP_CUDA_ERR_UNSUPPORTED) return rc;
   }
-  return launch_tc<A_MN, B_MN, false>(ctx, ta, tb, tcm, epi, M, N, K);
+  return launch_tc<A_MN, B_MN, false>(ctx, ta, tb, tcm, epi, M, N, K, ab_f16);
 }
 
 }  // namespace
 
 // General entry used by the public API and by composite paths (the training
-// step).  a_mn / b_mn select the operand layouts described at the top.
-int bwpp_gemm_launch_ex(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,
+// step).  a_mn / b_mn select the operand layouts described at the top;
+// ab_f16 = 1 takes f16 A and B (else bf16); out_bf16 = 1 writes 16-bit C,
+// f16 when out_f16 = 1 (else bf16); out_bf16 = 0 writes fp32 C.
+int bwpp_gemm_launch_dt(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,
                         const uint16_t *b, int b_mn, uint32_t ldb, void *c,
                         uint32_t ldc, uint32_t M, uint32_t N, uint32_t K,
                         const float *bias, int silu, const float *residual,
-                        uint32_t ldr, int out_bf16, int force_simt) {
+                        uint32_t ldr, int out_bf16, int force_simt, int ab_f16,
+                        int out_f16) {
   if (M == 0 || N == 0) return BWPP_CUDA_OK;
-  GemmEpi epi{bias, residual, ldr, silu ? 1 : 0, out_bf16 ? 1 : 0};
+  GemmEpi epi{bias, residual, ldr, silu ? 1 : 0, out_bf16 ? 1 : 0, out_f16 ? 1 : 0};
   const uint32_t out_es = out_bf16 ? 2 : 4;
   const bool tc_ok = !force_simt && K > 0 && al16(a) && al16(b) && al16(c) &&
                      (lda % 8) == 0 && (ldb % 8) == 0 && ((ldc * out_es) % 16) == 0 &&
@@ -539,7 +542,8 @@ int bwpp_gemm_launch_ex(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t 
   cudaStream_t s = ctx->stream;
   if (!tc_ok) {
     dim3 grid((N + ST - 1) / ST, (M + ST - 1) / ST);
-    gemm_simt_kernel<<<grid, dim3(ST, ST), 0, s>>>(a, b, c, M, N, K, lda, ldb, ldc, a_mn, b_mn, epi);
+    gemm_simt_kernel<<<grid, dim3(ST, ST), 0, s>>>(a, b, c, M, N, K, lda, ldb, ldc, a_mn, b_mn, epi,
+                                                   ab_f16 ? 1 : 0);
     BWPP_LAUNCH_CHECK(ctx, "gemm simt");
     return BWPP_CUDA_OK;
   }
@@ -547,7 +551,8 @@ int bwpp_gemm_launch_ex(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t 
   // of a pair would otherwise compute rows past M only).
   const bool pair = pairs_enabled() && M > (uint32_t)BM;
   CUtensorMap ta, tb, tb_pair, tcm;
-  const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto BF = ab_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto OUT16 = out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
   int rc = a_mn ? bwpp_make_tmap_2d(ctx, &ta, a, BF, M, K, (uint64_t)lda * 2, 64, BK, SW)
                 : bwpp_make_tmap_2d(ctx, &ta, a, BF, K, M, (uint64_t)lda * 2, BK, BM, SW);
@@ -561,16 +566,26 @@ int bwpp_gemm_launch_ex(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t 
                          : bwpp_make_tmap_2d(ctx, &tb_pair, b, BF, K, N, (uint64_t)ldb * 2, BK,
                                              GemmCfg<true>::BN_LOAD, SW);
   if (!rc)
-    rc = out_bf16 ? bwpp_make_tmap_2d(ctx, &tcm, c, BF, N, M, (uint64_t)ldc * 2, 64, 32, SW)
+    rc = out_bf16 ? bwpp_make_tmap_2d(ctx, &tcm, c, OUT16, N, M, (uint64_t)ldc * 2, 64, 32, SW)
                   : bwpp_make_tmap_2d(ctx, &tcm, c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M,
                                       (uint64_t)ldc * 4, EPI_COLS, 32, SW);
   if (rc) return rc;
+  const uint32_t f = ab_f16 ? 1u : 0u;
   if (a_mn) {
-    return b_mn ? launch_tc_any<true, true>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair)
-                : launch_tc_any<true, false>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair);
+    return b_mn ? launch_tc_any<true, true>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair, f)
+                : launch_tc_any<true, false>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair, f);
   }
-  return b_mn ? launch_tc_any<false, true>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair)
-              : launch_tc_any<false, false>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair);
+  return b_mn ? launch_tc_any<false, true>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair, f)
+              : launch_tc_any<false, false>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair, f);
+}
+
+int bwpp_gemm_launch_ex(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,
+                        const uint16_t *b, int b_mn, uint32_t ldb, void *c,
+                        uint32_t ldc, uint32_t M, uint32_t N, uint32_t K,
+                        const float *bias, int silu, const float *residual,
+                        uint32_t ldr, int out_bf16, int force_simt) {
+  return bwpp_gemm_launch_dt(ctx, a, a_mn, lda, b, b_mn, ldb, c, ldc, M, N, K, bias, silu,
+                             residual, ldr, out_bf16, force_simt, 0, 0);
 }
 
 // The reference-shaped matmul: A K-major, B MN-major, fp32 out.

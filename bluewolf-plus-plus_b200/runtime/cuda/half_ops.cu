@@ -1,0 +1,395 @@
+// f16 variants of the hot-path kernels for the reference's half ABI: the
+// MSL kernels compiler/codegen_metal.c:392-434 (bwpp_matmul_f16),
+// 457-556 (bwpp_attention_f16), 567-598 (bwpp_softmax_f16) and 609-636
+// (bwpp_rmsnorm_f16) take half buffers and compute in fp32; so do these.
+//   matmul:   f16 A/B on the tensor cores (tcgen05 kind::f16, f16 operand
+//             format), fp32 accumulation, epilogue in fp32, f16 C
+//   softmax / rmsnorm: f16 rows held in registers as fp32, f16 result
+//             rounded once (nearest even)
+//   attention: bwpp_cuda_attention_f16 in attention.cu
+// plus f16 <-> fp32 conversions, and half mirrors of the Metal dispatch
+// calls (runtime/metal/dispatch_stub.h:42-74) gated on the same
+// bwpp.meta tags as dispatch_stub.m.
+#include <math.h>
+#include <string.h>
+
+#include <type_traits>
+
+#include "bwpp_cuda_internal.cuh"
+
+int bwpp_gemm_launch_dt(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,
+                        const uint16_t *b, int b_mn, uint32_t ldb, void *c,
+                        uint32_t ldc, uint32_t M, uint32_t N, uint32_t K,
+                        const float *bias, int silu, const float *residual,
+                        uint32_t ldr, int out_bf16, int force_simt, int ab_f16,
+                        int out_f16);
+int bwpp_attention_launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                          const uint16_t *v, void *o, uint32_t BH, uint32_t Sq,
+                          uint32_t Skv, uint32_t Kd, uint32_t Dv, uint64_t q_bh,
+                          uint64_t k_bh, uint64_t v_bh, uint64_t o_bh,
+                          uint32_t ldq, uint32_t ldk, uint32_t ldv, uint32_t ldo,
+                          float scale, int causal, int f16);
+
+namespace {
+
+constexpr int kThreads = 256;
+
+inline bool al8(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
+// f16 row access: four halves (8 bytes, a warp touches 256 contiguous
+// bytes per instruction) or one half per element.
+template <bool V4>
+struct H;
+template <>
+struct H<true> {
+  static constexpr int W = 4;
+  __device__ static void load(const uint16_t *p, uint32_t i, float (&o)[4]) {
+    const uint2 t = __ldcs(reinterpret_cast<const uint2 *>(p) + i);
+    o[0] = load16<true>((uint16_t)(t.x & 0xFFFFu));
+    o[1] = load16<true>((uint16_t)(t.x >> 16));
+    o[2] = load16<true>((uint16_t)(t.y & 0xFFFFu));
+    o[3] = load16<true>((uint16_t)(t.y >> 16));
+  }
+  __device__ static void store(uint16_t *p, uint32_t i, const float (&v)[4]) {
+    __stcs(reinterpret_cast<uint2 *>(p) + i,
+           make_uint2(pack2_16<true>(v[0], v[1]), pack2_16<true>(v[2], v[3])));
+  }
+};
+template <>
+struct H<false> {
+  static constexpr int W = 1;
+  __device__ static void load(const uint16_t *p, uint32_t i, float (&o)[1]) {
+    o[0] = load16<true>(p[i]);
+  }
+  __device__ static void store(uint16_t *p, uint32_t i, const float (&v)[1]) {
+    p[i] = (uint16_t)(pack2_16<true>(v[0], 0.0f) & 0xFFFFu);
+  }
+};
+
+__device__ __forceinline__ float warp_block_reduce(float v, float *sv, bool is_max) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float t = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, t) : v + t;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // sv may still be read from the previous reduction
+  if (lane == 0) sv[warp] = v;
+  __syncthreads();
+  v = lane < (int)(blockDim.x >> 5) ? sv[lane] : (is_max ? -INFINITY : 0.0f);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float t = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, t) : v + t;
+  }
+  return v;
+}
+
+// Row softmax (max by strict '>', e = expf(x - max), inv = sum > 0 ? 1/sum
+// : 0) with the row in registers; rows wider than MAXV vectors per thread
+// take MAXV = 0, which streams the row three times.
+template <int MAXV, bool V4>
+__global__ void __launch_bounds__(kThreads)
+    softmax_f16_kernel(const uint16_t *__restrict__ x, uint16_t *__restrict__ y, uint32_t rows,
+                       uint32_t cols, uint32_t ld) {
+  using V = H<V4>;
+  constexpr int W = V::W;
+  __shared__ float sv[32];
+  const uint32_t nv = cols / W;
+  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint16_t *xr = x + (size_t)r * ld;
+    uint16_t *yr = y + (size_t)r * ld;
+    if (MAXV == 0) {
+      float m = -INFINITY;
+      for (uint32_t c = threadIdx.x; c < cols; c += kThreads) {
+        const float t = load16<true>(xr[c]);
+        if (t > m) m = t;
+      }
+      m = warp_block_reduce(m, sv, true);
+      float s = 0.0f;
+      for (uint32_t c = threadIdx.x; c < cols; c += kThreads) s += expf(load16<true>(xr[c]) - m);
+      s = warp_block_reduce(s, sv, false);
+      const float inv = s > 0.0f ? 1.0f / s : 0.0f;
+      for (uint32_t c = threadIdx.x; c < cols; c += kThreads)
+        yr[c] = (uint16_t)(pack2_16<true>(expf(load16<true>(xr[c]) - m) * inv, 0.0f) & 0xFFFFu);
+      continue;
+    }
+    constexpr int MV = MAXV > 0 ? MAXV : 1;
+    float xv[MV][W];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < MV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv) V::load(xr, idx, xv[i]);
+#pragma unroll
+      for (int w = 0; w < W; ++w)
+        if (idx < nv && xv[i][w] > m) m = xv[i][w];
+    }
+    m = warp_block_reduce(m, sv, true);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv)
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          xv[i][w] = expf(xv[i][w] - m);
+          s += xv[i][w];
+        }
+    }
+    s = warp_block_reduce(s, sv, false);
+    const float inv = s > 0.0f ? 1.0f / s : 0.0f;
+#pragma unroll
+    for (int i = 0; i < MV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv) {
+#pragma unroll
+        for (int w = 0; w < W; ++w) xv[i][w] *= inv;
+        V::store(yr, idx, xv[i]);
+      }
+    }
+  }
+}
+
+// y = x * rsqrt(mean(x^2) + eps) * gamma + beta (gamma / beta NULL: 1 / 0),
+// f16 in and out, fp32 arithmetic; MAXV = 0 streams the row twice.
+template <int MAXV, bool V4>
+__global__ void __launch_bounds__(kThreads)
+    rmsnorm_f16_kernel(const uint16_t *__restrict__ x, uint16_t *__restrict__ y,
+                       const uint16_t *__restrict__ gamma, const uint16_t *__restrict__ beta,
+                       uint32_t rows, uint32_t cols, uint32_t ld, float eps) {
+  using V = H<V4>;
+  constexpr int W = V::W;
+  __shared__ float sv[32];
+  const uint32_t nv = cols / W;
+  auto affine = [&](float v, uint32_t c) {
+    const float g = gamma ? load16<true>(gamma[c]) : 1.0f;
+    const float b = beta ? load16<true>(beta[c]) : 0.0f;
+    return v * g + b;
+  };
+  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint16_t *xr = x + (size_t)r * ld;
+    uint16_t *yr = y + (size_t)r * ld;
+    if (MAXV == 0) {
+      float ss = 0.0f;
+      for (uint32_t c = threadIdx.x; c < cols; c += kThreads) {
+        const float t = load16<true>(xr[c]);
+        ss = fmaf(t, t, ss);
+      }
+      ss = warp_block_reduce(ss, sv, false);
+      const float inv = rsqrtf(ss / (float)cols + eps);
+      for (uint32_t c = threadIdx.x; c < cols; c += kThreads)
+        yr[c] = (uint16_t)(pack2_16<true>(affine(load16<true>(xr[c]) * inv, c), 0.0f) & 0xFFFFu);
+      continue;
+    }
+    constexpr int MV = MAXV > 0 ? MAXV : 1;
+    float xv[MV][W];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv) {
+        V::load(xr, idx, xv[i]);
+#pragma unroll
+        for (int w = 0; w < W; ++w) ss = fmaf(xv[i][w], xv[i][w], ss);
+      }
+    }
+    ss = warp_block_reduce(ss, sv, false);
+    const float inv = rsqrtf(ss / (float)cols + eps);
+#pragma unroll
+    for (int i = 0; i < MV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv) {
+#pragma unroll
+        for (int w = 0; w < W; ++w) xv[i][w] = affine(xv[i][w] * inv, idx * W + w);
+        V::store(yr, idx, xv[i]);
+      }
+    }
+  }
+}
+
+__global__ void cast_f16_f32_kernel(const uint16_t *__restrict__ src, float *__restrict__ dst,
+                                    size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = load16<true>(src[i]);
+}
+
+__global__ void cast_f32_f16_kernel(const float *__restrict__ src, uint16_t *__restrict__ dst,
+                                    size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = (uint16_t)(pack2_16<true>(src[i], 0.0f) & 0xFFFFu);
+}
+
+uint32_t grid_rows(BwppCudaCtx *ctx, uint32_t rows) {
+  const uint32_t g = (uint32_t)ctx->num_sms * 8;
+  return rows < g ? (rows ? rows : 1) : g;
+}
+
+uint32_t grid_flat(BwppCudaCtx *ctx, size_t n) {
+  const size_t blocks = (n + 255) / 256;
+  const size_t cap = (size_t)ctx->num_sms * 16;
+  return (uint32_t)(blocks < cap ? (blocks ? blocks : 1) : cap);
+}
+
+// Picks MAXV (0 = streaming) for a row of nv vectors.
+template <typename F>
+void by_width(uint32_t nv, F &&f) {
+  const uint32_t per = (nv + kThreads - 1) / kThreads;
+  if (per <= 1) f(std::integral_constant<int, 1>{});
+  else if (per <= 2) f(std::integral_constant<int, 2>{});
+  else if (per <= 4) f(std::integral_constant<int, 4>{});
+  else if (per <= 8) f(std::integral_constant<int, 8>{});
+  else if (per <= 16) f(std::integral_constant<int, 16>{});
+  else f(std::integral_constant<int, 0>{});
+}
+
+bool has_tag(const char *src, const char *tag) {
+  return src && tag && strstr(src, tag) != nullptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bwpp_cuda_cast_f16_f32(BwppCudaCtx *ctx, const uint16_t *src, float *dst, size_t n) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (n == 0) return BWPP_CUDA_OK;
+  if (!src || !dst) return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "cast f16->f32: NULL");
+  cast_f16_f32_kernel<<<grid_flat(ctx, n), 256, 0, ctx->stream>>>(src, dst, n);
+  BWPP_LAUNCH_CHECK(ctx, "cast f16->f32");
+  return BWPP_CUDA_OK;
+}
+
+int bwpp_cuda_cast_f32_f16(BwppCudaCtx *ctx, const float *src, uint16_t *dst, size_t n) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (n == 0) return BWPP_CUDA_OK;
+  if (!src || !dst) return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "cast f32->f16: NULL");
+  cast_f32_f16_kernel<<<grid_flat(ctx, n), 256, 0, ctx->stream>>>(src, dst, n);
+  BWPP_LAUNCH_CHECK(ctx, "cast f32->f16");
+  return BWPP_CUDA_OK;
+}
+
+int bwpp_cuda_matmul_f16(BwppCudaCtx *ctx, const uint16_t *a, const uint16_t *b, uint16_t *c,
+                         uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                         uint32_t ldc, const uint16_t *bias, int apply_silu, int apply_bias) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (M && N && (!c || (K && (!a || !b))))
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "matmul f16: NULL buffer");
+  if (lda < K || ldb < N || ldc < N)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "matmul f16: leading dim smaller than row");
+  if (M == 0 || N == 0) return BWPP_CUDA_OK;
+  const float *bias32 = nullptr;
+  if (apply_bias && bias) {  // the epilogue adds an fp32 bias: widen the half one (exact)
+    float *w = static_cast<float *>(bwpp_ctx_workspace(ctx, (size_t)N * 4));
+    if (!w) return BWPP_CUDA_ERR_NOMEM;
+    cast_f16_f32_kernel<<<grid_flat(ctx, N), 256, 0, ctx->stream>>>(bias, w, N);
+    BWPP_LAUNCH_CHECK(ctx, "matmul f16 bias");
+    bias32 = w;
+  }
+  return bwpp_gemm_launch_dt(ctx, a, 0, lda, b, 1, ldb, c, ldc, M, N, K, bias32, apply_silu,
+                             nullptr, 0, 1, 0, 1, 1);
+}
+
+int bwpp_cuda_softmax_f16(BwppCudaCtx *ctx, const uint16_t *x, uint16_t *y, uint32_t rows,
+                          uint32_t cols, uint32_t ld) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (ld < cols || (rows && cols && (!x || !y)))
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "softmax f16: bad args");
+  if (rows == 0 || cols == 0) return BWPP_CUDA_OK;
+  const bool v4 = cols % 4 == 0 && ld % 4 == 0 && al8(x) && al8(y);
+  const uint32_t grid = grid_rows(ctx, rows);
+  cudaStream_t s = ctx->stream;
+  by_width(v4 ? cols / 4 : cols, [&](auto mv) {
+    constexpr int MV = decltype(mv)::value;
+    if (v4) softmax_f16_kernel<MV, true><<<grid, kThreads, 0, s>>>(x, y, rows, cols, ld);
+    else softmax_f16_kernel<MV, false><<<grid, kThreads, 0, s>>>(x, y, rows, cols, ld);
+  });
+  BWPP_LAUNCH_CHECK(ctx, "softmax f16");
+  return BWPP_CUDA_OK;
+}
+
+int bwpp_cuda_rmsnorm_f16(BwppCudaCtx *ctx, const uint16_t *x, uint16_t *y,
+                          const uint16_t *gamma, const uint16_t *beta, uint32_t rows,
+                          uint32_t cols, uint32_t ld, float eps) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (ld < cols || (rows && cols && (!x || !y)))
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "rmsnorm f16: bad args");
+  if (rows == 0 || cols == 0) return BWPP_CUDA_OK;
+  const bool v4 = cols % 4 == 0 && ld % 4 == 0 && al8(x) && al8(y);
+  const uint32_t grid = grid_rows(ctx, rows);
+  cudaStream_t s = ctx->stream;
+  by_width(v4 ? cols / 4 : cols, [&](auto mv) {
+    constexpr int MV = decltype(mv)::value;
+    if (v4)
+      rmsnorm_f16_kernel<MV, true><<<grid, kThreads, 0, s>>>(x, y, gamma, beta, rows, cols, ld, eps);
+    else
+      rmsnorm_f16_kernel<MV, false><<<grid, kThreads, 0, s>>>(x, y, gamma, beta, rows, cols, ld, eps);
+  });
+  BWPP_LAUNCH_CHECK(ctx, "rmsnorm f16");
+  return BWPP_CUDA_OK;
+}
+
+// ---- half mirrors of runtime/metal/dispatch_stub.h:42-74 ------------------
+// Same gating as dispatch_stub.m: a call whose source lacks the kernel's
+// bwpp.meta tag is a no-op returning OK; the matmul epilogue comes from the
+// #define / bwpp.meta epilogue tags (runtime/cpu/test_metal_parity.c:48-76).
+
+int bwpp_cuda_dispatch_matmul_f16(BwppCudaCtx *ctx, const uint16_t *a, const uint16_t *b,
+                                  uint16_t *c, const uint16_t *bias, BwppCudaMatmulParams p,
+                                  const char *source) {
+  if (!ctx || !a || !b || !c || !source) return BWPP_CUDA_ERR_ARG;
+  if (has_tag(source, "bwpp.meta: kernel=none") || !has_tag(source, "bwpp.meta: kernel=matmul_f16"))
+    return BWPP_CUDA_OK;
+  int ep_add = has_tag(source, "#define BWPP_EPILOGUE_ADD 1");
+  int ep_silu = has_tag(source, "#define BWPP_EPILOGUE_SILU 1");
+  if (!ep_add && !ep_silu) {
+    const char *t = strstr(source, "bwpp.meta: epilogue=");
+    if (t) {
+      t += strlen("bwpp.meta: epilogue=");
+      if (strncmp(t, "add_silu", 8) == 0) ep_add = ep_silu = 1;
+      else if (strncmp(t, "add", 3) == 0) ep_add = 1;
+      else if (strncmp(t, "silu", 4) == 0) ep_silu = 1;
+    }
+  }
+  // a missing bias buffer reads as zeros (dispatch_stub.m:103-110)
+  return bwpp_cuda_matmul_f16(ctx, a, b, c, p.M, p.N, p.K, p.lda, p.ldb, p.ldc, bias, ep_silu,
+                              ep_add);
+}
+
+int bwpp_cuda_dispatch_softmax_f16(BwppCudaCtx *ctx, const uint16_t *x, uint16_t *y,
+                                   BwppCudaSoftmaxParams p, const char *source) {
+  if (!ctx || !x || !y || !source) return BWPP_CUDA_ERR_ARG;
+  if (!has_tag(source, "softmax_f16")) return BWPP_CUDA_OK;
+  return bwpp_cuda_softmax_f16(ctx, x, y, p.rows, p.cols, p.ld);
+}
+
+int bwpp_cuda_dispatch_rmsnorm_f16(BwppCudaCtx *ctx, const uint16_t *x, const uint16_t *gamma,
+                                   const uint16_t *beta, uint16_t *y, BwppCudaRmsnormParams p,
+                                   const char *source) {
+  if (!ctx || !x || !y || !source) return BWPP_CUDA_ERR_ARG;
+  if (!has_tag(source, "rmsnorm_f16")) return BWPP_CUDA_OK;
+  return bwpp_cuda_rmsnorm_f16(ctx, x, y, gamma, beta, p.rows, p.cols, p.ld, p.eps);
+}
+
+int bwpp_cuda_dispatch_attention_f16(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                                     const uint16_t *v, uint16_t *o, BwppCudaAttentionParams p,
+                                     const char *source) {
+  if (!ctx || !q || !k || !v || !o || !source) return BWPP_CUDA_ERR_ARG;
+  if (!has_tag(source, "bwpp.meta: kernel=attention_f16")) return BWPP_CUDA_OK;
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  // one (b, h); per-head strides given so dense views (ld == D) take the
+  // tensor-core kernel
+  return bwpp_attention_launch(ctx, q, k, v, o, 1, p.M, p.N, p.K, p.D, (uint64_t)p.M * p.ldq,
+                               (uint64_t)p.N * p.ldk, (uint64_t)p.N * p.ldv,
+                               (uint64_t)p.M * p.ldo, p.ldq, p.ldk, p.ldv, p.ldo, 1.0f, 0, 1);
+}
+
+}  // extern "C"

@@ -23,11 +23,11 @@ int bwpp_cast_launch(BwppCudaCtx *ctx, const float *src, uint16_t *dst,
                      uint32_t rows, uint32_t cols, uint32_t ld_src,
                      uint32_t ld_dst);
 int bwpp_attention_launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
-                          const uint16_t *v, float *o, uint32_t BH, uint32_t Sq,
+                          const uint16_t *v, void *o, uint32_t BH, uint32_t Sq,
                           uint32_t Skv, uint32_t Kd, uint32_t Dv, uint64_t q_bh,
                           uint64_t k_bh, uint64_t v_bh, uint64_t o_bh,
                           uint32_t ldq, uint32_t ldk, uint32_t ldv, uint32_t ldo,
-                          float scale, int causal);
+                          float scale, int causal, int f16);
 
 namespace {
 
@@ -333,7 +333,7 @@ void bwpp_cuda_attention_f32(const float *q, const float *k, const float *v,
   if (!rc)
     rc = bwpp_attention_launch(ctx, q16, k16, v16, oo.ptr, 1, M, N, K, D,
                                (uint64_t)M * K, (uint64_t)N * K, (uint64_t)N * D,
-                               (uint64_t)M * oo.dld, K, K, D, oo.dld, 1.0f, 0);
+                               (uint64_t)M * oo.dld, K, K, D, oo.dld, 1.0f, 0, 0);
   if (!rc) rc = download(ctx, oo);
   finish(ctx, rc);
 }
@@ -422,7 +422,7 @@ int bwpp_cuda_dispatch_attention(BwppCudaCtx *ctx, const uint16_t *q,
   int rc = bwpp_ctx_enter(ctx);
   if (rc) return rc;
   return bwpp_attention_launch(ctx, q, k, v, o, 1, p.M, p.N, p.K, p.D, 0, 0, 0, 0,
-                               p.ldq, p.ldk, p.ldv, p.ldo, 1.0f, 0);
+                               p.ldq, p.ldk, p.ldv, p.ldo, 1.0f, 0, 0);
 }
 
 }  // extern "C"

@@ -435,6 +435,54 @@ int bwpp_cuda_dispatch_attention(BwppCudaCtx *ctx, const uint16_t *q,
                                  BwppCudaAttentionParams params,
                                  const char *source);
 
+/* ---- 4. f16 variants: the half ABI of the MSL kernels --------------------
+ * compiler/codegen_metal.c:392-434 (matmul), 457-556 (attention), 567-598
+ * (softmax), 609-636 (rmsnorm) read and write half; these take IEEE half
+ * bits (uint16_t) everywhere, compute in fp32 (tensor-core f16 operands with
+ * fp32 accumulation for the contractions) and round each result to half
+ * once, nearest even.  Stream-async like the bf16 / fp32 entry points. */
+
+/* C = epilogue(A * B) with bias[N] (half, added when apply_bias && bias),
+ * then SiLU when apply_silu; A [M, lda], B [K, ldb], C [M, ldc] row-major. */
+int bwpp_cuda_matmul_f16(BwppCudaCtx *ctx, const uint16_t *a, const uint16_t *b,
+                         uint16_t *c, uint32_t M, uint32_t N, uint32_t K,
+                         uint32_t lda, uint32_t ldb, uint32_t ldc,
+                         const uint16_t *bias, int apply_silu, int apply_bias);
+
+/* Q [B,H,Sq,D], K / V [B,H,Skv,D], O [B,H,Sq,D], all half. */
+int bwpp_cuda_attention_f16(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                            const uint16_t *v, uint16_t *o, uint32_t B, uint32_t H,
+                            uint32_t Sq, uint32_t Skv, uint32_t D, float scale,
+                            int causal);
+
+/* Row softmax of runtime/cpu/bwpp_cpu_ref.c:37-61 on half rows. */
+int bwpp_cuda_softmax_f16(BwppCudaCtx *ctx, const uint16_t *x, uint16_t *y,
+                          uint32_t rows, uint32_t cols, uint32_t ld);
+
+/* RMSNorm of runtime/cpu/bwpp_cpu_ref.c:63-90 on half rows (gamma / beta
+ * half or NULL). */
+int bwpp_cuda_rmsnorm_f16(BwppCudaCtx *ctx, const uint16_t *x, uint16_t *y,
+                          const uint16_t *gamma, const uint16_t *beta, uint32_t rows,
+                          uint32_t cols, uint32_t ld, float eps);
+
+/* Dense conversions between half bits and fp32 (nearest even to half). */
+int bwpp_cuda_cast_f16_f32(BwppCudaCtx *ctx, const uint16_t *src, float *dst, size_t n);
+int bwpp_cuda_cast_f32_f16(BwppCudaCtx *ctx, const float *src, uint16_t *dst, size_t n);
+
+/* Half mirrors of runtime/metal/dispatch_stub.h:42-74: every buffer half,
+ * same bwpp.meta gating and epilogue tags as the calls above. */
+int bwpp_cuda_dispatch_matmul_f16(BwppCudaCtx *ctx, const uint16_t *a, const uint16_t *b,
+                                  uint16_t *c, const uint16_t *bias,
+                                  BwppCudaMatmulParams params, const char *source);
+int bwpp_cuda_dispatch_softmax_f16(BwppCudaCtx *ctx, const uint16_t *x, uint16_t *y,
+                                   BwppCudaSoftmaxParams params, const char *source);
+int bwpp_cuda_dispatch_rmsnorm_f16(BwppCudaCtx *ctx, const uint16_t *x, const uint16_t *gamma,
+                                   const uint16_t *beta, uint16_t *y,
+                                   BwppCudaRmsnormParams params, const char *source);
+int bwpp_cuda_dispatch_attention_f16(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
+                                     const uint16_t *v, uint16_t *o,
+                                     BwppCudaAttentionParams params, const char *source);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif
