@@ -6,7 +6,8 @@
                                 rmsnorm_bwd|layernorm_fwd|layernorm_bwd|
                                 reduce_max_fwd|reduce_max_bwd|softmax_fwd|
                                 softmax_grad|silu_grad|reduce_sum_rows|
-                                reduce_sum_cols|broadcast_rows|tiny_model]
+                                reduce_sum_cols|broadcast_rows|gemm_f16|
+                                attention_f16|attention_causal_f16|tiny_model]
 
 Default workload (the headline): fused matmul + bias +
 SiLU, X[8192x4096] bf16 * W[4096x11008] bf16 + b[11008], fp32 out, rows of X
@@ -219,6 +220,51 @@ class GemmWorkload(Workload):
         return 2.0 * rows * self.N * self.K, dt, f"{rows} of 8192 rows x all 11008 columns, K=4096, fp32, row-split over {threads} threads"
 
 
+class GemmF16Workload(GemmWorkload):
+    """configs[1] shapes through the half ABI (bwpp_cuda_matmul_f16): f16 X, W,
+    b and C, fp32 accumulation."""
+    dtype = "f16"
+    profile = "gemm_tc_kernel_f16_config2"
+    e2e_api = "bwpp_cuda_matmul_f16; pinned host f16 X, W, b copied in and C copied out every step"
+
+    def setup(self):
+        super().setup()
+        t = self.torch
+        self.x = self.x.to(t.float16)
+        self.w = self.w.to(t.float16)
+        self.b = self.b.to(t.float16)
+        self.c = t.empty(self.m, self.N, dtype=t.float16, device="cuda")
+
+    def step(self):
+        self.ctx.matmul_f16(self.x, self.w, self.c, self.m, self.N, self.K, self.K, self.N, self.N,
+                            self.b, 1, 1)
+        return 2  # bias widening + GEMM
+
+    def config(self):
+        cfg = super().config()
+        cfg["workload"] = "fused matmul+bias+SiLU, half ABI (configs[1] shapes)"
+        cfg["inputs"] = "X,W ~ N(0,0.02) f16, b ~ U(-0.1,0.1) f16, out f16"
+        return cfg
+
+    def setup_e2e(self):
+        t = self.torch
+        self.ha, self.hb, self.hbias = (u.cpu().pin_memory() for u in (self.x, self.w, self.b))
+        self.hc = t.empty(self.m, self.N, dtype=t.float16).pin_memory()
+        self.h2d = (self.m * self.K + self.K * self.N + self.N) * 2
+        self.d2h = self.m * self.N * 2
+
+    def step_e2e(self):
+        self.x.copy_(self.ha, non_blocking=True)
+        self.w.copy_(self.hb, non_blocking=True)
+        self.b.copy_(self.hbias, non_blocking=True)
+        self.step()
+        self.hc.copy_(self.c, non_blocking=True)
+        self.torch.cuda.synchronize()
+
+    def cpu_sample(self, lib, threads):
+        return None
+
+
 class AttentionWorkload(Workload):
     """B=8 H=32 S=4096 d=128, bf16 in, fp32 out; heads over ranks."""
     B, H, S, D = 8, 32, 4096, 128
@@ -295,6 +341,45 @@ class AttentionWorkload(Workload):
         dt = time.perf_counter() - t0
         flops = sum(4.0 * self.D * ((r * (self.S // rows) + 1) if self.causal else self.S) for r in range(rows))
         return flops, dt, f"{rows} query rows of one (b,h), S={self.S}, d={self.D}, fp32, {threads} threads"
+
+
+class AttentionF16Workload(AttentionWorkload):
+    """configs[3] shapes through the half ABI (bwpp_cuda_attention_f16)."""
+    dtype = "f16"
+    profile = "attention_f16_config4"
+    e2e_api = "bwpp_cuda_attention_f16; pinned host f16 Q, K, V copied in and O copied out every step"
+
+    def setup(self):
+        super().setup()
+        t = self.torch
+        self.q, self.k, self.v = (u.to(t.float16) for u in (self.q, self.k, self.v))
+        self.o = t.empty(self.nh, self.S, self.D, dtype=t.float16, device="cuda")
+
+    def step(self):
+        self.ctx.attention_f16(self.q, self.k, self.v, self.o, 1, self.nh, self.S, self.S, self.D,
+                               self.D ** -0.5, int(self.causal))
+        return 1
+
+    def config(self):
+        cfg = super().config()
+        cfg["workload"] = cfg["workload"].replace("(BASELINE configs[3])", "half ABI (configs[3] shapes)")
+        return cfg
+
+    def setup_e2e(self):
+        self.hq, self.hk, self.hv = (u.cpu().pin_memory() for u in (self.q, self.k, self.v))
+        self.ho = self.torch.empty(self.nh, self.S, self.D, dtype=self.torch.float16).pin_memory()
+        self.h2d = 3 * self.nh * self.S * self.D * 2
+        self.d2h = self.nh * self.S * self.D * 2
+
+    def step_e2e(self):
+        for dst, src in ((self.q, self.hq), (self.k, self.hk), (self.v, self.hv)):
+            dst.copy_(src, non_blocking=True)
+        self.step()
+        self.ho.copy_(self.o, non_blocking=True)
+        self.torch.cuda.synchronize()
+
+    def cpu_sample(self, lib, threads):
+        return None
 
 
 class RowWorkload(Workload):
@@ -482,8 +567,12 @@ def make_workload(name, *a):
         return GemmWorkload(*a)
     if name == "tiny_model":
         return TinyModelWorkload(*a)
+    if name == "gemm_f16":
+        return GemmF16Workload(*a)
     if name in ("attention", "attention_causal"):
         return AttentionWorkload(*a, causal=name.endswith("causal"))
+    if name in ("attention_f16", "attention_causal_f16"):
+        return AttentionF16Workload(*a, causal="causal" in name)
     return RowWorkload(*a, op=name)
 
 
