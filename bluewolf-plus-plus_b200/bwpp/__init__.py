@@ -140,6 +140,19 @@ _SIGS = {
     "bwpp_cuda_dispatch_softmax_f16": (_i32, [_vp, _vp, _vp, SoftmaxParams, _cp]),
     "bwpp_cuda_dispatch_rmsnorm_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, RmsnormParams, _cp]),
     "bwpp_cuda_dispatch_attention_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, AttentionParams, _cp]),
+    # launch-plan executor
+    "bwpp_cuda_plan_create": (_i32, [_vp, _cp, _cp, _cp, _cp, C.POINTER(_vp)]),
+    "bwpp_cuda_plan_last_error": (_cp, []),
+    "bwpp_cuda_plan_describe": (_i32, [_vp, C.c_char_p, C.c_size_t]),
+    "bwpp_cuda_plan_find": (_i32, [_vp, _cp]),
+    "bwpp_cuda_plan_value_count": (_i32, [_vp]),
+    "bwpp_cuda_plan_value_info": (_i32, [_vp, _i32, C.POINTER(_i32), C.POINTER(_i32),
+                                         C.POINTER(C.c_int64), C.POINTER(_i32)]),
+    "bwpp_cuda_plan_bind": (_i32, [_vp, _i32, _vp]),
+    "bwpp_cuda_plan_value_ptr": (_vp, [_vp, _i32]),
+    "bwpp_cuda_plan_run": (_i32, [_vp]),
+    "bwpp_cuda_plan_launches": (C.c_size_t, [_vp]),
+    "bwpp_cuda_plan_destroy": (_i32, [_vp]),
 }
 
 _lib = None
@@ -322,6 +335,125 @@ class Ctx:
     def cast_f32_bf16(self, src, dst, rows, cols, ld_src):
         self.check(self.lib.bwpp_cuda_cast_f32_bf16(self.handle, _ptr(src), _ptr(dst), rows, cols, ld_src),
                    "cast_f32_bf16")
+
+
+class Plan:
+    """A graph of the reference compiler (its --dot / --grad-dot dump, and
+    optionally its --mem-plan dump) lowered onto the CUDA kernels.
+
+        plan = Plan(ctx, open("g.dot").read(), open("m.txt").read(), {"T": 128, "D": 256})
+        plan.bind("x", x_tensor); ...; plan.run(); y = plan.tensor("out")
+
+    ctx=None parses and lowers only (describe() works without a GPU)."""
+
+    DTYPES = {0: "float16", 1: "bfloat16", 2: "float32"}
+
+    def __init__(self, ctx, graph_dot: str, mem_plan: str | None = None, dims: dict | None = None,
+                 options: str | None = None):
+        self.lib = load()
+        self.ctx = ctx
+        spec = ",".join(f"{k}={int(v)}" for k, v in (dims or {}).items())
+        h = C.c_void_p()
+        rc = self.lib.bwpp_cuda_plan_create(ctx.handle if ctx is not None else None, graph_dot.encode(),
+                                            mem_plan.encode() if mem_plan else None, spec.encode(),
+                                            options.encode() if options else None, C.byref(h))
+        if rc != 0:
+            raise RuntimeError(f"plan_create: {status_string(rc)}: "
+                               f"{self.lib.bwpp_cuda_plan_last_error().decode()}")
+        self.handle = h
+        self._bound = {}
+
+    def describe(self) -> str:
+        n = self.lib.bwpp_cuda_plan_describe(self.handle, None, 0)
+        buf = C.create_string_buffer(n)
+        self.lib.bwpp_cuda_plan_describe(self.handle, buf, n)
+        return buf.value.decode()
+
+    def steps(self) -> list:
+        return [ln for ln in self.describe().splitlines() if ln and not ln.startswith("arena")]
+
+    def id(self, name_or_id) -> int:
+        if isinstance(name_or_id, int):
+            return name_or_id
+        vid = self.lib.bwpp_cuda_plan_find(self.handle, name_or_id.encode())
+        if vid < 0:
+            raise KeyError(name_or_id)
+        return vid
+
+    def info(self, name_or_id) -> dict:
+        vid = self.id(name_or_id)
+        dt, rank, flags = C.c_int(), C.c_int(), C.c_int()
+        dims = (C.c_int64 * 8)()
+        rc = self.lib.bwpp_cuda_plan_value_info(self.handle, vid, C.byref(dt), C.byref(rank), dims,
+                                                C.byref(flags))
+        if rc != 0:
+            raise KeyError(name_or_id)
+        return {"id": vid, "dtype": self.DTYPES[dt.value], "shape": tuple(dims[:rank.value]),
+                "input": bool(flags.value & 1), "output": bool(flags.value & 2),
+                "held": bool(flags.value & 4)}
+
+    def values(self) -> list:
+        out = []
+        for i in range(self.lib.bwpp_cuda_plan_value_count(self.handle)):
+            try:
+                out.append(self.info(i))
+            except KeyError:
+                pass
+        return out
+
+    def bind(self, name_or_id, tensor):
+        vid = self.id(name_or_id)
+        self._bound[vid] = tensor  # kept alive while the plan may read it
+        rc = self.lib.bwpp_cuda_plan_bind(self.handle, vid, _ptr(tensor))
+        if rc != 0:
+            raise RuntimeError(f"plan_bind({name_or_id}): {status_string(rc)}")
+
+    def run(self):
+        rc = self.lib.bwpp_cuda_plan_run(self.handle)
+        if self.ctx is None:
+            raise RuntimeError("plan_run: the plan was created without a context")
+        self.ctx.check(rc, "plan_run")
+
+    @property
+    def launches(self) -> int:
+        return int(self.lib.bwpp_cuda_plan_launches(self.handle))
+
+    def tensor(self, name_or_id):
+        """A torch view of a value held in the plan's memory (valid until close)."""
+        import torch
+        meta = self.info(name_or_id)
+        ptr = self.lib.bwpp_cuda_plan_value_ptr(self.handle, meta["id"])
+        if not ptr:
+            raise RuntimeError(f"{name_or_id} is not materialised")
+        dtype = getattr(torch, meta["dtype"])
+        n = 1
+        for d in meta["shape"]:
+            n *= d
+        esz = torch.empty(0, dtype=dtype).element_size()
+        return _cuda_view(ptr, n * esz, self.ctx.device if self.ctx is not None else 0).view(dtype) \
+            .reshape(meta["shape"])
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.bwpp_cuda_plan_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _cuda_view(ptr: int, nbytes: int, device: int):
+    """uint8 torch tensor aliasing nbytes of device memory at ptr (no copy)."""
+    import torch
+
+    class _Arr:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                    "version": 3}
+    with torch.cuda.device(device):
+        return torch.as_tensor(_Arr(), device=f"cuda:{device}")
 
 
 class TinyModel:

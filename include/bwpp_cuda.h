@@ -483,6 +483,45 @@ int bwpp_cuda_dispatch_attention_f16(BwppCudaCtx *ctx, const uint16_t *q, const 
                                      const uint16_t *v, uint16_t *o,
                                      BwppCudaAttentionParams params, const char *source);
 
+/* ---- 5. launch-plan executor ----------------------------------------------
+ * Runs a graph built by the reference compiler from its own dumps:
+ *   bwppc in.bwpp out.metal --entry fn --dot graph.dot [--mem-plan plan.txt]
+ *   (or --grad-dot for the gradient graph).
+ * graph_dot: the text of the graph dump (compiler/graph_ir.c:1326-1358);
+ * mem_plan: the text of the memory-plan dump (compiler/mem_plan.c:176-193) or
+ * NULL (every value then gets its own buffer); dims: "T=128,D=256,..." binds
+ * the symbolic dims; options: NULL or "eps=1e-5,fuse=1".
+ * With ctx == NULL the plan is parsed and lowered only (no device memory):
+ * bwpp_cuda_plan_describe shows the lowered steps.  Fusions: matmul ->
+ * softmax attention patterns into the attention kernel, transposes into GEMM
+ * operand layouts, matmul -> add(bias by dataflow) -> silu into the GEMM
+ * epilogue.  No counterpart in the reference (it has no executor for its
+ * graphs); the op vocabulary is compiler/include/graph_ir.h:39-57. */
+typedef struct BwppCudaPlan BwppCudaPlan;
+int bwpp_cuda_plan_create(BwppCudaCtx *ctx, const char *graph_dot, const char *mem_plan,
+                          const char *dims, const char *options, BwppCudaPlan **out);
+/* Message of the last failed bwpp_cuda_plan_create on this thread. */
+const char *bwpp_cuda_plan_last_error(void);
+/* Writes the lowered steps as text; returns the bytes needed (incl. NUL). */
+int bwpp_cuda_plan_describe(const BwppCudaPlan *plan, char *buf, size_t len);
+/* Value id of the value named `name` in the graph, or -1. */
+int bwpp_cuda_plan_find(const BwppCudaPlan *plan, const char *name);
+int bwpp_cuda_plan_value_count(const BwppCudaPlan *plan);
+/* dtype: 0 f16, 1 bf16, 2 f32; dims8 receives up to 8 dims; flags: bit 0
+ * graph input, bit 1 graph output, bit 2 held in the plan's memory. */
+int bwpp_cuda_plan_value_info(const BwppCudaPlan *plan, int id, int *dtype, int *rank,
+                              int64_t *dims8, int *flags);
+/* Binds a graph input (required before run) or output (optional: written
+ * there instead of the plan's memory) to caller device memory. */
+int bwpp_cuda_plan_bind(BwppCudaPlan *plan, int id, void *dev_ptr);
+/* Device address of a value held in the plan's memory (or bound). */
+void *bwpp_cuda_plan_value_ptr(const BwppCudaPlan *plan, int id);
+/* Enqueues every step on the ctx stream (stream-async, like the kernels). */
+int bwpp_cuda_plan_run(BwppCudaPlan *plan);
+/* Kernel launches the last run enqueued. */
+size_t bwpp_cuda_plan_launches(const BwppCudaPlan *plan);
+int bwpp_cuda_plan_destroy(BwppCudaPlan *plan);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

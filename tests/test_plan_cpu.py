@@ -1,0 +1,90 @@
+"""Launch-plan executor, lowering only (no GPU): the reference compiler's own
+graph / memory-plan dumps (tests/golden/plans/, made by make_plans.py with
+the unmodified bwppc) are parsed and lowered with ctx = NULL, and the step
+lists are checked: which nodes fuse (attention, transposes into GEMM
+layouts, bias-by-dataflow and SiLU into the GEMM epilogue), which run alone,
+and the errors for unbound dims, unknown ops and malformed dumps."""
+import os
+
+import pytest
+
+import bwpp
+
+PLANS = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "plans")
+TINY = dict(T=128, D=256, H=512, V=1000)
+
+
+def dump(name, ext=".dot"):
+    with open(os.path.join(PLANS, name + ext)) as f:
+        return f.read()
+
+
+def lower(name, dims, grad=False, mem=True, options=None):
+    return bwpp.Plan(None, dump(name, ".grad.dot" if grad else ".dot"),
+                     dump(name, ".mem.txt") if mem and not grad else None, dims, options)
+
+
+def kinds(plan):
+    return [" ".join(s.split()[2:]).split(" -> ")[0] for s in plan.steps()]
+
+
+def test_matmul_bias_silu_is_one_gemm():
+    assert kinds(lower("matmul_add_silu", dict(M=64, K=128, N=96))) == ["gemm +bias +silu"]
+
+
+def test_reshaped_bias_found_by_dataflow():
+    # the reference's own fusion pass loses the bias flag behind reshape(bias)
+    # (compiler/graph_ir.c:760-767); the executor finds it by dataflow
+    assert kinds(lower("matmul_add_bias_reshape", dict(M=64, K=128, N=96))) == ["gemm +bias"]
+    assert kinds(lower("multi_fn_bias", dict(M=64, K=128, N=96))) == ["gemm +bias"]
+
+
+def test_norms_and_plain_matmul():
+    assert kinds(lower("norms", dict(B=8, N=64))) == ["gemm", "softmax", "rmsnorm"]
+    assert kinds(lower("matmul", dict(M=8, K=16, N=32))) == ["gemm"]
+
+
+def test_attention_pattern_fuses_rank4():
+    p = lower("attention", dict(B=2, H=4, T=128, D=64))
+    assert kinds(p) == ["attention (fused transpose, matmul, softmax, matmul)"]
+    assert p.info(p.values()[-1]["id"])["shape"] == (2, 4, 128, 64)
+
+
+def test_tiny_model_forward_lowering():
+    p = lower("tiny_model", TINY)
+    k = kinds(p)
+    assert len(k) == 24
+    assert k.count("attention (fused transpose, matmul, softmax, matmul)") == 2
+    assert k.count("gemm +silu") == 2 and sum(x.startswith("gemm") for x in k) == 13
+    assert k.count("rmsnorm") == 4 and k.count("add") == 4 and k.count("softmax") == 1
+    assert "transpose" not in k
+    out = [v for v in p.values() if v["output"]]
+    assert len(out) == 1 and out[0]["shape"] == (128, 1000)
+
+
+def test_tiny_model_unfused_keeps_every_node():
+    k = kinds(lower("tiny_model", TINY, options="fuse=0"))
+    assert len(k) == 32 and k.count("transpose") == 2 and k.count("softmax") == 3
+
+
+def test_gradient_graphs_fold_every_transpose():
+    for name, dims in (("matmul_add_silu", dict(M=64, K=128, N=96)), ("norms", dict(B=8, N=64)),
+                       ("tiny_model", TINY), ("tiny_block", TINY), ("tiny_ffn", TINY)):
+        k = kinds(lower(name, dims, grad=True))
+        assert "transpose" not in k, (name, k)
+        assert any("^T" in x for x in k), (name, k)
+    k = kinds(lower("matmul_add_silu", dict(M=64, K=128, N=96), grad=True))
+    assert k == ["silu_grad", "reduce_sum", "reshape", "gemm B^T", "gemm A^T"]
+
+
+def test_errors_are_reported():
+    with pytest.raises(RuntimeError, match="dim N"):
+        lower("matmul", dict(M=8, K=16))
+    bad = dump("matmul").replace('label="matmul"', 'label="permute"')
+    with pytest.raises(RuntimeError, match="permute"):
+        bwpp.Plan(None, bad, None, dict(M=8, K=16, N=32))
+    with pytest.raises(RuntimeError):
+        bwpp.Plan(None, "not a graph", None, {})
+    with pytest.raises(RuntimeError, match="inner dims"):
+        lower("matmul", dict(M=8, K=16, N=32)).close() or bwpp.Plan(
+            None, dump("matmul").replace("[K,N]", "[N,K]"), None, dict(M=8, K=16, N=32))

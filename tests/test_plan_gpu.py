@@ -1,0 +1,205 @@
+"""Launch-plan executor on the GPU: graphs built by the reference compiler
+(its own --dot / --grad-dot / --mem-plan dumps of the reference examples,
+tests/golden/plans/) run end to end on the CUDA kernels and are compared with
+a CPU composition of the oracle's restatements of runtime/cpu/bwpp_cpu_ref.c
+(forward) or float64 torch autograd (gradient graphs, whose rules
+compiler/graph_ir.c:1529-1796 states but no reference kernel runs).
+
+Every value is stored as the graph declares it (f16), so intermediate
+results are rounded to half; tolerances: relative Frobenius <= 1e-2 for one
+contraction, <= 3e-2 for a composed model (as the training-step test)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import bwpp
+import oracle as O
+from conftest import rel_fro
+
+pytestmark = pytest.mark.gpu
+PLANS = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "plans")
+
+
+def dump(name, ext=".dot"):
+    with open(os.path.join(PLANS, name + ext)) as f:
+        return f.read()
+
+
+def half(rng, *shape, scale=1.0):
+    return (scale * rng.standard_normal(shape)).astype(np.float16)
+
+
+def f32(a):
+    return np.asarray(a, np.float32)
+
+
+def run(ctx, name, dims, inputs, grad=False, options=None, mem=True):
+    plan = bwpp.Plan(ctx, dump(name, ".grad.dot" if grad else ".dot"),
+                     dump(name, ".mem.txt") if mem and not grad else None, dims, options)
+    for key, arr in inputs.items():
+        plan.bind(key, torch.from_numpy(np.ascontiguousarray(arr)).cuda())
+    plan.run()
+    ctx.sync()
+    outs = {v["id"]: plan.tensor(v["id"]).float().cpu().numpy() for v in plan.values() if v["output"]}
+    launches = plan.launches
+    plan.close()
+    return outs, launches
+
+
+@pytest.mark.parametrize("fuse", [1, 0])
+def test_matmul_add_silu(ctx, fuse):
+    M, K, N = 200, 256, 384
+    rng = np.random.default_rng(1)
+    a, b, bias = half(rng, M, K, scale=0.5), half(rng, K, N, scale=0.5), half(rng, N, scale=0.1)
+    outs, launches = run(ctx, "matmul_add_silu", dict(M=M, K=K, N=N), {"a": a, "b": b, "bias": bias},
+                         options=f"fuse={fuse}")
+    ref = O.matmul(f32(a), f32(b), f32(bias), 1, 1)
+    (out,) = outs.values()
+    assert rel_fro(out, ref) <= 2e-3
+    assert launches == (1 if fuse else 3)
+
+
+def test_matmul_add_reshaped_bias(ctx):
+    M, K, N = 129, 136, 264
+    rng = np.random.default_rng(2)
+    a, b, bias = half(rng, M, K), half(rng, K, N), half(rng, N)
+    outs, launches = run(ctx, "matmul_add_bias_reshape", dict(M=M, K=K, N=N), {"a": a, "b": b, "bias": bias})
+    (out,) = outs.values()
+    assert rel_fro(out, O.matmul(f32(a), f32(b), f32(bias), 0, 1)) <= 2e-3 and launches == 1
+
+
+def test_norms_graph(ctx):
+    B, N = 96, 512
+    rng = np.random.default_rng(3)
+    x, w = half(rng, B, N, scale=0.2), half(rng, N, N, scale=0.2)
+    gamma = (1 + 0.1 * rng.standard_normal(N)).astype(np.float16)
+    outs, _ = run(ctx, "norms", dict(B=B, N=N), {"x": x, "w": w, "gamma": gamma})
+    y = O.matmul(f32(x), f32(w)).astype(np.float16)  # the graph stores y as f16
+    ref = O.rmsnorm(O.softmax(f32(y)), f32(gamma), None, 1e-5)
+    (out,) = outs.values()
+    assert rel_fro(out, ref) <= 1e-2
+
+
+@pytest.mark.parametrize("D", [64, 128, 96])
+def test_attention_graph_rank4(ctx, D):
+    B, H, T = 2, 3, 256
+    rng = np.random.default_rng(D)
+    q, k, v = (half(rng, B, H, T, D, scale=0.3) for _ in range(3))
+    outs, launches = run(ctx, "attention", dict(B=B, H=H, T=T, D=D), {"q": q, "k": k, "v": v})
+    ref = O.attention_bhsd(f32(q), f32(k), f32(v), 1.0, 0)  # the graph is unscaled, unmasked
+    (out,) = outs.values()
+    assert out.shape == (B, H, T, D) and launches == 1
+    assert rel_fro(out, ref) <= 1e-2
+
+
+def tiny_forward_ref(p, eps=1e-5):
+    """fp32 composition of examples/tiny_model.bwpp with the oracle restatements."""
+    def block(x, pre):
+        n1 = O.rmsnorm(x, p["g1" + pre], None, eps)
+        q, k, v = (O.matmul(n1, p[w + pre]) for w in ("wq", "wk", "wv"))
+        s = O.softmax(O.matmul(q, np.ascontiguousarray(k.T)))
+        a = O.matmul(O.matmul(s, v), p["wo" + pre])
+        x1 = x + a
+        n2 = O.rmsnorm(x1, p["g2" + pre], None, eps)
+        h = O.matmul(n2, p["w1" + pre])
+        h = h / (1 + np.exp(-h))
+        return x1 + O.matmul(h.astype(np.float32), p["w2" + pre])
+    h1 = block(p["x"], "1")
+    h2 = block(h1, "2")
+    return O.softmax(O.matmul(h2, p["wcls"]))
+
+
+@pytest.mark.parametrize("fuse", [1, 0])
+def test_tiny_model_forward(ctx, fuse):
+    T, D, H, V = 256, 128, 256, 512
+    rng = np.random.default_rng(7)
+    p = {"x": half(rng, T, D)}
+    for pre in ("1", "2"):
+        for w in ("wq", "wk", "wv", "wo"):
+            p[w + pre] = half(rng, D, D, scale=D ** -0.5)
+        p["w1" + pre] = half(rng, D, H, scale=D ** -0.5)
+        p["w2" + pre] = half(rng, H, D, scale=H ** -0.5)
+        p["g1" + pre] = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+        p["g2" + pre] = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    p["wcls"] = half(rng, D, V, scale=D ** -0.5)
+    outs, launches = run(ctx, "tiny_model", dict(T=T, D=D, H=H, V=V), p, options=f"fuse={fuse}")
+    ref = tiny_forward_ref({k: f32(v) for k, v in p.items()})
+    (out,) = outs.values()
+    assert out.shape == (T, V)
+    assert rel_fro(out, ref) <= 3e-2
+    assert launches == (24 if fuse else 32)
+
+
+def test_grad_graph_matmul_add_silu(ctx):
+    """Gradient graph: inputs a, b, bias, y = a@b + bias (activation) and the
+    output gradient; outputs dbias, da, db."""
+    M, K, N = 192, 128, 256
+    rng = np.random.default_rng(11)
+    a, b, bias = half(rng, M, K, scale=0.5), half(rng, K, N, scale=0.5), half(rng, N, scale=0.1)
+    y = (f32(a) @ f32(b) + f32(bias)).astype(np.float16)
+    dout = half(rng, M, N)
+    plan = bwpp.Plan(ctx, dump("matmul_add_silu", ".grad.dot"), None, dict(M=M, K=K, N=N))
+    seed = [v["id"] for v in plan.values() if v["input"] and v["id"] not in
+            (plan.id("a"), plan.id("b"), plan.id("bias"), plan.id("y"))]
+    assert len(seed) == 1
+    keep = []
+    for key, arr in (("a", a), ("b", b), ("bias", bias), ("y", y), (seed[0], dout)):
+        t = torch.from_numpy(arr).cuda()
+        keep.append(t)
+        plan.bind(key, t)
+    plan.run()
+    ctx.sync()
+    got = {v["shape"]: plan.tensor(v["id"]).double().cpu() for v in plan.values() if v["output"]}
+    at, bt, bit = (torch.tensor(f32(u), dtype=torch.float64, requires_grad=True) for u in (a, b, bias))
+    yt = at @ bt + bit
+    torch.nn.functional.silu(yt).backward(torch.tensor(f32(dout), dtype=torch.float64))
+    assert rel_fro(got[(N,)].numpy(), bit.grad.numpy()) <= 1e-2
+    assert rel_fro(got[(M, K)].numpy(), at.grad.numpy()) <= 1e-2
+    assert rel_fro(got[(K, N)].numpy(), bt.grad.numpy()) <= 1e-2
+    plan.close()
+
+
+def test_grad_graph_norms(ctx):
+    """rmsnorm(softmax(x @ w), gamma): gradients of x, w, gamma from the
+    reference compiler's gradient graph (rmsnorm_grad, softmax_grad,
+    reduce_sum, div, mul, transposed GEMMs)."""
+    B, N = 64, 256
+    rng = np.random.default_rng(13)
+    x, w = half(rng, B, N, scale=0.3), half(rng, N, N, scale=0.3)
+    gamma = (1 + 0.1 * rng.standard_normal(N)).astype(np.float16)
+    s = O.softmax(f32(x) @ f32(w)).astype(np.float16)
+    Y = O.rmsnorm(f32(s), f32(gamma), None, 1e-5).astype(np.float16)
+    dY = half(rng, B, N)
+    plan = bwpp.Plan(ctx, dump("norms", ".grad.dot"), None, dict(B=B, N=N))
+    named = {plan.id(n) for n in ("x", "w", "gamma", "s")}
+    unnamed = [v["id"] for v in plan.values() if v["input"] and v["id"] not in named]
+    # the rmsnorm_grad node reads (s, gamma, dY): the seed is its third input;
+    # the other unnamed input is the forward output Y
+    steps = plan.describe()
+    assert "rmsnorm_grad" in steps and len(unnamed) == 2
+    keep = []
+    dy_id, y_id = sorted(unnamed)  # dump order: v3 = dY seed, v6 = Y
+    for key, arr in (("x", x), ("w", w), ("gamma", gamma), ("s", s), (dy_id, dY), (y_id, Y)):
+        t = torch.from_numpy(np.ascontiguousarray(arr)).cuda()
+        keep.append(t)
+        plan.bind(key, t)
+    plan.run()
+    ctx.sync()
+    got = {v["shape"]: plan.tensor(v["id"]).double().cpu().numpy() for v in plan.values() if v["output"]}
+    xt, wt, gt = (torch.tensor(f32(u), dtype=torch.float64, requires_grad=True) for u in (x, w, gamma))
+    st = torch.softmax(xt @ wt, -1)
+    yt = st * torch.rsqrt((st * st).mean(-1, keepdim=True) + 1e-5) * gt
+    yt.backward(torch.tensor(f32(dY), dtype=torch.float64))
+    assert rel_fro(got[(N,)], gt.grad.numpy()) <= 2e-2
+    assert rel_fro(got[(B, N)], xt.grad.numpy()) <= 3e-2
+    assert rel_fro(got[(N, N)], wt.grad.numpy()) <= 3e-2
+    plan.close()
+
+
+def test_unbound_input_is_an_error(ctx):
+    plan = bwpp.Plan(ctx, dump("matmul"), dump("matmul", ".mem.txt"), dict(M=8, K=16, N=32))
+    with pytest.raises(bwpp.BwppError):
+        plan.run()
+    plan.close()
