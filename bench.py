@@ -7,7 +7,8 @@
                                 reduce_max_fwd|reduce_max_bwd|softmax_fwd|
                                 softmax_grad|silu_grad|reduce_sum_rows|
                                 reduce_sum_cols|broadcast_rows|gemm_f16|
-                                attention_f16|attention_causal_f16|tiny_model]
+                                attention_f16|attention_causal_f16|tiny_model|
+                                plan_tiny_model]
 
 Default workload (the headline): fused matmul + bias +
 SiLU, X[8192x4096] bf16 * W[4096x11008] bf16 + b[11008], fp32 out, rows of X
@@ -382,6 +383,83 @@ class AttentionF16Workload(AttentionWorkload):
         return None
 
 
+class PlanTinyModelWorkload(Workload):
+    """examples/tiny_model.bwpp through the launch-plan executor: the reference
+    compiler's own graph and memory-plan dumps (tests/golden/plans/), bound to
+    T=8192 tokens, D=1024, H=4096, V=32000, f16 as the graph declares; one
+    step = one forward pass of the graph (24 kernel steps)."""
+    T, D, H, V = 8192, 1024, 4096, 32000
+    kernel = "plan (tiny_model graph)"
+    profile = "plan_tiny_model"
+    dtype = "f16"
+    e2e_api = "bwpp_cuda_plan_run; pinned host f16 x copied in and the [T,V] probabilities copied out"
+
+    def setup(self):
+        t = self.torch
+        here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden", "plans")
+        dot = open(os.path.join(here, "tiny_model.dot")).read()
+        mem = open(os.path.join(here, "tiny_model.mem.txt")).read()
+        dims = dict(T=self.T, D=self.D, H=self.H, V=self.V)
+        self.plan = self.bwpp.Plan(self.ctx, dot, mem, dims)
+        g = t.Generator(device="cuda").manual_seed(6000 + self.rank)
+        self.inputs = {}
+        x_id = self.plan.id("x")
+        for v in self.plan.values():
+            if not v["input"]:
+                continue
+            shape = v["shape"]
+            # x ~ N(0, 1); weights [in, out] ~ N(0, 1/in); norm gains 1 + N(0, 0.01)
+            scale = 1.0 if (len(shape) == 1 or v["id"] == x_id) else shape[0] ** -0.5
+            x = t.randn(*shape, device="cuda", generator=g) * (0.1 if len(shape) == 1 else scale)
+            if len(shape) == 1:
+                x = x + 1.0  # norm gains near 1
+            self.inputs[v["id"]] = x.to(t.float16)
+            self.plan.bind(v["id"], self.inputs[v["id"]])
+        self.x_id = self.plan.id("x")
+        self.out_id = [v["id"] for v in self.plan.values() if v["output"]][0]
+
+    def step(self):
+        self.plan.run()
+        return self.plan.launches
+
+    def flops(self):
+        T, D, H, V = self.T, self.D, self.H, self.V
+        block = 3 * 2 * T * D * D + 2 * 2 * T * T * D + 2 * T * D * D + 2 * 2 * T * D * H
+        return 2 * block + 2 * T * D * V
+
+    def work_per_step(self):
+        return float(self.flops())
+
+    def total_work_per_step(self):
+        return float(self.flops() * self.world)
+
+    def config(self):
+        return {"workload": "examples/tiny_model.bwpp forward from the reference compiler's graph + "
+                            "memory-plan dumps, launch-plan executor",
+                "T": self.T, "D": self.D, "H": self.H, "V": self.V,
+                "parallelism": f"one replica per GPU ({self.world}), no collective",
+                "fusions": "silu and residual-add GEMM epilogues, transposes folded; attention "
+                            "unfused (head dim D > 256)",
+                "l2": "256 MiB written between timed steps (flush)"}
+
+    def setup_e2e(self):
+        t = self.torch
+        self.hx = self.inputs[self.x_id].cpu().pin_memory()
+        out = self.plan.tensor(self.out_id)
+        self.hout = t.empty(out.shape, dtype=out.dtype).pin_memory()
+        self.h2d = self.hx.numel() * 2
+        self.d2h = self.hout.numel() * 2
+
+    def step_e2e(self):
+        self.inputs[self.x_id].copy_(self.hx, non_blocking=True)
+        self.plan.run()
+        self.hout.copy_(self.plan.tensor(self.out_id), non_blocking=True)
+        self.torch.cuda.synchronize()
+
+    def cpu_sample(self, lib, threads):
+        return None
+
+
 class RowWorkload(Workload):
     """x[65536x4096] fp32, rows over ranks."""
     R, Cc = 65536, 4096
@@ -569,6 +647,8 @@ def make_workload(name, *a):
         return TinyModelWorkload(*a)
     if name == "gemm_f16":
         return GemmF16Workload(*a)
+    if name == "plan_tiny_model":
+        return PlanTinyModelWorkload(*a)
     if name in ("attention", "attention_causal"):
         return AttentionWorkload(*a, causal=name.endswith("causal"))
     if name in ("attention_f16", "attention_causal_f16"):

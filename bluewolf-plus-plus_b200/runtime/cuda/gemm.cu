@@ -71,11 +71,12 @@ struct GemmCfg {
 
 struct GemmEpi {
   const float *bias;      // [N] or nullptr
-  const float *residual;  // fp32 [M, ldr] added last, or nullptr
+  const void *residual;   // [M, ldr] added last, or nullptr: fp32, or 16-bit per res16
   uint32_t ldr;
   int silu;
   int out_bf16;           // 16-bit output (bf16, or f16 when out_f16)
   int out_f16;
+  int res16;              // residual element type: 0 fp32, 1 bf16, 2 f16
 };
 
 __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m,
@@ -310,8 +311,31 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = bwpp_silu_f(v[j]);
           }
-          if (epi.residual && my_row < M) {
-            const float *rr = epi.residual + (size_t)my_row * epi.ldr + cs;
+          if (epi.residual && my_row < M && epi.res16) {
+            // 16-bit residual (read before this chunk is stored: may alias C)
+            const uint16_t *rr =
+                static_cast<const uint16_t *>(epi.residual) + (size_t)my_row * epi.ldr + cs;
+            const bool f16 = epi.res16 == 2;
+            if (cs + 32 <= N && (epi.ldr & 7) == 0 &&
+                (reinterpret_cast<uintptr_t>(epi.residual) & 15) == 0) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint4 t = *reinterpret_cast<const uint4 *>(rr + 8 * j);
+                const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const uint16_t lo = (uint16_t)(w[e] & 0xFFFFu), hi = (uint16_t)(w[e] >> 16);
+                  v[8 * j + 2 * e] += f16 ? load16<true>(lo) : load16<false>(lo);
+                  v[8 * j + 2 * e + 1] += f16 ? load16<true>(hi) : load16<false>(hi);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (cs + j < N) v[j] += f16 ? load16<true>(rr[j]) : load16<false>(rr[j]);
+            }
+          } else if (epi.residual && my_row < M) {
+            const float *rr = static_cast<const float *>(epi.residual) + (size_t)my_row * epi.ldr + cs;
             if (cs + 32 <= N && (epi.ldr & 3) == 0 &&
                 (reinterpret_cast<uintptr_t>(epi.residual) & 15) == 0) {
 #pragma unroll
@@ -406,7 +430,12 @@ __global__ void gemm_simt_kernel(const uint16_t *__restrict__ a,
   if (row < M && col < N) {
     if (epi.bias) acc += epi.bias[col];
     if (epi.silu) acc = acc / (1.0f + expf(-acc));
-    if (epi.residual) acc += epi.residual[(size_t)row * epi.ldr + col];
+    if (epi.residual) {
+      const size_t ri = (size_t)row * epi.ldr + col;
+      const uint16_t *r16 = static_cast<const uint16_t *>(epi.residual);
+      acc += epi.res16 == 0 ? static_cast<const float *>(epi.residual)[ri]
+             : epi.res16 == 2 ? load16<true>(r16[ri]) : load16<false>(r16[ri]);
+    }
     if (epi.out_bf16) {
       const uint32_t w = epi.out_f16 ? pack2_16<true>(acc, 0.0f) : pack2_16<false>(acc, 0.0f);
       reinterpret_cast<uint16_t *>(c)[(size_t)row * ldc + col] = (uint16_t)(w & 0xFFFFu);
@@ -526,15 +555,16 @@ int launch_tc_any(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb
 // General entry used by the public API and by composite paths (the training
 // step).  a_mn / b_mn select the operand layouts described at the top;
 // ab_f16 = 1 takes f16 A and B (else bf16); out_bf16 = 1 writes 16-bit C,
-// f16 when out_f16 = 1 (else bf16); out_bf16 = 0 writes fp32 C.
+// f16 when out_f16 = 1 (else bf16); out_bf16 = 0 writes fp32 C.  The
+// residual is fp32 (res16 = 0), bf16 (1) or f16 (2); it may alias C.
 int bwpp_gemm_launch_dt(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,
                         const uint16_t *b, int b_mn, uint32_t ldb, void *c,
                         uint32_t ldc, uint32_t M, uint32_t N, uint32_t K,
-                        const float *bias, int silu, const float *residual,
+                        const float *bias, int silu, const void *residual,
                         uint32_t ldr, int out_bf16, int force_simt, int ab_f16,
-                        int out_f16) {
+                        int out_f16, int res16) {
   if (M == 0 || N == 0) return BWPP_CUDA_OK;
-  GemmEpi epi{bias, residual, ldr, silu ? 1 : 0, out_bf16 ? 1 : 0, out_f16 ? 1 : 0};
+  GemmEpi epi{bias, residual, ldr, silu ? 1 : 0, out_bf16 ? 1 : 0, out_f16 ? 1 : 0, res16};
   const uint32_t out_es = out_bf16 ? 2 : 4;
   const bool tc_ok = !force_simt && K > 0 && al16(a) && al16(b) && al16(c) &&
                      (lda % 8) == 0 && (ldb % 8) == 0 && ((ldc * out_es) % 16) == 0 &&
@@ -585,7 +615,7 @@ int bwpp_gemm_launch_ex(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t 
                         const float *bias, int silu, const float *residual,
                         uint32_t ldr, int out_bf16, int force_simt) {
   return bwpp_gemm_launch_dt(ctx, a, a_mn, lda, b, b_mn, ldb, c, ldc, M, N, K, bias, silu,
-                             residual, ldr, out_bf16, force_simt, 0, 0);
+                             residual, ldr, out_bf16, force_simt, 0, 0, 0);
 }
 
 // The reference-shaped matmul: A K-major, B MN-major, fp32 out.

@@ -14,10 +14,11 @@
 //     the graph states, compiler/graph_ir.c:1852-1899 pattern);
 //   * a transpose feeding only matmuls is folded into the GEMM operand layout
 //     (K-major B / MN-major A): no transposed copy;
-//   * matmul -> add(., [N] or reshape of [N]) -> silu fuses into the GEMM
-//     epilogue: bias found by dataflow, so the reshape(bias) form the
-//     reference's fusion pass misses (compiler/graph_ir.c:760-767,
-//     compiler/codegen_metal.c:17-123) fuses too;
+//   * matmul -> add(., [N] or reshape of [N]) -> silu -> add(., R) fuses into
+//     the GEMM epilogue (bias, SiLU, residual): bias found by dataflow, so the
+//     reshape(bias) form the reference's fusion pass misses
+//     (compiler/graph_ir.c:760-767, compiler/codegen_metal.c:17-123) fuses
+//     too;
 //   * everything else is one kernel per node (plan_ops.cu, half_ops.cu,
 //     norms.cu, reduce_max.cu).
 // A fusion is skipped when the memory plan hands one of its inputs' buffers
@@ -42,8 +43,8 @@
 int bwpp_gemm_launch_dt(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,
                         const uint16_t *b, int b_mn, uint32_t ldb, void *c, uint32_t ldc,
                         uint32_t M, uint32_t N, uint32_t K, const float *bias, int silu,
-                        const float *residual, uint32_t ldr, int out_bf16, int force_simt,
-                        int ab_f16, int out_f16);
+                        const void *residual, uint32_t ldr, int out_bf16, int force_simt,
+                        int ab_f16, int out_f16, int res16);
 int bwpp_attention_launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
                           const uint16_t *v, void *o, uint32_t BH, uint32_t Sq, uint32_t Skv,
                           uint32_t Kd, uint32_t Dv, uint64_t q_bh, uint64_t k_bh, uint64_t v_bh,
@@ -448,6 +449,9 @@ struct BwppCudaPlan {
         bool same_batch = true;
         for (size_t i = 0; i + 2 < qd.size(); ++i) same_batch &= qd[i] == kd[i] && kd[i] == vd[i];
         if (!same_batch || qd.back() != kd.back() || kd[kd.size() - 2] != vd[vd.size() - 2]) continue;
+        // head dims the attention kernels take (tcgen05: 64 / 128; CUDA cores:
+        // up to 256); wider heads run unfused (GEMM, softmax, GEMM)
+        if (qd.back() > 256 || vd.back() > 256) continue;
         if (vals[q].dtype != vals[k].dtype || vals[k].dtype != vals[v].dtype) continue;
         const std::vector<int> group = {tp, sp, pp, op_};
         if (!safe_to_defer({q, k, v}, std::min(tp, sp), op_, group)) continue;
@@ -530,6 +534,24 @@ struct BwppCudaPlan {
               last = sp;
               st.silu = 1;
               st.what += " +silu";
+            }
+          }
+          // residual: add(., R) with R of the output's full shape, added last
+          if (vals[cur].uses.size() == 1 && !vals[cur].output) {
+            const int rp = vals[cur].uses[0];
+            Node &R = nodes[rp];
+            if (R.op == "add" && R.in.size() == 2 && !R.fused && R.in[0] != R.in[1]) {
+              const int other = R.in[0] == cur ? R.in[1] : R.in[0];
+              const Val &ov = vals[other];
+              if (ov.numel() == vals[cur].numel() && ov.last() == N && ov.dtype == vals[cur].dtype &&
+                  safe_to_defer({st.a, st.b, st.bias, other}, i, rp, {i, last, rp})) {
+                R.fused = true;
+                vals[cur].live = false;
+                cur = R.out;
+                last = rp;
+                st.c = other;
+                st.what += " +residual";
+              }
             }
           }
           st.out = cur;
@@ -636,8 +658,10 @@ struct BwppCudaPlan {
       // at this node (compiler/mem_plan.c frees inputs before allocating the
       // output).  Row-wise and elementwise kernels run in place; these do
       // not, so their output gets a buffer of its own.
+      // (A GEMM's residual is read before the same elements are stored, so
+      // it may share the output's buffer.)
       if (st.kind == K_GEMM || st.kind == K_ATTN || st.kind == K_TRANSPOSE || st.kind == K_REDUCE) {
-        for (int x : {st.a, st.b, st.c, st.bias})
+        for (int x : {st.a, st.b, st.kind == K_GEMM ? -1 : st.c, st.bias})
           if (x >= 0 && !vals[x].input && vals[x].buffer >= 0 && vals[x].buffer == o.buffer)
             o.buffer = -1;
       }
@@ -772,12 +796,17 @@ struct BwppCudaPlan {
         const size_t osz = out16 ? 2 : 4;
         const int64_t a_b = (A.numel() / (M * K) > 1) ? M * K : 0;
         const int64_t b_b = (B.numel() / (K * N) > 1) ? K * N : 0;
-        for (int64_t i = 0; !rc && i < batch; ++i)
+        const Val *R = st.c >= 0 ? &vals[st.c] : nullptr;
+        const int res16 = !R ? 0 : R->dtype == DT_F16 ? 2 : R->dtype == DT_BF16 ? 1 : 0;
+        for (int64_t i = 0; !rc && i < batch; ++i) {
+          const void *res = R ? (const uint8_t *)R->ptr + (size_t)(i * M * N) * dt_size(R->dtype)
+                              : nullptr;
           rc = bwpp_gemm_launch_dt(c, pa + i * a_b, st.a_t, st.a_t ? (uint32_t)M : (uint32_t)K,
                                    pb + i * b_b, st.b_t ? 0 : 1, st.b_t ? (uint32_t)K : (uint32_t)N,
                                    (uint8_t *)dst + (size_t)(i * M * N) * osz, (uint32_t)N,
-                                   (uint32_t)M, (uint32_t)N, (uint32_t)K, bias, st.silu, nullptr, 0,
-                                   out16, 0, ab_f16, out_f16);
+                                   (uint32_t)M, (uint32_t)N, (uint32_t)K, bias, st.silu, res,
+                                   (uint32_t)N, out16, 0, ab_f16, out_f16, res16);
+        }
         launches += batch;
         if (!rc && conv_after) rc = bwpp_plan_convert(c, DT_F32, DT_BF16, dst, out, o.numel());
         break;
