@@ -270,7 +270,7 @@ class AttentionWorkload(Workload):
     """B=8 H=32 S=4096 d=128, bf16 in, fp32 out; heads over ranks."""
     B, H, S, D = 8, 32, 4096, 128
     kernel = "attention"
-    profile = "attention_config4"
+    profile = "attention_tc_kernel_config4"
 
     def __init__(self, *a, causal=False):
         super().__init__(*a)
@@ -347,7 +347,7 @@ class AttentionWorkload(Workload):
 class AttentionF16Workload(AttentionWorkload):
     """configs[3] shapes through the half ABI (bwpp_cuda_attention_f16)."""
     dtype = "f16"
-    profile = "attention_f16_config4"
+    profile = "attention_tc_kernel_f16_config4"
     e2e_api = "bwpp_cuda_attention_f16; pinned host f16 Q, K, V copied in and O copied out every step"
 
     def setup(self):
@@ -467,11 +467,20 @@ class RowWorkload(Workload):
     bound = "hbm"
     dtype = "f32"
 
+    KERNELS = {"rmsnorm_fwd": "norm_fwd_kernel", "layernorm_fwd": "norm_fwd_kernel",
+               "rmsnorm_bwd": "norm_bwd_kernel", "layernorm_bwd": "norm_bwd_kernel",
+               "reduce_max_fwd": "argmax_kernel", "reduce_max_bwd": "argmax_bwd_kernel",
+               "softmax_fwd": "softmax_rows_kernel", "softmax_grad": "softmax_grad_kernel",
+               "silu_grad": "silu_grad_kernel", "reduce_sum_rows": "row_sum_kernel",
+               "reduce_sum_cols": "col_partial_kernel", "broadcast_rows": "broadcast_kernel"}
+
     def __init__(self, *a, op="rmsnorm_fwd"):
         super().__init__(*a)
+        if op not in self.KERNELS:
+            raise SystemExit(f"unknown workload {op}")
         self.op = op
-        self.kernel = op
-        self.profile = f"{op}_config3"
+        self.kernel = self.KERNELS[op]
+        self.profile = f"{self.kernel}_{op}_config3"
 
     def setup(self):
         t = self.torch
@@ -581,7 +590,7 @@ class TinyModelWorkload(Workload):
     backward + NCCL gradient allreduce + SGD, data-parallel (weak scaling)."""
     L, D, H, F, B, S = 2, 2048, 16, 5632, 16, 2048
     kernel = "tiny_model step"
-    profile = "tiny_model_config5"
+    profile = "tiny_model_step_config5"
     scaling = "weak"
     e2e_api = "bwpp_cuda_tiny_model_step with pinned host x / target, loss read back to host"
 

@@ -88,8 +88,8 @@ __device__ __forceinline__ float warp_block_reduce(float v, float *sv, bool is_m
 // Row softmax (max by strict '>', e = expf(x - max), inv = sum > 0 ? 1/sum
 // : 0) with the row in registers; rows wider than MAXV vectors per thread
 // take MAXV = 0, which streams the row three times.
-template <int MAXV, bool V4>
-__global__ void __launch_bounds__(kThreads)
+template <int MAXV, bool V4, int NT = kThreads>
+__global__ void __launch_bounds__(NT)
     softmax_f16_kernel(const uint16_t *__restrict__ x, uint16_t *__restrict__ y, uint32_t rows,
                        uint32_t cols, uint32_t ld) {
   using V = H<V4>;
@@ -101,16 +101,16 @@ __global__ void __launch_bounds__(kThreads)
     uint16_t *yr = y + (size_t)r * ld;
     if (MAXV == 0) {
       float m = -INFINITY;
-      for (uint32_t c = threadIdx.x; c < cols; c += kThreads) {
+      for (uint32_t c = threadIdx.x; c < cols; c += NT) {
         const float t = load16<true>(xr[c]);
         if (t > m) m = t;
       }
       m = warp_block_reduce(m, sv, true);
       float s = 0.0f;
-      for (uint32_t c = threadIdx.x; c < cols; c += kThreads) s += expf(load16<true>(xr[c]) - m);
+      for (uint32_t c = threadIdx.x; c < cols; c += NT) s += expf(load16<true>(xr[c]) - m);
       s = warp_block_reduce(s, sv, false);
       const float inv = s > 0.0f ? 1.0f / s : 0.0f;
-      for (uint32_t c = threadIdx.x; c < cols; c += kThreads)
+      for (uint32_t c = threadIdx.x; c < cols; c += NT)
         yr[c] = (uint16_t)(pack2_16<true>(expf(load16<true>(xr[c]) - m) * inv, 0.0f) & 0xFFFFu);
       continue;
     }
@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(kThreads)
     float m = -INFINITY;
 #pragma unroll
     for (int i = 0; i < MV; ++i) {
-      const uint32_t idx = threadIdx.x + i * kThreads;
+      const uint32_t idx = threadIdx.x + i * NT;
       if (idx < nv) V::load(xr, idx, xv[i]);
 #pragma unroll
       for (int w = 0; w < W; ++w)
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kThreads)
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < MV; ++i) {
-      const uint32_t idx = threadIdx.x + i * kThreads;
+      const uint32_t idx = threadIdx.x + i * NT;
       if (idx < nv)
 #pragma unroll
         for (int w = 0; w < W; ++w) {
@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(kThreads)
     const float inv = s > 0.0f ? 1.0f / s : 0.0f;
 #pragma unroll
     for (int i = 0; i < MV; ++i) {
-      const uint32_t idx = threadIdx.x + i * kThreads;
+      const uint32_t idx = threadIdx.x + i * NT;
       if (idx < nv) {
 #pragma unroll
         for (int w = 0; w < W; ++w) xv[i][w] *= inv;
@@ -153,8 +153,8 @@ __global__ void __launch_bounds__(kThreads)
 
 // y = x * rsqrt(mean(x^2) + eps) * gamma + beta (gamma / beta NULL: 1 / 0),
 // f16 in and out, fp32 arithmetic; MAXV = 0 streams the row twice.
-template <int MAXV, bool V4>
-__global__ void __launch_bounds__(kThreads)
+template <int MAXV, bool V4, int NT = kThreads>
+__global__ void __launch_bounds__(NT)
     rmsnorm_f16_kernel(const uint16_t *__restrict__ x, uint16_t *__restrict__ y,
                        const uint16_t *__restrict__ gamma, const uint16_t *__restrict__ beta,
                        uint32_t rows, uint32_t cols, uint32_t ld, float eps) {
@@ -172,13 +172,13 @@ __global__ void __launch_bounds__(kThreads)
     uint16_t *yr = y + (size_t)r * ld;
     if (MAXV == 0) {
       float ss = 0.0f;
-      for (uint32_t c = threadIdx.x; c < cols; c += kThreads) {
+      for (uint32_t c = threadIdx.x; c < cols; c += NT) {
         const float t = load16<true>(xr[c]);
         ss = fmaf(t, t, ss);
       }
       ss = warp_block_reduce(ss, sv, false);
       const float inv = rsqrtf(ss / (float)cols + eps);
-      for (uint32_t c = threadIdx.x; c < cols; c += kThreads)
+      for (uint32_t c = threadIdx.x; c < cols; c += NT)
         yr[c] = (uint16_t)(pack2_16<true>(affine(load16<true>(xr[c]) * inv, c), 0.0f) & 0xFFFFu);
       continue;
     }
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kThreads)
     float ss = 0.0f;
 #pragma unroll
     for (int i = 0; i < MV; ++i) {
-      const uint32_t idx = threadIdx.x + i * kThreads;
+      const uint32_t idx = threadIdx.x + i * NT;
       if (idx < nv) {
         V::load(xr, idx, xv[i]);
 #pragma unroll
@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(kThreads)
     const float inv = rsqrtf(ss / (float)cols + eps);
 #pragma unroll
     for (int i = 0; i < MV; ++i) {
-      const uint32_t idx = threadIdx.x + i * kThreads;
+      const uint32_t idx = threadIdx.x + i * NT;
       if (idx < nv) {
 #pragma unroll
         for (int w = 0; w < W; ++w) xv[i][w] = affine(xv[i][w] * inv, idx * W + w);
@@ -233,18 +233,23 @@ uint32_t grid_flat(BwppCudaCtx *ctx, size_t n) {
   return (uint32_t)(blocks < cap ? (blocks ? blocks : 1) : cap);
 }
 
-// Picks MAXV (0 = streaming) for a row of nv vectors: up to 16 vectors of 4
-// halves per thread (rows of 16 K halves held in registers); wider rows
-// stream (measured faster than holding 32 vectors at one CTA per SM).
+// Picks the block size NT and MAXV (0 = streaming) for a row of nv vectors:
+// up to 16 vectors of 4 halves per thread at 256 threads (rows of 16 K
+// halves), then 8 per thread at 1024 threads (rows of 32 K halves held in
+// registers at 64 registers a thread, two CTAs per SM; 16 per thread would
+// spill under that cap); wider rows stream.
 template <typename F>
 void by_width(uint32_t nv, F &&f) {
   const uint32_t per = (nv + kThreads - 1) / kThreads;
-  if (per <= 1) f(std::integral_constant<int, 1>{});
-  else if (per <= 2) f(std::integral_constant<int, 2>{});
-  else if (per <= 4) f(std::integral_constant<int, 4>{});
-  else if (per <= 8) f(std::integral_constant<int, 8>{});
-  else if (per <= 16) f(std::integral_constant<int, 16>{});
-  else f(std::integral_constant<int, 0>{});
+  using I = std::integral_constant<int, 256>;
+  using W = std::integral_constant<int, 1024>;
+  if (per <= 1) f(std::integral_constant<int, 1>{}, I{});
+  else if (per <= 2) f(std::integral_constant<int, 2>{}, I{});
+  else if (per <= 4) f(std::integral_constant<int, 4>{}, I{});
+  else if (per <= 8) f(std::integral_constant<int, 8>{}, I{});
+  else if (per <= 16) f(std::integral_constant<int, 16>{}, I{});
+  else if (nv <= 1024 * 8) f(std::integral_constant<int, 8>{}, W{});
+  else f(std::integral_constant<int, 0>{}, I{});
 }
 
 bool has_tag(const char *src, const char *tag) {
@@ -307,10 +312,10 @@ int bwpp_cuda_softmax_f16(BwppCudaCtx *ctx, const uint16_t *x, uint16_t *y, uint
   const bool v4 = cols % 4 == 0 && ld % 4 == 0 && al8(x) && al8(y);
   const uint32_t grid = grid_rows(ctx, rows);
   cudaStream_t s = ctx->stream;
-  by_width(v4 ? cols / 4 : cols, [&](auto mv) {
-    constexpr int MV = decltype(mv)::value;
-    if (v4) softmax_f16_kernel<MV, true><<<grid, kThreads, 0, s>>>(x, y, rows, cols, ld);
-    else softmax_f16_kernel<MV, false><<<grid, kThreads, 0, s>>>(x, y, rows, cols, ld);
+  by_width(v4 ? cols / 4 : cols, [&](auto mv, auto nt) {
+    constexpr int MV = decltype(mv)::value, NT = decltype(nt)::value;
+    if (v4) softmax_f16_kernel<MV, true, NT><<<grid, NT, 0, s>>>(x, y, rows, cols, ld);
+    else softmax_f16_kernel<MV, false, NT><<<grid, NT, 0, s>>>(x, y, rows, cols, ld);
   });
   BWPP_LAUNCH_CHECK(ctx, "softmax f16");
   return BWPP_CUDA_OK;
@@ -327,12 +332,12 @@ int bwpp_cuda_rmsnorm_f16(BwppCudaCtx *ctx, const uint16_t *x, uint16_t *y,
   const bool v4 = cols % 4 == 0 && ld % 4 == 0 && al8(x) && al8(y);
   const uint32_t grid = grid_rows(ctx, rows);
   cudaStream_t s = ctx->stream;
-  by_width(v4 ? cols / 4 : cols, [&](auto mv) {
-    constexpr int MV = decltype(mv)::value;
+  by_width(v4 ? cols / 4 : cols, [&](auto mv, auto nt) {
+    constexpr int MV = decltype(mv)::value, NT = decltype(nt)::value;
     if (v4)
-      rmsnorm_f16_kernel<MV, true><<<grid, kThreads, 0, s>>>(x, y, gamma, beta, rows, cols, ld, eps);
+      rmsnorm_f16_kernel<MV, true, NT><<<grid, NT, 0, s>>>(x, y, gamma, beta, rows, cols, ld, eps);
     else
-      rmsnorm_f16_kernel<MV, false><<<grid, kThreads, 0, s>>>(x, y, gamma, beta, rows, cols, ld, eps);
+      rmsnorm_f16_kernel<MV, false, NT><<<grid, NT, 0, s>>>(x, y, gamma, beta, rows, cols, ld, eps);
   });
   BWPP_LAUNCH_CHECK(ctx, "rmsnorm f16");
   return BWPP_CUDA_OK;

@@ -90,7 +90,11 @@ def test_attention_f16(ctx, B, H, S, D, causal):
     assert err <= TOL_MM and err <= 5e-3, err
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (7, 33), (64, 4096), (5, 4100), (3, 9000)])
+WIDE = [(1, 1), (3, 5), (7, 33), (64, 4096), (5, 4100), (3, 9000), (5, 32000), (2, 30001),
+        (3, 40000)]
+
+
+@pytest.mark.parametrize("rows,cols", WIDE)
 def test_softmax_f16(ctx, rows, cols):
     rng = np.random.default_rng(rows + cols)
     x = half(rng, rows, cols, scale=3.0)
@@ -100,7 +104,7 @@ def test_softmax_f16(ctx, rows, cols):
     assert rel_fro(h(y), O.softmax(x.astype(np.float32))) <= TOL_ROW
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (7, 33), (64, 4096), (5, 4100), (3, 9000)])
+@pytest.mark.parametrize("rows,cols", WIDE)
 @pytest.mark.parametrize("affine", [0, 1])
 def test_rmsnorm_f16(ctx, rows, cols, affine):
     rng = np.random.default_rng(rows * 3 + cols + affine)
