@@ -6,13 +6,15 @@
 //   h  = h + a W2
 // then loss = mean((h - target)^2).  Forward, backward (autodiff rules of
 // compiler/graph_ir.c:1529-1583 matmul, 1709-1720 silu, 1735-1789 rmsnorm,
-// plus the attention backward), optional NCCL allreduce of the gradients,
+// plus the attention backward), optional NCCL allreduce of the gradients
+// (one bucket per layer, on a side stream, overlapped with the backward of
+// the layers below),
 // and an SGD update of the fp32 master weights with bf16 compute copies.
 //
 // Every product runs on the tcgen05 GEMM / attention kernels; the transposed
 // products of the backward use the GEMM's MN-major / K-major operand forms,
 // so nothing is transposed in memory.  Parameters and gradients are single
-// flat fp32 buffers (one allreduce).
+// flat fp32 buffers (one allreduce bucket per layer).
 #include <stdlib.h>
 #include <string.h>
 
@@ -85,6 +87,9 @@ struct BwppCudaTinyModel {
   float *part, *loss;
   float *norm_scratch;
   void *arena;       // one cudaMalloc for everything above
+  // gradient allreduce overlapped with the backward: one bucket per layer
+  cudaStream_t comm_stream;
+  cudaEvent_t grad_ready[16], bucket_done[16];
 };
 
 namespace {
@@ -193,7 +198,22 @@ int bwpp_cuda_tiny_model_create(BwppCudaCtx *ctx, const BwppCudaTinyModelConfig 
   if (!rc) rc = bwpp_sgd(ctx, m->params, m->grads, m->params16, off, 0.0f);  // bf16 copies
   if (!rc)
     rc = bwpp_check_cuda(ctx, cudaMemsetAsync(m->grads, 0, off * 4, ctx->stream), "grads");
+  if (!rc)
+    rc = bwpp_check_cuda(ctx, cudaStreamCreateWithFlags(&m->comm_stream, cudaStreamNonBlocking),
+                         "comm stream");
+  for (uint32_t l = 0; l < c.layers && !rc; ++l) {
+    rc = bwpp_check_cuda(ctx, cudaEventCreateWithFlags(&m->grad_ready[l], cudaEventDisableTiming),
+                         "grad event");
+    if (!rc)
+      rc = bwpp_check_cuda(ctx, cudaEventCreateWithFlags(&m->bucket_done[l], cudaEventDisableTiming),
+                           "bucket event");
+  }
   if (rc) {
+    for (uint32_t l = 0; l < c.layers; ++l) {
+      if (m->grad_ready[l]) cudaEventDestroy(m->grad_ready[l]);
+      if (m->bucket_done[l]) cudaEventDestroy(m->bucket_done[l]);
+    }
+    if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
     cudaFree(m->arena);
     free(m);
     return rc;
@@ -206,6 +226,12 @@ int bwpp_cuda_tiny_model_destroy(BwppCudaTinyModel *m) {
   if (!m) return BWPP_CUDA_ERR_ARG;
   bwpp_ctx_enter(m->ctx);
   cudaStreamSynchronize(m->ctx->stream);
+  cudaStreamSynchronize(m->comm_stream);
+  for (uint32_t l = 0; l < m->cfg.layers; ++l) {
+    cudaEventDestroy(m->grad_ready[l]);
+    cudaEventDestroy(m->bucket_done[l]);
+  }
+  cudaStreamDestroy(m->comm_stream);
   cudaFree(m->arena);
   free(m);
   return BWPP_CUDA_OK;
@@ -320,12 +346,28 @@ int bwpp_cuda_tiny_model_step(BwppCudaTinyModel *m, const float *x, const float 
                             3 * D, nullptr, 0, nullptr, 0, 0, 0));  // dn1 = dqkv Wqkv^T
     TRY(bwpp_norm_bwd_with_scratch(ctx, 0, a.h_in, P + p.g1, m->dtmp, m->dtmp, G + p.g1,
                                    nullptr, T, D, D, c.eps, m->norm_scratch));
+    // layer l's gradients are final: sum them over the ranks on the comm
+    // stream while the backward of layer l-1 runs (every rank issues the
+    // buckets in the same order, layers L-1 .. 0)
+    if (comm) {
+      const size_t begin = p.g1, count = p.w2 + (size_t)F * D - p.g1;
+      TRY(bwpp_check_cuda(ctx, cudaEventRecord(m->grad_ready[l], ctx->stream), "grad event"));
+      TRY(bwpp_check_cuda(ctx, cudaStreamWaitEvent(m->comm_stream, m->grad_ready[l], 0),
+                          "comm wait"));
+      TRY(bwpp_cuda_comm_allreduce_sum_f32(comm, G + begin, count, m->comm_stream));
+      TRY(bwpp_check_cuda(ctx, cudaEventRecord(m->bucket_done[l], m->comm_stream),
+                          "bucket event"));
+    }
     TRY(bwpp_add(ctx, m->dh, m->dtmp, (size_t)T * D));
     if (l > 0) TRY(bwpp_cast_launch(ctx, m->dh, m->dh16, T, D, D, D));
   }
-  // ---------------- data-parallel gradient sum, SGD on the mean gradient
+  // ---------------- data-parallel gradient sum (overlapped above), SGD on
+  // the mean gradient once every bucket has been summed
   const int nr = comm ? bwpp_comm_nranks(comm) : 1;
-  if (comm) TRY(bwpp_cuda_comm_allreduce_sum_f32(comm, G, m->nparams, ctx->stream));
+  if (comm)
+    for (uint32_t l = 0; l < c.layers; ++l)
+      TRY(bwpp_check_cuda(ctx, cudaStreamWaitEvent(ctx->stream, m->bucket_done[l], 0),
+                          "bucket wait"));
   if (lr != 0.0f) TRY(bwpp_sgd(ctx, P, G, P16, m->nparams, lr / (float)nr));
   if (loss_out)
     TRY(bwpp_check_cuda(ctx, cudaMemcpyAsync(loss_out, m->loss, 4, cudaMemcpyDefault, ctx->stream),
