@@ -79,6 +79,16 @@ struct GemmEpi {
   int res16;              // residual element type: 0 fp32, 1 bf16, 2 f16
 };
 
+// Work items of a launch, in rasterised tile order: items below split_begin
+// are whole tiles; from split_begin on, each remaining tile is cut into two
+// N halves (MMA N = BN / 2), so a short last wave spreads over twice as many
+// CTAs.  Item i >= split_begin is half (i - split_begin) % 2 of tile
+// split_begin + (i - split_begin) / 2.
+struct GemmWork {
+  uint32_t split_begin;
+  uint32_t items;
+};
+
 __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m,
                                             uint32_t tiles_n, uint32_t &mb,
                                             uint32_t &nb) {
@@ -96,7 +106,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmEpi epi,
-                   uint32_t M, uint32_t N, uint32_t K, uint32_t ab_f16, int *status) {
+                   uint32_t M, uint32_t N, uint32_t K, uint32_t ab_f16, const GemmWork work,
+                   int *status) {
   using Cfg = GemmCfg<PAIR>;
   constexpr int STAGES = Cfg::STAGES;
   // A and B both bf16, or both f16 (the half ABI)
@@ -119,8 +130,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t first_tile = PAIR ? cluster_id_x() : blockIdx.x;
   const uint32_t tile_step = PAIR ? cluster_count_x() : gridDim.x;
   const uint32_t tiles_m = (M + Cfg::TILE_M - 1) / Cfg::TILE_M, tiles_n = (N + BN - 1) / BN;
-  const uint32_t num_tiles = tiles_m * tiles_n;
   const uint32_t num_kb = (K + BK - 1) / BK;
+  // tile of work item `it`, the first accumulator column it owns and its width
+  auto item = [&](uint32_t it, uint32_t &mb, uint32_t &nb, uint32_t &n_off, uint32_t &wn) {
+    uint32_t t = it, half = 0;
+    wn = BN;
+    if (it >= work.split_begin) {
+      t = work.split_begin + (it - work.split_begin) / 2;
+      half = (it - work.split_begin) & 1;
+      wn = BN / 2;
+    }
+    tile_coords(t, tiles_m, tiles_n, mb, nb);
+    n_off = half * (BN / 2);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -156,11 +178,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
-      for (uint32_t t = first_tile; t < num_tiles && !*abort_flag; t += tile_step) {
-        uint32_t mb, nb;
-        tile_coords(t, tiles_m, tiles_n, mb, nb);
+      for (uint32_t it = first_tile; it < work.items && !*abort_flag; it += tile_step) {
+        uint32_t mb, nb, n_off, wn;
+        item(it, mb, nb, n_off, wn);
+        // A half tile loads the same boxes (the unused columns past its half
+        // are fetched and ignored), shifted to its N range; in a pair each
+        // CTA holds wn / 2 of the MMA's columns.
         const int32_t row0 = (int32_t)(mb * Cfg::TILE_M + rank * BM);
-        const int32_t col0 = (int32_t)(nb * BN + rank * Cfg::BN_LOAD);
+        const int32_t col0 = (int32_t)(nb * BN + n_off + rank * (PAIR ? wn / 2 : 0));
         for (uint32_t kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, status)) {
             *abort_flag = 1;
@@ -212,13 +237,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       };
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
-      for (uint32_t t = first_tile; t < num_tiles && !*abort_flag; t += tile_step) {
+      for (uint32_t it = first_tile; it < work.items && !*abort_flag; it += tile_step) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, status)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        uint32_t mb, nb, n_off, wn;
+        item(it, mb, nb, n_off, wn);
+        const uint32_t idesc = wn == BN ? IDESC
+            : make_idesc_f32acc(Cfg::TILE_M, BN / 2, A_MN ? 1u : 0u, B_MN ? 1u : 0u, ab_f16);
         bool ok = true;
         for (uint32_t kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, status)) {
@@ -239,8 +268,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                                      : make_smem_desc(a0 + ks * 32, 16, 1024, BWPP_SWIZZLE_128B);
             const uint64_t bd = B_MN ? make_smem_desc(b0 + ks * 2048, B_SUB, 1024, BWPP_SWIZZLE_128B)
                                      : make_smem_desc(b0 + ks * 32, 16, 1024, BWPP_SWIZZLE_128B);
-            if constexpr (PAIR) tc_mma_f16_ss_pair(d_tmem, ad, bd, IDESC, (kb | ks) != 0 ? 1u : 0u);
-            else tc_mma_f16_ss(d_tmem, ad, bd, IDESC, (kb | ks) != 0 ? 1u : 0u);
+            const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
+            if constexpr (PAIR) tc_mma_f16_ss_pair(d_tmem, ad, bd, idesc, accum);
+            else tc_mma_f16_ss(d_tmem, ad, bd, idesc, accum);
           }
           commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -263,9 +293,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int ew = warp - 2;
     uint8_t *stage_c = smem + Cfg::OFF_C + ew * 2 * EPI_BUF;
     uint32_t acc = 0, acc_phase = 0, buf = 0;
-    for (uint32_t t = first_tile; t < num_tiles && !*abort_flag; t += tile_step) {
-      uint32_t mb, nb;
-      tile_coords(t, tiles_m, tiles_n, mb, nb);
+    const int out16 = epi.out_bf16;
+    for (uint32_t it = first_tile; it < work.items && !*abort_flag; it += tile_step) {
+      uint32_t mb, nb, n_off, wn;
+      item(it, mb, nb, n_off, wn);
       if (!mbar_wait(&tfull[acc], acc_phase, status)) {
         *abort_flag = 1;
         break;
@@ -275,17 +306,17 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t my_row = row0 + lane;
       // fp32 out: 32-column chunks; bf16 out: 64-column chunks (two TMEM
       // loads).  Either way a chunk is 32 rows x 128 bytes in smem.
-      const int cw = epi.out_bf16 ? 64 : 32;
-      for (int c = 0; c < BN / cw; ++c) {
-        const uint32_t col0 = nb * BN + c * cw;
+      const int cw = out16 ? 64 : 32;
+      for (int c = 0; c < (int)wn / cw; ++c) {
+        const uint32_t col0 = nb * BN + n_off + c * cw;
         if (col0 >= N) break;  // warp-uniform
         uint32_t outw[32];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          if (h == 1 && !epi.out_bf16) break;
+          if (h == 1 && !out16) break;
           const uint32_t cs = col0 + h * 32;  // first column of this 32-wide part
           uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + (cs - nb * BN), r);
+          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + (cs - nb * BN - n_off), r);
           tc_wait_ld(r);
           float v[32];
 #pragma unroll
@@ -352,7 +383,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (cs + j < N) v[j] += rr[j];
             }
           }
-          if (epi.out_bf16) {
+          if (out16) {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
               outw[h * 16 + j] = epi.out_f16 ? pack2_16<true>(v[2 * j], v[2 * j + 1])
@@ -482,6 +513,13 @@ bool pairs_enabled() {
 // Launches the tensor-core kernel.  Returns BWPP_CUDA_ERR_UNSUPPORTED (with
 // nothing launched) when a CTA pair cannot be made resident, so the caller
 // can take the single-CTA kernel.
+//
+// Wave tail: with `cap` tiles in flight (CTA pairs, or SMs) the last wave
+// holds tiles % cap tiles.  When that tail fits twice into one wave, its
+// tiles run as two N halves each, in the same launch (a GEMM of fewer tiles
+// than half the CTAs runs entirely in halves).  (At 8 GPUs the
+// 8192 x 4096 x 11008 GEMM leaves 1024 rows per GPU: 172 pair tiles, 2.3
+// waves; the 24-tile tail becomes 48 half tiles.)
 template <bool A_MN, bool B_MN, bool PAIR>
 int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
               const CUtensorMap &tcm, const GemmEpi &epi, uint32_t M, uint32_t N,
@@ -500,25 +538,20 @@ int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
     g_attr_set[v + (PAIR ? 4 : 0)][dev] = true;
   }
   const uint32_t tiles = ((M + Cfg::TILE_M - 1) / Cfg::TILE_M) * ((N + BN - 1) / BN);
-  if constexpr (!PAIR) {
-    const uint32_t grid = tiles < (uint32_t)ctx->num_sms ? tiles : (uint32_t)ctx->num_sms;
-    kern<<<grid, THREADS, Cfg::SMEM_ALLOC, ctx->stream>>>(ta, tb, tcm, epi, M, N, K, ab_f16,
-                                                          ctx->status_word);
-    BWPP_LAUNCH_CHECK(ctx, "gemm tcgen05");
-    return BWPP_CUDA_OK;
-  } else {
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(ctx->num_sms & ~1), 1, 1);
-    cfg.blockDim = dim3(THREADS, 1, 1);
-    cfg.dynamicSmemBytes = Cfg::SMEM_ALLOC;
-    cfg.stream = ctx->stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = PAIR ? 2 : 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(ctx->num_sms & ~1), 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_ALLOC;
+  cfg.stream = ctx->stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = PAIR ? 1 : 0;
+  uint32_t cap = (uint32_t)ctx->num_sms;
+  if constexpr (PAIR) {
     int &pairs = g_pair_clusters[v][dev];
     if (pairs == 0) {
       int n = 0;
@@ -530,13 +563,17 @@ int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
       }
     }
     if (pairs < 0) return BWPP_CUDA_ERR_UNSUPPORTED;
-    const uint32_t clusters = tiles < (uint32_t)pairs ? tiles : (uint32_t)pairs;
-    cfg.gridDim = dim3(2 * clusters, 1, 1);
-    int *status = ctx->status_word;
-    return bwpp_check_cuda(ctx,
-                           cudaLaunchKernelEx(&cfg, kern, ta, tb, tcm, epi, M, N, K, ab_f16, status),
-                           "gemm tcgen05 pair");
+    cap = (uint32_t)pairs;
   }
+  const uint32_t full = tiles / cap, tail = tiles % cap;
+  const bool halve = tail > 0 && tail * 2 <= cap;
+  const GemmWork w{halve ? full * cap : tiles, halve ? full * cap + 2 * tail : tiles};
+  const uint32_t n = w.items < cap ? w.items : cap;
+  cfg.gridDim = dim3((PAIR ? 2 : 1) * n, 1, 1);
+  int *status = ctx->status_word;
+  return bwpp_check_cuda(
+      ctx, cudaLaunchKernelEx(&cfg, kern, ta, tb, tcm, epi, M, N, K, ab_f16, w, status),
+      PAIR ? "gemm tcgen05 pair" : "gemm tcgen05");
 }
 
 template <bool A_MN, bool B_MN>

@@ -236,3 +236,53 @@ def test_single_cta_kernel_with_pairs_disabled(ctx):
     assert out.returncode == 0, out.stderr[-2000:]
     worst = float(out.stdout.split("WORST")[-1])
     assert worst <= TIGHT, worst
+
+
+def test_wave_tail_in_half_tiles(ctx):
+    """The 8-GPU share of configs[1] (1024 x 4096 x 11008: 172 CTA-pair tiles,
+    2.3 waves) runs its last 24 tiles as 48 N-half tiles (MMA N = 128) in the
+    same launch.  Sampled rows from both the full waves and the halved tail
+    against the oracle."""
+    M, K, N = 1024, 4096, 11008
+    g = torch.Generator(device="cuda").manual_seed(77)
+    x = (torch.randn(M, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    w = (torch.randn(K, N, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    b = torch.rand(N, device="cuda", generator=g) * 0.2 - 0.1
+    c = torch.empty(M, N, device="cuda")
+    ctx.matmul_bf16(x, w, c, M, N, K, K, N, N, b, 1, 1)
+    ctx.sync()
+    rows = np.unique(np.concatenate([[0, 255, 256, 511, 512, 767, 768, 1023],
+                                     np.random.default_rng(3).integers(0, M, 40)]))
+    ref = O.matmul(np.ascontiguousarray(x[rows].float().cpu().numpy()),
+                   np.ascontiguousarray(w.float().cpu().numpy()), b.cpu().numpy(), 1, 1)
+    assert rel_fro(c[rows].cpu().numpy(), ref) <= TIGHT
+    # deterministic across calls
+    c2 = torch.empty_like(c)
+    ctx.matmul_bf16(x, w, c2, M, N, K, K, N, N, b, 1, 1)
+    ctx.sync()
+    assert torch.equal(c, c2)
+
+
+@pytest.mark.parametrize("out_bf16", [0, 1])
+def test_half_tiles_with_residual_and_16bit_out(ctx, out_bf16):
+    # 2 x 4 tiles of 256 x 256, fewer than half the CTA pairs: every tile runs
+    # as two N halves
+    M, N, K = 512, 1024, 1024
+    rng = np.random.default_rng(8 + out_bf16)
+    a16 = O.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    b16 = O.f32_to_bf16(rng.standard_normal((K, N)).astype(np.float32))
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, N).astype(np.float32)
+    ref = O.matmul(O.bf16_to_f32(a16), O.bf16_to_f32(b16), bias, 1, 1) + res
+    if out_bf16:
+        c = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        ctx.gemm_ex(dev(a16), dev(b16), c, M, N, K, K, N, N, out_bf16=1, silu=1, bias=dev(bias),
+                    residual=dev(res), ldr=N)
+        ctx.sync()
+        assert rel_fro(c.float().cpu().numpy(), ref) <= 5e-3
+    else:
+        cd = dev(res)  # residual aliases C: C = silu(A B + bias) + C
+        ctx.gemm_ex(dev(a16), dev(b16), cd, M, N, K, K, N, N, silu=1, bias=dev(bias), residual=cd,
+                    ldr=N)
+        ctx.sync()
+        assert rel_fro(host(cd), ref) <= TIGHT
