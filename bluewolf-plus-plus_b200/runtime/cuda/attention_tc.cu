@@ -35,7 +35,7 @@ constexpr int THREADS = 320;
 // Of every 8 score pairs, this many take exp2 on the FMA pipe (exp2_fma2),
 // the rest on MUFU: one ex2 per score would keep MUFU as busy as the tensor
 // core, so part of the load moves to the otherwise idle FMA pipe.
-constexpr int kEmuPairsPer8 = 0;
+constexpr int kEmuPairsPer8 = 2;
 
 template <int D, bool F16 = false>
 struct Cfg {
@@ -45,7 +45,7 @@ struct Cfg {
   static constexpr int OFF_K = 2 * TILE;    // 2 stages
   static constexpr int OFF_V = 4 * TILE;    // 2 stages
   static constexpr int OFF_BAR = 6 * TILE;
-  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int SMEM = OFF_BAR + 512 + 1024;
   static constexpr uint32_t TMEM_S = 0;        // S_A at 0, S_B at 128
   static constexpr uint32_t TMEM_O = 2 * BN;   // O_A at 256, O_B at 256 + D
   static constexpr uint32_t TMEM_COLS = 512;
@@ -56,15 +56,49 @@ struct Cfg {
 };
 
 struct Bars {
-  uint64_t q_full;
+  uint64_t q_full[2], q_empty[2];
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
-  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2];
+  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], o_free[2];
+  uint64_t sched_full[2], sched_empty[2];
   uint64_t drain;
+  int item[2];
   uint32_t tmem;
   int abort_flag;
 };
+static_assert(sizeof(Bars) <= 512, "barrier block");
 
+// Work item w (in the order CTAs take them): head bh = w / pairs, query
+// pair pairs - 1 - w % pairs of that head (the heaviest causal pair first),
+// i.e. rows q0 .. q0 + 255 as tiles A and B.
+struct Item {
+  uint32_t bh, q0;
+  int nblk[2], n;
+};
+
+__device__ __forceinline__ Item decode_item(int w, uint32_t pairs, uint32_t Sq, uint32_t Skv,
+                                            int causal) {
+  Item it;
+  it.bh = (uint32_t)w / pairs;
+  it.q0 = (pairs - 1 - (uint32_t)w % pairs) * 2 * BM;
+  it.nblk[0] = blocks_for(it.q0, Sq, Skv, causal);
+  it.nblk[1] = blocks_for(it.q0 + BM, Sq, Skv, causal);
+  it.n = max(it.nblk[0], it.nblk[1]);
+  return it;
+}
+
+// Persistent: one CTA per SM takes work items (256 query rows of one head)
+// until none is left: its first item is blockIdx.x, the next ones come from
+// the context's work counter (items gridDim.x, gridDim.x + 1, ... in
+// head-major order, so the CTAs running together share a few heads' K / V in
+// L2, and a CTA that drew a short causal item simply draws again).  The
+// producer publishes each item id through a two-slot ring (sched_full /
+// sched_empty); every role walks the same item sequence.  Across items the
+// K / V ring keeps streaming, the next item's Q is loaded as soon as the
+// last S MMAs of the current item release Q (q_empty), and the next item's
+// S MMAs run while the softmax warps are still in the previous epilogue; its
+// first PV waits for that epilogue to read O (o_free).  All barrier phases
+// are running counters over the CTA's whole item sequence.
 template <int D, bool F16>
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -72,39 +106,31 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const __grid_constant__ CUtensorMap tmV,
                         const AttnIO io, uint32_t BH, uint32_t Sq,
                         uint32_t Skv, float scale_log2, int causal,
-                        uint32_t pairs, int *status) {
+                        uint32_t pairs, int *sched, int *status) {
   using C = Cfg<D, F16>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
   Bars *bar = reinterpret_cast<Bars *>(smem + C::OFF_BAR);
   volatile int *abort_flag = &bar->abort_flag;
-
-  // Head-major order: the CTAs of one (b,h) run together and share its K / V
-  // through L2.  Within a head the heaviest (latest) query blocks go first,
-  // which evens out the causal tail.
-  const uint32_t lin = blockIdx.x;
-  const uint32_t bh = lin / pairs;
-  const uint32_t pair = pairs - 1 - lin % pairs;
-  const uint32_t q0 = pair * 2 * BM;
-  const int nblk[2] = {blocks_for(q0, Sq, Skv, causal),
-                       blocks_for(q0 + BM, Sq, Skv, causal)};
-  const int n = max(nblk[0], nblk[1]);
+  const int total = (int)(pairs * BH);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    mbar_init(&bar->q_full, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->q_full[s], 1);
+      mbar_init(&bar->q_empty[s], 1);
       mbar_init(&bar->k_full[s], 1);
       mbar_init(&bar->k_empty[s], 1);
+      mbar_init(&bar->v_full[s], 1);
+      mbar_init(&bar->v_empty[s], 1);
       mbar_init(&bar->s_full[s], 1);
       mbar_init(&bar->s_free[s], 4);
       mbar_init(&bar->p_full[s], 4);
       mbar_init(&bar->pv_done[s], 1);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bar->v_full[s], 1);
-      mbar_init(&bar->v_empty[s], 1);
+      mbar_init(&bar->o_free[s], 4);
+      mbar_init(&bar->sched_full[s], 1);
+      mbar_init(&bar->sched_empty[s], 9);  // MMA thread + 8 softmax warps
     }
     mbar_init(&bar->drain, 1);
     bar->abort_flag = 0;
@@ -125,39 +151,61 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     // ----------------------------------------------------------- producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(&bar->q_full, 2 * C::TILE);
-      for (int X = 0; X < 2; ++X)
-        load_rows<C::BOXES>(smem + C::OFF_Q + X * C::TILE, &tmQ, &bar->q_full, io, bh, Sq,
-                            q0 + X * BM);
-      auto load_k = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&bar->k_empty[s], ((j >> 1) & 1) ^ 1, status)) return false;
-        mbar_arrive_expect_tx(&bar->k_full[s], C::TILE);
-        load_rows<C::BOXES>(smem + C::OFF_K + s * C::TILE, &tmK, &bar->k_full[s], io, bh, Skv,
-                            j * BN);
-        return true;
-      };
-      bool ok = n > 0 ? load_k(0) : true;
-      for (int j = 0; j < n && ok && !*abort_flag; ++j) {
-        if (j + 1 < n && !load_k(j + 1)) { ok = false; break; }
-        const int vs = j & 1;
-        if (!mbar_wait(&bar->v_empty[vs], ((j >> 1) & 1) ^ 1, status)) { ok = false; break; }
-        mbar_arrive_expect_tx(&bar->v_full[vs], C::TILE);
-        load_rows<C::BOXES>(smem + C::OFF_V + vs * C::TILE, &tmV, &bar->v_full[vs], io, bh, Skv,
-                            j * BN);
+      uint32_t kc = 0, vc = 0;  // K / V blocks loaded so far
+      bool ok = true;
+      int w = (int)blockIdx.x;
+      for (uint32_t seq = 0; ok && !*abort_flag; ++seq) {
+        const int slot = seq & 1;
+        if (!mbar_wait(&bar->sched_empty[slot], ((seq >> 1) & 1) ^ 1, status)) { ok = false; break; }
+        bar->item[slot] = w < total ? w : -1;
+        mbar_arrive(&bar->sched_full[slot]);
+        if (w >= total) break;
+        const Item it = decode_item(w, pairs, Sq, Skv, causal);
+        // K(0) first (its slot frees with the previous item's last S MMAs),
+        // then both Q tiles.  Every item has at least one block (its first
+        // row is below Sq and Skv >= 1).
+        {
+          const int s = kc & 1;
+          if (!mbar_wait(&bar->k_empty[s], ((kc >> 1) & 1) ^ 1, status)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bar->k_full[s], C::TILE);
+          load_rows<C::BOXES>(smem + C::OFF_K + s * C::TILE, &tmK, &bar->k_full[s], io, it.bh, Skv, 0);
+          ++kc;
+        }
+        for (int X = 0; X < 2 && ok; ++X) {
+          if (!mbar_wait(&bar->q_empty[X], (seq & 1) ^ 1, status)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bar->q_full[X], C::TILE);
+          load_rows<C::BOXES>(smem + C::OFF_Q + X * C::TILE, &tmQ, &bar->q_full[X], io, it.bh, Sq,
+                              it.q0 + X * BM);
+        }
+        for (int j = 0; j < it.n && ok && !*abort_flag; ++j) {
+          if (j + 1 < it.n) {
+            const int s = kc & 1;
+            if (!mbar_wait(&bar->k_empty[s], ((kc >> 1) & 1) ^ 1, status)) { ok = false; break; }
+            mbar_arrive_expect_tx(&bar->k_full[s], C::TILE);
+            load_rows<C::BOXES>(smem + C::OFF_K + s * C::TILE, &tmK, &bar->k_full[s], io, it.bh,
+                                Skv, (j + 1) * BN);
+            ++kc;
+          }
+          const int vs = vc & 1;
+          if (!mbar_wait(&bar->v_empty[vs], ((vc >> 1) & 1) ^ 1, status)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bar->v_full[vs], C::TILE);
+          load_rows<C::BOXES>(smem + C::OFF_V + vs * C::TILE, &tmV, &bar->v_full[vs], io, it.bh, Skv,
+                              j * BN);
+          ++vc;
+        }
+        w = (int)gridDim.x + atomicAdd(sched, 1);
       }
       if (!ok) *abort_flag = 1;
     }
   } else if (warp == 1) {
     // -------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      bool ok = mbar_wait(&bar->q_full, 0, status);
       const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
       const uint32_t k_addr = smem_u32(smem + C::OFF_K);
       const uint32_t v_addr = smem_u32(smem + C::OFF_V);
-      // S_X = Q_X K_j^T into TMEM columns X * 128
-      auto issue_s = [&](int X, int j) {
-        const uint32_t qa = q_addr + X * C::TILE, ka = k_addr + (j & 1) * C::TILE;
+      // S_X = Q_X K^T into TMEM columns X * 128 (K in slot ks)
+      auto issue_s = [&](int X, int kslot) {
+        const uint32_t qa = q_addr + X * C::TILE, ka = k_addr + kslot * C::TILE;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const uint32_t off = (ks >> 2) * BOX + (ks & 3) * 32;
@@ -168,128 +216,164 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_commit(&bar->s_full[X]);
       };
-      // O_X += P_X V_j with P_X read from TMEM (bf16 pairs in the first 64
-      // columns of S_X: 16 keys = 8 columns per MMA) and V_j from smem
-      auto issue_pv = [&](int X, int j) {
-        const uint32_t va = v_addr + (j & 1) * C::TILE;
+      // O_X (+)= P_X V with P_X read from TMEM (bf16 pairs in the first 64
+      // columns of S_X: 16 keys = 8 columns per MMA) and V from smem slot vs
+      auto issue_pv = [&](int X, int vslot, bool first) {
+        const uint32_t va = v_addr + vslot * C::TILE;
         const uint32_t pt = tmem + C::TMEM_S + X * BN;
 #pragma unroll
         for (int ks = 0; ks < BN / 16; ++ks)
           tc_mma_f16_ts(tmem + C::TMEM_O + X * D, pt + ks * 8,
                         make_smem_desc(va + ks * 2048, BOX, 1024, BWPP_SWIZZLE_128B),
-                        C::IDESC_PV, (j > 0 || ks > 0) ? 1u : 0u);
+                        C::IDESC_PV, (!first || ks > 0) ? 1u : 0u);
         tc_commit(&bar->pv_done[X]);
       };
-      // block 0: S_A(0), S_B(0)
-      if (ok && n > 0) {
-        ok = mbar_wait(&bar->k_full[0], 0, status);
-        if (ok) {
-          tc_fence_after();
-          for (int X = 0; X < 2; ++X)
-            if (nblk[X] > 0) issue_s(X, 0);
-          tc_commit(&bar->k_empty[0]);
-        }
-      }
-      for (int j = 0; j < n && ok && !*abort_flag; ++j) {
-        bool v_ready = false, k_ready = false;
-        for (int X = 0; X < 2 && ok; ++X) {
-          if (j < nblk[X]) {
-            ok = mbar_wait(&bar->p_full[X], j & 1, status);
-            if (ok && !v_ready)
-              v_ready = ok = mbar_wait(&bar->v_full[j & 1], (j >> 1) & 1, status);
-            if (!ok) break;
-            tc_fence_after();
-            issue_pv(X, j);
+      uint32_t kc = 0, vc = 0;          // K / V blocks consumed
+      uint32_t sc[2] = {0, 0};          // S MMAs issued per tile
+      uint32_t pc[2] = {0, 0};          // P blocks consumed per tile
+      bool ok = true;
+      for (uint32_t seq = 0; ok && !*abort_flag; ++seq) {
+        const int slot = seq & 1;
+        if (!mbar_wait(&bar->sched_full[slot], (seq >> 1) & 1, status)) { ok = false; break; }
+        const int w = bar->item[slot];
+        mbar_arrive(&bar->sched_empty[slot]);
+        if (w < 0) break;
+        const Item it = decode_item(w, pairs, Sq, Skv, causal);
+        {
+          // block 0: S_A(0), S_B(0)
+          ok = mbar_wait(&bar->k_full[kc & 1], (kc >> 1) & 1, status);
+          for (int X = 0; X < 2 && ok; ++X) ok = mbar_wait(&bar->q_full[X], seq & 1, status);
+          for (int X = 0; X < 2 && ok; ++X) {
+            if (it.nblk[X] > 0) {
+              if (sc[X] > 0) ok = mbar_wait(&bar->s_free[X], (sc[X] - 1) & 1, status);
+              if (!ok) break;
+              tc_fence_after();
+              issue_s(X, kc & 1);
+              ++sc[X];
+            }
+            // Q_X is free once this item's last S_X MMA completes, so the
+            // next item's Q loads during this item's last block
+            if (it.nblk[X] <= 1) tc_commit(&bar->q_empty[X]);
           }
-          if (X == 1) tc_commit(&bar->v_empty[j & 1]);  // V_j free after PV_B(j)
-          if (j + 1 < nblk[X]) {
-            if (!k_ready)
-              k_ready = ok = mbar_wait(&bar->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, status);
-            if (ok) ok = mbar_wait(&bar->s_free[X], j & 1, status);
-            if (!ok) break;
-            tc_fence_after();
-            issue_s(X, j + 1);
+          if (!ok) break;
+          tc_commit(&bar->k_empty[kc & 1]);
+          ++kc;
+        }
+        for (int j = 0; j < it.n && ok && !*abort_flag; ++j) {
+          bool v_ready = false, k_ready = false;
+          for (int X = 0; X < 2 && ok; ++X) {
+            if (j < it.nblk[X]) {
+              ok = mbar_wait(&bar->p_full[X], pc[X] & 1, status);
+              ++pc[X];
+              // the first PV of an item overwrites O_X: the previous item's
+              // epilogue must have read it
+              if (ok && j == 0 && seq > 0) ok = mbar_wait(&bar->o_free[X], (seq - 1) & 1, status);
+              if (ok && !v_ready) v_ready = ok = mbar_wait(&bar->v_full[vc & 1], (vc >> 1) & 1, status);
+              if (!ok) break;
+              tc_fence_after();
+              issue_pv(X, vc & 1, j == 0);
+            }
+            if (X == 1) tc_commit(&bar->v_empty[vc & 1]);  // V free after PV_B(j)
+            if (j + 1 < it.nblk[X]) {
+              if (!k_ready) k_ready = ok = mbar_wait(&bar->k_full[kc & 1], (kc >> 1) & 1, status);
+              if (ok) ok = mbar_wait(&bar->s_free[X], (sc[X] - 1) & 1, status);
+              if (!ok) break;
+              tc_fence_after();
+              issue_s(X, kc & 1);
+              ++sc[X];
+              if (j + 2 == it.nblk[X]) tc_commit(&bar->q_empty[X]);
+            }
+          }
+          ++vc;
+          if (ok && j + 1 < it.n) {
+            tc_commit(&bar->k_empty[kc & 1]);
+            ++kc;
           }
         }
-        if (ok && j + 1 < n) tc_commit(&bar->k_empty[(j + 1) & 1]);
+        if (!ok) break;
+        // a tile with no block in this item (tile B past Sq) still takes
+        // the previous item's epilogue hand-off, keeping the phases aligned
+        for (int X = 0; X < 2 && ok; ++X)
+          if (it.nblk[X] == 0 && seq > 0) ok = mbar_wait(&bar->o_free[X], (seq - 1) & 1, status);
       }
       if (!ok) *abort_flag = 1;
       tc_commit(&bar->drain);
       mbar_wait(&bar->drain, 0, status);
     }
   } else {
-    // ------------------------------------------------------------- softmax
+    // --------------------------------------------------- softmax + epilogue
     const int X = (warp - 2) >> 2;    // query tile
     const int quarter = warp & 3;     // TMEM lanes 32*quarter ..
     const int row = quarter * 32 + lane;
-    const uint32_t m_row = q0 + X * BM + row;  // query index
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_col = tmem + lane_base + C::TMEM_S + X * BN;
     const uint32_t o_col = tmem + lane_base + C::TMEM_O + X * D;
-    float m_run = -INFINITY, l_run = 0.0f;
+    uint32_t sc = 0;   // S_X blocks consumed
+    uint32_t pvc = 0;  // PV_X MMAs before this item
     bool ok = true;
-    const int nb = nblk[X];
-    for (int j = 0; j < nb && ok; ++j) {
-      if (*abort_flag || !mbar_wait(&bar->s_full[X], j & 1, status)) {
-        *abort_flag = 1;
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // Two passes over S in TMEM (row max, then exp2 + pack) keep the
-      // 128-float row out of registers.  S_X(j+1) is only issued after
-      // PV_X(j), i.e. after this tile's P is published, so re-reading S here
-      // does not delay the tensor core.  Blocks that need no mask take a
-      // branch-free path; masked blocks compare each key with one limit.
-      const uint32_t n0 = (uint32_t)j * BN;
-      uint32_t lim = Skv - 1;                       // last visible key
-      if (causal && m_row < lim) lim = m_row;
-      const bool need_mask = n0 + BN - 1 > lim;
-      const int lim_rel = (int)lim - (int)n0;       // visible iff index <= lim_rel
-      // pass 1: all four 32-column loads in flight behind one wait, then a
-      // max over 8 independent chains
-      float mx;
-      {
-        uint32_t r[BN];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-          tmem_ld_32x32b_x32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-          tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
-        if (need_mask) {
-#pragma unroll
-          for (int i = 0; i < BN; ++i)
-            if (i > lim_rel) r[i] = __float_as_uint(-INFINITY);
-        }
-        float m8[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(r[k]);
-#pragma unroll
-        for (int i = 8; i < BN; i += 16)
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            m8[k] = max3(m8[k], __uint_as_float(r[i + k]), __uint_as_float(r[i + 8 + k]));
-        mx = fmaxf(fmaxf(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5])),
-                   fmaxf(m8[6], m8[7]));
-      }
-      const float m_new = fmaxf(m_run, mx);
-      // move the reference max only when it grows by more than 2^8
-      const bool move = (m_new - m_run) * scale_log2 > 8.0f;
-      const float m_use = move ? m_new : m_run;
-      const float alpha = move ? fast_exp2((m_run - m_new) * scale_log2) : 1.0f;
-      const float mb = m_use * scale_log2;
-      if (j > 0) {
-        // PV_X(j-1), which read P_X(j-1) from these TMEM columns, is done (its
-        // completion precedes S_X(j)'s, so this wait is immediate); O_X is
-        // stable for the rescale
-        if (!mbar_wait(&bar->pv_done[X], (j - 1) & 1, status)) {
-          *abort_flag = 1;
+    for (uint32_t seq = 0; ok; ++seq) {
+      const int slot = seq & 1;
+      if (!mbar_wait(&bar->sched_full[slot], (seq >> 1) & 1, status)) { ok = false; break; }
+      const int w = bar->item[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->sched_empty[slot]);
+      if (w < 0) break;
+      const Item it = decode_item(w, pairs, Sq, Skv, causal);
+      const uint32_t bh = it.bh;
+      const uint32_t m_row = it.q0 + X * BM + row;  // query index
+      const int nb = it.nblk[X];
+      float m_run = -INFINITY, l_run = 0.0f;
+      for (int j = 0; j < nb && ok; ++j) {
+        if (*abort_flag || !mbar_wait(&bar->s_full[X], sc & 1, status)) {
           ok = false;
           break;
         }
+        ++sc;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, move)) {
+        // Two passes over S in TMEM (row max, then exp2 + pack) keep the
+        // 128-float row out of registers.  Blocks that need no mask take a
+        // branch-free path; masked blocks compare each key with one limit.
+        const uint32_t n0 = (uint32_t)j * BN;
+        uint32_t lim = Skv - 1;                       // last visible key
+        if (causal && m_row < lim) lim = m_row;
+        const bool need_mask = n0 + BN - 1 > lim;
+        const int lim_rel = (int)lim - (int)n0;       // visible iff index <= lim_rel
+        // pass 1: all four 32-column loads in flight behind one wait, then a
+        // max over 8 independent chains
+        float mx;
+        {
+          uint32_t r[BN];
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c)
+            tmem_ld_32x32b_x32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c)
+            tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+          if (need_mask) {
+#pragma unroll
+            for (int i = 0; i < BN; ++i)
+              if (i > lim_rel) r[i] = __float_as_uint(-INFINITY);
+          }
+          float m8[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(r[k]);
+#pragma unroll
+          for (int i = 8; i < BN; i += 16)
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              m8[k] = max3(m8[k], __uint_as_float(r[i + k]), __uint_as_float(r[i + 8 + k]));
+          mx = fmaxf(fmaxf(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5])),
+                     fmaxf(m8[6], m8[7]));
+        }
+        const float m_new = fmaxf(m_run, mx);
+        // move the reference max only when it grows by more than 2^8
+        const bool move = (m_new - m_run) * scale_log2 > 8.0f;
+        const float m_use = move ? m_new : m_run;
+        const float alpha = move ? fast_exp2((m_run - m_new) * scale_log2) : 1.0f;
+        const float mb = m_use * scale_log2;
+        // Rescale O_X when a row's max moved.  PV_X(j-1) is complete: the
+        // commit that signalled S_X(j) was issued after it.
+        if (j > 0 && __any_sync(0xffffffffu, move)) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             uint32_t ro[32];
@@ -305,58 +389,59 @@ __global__ void __launch_bounds__(THREADS, 1)
             tmem_st_32x32b_x16(o_col + c * 32 + 16, w1);
           }
         }
-      }
-      // pass 2 (double-buffered loads): P = exp2(S*c - m) as bf16 pairs into
-      // TMEM columns [0, 64) of S_X, i.e. over S columns already read.  The
-      // row sum adds the fp32 values (paired lanes), the PV product sees bf16.
-      const uint64_t sc2 = f2pack(scale_log2, scale_log2);
-      const uint64_t nb2 = f2pack(-mb, -mb);
-      uint64_t acc2 = f2pack(0.0f, 0.0f);
-      uint32_t rbuf[2][32];
-      tmem_ld_32x32b_x32(s_col, rbuf[0]);
-      tc_wait_ld(rbuf[0]);
+        // pass 2 (double-buffered loads): P = exp2(S*c - m) as 16-bit pairs
+        // into TMEM columns [0, 64) of S_X, i.e. over S columns already
+        // read.  The row sum adds the fp32 values (paired lanes).
+        const uint64_t sc2 = f2pack(scale_log2, scale_log2);
+        const uint64_t nb2 = f2pack(-mb, -mb);
+        uint64_t acc2 = f2pack(0.0f, 0.0f);
+        uint32_t rbuf[2][32];
+        tmem_ld_32x32b_x32(s_col, rbuf[0]);
+        tc_wait_ld(rbuf[0]);
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t (&r)[32] = rbuf[c & 1];
-        if (c + 1 < BN / 32) tmem_ld_32x32b_x32(s_col + (c + 1) * 32, rbuf[(c + 1) & 1]);
-        if (need_mask) {
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t (&r)[32] = rbuf[c & 1];
+          if (c + 1 < BN / 32) tmem_ld_32x32b_x32(s_col + (c + 1) * 32, rbuf[(c + 1) & 1]);
+          if (need_mask) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i > lim_rel) r[i] = __float_as_uint(-INFINITY);
-        }
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float y0, y1, p0, p1;
-          f2unpack(f2fma(f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nb2),
-                   y0, y1);
-          if ((i & 7) >= 8 - kEmuPairsPer8) {
-            exp2_fma2(y0, y1, p0, p1);  // FMA pipe
-          } else {
-            p0 = fast_exp2(y0);  // MUFU
-            p1 = fast_exp2(y1);
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i > lim_rel) r[i] = __float_as_uint(-INFINITY);
           }
-          pk[i] = pack2_16<F16>(p0, p1);
-          acc2 = f2add(acc2, f2pack(p0, p1));
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float y0, y1, p0, p1;
+            f2unpack(f2fma(f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nb2),
+                     y0, y1);
+            if ((i & 7) >= 8 - kEmuPairsPer8) {
+              exp2_fma2(y0, y1, p0, p1);  // FMA pipe
+            } else {
+              p0 = fast_exp2(y0);  // MUFU
+              p1 = fast_exp2(y1);
+            }
+            pk[i] = pack2_16<F16>(p0, p1);
+            acc2 = f2add(acc2, f2pack(p0, p1));
+          }
+          tmem_st_32x32b_x16(s_col + c * 16, pk);
+          if (c + 1 < BN / 32) tc_wait_ld(rbuf[(c + 1) & 1]);
         }
-        tmem_st_32x32b_x16(s_col + c * 16, pk);
-        if (c + 1 < BN / 32) tc_wait_ld(rbuf[(c + 1) & 1]);
+        float psum_lo, psum_hi;
+        f2unpack(acc2, psum_lo, psum_hi);
+        l_run = l_run * alpha + psum_lo + psum_hi;
+        m_run = m_use;
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bar->s_free[X]);  // S_X may be overwritten
+          mbar_arrive(&bar->p_full[X]);  // P_X ready for PV_X(j)
+        }
       }
-      float psum_lo, psum_hi;
-      f2unpack(acc2, psum_lo, psum_hi);
-      l_run = l_run * alpha + psum_lo + psum_hi;
-      m_run = m_use;
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bar->s_free[X]);  // S_X may be overwritten
-        mbar_arrive(&bar->p_full[X]);  // P_X ready for PV_X(j)
-      }
-    }
-    // epilogue: O / l -> global (fp32)
-    if (ok && nb > 0) {
-      if (mbar_wait(&bar->pv_done[X], (nb - 1) & 1, status)) {
+      if (!ok) break;
+      // epilogue: O / l -> global, then hand O_X back to the MMA warp
+      if (nb > 0) {
+        pvc += (uint32_t)nb;
+        if (!mbar_wait(&bar->pv_done[X], (pvc - 1) & 1, status)) { ok = false; break; }
         tc_fence_after();
         const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
         const bool valid = m_row < Sq;
@@ -390,10 +475,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                   pack2_16<F16>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
           }
         }
-      } else {
-        *abort_flag = 1;
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->o_free[X]);
     }
+    if (!ok) *abort_flag = 1;
   }
 
   tc_fence_before();
@@ -453,12 +540,18 @@ int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_
     g_attr_set[di][ctx->device] = true;
   }
   const uint32_t pairs = (Sq + 2 * BM - 1) / (2 * BM);
-  const uint64_t grid = (uint64_t)pairs * BH;
-  if (grid > 0x7fffffffull)
-    return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "attention: grid too large");
+  const uint64_t items = (uint64_t)pairs * BH;
+  if (items > 0x7fffffffull)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "attention: too many work items");
+  // persistent: one CTA per SM (at most one per item); the work counter
+  // hands out the items after the first gridDim.x
+  const uint64_t grid = items < (uint64_t)ctx->num_sms ? items : (uint64_t)ctx->num_sms;
+  rc = bwpp_check_cuda(ctx, cudaMemsetAsync(ctx->sched_counter, 0, sizeof(int), ctx->stream),
+                       "attention work counter");
+  if (rc) return rc;
   attention_tc_kernel<D, F16><<<(unsigned)grid, THREADS, Cfg<D, F16>::SMEM, ctx->stream>>>(
       tq, tk, tv, io, BH, Sq, Skv, scale * 1.4426950408889634f, causal, pairs,
-      ctx->status_word);
+      ctx->sched_counter, ctx->status_word);
   BWPP_LAUNCH_CHECK(ctx, "attention tcgen05");
   return BWPP_CUDA_OK;
 }

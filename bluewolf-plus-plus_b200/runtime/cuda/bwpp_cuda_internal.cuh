@@ -24,6 +24,7 @@ struct BwppCudaCtx {
   int device;
   cudaStream_t stream;
   int *status_word;        // device int, 0 = ok, else a BWPP_CUDA_ERR_* code
+  int *sched_counter;      // device int next to it: work counter of persistent kernels
   void *workspace;         // device scratch (owned unless user_workspace)
   size_t workspace_bytes;
   int user_workspace;      // 1: set by bwpp_cuda_ctx_set_workspace, not freed

@@ -141,11 +141,12 @@ int bwpp_cuda_ctx_create(BwppCudaCtx **out, int device, void *stream) {
                                device),
         "cudaDeviceGetAttribute");
   if (rc == BWPP_CUDA_OK)
-    rc = bwpp_check_cuda(ctx, cudaMalloc(&ctx->status_word, sizeof(int)),
+    rc = bwpp_check_cuda(ctx, cudaMalloc(&ctx->status_word, 4 * sizeof(int)),
                          "status word");
   if (rc == BWPP_CUDA_OK)
-    rc = bwpp_check_cuda(ctx, cudaMemset(ctx->status_word, 0, sizeof(int)),
+    rc = bwpp_check_cuda(ctx, cudaMemset(ctx->status_word, 0, 4 * sizeof(int)),
                          "status word");
+  if (rc == BWPP_CUDA_OK) ctx->sched_counter = ctx->status_word + 1;
   if (rc != BWPP_CUDA_OK) {
     if (ctx->status_word) cudaFree(ctx->status_word);
     free(ctx);

@@ -203,3 +203,43 @@ def test_unbound_input_is_an_error(ctx):
     with pytest.raises(bwpp.BwppError):
         plan.run()
     plan.close()
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_graphs_in_other_storage_types(ctx, dtype):
+    """The same reference dumps with every value declared f32 or bf16: the
+    executor keeps that storage (f32 GEMM / attention operands are rounded to
+    bf16 for the tensor cores, arithmetic stays fp32)."""
+    tdt = {"f32": torch.float32, "bf16": torch.bfloat16}[dtype]
+    tol = 2e-2 if dtype == "bf16" else 1e-2
+
+    def run_dt(name, dims, inputs):
+        dot = dump(name).replace(" f16 [", f" {dtype} [").replace("nf16 [", f"n{dtype} [")
+        dot = dot.replace("\\nf16", f"\\n{dtype}").replace('"f16 ', f'"{dtype} ')
+        mem = dump(name, ".mem.txt").replace(" f16 ", f" {dtype} ")
+        plan = bwpp.Plan(ctx, dot, mem, dims)
+        assert all(v["dtype"] == {"f32": "float32", "bf16": "bfloat16"}[dtype] for v in plan.values())
+        for key, arr in inputs.items():
+            plan.bind(key, torch.from_numpy(np.ascontiguousarray(arr, np.float32)).cuda().to(tdt))
+        plan.run()
+        ctx.sync()
+        (out,) = [plan.tensor(v["id"]).float().cpu().numpy() for v in plan.values() if v["output"]]
+        plan.close()
+        return out
+
+    rng = np.random.default_rng(21)
+    M, K, N = 200, 256, 384
+    a, b, bias = f32(half(rng, M, K, scale=0.5)), f32(half(rng, K, N, scale=0.5)), f32(half(rng, N, scale=0.1))
+    out = run_dt("matmul_add_silu", dict(M=M, K=K, N=N), {"a": a, "b": b, "bias": bias})
+    rb = lambda t: torch.from_numpy(t).to(torch.bfloat16).float().numpy()  # noqa: E731
+    assert rel_fro(out, O.matmul(rb(a), rb(b), rb(bias) if dtype == "bf16" else bias, 1, 1)) <= tol
+    B_, N_ = 64, 512
+    x, w = f32(half(rng, B_, N_, scale=0.2)), f32(half(rng, N_, N_, scale=0.2))
+    gamma = (1 + 0.1 * rng.standard_normal(N_)).astype(np.float32)
+    out = run_dt("norms", dict(B=B_, N=N_), {"x": x, "w": w, "gamma": gamma})
+    ref = O.rmsnorm(O.softmax(O.matmul(rb(x), rb(w))), gamma, None, 1e-5)
+    assert rel_fro(out, ref) <= tol
+    Bh, H, T, D = 1, 2, 256, 128
+    q, k, v = (f32(half(rng, Bh, H, T, D, scale=0.3)) for _ in range(3))
+    out = run_dt("attention", dict(B=Bh, H=H, T=T, D=D), {"q": q, "k": k, "v": v})
+    assert rel_fro(out, O.attention_bhsd(rb(q), rb(k), rb(v), 1.0, 0)) <= tol
