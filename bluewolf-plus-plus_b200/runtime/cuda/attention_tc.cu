@@ -44,7 +44,10 @@ struct Cfg {
   static constexpr int OFF_Q = 0;           // 2 tiles
   static constexpr int OFF_K = 2 * TILE;    // 2 stages
   static constexpr int OFF_V = 4 * TILE;    // 2 stages
-  static constexpr int OFF_BAR = 6 * TILE;
+  // epilogue staging: 32 rows x 128 B per softmax warp
+  static constexpr int OFF_STAGE = 6 * TILE;
+  static constexpr int STAGE_WARP = 32 * 128;
+  static constexpr int OFF_BAR = OFF_STAGE + 8 * STAGE_WARP;
   static constexpr int SMEM = OFF_BAR + 512 + 1024;
   static constexpr uint32_t TMEM_S = 0;        // S_A at 0, S_B at 128
   static constexpr uint32_t TMEM_O = 2 * BN;   // O_A at 256, O_B at 256 + D
@@ -200,32 +203,36 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // -------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
-      const uint32_t k_addr = smem_u32(smem + C::OFF_K);
-      const uint32_t v_addr = smem_u32(smem + C::OFF_V);
-      // S_X = Q_X K^T into TMEM columns X * 128 (K in slot ks)
+      // Every smem descriptor is a base built once plus a byte offset known
+      // at compile time per k step (the start-address field is the low 14
+      // bits, addresses stay below 256 KB, so the add never carries out of
+      // it): a group of 8 MMAs then costs the tensor core's time, not the
+      // issuing thread's, which rebuilding descriptors per MMA made it.
+      const uint64_t dq = make_smem_desc(smem_u32(smem + C::OFF_Q), 16, 1024, BWPP_SWIZZLE_128B);
+      const uint64_t dk = make_smem_desc(smem_u32(smem + C::OFF_K), 16, 1024, BWPP_SWIZZLE_128B);
+      const uint64_t dv = make_smem_desc(smem_u32(smem + C::OFF_V), BOX, 1024, BWPP_SWIZZLE_128B);
+      // S_X = Q_X K^T into TMEM columns X * 128 (K in slot kslot)
       auto issue_s = [&](int X, int kslot) {
-        const uint32_t qa = q_addr + X * C::TILE, ka = k_addr + kslot * C::TILE;
+        const uint64_t qd = desc_add(dq, (uint32_t)X * C::TILE);
+        const uint64_t kd = desc_add(dk, (uint32_t)kslot * C::TILE);
+        const uint32_t d_tmem = tmem + C::TMEM_S + X * BN;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const uint32_t off = (ks >> 2) * BOX + (ks & 3) * 32;
-          tc_mma_f16_ss(tmem + C::TMEM_S + X * BN,
-                        make_smem_desc(qa + off, 16, 1024, BWPP_SWIZZLE_128B),
-                        make_smem_desc(ka + off, 16, 1024, BWPP_SWIZZLE_128B), C::IDESC_S,
-                        ks > 0 ? 1u : 0u);
+          tc_mma_f16_ss(d_tmem, desc_add(qd, off), desc_add(kd, off), C::IDESC_S, ks > 0 ? 1u : 0u);
         }
         tc_commit(&bar->s_full[X]);
       };
       // O_X (+)= P_X V with P_X read from TMEM (bf16 pairs in the first 64
-      // columns of S_X: 16 keys = 8 columns per MMA) and V from smem slot vs
+      // columns of S_X: 16 keys = 8 columns per MMA) and V from smem slot vslot
       auto issue_pv = [&](int X, int vslot, bool first) {
-        const uint32_t va = v_addr + vslot * C::TILE;
+        const uint64_t vd = desc_add(dv, (uint32_t)vslot * C::TILE);
         const uint32_t pt = tmem + C::TMEM_S + X * BN;
+        const uint32_t d_tmem = tmem + C::TMEM_O + X * D;
 #pragma unroll
         for (int ks = 0; ks < BN / 16; ++ks)
-          tc_mma_f16_ts(tmem + C::TMEM_O + X * D, pt + ks * 8,
-                        make_smem_desc(va + ks * 2048, BOX, 1024, BWPP_SWIZZLE_128B),
-                        C::IDESC_PV, (!first || ks > 0) ? 1u : 0u);
+          tc_mma_f16_ts(d_tmem, pt + ks * 8, desc_add(vd, ks * 2048), C::IDESC_PV,
+                        (!first || ks > 0) ? 1u : 0u);
         tc_commit(&bar->pv_done[X]);
       };
       uint32_t kc = 0, vc = 0;          // K / V blocks consumed
@@ -448,31 +455,61 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (valid && io.lse)
           io.lse[(size_t)bh * Sq + m_row] =
               l_run > 0.0f ? m_run * scale_log2 + __log2f(l_run) : -INFINITY;
-        float *orow = io.out_f32 ? io.out_f32 + ((size_t)bh * Sq + m_row) * D : nullptr;
-        uint16_t *brow = io.out_bf16 ? io.out_bf16 + ((size_t)(bh / io.H) * Sq + m_row) * io.ldo +
-                                           (size_t)(bh % io.H) * D
-                                     : nullptr;
+        // O leaves through shared memory: each thread stages its row's
+        // 128-byte chunk (16-byte pieces XOR-swizzled by row, so both the
+        // row-per-thread writes and the row-per-quarter-warp reads hit 32
+        // distinct banks), then every store instruction writes 4 whole
+        // 128-byte row segments instead of 32 scattered 16-byte pieces.
+        uint4 *stage = reinterpret_cast<uint4 *>(smem + C::OFF_STAGE + (warp - 2) * C::STAGE_WARP);
+        const uint32_t row0 = it.q0 + X * BM + quarter * 32;  // this warp's first row
+        const int sub = lane & 7;                             // 16-byte piece in a row
+        auto flush = [&](auto &&row_ptr) {
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int r = 4 * k + (lane >> 3);
+            const uint4 val = stage[r * 8 + (sub ^ (r & 7))];
+            if (row0 + r < Sq) *(row_ptr(row0 + r) + sub) = val;
+          }
+          __syncwarp();
+        };
+        if (io.out_f32) {
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(o_col + c * 32, r);
-          tc_wait_ld(r);
-          if (valid && orow) {
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(o_col + c * 32, r);
+            tc_wait_ld(r);
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-              __stcs(reinterpret_cast<float4 *>(orow + c * 32) + i,
-                     make_float4(__uint_as_float(r[4 * i]) * inv, __uint_as_float(r[4 * i + 1]) * inv,
-                                 __uint_as_float(r[4 * i + 2]) * inv,
-                                 __uint_as_float(r[4 * i + 3]) * inv));
+              stage[lane * 8 + (i ^ (lane & 7))] =
+                  make_uint4(__float_as_uint(__uint_as_float(r[4 * i]) * inv),
+                             __float_as_uint(__uint_as_float(r[4 * i + 1]) * inv),
+                             __float_as_uint(__uint_as_float(r[4 * i + 2]) * inv),
+                             __float_as_uint(__uint_as_float(r[4 * i + 3]) * inv));
+            flush([&](uint32_t m) {
+              return reinterpret_cast<uint4 *>(io.out_f32 + ((size_t)bh * Sq + m) * D + c * 32);
+            });
           }
-          if (valid && brow) {
+        }
+        if (io.out_bf16) {
+#pragma unroll 1
+          for (int c = 0; c < D / 64; ++c) {
+            uint32_t r[64];
+            tmem_ld_32x32b_x32(o_col + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+            tmem_ld_32x32b_x32(o_col + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+            tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+            tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[32]));
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              *reinterpret_cast<uint4 *>(brow + c * 32 + 8 * i) = make_uint4(
+            for (int i = 0; i < 8; ++i)
+              stage[lane * 8 + (i ^ (lane & 7))] = make_uint4(
                   pack2_16<F16>(__uint_as_float(r[8 * i]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
                   pack2_16<F16>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
                   pack2_16<F16>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
                   pack2_16<F16>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
+            flush([&](uint32_t m) {
+              return reinterpret_cast<uint4 *>(io.out_bf16 + ((size_t)(bh / io.H) * Sq + m) * io.ldo +
+                                               (size_t)(bh % io.H) * D + c * 64);
+            });
           }
         }
       }

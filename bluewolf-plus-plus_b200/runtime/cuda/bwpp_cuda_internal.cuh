@@ -328,6 +328,18 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr,
 
 #define BWPP_SWIZZLE_128B 2u
 
+// The descriptor of the shared-memory address `bytes` past the one `d`
+// describes.  The start address is d's low 14 bits (address >> 4); callers
+// keep the sum below 256 KB, so only the low word changes.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) {
+  uint32_t lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(d));
+  lo += bytes >> 4;
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+
 // Instruction descriptor, kind::f16 with fp32 D and A/B both bf16 (ab_f16 =
 // 0) or both f16 (ab_f16 = 1): A/B format fields 0 = f16, 1 = bf16.
 __host__ __device__ constexpr uint32_t make_idesc_f32acc(uint32_t M, uint32_t N,
