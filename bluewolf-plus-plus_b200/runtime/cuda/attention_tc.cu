@@ -6,8 +6,9 @@
 // B that ping-pong: while the softmax warps of one tile turn its S into P, the
 // tensor core works on the other tile.  Per 128-key block j:
 //   S_X = Q_X K_j^T          tcgen05 M=128 N=128 K=16 (Q, K K-major, bf16)
-//   P_X = exp2(S_X*c - m)    softmax warps, one thread per row; P as bf16
-//                            pairs written back into S_X's TMEM columns
+//   P_X = exp2(S_X*c - m)    softmax warps, two threads per row (64 keys
+//                            each); P as bf16 pairs written back into S_X's
+//                            TMEM columns
 //   O_X += P_X V_j           tcgen05 M=128 N=D K=16, A = P from TMEM,
 //                            B = V MN-major from smem
 // S_A, S_B, O_A, O_B live in TMEM (4 x 128 columns for D = 128).  The running
@@ -17,10 +18,11 @@
 // max to halve its instruction count; CTAs are ordered head-major so one
 // head's K / V is read from DRAM once and shared through L2.
 //
-// Warp roles (320 threads): warp 0 TMA producer (Q once; K and V
-// double-buffered, 3-D tensor maps so ragged S zero-fills per head),
-// warp 1 TMEM allocator + single-thread MMA issuer, warps 2-5 softmax of
-// tile A, warps 6-9 softmax of tile B (warp w reads TMEM lanes 32*(w%4)..).
+// Warp roles (576 threads): warps 0-7 softmax of tile A, warps 8-15
+// softmax of tile B (warp w reads TMEM lanes 32*(w%4)..; two warps per lane
+// quarter split the keys and O columns), warp 16 TMA producer (Q once; K
+// and V double-buffered, 3-D tensor maps so ragged S zero-fills per head),
+// warp 17 TMEM allocator + single-thread MMA issuer.
 // MMA issue order per block: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1), so one
 // tile's softmax always overlaps the other tile's MMAs.
 //
@@ -31,7 +33,10 @@
 namespace {
 
 using namespace bwpp_attn;
-constexpr int THREADS = 320;
+// warps 0-15 softmax, 16 producer, 17 MMA.  18 warps put 5 on two of the
+// SM's four register files (16K registers each), so a thread gets 96.
+constexpr int THREADS = 576;
+constexpr int W_PROD = 16, W_MMA = 17;
 // Of every 8 score pairs, this many take exp2 on the FMA pipe (exp2_fma2),
 // the rest on MUFU: one ex2 per score would keep MUFU as busy as the tensor
 // core, so part of the load moves to the otherwise idle FMA pipe.
@@ -46,8 +51,8 @@ struct Cfg {
   static constexpr int OFF_V = 4 * TILE;    // 2 stages
   // epilogue staging: 32 rows x 128 B per softmax warp
   static constexpr int OFF_STAGE = 6 * TILE;
-  static constexpr int STAGE_WARP = 32 * 128;
-  static constexpr int OFF_BAR = OFF_STAGE + 8 * STAGE_WARP;
+  static constexpr int STAGE_WARP = 32 * 64;
+  static constexpr int OFF_BAR = OFF_STAGE + 16 * STAGE_WARP;
   static constexpr int SMEM = OFF_BAR + 512 + 1024;
   static constexpr uint32_t TMEM_S = 0;        // S_A at 0, S_B at 128
   static constexpr uint32_t TMEM_O = 2 * BN;   // O_A at 256, O_B at 256 + D
@@ -64,6 +69,7 @@ struct Bars {
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], o_free[2];
   uint64_t sched_full[2], sched_empty[2];
+  uint64_t pair[8];  // the two halves of a tile's lane quarter: one phase per exchange
   uint64_t drain;
   int item[2];
   uint32_t tmem;
@@ -128,13 +134,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&bar->v_full[s], 1);
       mbar_init(&bar->v_empty[s], 1);
       mbar_init(&bar->s_full[s], 1);
-      mbar_init(&bar->s_free[s], 4);
-      mbar_init(&bar->p_full[s], 4);
+      mbar_init(&bar->s_free[s], 8);
+      mbar_init(&bar->p_full[s], 8);
       mbar_init(&bar->pv_done[s], 1);
-      mbar_init(&bar->o_free[s], 4);
+      mbar_init(&bar->o_free[s], 8);
       mbar_init(&bar->sched_full[s], 1);
-      mbar_init(&bar->sched_empty[s], 9);  // MMA thread + 8 softmax warps
+      mbar_init(&bar->sched_empty[s], 17);  // MMA thread + 16 softmax warps
     }
+    for (int p = 0; p < 8; ++p) mbar_init(&bar->pair[p], 2);
     mbar_init(&bar->drain, 1);
     bar->abort_flag = 0;
     fence_mbar_init();
@@ -142,7 +149,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
   }
-  if (warp == 1) {
+  if (warp == W_MMA) {
     tmem_alloc(&bar->tmem, C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -151,7 +158,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem;
 
-  if (warp == 0) {
+  if (warp == W_PROD) {
     // ----------------------------------------------------------- producer
     if (lane == 0) {
       uint32_t kc = 0, vc = 0;  // K / V blocks loaded so far
@@ -200,7 +207,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (!ok) *abort_flag = 1;
     }
-  } else if (warp == 1) {
+  } else if (warp == W_MMA) {
     // -------------------------------------------------------- MMA issuer
     if (lane == 0) {
       // Every smem descriptor is a base built once plus a byte offset known
@@ -223,15 +230,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_commit(&bar->s_full[X]);
       };
-      // O_X (+)= P_X V with P_X read from TMEM (bf16 pairs in the first 64
-      // columns of S_X: 16 keys = 8 columns per MMA) and V from smem slot vslot
+      // O_X (+)= P_X V with P_X read from TMEM (16-bit pairs: keys
+      // [64h, 64h + 64) in S_X columns [64h, 64h + 32), 16 keys = 8 columns
+      // per MMA) and V from smem slot vslot
       auto issue_pv = [&](int X, int vslot, bool first) {
         const uint64_t vd = desc_add(dv, (uint32_t)vslot * C::TILE);
         const uint32_t pt = tmem + C::TMEM_S + X * BN;
         const uint32_t d_tmem = tmem + C::TMEM_O + X * D;
 #pragma unroll
         for (int ks = 0; ks < BN / 16; ++ks)
-          tc_mma_f16_ts(d_tmem, pt + ks * 8, desc_add(vd, ks * 2048), C::IDESC_PV,
+          tc_mma_f16_ts(d_tmem, pt + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(vd, ks * 2048), C::IDESC_PV,
                         (!first || ks > 0) ? 1u : 0u);
         tc_commit(&bar->pv_done[X]);
       };
@@ -307,17 +315,51 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_commit(&bar->drain);
       mbar_wait(&bar->drain, 0, status);
     }
-  } else {
+  } else if (warp < W_PROD) {
     // --------------------------------------------------- softmax + epilogue
-    const int X = (warp - 2) >> 2;    // query tile
-    const int quarter = warp & 3;     // TMEM lanes 32*quarter ..
+    // Two warps share each 32-row lane quarter of a tile: half h takes keys
+    // [64h, 64h + 64) of every block (and writes their P into the first 32
+    // of its own 64 S columns) and O columns [h D/2, (h+1) D/2).  The halves
+    // agree on the row's reference max through shared memory (one
+    // mbarrier-paced exchange per block); their row sums meet once, in the
+    // epilogue.
+    const int sw = warp;                  // softmax warp 0..15
+    const int X = sw >> 3;                // query tile
+    const int h = (sw >> 2) & 1;          // key / O-column half
+    const int quarter = warp & 3;         // TMEM lanes 32*quarter ..
     const int row = quarter * 32 + lane;
+    uint64_t *pair_bar = &bar->pair[X * 4 + quarter];
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const uint32_t s_col = tmem + lane_base + C::TMEM_S + X * BN;
-    const uint32_t o_col = tmem + lane_base + C::TMEM_O + X * D;
+    const uint32_t s_col = tmem + lane_base + C::TMEM_S + X * BN + h * 64;
+    const uint32_t o_col = tmem + lane_base + C::TMEM_O + X * D + h * (D / 2);
+    // per-warp 2 KB: epilogue staging, and (outside the epilogue) two
+    // 32-float exchange slots the partner half reads
+    uint8_t *stage_raw = smem + C::OFF_STAGE + sw * C::STAGE_WARP;
+    const float *peer_xch =
+        reinterpret_cast<const float *>(smem + C::OFF_STAGE + (sw ^ 4) * C::STAGE_WARP);
+    bool ok = true;
+    uint32_t xc = 0;  // exchanges so far (slot and phase parity = xc & 1)
+    // Max or sum of v over the two halves of this row.  Slots are
+    // double-buffered: a warp rewrites a slot two exchanges later, and the
+    // exchange in between completes only after the partner arrived for it,
+    // i.e. after it read the slot.  The wait is bounded like every other:
+    // on expiry ok turns false and the warp unwinds.
+    auto pair_sync = [&]() {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pair_bar);
+      const bool done = mbar_wait(pair_bar, xc & 1, status);
+      ++xc;
+      return done;
+    };
+    auto pair_combine = [&](float v, bool sum) {
+      reinterpret_cast<float *>(stage_raw)[(xc & 1) * 32 + lane] = v;
+      const int slot = (int)(xc & 1) * 32;
+      if (!pair_sync()) ok = false;
+      const float o = peer_xch[slot + lane];
+      return sum ? v + o : fmaxf(v, o);
+    };
     uint32_t sc = 0;   // S_X blocks consumed
     uint32_t pvc = 0;  // PV_X MMAs before this item
-    bool ok = true;
     for (uint32_t seq = 0; ok; ++seq) {
       const int slot = seq & 1;
       if (!mbar_wait(&bar->sched_full[slot], (seq >> 1) & 1, status)) { ok = false; break; }
@@ -337,105 +379,88 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         ++sc;
         tc_fence_after();
-        // Two passes over S in TMEM (row max, then exp2 + pack) keep the
-        // 128-float row out of registers.  Blocks that need no mask take a
-        // branch-free path; masked blocks compare each key with one limit.
-        const uint32_t n0 = (uint32_t)j * BN;
+        uint32_t r[64];
+        tmem_ld_32x32b_x32(s_col, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld_32x32b_x32(s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        // keys n0 + i; blocks that need no mask take a branch-free path,
+        // masked ones compare each key with one limit
+        const uint32_t n0 = (uint32_t)j * BN + h * 64;
         uint32_t lim = Skv - 1;                       // last visible key
         if (causal && m_row < lim) lim = m_row;
-        const bool need_mask = n0 + BN - 1 > lim;
-        const int lim_rel = (int)lim - (int)n0;       // visible iff index <= lim_rel
-        // pass 1: all four 32-column loads in flight behind one wait, then a
-        // max over 8 independent chains
-        float mx;
-        {
-          uint32_t r[BN];
+        if (n0 + 63 > lim) {
+          const int lim_rel = (int)lim - (int)n0;     // visible iff index <= lim_rel
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c)
-            tmem_ld_32x32b_x32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
-#pragma unroll
-          for (int c = 0; c < BN / 32; ++c)
-            tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
-          if (need_mask) {
-#pragma unroll
-            for (int i = 0; i < BN; ++i)
-              if (i > lim_rel) r[i] = __float_as_uint(-INFINITY);
-          }
+          for (int i = 0; i < 64; ++i)
+            if (i > lim_rel) r[i] = __float_as_uint(-INFINITY);
+        }
+        auto block_max = [&]() {
           float m8[8];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(r[k]);
+          for (int k = 0; k < 8; ++k) m8[k] = max3(__uint_as_float(r[k]), __uint_as_float(r[8 + k]),
+                                                   __uint_as_float(r[16 + k]));
 #pragma unroll
-          for (int i = 8; i < BN; i += 16)
+          for (int i = 24; i < 64; i += 16)
 #pragma unroll
             for (int k = 0; k < 8; ++k)
               m8[k] = max3(m8[k], __uint_as_float(r[i + k]), __uint_as_float(r[i + 8 + k]));
-          mx = fmaxf(fmaxf(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5])),
-                     fmaxf(m8[6], m8[7]));
-        }
-        const float m_new = fmaxf(m_run, mx);
-        // move the reference max only when it grows by more than 2^8
+          return fmaxf(fmaxf(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5])),
+                       fmaxf(m8[6], m8[7]));
+        };
+        // the row's max over both halves; the reference max only moves when
+        // it grows by more than 2^8 (log2 domain), so O is rescaled rarely
+        const float m_new = fmaxf(m_run, pair_combine(block_max(), false));
+        if (!ok) break;
         const bool move = (m_new - m_run) * scale_log2 > 8.0f;
         const float m_use = move ? m_new : m_run;
         const float alpha = move ? fast_exp2((m_run - m_new) * scale_log2) : 1.0f;
-        const float mb = m_use * scale_log2;
-        // Rescale O_X when a row's max moved.  PV_X(j-1) is complete: the
-        // commit that signalled S_X(j) was issued after it.
+        // P = exp2(S*c - m) as 16-bit pairs into this half's first 32 S
+        // columns (already read); the row sum adds the fp32 values
+        {
+          const uint64_t sc2 = f2pack(scale_log2, scale_log2);
+          const float mb = m_use * scale_log2;
+          const uint64_t nb2 = f2pack(-mb, -mb);
+          uint64_t acc2[2] = {f2pack(0.0f, 0.0f), f2pack(0.0f, 0.0f)};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int e = c * 16 + 2 * i;
+              float y0, y1, p0, p1;
+              f2unpack(f2fma(f2pack(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, nb2), y0, y1);
+              if ((i & 7) >= 8 - kEmuPairsPer8) {
+                exp2_fma2(y0, y1, p0, p1);  // FMA pipe
+              } else {
+                p0 = fast_exp2(y0);  // MUFU
+                p1 = fast_exp2(y1);
+              }
+              pk[i] = pack2_16<F16>(p0, p1);
+              acc2[i & 1] = f2add(acc2[i & 1], f2pack(p0, p1));
+            }
+            tmem_st_32x32b_x8(s_col + c * 8, pk);
+          }
+          float a, b, c2, d;
+          f2unpack(acc2[0], a, b);
+          f2unpack(acc2[1], c2, d);
+          l_run = l_run * alpha + ((a + b) + (c2 + d));
+          m_run = m_use;
+        }
+        // Rescale this half's O columns when a row's max moved (after the
+        // exponentials, so S no longer occupies registers).  PV_X(j-1) is
+        // complete: the commit that signalled S_X(j) was issued after it.
         if (j > 0 && __any_sync(0xffffffffu, move)) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
-            uint32_t ro[32];
-            tmem_ld_32x32b_x32(o_col + c * 32, ro);
-            tc_wait_ld(ro);
-            uint32_t w0[16], w1[16];
+            uint32_t ro[16];
+            tmem_ld_32x32b_x16(o_col + c * 16, ro);
+            tc_wait_ld16(ro);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              w0[i] = __float_as_uint(__uint_as_float(ro[i]) * alpha);
-              w1[i] = __float_as_uint(__uint_as_float(ro[16 + i]) * alpha);
-            }
-            tmem_st_32x32b_x16(o_col + c * 32, w0);
-            tmem_st_32x32b_x16(o_col + c * 32 + 16, w1);
+            for (int i = 0; i < 16; ++i) ro[i] = __float_as_uint(__uint_as_float(ro[i]) * alpha);
+            tmem_st_32x32b_x16(o_col + c * 16, ro);
           }
         }
-        // pass 2 (double-buffered loads): P = exp2(S*c - m) as 16-bit pairs
-        // into TMEM columns [0, 64) of S_X, i.e. over S columns already
-        // read.  The row sum adds the fp32 values (paired lanes).
-        const uint64_t sc2 = f2pack(scale_log2, scale_log2);
-        const uint64_t nb2 = f2pack(-mb, -mb);
-        uint64_t acc2 = f2pack(0.0f, 0.0f);
-        uint32_t rbuf[2][32];
-        tmem_ld_32x32b_x32(s_col, rbuf[0]);
-        tc_wait_ld(rbuf[0]);
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t (&r)[32] = rbuf[c & 1];
-          if (c + 1 < BN / 32) tmem_ld_32x32b_x32(s_col + (c + 1) * 32, rbuf[(c + 1) & 1]);
-          if (need_mask) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c * 32 + i > lim_rel) r[i] = __float_as_uint(-INFINITY);
-          }
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float y0, y1, p0, p1;
-            f2unpack(f2fma(f2pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nb2),
-                     y0, y1);
-            if ((i & 7) >= 8 - kEmuPairsPer8) {
-              exp2_fma2(y0, y1, p0, p1);  // FMA pipe
-            } else {
-              p0 = fast_exp2(y0);  // MUFU
-              p1 = fast_exp2(y1);
-            }
-            pk[i] = pack2_16<F16>(p0, p1);
-            acc2 = f2add(acc2, f2pack(p0, p1));
-          }
-          tmem_st_32x32b_x16(s_col + c * 16, pk);
-          if (c + 1 < BN / 32) tc_wait_ld(rbuf[(c + 1) & 1]);
-        }
-        float psum_lo, psum_hi;
-        f2unpack(acc2, psum_lo, psum_hi);
-        l_run = l_run * alpha + psum_lo + psum_hi;
-        m_run = m_use;
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -450,65 +475,72 @@ __global__ void __launch_bounds__(THREADS, 1)
         pvc += (uint32_t)nb;
         if (!mbar_wait(&bar->pv_done[X], (pvc - 1) & 1, status)) { ok = false; break; }
         tc_fence_after();
-        const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-        const bool valid = m_row < Sq;
-        if (valid && io.lse)
+        const float l_tot = pair_combine(l_run, true);
+        // the partner has read this warp's slot before staging overwrites it
+        if (!ok || !pair_sync()) { ok = false; break; }
+        const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
+        if (h == 0 && m_row < Sq && io.lse)
           io.lse[(size_t)bh * Sq + m_row] =
-              l_run > 0.0f ? m_run * scale_log2 + __log2f(l_run) : -INFINITY;
-        // O leaves through shared memory: each thread stages its row's
-        // 128-byte chunk (16-byte pieces XOR-swizzled by row, so both the
-        // row-per-thread writes and the row-per-quarter-warp reads hit 32
-        // distinct banks), then every store instruction writes 4 whole
-        // 128-byte row segments instead of 32 scattered 16-byte pieces.
-        uint4 *stage = reinterpret_cast<uint4 *>(smem + C::OFF_STAGE + (warp - 2) * C::STAGE_WARP);
+              l_tot > 0.0f ? m_run * scale_log2 + __log2f(l_tot) : -INFINITY;
+        // O leaves through shared memory: each thread stages a 64-byte
+        // piece of its row (16-byte parts XOR-swizzled by row so the
+        // row-per-thread writes and the 8-rows-per-instruction reads both
+        // hit distinct banks); every store instruction then writes 8 rows x
+        // 64 contiguous bytes instead of 32 scattered 16-byte pieces.
+        uint4 *stage = reinterpret_cast<uint4 *>(stage_raw);
         const uint32_t row0 = it.q0 + X * BM + quarter * 32;  // this warp's first row
-        const int sub = lane & 7;                             // 16-byte piece in a row
+        const int part = lane & 3;
+        auto put = [&](int i, uint4 v) { stage[lane * 4 + (i ^ ((lane >> 1) & 3))] = v; };
         auto flush = [&](auto &&row_ptr) {
           __syncwarp();
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int r = 4 * k + (lane >> 3);
-            const uint4 val = stage[r * 8 + (sub ^ (r & 7))];
-            if (row0 + r < Sq) *(row_ptr(row0 + r) + sub) = val;
+          for (int k = 0; k < 4; ++k) {
+            const int rr = 8 * k + (lane >> 2);
+            const uint4 val = stage[rr * 4 + (part ^ ((rr >> 1) & 3))];
+            if (row0 + rr < Sq) *(row_ptr(row0 + rr) + part) = val;
           }
           __syncwarp();
         };
+        const uint32_t col0 = h * (D / 2);  // first O column of this half
         if (io.out_f32) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < D / 64; ++c) {
             uint32_t r[32];
             tmem_ld_32x32b_x32(o_col + c * 32, r);
             tc_wait_ld(r);
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              stage[lane * 8 + (i ^ (lane & 7))] =
-                  make_uint4(__float_as_uint(__uint_as_float(r[4 * i]) * inv),
-                             __float_as_uint(__uint_as_float(r[4 * i + 1]) * inv),
-                             __float_as_uint(__uint_as_float(r[4 * i + 2]) * inv),
-                             __float_as_uint(__uint_as_float(r[4 * i + 3]) * inv));
-            flush([&](uint32_t m) {
-              return reinterpret_cast<uint4 *>(io.out_f32 + ((size_t)bh * Sq + m) * D + c * 32);
-            });
+            for (int half16 = 0; half16 < 2; ++half16) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int e = half16 * 16 + 4 * i;
+                put(i, make_uint4(__float_as_uint(__uint_as_float(r[e]) * inv),
+                                  __float_as_uint(__uint_as_float(r[e + 1]) * inv),
+                                  __float_as_uint(__uint_as_float(r[e + 2]) * inv),
+                                  __float_as_uint(__uint_as_float(r[e + 3]) * inv)));
+              }
+              flush([&](uint32_t m) {
+                return reinterpret_cast<uint4 *>(io.out_f32 + ((size_t)bh * Sq + m) * D + col0 +
+                                                 c * 32 + half16 * 16);
+              });
+            }
           }
         }
         if (io.out_bf16) {
 #pragma unroll 1
           for (int c = 0; c < D / 64; ++c) {
-            uint32_t r[64];
-            tmem_ld_32x32b_x32(o_col + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-            tmem_ld_32x32b_x32(o_col + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-            tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-            tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(o_col + c * 32, r);
+            tc_wait_ld(r);
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              stage[lane * 8 + (i ^ (lane & 7))] = make_uint4(
+            for (int i = 0; i < 4; ++i)
+              put(i, make_uint4(
                   pack2_16<F16>(__uint_as_float(r[8 * i]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
                   pack2_16<F16>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
                   pack2_16<F16>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
-                  pack2_16<F16>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
+                  pack2_16<F16>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv)));
             flush([&](uint32_t m) {
               return reinterpret_cast<uint4 *>(io.out_bf16 + ((size_t)(bh / io.H) * Sq + m) * io.ldo +
-                                               (size_t)(bh % io.H) * D + c * 64);
+                                               (size_t)(bh % io.H) * D + col0 + c * 32);
             });
           }
         }
@@ -522,7 +554,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == W_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
