@@ -6,9 +6,9 @@
 // B that ping-pong: while the softmax warps of one tile turn its S into P, the
 // tensor core works on the other tile.  Per 128-key block j:
 //   S_X = Q_X K_j^T          tcgen05 M=128 N=128 K=16 (Q, K K-major, bf16)
-//   P_X = exp2(S_X*c - m)    softmax warps, two threads per row (64 keys
-//                            each); P as bf16 pairs written back into S_X's
-//                            TMEM columns
+//   P_X = exp2(S_X*c - m)    softmax warps, four threads per row (32 keys
+//                            each, 16-lane TMEM shapes); P as bf16 pairs
+//                            written back into S_X's TMEM columns
 //   O_X += P_X V_j           tcgen05 M=128 N=D K=16, A = P from TMEM,
 //                            B = V MN-major from smem
 // S_A, S_B, O_A, O_B live in TMEM (4 x 128 columns for D = 128).  The running
@@ -19,10 +19,10 @@
 // head's K / V is read from DRAM once and shared through L2.
 //
 // Warp roles (576 threads): warps 0-7 softmax of tile A, warps 8-15
-// softmax of tile B (warp w reads TMEM lanes 32*(w%4)..; two warps per lane
-// quarter split the keys and O columns), warp 16 TMA producer (Q once; K
-// and V double-buffered, 3-D tensor maps so ragged S zero-fills per head),
-// warp 17 TMEM allocator + single-thread MMA issuer.
+// softmax of tile B (warp w reads TMEM lanes 32*(w%4)..; the two warps of a
+// lane quarter take 16 rows each), warp 16 TMA producer (Q once; K and V
+// double-buffered, 3-D tensor maps so ragged S zero-fills per head), warp
+// 17 TMEM allocator + single-thread MMA issuer.
 // MMA issue order per block: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1), so one
 // tile's softmax always overlaps the other tile's MMAs.
 //
@@ -49,10 +49,7 @@ struct Cfg {
   static constexpr int OFF_Q = 0;           // 2 tiles
   static constexpr int OFF_K = 2 * TILE;    // 2 stages
   static constexpr int OFF_V = 4 * TILE;    // 2 stages
-  // epilogue staging: 32 rows x 128 B per softmax warp
-  static constexpr int OFF_STAGE = 6 * TILE;
-  static constexpr int STAGE_WARP = 32 * 64;
-  static constexpr int OFF_BAR = OFF_STAGE + 16 * STAGE_WARP;
+  static constexpr int OFF_BAR = 6 * TILE;
   static constexpr int SMEM = OFF_BAR + 512 + 1024;
   static constexpr uint32_t TMEM_S = 0;        // S_A at 0, S_B at 128
   static constexpr uint32_t TMEM_O = 2 * BN;   // O_A at 256, O_B at 256 + D
@@ -69,7 +66,6 @@ struct Bars {
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], o_free[2];
   uint64_t sched_full[2], sched_empty[2];
-  uint64_t pair[8];  // the two halves of a tile's lane quarter: one phase per exchange
   uint64_t drain;
   int item[2];
   uint32_t tmem;
@@ -141,7 +137,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&bar->sched_full[s], 1);
       mbar_init(&bar->sched_empty[s], 17);  // MMA thread + 16 softmax warps
     }
-    for (int p = 0; p < 8; ++p) mbar_init(&bar->pair[p], 2);
     mbar_init(&bar->drain, 1);
     bar->abort_flag = 0;
     fence_mbar_init();
@@ -230,16 +225,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_commit(&bar->s_full[X]);
       };
-      // O_X (+)= P_X V with P_X read from TMEM (16-bit pairs: keys
-      // [64h, 64h + 64) in S_X columns [64h, 64h + 32), 16 keys = 8 columns
-      // per MMA) and V from smem slot vslot
+      // O_X (+)= P_X V with P_X read from TMEM (16-bit pairs in key order
+      // in the first 64 columns of S_X: 16 keys = 8 columns per MMA) and V
+      // from smem slot vslot
       auto issue_pv = [&](int X, int vslot, bool first) {
         const uint64_t vd = desc_add(dv, (uint32_t)vslot * C::TILE);
         const uint32_t pt = tmem + C::TMEM_S + X * BN;
         const uint32_t d_tmem = tmem + C::TMEM_O + X * D;
 #pragma unroll
         for (int ks = 0; ks < BN / 16; ++ks)
-          tc_mma_f16_ts(d_tmem, pt + (ks >> 2) * 64 + (ks & 3) * 8, desc_add(vd, ks * 2048), C::IDESC_PV,
+          tc_mma_f16_ts(d_tmem, pt + ks * 8, desc_add(vd, ks * 2048), C::IDESC_PV,
                         (!first || ks > 0) ? 1u : 0u);
         tc_commit(&bar->pv_done[X]);
       };
@@ -317,47 +312,31 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp < W_PROD) {
     // --------------------------------------------------- softmax + epilogue
-    // Two warps share each 32-row lane quarter of a tile: half h takes keys
-    // [64h, 64h + 64) of every block (and writes their P into the first 32
-    // of its own 64 S columns) and O columns [h D/2, (h+1) D/2).  The halves
-    // agree on the row's reference max through shared memory (one
-    // mbarrier-paced exchange per block); their row sums meet once, in the
-    // epilogue.
-    const int sw = warp;                  // softmax warp 0..15
-    const int X = sw >> 3;                // query tile
-    const int h = (sw >> 2) & 1;          // key / O-column half
-    const int quarter = warp & 3;         // TMEM lanes 32*quarter ..
-    const int row = quarter * 32 + lane;
-    uint64_t *pair_bar = &bar->pair[X * 4 + quarter];
-    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const uint32_t s_col = tmem + lane_base + C::TMEM_S + X * BN + h * 64;
-    const uint32_t o_col = tmem + lane_base + C::TMEM_O + X * D + h * (D / 2);
-    // per-warp 2 KB: epilogue staging, and (outside the epilogue) two
-    // 32-float exchange slots the partner half reads
-    uint8_t *stage_raw = smem + C::OFF_STAGE + sw * C::STAGE_WARP;
-    const float *peer_xch =
-        reinterpret_cast<const float *>(smem + C::OFF_STAGE + (sw ^ 4) * C::STAGE_WARP);
+    // Eight warps per tile, two per TMEM lane quarter: warp (q, h) owns the
+    // 16 rows 32q + 16h .. + 15 and reads them with the 16-lane shapes.
+    // Thread t holds rows ra = base + t/4 and rb = ra + 8 and, of every
+    // 8-column group k, columns 8k + 2(t%4) and + 1: a row is spread over
+    // the 4 threads t/4 alike, so its max and sum are two shuffles and the
+    // warps share nothing.  P goes back as 16-bit pairs with 16x128b, which
+    // puts pair (8k + 2(t%4)) / 2 = 4k + t%4 of each row at that column:
+    // the packed P in key order in S_X's first 64 columns.
+    const int X = warp >> 3;                                  // query tile
+    const int quarter = warp & 3;                             // TMEM lane quarter
+    const int lane0 = quarter * 32 + ((warp >> 2) & 1) * 16;  // first row of this warp
+    const int ra = lane0 + (lane >> 2);                       // rows of this thread (in the tile)
+    const int cpair = 2 * (lane & 3);  // column offset within each 8-column group
+    const uint32_t lane_base = (uint32_t)lane0 << 16;
+    const uint32_t s_col = tmem + lane_base + C::TMEM_S + X * BN;
+    const uint32_t o_col = tmem + lane_base + C::TMEM_O + X * D;
+    auto quad_max = [](float v) {
+      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+      return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+    };
+    auto quad_sum = [](float v) {
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      return v + __shfl_xor_sync(0xffffffffu, v, 2);
+    };
     bool ok = true;
-    uint32_t xc = 0;  // exchanges so far (slot and phase parity = xc & 1)
-    // Max or sum of v over the two halves of this row.  Slots are
-    // double-buffered: a warp rewrites a slot two exchanges later, and the
-    // exchange in between completes only after the partner arrived for it,
-    // i.e. after it read the slot.  The wait is bounded like every other:
-    // on expiry ok turns false and the warp unwinds.
-    auto pair_sync = [&]() {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(pair_bar);
-      const bool done = mbar_wait(pair_bar, xc & 1, status);
-      ++xc;
-      return done;
-    };
-    auto pair_combine = [&](float v, bool sum) {
-      reinterpret_cast<float *>(stage_raw)[(xc & 1) * 32 + lane] = v;
-      const int slot = (int)(xc & 1) * 32;
-      if (!pair_sync()) ok = false;
-      const float o = peer_xch[slot + lane];
-      return sum ? v + o : fmaxf(v, o);
-    };
     uint32_t sc = 0;   // S_X blocks consumed
     uint32_t pvc = 0;  // PV_X MMAs before this item
     for (uint32_t seq = 0; ok; ++seq) {
@@ -369,9 +348,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (w < 0) break;
       const Item it = decode_item(w, pairs, Sq, Skv, causal);
       const uint32_t bh = it.bh;
-      const uint32_t m_row = it.q0 + X * BM + row;  // query index
+      const uint32_t qa = it.q0 + X * BM + ra, qb = qa + 8;  // query indices
+      // last visible key of each row
+      const uint32_t lim_a = causal && qa < Skv - 1 ? qa : Skv - 1;
+      const uint32_t lim_b = causal && qb < Skv - 1 ? qb : Skv - 1;
       const int nb = it.nblk[X];
-      float m_run = -INFINITY, l_run = 0.0f;
+      float m_a = -INFINITY, m_b = -INFINITY;  // reference maxima (scaled units)
+      float l_a = 0.0f, l_b = 0.0f;            // this thread's share of the row sums
       for (int j = 0; j < nb && ok; ++j) {
         if (*abort_flag || !mbar_wait(&bar->s_full[X], sc & 1, status)) {
           ok = false;
@@ -379,86 +362,100 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         ++sc;
         tc_fence_after();
+        // r[32h + 4k + e]: columns 64h + 8k + cpair + (e & 1); e < 2 row
+        // ra, e >= 2 row rb
         uint32_t r[64];
-        tmem_ld_32x32b_x32(s_col, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-        tmem_ld_32x32b_x32(s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tmem_ld_16x256b_x8(s_col, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld_16x256b_x8(s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-        // keys n0 + i; blocks that need no mask take a branch-free path,
-        // masked ones compare each key with one limit
-        const uint32_t n0 = (uint32_t)j * BN + h * 64;
-        uint32_t lim = Skv - 1;                       // last visible key
-        if (causal && m_row < lim) lim = m_row;
-        if (n0 + 63 > lim) {
-          const int lim_rel = (int)lim - (int)n0;     // visible iff index <= lim_rel
+        const uint32_t n0 = (uint32_t)j * BN;
+        if (n0 + BN - 1 > (lim_a < lim_b ? lim_a : lim_b)) {
+          // visible iff n0 + column <= lim
+          const int rel_a = (int)lim_a - (int)n0 - cpair, rel_b = (int)lim_b - (int)n0 - cpair;
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i > lim_rel) r[i] = __float_as_uint(-INFINITY);
+          for (int v = 0; v < 64; ++v) {
+            const int col = 8 * (v >> 2) + (v & 1);  // column - cpair
+            if (col > ((v & 2) ? rel_b : rel_a)) r[v] = __float_as_uint(-INFINITY);
+          }
         }
-        auto block_max = [&]() {
-          float m8[8];
+        float mxa, mxb;
+        {
+          float a4[4], b4[4];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) m8[k] = max3(__uint_as_float(r[k]), __uint_as_float(r[8 + k]),
-                                                   __uint_as_float(r[16 + k]));
+          for (int i = 0; i < 4; ++i) {
+            a4[i] = __uint_as_float(r[4 * i]);
+            b4[i] = __uint_as_float(r[4 * i + 2]);
+          }
 #pragma unroll
-          for (int i = 24; i < 64; i += 16)
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-              m8[k] = max3(m8[k], __uint_as_float(r[i + k]), __uint_as_float(r[i + 8 + k]));
-          return fmaxf(fmaxf(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5])),
-                       fmaxf(m8[6], m8[7]));
-        };
-        // the row's max over both halves; the reference max only moves when
-        // it grows by more than 2^8 (log2 domain), so O is rescaled rarely
-        const float m_new = fmaxf(m_run, pair_combine(block_max(), false));
-        if (!ok) break;
-        const bool move = (m_new - m_run) * scale_log2 > 8.0f;
-        const float m_use = move ? m_new : m_run;
-        const float alpha = move ? fast_exp2((m_run - m_new) * scale_log2) : 1.0f;
-        // P = exp2(S*c - m) as 16-bit pairs into this half's first 32 S
-        // columns (already read); the row sum adds the fp32 values
+          for (int v = 0; v < 64; v += 4) {
+            const int i = (v >> 2) & 3;
+            a4[i] = max3(a4[i], __uint_as_float(r[v]), __uint_as_float(r[v + 1]));
+            b4[i] = max3(b4[i], __uint_as_float(r[v + 2]), __uint_as_float(r[v + 3]));
+          }
+          mxa = quad_max(fmaxf(fmaxf(a4[0], a4[1]), fmaxf(a4[2], a4[3])));
+          mxb = quad_max(fmaxf(fmaxf(b4[0], b4[1]), fmaxf(b4[2], b4[3])));
+        }
+        // the reference max only moves when it grows by more than 2^8
+        // (log2 domain), so O is rescaled rarely
+        const float na = fmaxf(m_a, mxa), nb_ = fmaxf(m_b, mxb);
+        const bool mva = (na - m_a) * scale_log2 > 8.0f, mvb = (nb_ - m_b) * scale_log2 > 8.0f;
+        const float ua = mva ? na : m_a, ub = mvb ? nb_ : m_b;
+        const float alpha_a = mva ? fast_exp2((m_a - na) * scale_log2) : 1.0f;
+        const float alpha_b = mvb ? fast_exp2((m_b - nb_) * scale_log2) : 1.0f;
+        // P = exp2(S*c - m) as 16-bit pairs; the row sums add the fp32 values
         {
           const uint64_t sc2 = f2pack(scale_log2, scale_log2);
-          const float mb = m_use * scale_log2;
-          const uint64_t nb2 = f2pack(-mb, -mb);
-          uint64_t acc2[2] = {f2pack(0.0f, 0.0f), f2pack(0.0f, 0.0f)};
+          const uint64_t nba = f2pack(-ua * scale_log2, -ua * scale_log2);
+          const uint64_t nbb = f2pack(-ub * scale_log2, -ub * scale_log2);
+          uint64_t acc_a = f2pack(0.0f, 0.0f), acc_b = f2pack(0.0f, 0.0f);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t pk[8];
+          for (int hf = 0; hf < 2; ++hf) {
+            uint32_t pk[16];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int e = c * 16 + 2 * i;
-              float y0, y1, p0, p1;
-              f2unpack(f2fma(f2pack(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, nb2), y0, y1);
-              if ((i & 7) >= 8 - kEmuPairsPer8) {
-                exp2_fma2(y0, y1, p0, p1);  // FMA pipe
+            for (int k = 0; k < 8; ++k) {
+              const int v = hf * 32 + 4 * k;
+              float y0, y1, y2, y3, p0, p1, p2, p3;
+              f2unpack(f2fma(f2pack(__uint_as_float(r[v]), __uint_as_float(r[v + 1])), sc2, nba), y0, y1);
+              f2unpack(f2fma(f2pack(__uint_as_float(r[v + 2]), __uint_as_float(r[v + 3])), sc2, nbb), y2, y3);
+              // of every 8 pairs, kEmuPairsPer8 take the FMA pipe
+              if ((2 * (k & 3)) >= 8 - kEmuPairsPer8) {
+                exp2_fma2(y0, y1, p0, p1);
+                exp2_fma2(y2, y3, p2, p3);
               } else {
                 p0 = fast_exp2(y0);  // MUFU
                 p1 = fast_exp2(y1);
+                p2 = fast_exp2(y2);
+                p3 = fast_exp2(y3);
               }
-              pk[i] = pack2_16<F16>(p0, p1);
-              acc2[i & 1] = f2add(acc2[i & 1], f2pack(p0, p1));
+              pk[2 * k] = pack2_16<F16>(p0, p1);
+              pk[2 * k + 1] = pack2_16<F16>(p2, p3);
+              acc_a = f2add(acc_a, f2pack(p0, p1));
+              acc_b = f2add(acc_b, f2pack(p2, p3));
             }
-            tmem_st_32x32b_x8(s_col + c * 8, pk);
+            tmem_st_16x128b_x8(s_col + hf * 32, pk);
           }
-          float a, b, c2, d;
-          f2unpack(acc2[0], a, b);
-          f2unpack(acc2[1], c2, d);
-          l_run = l_run * alpha + ((a + b) + (c2 + d));
-          m_run = m_use;
+          float a0, a1, b0, b1;
+          f2unpack(acc_a, a0, a1);
+          f2unpack(acc_b, b0, b1);
+          l_a = l_a * alpha_a + (a0 + a1);
+          l_b = l_b * alpha_b + (b0 + b1);
+          m_a = ua;
+          m_b = ub;
         }
-        // Rescale this half's O columns when a row's max moved (after the
-        // exponentials, so S no longer occupies registers).  PV_X(j-1) is
-        // complete: the commit that signalled S_X(j) was issued after it.
-        if (j > 0 && __any_sync(0xffffffffu, move)) {
+        // Rescale O's rows whose max moved (after the exponentials, so S no
+        // longer occupies registers).  PV_X(j-1) is complete: the commit
+        // that signalled S_X(j) was issued after it.
+        if (j > 0 && __any_sync(0xffffffffu, mva || mvb)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t ro[16];
-            tmem_ld_32x32b_x16(o_col + c * 16, ro);
-            tc_wait_ld16(ro);
+          for (int c = 0; c < D / 64; ++c) {
+            uint32_t ro[32];
+            tmem_ld_16x256b_x8(o_col + c * 64, ro);
+            tc_wait_ld(ro);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) ro[i] = __float_as_uint(__uint_as_float(ro[i]) * alpha);
-            tmem_st_32x32b_x16(o_col + c * 16, ro);
+            for (int v = 0; v < 32; ++v)
+              ro[v] = __float_as_uint(__uint_as_float(ro[v]) * ((v & 2) ? alpha_b : alpha_a));
+            tmem_st_16x256b_x8(o_col + c * 64, ro);
           }
         }
         tc_wait_st();
@@ -475,73 +472,46 @@ __global__ void __launch_bounds__(THREADS, 1)
         pvc += (uint32_t)nb;
         if (!mbar_wait(&bar->pv_done[X], (pvc - 1) & 1, status)) { ok = false; break; }
         tc_fence_after();
-        const float l_tot = pair_combine(l_run, true);
-        // the partner has read this warp's slot before staging overwrites it
-        if (!ok || !pair_sync()) { ok = false; break; }
-        const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
-        if (h == 0 && m_row < Sq && io.lse)
-          io.lse[(size_t)bh * Sq + m_row] =
-              l_tot > 0.0f ? m_run * scale_log2 + __log2f(l_tot) : -INFINITY;
-        // O leaves through shared memory: each thread stages a 64-byte
-        // piece of its row (16-byte parts XOR-swizzled by row so the
-        // row-per-thread writes and the 8-rows-per-instruction reads both
-        // hit distinct banks); every store instruction then writes 8 rows x
-        // 64 contiguous bytes instead of 32 scattered 16-byte pieces.
-        uint4 *stage = reinterpret_cast<uint4 *>(stage_raw);
-        const uint32_t row0 = it.q0 + X * BM + quarter * 32;  // this warp's first row
-        const int part = lane & 3;
-        auto put = [&](int i, uint4 v) { stage[lane * 4 + (i ^ ((lane >> 1) & 3))] = v; };
-        auto flush = [&](auto &&row_ptr) {
-          __syncwarp();
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int rr = 8 * k + (lane >> 2);
-            const uint4 val = stage[rr * 4 + (part ^ ((rr >> 1) & 3))];
-            if (row0 + rr < Sq) *(row_ptr(row0 + rr) + part) = val;
-          }
-          __syncwarp();
-        };
-        const uint32_t col0 = h * (D / 2);  // first O column of this half
-        if (io.out_f32) {
+        const float la = quad_sum(l_a), lb = quad_sum(l_b);
+        const float inv_a = la > 0.0f ? 1.0f / la : 0.0f, inv_b = lb > 0.0f ? 1.0f / lb : 0.0f;
+        const bool va = qa < Sq, vb = qb < Sq;
+        if (io.lse && (lane & 3) == 0) {
+          if (va) io.lse[(size_t)bh * Sq + qa] = la > 0.0f ? m_a * scale_log2 + __log2f(la) : -INFINITY;
+          if (vb) io.lse[(size_t)bh * Sq + qb] = lb > 0.0f ? m_b * scale_log2 + __log2f(lb) : -INFINITY;
+        }
+        // Each store instruction writes 8 rows x 4 threads x one column
+        // pair: 8 whole 32-byte sectors for fp32.
 #pragma unroll 1
-          for (int c = 0; c < D / 64; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(o_col + c * 32, r);
-            tc_wait_ld(r);
+        for (int c = 0; c < D / 64; ++c) {
+          uint32_t ro[32];
+          tmem_ld_16x256b_x8(o_col + c * 64, ro);
+          tc_wait_ld(ro);
+          if (io.out_f32) {
+            float *oa = io.out_f32 + ((size_t)bh * Sq + qa) * D + c * 64 + cpair;
+            float *ob = oa + 8 * (size_t)D;
 #pragma unroll
-            for (int half16 = 0; half16 < 2; ++half16) {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int e = half16 * 16 + 4 * i;
-                put(i, make_uint4(__float_as_uint(__uint_as_float(r[e]) * inv),
-                                  __float_as_uint(__uint_as_float(r[e + 1]) * inv),
-                                  __float_as_uint(__uint_as_float(r[e + 2]) * inv),
-                                  __float_as_uint(__uint_as_float(r[e + 3]) * inv)));
-              }
-              flush([&](uint32_t m) {
-                return reinterpret_cast<uint4 *>(io.out_f32 + ((size_t)bh * Sq + m) * D + col0 +
-                                                 c * 32 + half16 * 16);
-              });
+            for (int k = 0; k < 8; ++k) {
+              if (va)
+                __stcs(reinterpret_cast<float2 *>(oa + 8 * k),
+                       make_float2(__uint_as_float(ro[4 * k]) * inv_a, __uint_as_float(ro[4 * k + 1]) * inv_a));
+              if (vb)
+                __stcs(reinterpret_cast<float2 *>(ob + 8 * k),
+                       make_float2(__uint_as_float(ro[4 * k + 2]) * inv_b, __uint_as_float(ro[4 * k + 3]) * inv_b));
             }
           }
-        }
-        if (io.out_bf16) {
-#pragma unroll 1
-          for (int c = 0; c < D / 64; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(o_col + c * 32, r);
-            tc_wait_ld(r);
+          if (io.out_bf16) {
+            const size_t head_col = (size_t)(bh % io.H) * D + c * 64 + cpair;
+            uint16_t *oa = io.out_bf16 + ((size_t)(bh / io.H) * Sq + qa) * io.ldo + head_col;
+            uint16_t *ob = oa + 8 * (size_t)io.ldo;
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              put(i, make_uint4(
-                  pack2_16<F16>(__uint_as_float(r[8 * i]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
-                  pack2_16<F16>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
-                  pack2_16<F16>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
-                  pack2_16<F16>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv)));
-            flush([&](uint32_t m) {
-              return reinterpret_cast<uint4 *>(io.out_bf16 + ((size_t)(bh / io.H) * Sq + m) * io.ldo +
-                                               (size_t)(bh % io.H) * D + col0 + c * 32);
-            });
+            for (int k = 0; k < 8; ++k) {
+              if (va)
+                *reinterpret_cast<uint32_t *>(oa + 8 * k) =
+                    pack2_16<F16>(__uint_as_float(ro[4 * k]) * inv_a, __uint_as_float(ro[4 * k + 1]) * inv_a);
+              if (vb)
+                *reinterpret_cast<uint32_t *>(ob + 8 * k) =
+                    pack2_16<F16>(__uint_as_float(ro[4 * k + 2]) * inv_b, __uint_as_float(ro[4 * k + 3]) * inv_b);
+            }
           }
         }
       }
