@@ -29,6 +29,14 @@ struct BwppCudaCtx {
   size_t workspace_bytes;
   int user_workspace;      // 1: set by bwpp_cuda_ctx_set_workspace, not freed
   int num_sms;
+  // Split-tail scratch of the tensor-core GEMM (allocated on first use, not
+  // when the caller owns the workspace): fp32 partial sums of tiles cut into
+  // K parts, and per-(slot, CTA, lane quarter) ready flags that hold the
+  // epoch of the launch that last published them.
+  float *gemm_partials;
+  uint32_t *gemm_flags;
+  uint32_t gemm_epoch;
+  int gemm_scratch_failed;
   char last_error[256];
 };
 
@@ -144,6 +152,37 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
   }
 }
 
+// ---- flags in global memory between CTAs of one launch ---------------------
+
+__device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits until *p == want (acquire: the publisher's earlier writes are then
+// visible to this thread).  Bounded like mbar_wait.
+__device__ __forceinline__ bool flag_wait(const uint32_t *p, uint32_t want, int *status,
+                                          uint64_t limit_ns = BWPP_WAIT_LIMIT_NS) {
+  if (ld_acquire_gpu(p) == want) return true;
+  const uint64_t t0 = bwpp_globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      if (ld_acquire_gpu(p) == want) return true;
+      __nanosleep(100);
+    }
+    if (bwpp_globaltimer() - t0 > limit_ns) {
+      bwpp_report(status, BWPP_CUDA_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // ---- TMA: each copy targets the issuing CTA only --------------------------
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,
@@ -183,6 +222,32 @@ __device__ __forceinline__ void tma_store_wait_all() {
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- per-thread asynchronous 16-byte copies global -> shared ---------------
+
+__device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Waits until at most `pending` (0..7) of this thread's committed groups are
+// still in flight.
+__device__ __forceinline__ void cp_async_wait_pending(int pending) {
+  switch (pending) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+    case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+    case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
+  }
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {

@@ -161,6 +161,7 @@ int bwpp_cuda_ctx_destroy(BwppCudaCtx *ctx) {
   bwpp_ctx_enter(ctx);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->workspace && !ctx->user_workspace) cudaFree(ctx->workspace);
+  if (ctx->gemm_partials) cudaFree(ctx->gemm_partials);
   if (ctx->status_word) cudaFree(ctx->status_word);
   free(ctx);
   return BWPP_CUDA_OK;

@@ -9,7 +9,7 @@
 // (b[n*ldb+k], i.e. a transposed weight).  The MN-major forms let the
 // autodiff products (dX = dY W^T, dW = X^T dY) run without transposes.
 //
-// Persistent, warp-specialised kernel (192 threads per CTA), in two forms:
+// Persistent, warp-specialised kernel (320 threads per CTA), in two forms:
 //   CTA pair (cluster of 2, tcgen05 cta_group::2), used when M > 128: the
 //     pair computes a 256 x 256 tile; each CTA loads 128 rows of A and 128
 //     columns of B per K step (32 KB, 6-stage ring) into its own shared
@@ -23,11 +23,20 @@
 //   warp 0       TMA producer, 128-byte swizzle
 //   warp 1       TMEM allocator + single-thread tcgen05.mma issuer; commits
 //                free the smem stage / publish the accumulator
-//   warps 2..5   epilogue: tcgen05.ld 32 lanes x 32 columns, +bias, SiLU,
-//                +residual, swizzled smem staging, TMA store (double-buffered)
+//   warps 2..9   epilogue, two warps per TMEM lane quarter taking alternate
+//                32-column chunks: tcgen05.ld 32 lanes x 32 columns, +bias
+//                (held in registers per tile, shuffled out), SiLU, +residual,
+//                swizzled smem staging, TMA store.  One warp per quarter left
+//                the SiLU latency-bound (12 us per fp32 tile, 7.6 us now).
 // Two 256-column fp32 accumulators in TMEM (512 columns): the epilogue of
 // tile i overlaps the main loop of tile i+1.  Tiles are rasterised in groups
 // of 8 M-blocks so CTAs running together share B panels in L2.
+// The main loop is bound by operand traffic from L2 into shared memory:
+// a CTA loads 32 KB per 64-deep K step of a pair tile at about 80 GB/s per
+// SM (~400 ns) against ~340 ns of MMA at the 1.5 GHz the part runs at under
+// this load (ncu: tensor pipe 82% active), so the tile shape, not the MMA
+// issue rate, sets the kernel's speed.
+// The wave tail is cut into K parts that run in one round (see GemmWork).
 //
 // Every wait is bounded (BWPP_WAIT_LIMIT_NS); an expired wait records
 // BWPP_CUDA_ERR_TIMEOUT, all roles unwind, TMEM is freed and the kernel ends.
@@ -43,7 +52,7 @@ namespace {
 constexpr int BM = 128, BN = 256, BK = 64;  // BM: rows per CTA; BN: accumulator width
 constexpr int A_STAGE = BM * BK * 2;        // 16 KB
 constexpr int B_SUB = 64 * BK * 2;          // 8 KB: 64 MN-columns x 64 K-rows
-constexpr int EPI_WARPS = 4;
+constexpr int EPI_WARPS = 8;   // two per TMEM lane quarter
 constexpr int EPI_COLS = 32;                // columns per TMEM load / store
 constexpr int EPI_BUF = 32 * EPI_COLS * 4;  // 4 KB: 32 rows x 128 B
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
@@ -59,10 +68,9 @@ struct GemmCfg {
   static constexpr int BN_LOAD = PAIR ? 128 : 256;  // B columns this CTA loads
   static constexpr int STAGES = PAIR ? 6 : 4;
   static constexpr int B_STAGE = BN_LOAD * BK * 2;
-  static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
   static constexpr int OFF_B = STAGES * A_STAGE;
   static constexpr int OFF_C = OFF_B + STAGES * B_STAGE;
-  static constexpr int OFF_BAR = OFF_C + EPI_WARPS * 2 * EPI_BUF;
+  static constexpr int OFF_BAR = OFF_C + EPI_WARPS * EPI_BUF;  // one staging buffer per warp
   static constexpr int SMEM_ALLOC = OFF_BAR + 256 + 1024;  // + slack for 1024-B alignment
   static constexpr uint32_t TILE_M = PAIR ? 2 * BM : BM;
   static_assert(SMEM_ALLOC <= 232448, "exceeds the 227 KB opt-in limit");
@@ -79,14 +87,43 @@ struct GemmEpi {
   int res16;              // residual element type: 0 fp32, 1 bf16, 2 f16
 };
 
-// Work items of a launch, in rasterised tile order: items below split_begin
-// are whole tiles; from split_begin on, each remaining tile is cut into two
-// N halves (MMA N = BN / 2), so a short last wave spreads over twice as many
-// CTAs.  Item i >= split_begin is half (i - split_begin) % 2 of tile
+// Work of a launch, handed out round-robin to `workers` workers (CTA pairs,
+// or CTAs): worker w takes items w, w + workers, w + 2 workers, ...
+// Items [0, items) are tiles in rasterised order.  Items below split_begin
+// are whole tiles; from split_begin on, each remaining tile is cut into two N
+// halves (MMA N = BN / 2), so a short last wave spreads over twice as many
+// workers.  Item i >= split_begin is half (i - split_begin) % 2 of tile
 // split_begin + (i - split_begin) / 2.
+// Split tail (sk_parts > 1): the sk_tiles tiles after the full waves are cut
+// into sk_parts K ranges, and items [items, items + sk_tiles * sk_parts)
+// hold them part-major (all tiles' part 0, then all tiles' part 1, ...);
+// sk_tiles * sk_parts <= workers, so the whole tail is one round: every part
+// of a tile runs at the same time, each as its worker's last item.  The
+// tile's output is shared out like a reduce-scatter: each epilogue warp's
+// k-th chunk belongs to part k % sk_parts.  A part first writes its fp32
+// partial sums of the chunks other parts own to its slot of `partials` and
+// publishes them, then waits for the other parts' flags, adds their partials
+// of its own chunks (in part order) and runs the epilogue on those chunks.
+// Publishing comes before waiting in every part, so no part waits on one
+// that waits on it.
 struct GemmWork {
   uint32_t split_begin;
   uint32_t items;
+  uint32_t workers;
+  uint32_t sk_tile0;   // first split tile (= items)
+  uint32_t sk_tiles;   // 0: no split tail
+  uint32_t sk_parts;
+  uint32_t epoch;      // flag value published by this launch
+  float *partials;     // [slot][TILE_M][BN] fp32, in TMEM chunk order
+  uint32_t *flags;     // [slot][2 CTAs][EPI_WARPS]
+};
+
+// One work item: a tile (or tile half) and the K blocks [kb0, kb1) of it.
+struct GemmItem {
+  uint32_t mb, nb, n_off, wn, kb0, kb1;
+  uint32_t role;       // 0 whole tile (or half), 3 split part
+  uint32_t part;       // split part: its K range index
+  uint32_t slot;       // split part: slot of part 0 of its tile (part p: slot + p)
 };
 
 __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m,
@@ -99,6 +136,40 @@ __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m,
   const uint32_t r = t - g * per_group;
   mb = first_m + r % gm;
   nb = r / gm;
+}
+
+// The item with round-robin index `it`; false past the last item.
+__device__ __forceinline__ bool get_item(const GemmWork &w, uint32_t tiles_m, uint32_t tiles_n,
+                                         uint32_t num_kb, uint32_t it, GemmItem &x) {
+  if (it < w.items) {
+    uint32_t t = it, half = 0;
+    x.wn = BN;
+    if (it >= w.split_begin) {
+      t = w.split_begin + (it - w.split_begin) / 2;
+      half = (it - w.split_begin) & 1;
+      x.wn = BN / 2;
+    }
+    tile_coords(t, tiles_m, tiles_n, x.mb, x.nb);
+    x.n_off = half * (BN / 2);
+    x.kb0 = 0;
+    x.kb1 = num_kb;
+    x.role = 0;
+    x.part = 0;
+    x.slot = 0;
+    return true;
+  }
+  const uint32_t j = it - w.items;
+  if (j >= w.sk_tiles * w.sk_parts) return false;
+  const uint32_t part = j / w.sk_tiles, tr = j - part * w.sk_tiles;
+  tile_coords(w.sk_tile0 + tr, tiles_m, tiles_n, x.mb, x.nb);
+  x.n_off = 0;
+  x.wn = BN;
+  x.kb0 = part * num_kb / w.sk_parts;
+  x.kb1 = (part + 1) * num_kb / w.sk_parts;
+  x.role = 3;
+  x.part = part;
+  x.slot = tr * w.sk_parts;
+  return true;
 }
 
 template <bool A_MN, bool B_MN, bool PAIR>
@@ -127,22 +198,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // rank 0 of a pair issues the MMAs and owns the barriers both CTAs feed
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
-  const uint32_t first_tile = PAIR ? cluster_id_x() : blockIdx.x;
-  const uint32_t tile_step = PAIR ? cluster_count_x() : gridDim.x;
+  const uint32_t worker = PAIR ? cluster_id_x() : blockIdx.x;
   const uint32_t tiles_m = (M + Cfg::TILE_M - 1) / Cfg::TILE_M, tiles_n = (N + BN - 1) / BN;
   const uint32_t num_kb = (K + BK - 1) / BK;
-  // tile of work item `it`, the first accumulator column it owns and its width
-  auto item = [&](uint32_t it, uint32_t &mb, uint32_t &nb, uint32_t &n_off, uint32_t &wn) {
-    uint32_t t = it, half = 0;
-    wn = BN;
-    if (it >= work.split_begin) {
-      t = work.split_begin + (it - work.split_begin) / 2;
-      half = (it - work.split_begin) & 1;
-      wn = BN / 2;
-    }
-    tile_coords(t, tiles_m, tiles_n, mb, nb);
-    n_off = half * (BN / 2);
-  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -178,22 +236,23 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
-      for (uint32_t it = first_tile; it < work.items && !*abort_flag; it += tile_step) {
-        uint32_t mb, nb, n_off, wn;
-        item(it, mb, nb, n_off, wn);
-        // A half tile loads the same boxes (the unused columns past its half
-        // are fetched and ignored), shifted to its N range; in a pair each
-        // CTA holds wn / 2 of the MMA's columns.
-        const int32_t row0 = (int32_t)(mb * Cfg::TILE_M + rank * BM);
-        const int32_t col0 = (int32_t)(nb * BN + n_off + rank * (PAIR ? wn / 2 : 0));
-        for (uint32_t kb = 0; kb < num_kb; ++kb) {
+      GemmItem x;
+      for (uint32_t it = worker;
+           !*abort_flag && get_item(work, tiles_m, tiles_n, num_kb, it, x); it += work.workers) {
+        // In a pair each CTA holds wn / 2 of the MMA's columns.
+        const int32_t row0 = (int32_t)(x.mb * Cfg::TILE_M + rank * BM);
+        const int32_t col0 = (int32_t)(x.nb * BN + x.n_off + rank * (PAIR ? x.wn / 2 : 0));
+        const uint32_t b_boxes = (PAIR ? x.wn / 2 : x.wn) / 64;
+        for (uint32_t kb = x.kb0; kb < x.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, status)) {
             *abort_flag = 1;
             break;
           }
-          // the pair's bytes all count on rank 0's barrier
+          // the pair's bytes all count on rank 0's barrier; a half tile
+          // loads half of this CTA's B columns
           if (rank == 0)
-            mbar_arrive_expect_tx(&full[stage], (PAIR ? 2 : 1) * Cfg::STAGE_BYTES);
+            mbar_arrive_expect_tx(&full[stage],
+                                  (PAIR ? 2 : 1) * (A_STAGE + (b_boxes * 64) * BK * 2));
           uint32_t fbar = 0;
           if constexpr (PAIR) fbar = cluster_addr(&full[stage], 0);
           auto load = [&](void *dst, const CUtensorMap *map, int32_t x, int32_t y) {
@@ -210,12 +269,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int j = 0; j < BM / 64; ++j)  // [64 K rows] x [64 M] boxes
               load(sa + j * B_SUB, &tmA, row0 + j * 64, k0);
           }
-          if (B_MN) {
-#pragma unroll
-            for (int j = 0; j < Cfg::BN_LOAD / 64; ++j)
-              load(sb + j * B_SUB, &tmB, col0 + j * 64, k0);
-          } else {
-            load(sb, &tmB, k0, col0);  // [BN_LOAD rows of N] x [64 K]: one box
+          // B in boxes of 64 columns: MN-major [64 K rows] x [64 N], K-major
+          // [64 N rows] x [64 K] (stacked boxes form one swizzled panel)
+          for (uint32_t j = 0; j < b_boxes; ++j) {
+            if (B_MN) load(sb + j * B_SUB, &tmB, col0 + (int32_t)j * 64, k0);
+            else load(sb + j * B_SUB, &tmB, k0, col0 + (int32_t)j * 64);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -237,19 +295,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       };
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
-      for (uint32_t it = first_tile; it < work.items && !*abort_flag; it += tile_step) {
+      GemmItem x;
+      for (uint32_t it = worker;
+           !*abort_flag && get_item(work, tiles_m, tiles_n, num_kb, it, x); it += work.workers) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, status)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        uint32_t mb, nb, n_off, wn;
-        item(it, mb, nb, n_off, wn);
-        const uint32_t idesc = wn == BN ? IDESC
+        const uint32_t idesc = x.wn == BN ? IDESC
             : make_idesc_f32acc(Cfg::TILE_M, BN / 2, A_MN ? 1u : 0u, B_MN ? 1u : 0u, ab_f16);
         bool ok = true;
-        for (uint32_t kb = 0; kb < num_kb; ++kb) {
+        for (uint32_t kb = x.kb0; kb < x.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, status)) {
             *abort_flag = 1;
             ok = false;
@@ -268,7 +326,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                      : make_smem_desc(a0 + ks * 32, 16, 1024, BWPP_SWIZZLE_128B);
             const uint64_t bd = B_MN ? make_smem_desc(b0 + ks * 2048, B_SUB, 1024, BWPP_SWIZZLE_128B)
                                      : make_smem_desc(b0 + ks * 32, 16, 1024, BWPP_SWIZZLE_128B);
-            const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
+            const uint32_t accum = (kb != x.kb0 || ks != 0) ? 1u : 0u;
             if constexpr (PAIR) tc_mma_f16_ss_pair(d_tmem, ad, bd, idesc, accum);
             else tc_mma_f16_ss(d_tmem, ad, bd, idesc, accum);
           }
@@ -291,52 +349,176 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int ew = warp - 2;
-    uint8_t *stage_c = smem + Cfg::OFF_C + ew * 2 * EPI_BUF;
-    uint32_t acc = 0, acc_phase = 0, buf = 0;
+    const int sub = ew >> 2;  // the two warps of a quarter take alternate chunks
+    uint8_t *stage_c = smem + Cfg::OFF_C + ew * EPI_BUF;
+    uint32_t acc = 0, acc_phase = 0;
     const int out16 = epi.out_bf16;
-    for (uint32_t it = first_tile; it < work.items && !*abort_flag; it += tile_step) {
-      uint32_t mb, nb, n_off, wn;
-      item(it, mb, nb, n_off, wn);
+    const int cw = out16 ? 64 : 32;  // chunk: 32 rows x 128 bytes of output
+    const int per = out16 ? 2 : 1;   // 32-column accumulator parts per chunk
+    const uint32_t tq = (uint32_t)(q * 32) << 16;  // TMEM lane base of this warp
+    // accumulator column of this warp's i-th 32-column part (chunks sub,
+    // sub + 2, ...)
+    auto part_col = [&](int i) { return (uint32_t)((sub + 2 * (i / per)) * cw + (i % per) * 32); };
+    // partial slots: [slot][CTA rank][32-column chunk][float4 index][row];
+    // one warp's 32 rows of one float4 index are 512 contiguous bytes
+    auto slot_rows = [&](uint32_t sl) {
+      return work.partials + (size_t)sl * Cfg::TILE_M * BN + (size_t)rank * BM * BN +
+             (size_t)(q * 32 + lane) * 4;
+    };
+    auto flag_of = [&](uint32_t sl) { return work.flags + (sl * 2 + rank) * EPI_WARPS + ew; };
+    GemmItem x;
+    for (uint32_t it = worker;
+         !*abort_flag && get_item(work, tiles_m, tiles_n, num_kb, it, x); it += work.workers) {
+      const uint32_t mb = x.mb, nb = x.nb, n_off = x.n_off, wn = x.wn;
+      // This item's bias, loaded before the accumulator is ready: lane l
+      // holds columns 8l .. 8l+7 of the item, handed out by shuffles.
+      float breg[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (epi.bias) {
+        const uint32_t bc = nb * BN + n_off + (uint32_t)lane * 8;
+        if (bc + 8 <= N) {
+          const float4 b0 = __ldg(reinterpret_cast<const float4 *>(epi.bias + bc));
+          const float4 b1 = __ldg(reinterpret_cast<const float4 *>(epi.bias + bc) + 1);
+          breg[0] = b0.x; breg[1] = b0.y; breg[2] = b0.z; breg[3] = b0.w;
+          breg[4] = b1.x; breg[5] = b1.y; breg[6] = b1.z; breg[7] = b1.w;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) breg[i] = bc + i < N ? __ldg(epi.bias + bc + i) : 0.f;
+        }
+      }
       if (!mbar_wait(&tfull[acc], acc_phase, status)) {
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
+      // chunks with columns below N; this warp takes chunks sub, sub + 2, ...
+      const uint32_t first_col = nb * BN + n_off;
+      const int nchunks = (int)min(wn / cw, (N - first_col + cw - 1) / cw);
+      const int my_chunks = nchunks > sub ? (nchunks - sub + 1) / 2 : 0;
+      // split part: this warp's chunk k belongs to part k % parts
+      const bool split = x.role == 3;
+      const int parts = split ? (int)work.sk_parts : 1;
+      const int mine = split ? (int)x.part : 0;
+      const uint32_t n_contrib = split ? (uint32_t)parts - 1 : 0;
+      const int own_chunks = my_chunks > mine ? (my_chunks - mine + parts - 1) / parts : 0;
+      if (split) {
+        // partial sums of the chunks other parts own, to this part's slot;
+        // then publish them (every lane's stores precede the flag)
+        float *dst = slot_rows(x.slot + x.part);
+        for (int k = 0; k < my_chunks; ++k) {
+          if (k % parts == mine) continue;
+          for (int h = 0; h < per; ++h) {
+            const uint32_t cc = part_col(k * per + h);
+            uint32_t w[32];
+            tmem_ld_32x32b_x32(tmem_base + tq + acc * BN + cc, w);
+            tc_wait_ld(w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              __stcg(reinterpret_cast<float4 *>(dst + (size_t)(cc / 32) * BM * 32 + j * BM * 4),
+                     make_float4(__uint_as_float(w[4 * j]), __uint_as_float(w[4 * j + 1]),
+                                 __uint_as_float(w[4 * j + 2]), __uint_as_float(w[4 * j + 3])));
+          }
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_gpu(flag_of(x.slot + x.part), work.epoch);
+      }
+      // the other parts' slots, in part order
+      auto contrib_slot = [&](uint32_t c) { return x.slot + (c < (uint32_t)mine ? c : c + 1); };
+      // Partials are staged through shared memory with per-thread async
+      // copies, `depth` parts ahead, so many loads are in flight.  The
+      // operand ring is free once this item's MMAs are done, as a split part
+      // is always its worker's last item (checked; else plain loads).  Each
+      // warp takes an eighth of the ring: `depth` x n_contrib blocks of 4 KB
+      // ([float4 index][lane] x 16 B, each lane reads back its own).
+      constexpr uint32_t RING_SHARE = Cfg::OFF_C / EPI_WARPS;
+      int depth = 0;
+      const uint32_t pbuf = smem_u32(smem) + (uint32_t)ew * RING_SHARE;
+      const int own_parts = own_chunks * per;
+      // accumulator column of this warp's t-th owned 32-column part
+      auto own_col = [&](int t) { return part_col((mine + (t / per) * parts) * per + t % per); };
+      int issued = 0;
+      auto issue = [&](int t) {
+        const uint32_t base = pbuf + (uint32_t)((t % depth) * n_contrib) * 4096u + lane * 16u;
+        const uint32_t pc = own_col(t) / 32;
+        for (uint32_t c = 0; c < n_contrib; ++c) {
+          const float *src = slot_rows(contrib_slot(c)) + (size_t)pc * BM * 32;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) cp_async_16(base + c * 4096u + j * 512u, src + j * BM * 4);
+        }
+        cp_async_commit();
+        ++issued;
+      };
+      if (n_contrib) {
+        bool ok = true;
+        for (uint32_t c = 0; c < n_contrib; ++c)
+          ok = ok && flag_wait(flag_of(contrib_slot(c)), work.epoch, status);
+        if (!__all_sync(0xffffffffu, ok)) {
+          *abort_flag = 1;
+          break;
+        }
+        GemmItem later;
+        const int fit = (int)(RING_SHARE / (4096u * n_contrib));
+        if (!get_item(work, tiles_m, tiles_n, num_kb, it + work.workers, later) && fit >= 1) {
+          depth = fit < 8 ? fit : 8;
+          fence_proxy_async_smem();  // the ring was last used by TMA and the tensor core
+          for (int t = 0; t < depth && t < own_parts; ++t) issue(t);
+        }
+      }
       const uint32_t row0 = mb * Cfg::TILE_M + rank * BM + q * 32;
       const uint32_t my_row = row0 + lane;
-      // fp32 out: 32-column chunks; bf16 out: 64-column chunks (two TMEM
-      // loads).  Either way a chunk is 32 rows x 128 bytes in smem.
-      const int cw = out16 ? 64 : 32;
-      for (int c = 0; c < (int)wn / cw; ++c) {
-        const uint32_t col0 = nb * BN + n_off + c * cw;
-        if (col0 >= N) break;  // warp-uniform
+      for (int ko = 0; ko < own_chunks; ++ko) {
+        const int k = mine + ko * parts;  // this warp's chunk index
+        const uint32_t col0 = first_col + (uint32_t)(sub + 2 * k) * cw;
         uint32_t outw[32];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           if (h == 1 && !out16) break;
-          const uint32_t cs = col0 + h * 32;  // first column of this 32-wide part
+          const int t = ko * per + h;           // this warp's owned-part index
+          const uint32_t cs = col0 + h * 32;    // first column of this 32-wide part
+          const uint32_t cc = cs - first_col;   // accumulator column
           uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + (cs - nb * BN - n_off), r);
+          tmem_ld_32x32b_x32(tmem_base + tq + acc * BN + cc, r);
           tc_wait_ld(r);
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          if (epi.bias) {
-            if (cs + 32 <= N) {
-              const float4 *b4 = reinterpret_cast<const float4 *>(epi.bias + cs);
+          if (n_contrib) {
+            const int pc = (int)(cc / 32);
+            if (depth) {
+              cp_async_wait_pending(issued - (t + 1));
+              const uint8_t *blk = smem + (size_t)ew * RING_SHARE +
+                                   (size_t)((t % depth) * n_contrib) * 4096u + lane * 16u;
+#pragma unroll 1
+              for (uint32_t c = 0; c < n_contrib; ++c) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 bb = __ldg(b4 + j);
-                v[4 * j] += bb.x;
-                v[4 * j + 1] += bb.y;
-                v[4 * j + 2] += bb.z;
-                v[4 * j + 3] += bb.w;
+                for (int j = 0; j < 8; ++j) {
+                  const float4 pv = *reinterpret_cast<const float4 *>(blk + c * 4096u + j * 512u);
+                  v[4 * j] += pv.x;
+                  v[4 * j + 1] += pv.y;
+                  v[4 * j + 2] += pv.z;
+                  v[4 * j + 3] += pv.w;
+                }
               }
+              if (t + depth < own_parts) issue(t + depth);  // into the block just read
             } else {
+#pragma unroll 1
+              for (uint32_t c = 0; c < n_contrib; ++c) {
+                const float *src = slot_rows(contrib_slot(c)) + (size_t)pc * BM * 32;
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (cs + j < N) v[j] += __ldg(epi.bias + cs + j);
+                for (int j = 0; j < 8; ++j) {
+                  const float4 pv = __ldcg(reinterpret_cast<const float4 *>(src + j * BM * 4));
+                  v[4 * j] += pv.x;
+                  v[4 * j + 1] += pv.y;
+                  v[4 * j + 2] += pv.z;
+                  v[4 * j + 3] += pv.w;
+                }
+              }
             }
+          }
+          if (epi.bias) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              v[j] += __shfl_sync(0xffffffffu, breg[j & 7], (int)(cc >> 3) + (j >> 3));
           }
           if (epi.silu) {
 #pragma unroll
@@ -393,10 +575,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int j = 0; j < 32; ++j) outw[j] = __float_as_uint(v[j]);
           }
         }
-        // the store that last used this buffer has finished reading it
-        if (lane == 0) tma_store_wait_read<1>();
+        // the previous store from this warp's buffer has finished reading it
+        if (lane == 0) tma_store_wait_read<0>();
         __syncwarp();
-        uint8_t *sc = stage_c + buf * EPI_BUF;
+        uint8_t *sc = stage_c;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           *reinterpret_cast<uint4 *>(sc + lane * 128 + ((j ^ (lane & 7)) << 4)) =
@@ -407,8 +589,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_store_2d(&tmC, sc, (int32_t)col0, (int32_t)row0);
           tma_store_commit();
         }
-        buf ^= 1;
       }
+      if (depth) cp_async_wait_pending(0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -500,6 +682,35 @@ int g_pair_clusters[4][64] = {};  // resident CTA pairs per device (0: not queri
 
 inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Split-tail scratch of ctx: 2 * num_sms fp32 slots of BM x BN (a CTA-pair
+// slot takes two of them; a launch uses at most cap slots) and 16 flags
+// per slot (2 CTAs x 8 epilogue warps).  Allocated on first use; never when the caller owns the workspace
+// (then GEMMs use the half-tile tail).
+bool gemm_scratch(BwppCudaCtx *ctx) {
+  if (ctx->gemm_partials) return true;
+  if (ctx->user_workspace || ctx->gemm_scratch_failed) return false;
+  const size_t slots = 2 * (size_t)ctx->num_sms;
+  const size_t part_bytes = slots * BM * BN * sizeof(float);
+  const size_t flag_bytes = slots * 2 * EPI_WARPS * sizeof(uint32_t);
+  void *p = nullptr;
+  if (cudaMalloc(&p, part_bytes + flag_bytes) != cudaSuccess) {
+    (void)cudaGetLastError();
+    ctx->gemm_scratch_failed = 1;
+    return false;
+  }
+  if (cudaMemsetAsync(static_cast<uint8_t *>(p) + part_bytes, 0, flag_bytes, ctx->stream) !=
+      cudaSuccess) {
+    (void)cudaGetLastError();
+    cudaFree(p);
+    ctx->gemm_scratch_failed = 1;
+    return false;
+  }
+  ctx->gemm_partials = static_cast<float *>(p);
+  ctx->gemm_flags = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(p) + part_bytes);
+  ctx->gemm_epoch = 0;
+  return true;
+}
+
 // CTA pairs are used unless BWPP_GEMM_CTA_PAIR=0 (then every GEMM runs the
 // single-CTA kernel).
 bool pairs_enabled() {
@@ -515,11 +726,13 @@ bool pairs_enabled() {
 // can take the single-CTA kernel.
 //
 // Wave tail: with `cap` tiles in flight (CTA pairs, or SMs) the last wave
-// holds tiles % cap tiles.  When that tail fits twice into one wave, its
-// tiles run as two N halves each, in the same launch (a GEMM of fewer tiles
-// than half the CTAs runs entirely in halves).  (At 8 GPUs the
+// holds tiles % cap tiles.  Those tiles are cut into K parts in the same
+// launch (GemmWork: split tail), so the tail takes a fraction of a tile's
+// time; a GEMM of fewer tiles than cap is all tail.  (At 8 GPUs the
 // 8192 x 4096 x 11008 GEMM leaves 1024 rows per GPU: 172 pair tiles, 2.3
-// waves; the 24-tile tail becomes 48 half tiles.)
+// waves; the 24-tile tail runs as 3 x 24 third-tiles in one round.)  When
+// no split applies (a tail of more than half a round, under 8 K blocks, or
+// no scratch), a tail that fits twice into one round runs as N halves.
 template <bool A_MN, bool B_MN, bool PAIR>
 int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
               const CUtensorMap &tcm, const GemmEpi &epi, uint32_t M, uint32_t N,
@@ -566,9 +779,37 @@ int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
     cap = (uint32_t)pairs;
   }
   const uint32_t full = tiles / cap, tail = tiles % cap;
-  const bool halve = tail > 0 && tail * 2 <= cap;
-  const GemmWork w{halve ? full * cap : tiles, halve ? full * cap + 2 * tail : tiles};
-  const uint32_t n = w.items < cap ? w.items : cap;
+  const uint32_t num_kb = (K + BK - 1) / BK;
+  GemmWork w{};
+  w.workers = cap;
+  w.items = w.split_begin = full * cap;
+  // Split tail: cut the `tail` tiles after the full waves into as many K
+  // parts as fit in one round (tail * parts <= cap), at most 8, each at
+  // least 4 K blocks.
+  uint32_t parts = 1;
+  if (tail > 0) {
+    parts = cap / tail;
+    if (parts > 8) parts = 8;
+    while (parts > 1 && num_kb / parts < 4) --parts;
+    if (parts > 1 && !gemm_scratch(ctx)) parts = 1;
+  }
+  if (parts > 1) {
+    w.sk_tile0 = w.items;
+    w.sk_tiles = tail;
+    w.sk_parts = parts;
+    w.epoch = ++ctx->gemm_epoch;
+    if (w.epoch == 0) w.epoch = ++ctx->gemm_epoch;  // 0 is the flags' initial value
+    w.partials = ctx->gemm_partials;
+    w.flags = ctx->gemm_flags;
+  } else {
+    // whole tiles; a tail that fits twice into one round runs as N halves
+    const bool halve = tail > 0 && tail * 2 <= cap;
+    w.split_begin = halve ? full * cap : tiles;
+    w.items = halve ? full * cap + 2 * tail : tiles;
+  }
+  const uint64_t total = (uint64_t)w.items + (uint64_t)w.sk_tiles * w.sk_parts;
+  const uint32_t n = total < cap ? (uint32_t)total : cap;
+  w.workers = n;
   cfg.gridDim = dim3((PAIR ? 2 : 1) * n, 1, 1);
   int *status = ctx->status_word;
   return bwpp_check_cuda(
@@ -578,10 +819,10 @@ int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
 
 template <bool A_MN, bool B_MN>
 int launch_tc_any(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
-                  const CUtensorMap &tb_pair, const CUtensorMap &tcm, const GemmEpi &epi,
+                  const CUtensorMap &tcm, const GemmEpi &epi,
                   uint32_t M, uint32_t N, uint32_t K, bool pair, uint32_t ab_f16) {
   if (pair) {
-    const int rc = launch_tc<A_MN, B_MN, true>(ctx, ta, tb_pair, tcm, epi, M, N, K, ab_f16);
+    const int rc = launch_tc<A_MN, B_MN, true>(ctx, ta, tb, tcm, epi, M, N, K, ab_f16);
     if (rc != BWPP_CUDA_ERR_UNSUPPORTED) return rc;
   }
   return launch_tc<A_MN, B_MN, false>(ctx, ta, tb, tcm, epi, M, N, K, ab_f16);
@@ -617,21 +858,16 @@ int bwpp_gemm_launch_dt(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t 
   // CTA pairs take GEMMs with more than one 128-row block (the second CTA
   // of a pair would otherwise compute rows past M only).
   const bool pair = pairs_enabled() && M > (uint32_t)BM;
-  CUtensorMap ta, tb, tb_pair, tcm;
+  CUtensorMap ta, tb, tcm;
   const auto BF = ab_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto OUT16 = out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
   int rc = a_mn ? bwpp_make_tmap_2d(ctx, &ta, a, BF, M, K, (uint64_t)lda * 2, 64, BK, SW)
                 : bwpp_make_tmap_2d(ctx, &ta, a, BF, K, M, (uint64_t)lda * 2, BK, BM, SW);
-  // B boxes: MN-major 64 columns x 64 K rows; K-major 64 K x (256 or, for a
-  // pair, 128) rows of N
+  // B boxes: MN-major 64 columns x 64 K rows; K-major 64 K x 64 rows of N
   if (!rc)
     rc = b_mn ? bwpp_make_tmap_2d(ctx, &tb, b, BF, N, K, (uint64_t)ldb * 2, 64, BK, SW)
-              : bwpp_make_tmap_2d(ctx, &tb, b, BF, K, N, (uint64_t)ldb * 2, BK, BN, SW);
-  if (!rc)
-    rc = (b_mn || !pair) ? (tb_pair = tb, 0)
-                         : bwpp_make_tmap_2d(ctx, &tb_pair, b, BF, K, N, (uint64_t)ldb * 2, BK,
-                                             GemmCfg<true>::BN_LOAD, SW);
+              : bwpp_make_tmap_2d(ctx, &tb, b, BF, K, N, (uint64_t)ldb * 2, BK, 64, SW);
   if (!rc)
     rc = out_bf16 ? bwpp_make_tmap_2d(ctx, &tcm, c, OUT16, N, M, (uint64_t)ldc * 2, 64, 32, SW)
                   : bwpp_make_tmap_2d(ctx, &tcm, c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M,
@@ -639,11 +875,11 @@ int bwpp_gemm_launch_dt(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t 
   if (rc) return rc;
   const uint32_t f = ab_f16 ? 1u : 0u;
   if (a_mn) {
-    return b_mn ? launch_tc_any<true, true>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair, f)
-                : launch_tc_any<true, false>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair, f);
+    return b_mn ? launch_tc_any<true, true>(ctx, ta, tb, tcm, epi, M, N, K, pair, f)
+                : launch_tc_any<true, false>(ctx, ta, tb, tcm, epi, M, N, K, pair, f);
   }
-  return b_mn ? launch_tc_any<false, true>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair, f)
-              : launch_tc_any<false, false>(ctx, ta, tb, tb_pair, tcm, epi, M, N, K, pair, f);
+  return b_mn ? launch_tc_any<false, true>(ctx, ta, tb, tcm, epi, M, N, K, pair, f)
+              : launch_tc_any<false, false>(ctx, ta, tb, tcm, epi, M, N, K, pair, f);
 }
 
 int bwpp_gemm_launch_ex(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,

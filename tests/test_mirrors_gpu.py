@@ -48,6 +48,27 @@ def test_cpu_mirror_matmul_strided_host():
     assert (c[:, N:] == 7.0).all()
 
 
+@pytest.mark.parametrize("M,N,K,pad,bias_on", [(2500, 2100, 300, 3, 1), (1100, 5000, 160, 0, 0),
+                                               (4096, 900, 96, 5, 1)])
+def test_cpu_mirror_matmul_host_pipelined(M, N, K, pad, bias_on):
+    """Host A, B and C large enough to be cut into row and column chunks:
+    uploads, GEMMs of each L-shaped region and strided downloads overlap on
+    three streams.  Every element of C (and none of its padding) is written."""
+    lda, ldb, ldc = K + pad, N + pad, N + 2 * pad
+    rng = np.random.default_rng(M + N)
+    a = rng.standard_normal((M, lda)).astype(np.float32)
+    b = rng.standard_normal((K, ldb)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, N).astype(np.float32) if bias_on else None
+    c = np.full((M, ldc), 7.0, np.float32)
+    ref = O.matmul(O.round_bf16(np.ascontiguousarray(a[:, :K])),
+                   O.round_bf16(np.ascontiguousarray(b[:, :N])), bias, bias_on, bias_on)
+    for _ in range(2):  # the second call reuses the copy streams and events
+        bwpp.matmul_f32(a, b, c, M, N, K, lda, ldb, ldc, bias, bias_on, bias_on)
+        assert rel_fro(c[:, :N], ref) <= 2e-4
+        assert (c[:, N:] == 7.0).all()
+        c[:, :N] = np.nan
+
+
 @pytest.mark.parametrize("where", ["host", "device"])
 def test_cpu_mirror_rows(ctx, where):
     rng = np.random.default_rng(4)
