@@ -669,6 +669,25 @@ def make_workload(name, *a):
 # reference arm: the reference's own CPU code on the host cores
 # ---------------------------------------------------------------------------
 
+def reference_config(name, world):
+    """The `config` our arm reports for this workload at this world size (rank 0's
+    shard sizes), built without a GPU."""
+    wl = make_workload(name, 0, world, None, None, None)
+    if isinstance(wl, GemmWorkload):
+        wl.r0, wl.r1 = split_rows(wl.M, 0, world)
+        wl.m = wl.r1 - wl.r0
+    elif isinstance(wl, AttentionWorkload):
+        wl.h0, wl.h1 = split_rows(wl.B * wl.H, 0, world)
+        wl.nh = wl.h1 - wl.h0
+    elif isinstance(wl, RowWorkload):
+        wl.r0, wl.r1 = split_rows(wl.R, 0, world)
+        wl.m = wl.r1 - wl.r0
+    try:
+        return wl.config()
+    except AttributeError:
+        return {"workload": name}
+
+
 def run_reference(args, world):
     import oracle as O
     rank = int(os.environ.get("RANK", "0"))
@@ -680,6 +699,7 @@ def run_reference(args, world):
         lib, kind = O.oracle_lib(), "port"
     threads = O.cpu_threads()
     wl = make_workload(args.workload, 0, 1, None, None, None)
+    cfg = reference_config(args.workload, world)
     for _ in range(args.warmup):
         wl.cpu_sample(lib, threads)
     work, secs = 0.0, 0.0
@@ -689,10 +709,10 @@ def run_reference(args, world):
         work += w
         secs += dt
     value = wl.scale(work, secs)
-    cfg = {"workload": args.workload}
     line = {"metric": METRIC, "value": value, "unit": wl.unit, "impl": "reference", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / max(args.steps, 1),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": getattr(wl, "scaling", "strong"), "vs_baseline": None,
+            "dtype": "f32",
             "data": "synthetic (seeded), fp32 copies of the benchmark inputs", "config": cfg,
             "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": kind,
                              "sample": sample},
