@@ -14,8 +14,11 @@
 //                    softmax warps (one key per thread) form P^T and dS^T ->
 //                    smem bf16, dV += P^T dO and dK += dS^T Q accumulate in
 //                    TMEM.
-// Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer, 2-5 softmax.  All
-// waits are bounded (BWPP_WAIT_LIMIT_NS) as in the forward kernel.
+// Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer, 2-9 softmax (two
+// per TMEM lane quarter, each taking half of a block's 128 columns: with one
+// warp per quarter the exp2 / dS / pack work left the tensor core idle most
+// of the time).  All waits are bounded (BWPP_WAIT_LIMIT_NS) as in the
+// forward kernel.
 // Operands reuse the forward's smem layouts: a 128-row tile is two 64-column
 // 128-byte-swizzle boxes; read K-major for S-type products and MN-major when
 // it is the B of dQ / dK / dV.
@@ -27,7 +30,8 @@ using namespace bwpp_attn;
 
 constexpr int D = 128;
 constexpr int TILE = 2 * BOX;  // 128 rows x 128 bf16
-constexpr int THREADS = 192;
+constexpr int SM_WARPS = 8;  // softmax warps: two per TMEM lane quarter, half the columns each
+constexpr int THREADS = 64 + 32 * SM_WARPS;
 constexpr uint32_t IDESC_KK = make_idesc_bf16_f32(128, 128, 0, 0);  // S-type
 constexpr uint32_t IDESC_KM = make_idesc_bf16_f32(128, D, 0, 1);    // dQ / dK / dV
 
@@ -63,9 +67,9 @@ __device__ __forceinline__ void mma_km(uint32_t d, uint32_t a, uint32_t b, bool 
 
 // Writes a row of 128 fp32 TMEM values (x scale) as bf16 to global memory.
 __device__ __forceinline__ void store_row_bf16(uint32_t taddr, uint16_t *dst, float scale,
-                                               bool valid) {
+                                               bool valid, int half) {
 #pragma unroll 1
-  for (int c = 0; c < D / 32; ++c) {
+  for (int c = half * (D / 64); c < (half + 1) * (D / 64); ++c) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(taddr + c * 32, r);
     tc_wait_ld(r);
@@ -117,8 +121,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&bar->kv_empty[s], 1);
     }
     mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->s_free, 4);
-    mbar_init(&bar->ds_full, 4);
+    mbar_init(&bar->s_free, SM_WARPS);
+    mbar_init(&bar->ds_full, SM_WARPS);
     mbar_init(&bar->dq_done, 1);
     mbar_init(&bar->drain, 1);
     bar->abort_flag = 0;
@@ -178,6 +182,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // which 64 columns of each block
     const int row = quarter * 32 + lane;
     const uint32_t m = q0 + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
@@ -204,7 +209,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (causal && m < lim) lim = m;
       const int lim_rel = (int)lim - (int)n0;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
         uint32_t rs[32], rp[32];
         tmem_ld_32x32b_x32(tmem + lane_base + c * 32, rs);
         tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, rp);
@@ -239,7 +244,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         uint16_t *dst = io.d0 + ((size_t)(bh / io.in.H) * Sq + m) * io.ldd +
                         (size_t)(bh % io.in.H) * D;
-        store_row_bf16(tmem + lane_base + 256, dst, scale, valid);
+        store_row_bf16(tmem + lane_base + 256, dst, scale, valid, half);
       } else {
         *abort_flag = 1;
       }
@@ -292,10 +297,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&bar->qd_full, 1);
     mbar_init(&bar->qd_empty, 1);
     mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->s_free, 4);
-    mbar_init(&bar->p_full, 4);
+    mbar_init(&bar->s_free, SM_WARPS);
+    mbar_init(&bar->p_full, SM_WARPS);
     mbar_init(&bar->pdone, 1);
-    mbar_init(&bar->staged, 128);
+    mbar_init(&bar->staged, 32 * SM_WARPS);
     mbar_init(&bar->drain, 1);
     bar->abort_flag = 0;
     fence_mbar_init();
@@ -353,8 +358,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;     // which 64 query columns of each tile
     const int row = quarter * 32 + lane;  // key within the block
-    const int tid = threadIdx.x - 64;     // 0..127 over the softmax warps
+    const int tid = (threadIdx.x - 64) & 127;  // both halves stage the same 128 values
     const uint32_t key = k0 + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     uint8_t *pt_tile = smem + K_OFF_PT;
@@ -392,7 +398,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float *ls = lse_s + (it & 1) * 128;
       const float *dd = del_s + (it & 1) * 128;
 #pragma unroll 1
-      for (int c = 0; c < BM / 32; ++c) {
+      for (int c = half * (BM / 64); c < (half + 1) * (BM / 64); ++c) {
         uint32_t rs[32], rp[32];
         tmem_ld_32x32b_x32(tmem + lane_base + c * 32, rs);
         tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, rp);
@@ -429,14 +435,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (ok && n > 0) {
       if (mbar_wait(&bar->pdone, (n - 1) & 1, status)) {
         tc_fence_after();
-        store_row_bf16(tmem + lane_base + 256, dv_dst, 1.0f, valid);
-        store_row_bf16(tmem + lane_base + 384, dk_dst, scale, valid);
+        store_row_bf16(tmem + lane_base + 256, dv_dst, 1.0f, valid, half);
+        store_row_bf16(tmem + lane_base + 384, dk_dst, scale, valid, half);
       } else {
         *abort_flag = 1;
       }
     } else if (ok && valid) {
       // no query sees these keys: zero gradients
-      for (int c = 0; c < D; c += 8) {
+      for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 8) {
         *reinterpret_cast<uint4 *>(dk_dst + c) = make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4 *>(dv_dst + c) = make_uint4(0, 0, 0, 0);
       }

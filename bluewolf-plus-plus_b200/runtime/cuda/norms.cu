@@ -145,7 +145,8 @@ __global__ void __launch_bounds__(kThreads)
     norm_bwd_kernel(const float *__restrict__ x, const float *__restrict__ gamma,
                     const float *__restrict__ dy, float *__restrict__ dx,
                     float *__restrict__ part_g, float *__restrict__ part_b,
-                    uint32_t rows, uint32_t cols, uint32_t ld, float eps) {
+                    uint32_t rows, uint32_t cols, uint32_t ld, float eps,
+                    float *__restrict__ acc, uint16_t *__restrict__ acc16) {
   using V = Vec<V4>;
   constexpr int W = V::W;
   __shared__ float red[4 * 32];
@@ -211,7 +212,27 @@ __global__ void __launch_bounds__(kThreads)
         o[w] = rs * (g - mg - xh * mgx);
         xv[i][w] = xh;  // keep xhat for the partials below
       }
-      V::store(dxr, idx, o);
+      if (acc) {
+        // residual-gradient form: acc += dx (and acc16 = bf16(acc)); dx
+        // itself is not written
+        float *ar = acc + (size_t)r * ld;
+        float h[W];
+        V::load_stream(ar, idx, h);
+#pragma unroll
+        for (int w = 0; w < W; ++w) h[w] += o[w];
+        V::store(ar, idx, h);
+        if (acc16) {
+          uint16_t *hr = acc16 + (size_t)r * ld;
+          if constexpr (W == 4) {
+            *reinterpret_cast<uint2 *>(hr + 4 * (size_t)idx) =
+                make_uint2(pack2_16<false>(h[0], h[1]), pack2_16<false>(h[2], h[3]));
+          } else {
+            hr[idx] = (uint16_t)(pack2_16<false>(h[0], 0.0f) & 0xFFFFu);
+          }
+        }
+      } else {
+        V::store(dxr, idx, o);
+      }
       if (part_g) {
         // 128-bit shared accesses: a warp touches 512 contiguous bytes
         if constexpr (W == 4) {
@@ -362,14 +383,17 @@ int norm_fwd(BwppCudaCtx *ctx, const float *x, float *y, const float *gamma,
 
 uint32_t bwd_grid(BwppCudaCtx *ctx, uint32_t rows) { return row_grid(ctx, rows, 4); }
 
+// acc != NULL: instead of writing dx, add it into acc (and write bf16(acc) to
+// acc16 when given); only rows held in registers (cols <= 8192 with dgamma).
 template <bool CENTERED>
 int norm_bwd(BwppCudaCtx *ctx, const float *x, const float *gamma,
              const float *dy, float *dx, float *dgamma, float *dbeta,
              uint32_t rows, uint32_t cols, uint32_t ld, float eps,
-             float *scratch /* may be NULL: ctx workspace */) {
+             float *scratch /* may be NULL: ctx workspace */,
+             float *acc = nullptr, uint16_t *acc16 = nullptr) {
   int rc = bwpp_ctx_enter(ctx);
   if (rc) return rc;
-  if (!x || !dy || !dx || ld < cols)
+  if (!x || !dy || (!dx && !acc) || ld < cols)
     return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG, "norm bwd: bad args");
   if (cols == 0) return BWPP_CUDA_OK;
   cudaStream_t s = ctx->stream;
@@ -389,15 +413,18 @@ int norm_bwd(BwppCudaCtx *ctx, const float *x, const float *gamma,
     pb = scratch + (size_t)grid * cols;
   }
   const bool v4 = cols % 4 == 0 && ld % 4 == 0 && aligned16(x) && aligned16(dy) &&
-                  aligned16(dx) && aligned16(gamma);
+                  aligned16(dx) && aligned16(gamma) && aligned16(acc) &&
+                  (reinterpret_cast<uintptr_t>(acc16) & 7u) == 0;
   const uint32_t nv = v4 ? cols / 4 : cols;
   int mv = pick_maxv(nv, kMaxVecBwd);
   // partials in shared memory: 2 * cols floats per CTA
   const size_t acc_bytes = pg ? sizeof(float) * 2 * (size_t)cols : 0;
   if (acc_bytes > 48 * 1024) mv = 0;  // wide rows: looped kernel (global partials)
+  if (acc && mv == 0)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "norm bwd accumulate: row too wide");
 #define BWPP_BWD(MV, V4)                                                     \
   norm_bwd_kernel<MV, V4, CENTERED><<<grid, kThreads, acc_bytes, s>>>(       \
-      x, gamma, dy, dx, pg, pb, rows, cols, ld, eps)
+      x, gamma, dy, dx, pg, pb, rows, cols, ld, eps, acc, acc16)
   if (mv == 0) {
     norm_bwd_looped_kernel<CENTERED><<<grid, kThreads, 0, s>>>(
         x, gamma, dy, dx, pg, pb, rows, cols, ld, eps);
@@ -440,6 +467,20 @@ int bwpp_norm_bwd_with_scratch(BwppCudaCtx *ctx, int centered, const float *x,
                                    cols, ld, eps, scratch)
                   : norm_bwd<false>(ctx, x, gamma, dy, dx, dgamma, dbeta, rows,
                                     cols, ld, eps, scratch);
+}
+
+// Backward folded into a residual gradient: acc += dx, acc16 = bf16(acc)
+// (acc16 may be NULL), dx never stored.  Rows must fit the register-resident
+// kernel (BWPP_CUDA_ERR_UNSUPPORTED otherwise, with nothing launched).
+int bwpp_norm_bwd_accumulate(BwppCudaCtx *ctx, int centered, const float *x,
+                             const float *gamma, const float *dy, float *acc,
+                             uint16_t *acc16, float *dgamma, float *dbeta,
+                             uint32_t rows, uint32_t cols, uint32_t ld, float eps,
+                             float *scratch) {
+  return centered ? norm_bwd<true>(ctx, x, gamma, dy, nullptr, dgamma, dbeta, rows, cols, ld,
+                                   eps, scratch, acc, acc16)
+                  : norm_bwd<false>(ctx, x, gamma, dy, nullptr, dgamma, dbeta, rows, cols, ld,
+                                    eps, scratch, acc, acc16);
 }
 
 extern "C" {
@@ -573,7 +614,7 @@ extern "C" int bwpp_cuda_rmsnorm_bwd_f32_noalloc(
   if (acc_bytes > 48 * 1024) mv = 0;
 #define BWPP_NA_BWD(MV, V4)                                                     \
   norm_bwd_kernel<MV, V4, false><<<grid, kThreads, acc_bytes, s>>>(             \
-      x, gamma, dy, dx, pg, pb, rows, cols, ld, eps)
+      x, gamma, dy, dx, pg, pb, rows, cols, ld, eps, nullptr, nullptr)
   if (mv == 0) {
     norm_bwd_looped_kernel<false><<<grid, kThreads, 0, s>>>(x, gamma, dy, dx, pg, pb, rows,
                                                             cols, ld, eps);

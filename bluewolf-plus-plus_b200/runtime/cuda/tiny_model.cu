@@ -41,6 +41,11 @@ int bwpp_attn_delta(BwppCudaCtx *ctx, const uint16_t *dO, const uint16_t *O, flo
                     uint32_t B, uint32_t S, uint32_t H, uint32_t Dh);
 int bwpp_sgd(BwppCudaCtx *ctx, float *w, const float *g, uint16_t *w16, size_t n, float lr);
 int bwpp_add(BwppCudaCtx *ctx, float *a, const float *b, size_t n);
+int bwpp_norm_bwd_accumulate(BwppCudaCtx *ctx, int centered, const float *x,
+                             const float *gamma, const float *dy, float *acc,
+                             uint16_t *acc16, float *dgamma, float *dbeta,
+                             uint32_t rows, uint32_t cols, uint32_t ld, float eps,
+                             float *scratch);
 int bwpp_fill_normal(BwppCudaCtx *ctx, float *w, size_t n, uint64_t seed, float mean,
                      float stddev);
 int bwpp_attention_fwd_train(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
@@ -95,6 +100,22 @@ struct BwppCudaTinyModel {
 namespace {
 
 size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// dh += rmsnorm_bwd(x, gamma, dtmp) and dgamma; dh16 = bf16(dh) when given.
+// One pass (the norm backward adds its dx into dh) when the row fits the
+// register-resident kernel; else the norm backward, an add and a cast.
+int norm_bwd_into_dh(BwppCudaCtx *ctx, BwppCudaTinyModel *m, const float *x,
+                     const float *gamma, float *dgamma, uint32_t T, uint32_t D, float eps,
+                     uint16_t *dh16) {
+  int rc = bwpp_norm_bwd_accumulate(ctx, 0, x, gamma, m->dtmp, m->dh, dh16, dgamma, nullptr, T,
+                                    D, D, eps, m->norm_scratch);
+  if (rc != BWPP_CUDA_ERR_UNSUPPORTED) return rc;
+  rc = bwpp_norm_bwd_with_scratch(ctx, 0, x, gamma, m->dtmp, m->dtmp, dgamma, nullptr, T, D, D,
+                                  eps, m->norm_scratch);
+  if (!rc) rc = bwpp_add(ctx, m->dh, m->dtmp, (size_t)T * D);
+  if (!rc && dh16) rc = bwpp_cast_launch(ctx, m->dh, dh16, T, D, D, D);
+  return rc;
+}
 
 }  // namespace
 
@@ -326,11 +347,8 @@ int bwpp_cuda_tiny_model_step(BwppCudaTinyModel *m, const float *x, const float 
                             nullptr, 0, nullptr, 0, 0, 0));  // dW13 = n2^T dgu
     TRY(bwpp_gemm_launch_ex(ctx, m->dgu, 0, 2 * F, P16 + p.w13, 0, 2 * F, m->dtmp, D, T, D,
                             2 * F, nullptr, 0, nullptr, 0, 0, 0));  // dn2 = dgu W13^T
-    // h_mid feeds rmsnorm(g2) and the residual: dh += rmsnorm_bwd(dn2)
-    TRY(bwpp_norm_bwd_with_scratch(ctx, 0, a.h_mid, P + p.g2, m->dtmp, m->dtmp, G + p.g2,
-                                   nullptr, T, D, D, c.eps, m->norm_scratch));
-    TRY(bwpp_add(ctx, m->dh, m->dtmp, (size_t)T * D));
-    TRY(bwpp_cast_launch(ctx, m->dh, m->dh16, T, D, D, D));
+    // h_mid feeds rmsnorm(g2) and the residual: dh += rmsnorm_bwd(dn2), dh16 = bf16(dh)
+    TRY(norm_bwd_into_dh(ctx, m, a.h_mid, P + p.g2, G + p.g2, T, D, c.eps, m->dh16));
     // h_mid = h_in + o Wo
     TRY(bwpp_gemm_launch_ex(ctx, a.o, 1, D, m->dh16, 1, D, G + p.wo, D, D, D, T, nullptr, 0,
                             nullptr, 0, 0, 0));  // dWo = o^T dh
@@ -344,8 +362,10 @@ int bwpp_cuda_tiny_model_step(BwppCudaTinyModel *m, const float *x, const float 
                             nullptr, 0, nullptr, 0, 0, 0));  // dWqkv = n1^T dqkv
     TRY(bwpp_gemm_launch_ex(ctx, m->dqkv, 0, 3 * D, P16 + p.wqkv, 0, 3 * D, m->dtmp, D, T, D,
                             3 * D, nullptr, 0, nullptr, 0, 0, 0));  // dn1 = dqkv Wqkv^T
-    TRY(bwpp_norm_bwd_with_scratch(ctx, 0, a.h_in, P + p.g1, m->dtmp, m->dtmp, G + p.g1,
-                                   nullptr, T, D, D, c.eps, m->norm_scratch));
+    // h_in feeds rmsnorm(g1) and the residual: dh += rmsnorm_bwd(dn1) (dh16 only
+    // when a lower layer still reads it)
+    TRY(norm_bwd_into_dh(ctx, m, a.h_in, P + p.g1, G + p.g1, T, D, c.eps,
+                         l > 0 ? m->dh16 : nullptr));
     // layer l's gradients are final: sum them over the ranks on the comm
     // stream while the backward of layer l-1 runs (every rank issues the
     // buckets in the same order, layers L-1 .. 0)
@@ -358,8 +378,6 @@ int bwpp_cuda_tiny_model_step(BwppCudaTinyModel *m, const float *x, const float 
       TRY(bwpp_check_cuda(ctx, cudaEventRecord(m->bucket_done[l], m->comm_stream),
                           "bucket event"));
     }
-    TRY(bwpp_add(ctx, m->dh, m->dtmp, (size_t)T * D));
-    if (l > 0) TRY(bwpp_cast_launch(ctx, m->dh, m->dh16, T, D, D, D));
   }
   // ---------------- data-parallel gradient sum (overlapped above), SGD on
   // the mean gradient once every bucket has been summed
