@@ -93,8 +93,15 @@ constexpr int Q_OFF_Q = 0, Q_OFF_DO = TILE, Q_OFF_K = 2 * TILE, Q_OFF_V = 4 * TI
 constexpr int Q_SMEM = Q_OFF_BAR + 256 + 1024;
 static_assert(Q_SMEM <= 232448, "dq smem");
 
+// Pipeline of bwd_dq_kernel, per key block j (K / V double-buffered):
+//   MMA:     S(j+1) once S(j) is read | dQ(j) once dS(j) is in smem |
+//            dP(j+1) (dP(j) was read before dS(j) was published)
+//   softmax: P(j) = exp2(...) from S(j) into registers -> s_read;
+//            dS(j) = P (dP(j) - delta) -> smem -> ds_full
+// so S(j+1) and dQ(j) run on the tensor core while the softmax finishes
+// block j, and the exp2 work of block j+1 overlaps dP(j+1).
 struct QBars {
-  uint64_t qd_full, kv_full[2], kv_empty[2], s_full, s_free, ds_full, dq_done, drain;
+  uint64_t qd_full, kv_full[2], kv_empty[2], s_full, dp_full, s_read, ds_full, dq_done, drain;
   uint32_t tmem;
   int abort_flag;
 };
@@ -121,7 +128,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&bar->kv_empty[s], 1);
     }
     mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->s_free, SM_WARPS);
+    mbar_init(&bar->dp_full, 1);
+    mbar_init(&bar->s_read, SM_WARPS);
     mbar_init(&bar->ds_full, SM_WARPS);
     mbar_init(&bar->dq_done, 1);
     mbar_init(&bar->drain, 1);
@@ -158,23 +166,37 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = mbar_wait(&bar->qd_full, 0, status);
       const uint32_t qa = smem_u32(smem + Q_OFF_Q), da = smem_u32(smem + Q_OFF_DO);
       const uint32_t dsa = smem_u32(smem + Q_OFF_DS);
+      auto ka = [&](int j) { return smem_u32(smem + Q_OFF_K + (j & 1) * TILE); };
+      auto va = [&](int j) { return smem_u32(smem + Q_OFF_V + (j & 1) * TILE); };
+      if (ok && n > 0) {
+        ok = mbar_wait(&bar->kv_full[0], 0, status);
+        if (ok) {
+          tc_fence_after();
+          mma_kk(tmem + 0, qa, ka(0));    // S(0)  = Q  K_0^T
+          tc_commit(&bar->s_full);
+          mma_kk(tmem + 128, da, va(0));  // dP(0) = dO V_0^T
+          tc_commit(&bar->dp_full);
+        }
+      }
       for (int j = 0; j < n && ok && !*abort_flag; ++j) {
-        const int s = j & 1;
-        const uint32_t ka = smem_u32(smem + Q_OFF_K + s * TILE);
-        const uint32_t va = smem_u32(smem + Q_OFF_V + s * TILE);
-        ok = mbar_wait(&bar->kv_full[s], (j >> 1) & 1, status);
-        if (ok && j > 0) ok = mbar_wait(&bar->s_free, (j - 1) & 1, status);
-        if (!ok) break;
-        tc_fence_after();
-        mma_kk(tmem + 0, qa, ka);    // S  = Q  K_j^T
-        mma_kk(tmem + 128, da, va);  // dP = dO V_j^T
-        tc_commit(&bar->s_full);
+        if (j + 1 < n) {
+          ok = mbar_wait(&bar->kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, status) &&
+               mbar_wait(&bar->s_read, j & 1, status);
+          if (!ok) break;
+          tc_fence_after();
+          mma_kk(tmem + 0, qa, ka(j + 1));  // S(j+1), over the S(j) just read
+          tc_commit(&bar->s_full);
+        }
         ok = mbar_wait(&bar->ds_full, j & 1, status);
         if (!ok) break;
         tc_fence_after();
-        mma_km(tmem + 256, dsa, ka, j > 0);  // dQ += dS K_j
+        mma_km(tmem + 256, dsa, ka(j), j > 0);  // dQ += dS(j) K_j
         tc_commit(&bar->dq_done);
-        tc_commit(&bar->kv_empty[s]);
+        tc_commit(&bar->kv_empty[j & 1]);
+        if (j + 1 < n) {
+          mma_kk(tmem + 128, da, va(j + 1));  // dP(j+1), over the dP(j) read for dS(j)
+          tc_commit(&bar->dp_full);
+        }
       }
       if (!ok) *abort_flag = 1;
       tc_commit(&bar->drain);
@@ -198,46 +220,54 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      // dS smem is free once dQ(j-1) is done (it completed before S(j))
-      if (j > 0 && !mbar_wait(&bar->dq_done, (j - 1) & 1, status)) {
-        *abort_flag = 1;
-        ok = false;
-        break;
-      }
       const uint32_t n0 = (uint32_t)j * BN;
       uint32_t lim = Skv - 1;
       if (causal && m < lim) lim = m;
       const int lim_rel = (int)lim - (int)n0;
-#pragma unroll 1
-      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-        uint32_t rs[32], rp[32];
+      // P for this warp's 64 columns, kept in registers
+      float p[BN / 2];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = half * 2 + cc;
+        uint32_t rs[32];
         tmem_ld_32x32b_x32(tmem + lane_base + c * 32, rs);
-        tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, rp);
         tc_wait_ld(rs);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = c * 32 + i;
+          p[cc * 32 + i] = (col <= lim_rel)
+                               ? fast_exp2(fmaf(__uint_as_float(rs[i]), scale_log2, -lse))
+                               : 0.0f;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->s_read);  // S(j+1) may now overwrite S(j)
+      // dS smem is free once dQ(j-1) is done
+      if (!mbar_wait(&bar->dp_full, j & 1, status) ||
+          (j > 0 && !mbar_wait(&bar->dq_done, (j - 1) & 1, status))) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = half * 2 + cc;
+        uint32_t rp[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, rp);
         tc_wait_ld(rp);
         uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float ds[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int col = c * 32 + 2 * i + e;
-            const float p = (col <= lim_rel)
-                                ? fast_exp2(fmaf(__uint_as_float(rs[2 * i + e]), scale_log2, -lse))
-                                : 0.0f;
-            ds[e] = p * (__uint_as_float(rp[2 * i + e]) - dl);
-          }
-          pk[i] = pack_bf16(ds[0], ds[1]);
-        }
+        for (int i = 0; i < 16; ++i)
+          pk[i] = pack_bf16(p[cc * 32 + 2 * i] * (__uint_as_float(rp[2 * i]) - dl),
+                            p[cc * 32 + 2 * i + 1] * (__uint_as_float(rp[2 * i + 1]) - dl));
         store_swizzled_chunk(ds_tile, row, c, pk);
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bar->s_free);
-        mbar_arrive(&bar->ds_full);
-      }
+      if (lane == 0) mbar_arrive(&bar->ds_full);  // also: dP(j) has been read
     }
     if (ok && n > 0) {
       if (mbar_wait(&bar->dq_done, (n - 1) & 1, status)) {
