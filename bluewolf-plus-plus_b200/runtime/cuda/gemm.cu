@@ -85,6 +85,12 @@ struct GemmEpi {
   int out_bf16;           // 16-bit output (bf16, or f16 when out_f16)
   int out_f16;
   int res16;              // residual element type: 0 fp32, 1 bf16, 2 f16
+  // SwiGLU backward (glu != nullptr): the product is d(a) for a = silu(gate)
+  // * up; glu holds [gate | up] bf16 rows (gate column f, up column glu_F + f,
+  // pitch ldglu).  C receives d(gate) (bf16), glu_up_out d(up) (same pitch).
+  const uint16_t *glu;
+  uint16_t *glu_up_out;
+  uint32_t ldglu, glu_F;
 };
 
 // Work of a launch, handed out round-robin to `workers` workers (CTA pairs,
@@ -520,6 +526,51 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int j = 0; j < 32; ++j)
               v[j] += __shfl_sync(0xffffffffu, breg[j & 7], (int)(cc >> 3) + (j >> 3));
           }
+          if (epi.glu && my_row < M) {
+            // SwiGLU backward: with s = sigmoid(gate), d(gate) = v up s (1 +
+            // gate (1 - s)) replaces v; d(up) = v gate s is stored here
+            const uint16_t *gr = epi.glu + (size_t)my_row * epi.ldglu + cs;
+            const uint16_t *ur = gr + epi.glu_F;
+            uint16_t *dur = epi.glu_up_out + (size_t)my_row * epi.ldglu + cs;
+            if (cs + 32 <= N) {
+              uint32_t gw[16], uw[16], dw[16];
+#pragma unroll
+              for (int k4 = 0; k4 < 4; ++k4) {
+                const uint4 tg = *reinterpret_cast<const uint4 *>(gr + 8 * k4);
+                const uint4 tu = *reinterpret_cast<const uint4 *>(ur + 8 * k4);
+                gw[4 * k4] = tg.x; gw[4 * k4 + 1] = tg.y; gw[4 * k4 + 2] = tg.z; gw[4 * k4 + 3] = tg.w;
+                uw[4 * k4] = tu.x; uw[4 * k4 + 1] = tu.y; uw[4 * k4 + 2] = tu.z; uw[4 * k4 + 3] = tu.w;
+              }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                float du[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const float g = load16<false>((uint16_t)(gw[i] >> (16 * e)));
+                  const float u = load16<false>((uint16_t)(uw[i] >> (16 * e)));
+                  const float sg = __fdividef(1.0f, 1.0f + __expf(-g));
+                  const float d = v[2 * i + e];
+                  v[2 * i + e] = d * u * sg * (1.0f + g * (1.0f - sg));
+                  du[e] = d * g * sg;
+                }
+                dw[i] = pack2_16<false>(du[0], du[1]);
+              }
+#pragma unroll
+              for (int k4 = 0; k4 < 4; ++k4)
+                *reinterpret_cast<uint4 *>(dur + 8 * k4) =
+                    make_uint4(dw[4 * k4], dw[4 * k4 + 1], dw[4 * k4 + 2], dw[4 * k4 + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (cs + j >= N) continue;
+                const float g = load16<false>(gr[j]), u = load16<false>(ur[j]);
+                const float sg = __fdividef(1.0f, 1.0f + __expf(-g));
+                const float d = v[j];
+                v[j] = d * u * sg * (1.0f + g * (1.0f - sg));
+                dur[j] = (uint16_t)(pack2_16<false>(d * g * sg, 0.0f) & 0xFFFFu);
+              }
+            }
+          }
           if (epi.silu) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = bwpp_silu_f(v[j]);
@@ -880,6 +931,43 @@ int bwpp_gemm_launch_dt(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t 
   }
   return b_mn ? launch_tc_any<false, true>(ctx, ta, tb, tcm, epi, M, N, K, pair, f)
               : launch_tc_any<false, false>(ctx, ta, tb, tcm, epi, M, N, K, pair, f);
+}
+
+// d(gate | up) of a SwiGLU from the product d(a) = A B (M x F), fused into the
+// tensor-core GEMM's epilogue: dgu[m, f] = d(gate), dgu[m, F + f] = d(up),
+// read against gu = [gate | up] (all bf16, pitch ldgu = 2F or more).  The
+// fp32 d(a) is never stored.  BWPP_CUDA_ERR_UNSUPPORTED (nothing launched)
+// for shapes the tensor-core path cannot take.
+int bwpp_gemm_launch_glu_bwd(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,
+                             const uint16_t *b, int b_mn, uint32_t ldb, const uint16_t *gu,
+                             uint16_t *dgu, uint32_t ldgu, uint32_t M, uint32_t F, uint32_t K) {
+  if (M == 0 || F == 0) return BWPP_CUDA_OK;
+  if (K == 0 || !al16(a) || !al16(b) || !al16(dgu) || !al16(gu) || (lda % 8) || (ldb % 8) ||
+      (ldgu % 8) || (F % 8) || ldgu < 2 * F)
+    return BWPP_CUDA_ERR_UNSUPPORTED;
+  GemmEpi epi{};
+  epi.out_bf16 = 1;
+  epi.glu = gu;
+  epi.glu_up_out = dgu + F;
+  epi.ldglu = ldgu;
+  epi.glu_F = F;
+  const bool pair = pairs_enabled() && M > (uint32_t)BM;
+  CUtensorMap ta, tb, tcm;
+  const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  int rc = a_mn ? bwpp_make_tmap_2d(ctx, &ta, a, BF, M, K, (uint64_t)lda * 2, 64, BK, SW)
+                : bwpp_make_tmap_2d(ctx, &ta, a, BF, K, M, (uint64_t)lda * 2, BK, BM, SW);
+  if (!rc)
+    rc = b_mn ? bwpp_make_tmap_2d(ctx, &tb, b, BF, F, K, (uint64_t)ldb * 2, 64, BK, SW)
+              : bwpp_make_tmap_2d(ctx, &tb, b, BF, K, F, (uint64_t)ldb * 2, BK, 64, SW);
+  if (!rc) rc = bwpp_make_tmap_2d(ctx, &tcm, dgu, BF, F, M, (uint64_t)ldgu * 2, 64, 32, SW);
+  if (rc) return rc;
+  if (a_mn) {
+    return b_mn ? launch_tc_any<true, true>(ctx, ta, tb, tcm, epi, M, F, K, pair, 0)
+                : launch_tc_any<true, false>(ctx, ta, tb, tcm, epi, M, F, K, pair, 0);
+  }
+  return b_mn ? launch_tc_any<false, true>(ctx, ta, tb, tcm, epi, M, F, K, pair, 0)
+              : launch_tc_any<false, false>(ctx, ta, tb, tcm, epi, M, F, K, pair, 0);
 }
 
 int bwpp_gemm_launch_ex(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,

@@ -24,6 +24,9 @@ int bwpp_gemm_launch_ex(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t 
                         const uint16_t *b, int b_mn, uint32_t ldb, void *c, uint32_t ldc,
                         uint32_t M, uint32_t N, uint32_t K, const float *bias, int silu,
                         const float *residual, uint32_t ldr, int out_bf16, int force_simt);
+int bwpp_gemm_launch_glu_bwd(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,
+                             const uint16_t *b, int b_mn, uint32_t ldb, const uint16_t *gu,
+                             uint16_t *dgu, uint32_t ldgu, uint32_t M, uint32_t F, uint32_t K);
 int bwpp_cast_launch(BwppCudaCtx *ctx, const float *src, uint16_t *dst, uint32_t rows,
                      uint32_t cols, uint32_t ld_src, uint32_t ld_dst);
 int bwpp_rmsnorm_bf16out(BwppCudaCtx *ctx, const float *x, const float *gamma, uint16_t *y,
@@ -340,9 +343,17 @@ int bwpp_cuda_tiny_model_step(BwppCudaTinyModel *m, const float *x, const float 
     // h_out = h_mid + a W2
     TRY(bwpp_gemm_launch_ex(ctx, a.a, 1, F, m->dh16, 1, D, G + p.w2, D, F, D, T, nullptr, 0,
                             nullptr, 0, 0, 0));  // dW2 = a^T dh
-    TRY(bwpp_gemm_launch_ex(ctx, m->dh16, 0, D, P16 + p.w2, 0, D, m->da, F, T, F, D, nullptr, 0,
-                            nullptr, 0, 0, 0));  // da = dh W2^T
-    TRY(bwpp_swiglu_bwd(ctx, a.gu, m->da, m->dgu, T, F));
+    // da = dh W2^T and the SwiGLU backward into dgu in one GEMM (its epilogue
+    // reads gu); unfused through fp32 da where that path cannot be taken
+    rc = bwpp_gemm_launch_glu_bwd(ctx, m->dh16, 0, D, P16 + p.w2, 0, D, a.gu, m->dgu, 2 * F, T, F,
+                                  D);
+    if (rc == BWPP_CUDA_ERR_UNSUPPORTED) {
+      TRY(bwpp_gemm_launch_ex(ctx, m->dh16, 0, D, P16 + p.w2, 0, D, m->da, F, T, F, D, nullptr, 0,
+                              nullptr, 0, 0, 0));
+      TRY(bwpp_swiglu_bwd(ctx, a.gu, m->da, m->dgu, T, F));
+    } else if (rc) {
+      return rc;
+    }
     TRY(bwpp_gemm_launch_ex(ctx, a.n2, 1, D, m->dgu, 1, 2 * F, G + p.w13, 2 * F, D, 2 * F, T,
                             nullptr, 0, nullptr, 0, 0, 0));  // dW13 = n2^T dgu
     TRY(bwpp_gemm_launch_ex(ctx, m->dgu, 0, 2 * F, P16 + p.w13, 0, 2 * F, m->dtmp, D, T, D,
