@@ -291,17 +291,35 @@ __global__ void __launch_bounds__(THREADS, 1)
 // ---------------------------------------------------------------------------
 // dK, dV
 // ---------------------------------------------------------------------------
-constexpr int K_OFF_K = 0, K_OFF_V = TILE, K_OFF_Q = 2 * TILE, K_OFF_DO = 3 * TILE,
-              K_OFF_PT = 4 * TILE, K_OFF_DST = 5 * TILE, K_OFF_LSE = 6 * TILE,
-              K_OFF_BAR = K_OFF_LSE + 2 * 2 * 128 * 4;
+// Q / dO double-buffered in smem; P^T and dS^T never touch smem: the softmax
+// writes them as bf16 pairs into TMEM over the S^T / dP^T columns they were
+// computed from (half h of the 128 queries: columns 64h .. 64h+31 of S^T,
+// resp. 128 + 64h .. of dP^T, inside the range that warp itself read), and
+// the dV / dK MMAs take them as the A operand from TMEM.  MMA order per query
+// tile i:  S^T(i), dP^T(i) | dV(i) once P^T(i) is stored | S^T(i+1) (over
+// P^T(i), after dV(i) in issue order) | dK(i) once dS^T(i) is stored |
+// dP^T(i+1) (over dS^T(i)), so the exp2 work of tile i+1 overlaps dK(i).
+constexpr int K_OFF_K = 0, K_OFF_V = TILE, K_OFF_Q = 2 * TILE, K_OFF_DO = 4 * TILE,
+              K_OFF_LSE = 6 * TILE, K_OFF_BAR = K_OFF_LSE + 2 * 2 * 128 * 4;
 constexpr int K_SMEM = K_OFF_BAR + 256 + 1024;
 static_assert(K_SMEM <= 232448, "dkdv smem");
 
 struct KBars {
-  uint64_t kv_full, qd_full, qd_empty, s_full, s_free, p_full, pdone, staged, drain;
+  uint64_t kv_full, qd_full[2], qd_empty[2], s_full, dp_full, pt_full, dst_full, staged, drain;
   uint32_t tmem;
   int abort_flag;
 };
+
+// D(128 x D) (+)= A(128 x 128 queries, bf16 pairs in TMEM at the half-split
+// columns a0 + [0, 32) and a0 + [64, 96)) B(128 queries x D, MN-major smem)
+__device__ __forceinline__ void mma_tm(uint32_t d, uint32_t a0, uint32_t b, bool acc) {
+#pragma unroll
+  for (int ks = 0; ks < 128 / 16; ++ks) {
+    const uint32_t acol = a0 + (ks >> 2) * 64 + (ks & 3) * 8;
+    tc_mma_f16_ts(d, acol, make_smem_desc(b + ks * 2048, BOX, 1024, BWPP_SWIZZLE_128B), IDESC_KM,
+                  (acc || ks > 0) ? 1u : 0u);
+  }
+}
 
 __global__ void __launch_bounds__(THREADS, 1)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -324,12 +342,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->kv_full, 1);
-    mbar_init(&bar->qd_full, 1);
-    mbar_init(&bar->qd_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->qd_full[s], 1);
+      mbar_init(&bar->qd_empty[s], 1);
+    }
     mbar_init(&bar->s_full, 1);
-    mbar_init(&bar->s_free, SM_WARPS);
-    mbar_init(&bar->p_full, SM_WARPS);
-    mbar_init(&bar->pdone, 1);
+    mbar_init(&bar->dp_full, 1);
+    mbar_init(&bar->pt_full, SM_WARPS);
+    mbar_init(&bar->dst_full, SM_WARPS);
     mbar_init(&bar->staged, 32 * SM_WARPS);
     mbar_init(&bar->drain, 1);
     bar->abort_flag = 0;
@@ -350,37 +370,54 @@ __global__ void __launch_bounds__(THREADS, 1)
       load_rows<2>(smem + K_OFF_K, &tmK, &bar->kv_full, io.in, bh, Skv, k0);
       load_rows<2>(smem + K_OFF_V, &tmV, &bar->kv_full, io.in, bh, Skv, k0);
       for (int it = 0; it < n && !*abort_flag; ++it) {
-        if (!mbar_wait(&bar->qd_empty, (it & 1) ^ 1, status)) {
+        const int s = it & 1;
+        if (!mbar_wait(&bar->qd_empty[s], ((it >> 1) & 1) ^ 1, status)) {
           *abort_flag = 1;
           break;
         }
         const uint32_t qs = (i0 + it) * BM;
-        mbar_arrive_expect_tx(&bar->qd_full, 2 * TILE);
-        load_rows<2>(smem + K_OFF_Q, &tmQ, &bar->qd_full, io.in, bh, Sq, qs);
-        load_rows<2>(smem + K_OFF_DO, &tmDO, &bar->qd_full, io.in, bh, Sq, qs);
+        mbar_arrive_expect_tx(&bar->qd_full[s], 2 * TILE);
+        load_rows<2>(smem + K_OFF_Q + s * TILE, &tmQ, &bar->qd_full[s], io.in, bh, Sq, qs);
+        load_rows<2>(smem + K_OFF_DO + s * TILE, &tmDO, &bar->qd_full[s], io.in, bh, Sq, qs);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       bool ok = mbar_wait(&bar->kv_full, 0, status);
       const uint32_t ka = smem_u32(smem + K_OFF_K), va = smem_u32(smem + K_OFF_V);
-      const uint32_t qa = smem_u32(smem + K_OFF_Q), da = smem_u32(smem + K_OFF_DO);
-      const uint32_t pa = smem_u32(smem + K_OFF_PT), dsa = smem_u32(smem + K_OFF_DST);
+      auto qa = [&](int it) { return smem_u32(smem + K_OFF_Q + (it & 1) * TILE); };
+      auto da = [&](int it) { return smem_u32(smem + K_OFF_DO + (it & 1) * TILE); };
+      if (ok && n > 0) {
+        ok = mbar_wait(&bar->qd_full[0], 0, status);
+        if (ok) {
+          tc_fence_after();
+          mma_kk(tmem + 0, ka, qa(0));    // S^T(0)  = K  Q_0^T
+          tc_commit(&bar->s_full);
+          mma_kk(tmem + 128, va, da(0));  // dP^T(0) = V dO_0^T
+          tc_commit(&bar->dp_full);
+        }
+      }
       for (int it = 0; it < n && ok && !*abort_flag; ++it) {
-        ok = mbar_wait(&bar->qd_full, it & 1, status);
-        if (ok && it > 0) ok = mbar_wait(&bar->s_free, (it - 1) & 1, status);
+        ok = mbar_wait(&bar->pt_full, it & 1, status);
         if (!ok) break;
         tc_fence_after();
-        mma_kk(tmem + 0, ka, qa);    // S^T  = K  Q_i^T
-        mma_kk(tmem + 128, va, da);  // dP^T = V dO_i^T
-        tc_commit(&bar->s_full);
-        ok = mbar_wait(&bar->p_full, it & 1, status);
+        mma_tm(tmem + 256, tmem + 0, da(it), it > 0);  // dV += P^T(it) dO_it
+        if (it + 1 < n) {
+          ok = mbar_wait(&bar->qd_full[(it + 1) & 1], ((it + 1) >> 1) & 1, status);
+          if (!ok) break;
+          tc_fence_after();
+          mma_kk(tmem + 0, ka, qa(it + 1));  // S^T(it+1), after dV(it) read P^T(it)
+          tc_commit(&bar->s_full);
+        }
+        ok = mbar_wait(&bar->dst_full, it & 1, status);
         if (!ok) break;
         tc_fence_after();
-        mma_km(tmem + 256, pa, da, it > 0);   // dV += P^T  dO_i
-        mma_km(tmem + 384, dsa, qa, it > 0);  // dK += dS^T Q_i
-        tc_commit(&bar->pdone);
-        tc_commit(&bar->qd_empty);
+        mma_tm(tmem + 384, tmem + 128, qa(it), it > 0);  // dK += dS^T(it) Q_it
+        tc_commit(&bar->qd_empty[it & 1]);
+        if (it + 1 < n) {
+          mma_kk(tmem + 128, va, da(it + 1));  // dP^T(it+1), after dK(it) read dS^T(it)
+          tc_commit(&bar->dp_full);
+        }
       }
       if (!ok) *abort_flag = 1;
       tc_commit(&bar->drain);
@@ -393,8 +430,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int tid = (threadIdx.x - 64) & 127;  // both halves stage the same 128 values
     const uint32_t key = k0 + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    uint8_t *pt_tile = smem + K_OFF_PT;
-    uint8_t *dst_tile = smem + K_OFF_DST;
     bool ok = true;
     for (int it = 0; it < n && ok; ++it) {
       const uint32_t qs = (i0 + it) * BM;
@@ -414,12 +449,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      // P^T / dS^T smem free once dV / dK of the previous tile are done
-      if (it > 0 && !mbar_wait(&bar->pdone, (it - 1) & 1, status)) {
-        *abort_flag = 1;
-        ok = false;
-        break;
-      }
       // query q = qs + col is visible to this key iff q >= key (causal),
       // q < Sq and key < Skv
       int first_rel = causal ? (int)key - (int)qs : 0;  // first visible col
@@ -427,43 +456,66 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int last_rel = key < Skv ? (int)min(Sq - 1 - qs, (uint32_t)127) : -1;
       const float *ls = lse_s + (it & 1) * 128;
       const float *dd = del_s + (it & 1) * 128;
-#pragma unroll 1
-      for (int c = half * (BM / 64); c < (half + 1) * (BM / 64); ++c) {
-        uint32_t rs[32], rp[32];
+      // P^T for this warp's 64 queries: registers, and bf16 pairs into TMEM
+      float p[64];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = half * 2 + cc;
+        uint32_t rs[32];
         tmem_ld_32x32b_x32(tmem + lane_base + c * 32, rs);
-        tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, rp);
         tc_wait_ld(rs);
-        tc_wait_ld(rp);
-        uint32_t pk[16], dk[16];
+        uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float p[2], ds[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int col = c * 32 + 2 * i + e;
             const bool vis = col >= first_rel && col <= last_rel;
-            p[e] = vis ? fast_exp2(fmaf(__uint_as_float(rs[2 * i + e]), scale_log2, -ls[col])) : 0.0f;
-            ds[e] = p[e] * (__uint_as_float(rp[2 * i + e]) - dd[col]);
+            p[cc * 32 + 2 * i + e] =
+                vis ? fast_exp2(fmaf(__uint_as_float(rs[2 * i + e]), scale_log2, -ls[col])) : 0.0f;
           }
-          pk[i] = pack_bf16(p[0], p[1]);
-          dk[i] = pack_bf16(ds[0], ds[1]);
+          pk[i] = pack_bf16(p[cc * 32 + 2 * i], p[cc * 32 + 2 * i + 1]);
         }
-        store_swizzled_chunk(pt_tile, row, c, pk);
-        store_swizzled_chunk(dst_tile, row, c, dk);
+        tmem_st_32x32b_x16(tmem + lane_base + half * 64 + cc * 16, pk);
       }
-      fence_proxy_async_smem();
+      tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bar->s_free);
-        mbar_arrive(&bar->p_full);
+      if (lane == 0) mbar_arrive(&bar->pt_full);  // also: S^T(it) has been read
+      if (!mbar_wait(&bar->dp_full, it & 1, status)) {
+        *abort_flag = 1;
+        ok = false;
+        break;
       }
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = half * 2 + cc;
+        uint32_t rp[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, rp);
+        tc_wait_ld(rp);
+        uint32_t dk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int col = c * 32 + 2 * i;
+          dk[i] = pack_bf16(p[cc * 32 + 2 * i] * (__uint_as_float(rp[2 * i]) - dd[col]),
+                            p[cc * 32 + 2 * i + 1] * (__uint_as_float(rp[2 * i + 1]) - dd[col + 1]));
+        }
+        tmem_st_32x32b_x16(tmem + lane_base + 128 + half * 64 + cc * 16, dk);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->dst_full);  // also: dP^T(it) has been read
     }
     const bool valid = key < Skv;
     uint16_t *dk_dst = io.d0 + ((size_t)(bh / io.in.H) * Skv + key) * io.ldd + (size_t)(bh % io.in.H) * D;
     uint16_t *dv_dst = io.d1 + ((size_t)(bh / io.in.H) * Skv + key) * io.ldd + (size_t)(bh % io.in.H) * D;
     if (ok && n > 0) {
-      if (mbar_wait(&bar->pdone, (n - 1) & 1, status)) {
+      // every MMA, dK(n-1) last, has completed when the drain-side commit of
+      // qd_empty for the last tile has arrived
+      const int s = (n - 1) & 1;
+      if (mbar_wait(&bar->qd_empty[s], ((n - 1) >> 1) & 1, status)) {
         tc_fence_after();
         store_row_bf16(tmem + lane_base + 256, dv_dst, 1.0f, valid, half);
         store_row_bf16(tmem + lane_base + 384, dk_dst, scale, valid, half);
