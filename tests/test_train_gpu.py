@@ -40,7 +40,9 @@ def heads(t, B, S, H, D=128):  # token-major [B*S, H*D] -> [B, H, S, D]
     return t.reshape(B, S, H, D).permute(0, 2, 1, 3)
 
 
-@pytest.mark.parametrize("B,H,S", [(2, 2, 256), (1, 3, 384), (2, 1, 128)])
+# (1, 2, 1024): 8 query / key tiles, so every pipeline barrier wraps its
+# phase several times; (1, 1, 200): a ragged last tile (zero-filled rows)
+@pytest.mark.parametrize("B,H,S", [(2, 2, 256), (1, 3, 384), (2, 1, 128), (1, 2, 1024), (1, 1, 200)])
 @pytest.mark.parametrize("causal", [1, 0])
 def test_attention_fwd_lse_and_bwd(ctx, B, H, S, causal):
     D, lib = 128, bwpp.load()
