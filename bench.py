@@ -7,8 +7,8 @@
                                 reduce_max_fwd|reduce_max_bwd|softmax_fwd|
                                 softmax_grad|silu_grad|reduce_sum_rows|
                                 reduce_sum_cols|broadcast_rows|gemm_f16|
-                                attention_f16|attention_causal_f16|tiny_model|
-                                plan_tiny_model]
+                                attention_f16|attention_causal_f16|attention_bwd|
+                                tiny_model|plan_tiny_model]
 
 Default workload (the headline): fused matmul + bias +
 SiLU, X[8192x4096] bf16 * W[4096x11008] bf16 + b[11008], fp32 out, rows of X
@@ -344,6 +344,82 @@ class AttentionWorkload(Workload):
         return flops, dt, f"{rows} query rows of one (b,h), S={self.S}, d={self.D}, fp32, {threads} threads"
 
 
+class AttentionBwdWorkload(Workload):
+    """Attention backward of the tiny_model training step (16 x 128
+    heads, causal, seq 2048, batch 16 per GPU): bwpp_cuda_attention_bwd_bf16 (delta, then
+    the dQ and dK/dV kernels) on token-major bf16 Q, K, V, O, dO; batch over ranks.
+    Work is counted as 2.5 x the causal forward's FLOPs (five products of the forward's
+    size: S, dP and the dQ / dK / dV products, the recomputed S^T / dP^T not counted)."""
+    B, H, S, D = 16, 16, 2048, 128
+    kernel = "bwd_dq_kernel + bwd_dkdv_kernel"
+    profile = "attention_bwd_tiny_model"
+    e2e_api = "bwpp_cuda_attention_bwd_bf16; pinned host Q, K, V, O, dO, lse in, dQ, dK, dV out"
+
+    def setup(self):
+        t = self.torch
+        self.b0, self.b1 = split_rows(self.B, self.rank, self.world)
+        self.nb = self.b1 - self.b0
+        T, HD = self.nb * self.S, self.H * self.D
+        g = t.Generator(device="cuda").manual_seed(6000 + self.b0)
+        self.q, self.k, self.v, self.do = (t.randn(T, HD, device="cuda", generator=g).to(t.bfloat16)
+                                           for _ in range(4))
+        self.o = t.empty(T, HD, dtype=t.bfloat16, device="cuda")
+        self.lse = t.empty(self.nb * self.H * self.S, device="cuda")
+        self.dq, self.dk, self.dv = (t.empty(T, HD, dtype=t.bfloat16, device="cuda") for _ in range(3))
+        self.lib = self.bwpp.load()
+        self.ctx.check(self.lib.bwpp_cuda_attention_fwd_lse_bf16(
+            self.ctx.handle, self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), HD, self.nb,
+            self.H, self.S, self.D ** -0.5, 1, self.o.data_ptr(), HD, self.lse.data_ptr()), "fwd_lse")
+        self.ctx.sync()
+
+    def _bwd(self, q, k, v, o, do, lse, dq, dk, dv):
+        HD = self.H * self.D
+        self.ctx.check(self.lib.bwpp_cuda_attention_bwd_bf16(
+            self.ctx.handle, q.data_ptr(), k.data_ptr(), v.data_ptr(), HD, o.data_ptr(), HD,
+            do.data_ptr(), HD, lse.data_ptr(), self.nb, self.H, self.S, self.D ** -0.5, 1,
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), HD), "attention bwd")
+
+    def step(self):
+        self._bwd(self.q, self.k, self.v, self.o, self.do, self.lse, self.dq, self.dk, self.dv)
+        return 3  # delta, dQ, dK / dV
+
+    def flops_per_head(self):
+        return 2.5 * 4.0 * self.D * self.S * (self.S + 1) / 2
+
+    def work_per_step(self):
+        return self.nb * self.H * self.flops_per_head()
+
+    def total_work_per_step(self):
+        return self.B * self.H * self.flops_per_head()
+
+    def config(self):
+        return {"workload": "attention backward, causal (the tiny_model step's attention, "
+                            "BASELINE configs[4])",
+                "B": self.B, "H": self.H, "S": self.S, "D": self.D, "batch_per_gpu": self.nb,
+                "parallelism": f"batch over {self.world} GPU(s), no collective",
+                "flops": "2.5 x the causal forward (S, dP, dQ, dK, dV products)",
+                "l2": "256 MiB written between timed steps (flush)"}
+
+    def setup_e2e(self):
+        t = self.torch
+        self.hin = [u.cpu().pin_memory() for u in (self.q, self.k, self.v, self.o, self.do, self.lse)]
+        self.hout = [t.empty_like(u, device="cpu").pin_memory() for u in (self.dq, self.dk, self.dv)]
+        self.h2d = sum(u.numel() * u.element_size() for u in self.hin)
+        self.d2h = sum(u.numel() * u.element_size() for u in self.hout)
+
+    def step_e2e(self):
+        dev = (self.q, self.k, self.v, self.o, self.do, self.lse)
+        for d, h in zip(dev, self.hin):
+            d.copy_(h, non_blocking=True)
+        self.step()
+        for h, d in zip(self.hout, (self.dq, self.dk, self.dv)):
+            h.copy_(d, non_blocking=True)
+        self.torch.cuda.synchronize()
+
+    def cpu_sample(self, lib, threads):
+        return None  # the reference has no attention backward
+
+
 class AttentionF16Workload(AttentionWorkload):
     """configs[3] shapes through the half ABI (bwpp_cuda_attention_f16)."""
     dtype = "f16"
@@ -662,6 +738,8 @@ def make_workload(name, *a):
         return AttentionWorkload(*a, causal=name.endswith("causal"))
     if name in ("attention_f16", "attention_causal_f16"):
         return AttentionF16Workload(*a, causal="causal" in name)
+    if name == "attention_bwd":
+        return AttentionBwdWorkload(*a)
     return RowWorkload(*a, op=name)
 
 
@@ -679,6 +757,9 @@ def reference_config(name, world):
     elif isinstance(wl, AttentionWorkload):
         wl.h0, wl.h1 = split_rows(wl.B * wl.H, 0, world)
         wl.nh = wl.h1 - wl.h0
+    elif isinstance(wl, AttentionBwdWorkload):
+        wl.b0, wl.b1 = split_rows(wl.B, 0, world)
+        wl.nb = wl.b1 - wl.b0
     elif isinstance(wl, RowWorkload):
         wl.r0, wl.r1 = split_rows(wl.R, 0, world)
         wl.m = wl.r1 - wl.r0
@@ -700,6 +781,10 @@ def run_reference(args, world):
     threads = O.cpu_threads()
     wl = make_workload(args.workload, 0, 1, None, None, None)
     cfg = reference_config(args.workload, world)
+    if wl.cpu_sample(lib, threads) is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          f"the reference has no CPU implementation of {args.workload}"}), flush=True)
+        return
     for _ in range(args.warmup):
         wl.cpu_sample(lib, threads)
     work, secs = 0.0, 0.0

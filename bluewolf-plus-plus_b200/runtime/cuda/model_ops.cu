@@ -87,6 +87,27 @@ __global__ void swiglu_fwd_kernel(const uint16_t *__restrict__ gu, uint16_t *__r
   }
 }
 
+// The same, 8 columns per thread (128-bit loads and stores, 32-bit index
+// arithmetic): F % 8 == 0, rows * F / 8 < 2^32, 16-byte aligned rows.
+__global__ void swiglu_fwd_v8_kernel(const uint16_t *__restrict__ gu, uint16_t *__restrict__ a,
+                                     uint32_t rows, uint32_t F) {
+  const uint32_t fv = F / 8, n = rows * fv;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const uint32_t t = i / fv, f = (i - t * fv) * 8;
+    const uint4 g4 = __ldcs(reinterpret_cast<const uint4 *>(gu + (size_t)t * 2 * F + f));
+    const uint4 u4 = __ldcs(reinterpret_cast<const uint4 *>(gu + (size_t)t * 2 * F + F + f));
+    const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w}, uw[4] = {u4.x, u4.y, u4.z, u4.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float g0 = __uint_as_float(gw[k] << 16), g1 = __uint_as_float(gw[k] & 0xFFFF0000u);
+      const float u0 = __uint_as_float(uw[k] << 16), u1 = __uint_as_float(uw[k] & 0xFFFF0000u);
+      o[k] = f2bf2(g0 * sigmoidf_(g0) * u0, g1 * sigmoidf_(g1) * u1);
+    }
+    __stcs(reinterpret_cast<uint4 *>(a + (size_t)t * F + f), make_uint4(o[0], o[1], o[2], o[3]));
+  }
+}
+
 // dgu[t, f] = da * up * silu'(gate), dgu[t, F + f] = da * silu(gate)
 // silu'(g) = s (1 + g (1 - s)), s = sigmoid(g); da is fp32 [rows, F].
 __global__ void swiglu_bwd_kernel(const uint16_t *__restrict__ gu, const float *__restrict__ da,
@@ -146,6 +167,33 @@ __global__ void loss_sum_kernel(const float *__restrict__ part, uint32_t nparts,
 
 // delta[(b*H + h) * S + s] = sum_d dO[t, h*Dh + d] * O[t, h*Dh + d], t = b*S + s
 // (token-major bf16 [T, H*Dh]); one warp per (t, h), Dh = 128.
+// delta[b, h, s] = sum_d dO[t, h, d] * O[t, h, d] for head dim 128: a half
+// warp per (token, head), 16-byte loads, 32-bit indices, grid-stride.
+__global__ void attn_delta128_kernel(const uint16_t *__restrict__ dO,
+                                     const uint16_t *__restrict__ Ot, float *__restrict__ delta,
+                                     uint32_t S, uint32_t H, uint32_t items) {
+  const uint32_t lane16 = threadIdx.x & 15;
+  for (uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 4; w < items;
+       w += (gridDim.x * blockDim.x) >> 4) {
+    const size_t off = (size_t)w * 128 + lane16 * 8;  // token-major, head h at column 128 h
+    const uint4 x = __ldcs(reinterpret_cast<const uint4 *>(dO + off));
+    const uint4 y = __ldcs(reinterpret_cast<const uint4 *>(Ot + off));
+    const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, yw[4] = {y.x, y.y, y.z, y.w};
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      s += __uint_as_float(xw[k] << 16) * __uint_as_float(yw[k] << 16) +
+           __uint_as_float(xw[k] & 0xFFFF0000u) * __uint_as_float(yw[k] & 0xFFFF0000u);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane16 == 0) {
+      const uint32_t t = w / H, h = w - t * H;
+      const uint32_t b_ = t / S, s_ = t - b_ * S;
+      delta[((size_t)b_ * H + h) * S + s_] = s;
+    }
+  }
+}
+
 __global__ void attn_delta_kernel(const uint16_t *__restrict__ dO, const uint16_t *__restrict__ Ot,
                                   float *__restrict__ delta, uint32_t B, uint32_t S, uint32_t H,
                                   uint32_t Dh) {
@@ -240,6 +288,13 @@ int bwpp_rmsnorm_bf16out(BwppCudaCtx *ctx, const float *x, const float *gamma, u
 
 int bwpp_swiglu_fwd(BwppCudaCtx *ctx, const uint16_t *gu, uint16_t *a, uint32_t rows, uint32_t F) {
   if (F % 2) return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "swiglu: odd F");
+  if (F % 8 == 0 && (size_t)rows * (F / 8) < (1ull << 31) &&
+      (reinterpret_cast<uintptr_t>(gu) & 15) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+    swiglu_fwd_v8_kernel<<<grid_for(ctx, (size_t)rows * F / 8, 256), 256, 0, ctx->stream>>>(
+        gu, a, rows, F);
+    BWPP_LAUNCH_CHECK(ctx, "swiglu fwd");
+    return BWPP_CUDA_OK;
+  }
   swiglu_fwd_kernel<<<grid_for(ctx, (size_t)rows * F / 2, 256), 256, 0, ctx->stream>>>(gu, a, rows, F);
   BWPP_LAUNCH_CHECK(ctx, "swiglu fwd");
   return BWPP_CUDA_OK;
@@ -269,6 +324,13 @@ int bwpp_mse(BwppCudaCtx *ctx, const float *h, const float *t, float *dh, uint16
 int bwpp_attn_delta(BwppCudaCtx *ctx, const uint16_t *dO, const uint16_t *O, float *delta,
                     uint32_t B, uint32_t S, uint32_t H, uint32_t Dh) {
   const uint64_t warps = (uint64_t)B * S * H;
+  if (Dh == 128 && warps < (1ull << 31) && (reinterpret_cast<uintptr_t>(dO) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(O) & 15) == 0) {
+    attn_delta128_kernel<<<grid_for(ctx, warps * 16, 256), 256, 0, ctx->stream>>>(
+        dO, O, delta, S, H, (uint32_t)warps);
+    BWPP_LAUNCH_CHECK(ctx, "attention delta");
+    return BWPP_CUDA_OK;
+  }
   attn_delta_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, ctx->stream>>>(dO, O, delta, B,
                                                                                    S, H, Dh);
   BWPP_LAUNCH_CHECK(ctx, "attention delta");
