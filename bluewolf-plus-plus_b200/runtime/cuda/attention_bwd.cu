@@ -100,11 +100,33 @@ static_assert(Q_SMEM <= 232448, "dq smem");
 //            dS(j) = P (dP(j) - delta) -> smem -> ds_full
 // so S(j+1) and dQ(j) run on the tensor core while the softmax finishes
 // block j, and the exp2 work of block j+1 overlaps dP(j+1).
+// Persistent: one CTA per SM walks the (head, 128-row tile) items heaviest
+// first (item i: tile qtiles-1 - i / BH of head i % BH), CTA c taking items
+// c, c + grid, ...  Block-level barrier phases follow a block counter that
+// runs on across items.  The two dQ accumulators (TMEM columns 256, 384)
+// alternate between items, so an item's dQ store overlaps the next item's
+// MMAs; Q / dO are released after an item's last S / dP MMA, so the next
+// item's loads overlap its tail.
 struct QBars {
-  uint64_t qd_full, kv_full[2], kv_empty[2], s_full, dp_full, s_read, ds_full, dq_done, drain;
+  uint64_t qd_full, qd_empty, kv_full[2], kv_empty[2], s_full, dp_full, s_read, ds_full, dq_done,
+      acc_free[2], drain;
   uint32_t tmem;
   int abort_flag;
 };
+
+struct QItem {
+  uint32_t bh, q0;
+  int n;
+};
+
+__device__ __forceinline__ QItem q_item(uint32_t i, uint32_t BH, uint32_t qtiles, uint32_t Sq,
+                                        uint32_t Skv, int causal) {
+  QItem it;
+  it.bh = i % BH;
+  it.q0 = (qtiles - 1 - i / BH) * BM;  // heavy first
+  it.n = blocks_for(it.q0, Sq, Skv, causal);
+  return it;
+}
 
 __global__ void __launch_bounds__(THREADS, 1)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -116,16 +138,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
   QBars *bar = reinterpret_cast<QBars *>(smem + Q_OFF_BAR);
   volatile int *abort_flag = &bar->abort_flag;
-  const uint32_t bh = blockIdx.x / qtiles;
-  const uint32_t q0 = (qtiles - 1 - blockIdx.x % qtiles) * BM;  // heavy first
-  const int n = blocks_for(q0, Sq, Skv, causal);
+  const uint32_t items = BH * qtiles;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->qd_full, 1);
+    mbar_init(&bar->qd_empty, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar->kv_full[s], 1);
       mbar_init(&bar->kv_empty[s], 1);
+      mbar_init(&bar->acc_free[s], SM_WARPS);
     }
     mbar_init(&bar->s_full, 1);
     mbar_init(&bar->dp_full, 1);
@@ -143,60 +165,83 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = bar->tmem;  // S at 0, dP at 128, dQ at 256
+  const uint32_t tmem = bar->tmem;  // S at 0, dP at 128, dQ at 256 / 384 (by item parity)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(&bar->qd_full, 2 * TILE);
-      load_rows<2>(smem + Q_OFF_Q, &tmQ, &bar->qd_full, io.in, bh, Sq, q0);
-      load_rows<2>(smem + Q_OFF_DO, &tmDO, &bar->qd_full, io.in, bh, Sq, q0);
-      for (int j = 0; j < n && !*abort_flag; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&bar->kv_empty[s], ((j >> 1) & 1) ^ 1, status)) {
+      uint32_t kvc = 0;  // K / V blocks loaded
+      int k = 0;         // items with work, in every role
+      for (uint32_t i = blockIdx.x; i < items && !*abort_flag; i += gridDim.x) {
+        const QItem it = q_item(i, BH, qtiles, Sq, Skv, causal);
+        if (it.n == 0) continue;
+        if (!mbar_wait(&bar->qd_empty, (k++ & 1) ^ 1, status)) {
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&bar->kv_full[s], 2 * TILE);
-        load_rows<2>(smem + Q_OFF_K + s * TILE, &tmK, &bar->kv_full[s], io.in, bh, Skv, j * BN);
-        load_rows<2>(smem + Q_OFF_V + s * TILE, &tmV, &bar->kv_full[s], io.in, bh, Skv, j * BN);
+        mbar_arrive_expect_tx(&bar->qd_full, 2 * TILE);
+        load_rows<2>(smem + Q_OFF_Q, &tmQ, &bar->qd_full, io.in, it.bh, Sq, it.q0);
+        load_rows<2>(smem + Q_OFF_DO, &tmDO, &bar->qd_full, io.in, it.bh, Sq, it.q0);
+        for (int j = 0; j < it.n && !*abort_flag; ++j, ++kvc) {
+          const int s = kvc & 1;
+          if (!mbar_wait(&bar->kv_empty[s], ((kvc >> 1) & 1) ^ 1, status)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&bar->kv_full[s], 2 * TILE);
+          load_rows<2>(smem + Q_OFF_K + s * TILE, &tmK, &bar->kv_full[s], io.in, it.bh, Skv, j * BN);
+          load_rows<2>(smem + Q_OFF_V + s * TILE, &tmV, &bar->kv_full[s], io.in, it.bh, Skv, j * BN);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      bool ok = mbar_wait(&bar->qd_full, 0, status);
       const uint32_t qa = smem_u32(smem + Q_OFF_Q), da = smem_u32(smem + Q_OFF_DO);
       const uint32_t dsa = smem_u32(smem + Q_OFF_DS);
-      auto ka = [&](int j) { return smem_u32(smem + Q_OFF_K + (j & 1) * TILE); };
-      auto va = [&](int j) { return smem_u32(smem + Q_OFF_V + (j & 1) * TILE); };
-      if (ok && n > 0) {
-        ok = mbar_wait(&bar->kv_full[0], 0, status);
-        if (ok) {
-          tc_fence_after();
-          mma_kk(tmem + 0, qa, ka(0));    // S(0)  = Q  K_0^T
-          tc_commit(&bar->s_full);
-          mma_kk(tmem + 128, da, va(0));  // dP(0) = dO V_0^T
-          tc_commit(&bar->dp_full);
-        }
-      }
-      for (int j = 0; j < n && ok && !*abort_flag; ++j) {
-        if (j + 1 < n) {
-          ok = mbar_wait(&bar->kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, status) &&
-               mbar_wait(&bar->s_read, j & 1, status);
-          if (!ok) break;
-          tc_fence_after();
-          mma_kk(tmem + 0, qa, ka(j + 1));  // S(j+1), over the S(j) just read
-          tc_commit(&bar->s_full);
-        }
-        ok = mbar_wait(&bar->ds_full, j & 1, status);
+      auto ka = [&](uint32_t c) { return smem_u32(smem + Q_OFF_K + (c & 1) * TILE); };
+      auto va = [&](uint32_t c) { return smem_u32(smem + Q_OFF_V + (c & 1) * TILE); };
+      uint32_t g = 0;  // key blocks of all earlier items (the K / V stage counter too)
+      bool ok = true;
+      int k = -1;
+      for (uint32_t i = blockIdx.x; i < items && ok && !*abort_flag; i += gridDim.x) {
+        const QItem it = q_item(i, BH, qtiles, Sq, Skv, causal);
+        if (it.n == 0) continue;
+        ++k;
+        const uint32_t acc = tmem + 256 + (uint32_t)(k & 1) * 128;
+        // block 0: S and dP (the previous item's last S / dP were read before
+        // its last dS was published, which its last dQ waited for)
+        ok = mbar_wait(&bar->qd_full, k & 1, status) &&
+             mbar_wait(&bar->kv_full[g & 1], (g >> 1) & 1, status) &&
+             (k < 2 || mbar_wait(&bar->acc_free[k & 1], ((k >> 1) - 1) & 1, status));
         if (!ok) break;
         tc_fence_after();
-        mma_km(tmem + 256, dsa, ka(j), j > 0);  // dQ += dS(j) K_j
-        tc_commit(&bar->dq_done);
-        tc_commit(&bar->kv_empty[j & 1]);
-        if (j + 1 < n) {
-          mma_kk(tmem + 128, da, va(j + 1));  // dP(j+1), over the dP(j) read for dS(j)
-          tc_commit(&bar->dp_full);
+        mma_kk(tmem + 0, qa, ka(g));    // S  = Q  K_0^T
+        tc_commit(&bar->s_full);
+        mma_kk(tmem + 128, da, va(g));  // dP = dO V_0^T
+        tc_commit(&bar->dp_full);
+        if (it.n == 1) tc_commit(&bar->qd_empty);  // Q / dO: last S / dP issued
+        for (int j = 0; j < it.n && ok && !*abort_flag; ++j) {
+          const uint32_t gj = g + (uint32_t)j;
+          if (j + 1 < it.n) {
+            ok = mbar_wait(&bar->kv_full[(gj + 1) & 1], ((gj + 1) >> 1) & 1, status) &&
+                 mbar_wait(&bar->s_read, gj & 1, status);
+            if (!ok) break;
+            tc_fence_after();
+            mma_kk(tmem + 0, qa, ka(gj + 1));  // S(j+1), over the S(j) just read
+            tc_commit(&bar->s_full);
+          }
+          ok = mbar_wait(&bar->ds_full, gj & 1, status);
+          if (!ok) break;
+          tc_fence_after();
+          mma_km(acc, dsa, ka(gj), j > 0);  // dQ += dS(j) K_j
+          tc_commit(&bar->dq_done);
+          tc_commit(&bar->kv_empty[gj & 1]);
+          if (j + 1 < it.n) {
+            mma_kk(tmem + 128, da, va(gj + 1));  // dP(j+1), over the dP(j) read for dS(j)
+            tc_commit(&bar->dp_full);
+            if (j + 2 == it.n) tc_commit(&bar->qd_empty);
+          }
         }
+        g += (uint32_t)it.n;
       }
       if (!ok) *abort_flag = 1;
       tc_commit(&bar->drain);
@@ -206,78 +251,98 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;  // which 64 columns of each block
     const int row = quarter * 32 + lane;
-    const uint32_t m = q0 + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    const bool valid = m < Sq;
-    const float lse = valid ? io.lse[(size_t)bh * Sq + m] : INFINITY;
-    const float dl = valid ? io.delta[(size_t)bh * Sq + m] : 0.0f;
     uint8_t *ds_tile = smem + Q_OFF_DS;
     bool ok = true;
-    for (int j = 0; j < n && ok; ++j) {
-      if (*abort_flag || !mbar_wait(&bar->s_full, j & 1, status)) {
-        *abort_flag = 1;
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t n0 = (uint32_t)j * BN;
-      uint32_t lim = Skv - 1;
-      if (causal && m < lim) lim = m;
-      const int lim_rel = (int)lim - (int)n0;
-      // P for this warp's 64 columns, kept in registers
-      float p[BN / 2];
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = half * 2 + cc;
-        uint32_t rs[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + c * 32, rs);
-        tc_wait_ld(rs);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = c * 32 + i;
-          p[cc * 32 + i] = (col <= lim_rel)
-                               ? fast_exp2(fmaf(__uint_as_float(rs[i]), scale_log2, -lse))
-                               : 0.0f;
+    uint32_t g = 0;
+    int k = -1;
+    for (uint32_t i = blockIdx.x; i < items && ok; i += gridDim.x) {
+      const QItem it = q_item(i, BH, qtiles, Sq, Skv, causal);
+      if (it.n == 0) continue;
+      ++k;
+      const uint32_t bh = it.bh, m = it.q0 + row;
+      const bool valid = m < Sq;
+      const float lse = valid ? io.lse[(size_t)bh * Sq + m] : INFINITY;
+      const float dl = valid ? io.delta[(size_t)bh * Sq + m] : 0.0f;
+      const uint32_t acc = tmem + 256 + (uint32_t)(k & 1) * 128;
+      for (int j = 0; j < it.n && ok; ++j) {
+        const uint32_t gj = g + (uint32_t)j;
+        if (*abort_flag || !mbar_wait(&bar->s_full, gj & 1, status)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        const uint32_t n0 = (uint32_t)j * BN;
+        uint32_t lim = Skv - 1;
+        if (causal && m < lim) lim = m;
+        const int lim_rel = (int)lim - (int)n0;
+        // P for this warp's 64 columns, kept in registers (both 32-column
+        // loads in flight before one wait)
+        float p[BN / 2];
+        {
+          uint32_t rs[2][32];
+          tmem_ld_32x32b_x32(tmem + lane_base + half * 64, rs[0]);
+          tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, rs[1]);
+          tc_wait_ld(rs[0]);
+          tc_wait_ld(rs[1]);
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int col = (half * 2 + cc) * 32 + e;
+              p[cc * 32 + e] = (col <= lim_rel)
+                                   ? fast_exp2(fmaf(__uint_as_float(rs[cc][e]), scale_log2, -lse))
+                                   : 0.0f;
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->s_read);  // S(j+1) may now overwrite S(j)
+        // dS smem is free once the dQ MMA of the previous block is done
+        if (!mbar_wait(&bar->dp_full, gj & 1, status) ||
+            (gj > 0 && !mbar_wait(&bar->dq_done, (gj - 1) & 1, status))) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        {
+          uint32_t rp[2][32];
+          tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64, rp[0]);
+          tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, rp[1]);
+          tc_wait_ld(rp[0]);
+          tc_wait_ld(rp[1]);
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              pk[e] = pack_bf16(p[cc * 32 + 2 * e] * (__uint_as_float(rp[cc][2 * e]) - dl),
+                                p[cc * 32 + 2 * e + 1] * (__uint_as_float(rp[cc][2 * e + 1]) - dl));
+            store_swizzled_chunk(ds_tile, row, half * 2 + cc, pk);
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->ds_full);  // also: dP(j) has been read
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->s_read);  // S(j+1) may now overwrite S(j)
-      // dS smem is free once dQ(j-1) is done
-      if (!mbar_wait(&bar->dp_full, j & 1, status) ||
-          (j > 0 && !mbar_wait(&bar->dq_done, (j - 1) & 1, status))) {
+      if (!ok) break;
+      g += (uint32_t)it.n;
+      // this item's dQ: all its MMAs are done when its last dq_done arrives
+      if (!mbar_wait(&bar->dq_done, (g - 1) & 1, status)) {
         *abort_flag = 1;
         ok = false;
         break;
       }
       tc_fence_after();
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = half * 2 + cc;
-        uint32_t rp[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, rp);
-        tc_wait_ld(rp);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          pk[i] = pack_bf16(p[cc * 32 + 2 * i] * (__uint_as_float(rp[2 * i]) - dl),
-                            p[cc * 32 + 2 * i + 1] * (__uint_as_float(rp[2 * i + 1]) - dl));
-        store_swizzled_chunk(ds_tile, row, c, pk);
-      }
-      fence_proxy_async_smem();
+      uint16_t *dst = io.d0 + ((size_t)(bh / io.in.H) * Sq + m) * io.ldd +
+                      (size_t)(bh % io.in.H) * D;
+      store_row_bf16(acc + lane_base, dst, scale, valid, half);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->ds_full);  // also: dP(j) has been read
-    }
-    if (ok && n > 0) {
-      if (mbar_wait(&bar->dq_done, (n - 1) & 1, status)) {
-        tc_fence_after();
-        uint16_t *dst = io.d0 + ((size_t)(bh / io.in.H) * Sq + m) * io.ldd +
-                        (size_t)(bh % io.in.H) * D;
-        store_row_bf16(tmem + lane_base + 256, dst, scale, valid, half);
-      } else {
-        *abort_flag = 1;
-      }
+      if (lane == 0) mbar_arrive(&bar->acc_free[k & 1]);
     }
   }
   tc_fence_before();
@@ -458,25 +523,30 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float *dd = del_s + (it & 1) * 128;
       // P^T for this warp's 64 queries: registers, and bf16 pairs into TMEM
       float p[64];
+      {
+        uint32_t rs[2][32];  // both 32-column loads in flight before one wait
+        tmem_ld_32x32b_x32(tmem + lane_base + half * 64, rs[0]);
+        tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, rs[1]);
+        tc_wait_ld(rs[0]);
+        tc_wait_ld(rs[1]);
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = half * 2 + cc;
-        uint32_t rs[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + c * 32, rs);
-        tc_wait_ld(rs);
-        uint32_t pk[16];
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = half * 2 + cc;
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < 16; ++i) {
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int col = c * 32 + 2 * i + e;
-            const bool vis = col >= first_rel && col <= last_rel;
-            p[cc * 32 + 2 * i + e] =
-                vis ? fast_exp2(fmaf(__uint_as_float(rs[2 * i + e]), scale_log2, -ls[col])) : 0.0f;
+            for (int e = 0; e < 2; ++e) {
+              const int col = c * 32 + 2 * i + e;
+              const bool vis = col >= first_rel && col <= last_rel;
+              p[cc * 32 + 2 * i + e] =
+                  vis ? fast_exp2(fmaf(__uint_as_float(rs[cc][2 * i + e]), scale_log2, -ls[col]))
+                      : 0.0f;
+            }
+            pk[i] = pack_bf16(p[cc * 32 + 2 * i], p[cc * 32 + 2 * i + 1]);
           }
-          pk[i] = pack_bf16(p[cc * 32 + 2 * i], p[cc * 32 + 2 * i + 1]);
+          tmem_st_32x32b_x16(tmem + lane_base + half * 64 + cc * 16, pk);
         }
-        tmem_st_32x32b_x16(tmem + lane_base + half * 64 + cc * 16, pk);
       }
       tc_wait_st();
       tc_fence_before();
@@ -488,20 +558,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
+      {
+        uint32_t rp[2][32];
+        tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64, rp[0]);
+        tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, rp[1]);
+        tc_wait_ld(rp[0]);
+        tc_wait_ld(rp[1]);
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = half * 2 + cc;
-        uint32_t rp[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + 128 + c * 32, rp);
-        tc_wait_ld(rp);
-        uint32_t dk[16];
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = half * 2 + cc;
+          uint32_t dk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = c * 32 + 2 * i;
-          dk[i] = pack_bf16(p[cc * 32 + 2 * i] * (__uint_as_float(rp[2 * i]) - dd[col]),
-                            p[cc * 32 + 2 * i + 1] * (__uint_as_float(rp[2 * i + 1]) - dd[col + 1]));
+          for (int i = 0; i < 16; ++i) {
+            const int col = c * 32 + 2 * i;
+            dk[i] = pack_bf16(p[cc * 32 + 2 * i] * (__uint_as_float(rp[cc][2 * i]) - dd[col]),
+                              p[cc * 32 + 2 * i + 1] *
+                                  (__uint_as_float(rp[cc][2 * i + 1]) - dd[col + 1]));
+          }
+          tmem_st_32x32b_x16(tmem + lane_base + 128 + half * 64 + cc * 16, dk);
         }
-        tmem_st_32x32b_x16(tmem + lane_base + 128 + half * 64 + cc * 16, dk);
       }
       tc_wait_st();
       tc_fence_before();
@@ -592,8 +667,9 @@ int bwpp_attention_bwd_train(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t
   const float sl2 = scale * 1.4426950408889634f;
   const uint32_t tiles = (S + 127) / 128;
   BwdIO io{dq, nullptr, ldd, lse, delta, AttnIO{nullptr, nullptr, 0, nullptr, 1, H}};
-  bwd_dq_kernel<<<tiles * BH, THREADS, Q_SMEM, ctx->stream>>>(tq, tk, tv, tdo, io, BH, S, S, scale,
-                                                              sl2, causal, tiles, ctx->status_word);
+  const uint32_t dq_grid = min((uint32_t)ctx->num_sms, tiles * BH);  // persistent
+  bwd_dq_kernel<<<dq_grid, THREADS, Q_SMEM, ctx->stream>>>(tq, tk, tv, tdo, io, BH, S, S, scale, sl2,
+                                                           causal, tiles, ctx->status_word);
   BWPP_LAUNCH_CHECK(ctx, "attention bwd dq");
   BwdIO io2{dk, dv, ldd, lse, delta, AttnIO{nullptr, nullptr, 0, nullptr, 1, H}};
   bwd_dkdv_kernel<<<tiles * BH, THREADS, K_SMEM, ctx->stream>>>(tq, tk, tv, tdo, io2, BH, S, S, scale,
