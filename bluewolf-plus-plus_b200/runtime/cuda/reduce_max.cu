@@ -223,14 +223,26 @@ __global__ void __launch_bounds__(kThreads)
   constexpr int W = V::W;
   __shared__ float sv[32];
   const uint32_t nv = cols / W;
-  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+  // The next row's loads are issued before this row's two block reductions,
+  // so a CTA keeps a second row in flight through its serial phases.
+  float xv[MAXV][W];
+  auto load_row = [&](uint32_t r, float (&dst)[MAXV][W]) {
     const float *xr = x + (size_t)r * ld;
-    float xv[MAXV][W];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const uint32_t idx = threadIdx.x + i * kThreads;
+      if (idx < nv) V::load_stream(xr, idx, dst[i]);
+    }
+  };
+  if (blockIdx.x < rows) load_row(blockIdx.x, xv);
+  for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    float nx[MAXV][W];
+    const uint32_t rn = r + gridDim.x;
+    if (rn < rows) load_row(rn, nx);
     float m = -INFINITY;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
       const uint32_t idx = threadIdx.x + i * kThreads;
-      if (idx < nv) V::load_stream(xr, idx, xv[i]);
 #pragma unroll
       for (int w = 0; w < W; ++w)
         if (idx < nv && xv[i][w] > m) m = xv[i][w];
@@ -259,6 +271,10 @@ __global__ void __launch_bounds__(kThreads)
         V::store(yr, idx, xv[i]);
       }
     }
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+#pragma unroll
+      for (int w = 0; w < W; ++w) xv[i][w] = nx[i][w];
   }
 }
 
