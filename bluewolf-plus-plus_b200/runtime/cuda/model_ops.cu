@@ -71,6 +71,38 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The same with one warp per row (cols % 128 == 0, cols <= 2048): the row
+// stays in the warp's registers (up to 16 float4 per lane) and the sum of
+// squares needs only shuffles, so many rows are in flight per SM and no
+// block barrier stalls a CTA between load and store.
+template <int NV4>  // float4 per lane
+__global__ void __launch_bounds__(256)
+    rmsnorm_bf16out_warp_kernel(const float *__restrict__ x, const float *__restrict__ gamma,
+                                uint16_t *__restrict__ y, uint32_t rows, uint32_t cols, float eps) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
+  for (uint32_t r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += nwarps) {
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)r * cols);
+    float4 v[NV4];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) {
+      v[i] = __ldcs(xr + lane + 32 * i);
+      ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.0f / sqrtf(ss / (float)cols + eps);
+    uint2 *yr = reinterpret_cast<uint2 *>(y + (size_t)r * cols);
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) {
+      const float4 g = __ldg(reinterpret_cast<const float4 *>(gamma) + lane + 32 * i);
+      yr[lane + 32 * i] = make_uint2(f2bf2(v[i].x * inv * g.x, v[i].y * inv * g.y),
+                                     f2bf2(v[i].z * inv * g.z, v[i].w * inv * g.w));
+    }
+  }
+}
+
 // a[t, f] = silu(gu[t, f]) * gu[t, F + f]   (gate | up halves)
 __global__ void swiglu_fwd_kernel(const uint16_t *__restrict__ gu, uint16_t *__restrict__ a,
                                   uint32_t rows, uint32_t F) {
@@ -279,6 +311,33 @@ int bwpp_rmsnorm_bf16out(BwppCudaCtx *ctx, const float *x, const float *gamma, u
                          uint32_t rows, uint32_t cols, float eps) {
   if (cols % 4 || cols > 256 * 4 * 8)
     return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "rmsnorm bf16: cols");
+  if (cols % 128 == 0 && cols <= 2048 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(gamma) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 7) == 0) {
+    const unsigned grid = grid_for(ctx, (size_t)rows * 32, 256);
+#define BWPP_RMSW(N) \
+  rmsnorm_bf16out_warp_kernel<N><<<grid, 256, 0, ctx->stream>>>(x, gamma, y, rows, cols, eps)
+    switch (cols / 128) {
+      case 1: BWPP_RMSW(1); break;
+      case 2: BWPP_RMSW(2); break;
+      case 3: BWPP_RMSW(3); break;
+      case 4: BWPP_RMSW(4); break;
+      case 5: BWPP_RMSW(5); break;
+      case 6: BWPP_RMSW(6); break;
+      case 7: BWPP_RMSW(7); break;
+      case 8: BWPP_RMSW(8); break;
+      case 9: BWPP_RMSW(9); break;
+      case 10: BWPP_RMSW(10); break;
+      case 11: BWPP_RMSW(11); break;
+      case 12: BWPP_RMSW(12); break;
+      case 13: BWPP_RMSW(13); break;
+      case 14: BWPP_RMSW(14); break;
+      case 15: BWPP_RMSW(15); break;
+      default: BWPP_RMSW(16); break;
+    }
+#undef BWPP_RMSW
+    BWPP_LAUNCH_CHECK(ctx, "rmsnorm bf16");
+    return BWPP_CUDA_OK;
+  }
   const unsigned cap = (unsigned)ctx->num_sms * 8;
   const unsigned grid = rows < cap ? (rows ? rows : 1) : cap;
   rmsnorm_bf16out_kernel<<<grid, 256, 0, ctx->stream>>>(x, gamma, y, rows, cols, eps);
