@@ -140,7 +140,10 @@ __global__ void __launch_bounds__(kThreads)
 // which keeps var well conditioned when |mean| >> std.  The CTA's dgamma /
 // dbeta partials live in shared memory (each thread owns fixed columns, so
 // there are no conflicts), leaving registers for more resident CTAs.
-template <int MAXV, bool V4, bool CENTERED>
+// ACC: the residual-gradient form (acc += dx, acc16 = bf16(acc)), a separate
+// instantiation so the plain kernels keep their register count (they fill an
+// SM with 4 CTAs at <= 64 registers).
+template <int MAXV, bool V4, bool CENTERED, bool ACC = false>
 __global__ void __launch_bounds__(kThreads)
     norm_bwd_kernel(const float *__restrict__ x, const float *__restrict__ gamma,
                     const float *__restrict__ dy, float *__restrict__ dx,
@@ -212,7 +215,7 @@ __global__ void __launch_bounds__(kThreads)
         o[w] = rs * (g - mg - xh * mgx);
         xv[i][w] = xh;  // keep xhat for the partials below
       }
-      if (acc) {
+      if constexpr (ACC) {
         // residual-gradient form: acc += dx (and acc16 = bf16(acc)); dx
         // itself is not written
         float *ar = acc + (size_t)r * ld;
@@ -422,9 +425,11 @@ int norm_bwd(BwppCudaCtx *ctx, const float *x, const float *gamma,
   if (acc_bytes > 48 * 1024) mv = 0;  // wide rows: looped kernel (global partials)
   if (acc && mv == 0)
     return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "norm bwd accumulate: row too wide");
-#define BWPP_BWD(MV, V4)                                                     \
-  norm_bwd_kernel<MV, V4, CENTERED><<<grid, kThreads, acc_bytes, s>>>(       \
-      x, gamma, dy, dx, pg, pb, rows, cols, ld, eps, acc, acc16)
+#define BWPP_BWD(MV, V4)                                                           \
+  (acc ? norm_bwd_kernel<MV, V4, CENTERED, true><<<grid, kThreads, acc_bytes, s>>>(  \
+             x, gamma, dy, dx, pg, pb, rows, cols, ld, eps, acc, acc16)              \
+       : norm_bwd_kernel<MV, V4, CENTERED, false><<<grid, kThreads, acc_bytes, s>>>( \
+             x, gamma, dy, dx, pg, pb, rows, cols, ld, eps, nullptr, nullptr))
   if (mv == 0) {
     norm_bwd_looped_kernel<CENTERED><<<grid, kThreads, 0, s>>>(
         x, gamma, dy, dx, pg, pb, rows, cols, ld, eps);
