@@ -107,7 +107,11 @@ int bwpp_cuda_ctx_set_stream(BwppCudaCtx *ctx, void *stream);
 /* Hands the context caller-owned device scratch (e.g. an arena slice).  With
  * a workspace set the context never allocates; a call that needs more than
  * `bytes` fails with BWPP_CUDA_ERR_NOMEM.  NULL / 0 returns to ctx-owned
- * scratch. */
+ * scratch.  (Without one, the first tensor-core GEMM whose last round is cut
+ * into K parts allocates a fixed split-tail scratch, 2 x SM count tiles of
+ * 128 x 256 fp32, about 38 MB on a B200, kept until the context is
+ * destroyed; with one set beforehand, GEMMs run that round as whole tiles
+ * or N halves instead.) */
 int bwpp_cuda_ctx_set_workspace(BwppCudaCtx *ctx, void *device_ptr,
                                 size_t bytes);
 /* Copies `bytes` between any two host / device buffers (e.g. filling arena
@@ -368,7 +372,12 @@ int bwpp_cuda_tiny_model_step(BwppCudaTinyModel *model, const float *x,
 
 /* ---- 2. mirrors of runtime/cpu/bwpp_cpu_ref.h:6-58 ---------------------- */
 /* Same argument lists; host or device pointers; synchronous; the calling
- * thread's context on the current device is created on first use. */
+ * thread's context on the current device is created on first use.
+ * bwpp_cuda_matmul_f32 with A, B and C all in host memory (and at least two
+ * chunks of 1024 rows or columns) overlaps its copies with the GEMMs: A goes
+ * up in row chunks and B in column chunks on one stream, each newly complete
+ * L-shaped region of C is computed on the context stream and comes back on a
+ * third; both streams belong to the calling thread and live as long as it. */
 
 void bwpp_cuda_matmul_f32(const float *a, const float *b, float *c, uint32_t M,
                           uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
