@@ -638,26 +638,48 @@ class RowWorkload(Workload):
             raise NotImplementedError
         self.bwpp.rmsnorm_f32(self.hx, self.hy, self.hg, self.hbt, self.m, self.Cc, self.Cc, 1e-5)
 
+    # the reference's own CPU function for this op (runtime/cpu/bwpp_cpu_ref.h), where
+    # it has one: rmsnorm forward, softmax, and the reduce_max mask / grad pair (the
+    # reference's form of the max and its routed gradient)
+    REF_OPS = ("rmsnorm_fwd", "softmax_fwd", "reduce_max_fwd", "reduce_max_bwd")
+
     def cpu_sample(self, lib, threads):
-        import oracle as O
-        if self.op != "rmsnorm_fwd":
-            return None
-        rows = 4096
-        rng = np.random.default_rng(3000)
-        x = rng.standard_normal((rows, self.Cc), dtype=np.float32)
-        y = np.zeros_like(x)
-        g = (1 + 0.1 * rng.standard_normal(self.Cc)).astype(np.float32)
         import ctypes as C
+
+        import oracle as O
+        if self.op not in self.REF_OPS:
+            return None
+        rows, cols = 4096, self.Cc
+        rng = np.random.default_rng(3000)
+        x = rng.standard_normal((rows, cols), dtype=np.float32)
+        y = np.zeros_like(x)
+        g = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+        dy = rng.standard_normal(rows).astype(np.float32)
         fp = C.POINTER(C.c_float)
+        at = lambda a, r0: C.cast(C.c_void_p(a.ctypes.data + r0 * cols * 4), fp)
+        if self.op == "reduce_max_bwd":
+            lib.reduce_max_mask_f32(x.ctypes.data_as(fp), y.ctypes.data_as(fp), rows, cols, 1)
 
         def part(r0, r1):
-            lib.rmsnorm_f32(C.cast(C.c_void_p(x.ctypes.data + r0 * self.Cc * 4), fp),
-                            C.cast(C.c_void_p(y.ctypes.data + r0 * self.Cc * 4), fp),
-                            g.ctypes.data_as(fp), None, r1 - r0, self.Cc, self.Cc, 1e-5)
+            n = r1 - r0
+            if self.op == "rmsnorm_fwd":
+                lib.rmsnorm_f32(at(x, r0), at(y, r0), g.ctypes.data_as(fp), None, n, cols, cols, 1e-5)
+            elif self.op == "softmax_fwd":
+                lib.softmax_f32(at(x, r0), at(y, r0), n, cols, cols)
+            elif self.op == "reduce_max_fwd":
+                lib.reduce_max_mask_f32(at(x, r0), at(y, r0), n, cols, 1)
+            else:  # gradient routed through the mask: dx = mask * dy[row]
+                lib.reduce_max_grad_f32(at(y, r0), C.cast(C.c_void_p(dy.ctypes.data + r0 * 4), fp),
+                                        at(x, r0), n, cols, 1)
         t0 = time.perf_counter()
         O.run_rows_threaded(part, rows, threads)
         dt = time.perf_counter() - t0
-        return 2.0 * rows * self.Cc * 4, dt, f"{rows} of 65536 rows, fp32, {threads} threads"
+        fn = {"rmsnorm_fwd": "bwpp_cpu_rmsnorm_f32", "softmax_fwd": "bwpp_cpu_softmax_f32",
+              "reduce_max_fwd": "bwpp_cpu_reduce_max_mask_f32 (axis 1)",
+              "reduce_max_bwd": "bwpp_cpu_reduce_max_grad_f32 (axis 1, on its mask)"}[self.op]
+        return (float(self.bytes_for(rows)), dt,
+                f"{fn} on {rows} of 65536 rows, fp32, {threads} threads (credited with this "
+                f"workload's algorithmic bytes per row)")
 
 
 class TinyModelWorkload(Workload):
