@@ -1,0 +1,49 @@
+"""bench.py's reference arm, on CPU: it reports the CUDA arm's config for the
+same workload and world size, and prints an `unavailable` line (exit 0) for a
+workload the reference has no CPU code for."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+import bench  # noqa: E402
+
+
+@pytest.mark.parametrize("name,world,key,value", [
+    ("gemm", 8, "rows_per_gpu", 1024),
+    ("gemm", 1, "rows_per_gpu", 8192),
+    ("attention_causal", 4, "heads_per_gpu", 64),
+    ("rmsnorm_bwd", 2, "rows_per_gpu", 32768),
+    ("attention_bwd", 4, "batch_per_gpu", 4),
+    ("tiny_model", 8, "global_batch", 128),
+])
+def test_reference_config_matches_the_cuda_arm(name, world, key, value):
+    cfg = bench.reference_config(name, world)
+    assert cfg[key] == value
+    assert cfg["workload"] != name  # the descriptive config, not the bare name
+
+
+def _reference_line(workload):
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
+                          "--workload", workload, "--steps", "1", "--warmup", "0"],
+                         capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+def test_reference_arm_without_cpu_code_prints_unavailable():
+    d = _reference_line("tiny_model")
+    assert d["impl"] == "reference" and "no CPU implementation" in d["unavailable"]
+
+
+def test_reference_arm_row_op_uses_the_reference_function():
+    d = _reference_line("softmax_fwd")
+    assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "GB/s"
+    assert "bwpp_cpu_softmax_f32" in d["cpu_baseline"]["sample"]
+    assert d["config"]["rows_per_gpu"] == 65536
+    assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
