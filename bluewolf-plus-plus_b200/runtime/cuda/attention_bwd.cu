@@ -24,6 +24,8 @@
 // it is the B of dQ / dK / dV.
 #include "attention_common.cuh"
 
+#include <type_traits>
+
 namespace {
 
 using namespace bwpp_attn;
@@ -278,7 +280,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (causal && m < lim) lim = m;
         const int lim_rel = (int)lim - (int)n0;
         // P for this warp's 64 columns, kept in registers (both 32-column
-        // loads in flight before one wait)
+        // loads in flight before one wait).  Of every 8 column pairs, 2 take
+        // exp2 on the FMA pipe; blocks below the diagonal skip the mask.
         float p[BN / 2];
         {
           uint32_t rs[2][32];
@@ -286,15 +289,38 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, rs[1]);
           tc_wait_ld(rs[0]);
           tc_wait_ld(rs[1]);
+          const uint64_t sc2 = f2pack(scale_log2, scale_log2), nl2 = f2pack(-lse, -lse);
+          auto pq = [&](auto masked) {
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc)
+            for (int cc = 0; cc < 2; ++cc)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int col = (half * 2 + cc) * 32 + e;
-              p[cc * 32 + e] = (col <= lim_rel)
-                                   ? fast_exp2(fmaf(__uint_as_float(rs[cc][e]), scale_log2, -lse))
-                                   : 0.0f;
-            }
+              for (int g = 0; g < 8; ++g) {
+                const uint32_t *r = &rs[cc][4 * g];
+                float y[4], e[4];
+                f2unpack(f2fma(f2pack(__uint_as_float(r[0]), __uint_as_float(r[1])), sc2, nl2),
+                         y[0], y[1]);
+                f2unpack(f2fma(f2pack(__uint_as_float(r[2]), __uint_as_float(r[3])), sc2, nl2),
+                         y[2], y[3]);
+                if ((g & 3) == 3) {
+                  exp2_fma2(y[0], y[1], e[0], e[1]);
+                  exp2_fma2(y[2], y[3], e[2], e[3]);
+                } else {
+#pragma unroll
+                  for (int k = 0; k < 4; ++k) e[k] = fast_exp2(y[k]);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  if constexpr (decltype(masked)::value) {
+                    if ((half * 2 + cc) * 32 + 4 * g + k > lim_rel) e[k] = 0.0f;
+                  }
+                  p[cc * 32 + 4 * g + k] = e[k];
+                }
+              }
+          };
+          if (__all_sync(0xffffffffu, lim_rel >= BN - 1))
+            pq(std::false_type{});
+          else
+            pq(std::true_type{});
         }
         tc_fence_before();
         __syncwarp();
@@ -313,13 +339,21 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, rp[1]);
           tc_wait_ld(rp[0]);
           tc_wait_ld(rp[1]);
+          const uint64_t nd2 = f2pack(-dl, -dl);
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
             uint32_t pk[16];
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              pk[e] = pack_bf16(p[cc * 32 + 2 * e] * (__uint_as_float(rp[cc][2 * e]) - dl),
-                                p[cc * 32 + 2 * e + 1] * (__uint_as_float(rp[cc][2 * e + 1]) - dl));
+            for (int e = 0; e < 16; ++e) {
+              // dS = P (dP - delta), a masked P being 0
+              float t0, t1;
+              f2unpack(f2mul(f2pack(p[cc * 32 + 2 * e], p[cc * 32 + 2 * e + 1]),
+                             f2add(f2pack(__uint_as_float(rp[cc][2 * e]),
+                                          __uint_as_float(rp[cc][2 * e + 1])),
+                                   nd2)),
+                       t0, t1);
+              pk[e] = pack_bf16(t0, t1);
+            }
             store_swizzled_chunk(ds_tile, row, half * 2 + cc, pk);
           }
         }
@@ -496,17 +530,24 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t key = k0 + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
+    // -lse / -delta of one query per thread, loaded a tile ahead so the
+    // global loads' latency hides behind the current tile
+    float nl = -INFINITY, nd = 0.0f;
+    auto fetch = [&](int t) {
+      const uint32_t q = (i0 + t) * BM + tid;
+      nl = q < Sq ? -io.lse[(size_t)bh * Sq + q] : -INFINITY;
+      nd = q < Sq ? -io.delta[(size_t)bh * Sq + q] : 0.0f;
+    };
+    if (n > 0) fetch(0);
     for (int it = 0; it < n && ok; ++it) {
       const uint32_t qs = (i0 + it) * BM;
-      // stage this tile's lse / delta (one query per thread) in buffer it & 1;
-      // every thread passed phase it-1 only after all had finished tile it-2,
-      // so the buffer is free.  Bounded wait, like every other.
-      {
-        const uint32_t q = qs + tid;
-        lse_s[(it & 1) * 128 + tid] = q < Sq ? io.lse[(size_t)bh * Sq + q] : INFINITY;
-        del_s[(it & 1) * 128 + tid] = q < Sq ? io.delta[(size_t)bh * Sq + q] : 0.0f;
-        mbar_arrive(&bar->staged);
-      }
+      // stage this tile's -lse / -delta in buffer it & 1; every thread passed
+      // phase it-1 only after all had finished tile it-2, so the buffer is
+      // free.  Bounded wait, like every other.
+      lse_s[(it & 1) * 128 + tid] = nl;
+      del_s[(it & 1) * 128 + tid] = nd;
+      mbar_arrive(&bar->staged);
+      if (it + 1 < n) fetch(it + 1);
       if (*abort_flag || !mbar_wait(&bar->staged, it & 1, status) ||
           !mbar_wait(&bar->s_full, it & 1, status)) {
         *abort_flag = 1;
@@ -519,9 +560,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       int first_rel = causal ? (int)key - (int)qs : 0;  // first visible col
       if (first_rel < 0) first_rel = 0;
       const int last_rel = key < Skv ? (int)min(Sq - 1 - qs, (uint32_t)127) : -1;
-      const float *ls = lse_s + (it & 1) * 128;
-      const float *dd = del_s + (it & 1) * 128;
-      // P^T for this warp's 64 queries: registers, and bf16 pairs into TMEM
+      const float *nls = lse_s + (it & 1) * 128;  // -lse per query
+      const float *ndd = del_s + (it & 1) * 128;  // -delta per query
+      // P^T for this warp's 64 queries: registers, and bf16 pairs into TMEM.
+      // Of every 8 column pairs, 2 take exp2 on the FMA pipe (exp2_fma2) to
+      // share the load with MUFU.  Tiles off the diagonal skip the mask.
       float p[64];
       {
         uint32_t rs[2][32];  // both 32-column loads in flight before one wait
@@ -529,24 +572,50 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, rs[1]);
         tc_wait_ld(rs[0]);
         tc_wait_ld(rs[1]);
+        const uint64_t sc2 = f2pack(scale_log2, scale_log2);
+        auto pt = [&](auto masked) {
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = half * 2 + cc;
-          uint32_t pk[16];
+          for (int cc = 0; cc < 2; ++cc) {
+            const int c = half * 2 + cc;
+            const float4 *l4 = reinterpret_cast<const float4 *>(nls + c * 32);
+            uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+            for (int g = 0; g < 8; ++g) {
+              const float4 l = l4[g];
+              const uint32_t *r = &rs[cc][4 * g];
+              float y[4], e[4];
+              f2unpack(f2fma(f2pack(__uint_as_float(r[0]), __uint_as_float(r[1])), sc2,
+                             f2pack(l.x, l.y)),
+                       y[0], y[1]);
+              f2unpack(f2fma(f2pack(__uint_as_float(r[2]), __uint_as_float(r[3])), sc2,
+                             f2pack(l.z, l.w)),
+                       y[2], y[3]);
+              if ((g & 3) == 3) {
+                exp2_fma2(y[0], y[1], e[0], e[1]);
+                exp2_fma2(y[2], y[3], e[2], e[3]);
+              } else {
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int col = c * 32 + 2 * i + e;
-              const bool vis = col >= first_rel && col <= last_rel;
-              p[cc * 32 + 2 * i + e] =
-                  vis ? fast_exp2(fmaf(__uint_as_float(rs[cc][2 * i + e]), scale_log2, -ls[col]))
-                      : 0.0f;
+                for (int k = 0; k < 4; ++k) e[k] = fast_exp2(y[k]);
+              }
+              if constexpr (decltype(masked)::value) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const int col = c * 32 + 4 * g + k;
+                  if (col < first_rel || col > last_rel) e[k] = 0.0f;
+                }
+              }
+#pragma unroll
+              for (int k = 0; k < 4; ++k) p[cc * 32 + 4 * g + k] = e[k];
+              pk[2 * g] = pack_bf16(e[0], e[1]);
+              pk[2 * g + 1] = pack_bf16(e[2], e[3]);
             }
-            pk[i] = pack_bf16(p[cc * 32 + 2 * i], p[cc * 32 + 2 * i + 1]);
+            tmem_st_32x32b_x16(tmem + lane_base + half * 64 + cc * 16, pk);
           }
-          tmem_st_32x32b_x16(tmem + lane_base + half * 64 + cc * 16, pk);
-        }
+        };
+        if (__all_sync(0xffffffffu, first_rel == 0 && last_rel == 127))
+          pt(std::false_type{});
+        else
+          pt(std::true_type{});
       }
       tc_wait_st();
       tc_fence_before();
@@ -567,13 +636,25 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
           const int c = half * 2 + cc;
+          const float4 *d4 = reinterpret_cast<const float4 *>(ndd + c * 32);
           uint32_t dk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int col = c * 32 + 2 * i;
-            dk[i] = pack_bf16(p[cc * 32 + 2 * i] * (__uint_as_float(rp[cc][2 * i]) - dd[col]),
-                              p[cc * 32 + 2 * i + 1] *
-                                  (__uint_as_float(rp[cc][2 * i + 1]) - dd[col + 1]));
+          for (int g = 0; g < 8; ++g) {
+            // dS^T = P^T (dP^T - delta), a masked P^T being 0
+            const float4 d = d4[g];
+            const uint32_t *r = &rp[cc][4 * g];
+            const float *pp = &p[cc * 32 + 4 * g];
+            float t0, t1, t2, t3;
+            f2unpack(f2mul(f2pack(pp[0], pp[1]),
+                           f2add(f2pack(__uint_as_float(r[0]), __uint_as_float(r[1])),
+                                 f2pack(d.x, d.y))),
+                     t0, t1);
+            f2unpack(f2mul(f2pack(pp[2], pp[3]),
+                           f2add(f2pack(__uint_as_float(r[2]), __uint_as_float(r[3])),
+                                 f2pack(d.z, d.w))),
+                     t2, t3);
+            dk[2 * g] = pack_bf16(t0, t1);
+            dk[2 * g + 1] = pack_bf16(t2, t3);
           }
           tmem_st_32x32b_x16(tmem + lane_base + 128 + half * 64 + cc * 16, dk);
         }

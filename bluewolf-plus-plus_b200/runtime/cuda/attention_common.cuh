@@ -91,6 +91,12 @@ __device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
   return d;
 }
 
+__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // 2^x for two lanes on the FMA pipe, to take load off the MUFU unit
 // (ex2): x = n + f with n = round(x) (magic-constant add: 1.5 * 2^23 leaves
 // round(x) in the low mantissa bits), f in [-0.5, 0.5]; 2^f from a cubic
