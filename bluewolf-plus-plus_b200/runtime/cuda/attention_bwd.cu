@@ -45,25 +45,31 @@ struct BwdIO {
   AttnIO in;          // input layout (tok / H)
 };
 
+// The issue loops below build each descriptor's low word once and step it by
+// (offset >> 4): the issuing thread shares its SM sub-partition with two busy
+// softmax warps, so every instruction it saves shortens the MMA stream.
+// (SBO 1024 and the 128-byte swizzle for both K- and MN-major boxes; the
+// LBO, 16 resp. BOX bytes, sits in the low word)
+constexpr uint32_t HI_SW = smem_desc_hi(1024, BWPP_SWIZZLE_128B);
+
 __device__ __forceinline__ void mma_kk(uint32_t d, uint32_t a, uint32_t b) {
   // D(128 x 128) = A(128 x D) B(128 x D)^T, both K-major
+  const uint32_t alo = smem_desc_lo(a, 16), blo = smem_desc_lo(b, 16);
 #pragma unroll
   for (int ks = 0; ks < D / 16; ++ks) {
-    const uint32_t off = (ks >> 2) * BOX + (ks & 3) * 32;
-    tc_mma_f16_ss(d, make_smem_desc(a + off, 16, 1024, BWPP_SWIZZLE_128B),
-                  make_smem_desc(b + off, 16, 1024, BWPP_SWIZZLE_128B), IDESC_KK,
-                  ks > 0 ? 1u : 0u);
+    const uint32_t off = ((ks >> 2) * BOX + (ks & 3) * 32) >> 4;
+    tc_mma_f16_ss_w(d, alo + off, HI_SW, blo + off, HI_SW, IDESC_KK, ks > 0 ? 1u : 0u);
   }
 }
 
 __device__ __forceinline__ void mma_km(uint32_t d, uint32_t a, uint32_t b, bool acc) {
   // D(128 x D) += A(128 x 128, K-major) B(128 x D, MN-major)
+  const uint32_t alo = smem_desc_lo(a, 16), blo = smem_desc_lo(b, BOX);
 #pragma unroll
   for (int ks = 0; ks < 128 / 16; ++ks) {
-    const uint32_t aoff = (ks >> 2) * BOX + (ks & 3) * 32;
-    tc_mma_f16_ss(d, make_smem_desc(a + aoff, 16, 1024, BWPP_SWIZZLE_128B),
-                  make_smem_desc(b + ks * 2048, BOX, 1024, BWPP_SWIZZLE_128B), IDESC_KM,
-                  (acc || ks > 0) ? 1u : 0u);
+    const uint32_t aoff = ((ks >> 2) * BOX + (ks & 3) * 32) >> 4;
+    tc_mma_f16_ss_w(d, alo + aoff, HI_SW, blo + ((ks * 2048) >> 4), HI_SW, IDESC_KM,
+                    (acc || ks > 0) ? 1u : 0u);
   }
 }
 
@@ -404,7 +410,8 @@ constexpr int K_SMEM = K_OFF_BAR + 256 + 1024;
 static_assert(K_SMEM <= 232448, "dkdv smem");
 
 struct KBars {
-  uint64_t kv_full, qd_full[2], qd_empty[2], s_full, dp_full, pt_full, dst_full, staged, drain;
+  uint64_t kv_full, q_full[2], q_empty[2], do_full[2], do_empty[2], s_full, dp_full, pt_full,
+      dst_full, staged, drain;
   uint32_t tmem;
   int abort_flag;
 };
@@ -412,11 +419,11 @@ struct KBars {
 // D(128 x D) (+)= A(128 x 128 queries, bf16 pairs in TMEM at the half-split
 // columns a0 + [0, 32) and a0 + [64, 96)) B(128 queries x D, MN-major smem)
 __device__ __forceinline__ void mma_tm(uint32_t d, uint32_t a0, uint32_t b, bool acc) {
+  const uint32_t blo = smem_desc_lo(b, BOX);
 #pragma unroll
   for (int ks = 0; ks < 128 / 16; ++ks) {
     const uint32_t acol = a0 + (ks >> 2) * 64 + (ks & 3) * 8;
-    tc_mma_f16_ts(d, acol, make_smem_desc(b + ks * 2048, BOX, 1024, BWPP_SWIZZLE_128B), IDESC_KM,
-                  (acc || ks > 0) ? 1u : 0u);
+    tc_mma_f16_ts_w(d, acol, blo + ((ks * 2048) >> 4), HI_SW, IDESC_KM, (acc || ks > 0) ? 1u : 0u);
   }
 }
 
@@ -442,8 +449,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bar->kv_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&bar->qd_full[s], 1);
-      mbar_init(&bar->qd_empty[s], 1);
+      mbar_init(&bar->q_full[s], 1);
+      mbar_init(&bar->q_empty[s], 1);
+      mbar_init(&bar->do_full[s], 1);
+      mbar_init(&bar->do_empty[s], 1);
     }
     mbar_init(&bar->s_full, 1);
     mbar_init(&bar->dp_full, 1);
@@ -468,16 +477,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive_expect_tx(&bar->kv_full, 2 * TILE);
       load_rows<2>(smem + K_OFF_K, &tmK, &bar->kv_full, io.in, bh, Skv, k0);
       load_rows<2>(smem + K_OFF_V, &tmV, &bar->kv_full, io.in, bh, Skv, k0);
+      // Q and dO have their own slots: dO(it) is free once dV(it) is done,
+      // Q(it) only after dK(it), so each load starts as early as it can
       for (int it = 0; it < n && !*abort_flag; ++it) {
         const int s = it & 1;
-        if (!mbar_wait(&bar->qd_empty[s], ((it >> 1) & 1) ^ 1, status)) {
+        const uint32_t par = ((it >> 1) & 1) ^ 1;
+        const uint32_t qs = (i0 + it) * BM;
+        if (!mbar_wait(&bar->q_empty[s], par, status)) {
           *abort_flag = 1;
           break;
         }
-        const uint32_t qs = (i0 + it) * BM;
-        mbar_arrive_expect_tx(&bar->qd_full[s], 2 * TILE);
-        load_rows<2>(smem + K_OFF_Q + s * TILE, &tmQ, &bar->qd_full[s], io.in, bh, Sq, qs);
-        load_rows<2>(smem + K_OFF_DO + s * TILE, &tmDO, &bar->qd_full[s], io.in, bh, Sq, qs);
+        mbar_arrive_expect_tx(&bar->q_full[s], TILE);
+        load_rows<2>(smem + K_OFF_Q + s * TILE, &tmQ, &bar->q_full[s], io.in, bh, Sq, qs);
+        if (!mbar_wait(&bar->do_empty[s], par, status)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&bar->do_full[s], TILE);
+        load_rows<2>(smem + K_OFF_DO + s * TILE, &tmDO, &bar->do_full[s], io.in, bh, Sq, qs);
       }
     }
   } else if (warp == 1) {
@@ -487,11 +504,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       auto qa = [&](int it) { return smem_u32(smem + K_OFF_Q + (it & 1) * TILE); };
       auto da = [&](int it) { return smem_u32(smem + K_OFF_DO + (it & 1) * TILE); };
       if (ok && n > 0) {
-        ok = mbar_wait(&bar->qd_full[0], 0, status);
+        ok = mbar_wait(&bar->q_full[0], 0, status);
         if (ok) {
           tc_fence_after();
-          mma_kk(tmem + 0, ka, qa(0));    // S^T(0)  = K  Q_0^T
+          mma_kk(tmem + 0, ka, qa(0));  // S^T(0)  = K  Q_0^T
           tc_commit(&bar->s_full);
+          ok = mbar_wait(&bar->do_full[0], 0, status);
+        }
+        if (ok) {
+          tc_fence_after();
           mma_kk(tmem + 128, va, da(0));  // dP^T(0) = V dO_0^T
           tc_commit(&bar->dp_full);
         }
@@ -501,8 +522,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ok) break;
         tc_fence_after();
         mma_tm(tmem + 256, tmem + 0, da(it), it > 0);  // dV += P^T(it) dO_it
+        tc_commit(&bar->do_empty[it & 1]);
         if (it + 1 < n) {
-          ok = mbar_wait(&bar->qd_full[(it + 1) & 1], ((it + 1) >> 1) & 1, status);
+          ok = mbar_wait(&bar->q_full[(it + 1) & 1], ((it + 1) >> 1) & 1, status);
           if (!ok) break;
           tc_fence_after();
           mma_kk(tmem + 0, ka, qa(it + 1));  // S^T(it+1), after dV(it) read P^T(it)
@@ -512,8 +534,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ok) break;
         tc_fence_after();
         mma_tm(tmem + 384, tmem + 128, qa(it), it > 0);  // dK += dS^T(it) Q_it
-        tc_commit(&bar->qd_empty[it & 1]);
+        tc_commit(&bar->q_empty[it & 1]);
         if (it + 1 < n) {
+          ok = mbar_wait(&bar->do_full[(it + 1) & 1], ((it + 1) >> 1) & 1, status);
+          if (!ok) break;
+          tc_fence_after();
           mma_kk(tmem + 128, va, da(it + 1));  // dP^T(it+1), after dK(it) read dS^T(it)
           tc_commit(&bar->dp_full);
         }
@@ -669,9 +694,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint16_t *dv_dst = io.d1 + ((size_t)(bh / io.in.H) * Skv + key) * io.ldd + (size_t)(bh % io.in.H) * D;
     if (ok && n > 0) {
       // every MMA, dK(n-1) last, has completed when the drain-side commit of
-      // qd_empty for the last tile has arrived
+      // q_empty for the last tile has arrived
       const int s = (n - 1) & 1;
-      if (mbar_wait(&bar->qd_empty[s], ((n - 1) >> 1) & 1, status)) {
+      if (mbar_wait(&bar->q_empty[s], ((n - 1) >> 1) & 1, status)) {
         tc_fence_after();
         store_row_bf16(tmem + lane_base + 256, dv_dst, 1.0f, valid, half);
         store_row_bf16(tmem + lane_base + 384, dk_dst, scale, valid, half);

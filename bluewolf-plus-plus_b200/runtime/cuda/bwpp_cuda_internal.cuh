@@ -467,6 +467,45 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr,
 
 #define BWPP_SWIZZLE_128B 2u
 
+// The same descriptor as two 32-bit words, for issue loops that step the
+// address: the low word holds (address >> 4) in bits 0-13 and LBO >> 4 in
+// bits 16-29, the high word SBO >> 4, the fixed version bit and the swizzle.
+// Shared-memory addresses stay below 2^18, so stepping the low word by
+// (offset >> 4) never carries into the LBO field: one add per operand.
+__device__ __forceinline__ uint32_t smem_desc_lo(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+__host__ __device__ constexpr uint32_t smem_desc_hi(uint32_t sbo_bytes, uint32_t swizzle_mode) {
+  return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | ((swizzle_mode & 7u) << 29);
+}
+
+// D(tmem) (+)= A(smem) * B(smem) from descriptor words (see smem_desc_lo).
+__device__ __forceinline__ void tc_mma_f16_ss_w(uint32_t d_tmem, uint32_t alo, uint32_t ahi,
+                                                uint32_t blo, uint32_t bhi, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "mov.b64 da, {%1, %2};\n\t"
+      "mov.b64 db, {%3, %4};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(alo), "r"(ahi), "r"(blo), "r"(bhi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D(tmem) (+)= A(tmem) * B(smem) from descriptor words.
+__device__ __forceinline__ void tc_mma_f16_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint32_t blo,
+                                                uint32_t bhi, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(blo), "r"(bhi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // The descriptor of the shared-memory address `bytes` past the one `d`
 // describes.  The start address is d's low 14 bits (address >> 4); callers
 // keep the sum below 256 KB, so only the low word changes.
