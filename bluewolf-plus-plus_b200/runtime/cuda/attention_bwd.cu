@@ -43,6 +43,7 @@ struct BwdIO {
   const float *lse;   // [B*H, Sq]
   const float *delta; // [B*H, Sq]
   AttnIO in;          // input layout (tok / H)
+  int tma_out;        // dkdv kernel: dK / dV leave through the tmDK / tmDV maps
 };
 
 // The issue loops below build each descriptor's low word once and step it by
@@ -90,6 +91,26 @@ __device__ __forceinline__ void store_row_bf16(uint32_t taddr, uint16_t *dst, fl
             pack_bf16(__uint_as_float(r[8 * i + 4]) * scale, __uint_as_float(r[8 * i + 5]) * scale),
             pack_bf16(__uint_as_float(r[8 * i + 6]) * scale, __uint_as_float(r[8 * i + 7]) * scale));
     }
+  }
+}
+
+// Converts this thread's 64 fp32 TMEM columns at taddr (x scale) to bf16 and
+// writes them as row `row` of the 64-column box `half` of a 128-byte-swizzle
+// tile (both 32-column loads in flight before one wait).
+__device__ __forceinline__ void stage_row_bf16(uint32_t taddr, uint8_t *tile, int row, int half,
+                                               float scale) {
+  uint32_t r[2][32];
+  tmem_ld_32x32b_x32(taddr, r[0]);
+  tmem_ld_32x32b_x32(taddr + 32, r[1]);
+  tc_wait_ld(r[0]);
+  tc_wait_ld(r[1]);
+#pragma unroll
+  for (int cc = 0; cc < 2; ++cc) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      pk[i] = pack_bf16(__uint_as_float(r[cc][2 * i]) * scale, __uint_as_float(r[cc][2 * i + 1]) * scale);
+    store_swizzled_chunk(tile, row, half * 2 + cc, pk);
   }
 }
 
@@ -411,7 +432,7 @@ static_assert(K_SMEM <= 232448, "dkdv smem");
 
 struct KBars {
   uint64_t kv_full, q_full[2], q_empty[2], do_full[2], do_empty[2], s_full, dp_full, pt_full,
-      dst_full, staged, drain;
+      dst_full, staged, drain, out_staged;
   uint32_t tmem;
   int abort_flag;
 };
@@ -430,6 +451,7 @@ __device__ __forceinline__ void mma_tm(uint32_t d, uint32_t a0, uint32_t b, bool
 __global__ void __launch_bounds__(THREADS, 1)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const __grid_constant__ CUtensorMap tmDK, const __grid_constant__ CUtensorMap tmDV,
                     const BwdIO io, uint32_t BH, uint32_t Sq, uint32_t Skv, float scale,
                     float scale_log2, int causal, uint32_t kblocks, int *status) {
   extern __shared__ uint8_t smem_raw[];
@@ -460,6 +482,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&bar->dst_full, SM_WARPS);
     mbar_init(&bar->staged, 32 * SM_WARPS);
     mbar_init(&bar->drain, 1);
+    mbar_init(&bar->out_staged, 32 * SM_WARPS);
     bar->abort_flag = 0;
     fence_mbar_init();
   }
@@ -696,12 +719,36 @@ __global__ void __launch_bounds__(THREADS, 1)
       // every MMA, dK(n-1) last, has completed when the drain-side commit of
       // q_empty for the last tile has arrived
       const int s = (n - 1) & 1;
-      if (mbar_wait(&bar->q_empty[s], ((n - 1) >> 1) & 1, status)) {
+      const bool done = mbar_wait(&bar->q_empty[s], ((n - 1) >> 1) & 1, status);
+      if (done)
         tc_fence_after();
+      else
+        *abort_flag = 1;
+      if (io.tma_out) {
+        // stage dV / dK as bf16 in the (now idle) dO / Q slot 0, laid out like
+        // the loaded tiles (two 64-column boxes, 128-byte swizzle), and send
+        // both tiles with four TMA stores: whole rows leave as bulk writes,
+        // and rows past Skv are clipped by the map.  The staging barrier
+        // (every softmax thread arrives, done or not) has a bounded wait.
+        uint8_t *sv = smem + K_OFF_DO, *sk = smem + K_OFF_Q;
+        if (done) {
+          stage_row_bf16(tmem + lane_base + 256 + half * 64, sv, row, half, 1.0f);
+          stage_row_bf16(tmem + lane_base + 384 + half * 64, sk, row, half, scale);
+          fence_proxy_async_smem();
+        }
+        mbar_arrive(&bar->out_staged);
+        if (threadIdx.x == 64 && done && mbar_wait(&bar->out_staged, 0, status)) {
+          const int32_t hh = (int32_t)(bh % io.in.H), bb = (int32_t)(bh / io.in.H);
+          for (int box = 0; box < 2; ++box) {
+            tma_store_4d(&tmDV, sv + box * BOX, box * 64, hh, (int32_t)k0, bb);
+            tma_store_4d(&tmDK, sk + box * BOX, box * 64, hh, (int32_t)k0, bb);
+          }
+          tma_store_commit();
+          tma_store_wait_read<0>();  // smem read; the writes finish on their own
+        }
+      } else if (done) {
         store_row_bf16(tmem + lane_base + 256, dv_dst, 1.0f, valid, half);
         store_row_bf16(tmem + lane_base + 384, dk_dst, scale, valid, half);
-      } else {
-        *abort_flag = 1;
       }
     } else if (ok && valid) {
       // no query sees these keys: zero gradients
@@ -736,6 +783,24 @@ int make_map(BwppCudaCtx *ctx, CUtensorMap *map, const void *base, uint32_t S, u
   return BWPP_CUDA_OK;
 }
 
+// dK / dV as a TMA store target: token-major rows b*S + s, head h at column
+// h*128, pitch ld; 4-D {D, H, S, B} so a box never crosses into the next
+// sequence (rows past S are clipped).  Returns false where TMA cannot take
+// the layout (base or pitch not 16-byte aligned); the kernel then stores rows
+// directly.
+bool make_out_map(CUtensorMap *map, const void *base, uint32_t S, uint32_t B, uint32_t H,
+                  uint32_t ld) {
+  bwpp_encode_tiled_fn enc = bwpp_get_encode_tiled();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || (ld % 8)) return false;
+  cuuint64_t dims[4] = {D, H, S, B};
+  cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)ld * 2, (cuuint64_t)S * ld * 2};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool g_attr[64] = {};
 
 }  // namespace
@@ -748,7 +813,11 @@ int bwpp_attention_bwd_train(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t
                              uint32_t ld_do, const float *lse, const float *delta,
                              uint32_t B, uint32_t H, uint32_t S, float scale, int causal,
                              uint16_t *dq, uint16_t *dk, uint16_t *dv, uint32_t ldd) {
-  if (S == 0 || !(scale > 0.0f) || (ld_in % 8) || (ld_do % 8) || (ldd % 8))
+  // 16-byte rows: the tensor maps and the 128-bit stores need aligned
+  // pitches and output bases
+  if (S == 0 || !(scale > 0.0f) || (ld_in % 8) || (ld_do % 8) || (ldd % 8) ||
+      ((reinterpret_cast<uintptr_t>(dq) | reinterpret_cast<uintptr_t>(dk) |
+        reinterpret_cast<uintptr_t>(dv)) & 15u))
     return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "attention bwd: layout");
   const uint32_t BH = B * H;
   CUtensorMap tq, tk, tv, tdo;
@@ -777,9 +846,13 @@ int bwpp_attention_bwd_train(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t
   bwd_dq_kernel<<<dq_grid, THREADS, Q_SMEM, ctx->stream>>>(tq, tk, tv, tdo, io, BH, S, S, scale, sl2,
                                                            causal, tiles, ctx->status_word);
   BWPP_LAUNCH_CHECK(ctx, "attention bwd dq");
-  BwdIO io2{dk, dv, ldd, lse, delta, AttnIO{nullptr, nullptr, 0, nullptr, 1, H}};
-  bwd_dkdv_kernel<<<tiles * BH, THREADS, K_SMEM, ctx->stream>>>(tq, tk, tv, tdo, io2, BH, S, S, scale,
-                                                                sl2, causal, tiles, ctx->status_word);
+  BwdIO io2{dk, dv, ldd, lse, delta, AttnIO{nullptr, nullptr, 0, nullptr, 1, H}, 0};
+  CUtensorMap tdk, tdv;
+  io2.tma_out = make_out_map(&tdk, dk, S, B, H, ldd) && make_out_map(&tdv, dv, S, B, H, ldd);
+  if (!io2.tma_out) tdk = tdv = tq;  // unused
+  bwd_dkdv_kernel<<<tiles * BH, THREADS, K_SMEM, ctx->stream>>>(tq, tk, tv, tdo, tdk, tdv, io2, BH, S,
+                                                                S, scale, sl2, causal, tiles,
+                                                                ctx->status_word);
   BWPP_LAUNCH_CHECK(ctx, "attention bwd dkdv");
   return BWPP_CUDA_OK;
 }

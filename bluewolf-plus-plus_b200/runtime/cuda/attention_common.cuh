@@ -55,6 +55,16 @@ __device__ __forceinline__ void load_rows(uint8_t *dst, const CUtensorMap *map, 
   }
 }
 
+// TMA store of one box from this CTA's shared memory (bulk async group).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void *src, int32_t x,
+                                             int32_t y, int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -145,7 +155,7 @@ __device__ __forceinline__ int blocks_for(uint32_t r0, uint32_t Sq, uint32_t Skv
 // 10 warps: two SM sub-partitions host three warps each, which caps the
 // kernel at 168 registers per thread (16384 / (3 * 32), rounded down to 8).
 
-// Writes 32 packed bf16 pairs (64 values: columns c*32 .. c*32+31 of a row
+// Writes 16 packed bf16 pairs (32 values: columns c*32 .. c*32+31 of a row
 // within a 128-column tile) into a K-major 128-byte-swizzle tile: two 64-column
 // atoms of 16 KB, row r at r*128, 16-byte chunk q at (q ^ (r & 7)) * 16.
 __device__ __forceinline__ void store_swizzled_chunk(uint8_t *tile, int row, int c,

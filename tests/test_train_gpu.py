@@ -41,8 +41,10 @@ def heads(t, B, S, H, D=128):  # token-major [B*S, H*D] -> [B, H, S, D]
 
 
 # (1, 2, 1024): 8 query / key tiles, so every pipeline barrier wraps its
-# phase several times; (1, 1, 200): a ragged last tile (zero-filled rows)
-@pytest.mark.parametrize("B,H,S", [(2, 2, 256), (1, 3, 384), (2, 1, 128), (1, 2, 1024), (1, 1, 200)])
+# phase several times; (1, 1, 200): a ragged last tile (zero-filled rows);
+# (2, 2, 200): the ragged tile's dK / dV store stops at its own sequence
+@pytest.mark.parametrize("B,H,S", [(2, 2, 256), (1, 3, 384), (2, 1, 128), (1, 2, 1024), (1, 1, 200),
+                                   (2, 2, 200)])
 @pytest.mark.parametrize("causal", [1, 0])
 def test_attention_fwd_lse_and_bwd(ctx, B, H, S, causal):
     D, lib = 128, bwpp.load()
@@ -70,6 +72,19 @@ def test_attention_fwd_lse_and_bwd(ctx, B, H, S, causal):
     for got, ref in ((dq, qf.grad), (dk, kf.grad), (dv, vf.grad)):
         err = rel_fro(heads(got.double().cpu(), B, S, H).numpy(), ref.numpy())
         assert err <= 1e-2, err
+
+
+def test_attention_bwd_rejects_unaligned_outputs(ctx):
+    """Output bases off a 16-byte boundary are refused (the backward kernels
+    store 16-byte vectors and bulk tiles)."""
+    lib, B, H, S = bwpp.load(), 1, 1, 128
+    T, HD = B * S, H * 128
+    x = torch.zeros(T * HD + 8, dtype=torch.bfloat16, device="cuda")
+    lse = torch.zeros(B * H * S, device="cuda")
+    p = x.data_ptr()
+    rc = lib.bwpp_cuda_attention_bwd_bf16(ctx.handle, p, p, p, HD, p, HD, p, HD, lse.data_ptr(), B, H, S,
+                                          0.1, 1, p, p + 8, p, HD)
+    assert rc == bwpp.ERR_UNSUPPORTED
 
 
 # ---- tiny_model step -----------------------------------------------------------
