@@ -431,11 +431,35 @@ constexpr int K_SMEM = K_OFF_BAR + 256 + 1024;
 static_assert(K_SMEM <= 232448, "dkdv smem");
 
 struct KBars {
-  uint64_t kv_full, q_full[2], q_empty[2], do_full[2], do_empty[2], s_full, dp_full, pt_full,
-      dst_full, staged, drain, out_staged;
+  uint64_t kv_full, kv_empty, q_full[2], q_empty[2], do_full[2], do_empty[2], s_full, dp_full,
+      pt_full, dst_full, staged, acc_full, acc_free, out_staged, sched_full[2], sched_empty[2],
+      drain;
+  int item[2];
   uint32_t tmem;
   int abort_flag;
 };
+static_assert(sizeof(KBars) <= 256, "dkdv barriers");
+
+// Work item w: 128 keys (k0) of head bh, seen by query tiles i0 .. qtiles-1.
+// Items go in groups of hg heads (about one item per SM), so the CTAs running
+// together share a few heads' Q / dO in L2; inside a group the heaviest key
+// blocks come first (causal: key block 0 is seen by every query tile), so the
+// CTAs that draw from the work counter last get the short items.
+struct KItem {
+  uint32_t bh, k0, i0;
+  int n;  // query tiles
+};
+__device__ __forceinline__ KItem k_item(uint32_t w, uint32_t BH, uint32_t kblocks,
+                                        uint32_t qtiles, uint32_t hg, int causal) {
+  const uint32_t per = hg * kblocks, grp = w / per, r = w % per;
+  const uint32_t h0 = grp * hg, hn = min(hg, BH - h0);
+  KItem it;
+  it.bh = h0 + r % hn;
+  it.k0 = (r / hn) * BN;
+  it.i0 = causal ? min(it.k0 / BM, qtiles) : 0;  // first query tile that sees k0
+  it.n = (int)(qtiles - it.i0);
+  return it;
+}
 
 // D(128 x D) (+)= A(128 x 128 queries, bf16 pairs in TMEM at the half-split
 // columns a0 + [0, 32) and a0 + [64, 96)) B(128 queries x D, MN-major smem)
@@ -448,12 +472,23 @@ __device__ __forceinline__ void mma_tm(uint32_t d, uint32_t a0, uint32_t b, bool
   }
 }
 
+// Persistent: one CTA per SM takes items until none is left: its first item is
+// blockIdx.x, the next come from the context's work counter.  The producer
+// publishes each item through a two-slot ring (sched_full / sched_empty);
+// every role walks the same sequence, and all barrier phases count tiles (g)
+// or items (k) over the CTA's whole sequence.  Across items: the next item's
+// K / V load as soon as the last S^T / dP^T MMAs of the current one are done
+// (kv_empty), its first Q / dO into the free slots, and its S^T(0) / dP^T(0)
+// MMAs run while the softmax warps drain the current dV / dK (acc_full); its
+// first dV MMA waits for that drain (acc_free).  The drain stages the bf16
+// tiles in the last tile's Q / dO slots, which the TMA stores then release.
 __global__ void __launch_bounds__(THREADS, 1)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     const __grid_constant__ CUtensorMap tmDK, const __grid_constant__ CUtensorMap tmDV,
                     const BwdIO io, uint32_t BH, uint32_t Sq, uint32_t Skv, float scale,
-                    float scale_log2, int causal, uint32_t kblocks, int *status) {
+                    float scale_log2, int causal, uint32_t kblocks, uint32_t hg, int *sched,
+                    int *status) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -461,28 +496,30 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int *abort_flag = &bar->abort_flag;
   float *lse_s = reinterpret_cast<float *>(smem + K_OFF_LSE);  // [2][128]
   float *del_s = lse_s + 2 * 128;                              // [2][128]
-  const uint32_t bh = blockIdx.x / kblocks;
-  const uint32_t k0 = (blockIdx.x % kblocks) * BN;
   const uint32_t qtiles = (Sq + BM - 1) / BM;
-  const uint32_t i0 = causal ? min(k0 / BM, qtiles) : 0;  // first query tile that sees k0
-  const int n = (int)(qtiles - i0);
+  const int total = (int)(BH * kblocks);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->kv_full, 1);
+    mbar_init(&bar->kv_empty, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar->q_full[s], 1);
       mbar_init(&bar->q_empty[s], 1);
       mbar_init(&bar->do_full[s], 1);
       mbar_init(&bar->do_empty[s], 1);
+      mbar_init(&bar->sched_full[s], 1);
+      mbar_init(&bar->sched_empty[s], 1 + SM_WARPS);  // MMA thread + softmax warps
     }
     mbar_init(&bar->s_full, 1);
     mbar_init(&bar->dp_full, 1);
     mbar_init(&bar->pt_full, SM_WARPS);
     mbar_init(&bar->dst_full, SM_WARPS);
     mbar_init(&bar->staged, 32 * SM_WARPS);
-    mbar_init(&bar->drain, 1);
+    mbar_init(&bar->acc_full, 1);
+    mbar_init(&bar->acc_free, SM_WARPS);
     mbar_init(&bar->out_staged, 32 * SM_WARPS);
+    mbar_init(&bar->drain, 1);
     bar->abort_flag = 0;
     fence_mbar_init();
   }
@@ -496,266 +533,350 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = bar->tmem;  // S^T 0, dP^T 128, dV 256, dK 384
 
   if (warp == 0) {
+    // ------------------------------------------------- scheduler + producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(&bar->kv_full, 2 * TILE);
-      load_rows<2>(smem + K_OFF_K, &tmK, &bar->kv_full, io.in, bh, Skv, k0);
-      load_rows<2>(smem + K_OFF_V, &tmV, &bar->kv_full, io.in, bh, Skv, k0);
-      // Q and dO have their own slots: dO(it) is free once dV(it) is done,
-      // Q(it) only after dK(it), so each load starts as early as it can
-      for (int it = 0; it < n && !*abort_flag; ++it) {
-        const int s = it & 1;
-        const uint32_t par = ((it >> 1) & 1) ^ 1;
-        const uint32_t qs = (i0 + it) * BM;
-        if (!mbar_wait(&bar->q_empty[s], par, status)) {
-          *abort_flag = 1;
+      bool ok = true;
+      uint32_t g = 0, k = 0;  // tiles / items (with query tiles) loaded so far
+      int w = (int)blockIdx.x;
+      for (uint32_t seq = 0; ok && !*abort_flag; ++seq) {
+        const int slot = seq & 1;
+        if (!mbar_wait(&bar->sched_empty[slot], ((seq >> 1) & 1) ^ 1, status)) {
+          ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&bar->q_full[s], TILE);
-        load_rows<2>(smem + K_OFF_Q + s * TILE, &tmQ, &bar->q_full[s], io.in, bh, Sq, qs);
-        if (!mbar_wait(&bar->do_empty[s], par, status)) {
-          *abort_flag = 1;
-          break;
+        bar->item[slot] = w < total ? w : -1;
+        mbar_arrive(&bar->sched_full[slot]);
+        if (w >= total) break;
+        const KItem it = k_item((uint32_t)w, BH, kblocks, qtiles, hg, causal);
+        if (it.n > 0) {
+          if (k > 0 && !mbar_wait(&bar->kv_empty, (k - 1) & 1, status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bar->kv_full, 2 * TILE);
+          load_rows<2>(smem + K_OFF_K, &tmK, &bar->kv_full, io.in, it.bh, Skv, it.k0);
+          load_rows<2>(smem + K_OFF_V, &tmV, &bar->kv_full, io.in, it.bh, Skv, it.k0);
+          // Q and dO have their own slots: dO(t) is free once dV(t) is
+          // done, Q(t) only after dK(t), so each load starts as early as it can
+          for (int t = 0; t < it.n; ++t, ++g) {
+            const int s = g & 1;
+            const uint32_t par = ((g >> 1) & 1) ^ 1;
+            const uint32_t qs = (it.i0 + t) * BM;
+            if (!mbar_wait(&bar->q_empty[s], par, status)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bar->q_full[s], TILE);
+            load_rows<2>(smem + K_OFF_Q + s * TILE, &tmQ, &bar->q_full[s], io.in, it.bh, Sq, qs);
+            if (!mbar_wait(&bar->do_empty[s], par, status)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bar->do_full[s], TILE);
+            load_rows<2>(smem + K_OFF_DO + s * TILE, &tmDO, &bar->do_full[s], io.in, it.bh, Sq, qs);
+          }
+          ++k;
         }
-        mbar_arrive_expect_tx(&bar->do_full[s], TILE);
-        load_rows<2>(smem + K_OFF_DO + s * TILE, &tmDO, &bar->do_full[s], io.in, bh, Sq, qs);
+        w = (int)gridDim.x + atomicAdd(sched, 1);
       }
+      if (!ok) *abort_flag = 1;
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA
     if (lane == 0) {
-      bool ok = mbar_wait(&bar->kv_full, 0, status);
+      bool ok = true;
+      uint32_t g = 0, k = 0;
       const uint32_t ka = smem_u32(smem + K_OFF_K), va = smem_u32(smem + K_OFF_V);
-      auto qa = [&](int it) { return smem_u32(smem + K_OFF_Q + (it & 1) * TILE); };
-      auto da = [&](int it) { return smem_u32(smem + K_OFF_DO + (it & 1) * TILE); };
-      if (ok && n > 0) {
-        ok = mbar_wait(&bar->q_full[0], 0, status);
-        if (ok) {
-          tc_fence_after();
-          mma_kk(tmem + 0, ka, qa(0));  // S^T(0)  = K  Q_0^T
-          tc_commit(&bar->s_full);
-          ok = mbar_wait(&bar->do_full[0], 0, status);
+      auto qa = [&](uint32_t gg) { return smem_u32(smem + K_OFF_Q + (gg & 1) * TILE); };
+      auto da = [&](uint32_t gg) { return smem_u32(smem + K_OFF_DO + (gg & 1) * TILE); };
+      for (uint32_t seq = 0; ok; ++seq) {
+        const int slot = seq & 1;
+        if (!mbar_wait(&bar->sched_full[slot], (seq >> 1) & 1, status)) {
+          ok = false;
+          break;
         }
-        if (ok) {
-          tc_fence_after();
-          mma_kk(tmem + 128, va, da(0));  // dP^T(0) = V dO_0^T
-          tc_commit(&bar->dp_full);
-        }
-      }
-      for (int it = 0; it < n && ok && !*abort_flag; ++it) {
-        ok = mbar_wait(&bar->pt_full, it & 1, status);
+        const int w = bar->item[slot];
+        mbar_arrive(&bar->sched_empty[slot]);
+        if (w < 0) break;
+        const int n = k_item((uint32_t)w, BH, kblocks, qtiles, hg, causal).n;
+        if (n == 0) continue;
+        const uint32_t g0 = g;
+        ok = mbar_wait(&bar->kv_full, k & 1, status) &&
+             mbar_wait(&bar->q_full[g0 & 1], (g0 >> 1) & 1, status);
         if (!ok) break;
         tc_fence_after();
-        mma_tm(tmem + 256, tmem + 0, da(it), it > 0);  // dV += P^T(it) dO_it
-        tc_commit(&bar->do_empty[it & 1]);
-        if (it + 1 < n) {
-          ok = mbar_wait(&bar->q_full[(it + 1) & 1], ((it + 1) >> 1) & 1, status);
-          if (!ok) break;
-          tc_fence_after();
-          mma_kk(tmem + 0, ka, qa(it + 1));  // S^T(it+1), after dV(it) read P^T(it)
-          tc_commit(&bar->s_full);
-        }
-        ok = mbar_wait(&bar->dst_full, it & 1, status);
+        mma_kk(tmem + 0, ka, qa(g0));  // S^T(0)  = K  Q_0^T
+        tc_commit(&bar->s_full);
+        ok = mbar_wait(&bar->do_full[g0 & 1], (g0 >> 1) & 1, status);
         if (!ok) break;
         tc_fence_after();
-        mma_tm(tmem + 384, tmem + 128, qa(it), it > 0);  // dK += dS^T(it) Q_it
-        tc_commit(&bar->q_empty[it & 1]);
-        if (it + 1 < n) {
-          ok = mbar_wait(&bar->do_full[(it + 1) & 1], ((it + 1) >> 1) & 1, status);
+        mma_kk(tmem + 128, va, da(g0));  // dP^T(0) = V dO_0^T
+        tc_commit(&bar->dp_full);
+        if (n == 1) tc_commit(&bar->kv_empty);  // K / V read for the last time
+        for (int t = 0; t < n && ok && !*abort_flag; ++t) {
+          const uint32_t gg = g0 + t;
+          ok = mbar_wait(&bar->pt_full, gg & 1, status);
+          // the first dV of an item overwrites the accumulator the previous
+          // item's drain reads
+          if (ok && t == 0 && k > 0) ok = mbar_wait(&bar->acc_free, (k - 1) & 1, status);
           if (!ok) break;
           tc_fence_after();
-          mma_kk(tmem + 128, va, da(it + 1));  // dP^T(it+1), after dK(it) read dS^T(it)
-          tc_commit(&bar->dp_full);
+          mma_tm(tmem + 256, tmem + 0, da(gg), t > 0);  // dV += P^T(t) dO_t
+          if (t + 1 < n) {
+            tc_commit(&bar->do_empty[gg & 1]);  // the last tile's slot: released by the drain
+            ok = mbar_wait(&bar->q_full[(gg + 1) & 1], ((gg + 1) >> 1) & 1, status);
+            if (!ok) break;
+            tc_fence_after();
+            mma_kk(tmem + 0, ka, qa(gg + 1));  // S^T(t+1), after dV(t) read P^T(t)
+            tc_commit(&bar->s_full);
+          }
+          ok = mbar_wait(&bar->dst_full, gg & 1, status);
+          if (!ok) break;
+          tc_fence_after();
+          mma_tm(tmem + 384, tmem + 128, qa(gg), t > 0);  // dK += dS^T(t) Q_t
+          tc_commit(t + 1 < n ? &bar->q_empty[gg & 1] : &bar->acc_full);
+          if (t + 1 < n) {
+            ok = mbar_wait(&bar->do_full[(gg + 1) & 1], ((gg + 1) >> 1) & 1, status);
+            if (!ok) break;
+            tc_fence_after();
+            mma_kk(tmem + 128, va, da(gg + 1));  // dP^T(t+1), after dK(t) read dS^T(t)
+            tc_commit(&bar->dp_full);
+            if (t + 2 == n) tc_commit(&bar->kv_empty);
+          }
         }
+        g += (uint32_t)n;
+        ++k;
       }
       if (!ok) *abort_flag = 1;
       tc_commit(&bar->drain);
       mbar_wait(&bar->drain, 0, status);
     }
   } else {
+    // -------------------------------------------------------------- softmax
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;     // which 64 query columns of each tile
     const int row = quarter * 32 + lane;  // key within the block
     const int tid = (threadIdx.x - 64) & 127;  // both halves stage the same 128 values
-    const uint32_t key = k0 + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
-    // -lse / -delta of one query per thread, loaded a tile ahead so the
-    // global loads' latency hides behind the current tile
-    float nl = -INFINITY, nd = 0.0f;
-    auto fetch = [&](int t) {
-      const uint32_t q = (i0 + t) * BM + tid;
-      nl = q < Sq ? -io.lse[(size_t)bh * Sq + q] : -INFINITY;
-      nd = q < Sq ? -io.delta[(size_t)bh * Sq + q] : 0.0f;
-    };
-    if (n > 0) fetch(0);
-    for (int it = 0; it < n && ok; ++it) {
-      const uint32_t qs = (i0 + it) * BM;
-      // stage this tile's -lse / -delta in buffer it & 1; every thread passed
-      // phase it-1 only after all had finished tile it-2, so the buffer is
-      // free.  Bounded wait, like every other.
-      lse_s[(it & 1) * 128 + tid] = nl;
-      del_s[(it & 1) * 128 + tid] = nd;
-      mbar_arrive(&bar->staged);
-      if (it + 1 < n) fetch(it + 1);
-      if (*abort_flag || !mbar_wait(&bar->staged, it & 1, status) ||
-          !mbar_wait(&bar->s_full, it & 1, status)) {
-        *abort_flag = 1;
+    uint32_t gt = 0, k = 0;  // tiles / items done (the inner loops use g for column groups)
+    for (uint32_t seq = 0; ok; ++seq) {
+      const int slot = seq & 1;
+      if (!mbar_wait(&bar->sched_full[slot], (seq >> 1) & 1, status)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      // query q = qs + col is visible to this key iff q >= key (causal),
-      // q < Sq and key < Skv
-      int first_rel = causal ? (int)key - (int)qs : 0;  // first visible col
-      if (first_rel < 0) first_rel = 0;
-      const int last_rel = key < Skv ? (int)min(Sq - 1 - qs, (uint32_t)127) : -1;
-      const float *nls = lse_s + (it & 1) * 128;  // -lse per query
-      const float *ndd = del_s + (it & 1) * 128;  // -delta per query
-      // P^T for this warp's 64 queries: registers, and bf16 pairs into TMEM.
-      // Of every 8 column pairs, 2 take exp2 on the FMA pipe (exp2_fma2) to
-      // share the load with MUFU.  Tiles off the diagonal skip the mask.
-      float p[64];
-      {
-        uint32_t rs[2][32];  // both 32-column loads in flight before one wait
-        tmem_ld_32x32b_x32(tmem + lane_base + half * 64, rs[0]);
-        tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, rs[1]);
-        tc_wait_ld(rs[0]);
-        tc_wait_ld(rs[1]);
-        const uint64_t sc2 = f2pack(scale_log2, scale_log2);
-        auto pt = [&](auto masked) {
-#pragma unroll
+      const int w = bar->item[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->sched_empty[slot]);
+      if (w < 0) break;
+      const KItem itm = k_item((uint32_t)w, BH, kblocks, qtiles, hg, causal);
+      const uint32_t bh = itm.bh, k0 = itm.k0, i0 = itm.i0;
+      const int n = itm.n;
+      const uint32_t key = k0 + row;
+      const bool valid = key < Skv;
+      uint16_t *dk_dst = io.d0 + ((size_t)(bh / io.in.H) * Skv + key) * io.ldd + (size_t)(bh % io.in.H) * D;
+      uint16_t *dv_dst = io.d1 + ((size_t)(bh / io.in.H) * Skv + key) * io.ldd + (size_t)(bh % io.in.H) * D;
+      if (n == 0) {
+        // no query sees these keys: zero gradients
+        if (valid)
+          for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 8) {
+            *reinterpret_cast<uint4 *>(dk_dst + c) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4 *>(dv_dst + c) = make_uint4(0, 0, 0, 0);
+          }
+        continue;
+      }
+      // -lse / -delta of one query per thread, loaded a tile ahead so the
+      // global loads' latency hides behind the current tile
+      float nl = -INFINITY, nd = 0.0f;
+      auto fetch = [&](int t) {
+        const uint32_t q = (i0 + t) * BM + tid;
+        nl = q < Sq ? -io.lse[(size_t)bh * Sq + q] : -INFINITY;
+        nd = q < Sq ? -io.delta[(size_t)bh * Sq + q] : 0.0f;
+      };
+      fetch(0);
+      for (int t = 0; t < n && ok; ++t) {
+        const uint32_t gg = gt + t;
+        const uint32_t qs = (i0 + t) * BM;
+        // stage this tile's -lse / -delta in buffer gg & 1; every thread
+        // passed phase gg-1 only after all had finished tile gg-2, so the
+        // buffer is free.  Bounded wait, like every other.
+        lse_s[(gg & 1) * 128 + tid] = nl;
+        del_s[(gg & 1) * 128 + tid] = nd;
+        mbar_arrive(&bar->staged);
+        if (t + 1 < n) fetch(t + 1);
+        if (*abort_flag || !mbar_wait(&bar->staged, gg & 1, status) ||
+            !mbar_wait(&bar->s_full, gg & 1, status)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // query q = qs + col is visible to this key iff q >= key (causal),
+        // q < Sq and key < Skv
+        int first_rel = causal ? (int)key - (int)qs : 0;  // first visible col
+        if (first_rel < 0) first_rel = 0;
+        const int last_rel = key < Skv ? (int)min(Sq - 1 - qs, (uint32_t)127) : -1;
+        const float *nls = lse_s + (gg & 1) * 128;  // -lse per query
+        const float *ndd = del_s + (gg & 1) * 128;  // -delta per query
+        // P^T for this warp's 64 queries: registers, and bf16 pairs into TMEM.
+        // Of every 8 column pairs, 2 take exp2 on the FMA pipe (exp2_fma2) to
+        // share the load with MUFU.  Tiles off the diagonal skip the mask.
+        float p[64];
+        {
+          uint32_t rs[2][32];  // both 32-column loads in flight before one wait
+          tmem_ld_32x32b_x32(tmem + lane_base + half * 64, rs[0]);
+          tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, rs[1]);
+          tc_wait_ld(rs[0]);
+          tc_wait_ld(rs[1]);
+          const uint64_t sc2 = f2pack(scale_log2, scale_log2);
+          auto pt = [&](auto masked) {
+  #pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+              const int c = half * 2 + cc;
+              const float4 *l4 = reinterpret_cast<const float4 *>(nls + c * 32);
+              uint32_t pk[16];
+  #pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                const float4 l = l4[g];
+                const uint32_t *r = &rs[cc][4 * g];
+                float y[4], e[4];
+                f2unpack(f2fma(f2pack(__uint_as_float(r[0]), __uint_as_float(r[1])), sc2,
+                               f2pack(l.x, l.y)),
+                         y[0], y[1]);
+                f2unpack(f2fma(f2pack(__uint_as_float(r[2]), __uint_as_float(r[3])), sc2,
+                               f2pack(l.z, l.w)),
+                         y[2], y[3]);
+                if ((g & 3) == 3) {
+                  exp2_fma2(y[0], y[1], e[0], e[1]);
+                  exp2_fma2(y[2], y[3], e[2], e[3]);
+                } else {
+  #pragma unroll
+                  for (int k = 0; k < 4; ++k) e[k] = fast_exp2(y[k]);
+                }
+                if constexpr (decltype(masked)::value) {
+  #pragma unroll
+                  for (int k = 0; k < 4; ++k) {
+                    const int col = c * 32 + 4 * g + k;
+                    if (col < first_rel || col > last_rel) e[k] = 0.0f;
+                  }
+                }
+  #pragma unroll
+                for (int k = 0; k < 4; ++k) p[cc * 32 + 4 * g + k] = e[k];
+                pk[2 * g] = pack_bf16(e[0], e[1]);
+                pk[2 * g + 1] = pack_bf16(e[2], e[3]);
+              }
+              tmem_st_32x32b_x16(tmem + lane_base + half * 64 + cc * 16, pk);
+            }
+          };
+          if (__all_sync(0xffffffffu, first_rel == 0 && last_rel == 127))
+            pt(std::false_type{});
+          else
+            pt(std::true_type{});
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->pt_full);  // also: S^T(t) has been read
+        if (!mbar_wait(&bar->dp_full, gg & 1, status)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        {
+          uint32_t rp[2][32];
+          tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64, rp[0]);
+          tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, rp[1]);
+          tc_wait_ld(rp[0]);
+          tc_wait_ld(rp[1]);
+  #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
             const int c = half * 2 + cc;
-            const float4 *l4 = reinterpret_cast<const float4 *>(nls + c * 32);
-            uint32_t pk[16];
-#pragma unroll
+            const float4 *d4 = reinterpret_cast<const float4 *>(ndd + c * 32);
+            uint32_t dk[16];
+  #pragma unroll
             for (int g = 0; g < 8; ++g) {
-              const float4 l = l4[g];
-              const uint32_t *r = &rs[cc][4 * g];
-              float y[4], e[4];
-              f2unpack(f2fma(f2pack(__uint_as_float(r[0]), __uint_as_float(r[1])), sc2,
-                             f2pack(l.x, l.y)),
-                       y[0], y[1]);
-              f2unpack(f2fma(f2pack(__uint_as_float(r[2]), __uint_as_float(r[3])), sc2,
-                             f2pack(l.z, l.w)),
-                       y[2], y[3]);
-              if ((g & 3) == 3) {
-                exp2_fma2(y[0], y[1], e[0], e[1]);
-                exp2_fma2(y[2], y[3], e[2], e[3]);
-              } else {
-#pragma unroll
-                for (int k = 0; k < 4; ++k) e[k] = fast_exp2(y[k]);
-              }
-              if constexpr (decltype(masked)::value) {
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  const int col = c * 32 + 4 * g + k;
-                  if (col < first_rel || col > last_rel) e[k] = 0.0f;
-                }
-              }
-#pragma unroll
-              for (int k = 0; k < 4; ++k) p[cc * 32 + 4 * g + k] = e[k];
-              pk[2 * g] = pack_bf16(e[0], e[1]);
-              pk[2 * g + 1] = pack_bf16(e[2], e[3]);
+              // dS^T = P^T (dP^T - delta), a masked P^T being 0
+              const float4 d = d4[g];
+              const uint32_t *r = &rp[cc][4 * g];
+              const float *pp = &p[cc * 32 + 4 * g];
+              float t0, t1, t2, t3;
+              f2unpack(f2mul(f2pack(pp[0], pp[1]),
+                             f2add(f2pack(__uint_as_float(r[0]), __uint_as_float(r[1])),
+                                   f2pack(d.x, d.y))),
+                       t0, t1);
+              f2unpack(f2mul(f2pack(pp[2], pp[3]),
+                             f2add(f2pack(__uint_as_float(r[2]), __uint_as_float(r[3])),
+                                   f2pack(d.z, d.w))),
+                       t2, t3);
+              dk[2 * g] = pack_bf16(t0, t1);
+              dk[2 * g + 1] = pack_bf16(t2, t3);
             }
-            tmem_st_32x32b_x16(tmem + lane_base + half * 64 + cc * 16, pk);
+            tmem_st_32x32b_x16(tmem + lane_base + 128 + half * 64 + cc * 16, dk);
           }
-        };
-        if (__all_sync(0xffffffffu, first_rel == 0 && last_rel == 127))
-          pt(std::false_type{});
-        else
-          pt(std::true_type{});
-      }
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->pt_full);  // also: S^T(it) has been read
-      if (!mbar_wait(&bar->dp_full, it & 1, status)) {
-        *abort_flag = 1;
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      {
-        uint32_t rp[2][32];
-        tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64, rp[0]);
-        tmem_ld_32x32b_x32(tmem + lane_base + 128 + half * 64 + 32, rp[1]);
-        tc_wait_ld(rp[0]);
-        tc_wait_ld(rp[1]);
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = half * 2 + cc;
-          const float4 *d4 = reinterpret_cast<const float4 *>(ndd + c * 32);
-          uint32_t dk[16];
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            // dS^T = P^T (dP^T - delta), a masked P^T being 0
-            const float4 d = d4[g];
-            const uint32_t *r = &rp[cc][4 * g];
-            const float *pp = &p[cc * 32 + 4 * g];
-            float t0, t1, t2, t3;
-            f2unpack(f2mul(f2pack(pp[0], pp[1]),
-                           f2add(f2pack(__uint_as_float(r[0]), __uint_as_float(r[1])),
-                                 f2pack(d.x, d.y))),
-                     t0, t1);
-            f2unpack(f2mul(f2pack(pp[2], pp[3]),
-                           f2add(f2pack(__uint_as_float(r[2]), __uint_as_float(r[3])),
-                                 f2pack(d.z, d.w))),
-                     t2, t3);
-            dk[2 * g] = pack_bf16(t0, t1);
-            dk[2 * g + 1] = pack_bf16(t2, t3);
-          }
-          tmem_st_32x32b_x16(tmem + lane_base + 128 + half * 64 + cc * 16, dk);
         }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->dst_full);  // also: dP^T(t) has been read
       }
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->dst_full);  // also: dP^T(it) has been read
-    }
-    const bool valid = key < Skv;
-    uint16_t *dk_dst = io.d0 + ((size_t)(bh / io.in.H) * Skv + key) * io.ldd + (size_t)(bh % io.in.H) * D;
-    uint16_t *dv_dst = io.d1 + ((size_t)(bh / io.in.H) * Skv + key) * io.ldd + (size_t)(bh % io.in.H) * D;
-    if (ok && n > 0) {
-      // every MMA, dK(n-1) last, has completed when the drain-side commit of
-      // q_empty for the last tile has arrived
-      const int s = (n - 1) & 1;
-      const bool done = mbar_wait(&bar->q_empty[s], ((n - 1) >> 1) & 1, status);
+      if (!ok) break;
+      // drain: every MMA of the item, dK(n-1) last, is done at acc_full
+      const int sl = (int)((gt + n - 1) & 1);
+      const bool done = mbar_wait(&bar->acc_full, k & 1, status);
       if (done)
         tc_fence_after();
       else
         *abort_flag = 1;
       if (io.tma_out) {
-        // stage dV / dK as bf16 in the (now idle) dO / Q slot 0, laid out like
+        // stage dV / dK as bf16 in the last tile's dO / Q slot, laid out like
         // the loaded tiles (two 64-column boxes, 128-byte swizzle), and send
-        // both tiles with four TMA stores: whole rows leave as bulk writes,
-        // and rows past Skv are clipped by the map.  The staging barrier
-        // (every softmax thread arrives, done or not) has a bounded wait.
-        uint8_t *sv = smem + K_OFF_DO, *sk = smem + K_OFF_Q;
+        // both with four TMA stores: whole rows leave as bulk writes, and rows
+        // past Skv are clipped by the map.  The staging barrier (every
+        // softmax thread arrives, done or not) has a bounded wait.
+        uint8_t *sv = smem + K_OFF_DO + sl * TILE, *sk = smem + K_OFF_Q + sl * TILE;
         if (done) {
           stage_row_bf16(tmem + lane_base + 256 + half * 64, sv, row, half, 1.0f);
           stage_row_bf16(tmem + lane_base + 384 + half * 64, sk, row, half, scale);
-          fence_proxy_async_smem();
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->acc_free);  // dV / dK read out of TMEM
+        fence_proxy_async_smem();
         mbar_arrive(&bar->out_staged);
-        if (threadIdx.x == 64 && done && mbar_wait(&bar->out_staged, 0, status)) {
-          const int32_t hh = (int32_t)(bh % io.in.H), bb = (int32_t)(bh / io.in.H);
-          for (int box = 0; box < 2; ++box) {
-            tma_store_4d(&tmDV, sv + box * BOX, box * 64, hh, (int32_t)k0, bb);
-            tma_store_4d(&tmDK, sk + box * BOX, box * 64, hh, (int32_t)k0, bb);
+        if (threadIdx.x == 64) {
+          if (done && mbar_wait(&bar->out_staged, k & 1, status)) {
+            const int32_t hh = (int32_t)(bh % io.in.H), bb = (int32_t)(bh / io.in.H);
+            for (int box = 0; box < 2; ++box) {
+              tma_store_4d(&tmDV, sv + box * BOX, box * 64, hh, (int32_t)k0, bb);
+              tma_store_4d(&tmDK, sk + box * BOX, box * 64, hh, (int32_t)k0, bb);
+            }
+            tma_store_commit();
+            tma_store_wait_read<0>();  // smem read; the writes finish on their own
           }
-          tma_store_commit();
-          tma_store_wait_read<0>();  // smem read; the writes finish on their own
+          mbar_arrive(&bar->q_empty[sl]);  // the slots go back to the producer
+          mbar_arrive(&bar->do_empty[sl]);
         }
-      } else if (done) {
-        store_row_bf16(tmem + lane_base + 256, dv_dst, 1.0f, valid, half);
-        store_row_bf16(tmem + lane_base + 384, dk_dst, scale, valid, half);
+      } else {
+        if (done) {
+          store_row_bf16(tmem + lane_base + 256, dv_dst, 1.0f, valid, half);
+          store_row_bf16(tmem + lane_base + 384, dk_dst, scale, valid, half);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->acc_free);
+        if (threadIdx.x == 64) {
+          mbar_arrive(&bar->q_empty[sl]);
+          mbar_arrive(&bar->do_empty[sl]);
+        }
       }
-    } else if (ok && valid) {
-      // no query sees these keys: zero gradients
-      for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 8) {
-        *reinterpret_cast<uint4 *>(dk_dst + c) = make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4 *>(dv_dst + c) = make_uint4(0, 0, 0, 0);
+      if (!done) {
+        ok = false;
+        break;
       }
+      gt += (uint32_t)n;
+      ++k;
     }
   }
   tc_fence_before();
@@ -850,9 +971,17 @@ int bwpp_attention_bwd_train(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t
   CUtensorMap tdk, tdv;
   io2.tma_out = make_out_map(&tdk, dk, S, B, H, ldd) && make_out_map(&tdv, dv, S, B, H, ldd);
   if (!io2.tma_out) tdk = tdv = tq;  // unused
-  bwd_dkdv_kernel<<<tiles * BH, THREADS, K_SMEM, ctx->stream>>>(tq, tk, tv, tdo, tdk, tdv, io2, BH, S,
-                                                                S, scale, sl2, causal, tiles,
-                                                                ctx->status_word);
+  // persistent: one CTA per SM (at most one per item); the work counter
+  // hands out items gridDim.x, gridDim.x + 1, ...
+  const uint32_t kv_items = tiles * BH;
+  const uint32_t kv_grid = min((uint32_t)ctx->num_sms, kv_items);
+  const uint32_t hg = max(1u, (uint32_t)ctx->num_sms / tiles);  // heads per item group
+  rc = bwpp_check_cuda(ctx, cudaMemsetAsync(ctx->sched_counter, 0, sizeof(int), ctx->stream),
+                       "attention bwd work counter");
+  if (rc) return rc;
+  bwd_dkdv_kernel<<<kv_grid, THREADS, K_SMEM, ctx->stream>>>(tq, tk, tv, tdo, tdk, tdv, io2, BH, S, S,
+                                                             scale, sl2, causal, tiles, hg,
+                                                             ctx->sched_counter, ctx->status_word);
   BWPP_LAUNCH_CHECK(ctx, "attention bwd dkdv");
   return BWPP_CUDA_OK;
 }
