@@ -432,8 +432,8 @@ static_assert(K_SMEM <= 232448, "dkdv smem");
 
 struct KBars {
   uint64_t kv_full, kv_empty, q_full[2], q_empty[2], do_full[2], do_empty[2], s_full, dp_full,
-      pt_full, dst_full, staged, acc_full, acc_free, out_staged, sched_full[2], sched_empty[2],
-      drain;
+      pt_full, dst_full, staged, acc_full, acc_free, out_staged[2], sched_full[2],
+      sched_empty[2], drain;
   int item[2];
   uint32_t tmem;
   int abort_flag;
@@ -481,7 +481,8 @@ __device__ __forceinline__ void mma_tm(uint32_t d, uint32_t a0, uint32_t b, bool
 // (kv_empty), its first Q / dO into the free slots, and its S^T(0) / dP^T(0)
 // MMAs run while the softmax warps drain the current dV / dK (acc_full); its
 // first dV MMA waits for that drain (acc_free).  The drain stages the bf16
-// tiles in the last tile's Q / dO slots, which the TMA stores then release.
+// tiles in the last tile's Q / dO slots; the producer thread stores them with
+// TMA before it loads into those slots again.
 __global__ void __launch_bounds__(THREADS, 1)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -518,7 +519,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&bar->staged, 32 * SM_WARPS);
     mbar_init(&bar->acc_full, 1);
     mbar_init(&bar->acc_free, SM_WARPS);
-    mbar_init(&bar->out_staged, 32 * SM_WARPS);
+    mbar_init(&bar->out_staged[0], 32 * SM_WARPS);  // by item parity
+    mbar_init(&bar->out_staged[1], 32 * SM_WARPS);
     mbar_init(&bar->drain, 1);
     bar->abort_flag = 0;
     fence_mbar_init();
@@ -538,6 +540,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = true;
       uint32_t g = 0, k = 0;  // tiles / items (with query tiles) loaded so far
       int w = (int)blockIdx.x;
+      // The drain of an item leaves its bf16 dV / dK tiles in its last tile's
+      // dO / Q slot; this thread stores them (oldest first) before it loads
+      // into that slot again, or before it exits, so no softmax warp waits on
+      // a store.  At most two drains are pending: slots alternate by tile.
+      struct Pend {
+        uint32_t k, bh, k0;
+        int sl;
+      } pq[2] = {};
+      int np = 0;
+      auto flush_one = [&]() {
+        const Pend e = pq[0];
+        pq[0] = pq[1];
+        --np;
+        const bool staged = mbar_wait(&bar->out_staged[e.k & 1], (e.k >> 1) & 1, status);
+        if (staged && io.tma_out) {
+          const int32_t hh = (int32_t)(e.bh % io.in.H), bb = (int32_t)(e.bh / io.in.H);
+          for (int box = 0; box < 2; ++box) {
+            tma_store_4d(&tmDV, smem + K_OFF_DO + e.sl * TILE + box * BOX, box * 64, hh,
+                         (int32_t)e.k0, bb);
+            tma_store_4d(&tmDK, smem + K_OFF_Q + e.sl * TILE + box * BOX, box * 64, hh,
+                         (int32_t)e.k0, bb);
+          }
+          tma_store_commit();
+          tma_store_wait_read<0>();  // smem read; the writes finish on their own
+        }
+        mbar_arrive(&bar->q_empty[e.sl]);  // the slots of that item's last tile, free again
+        mbar_arrive(&bar->do_empty[e.sl]);
+        return staged;
+      };
       for (uint32_t seq = 0; ok && !*abort_flag; ++seq) {
         const int slot = seq & 1;
         if (!mbar_wait(&bar->sched_empty[slot], ((seq >> 1) & 1) ^ 1, status)) {
@@ -562,6 +593,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int s = g & 1;
             const uint32_t par = ((g >> 1) & 1) ^ 1;
             const uint32_t qs = (it.i0 + t) * BM;
+            while (ok && np > 0 && (pq[0].sl == s || (np == 2 && pq[1].sl == s))) ok = flush_one();
+            if (!ok) break;
             if (!mbar_wait(&bar->q_empty[s], par, status)) {
               ok = false;
               break;
@@ -575,10 +608,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_arrive_expect_tx(&bar->do_full[s], TILE);
             load_rows<2>(smem + K_OFF_DO + s * TILE, &tmDO, &bar->do_full[s], io.in, it.bh, Sq, qs);
           }
+          if (ok && np == 2) ok = flush_one();
+          pq[np++] = Pend{k, it.bh, it.k0, (int)((g - 1) & 1)};
           ++k;
         }
         w = (int)gridDim.x + atomicAdd(sched, 1);
       }
+      while (ok && np > 0) ok = flush_one();
       if (!ok) *abort_flag = 1;
     }
   } else if (warp == 1) {
@@ -831,10 +867,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         *abort_flag = 1;
       if (io.tma_out) {
         // stage dV / dK as bf16 in the last tile's dO / Q slot, laid out like
-        // the loaded tiles (two 64-column boxes, 128-byte swizzle), and send
-        // both with four TMA stores: whole rows leave as bulk writes, and rows
-        // past Skv are clipped by the map.  The staging barrier (every
-        // softmax thread arrives, done or not) has a bounded wait.
+        // the loaded tiles (two 64-column boxes, 128-byte swizzle); the
+        // producer thread sends them with four TMA stores (whole rows leave
+        // as bulk writes, rows past Skv are clipped by the map) before it
+        // reuses the slot
         uint8_t *sv = smem + K_OFF_DO + sl * TILE, *sk = smem + K_OFF_Q + sl * TILE;
         if (done) {
           stage_row_bf16(tmem + lane_base + 256 + half * 64, sv, row, half, 1.0f);
@@ -844,20 +880,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar->acc_free);  // dV / dK read out of TMEM
         fence_proxy_async_smem();
-        mbar_arrive(&bar->out_staged);
-        if (threadIdx.x == 64) {
-          if (done && mbar_wait(&bar->out_staged, k & 1, status)) {
-            const int32_t hh = (int32_t)(bh % io.in.H), bb = (int32_t)(bh / io.in.H);
-            for (int box = 0; box < 2; ++box) {
-              tma_store_4d(&tmDV, sv + box * BOX, box * 64, hh, (int32_t)k0, bb);
-              tma_store_4d(&tmDK, sk + box * BOX, box * 64, hh, (int32_t)k0, bb);
-            }
-            tma_store_commit();
-            tma_store_wait_read<0>();  // smem read; the writes finish on their own
-          }
-          mbar_arrive(&bar->q_empty[sl]);  // the slots go back to the producer
-          mbar_arrive(&bar->do_empty[sl]);
-        }
       } else {
         if (done) {
           store_row_bf16(tmem + lane_base + 256, dv_dst, 1.0f, valid, half);
@@ -866,11 +888,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar->acc_free);
-        if (threadIdx.x == 64) {
-          mbar_arrive(&bar->q_empty[sl]);
-          mbar_arrive(&bar->do_empty[sl]);
-        }
       }
+      mbar_arrive(&bar->out_staged[k & 1]);  // every softmax thread, done or not
       if (!done) {
         ok = false;
         break;
