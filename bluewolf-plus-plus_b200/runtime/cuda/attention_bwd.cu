@@ -137,11 +137,13 @@ static_assert(Q_SMEM <= 232448, "dq smem");
 // MMAs; Q / dO are released after an item's last S / dP MMA, so the next
 // item's loads overlap its tail.
 struct QBars {
-  uint64_t qd_full, qd_empty, kv_full[2], kv_empty[2], s_full, dp_full, s_read, ds_full, dq_done,
+  uint64_t qd_full, qd_empty, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full, dp_full,
+      s_read, ds_full, dq_done,
       acc_free[2], drain;
   uint32_t tmem;
   int abort_flag;
 };
+static_assert(sizeof(QBars) <= 256, "dq barriers");
 
 struct QItem {
   uint32_t bh, q0;
@@ -174,8 +176,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&bar->qd_full, 1);
     mbar_init(&bar->qd_empty, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&bar->kv_full[s], 1);
-      mbar_init(&bar->kv_empty[s], 1);
+      mbar_init(&bar->k_full[s], 1);
+      mbar_init(&bar->k_empty[s], 1);
+      mbar_init(&bar->v_full[s], 1);
+      mbar_init(&bar->v_empty[s], 1);
       mbar_init(&bar->acc_free[s], SM_WARPS);
     }
     mbar_init(&bar->s_full, 1);
@@ -212,13 +216,21 @@ __global__ void __launch_bounds__(THREADS, 1)
         load_rows<2>(smem + Q_OFF_DO, &tmDO, &bar->qd_full, io.in, it.bh, Sq, it.q0);
         for (int j = 0; j < it.n && !*abort_flag; ++j, ++kvc) {
           const int s = kvc & 1;
-          if (!mbar_wait(&bar->kv_empty[s], ((kvc >> 1) & 1) ^ 1, status)) {
+          // K and V have their own slots: V(j) is free once dP(j) is done,
+          // K(j) only after dQ(j), so the K load S(j+2) waits for is alone
+          const uint32_t par = ((kvc >> 1) & 1) ^ 1;
+          if (!mbar_wait(&bar->k_empty[s], par, status)) {
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&bar->kv_full[s], 2 * TILE);
-          load_rows<2>(smem + Q_OFF_K + s * TILE, &tmK, &bar->kv_full[s], io.in, it.bh, Skv, j * BN);
-          load_rows<2>(smem + Q_OFF_V + s * TILE, &tmV, &bar->kv_full[s], io.in, it.bh, Skv, j * BN);
+          mbar_arrive_expect_tx(&bar->k_full[s], TILE);
+          load_rows<2>(smem + Q_OFF_K + s * TILE, &tmK, &bar->k_full[s], io.in, it.bh, Skv, j * BN);
+          if (!mbar_wait(&bar->v_empty[s], par, status)) {
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&bar->v_full[s], TILE);
+          load_rows<2>(smem + Q_OFF_V + s * TILE, &tmV, &bar->v_full[s], io.in, it.bh, Skv, j * BN);
         }
       }
     }
@@ -239,19 +251,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         // block 0: S and dP (the previous item's last S / dP were read before
         // its last dS was published, which its last dQ waited for)
         ok = mbar_wait(&bar->qd_full, k & 1, status) &&
-             mbar_wait(&bar->kv_full[g & 1], (g >> 1) & 1, status) &&
+             mbar_wait(&bar->k_full[g & 1], (g >> 1) & 1, status) &&
              (k < 2 || mbar_wait(&bar->acc_free[k & 1], ((k >> 1) - 1) & 1, status));
         if (!ok) break;
         tc_fence_after();
-        mma_kk(tmem + 0, qa, ka(g));    // S  = Q  K_0^T
+        mma_kk(tmem + 0, qa, ka(g));  // S  = Q  K_0^T
         tc_commit(&bar->s_full);
+        ok = mbar_wait(&bar->v_full[g & 1], (g >> 1) & 1, status);
+        if (!ok) break;
+        tc_fence_after();
         mma_kk(tmem + 128, da, va(g));  // dP = dO V_0^T
         tc_commit(&bar->dp_full);
+        tc_commit(&bar->v_empty[g & 1]);
         if (it.n == 1) tc_commit(&bar->qd_empty);  // Q / dO: last S / dP issued
         for (int j = 0; j < it.n && ok && !*abort_flag; ++j) {
           const uint32_t gj = g + (uint32_t)j;
           if (j + 1 < it.n) {
-            ok = mbar_wait(&bar->kv_full[(gj + 1) & 1], ((gj + 1) >> 1) & 1, status) &&
+            ok = mbar_wait(&bar->k_full[(gj + 1) & 1], ((gj + 1) >> 1) & 1, status) &&
                  mbar_wait(&bar->s_read, gj & 1, status);
             if (!ok) break;
             tc_fence_after();
@@ -263,10 +279,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
           mma_km(acc, dsa, ka(gj), j > 0);  // dQ += dS(j) K_j
           tc_commit(&bar->dq_done);
-          tc_commit(&bar->kv_empty[gj & 1]);
+          tc_commit(&bar->k_empty[gj & 1]);
           if (j + 1 < it.n) {
+            ok = mbar_wait(&bar->v_full[(gj + 1) & 1], ((gj + 1) >> 1) & 1, status);
+            if (!ok) break;
+            tc_fence_after();
             mma_kk(tmem + 128, da, va(gj + 1));  // dP(j+1), over the dP(j) read for dS(j)
             tc_commit(&bar->dp_full);
+            tc_commit(&bar->v_empty[(gj + 1) & 1]);
             if (j + 2 == it.n) tc_commit(&bar->qd_empty);
           }
         }
@@ -432,7 +452,7 @@ static_assert(K_SMEM <= 232448, "dkdv smem");
 
 struct KBars {
   uint64_t kv_full, kv_empty, q_full[2], q_empty[2], do_full[2], do_empty[2], s_full, dp_full,
-      pt_full, dst_full, staged, acc_full, acc_free, out_staged[2], sched_full[2],
+      pt_half[2], dst_full, staged, acc_full, acc_free, out_staged[2], sched_full[2],
       sched_empty[2], drain;
   int item[2];
   uint32_t tmem;
@@ -463,6 +483,19 @@ __device__ __forceinline__ KItem k_item(uint32_t w, uint32_t BH, uint32_t kblock
 
 // D(128 x D) (+)= A(128 x 128 queries, bf16 pairs in TMEM at the half-split
 // columns a0 + [0, 32) and a0 + [64, 96)) B(128 queries x D, MN-major smem)
+// The K steps of mma_tm in two parts: part 0 covers queries 0-31 and 64-95
+// (the first 32-query part each softmax half forms), part 1 the others.
+__device__ __forceinline__ void mma_tm_part(uint32_t d, uint32_t a0, uint32_t b, bool acc,
+                                            int part) {
+  const uint32_t blo = smem_desc_lo(b, BOX);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int ks = (i >> 1) * 4 + part * 2 + (i & 1);  // part 0: 0, 1, 4, 5; part 1: 2, 3, 6, 7
+    const uint32_t acol = a0 + (ks >> 2) * 64 + (ks & 3) * 8;
+    tc_mma_f16_ts_w(d, acol, blo + ((ks * 2048) >> 4), HI_SW, IDESC_KM, (acc || i > 0) ? 1u : 0u);
+  }
+}
+
 __device__ __forceinline__ void mma_tm(uint32_t d, uint32_t a0, uint32_t b, bool acc) {
   const uint32_t blo = smem_desc_lo(b, BOX);
 #pragma unroll
@@ -514,7 +547,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     mbar_init(&bar->s_full, 1);
     mbar_init(&bar->dp_full, 1);
-    mbar_init(&bar->pt_full, SM_WARPS);
+    mbar_init(&bar->pt_half[0], SM_WARPS);
+    mbar_init(&bar->pt_half[1], SM_WARPS);
     mbar_init(&bar->dst_full, SM_WARPS);
     mbar_init(&bar->staged, 32 * SM_WARPS);
     mbar_init(&bar->acc_full, 1);
@@ -651,13 +685,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (n == 1) tc_commit(&bar->kv_empty);  // K / V read for the last time
         for (int t = 0; t < n && ok && !*abort_flag; ++t) {
           const uint32_t gg = g0 + t;
-          ok = mbar_wait(&bar->pt_full, gg & 1, status);
+          ok = mbar_wait(&bar->pt_half[0], gg & 1, status);
           // the first dV of an item overwrites the accumulator the previous
           // item's drain reads
           if (ok && t == 0 && k > 0) ok = mbar_wait(&bar->acc_free, (k - 1) & 1, status);
           if (!ok) break;
           tc_fence_after();
-          mma_tm(tmem + 256, tmem + 0, da(gg), t > 0);  // dV += P^T(t) dO_t
+          mma_tm_part(tmem + 256, tmem + 0, da(gg), t > 0, 0);  // dV += P^T(t) dO_t: queries
+          ok = mbar_wait(&bar->pt_half[1], gg & 1, status);     // 0-31, 64-95, then the rest
+          if (!ok) break;
+          tc_fence_after();
+          mma_tm_part(tmem + 256, tmem + 0, da(gg), true, 1);
           if (t + 1 < n) {
             tc_commit(&bar->do_empty[gg & 1]);  // the last tile's slot: released by the drain
             ok = mbar_wait(&bar->q_full[(gg + 1) & 1], ((gg + 1) >> 1) & 1, status);
@@ -803,6 +841,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 pk[2 * g + 1] = pack_bf16(e[2], e[3]);
               }
               tmem_st_32x32b_x16(tmem + lane_base + half * 64 + cc * 16, pk);
+              // each 32-query part of P^T is signalled on its own, so the
+              // dV MMAs over it start while the next part is formed
+              tc_wait_st();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&bar->pt_half[cc]);  // cc 1: S^T(t) has been read
             }
           };
           if (__all_sync(0xffffffffu, first_rel == 0 && last_rel == 127))
@@ -810,10 +854,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           else
             pt(std::true_type{});
         }
-        tc_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar->pt_full);  // also: S^T(t) has been read
         if (!mbar_wait(&bar->dp_full, gg & 1, status)) {
           *abort_flag = 1;
           ok = false;
