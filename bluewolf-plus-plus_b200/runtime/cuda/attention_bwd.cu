@@ -129,9 +129,9 @@ static_assert(Q_SMEM <= 232448, "dq smem");
 //            dS(j) = P (dP(j) - delta) -> smem -> ds_full
 // so S(j+1) and dQ(j) run on the tensor core while the softmax finishes
 // block j, and the exp2 work of block j+1 overlaps dP(j+1).
-// Persistent: one CTA per SM walks the (head, 128-row tile) items heaviest
-// first (item i: tile qtiles-1 - i / BH of head i % BH), CTA c taking items
-// c, c + grid, ...  Block-level barrier phases follow a block counter that
+// Persistent: one CTA per SM walks the (head, 128-row tile) items in rounds
+// (q_pick: a round is gridDim.x consecutive items of a few heads, every other
+// round taken in reverse so heavy and light tiles even out).  Block-level barrier phases follow a block counter that
 // runs on across items.  The two dQ accumulators (TMEM columns 256, 384)
 // alternate between items, so an item's dQ store overlaps the next item's
 // MMAs; Q / dO are released after an item's last S / dP MMA, so the next
@@ -150,13 +150,22 @@ struct QItem {
   int n;
 };
 
+// Item i: head i / qtiles, its tiles heaviest (last) first.
 __device__ __forceinline__ QItem q_item(uint32_t i, uint32_t BH, uint32_t qtiles, uint32_t Sq,
                                         uint32_t Skv, int causal) {
   QItem it;
-  it.bh = i % BH;
-  it.q0 = (qtiles - 1 - i / BH) * BM;  // heavy first
+  it.bh = i / qtiles;
+  it.q0 = (qtiles - 1 - i % qtiles) * BM;
   it.n = blocks_for(it.q0, Sq, Skv, causal);
   return it;
+}
+
+// The item CTA c takes in its round j: rounds of gridDim.x consecutive items
+// (a few heads, whose K / V the CTAs of a round share in L2), every other
+// round walked backwards so that the heavy and light positions of a head's
+// tiles even out over each CTA's rounds.  Past the last item: >= items.
+__device__ __forceinline__ uint32_t q_pick(uint32_t rnd) {
+  return rnd * gridDim.x + ((rnd & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x);
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -204,7 +213,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       uint32_t kvc = 0;  // K / V blocks loaded
       int k = 0;         // items with work, in every role
-      for (uint32_t i = blockIdx.x; i < items && !*abort_flag; i += gridDim.x) {
+      for (uint32_t rnd = 0; rnd * gridDim.x < items && !*abort_flag; ++rnd) {
+        const uint32_t i = q_pick(rnd);
+        if (i >= items) continue;
         const QItem it = q_item(i, BH, qtiles, Sq, Skv, causal);
         if (it.n == 0) continue;
         if (!mbar_wait(&bar->qd_empty, (k++ & 1) ^ 1, status)) {
@@ -243,7 +254,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t g = 0;  // key blocks of all earlier items (the K / V stage counter too)
       bool ok = true;
       int k = -1;
-      for (uint32_t i = blockIdx.x; i < items && ok && !*abort_flag; i += gridDim.x) {
+      for (uint32_t rnd = 0; rnd * gridDim.x < items && ok && !*abort_flag; ++rnd) {
+        const uint32_t i = q_pick(rnd);
+        if (i >= items) continue;
         const QItem it = q_item(i, BH, qtiles, Sq, Skv, causal);
         if (it.n == 0) continue;
         ++k;
@@ -305,7 +318,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool ok = true;
     uint32_t g = 0;
     int k = -1;
-    for (uint32_t i = blockIdx.x; i < items && ok; i += gridDim.x) {
+    for (uint32_t rnd = 0; rnd * gridDim.x < items && ok; ++rnd) {
+      const uint32_t i = q_pick(rnd);
+      if (i >= items) continue;
       const QItem it = q_item(i, BH, qtiles, Sq, Skv, causal);
       if (it.n == 0) continue;
       ++k;
