@@ -117,8 +117,12 @@ __device__ __forceinline__ void stage_row_bf16(uint32_t taddr, uint8_t *tile, in
 // ---------------------------------------------------------------------------
 // dQ
 // ---------------------------------------------------------------------------
-constexpr int Q_OFF_Q = 0, Q_OFF_DO = TILE, Q_OFF_K = 2 * TILE, Q_OFF_V = 4 * TILE,
-              Q_OFF_DS = 6 * TILE, Q_OFF_BAR = 7 * TILE;
+// K in a ring of three slots (K(j) is read by S(j) and, a block later, by
+// dQ(j)); V in one slot (V(j) is read by dP(j) alone, and V(j+1) loads while
+// dQ(j) runs).
+constexpr int K_SLOTS = 3;
+constexpr int Q_OFF_Q = 0, Q_OFF_DO = TILE, Q_OFF_K = 2 * TILE, Q_OFF_V = (2 + K_SLOTS) * TILE,
+              Q_OFF_DS = (3 + K_SLOTS) * TILE, Q_OFF_BAR = (4 + K_SLOTS) * TILE;
 constexpr int Q_SMEM = Q_OFF_BAR + 256 + 1024;
 static_assert(Q_SMEM <= 232448, "dq smem");
 
@@ -137,7 +141,7 @@ static_assert(Q_SMEM <= 232448, "dq smem");
 // MMAs; Q / dO are released after an item's last S / dP MMA, so the next
 // item's loads overlap its tail.
 struct QBars {
-  uint64_t qd_full, qd_empty, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full, dp_full,
+  uint64_t qd_full, qd_empty, k_full[K_SLOTS], k_empty[K_SLOTS], v_full, v_empty, s_full, dp_full,
       s_read, ds_full, dq_done,
       acc_free[2], drain;
   uint32_t tmem;
@@ -184,13 +188,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bar->qd_full, 1);
     mbar_init(&bar->qd_empty, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < K_SLOTS; ++s) {
       mbar_init(&bar->k_full[s], 1);
       mbar_init(&bar->k_empty[s], 1);
-      mbar_init(&bar->v_full[s], 1);
-      mbar_init(&bar->v_empty[s], 1);
-      mbar_init(&bar->acc_free[s], SM_WARPS);
     }
+    mbar_init(&bar->v_full, 1);
+    mbar_init(&bar->v_empty, 1);
+    for (int s = 0; s < 2; ++s) mbar_init(&bar->acc_free[s], SM_WARPS);
     mbar_init(&bar->s_full, 1);
     mbar_init(&bar->dp_full, 1);
     mbar_init(&bar->s_read, SM_WARPS);
@@ -226,22 +230,21 @@ __global__ void __launch_bounds__(THREADS, 1)
         load_rows<2>(smem + Q_OFF_Q, &tmQ, &bar->qd_full, io.in, it.bh, Sq, it.q0);
         load_rows<2>(smem + Q_OFF_DO, &tmDO, &bar->qd_full, io.in, it.bh, Sq, it.q0);
         for (int j = 0; j < it.n && !*abort_flag; ++j, ++kvc) {
-          const int s = kvc & 1;
-          // K and V have their own slots: V(j) is free once dP(j) is done,
-          // K(j) only after dQ(j), so the K load S(j+2) waits for is alone
-          const uint32_t par = ((kvc >> 1) & 1) ^ 1;
-          if (!mbar_wait(&bar->k_empty[s], par, status)) {
+          // K(j) waits for dQ(j-3) to release its slot, V(j) for dP(j-1):
+          // in that order they come free
+          const int s = (int)(kvc % K_SLOTS);
+          if (!mbar_wait(&bar->k_empty[s], ((kvc / K_SLOTS) & 1) ^ 1, status)) {
             *abort_flag = 1;
             break;
           }
           mbar_arrive_expect_tx(&bar->k_full[s], TILE);
           load_rows<2>(smem + Q_OFF_K + s * TILE, &tmK, &bar->k_full[s], io.in, it.bh, Skv, j * BN);
-          if (!mbar_wait(&bar->v_empty[s], par, status)) {
+          if (!mbar_wait(&bar->v_empty, (kvc & 1) ^ 1, status)) {
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&bar->v_full[s], TILE);
-          load_rows<2>(smem + Q_OFF_V + s * TILE, &tmV, &bar->v_full[s], io.in, it.bh, Skv, j * BN);
+          mbar_arrive_expect_tx(&bar->v_full, TILE);
+          load_rows<2>(smem + Q_OFF_V, &tmV, &bar->v_full, io.in, it.bh, Skv, j * BN);
         }
       }
     }
@@ -249,8 +252,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       const uint32_t qa = smem_u32(smem + Q_OFF_Q), da = smem_u32(smem + Q_OFF_DO);
       const uint32_t dsa = smem_u32(smem + Q_OFF_DS);
-      auto ka = [&](uint32_t c) { return smem_u32(smem + Q_OFF_K + (c & 1) * TILE); };
-      auto va = [&](uint32_t c) { return smem_u32(smem + Q_OFF_V + (c & 1) * TILE); };
+      auto ka = [&](uint32_t c) { return smem_u32(smem + Q_OFF_K + (c % K_SLOTS) * TILE); };
+      const uint32_t va = smem_u32(smem + Q_OFF_V);
+      auto kfull = [&](uint32_t c) { return &bar->k_full[c % K_SLOTS]; };
+      auto kpar = [&](uint32_t c) { return (c / K_SLOTS) & 1; };
       uint32_t g = 0;  // key blocks of all earlier items (the K / V stage counter too)
       bool ok = true;
       int k = -1;
@@ -264,23 +269,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         // block 0: S and dP (the previous item's last S / dP were read before
         // its last dS was published, which its last dQ waited for)
         ok = mbar_wait(&bar->qd_full, k & 1, status) &&
-             mbar_wait(&bar->k_full[g & 1], (g >> 1) & 1, status) &&
+             mbar_wait(kfull(g), kpar(g), status) &&
              (k < 2 || mbar_wait(&bar->acc_free[k & 1], ((k >> 1) - 1) & 1, status));
         if (!ok) break;
         tc_fence_after();
         mma_kk(tmem + 0, qa, ka(g));  // S  = Q  K_0^T
         tc_commit(&bar->s_full);
-        ok = mbar_wait(&bar->v_full[g & 1], (g >> 1) & 1, status);
+        ok = mbar_wait(&bar->v_full, g & 1, status);
         if (!ok) break;
         tc_fence_after();
-        mma_kk(tmem + 128, da, va(g));  // dP = dO V_0^T
+        mma_kk(tmem + 128, da, va);  // dP = dO V_0^T
         tc_commit(&bar->dp_full);
-        tc_commit(&bar->v_empty[g & 1]);
+        tc_commit(&bar->v_empty);
         if (it.n == 1) tc_commit(&bar->qd_empty);  // Q / dO: last S / dP issued
         for (int j = 0; j < it.n && ok && !*abort_flag; ++j) {
           const uint32_t gj = g + (uint32_t)j;
           if (j + 1 < it.n) {
-            ok = mbar_wait(&bar->k_full[(gj + 1) & 1], ((gj + 1) >> 1) & 1, status) &&
+            ok = mbar_wait(kfull(gj + 1), kpar(gj + 1), status) &&
                  mbar_wait(&bar->s_read, gj & 1, status);
             if (!ok) break;
             tc_fence_after();
@@ -292,14 +297,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
           mma_km(acc, dsa, ka(gj), j > 0);  // dQ += dS(j) K_j
           tc_commit(&bar->dq_done);
-          tc_commit(&bar->k_empty[gj & 1]);
+          tc_commit(&bar->k_empty[gj % K_SLOTS]);
           if (j + 1 < it.n) {
-            ok = mbar_wait(&bar->v_full[(gj + 1) & 1], ((gj + 1) >> 1) & 1, status);
+            ok = mbar_wait(&bar->v_full, (gj + 1) & 1, status);
             if (!ok) break;
             tc_fence_after();
-            mma_kk(tmem + 128, da, va(gj + 1));  // dP(j+1), over the dP(j) read for dS(j)
+            mma_kk(tmem + 128, da, va);  // dP(j+1), over the dP(j) read for dS(j)
             tc_commit(&bar->dp_full);
-            tc_commit(&bar->v_empty[(gj + 1) & 1]);
+            tc_commit(&bar->v_empty);
             if (j + 2 == it.n) tc_commit(&bar->qd_empty);
           }
         }
