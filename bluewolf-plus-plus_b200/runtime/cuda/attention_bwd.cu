@@ -126,16 +126,18 @@ constexpr int Q_OFF_Q = 0, Q_OFF_DO = TILE, Q_OFF_K = 2 * TILE, Q_OFF_V = (2 + K
 constexpr int Q_SMEM = Q_OFF_BAR + 256 + 1024;
 static_assert(Q_SMEM <= 232448, "dq smem");
 
-// Pipeline of bwd_dq_kernel, per key block j (K / V double-buffered):
-//   MMA:     S(j+1) once S(j) is read | dQ(j) once dS(j) is in smem |
-//            dP(j+1) (dP(j) was read before dS(j) was published)
-//   softmax: P(j) = exp2(...) from S(j) into registers -> s_read;
+// Pipeline of bwd_dq_kernel, per key block j (K in a ring of three, V in one
+// slot):
+//   MMA:     S(j+1) once S(j) is read | dP(j+1) once dS(j) is in smem (dP(j)
+//            was read for it) | dQ(j)
+//   softmax: S(j) into registers -> s_read; P(j) = exp2(...);
 //            dS(j) = P (dP(j) - delta) -> smem -> ds_full
-// so S(j+1) and dQ(j) run on the tensor core while the softmax finishes
-// block j, and the exp2 work of block j+1 overlaps dP(j+1).
+// so S(j+1) runs on the tensor core while the softmax works on block j, and
+// dP(j+1) is ready when dQ(j) has read dS(j) and the smem tile is free again.
 // Persistent: one CTA per SM walks the (head, 128-row tile) items in rounds
 // (q_pick: a round is gridDim.x consecutive items of a few heads, every other
-// round taken in reverse so heavy and light tiles even out).  Block-level barrier phases follow a block counter that
+// round taken in reverse so heavy and light tiles even out).  Block-level
+// barrier phases follow a block counter that
 // runs on across items.  The two dQ accumulators (TMEM columns 256, 384)
 // alternate between items, so an item's dQ store overlaps the next item's
 // MMAs; Q / dO are released after an item's last S / dP MMA, so the next
@@ -295,18 +297,20 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = mbar_wait(&bar->ds_full, gj & 1, status);
           if (!ok) break;
           tc_fence_after();
-          mma_km(acc, dsa, ka(gj), j > 0);  // dQ += dS(j) K_j
-          tc_commit(&bar->dq_done);
-          tc_commit(&bar->k_empty[gj % K_SLOTS]);
+          // dP(j+1) first (over the dP(j) read for dS(j)): the softmax needs it
+          // for dS(j+1) as soon as dQ(j) has read dS(j)
           if (j + 1 < it.n) {
             ok = mbar_wait(&bar->v_full, (gj + 1) & 1, status);
             if (!ok) break;
             tc_fence_after();
-            mma_kk(tmem + 128, da, va);  // dP(j+1), over the dP(j) read for dS(j)
+            mma_kk(tmem + 128, da, va);
             tc_commit(&bar->dp_full);
             tc_commit(&bar->v_empty);
             if (j + 2 == it.n) tc_commit(&bar->qd_empty);
           }
+          mma_km(acc, dsa, ka(gj), j > 0);  // dQ += dS(j) K_j
+          tc_commit(&bar->dq_done);
+          tc_commit(&bar->k_empty[gj % K_SLOTS]);
         }
         g += (uint32_t)it.n;
       }
@@ -356,6 +360,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld_32x32b_x32(tmem + lane_base + half * 64 + 32, rs[1]);
           tc_wait_ld(rs[0]);
           tc_wait_ld(rs[1]);
+          // S(j) is in registers: S(j+1) may now overwrite it, and runs
+          // while this block's exp2 and dS work goes on
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar->s_read);
           const uint64_t sc2 = f2pack(scale_log2, scale_log2), nl2 = f2pack(-lse, -lse);
           auto pq = [&](auto masked) {
 #pragma unroll
@@ -389,9 +398,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           else
             pq(std::true_type{});
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bar->s_read);  // S(j+1) may now overwrite S(j)
         // dS smem is free once the dQ MMA of the previous block is done
         if (!mbar_wait(&bar->dp_full, gj & 1, status) ||
             (gj > 0 && !mbar_wait(&bar->dq_done, (gj - 1) & 1, status))) {
