@@ -4,16 +4,16 @@
 // gradient and delta = rowsum(dO * O):
 //   dP = dO V^T,  dS = P * (dP - delta),
 //   dQ = scale * dS K,  dK = scale * dS^T Q,  dV = P^T dO
-// Two kernels, no atomics:
-//   bwd_dq_kernel    one CTA per (head, 128 query rows); loops over 128-key
-//                    blocks: S = Q K^T and dP = dO V^T into TMEM, the softmax
-//                    warps (one query row per thread) form dS -> smem bf16,
+// Two persistent kernels (one CTA per SM), no atomics:
+//   bwd_dq_kernel    items (head, 128 query rows); loops over 128-key blocks:
+//                    S = Q K^T and dP = dO V^T into TMEM, the softmax warps
+//                    (one query row per thread) form dS -> smem bf16,
 //                    dQ += dS K accumulates in TMEM.
-//   bwd_dkdv_kernel  one CTA per (head, 128 keys); loops over 128-row query
-//                    tiles: S^T = K Q^T and dP^T = V dO^T into TMEM, the
-//                    softmax warps (one key per thread) form P^T and dS^T ->
-//                    smem bf16, dV += P^T dO and dK += dS^T Q accumulate in
-//                    TMEM.
+//   bwd_dkdv_kernel  items (head, 128 keys) from a work counter; loops over
+//                    128-row query tiles: S^T = K Q^T and dP^T = V dO^T into
+//                    TMEM, the softmax warps (one key per thread) form P^T and
+//                    dS^T as bf16 in TMEM, dV += P^T dO and dK += dS^T Q
+//                    accumulate in TMEM.
 // Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer, 2-9 softmax (two
 // per TMEM lane quarter, each taking half of a block's 128 columns: with one
 // warp per quarter the exp2 / dS / pack work left the tensor core idle most
@@ -468,9 +468,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 // computed from (half h of the 128 queries: columns 64h .. 64h+31 of S^T,
 // resp. 128 + 64h .. of dP^T, inside the range that warp itself read), and
 // the dV / dK MMAs take them as the A operand from TMEM.  MMA order per query
-// tile i:  S^T(i), dP^T(i) | dV(i) once P^T(i) is stored | S^T(i+1) (over
-// P^T(i), after dV(i) in issue order) | dK(i) once dS^T(i) is stored |
-// dP^T(i+1) (over dS^T(i)), so the exp2 work of tile i+1 overlaps dK(i).
+// tile i:  S^T(i), dP^T(i) | dV(i), in two halves as each half of P^T(i) is
+// stored | S^T(i+1) (over P^T(i), after dV(i) in issue order) | dK(i) once
+// dS^T(i) is stored | dP^T(i+1) (over dS^T(i)), so the exp2 work of tile i+1
+// overlaps dK(i).
 constexpr int K_OFF_K = 0, K_OFF_V = TILE, K_OFF_Q = 2 * TILE, K_OFF_DO = 4 * TILE,
               K_OFF_LSE = 6 * TILE, K_OFF_BAR = K_OFF_LSE + 2 * 2 * 128 * 4;
 constexpr int K_SMEM = K_OFF_BAR + 256 + 1024;
