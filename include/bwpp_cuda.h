@@ -185,7 +185,8 @@ int bwpp_cuda_attention_bf16(BwppCudaCtx *ctx, const uint16_t *q,
  * Forward writes O (bf16, pitch ldo) and the base-2 log-sum-exp of the
  * scaled scores per query, lse [B*H, S] fp32.  Backward takes O, dO and lse
  * and writes dQ, dK, dV (bf16, pitch ldd); it uses ctx scratch
- * (4 * B*H*S bytes). */
+ * (4 * B*H*S bytes).  Every pitch must be a multiple of 8 elements and the
+ * dQ, dK, dV bases 16-byte aligned, else BWPP_CUDA_ERR_UNSUPPORTED. */
 int bwpp_cuda_attention_fwd_lse_bf16(BwppCudaCtx *ctx, const uint16_t *q,
                                      const uint16_t *k, const uint16_t *v,
                                      uint32_t ld_qkv, uint32_t B, uint32_t H,
