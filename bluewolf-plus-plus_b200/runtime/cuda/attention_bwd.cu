@@ -145,7 +145,7 @@ static_assert(Q_SMEM <= 232448, "dq smem");
 struct QBars {
   uint64_t qd_full, qd_empty, k_full[K_SLOTS], k_empty[K_SLOTS], v_full, v_empty, s_full, dp_full,
       s_read, ds_full, dq_done,
-      acc_free[2], drain;
+      acc_free[2], drain, out_staged, ds_free;
   uint32_t tmem;
   int abort_flag;
 };
@@ -177,7 +177,7 @@ __device__ __forceinline__ uint32_t q_pick(uint32_t rnd) {
 __global__ void __launch_bounds__(THREADS, 1)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                  const BwdIO io, uint32_t BH, uint32_t Sq, uint32_t Skv, float scale,
+                  const __grid_constant__ CUtensorMap tmDQ, const BwdIO io, uint32_t BH, uint32_t Sq, uint32_t Skv, float scale,
                   float scale_log2, int causal, uint32_t qtiles, int *status) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -197,6 +197,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&bar->v_full, 1);
     mbar_init(&bar->v_empty, 1);
     for (int s = 0; s < 2; ++s) mbar_init(&bar->acc_free[s], SM_WARPS);
+    mbar_init(&bar->out_staged, 32 * SM_WARPS);
+    mbar_init(&bar->ds_free, 1);
     mbar_init(&bar->s_full, 1);
     mbar_init(&bar->dp_full, 1);
     mbar_init(&bar->s_read, SM_WARPS);
@@ -398,9 +400,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           else
             pq(std::true_type{});
         }
-        // dS smem is free once the dQ MMA of the previous block is done
+        // dS smem is free once the dQ MMA of the previous block is done and,
+        // in an item's first block, once the previous item's dQ tile staged
+        // there has been read by its TMA store
         if (!mbar_wait(&bar->dp_full, gj & 1, status) ||
-            (gj > 0 && !mbar_wait(&bar->dq_done, (gj - 1) & 1, status))) {
+            (gj > 0 && !mbar_wait(&bar->dq_done, (gj - 1) & 1, status)) ||
+            (io.tma_out && j == 0 && k > 0 && !mbar_wait(&bar->ds_free, (k - 1) & 1, status))) {
           *abort_flag = 1;
           ok = false;
           break;
@@ -444,12 +449,36 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      uint16_t *dst = io.d0 + ((size_t)(bh / io.in.H) * Sq + m) * io.ldd +
-                      (size_t)(bh % io.in.H) * D;
-      store_row_bf16(acc + lane_base, dst, scale, valid, half);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->acc_free[k & 1]);
+      if (io.tma_out) {
+        // dQ (x scale, bf16) staged in the dS tile, whose last reader dQ(n-1)
+        // is done, and sent with two TMA stores (rows past Sq clipped by the
+        // map); the issuing thread releases the tile when they have read it
+        stage_row_bf16(acc + lane_base + half * 64, ds_tile, row, half, scale);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->acc_free[k & 1]);
+        fence_proxy_async_smem();
+        mbar_arrive(&bar->out_staged);
+        if (threadIdx.x == 64) {
+          if (mbar_wait(&bar->out_staged, k & 1, status)) {
+            const int32_t hh = (int32_t)(bh % io.in.H), bb = (int32_t)(bh / io.in.H);
+            tma_store_4d(&tmDQ, ds_tile, 0, hh, (int32_t)it.q0, bb);
+            tma_store_4d(&tmDQ, ds_tile + BOX, 64, hh, (int32_t)it.q0, bb);
+            tma_store_commit();
+            tma_store_wait_read<0>();  // smem read; the writes finish on their own
+          } else {
+            *abort_flag = 1;
+          }
+          mbar_arrive(&bar->ds_free);
+        }
+      } else {
+        uint16_t *dst = io.d0 + ((size_t)(bh / io.in.H) * Sq + m) * io.ldd +
+                        (size_t)(bh % io.in.H) * D;
+        store_row_bf16(acc + lane_base, dst, scale, valid, half);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->acc_free[k & 1]);
+      }
     }
   }
   tc_fence_before();
@@ -1048,10 +1077,13 @@ int bwpp_attention_bwd_train(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t
   }
   const float sl2 = scale * 1.4426950408889634f;
   const uint32_t tiles = (S + 127) / 128;
-  BwdIO io{dq, nullptr, ldd, lse, delta, AttnIO{nullptr, nullptr, 0, nullptr, 1, H}};
+  BwdIO io{dq, nullptr, ldd, lse, delta, AttnIO{nullptr, nullptr, 0, nullptr, 1, H}, 0};
+  CUtensorMap tdq;
+  io.tma_out = make_out_map(&tdq, dq, S, B, H, ldd);
+  if (!io.tma_out) tdq = tq;  // unused
   const uint32_t dq_grid = min((uint32_t)ctx->num_sms, tiles * BH);  // persistent
-  bwd_dq_kernel<<<dq_grid, THREADS, Q_SMEM, ctx->stream>>>(tq, tk, tv, tdo, io, BH, S, S, scale, sl2,
-                                                           causal, tiles, ctx->status_word);
+  bwd_dq_kernel<<<dq_grid, THREADS, Q_SMEM, ctx->stream>>>(tq, tk, tv, tdo, tdq, io, BH, S, S, scale,
+                                                           sl2, causal, tiles, ctx->status_word);
   BWPP_LAUNCH_CHECK(ctx, "attention bwd dq");
   BwdIO io2{dk, dv, ldd, lse, delta, AttnIO{nullptr, nullptr, 0, nullptr, 1, H}, 0};
   CUtensorMap tdk, tdv;
