@@ -47,3 +47,12 @@ def test_reference_arm_row_op_uses_the_reference_function():
     assert d["config"]["rows_per_gpu"] == 65536
     assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+
+
+@pytest.mark.parametrize("name", ["gemm_tc_kernel_config2", "attention_tc_kernel_config4",
+                                  "attention_bwd_tiny_model", "norm_fwd_kernel_rmsnorm_fwd_config3",
+                                  "softmax_rows_kernel_softmax_fwd_config3"])
+def test_profile_traffic_is_recorded(name):
+    """The roofline's `traffic` comes from the committed ncu summary of the kernel."""
+    traffic = bench.profile_traffic(name)
+    assert traffic is not None and traffic > 1e8
