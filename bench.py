@@ -692,13 +692,18 @@ class TinyModelWorkload(Workload):
     scaling = "weak"
     e2e_api = "bwpp_cuda_tiny_model_step with pinned host x / target, loss read back to host"
 
+    def batch(self, r):
+        """Rank r's inputs and targets (seeded per rank; any GPU regenerates them)."""
+        t = self.torch
+        g = t.Generator(device="cuda").manual_seed(5000 + r)
+        x = t.randn(self.B * self.S, self.D, device="cuda", generator=g)
+        return x, t.randn(self.B * self.S, self.D, device="cuda", generator=g)
+
     def setup(self):
         t = self.torch
         self.model = self.bwpp.TinyModel(self.ctx, self.L, self.D, self.H, self.F, self.B, self.S,
                                          1e-5, seed=1)
-        g = t.Generator(device="cuda").manual_seed(5000 + self.rank)
-        self.x = t.randn(self.B * self.S, self.D, device="cuda", generator=g)
-        self.tgt = t.randn(self.B * self.S, self.D, device="cuda", generator=g)
+        self.x, self.tgt = self.batch(self.rank)
         self.loss = t.empty(1, device="cuda")
         self.comm = None
         if self.world > 1:
@@ -731,6 +736,52 @@ class TinyModelWorkload(Workload):
                                "102.8M fp32 gradients",
                 "flops": "3 x forward (GEMMs + causal attention)",
                 "l2": "working set (GBs) far larger than L2"}
+
+    def dp_check(self):
+        """After the timed steps (every rank calls this; same collectives in the
+        same order):
+          replicas_bit_identical  every rank's fp32 parameters equal rank 0's bit
+                                  for bit (NCCL broadcast + compare)
+          allreduce_rel_err       one more step at lr = 0 gives the gradient summed
+                                  over ranks; rank 0 regenerates every rank's batch,
+                                  recomputes each gradient locally (no comm) and
+                                  sums them: ||G - sum|| / ||sum|| (fp64)
+          update_rel_err          the same for the SGD update -(lr / N) G"""
+        t = self.torch
+        n = self.model.count
+        out = {"ranks": self.world}
+        p = t.empty(n, device="cuda")
+        self.model.get(p, None)
+        if self.world > 1:
+            import torch.distributed as dist
+            ref = p.clone()
+            dist.broadcast(ref, 0)
+            same = t.tensor([1 if bool(t.equal(ref, p)) else 0], dtype=t.int32, device="cuda")
+            dist.all_reduce(same, op=dist.ReduceOp.MIN)
+            out["replicas_bit_identical"] = bool(same.item())
+            del ref
+        else:
+            out["replicas_bit_identical"] = True
+        self.model.step(self.x, self.tgt, lr=0.0, comm=self.comm)
+        g = t.empty(n, device="cuda")
+        self.model.get(None, g)
+        if self.rank == 0:
+            acc = t.zeros(n, dtype=t.float64, device="cuda")
+            buf = t.empty(n, device="cuda")
+            for r in range(self.world):
+                xr, tr = self.batch(r)
+                self.model.step(xr, tr, lr=0.0)
+                self.model.get(None, buf)
+                acc += buf.double()
+                del xr, tr
+            err = float(t.linalg.norm(g.double() - acc) / t.linalg.norm(acc))
+            out["allreduce_rel_err"] = err
+            out["update_rel_err"] = err  # the update is -(lr / N) times the summed gradient
+            out["bound"] = "fp32 reassociation of the sum over ranks (NCCL order vs rank order)"
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        return out
 
     def setup_e2e(self):
         self.hx = self.x.cpu().pin_memory()
@@ -824,12 +875,147 @@ def run_reference(args, world):
             "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": kind,
                              "sample": sample},
             "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    # the same suite as our arm's "workloads": the reference's CPU code for each
+    # config where it has one (median of 3 bounded samples)
+    workloads = {}
+    for name in suite_names(args.workloads, args.workload):
+        sw = make_workload(name, 0, 1, None, None, None)
+        cb = cpu_baseline_of(sw)
+        if cb is None:
+            workloads[name] = {"unavailable": f"the reference has no CPU implementation of {name}"}
+        else:
+            workloads[name] = {"value": cb["value"], "unit": cb["unit"], "cpu_baseline": cb,
+                               "config": reference_config(name, world)}
+    if workloads:
+        line["workloads"] = workloads
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+
+# The rest of BASELINE's configs, measured in the same default run (one
+# workload at a time, each released before the next) and reported under
+# "workloads" in the JSON line; the reference's bench/bench_cpu.c likewise
+# covers matmul, softmax and rmsnorm in one run.
+SUITE = ("attention", "attention_causal", "rmsnorm_fwd", "rmsnorm_bwd", "layernorm_fwd",
+         "layernorm_bwd", "reduce_max_fwd", "reduce_max_bwd", "softmax_fwd", "tiny_model")
+
+
+def suite_names(arg, primary):
+    if arg in ("", "none"):
+        return []
+    names = SUITE if arg == "all" else tuple(n for n in arg.split(",") if n)
+    return [n for n in names if n != primary]
+
+
+def time_steps(wl, steps, warmup, torch, ctx, flush, barrier, dist, clocks=None):
+    """W untimed steps, then K steps with CUDA events around each on the
+    launching stream (an L2 flush before each); max over ranks of the sum."""
+    stream = torch.cuda.current_stream()
+    for _ in range(max(warmup, 0)):
+        wl.step()
+    ctx.sync()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    launches = 0
+    barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    for i in range(steps):
+        flush.fill_(float(i))
+        starts[i].record(stream)
+        launches += wl.step()
+        ends[i].record(stream)
+        if clocks:
+            clocks.poll()
+    while not ends[-1].query():
+        if clocks:
+            clocks.poll()
+        time.sleep(0.001)
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.poll(force=True)
+    barrier()
+    wall = time.perf_counter() - wall0
+    ctx.sync()
+    per_step_ms = [st.elapsed_time(en) for st, en in zip(starts, ends)]
+    total_s = max_over_ranks(sum(per_step_ms) / 1e3, dist, "cuda")
+    return total_s, sum(per_step_ms) / 1e3 / steps, launches, wall
+
+
+def roofline_of(wl, my_launch_s):
+    hbm, tflops, tflops_sus, src = peaks()
+    achieved = wl.scale(wl.work_per_step(), my_launch_s)
+    # a kernel timed alone is compared with the burst GEMM peak, a multi-kernel
+    # training step (seconds of back-to-back work) with the sustained one
+    peak = (tflops_sus if getattr(wl, "scaling", "") == "weak" else tflops) \
+        if wl.unit == "TFLOP/s" else hbm
+    # ncu dram bytes of one full-size (N = 1) launch, scaled to this rank's share
+    traffic = profile_traffic(wl.profile)
+    if traffic is not None:
+        traffic = traffic * wl.work_per_step() / wl.total_work_per_step()
+    r = {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": wl.unit,
+         "frac": achieved / peak, "traffic": traffic,
+         "peak_source": f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback",
+         "kernel": wl.kernel}
+    if getattr(wl, "scaling", "") == "weak":
+        r["peak_kind"] = "bf16_tflops_sustained"
+    return r
+
+
+def cpu_baseline_of(wl, repeats=3):
+    """The reference's own CPU code (oracle/_ref; the oracle port if absent) on
+    a bounded sample of this workload: one warm-up call, then the median rate
+    of `repeats` timed calls.  None where the reference has no CPU code."""
+    import oracle as O
+    lib, kind = O.ref_lib(), "reference"
+    if lib is None:
+        lib, kind = O.oracle_lib(), "port"
+    threads = O.cpu_threads()
+    if wl.cpu_sample(lib, threads) is None:
+        return None
+    rates, secs, sample = [], [], ""
+    for _ in range(repeats):
+        w, dt, sample = wl.cpu_sample(lib, threads)
+        rates.append(wl.scale(w, dt))
+        secs.append(dt)
+    return {"value": float(np.median(rates)), "unit": wl.unit, "cores": threads, "kind": kind,
+            "sample": sample, "repeats": repeats, "seconds": float(np.median(secs)),
+            "spread": [float(min(rates)), float(max(rates))]}
+
+
+def run_suite(names, args, rank, world, torch, bwpp, ctx, flush, barrier, dist):
+    out = {}
+    for name in names:
+        wl = make_workload(name, rank, world, torch, bwpp, ctx)
+        if args.rows and isinstance(wl, RowWorkload):
+            wl.R = args.rows
+        wl.setup()
+        total_s, my_s, launches, _ = time_steps(wl, args.steps, args.warmup, torch, ctx, flush,
+                                                barrier, dist)
+        entry = {"value": wl.scale(wl.total_work_per_step() * args.steps, total_s), "unit": wl.unit,
+                 "ms_per_step": 1e3 * total_s / args.steps, "scaling": getattr(wl, "scaling", "strong"),
+                 "dtype": wl.dtype, "gpu_launches": launches, "roofline": roofline_of(wl, my_s),
+                 "config": wl.config()}
+        if hasattr(wl, "dp_check"):
+            entry["dp_check"] = wl.dp_check()
+        if rank == 0 and world == 1 and not args.no_cpu:
+            entry["cpu_baseline"] = cpu_baseline_of(wl)
+        if getattr(wl, "comm", None):
+            torch.cuda.synchronize()
+            bwpp.load().bwpp_cuda_comm_destroy(wl.comm)
+            wl.comm = None
+        if hasattr(wl, "model"):
+            wl.model.close()
+        out[name] = entry
+        del wl
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        barrier()
+    return out
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -838,11 +1024,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="gemm")
+    ap.add_argument("--workloads", default=None,
+                    help="extra workloads reported under 'workloads': all (default with the "
+                         "gemm headline), none, or a comma list")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--rows", type=int, default=0,
                     help="row-workload rows (default 65536; smaller only for profiler captures)")
     args = ap.parse_args()
+    if args.workloads is None:
+        args.workloads = "all" if args.workload == "gemm" else "none"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         run_reference(args, world)
@@ -870,56 +1061,16 @@ def main():
         wl.R = args.rows
     wl.setup()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
-    stream = torch.cuda.current_stream()
-
-    for _ in range(max(args.warmup, 0)):
-        wl.step()
-    ctx.sync()
 
     # ---- timed region: K steps, events around each step on the launch stream
     clocks = ClockSampler(local)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    launches = 0
-    barrier()
-    torch.cuda.synchronize()
-    wall0 = time.perf_counter()
-    for i in range(args.steps):
-        flush.fill_(float(i))
-        starts[i].record(stream)
-        launches += wl.step()
-        ends[i].record(stream)
-        clocks.poll()
-    while not ends[-1].query():
-        clocks.poll()
-        time.sleep(0.001)
-    torch.cuda.synchronize()
-    clocks.poll(force=True)
-    barrier()
-    wall = time.perf_counter() - wall0
-    ctx.sync()
-    per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_s = max_over_ranks(sum(per_step_ms) / 1e3, dist, "cuda")
+    total_s, my_launch_s, launches, wall = time_steps(wl, args.steps, args.warmup, torch, ctx,
+                                                      flush, barrier, dist, clocks)
     value = wl.scale(wl.total_work_per_step() * args.steps, total_s)
     ms_per_step = 1e3 * total_s / args.steps
-    my_launch_s = sum(per_step_ms) / 1e3 / args.steps
 
     # ---- roofline of the dominant kernel (this rank's launches)
-    hbm, tflops, tflops_sus, src = peaks()
-    achieved = wl.scale(wl.work_per_step(), my_launch_s)
-    # a kernel timed alone is compared with the burst GEMM peak, a multi-kernel
-    # training step (seconds of back-to-back work) with the sustained one
-    peak = (tflops_sus if getattr(wl, "scaling", "") == "weak" else tflops) \
-        if wl.unit == "TFLOP/s" else hbm
-    # ncu dram bytes of one full-size (N = 1) launch, scaled to this rank's share
-    traffic = profile_traffic(wl.profile)
-    if traffic is not None:
-        traffic = traffic * wl.work_per_step() / wl.total_work_per_step()
-    roofline = {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": wl.unit,
-                "frac": achieved / peak, "traffic": traffic, "peak_source": f"{src} (MEASURED_PEAKS.json)"
-                if src == "measured" else "fallback", "kernel": wl.kernel}
-    if getattr(wl, "scaling", "") == "weak":
-        roofline["peak_kind"] = "bf16_tflops_sustained"
+    roofline = roofline_of(wl, my_launch_s)
 
     # ---- e2e through the C ABI mirror with host buffers
     e2e = None
@@ -943,30 +1094,34 @@ def main():
     # ---- CPU baseline: the reference's own code on this host (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        import oracle as O
-        lib, kind = O.ref_lib(), "reference"
-        if lib is None:
-            lib, kind = O.oracle_lib(), "port"
-        threads = O.cpu_threads()
-        r = wl.cpu_sample(lib, threads)
-        if r is not None:
-            w, dt, sample = r
-            cpu = {"value": wl.scale(w, dt), "unit": wl.unit, "cores": threads, "kind": kind,
-                   "sample": sample, "seconds": dt}
+        cpu = cpu_baseline_of(wl)
 
+    dp = wl.dp_check() if hasattr(wl, "dp_check") else None
     if getattr(wl, "comm", None):
         torch.cuda.synchronize()
         bwpp.load().bwpp_cuda_comm_destroy(wl.comm)
         wl.comm = None
+    line = {"metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": getattr(wl, "scaling", "strong"), "vs_baseline": None, "dtype": wl.dtype,
+            "data": "synthetic (seeded torch generators), shapes and distributions of the BASELINE config",
+            "config": wl.config(), "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": launches, "clocks": clocks.summary(), "wall_s_timed_region": wall}
+    if dp is not None:
+        line["dp_check"] = dp
+
+    # ---- the other BASELINE configs, each measured the same way
+    names = suite_names(args.workloads, args.workload)
+    if names:
+        if hasattr(wl, "model"):
+            wl.model.close()
+        del wl
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        line["workloads"] = run_suite(names, args, rank, world, torch, bwpp, ctx, flush, barrier, dist)
     if world > 1:
         dist.barrier()
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-                "scaling": getattr(wl, "scaling", "strong"), "vs_baseline": None, "dtype": wl.dtype,
-                "data": "synthetic (seeded torch generators), shapes and distributions of the BASELINE config",
-                "config": wl.config(), "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": launches, "clocks": clocks.summary(), "wall_s_timed_region": wall}
         print(json.dumps(line), flush=True)
     ctx.close()
     if world > 1:

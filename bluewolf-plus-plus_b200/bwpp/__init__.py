@@ -86,6 +86,7 @@ _SIGS = {
     "bwpp_cuda_ctx_last_error": (_cp, [_vp]),
     "bwpp_cuda_device_count": (_i32, []),
     "bwpp_cuda_selftest_wait_timeout": (_i32, [_vp, _u32]),
+    "bwpp_cuda_selftest_occupy": (_i32, [_vp, _vp, _u32, _u32, _u32]),
     "bwpp_cuda_matmul_bf16": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _i32, _i32]),
     "bwpp_cuda_gemm_bf16_ex": (_i32, [_vp, _vp, _vp, _vp, C.POINTER(GemmParams)]),
     "bwpp_cuda_attention_bf16": (_i32, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _i32]),
@@ -113,6 +114,7 @@ _SIGS = {
     "bwpp_cuda_tiny_model_param_count": (_sz, [_vp]),
     "bwpp_cuda_tiny_model_get": (_i32, [_vp, _vp, _vp]),
     "bwpp_cuda_tiny_model_set_params": (_i32, [_vp, _vp]),
+    "bwpp_cuda_tiny_model_input_grad": (_i32, [_vp, _vp]),
     "bwpp_cuda_attention_fwd_lse_bf16": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _f32, _i32,
                                                 _vp, _u32, _vp]),
     "bwpp_cuda_attention_bwd_bf16": (_i32, [_vp, _vp, _vp, _vp, _u32, _vp, _u32, _vp, _u32, _vp,
@@ -475,6 +477,10 @@ class TinyModel:
     def get(self, params_out=None, grads_out=None):
         self.ctx.check(self.lib.bwpp_cuda_tiny_model_get(self.handle, _ptr(params_out), _ptr(grads_out)),
                        "tiny_model_get")
+
+    def input_grad(self, dx_out):
+        self.ctx.check(self.lib.bwpp_cuda_tiny_model_input_grad(self.handle, _ptr(dx_out)),
+                       "tiny_model_input_grad")
 
     def set_params(self, params):
         self.ctx.check(self.lib.bwpp_cuda_tiny_model_set_params(self.handle, _ptr(params)),

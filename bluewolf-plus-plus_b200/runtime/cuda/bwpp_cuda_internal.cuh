@@ -34,7 +34,7 @@ struct BwppCudaCtx {
   // K parts, and per-(slot, CTA, lane quarter) ready flags that hold the
   // epoch of the launch that last published them.
   float *gemm_partials;
-  uint32_t *gemm_flags;
+  unsigned long long *gemm_counters;
   uint32_t gemm_epoch;
   int gemm_scratch_failed;
   char last_error[256];

@@ -236,9 +236,35 @@ __global__ void selftest_wait_kernel(uint64_t limit_ns, int *status) {
   fence_mbar_init();
   mbar_wait(&bar, 0, status, limit_ns);
 }
+// Holds an SM slot for `busy_ns` of %globaltimer (no memory traffic).
+__global__ void selftest_occupy_kernel(uint64_t busy_ns) {
+  extern __shared__ uint8_t held[];
+  const uint64_t t0 = bwpp_globaltimer();
+  while (bwpp_globaltimer() - t0 < busy_ns) __nanosleep(1000);
+  if (threadIdx.x == 0 && busy_ns == ~0ull) held[0] = 0;  // keeps the smem request
+}
 }  // namespace
 
 extern "C" {
+
+int bwpp_cuda_selftest_occupy(BwppCudaCtx *ctx, void *stream, uint32_t ctas,
+                              uint32_t smem_bytes, uint32_t busy_ms) {
+  int rc = bwpp_ctx_enter(ctx);
+  if (rc) return rc;
+  if (ctas == 0 || ctas > 4096 || busy_ms == 0 || busy_ms > 3000 || smem_bytes > 227 * 1024)
+    return bwpp_set_error(ctx, BWPP_CUDA_ERR_ARG,
+                          "selftest_occupy: 1..4096 CTAs, 1..3000 ms, <= 227 KB shared memory");
+  rc = bwpp_check_cuda(ctx,
+                       cudaFuncSetAttribute(selftest_occupy_kernel,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)smem_bytes),
+                       "selftest_occupy smem attribute");
+  if (rc) return rc;
+  selftest_occupy_kernel<<<ctas, 32, smem_bytes, (cudaStream_t)stream>>>(
+      (uint64_t)busy_ms * 1000000ull);
+  BWPP_LAUNCH_CHECK(ctx, "selftest occupy");
+  return BWPP_CUDA_OK;
+}
 
 int bwpp_cuda_selftest_wait_timeout(BwppCudaCtx *ctx, uint32_t limit_ms) {
   int rc = bwpp_ctx_enter(ctx);

@@ -103,15 +103,21 @@ struct GemmEpi {
 // Split tail (sk_parts > 1): the sk_tiles tiles after the full waves are cut
 // into sk_parts K ranges, and items [items, items + sk_tiles * sk_parts)
 // hold them part-major (all tiles' part 0, then all tiles' part 1, ...);
-// sk_tiles * sk_parts <= workers, so the whole tail is one round: every part
-// of a tile runs at the same time, each as its worker's last item.  The
-// tile's output is shared out like a reduce-scatter: each epilogue warp's
-// k-th chunk belongs to part k % sk_parts.  A part first writes its fp32
-// partial sums of the chunks other parts own to its slot of `partials` and
-// publishes them, then waits for the other parts' flags, adds their partials
-// of its own chunks (in part order) and runs the epilogue on those chunks.
-// Publishing comes before waiting in every part, so no part waits on one
-// that waits on it.
+// sk_tiles * sk_parts <= workers, so the whole tail is normally one round,
+// each part its worker's last item.  The tile's output is shared out like a
+// reduce-scatter: an epilogue warp's chunks fall into sk_parts classes
+// (chunk k is in class k % sk_parts), and each class is finished by the part
+// that reaches it last.  A part visits the classes in the order part + 1,
+// part + 2, ..., part (its "own" class last).  At each class it counts
+// itself in (an epoch-tagged arrival counter); if others are still to come,
+// it writes its fp32 partials of that class to its slot of `partials` and
+// counts them written; the last to arrive instead owns the class: once the
+// written count shows every other part's partials, it adds them (in part
+// order) to its own accumulator and runs the epilogue on those chunks.
+// A part waits only for parts that have already arrived, so they are
+// running and finish their writes on their own: the split tail needs no
+// two CTAs resident at the same time (kernels of other streams may hold
+// SMs), and when all parts run together each ends up owning its own class.
 struct GemmWork {
   uint32_t split_begin;
   uint32_t items;
@@ -119,17 +125,58 @@ struct GemmWork {
   uint32_t sk_tile0;   // first split tile (= items)
   uint32_t sk_tiles;   // 0: no split tail
   uint32_t sk_parts;
-  uint32_t epoch;      // flag value published by this launch
+  uint32_t epoch;      // tag of this launch's counts (counter high word)
   float *partials;     // [slot][TILE_M][BN] fp32, in TMEM chunk order
-  uint32_t *flags;     // [slot][2 CTAs][EPI_WARPS]
+  unsigned long long *counters;  // [slot][2 CTAs][EPI_WARPS][arrived, written]
 };
+
+// Counts one arrival on an epoch-tagged counter (high word: epoch, low word:
+// count; a word from an earlier launch reads as a count of 0) and returns the
+// count before it.  At most sk_parts warps contend, so the loop ends.
+__device__ __forceinline__ uint32_t epoch_arrive(unsigned long long *p, uint32_t epoch) {
+  unsigned long long cur = *reinterpret_cast<volatile unsigned long long *>(p);
+  while (true) {
+    const unsigned long long base =
+        (uint32_t)(cur >> 32) == epoch ? cur : ((unsigned long long)epoch << 32);
+    const unsigned long long prev = atomicCAS(p, cur, base + 1);
+    if (prev == cur) return (uint32_t)base;
+    cur = prev;
+  }
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits (bounded) until the counter reads `count` in this epoch; acquire, so
+// the counted writers' partials are then visible.
+__device__ __forceinline__ bool epoch_wait(const unsigned long long *p, uint32_t epoch,
+                                           uint32_t count, int *status) {
+  const unsigned long long want = ((unsigned long long)epoch << 32) | count;
+  if (ld_acquire_gpu_u64(p) == want) return true;
+  const uint64_t t0 = bwpp_globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      if (ld_acquire_gpu_u64(p) == want) return true;
+      __nanosleep(64);
+    }
+    if (bwpp_globaltimer() - t0 > BWPP_WAIT_LIMIT_NS) {
+      bwpp_report(status, BWPP_CUDA_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
 
 // One work item: a tile (or tile half) and the K blocks [kb0, kb1) of it.
 struct GemmItem {
   uint32_t mb, nb, n_off, wn, kb0, kb1;
   uint32_t role;       // 0 whole tile (or half), 3 split part
   uint32_t part;       // split part: its K range index
-  uint32_t slot;       // split part: slot of part 0 of its tile (part p: slot + p)
+  uint32_t slot;       // split part: slot of part 0 of its tile (part p: slot + p;
+                       // class c's counters: slot + c)
 };
 
 __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m,
@@ -371,7 +418,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       return work.partials + (size_t)sl * Cfg::TILE_M * BN + (size_t)rank * BM * BN +
              (size_t)(q * 32 + lane) * 4;
     };
-    auto flag_of = [&](uint32_t sl) { return work.flags + (sl * 2 + rank) * EPI_WARPS + ew; };
+    // class counters of a split tile: [slot][CTA rank][epilogue warp][arrived, written]
+    auto counter_of = [&](uint32_t sl) {
+      return work.counters + ((size_t)(sl * 2 + rank) * EPI_WARPS + ew) * 2;
+    };
     GemmItem x;
     for (uint32_t it = worker;
          !*abort_flag && get_item(work, tiles_m, tiles_n, num_kb, it, x); it += work.workers) {
@@ -400,36 +450,51 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t first_col = nb * BN + n_off;
       const int nchunks = (int)min(wn / cw, (N - first_col + cw - 1) / cw);
       const int my_chunks = nchunks > sub ? (nchunks - sub + 1) / 2 : 0;
-      // split part: this warp's chunk k belongs to part k % parts
+      // split part: this warp's chunk k is in class k % parts; the part that
+      // reaches a class last finishes it (see GemmWork)
       const bool split = x.role == 3;
       const int parts = split ? (int)work.sk_parts : 1;
-      const int mine = split ? (int)x.part : 0;
+      const int me = split ? (int)x.part : 0;
       const uint32_t n_contrib = split ? (uint32_t)parts - 1 : 0;
-      const int own_chunks = my_chunks > mine ? (my_chunks - mine + parts - 1) / parts : 0;
+      auto class_chunks = [&](int c) {
+        return my_chunks > c ? (my_chunks - c + parts - 1) / parts : 0;
+      };
+      uint32_t owned = split ? 0u : 1u;  // bit c: this part finishes class c
       if (split) {
-        // partial sums of the chunks other parts own, to this part's slot;
-        // then publish them (every lane's stores precede the flag)
         float *dst = slot_rows(x.slot + x.part);
-        for (int k = 0; k < my_chunks; ++k) {
-          if (k % parts == mine) continue;
-          for (int h = 0; h < per; ++h) {
-            const uint32_t cc = part_col(k * per + h);
-            uint32_t w[32];
-            tmem_ld_32x32b_x32(tmem_base + tq + acc * BN + cc, w);
-            tc_wait_ld(w);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              __stcg(reinterpret_cast<float4 *>(dst + (size_t)(cc / 32) * BM * 32 + j * BM * 4),
-                     make_float4(__uint_as_float(w[4 * j]), __uint_as_float(w[4 * j + 1]),
-                                 __uint_as_float(w[4 * j + 2]), __uint_as_float(w[4 * j + 3])));
+        for (int i = 1; i <= parts; ++i) {
+          const int c = (me + i) % parts;  // this part's own class last
+          if (class_chunks(c) == 0) continue;
+          unsigned long long *ctr = counter_of(x.slot + c);
+          uint32_t before = 0;
+          if (lane == 0) before = epoch_arrive(ctr, work.epoch);
+          before = __shfl_sync(0xffffffffu, before, 0);
+          if (before == (uint32_t)parts - 1) {  // every other part is in: finish it here
+            owned |= 1u << c;
+            continue;
           }
+          // others still to come: this part's partial sums of class c to its
+          // slot, then count them written (every lane's stores come first)
+          for (int k = c; k < my_chunks; k += parts) {
+            for (int h = 0; h < per; ++h) {
+              const uint32_t cc = part_col(k * per + h);
+              uint32_t w[32];
+              tmem_ld_32x32b_x32(tmem_base + tq + acc * BN + cc, w);
+              tc_wait_ld(w);
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                __stcg(reinterpret_cast<float4 *>(dst + (size_t)(cc / 32) * BM * 32 + j * BM * 4),
+                       make_float4(__uint_as_float(w[4 * j]), __uint_as_float(w[4 * j + 1]),
+                                   __uint_as_float(w[4 * j + 2]), __uint_as_float(w[4 * j + 3])));
+            }
+          }
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) epoch_arrive(ctr + 1, work.epoch);
         }
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) st_release_gpu(flag_of(x.slot + x.part), work.epoch);
       }
       // the other parts' slots, in part order
-      auto contrib_slot = [&](uint32_t c) { return x.slot + (c < (uint32_t)mine ? c : c + 1); };
+      auto contrib_slot = [&](uint32_t c) { return x.slot + (c < (uint32_t)me ? c : c + 1); };
       // Partials are staged through shared memory with per-thread async
       // copies, `depth` parts ahead, so many loads are in flight.  The
       // operand ring is free once this item's MMAs are done, as a split part
@@ -438,210 +503,232 @@ __global__ void __launch_bounds__(THREADS, 1)
       // ([float4 index][lane] x 16 B, each lane reads back its own).
       constexpr uint32_t RING_SHARE = Cfg::OFF_C / EPI_WARPS;
       int depth = 0;
-      const uint32_t pbuf = smem_u32(smem) + (uint32_t)ew * RING_SHARE;
-      const int own_parts = own_chunks * per;
-      // accumulator column of this warp's t-th owned 32-column part
-      auto own_col = [&](int t) { return part_col((mine + (t / per) * parts) * per + t % per); };
-      int issued = 0;
-      auto issue = [&](int t) {
-        const uint32_t base = pbuf + (uint32_t)((t % depth) * n_contrib) * 4096u + lane * 16u;
-        const uint32_t pc = own_col(t) / 32;
-        for (uint32_t c = 0; c < n_contrib; ++c) {
-          const float *src = slot_rows(contrib_slot(c)) + (size_t)pc * BM * 32;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) cp_async_16(base + c * 4096u + j * 512u, src + j * BM * 4);
-        }
-        cp_async_commit();
-        ++issued;
-      };
       if (n_contrib) {
-        bool ok = true;
-        for (uint32_t c = 0; c < n_contrib; ++c)
-          ok = ok && flag_wait(flag_of(contrib_slot(c)), work.epoch, status);
-        if (!__all_sync(0xffffffffu, ok)) {
-          *abort_flag = 1;
-          break;
-        }
         GemmItem later;
         const int fit = (int)(RING_SHARE / (4096u * n_contrib));
         if (!get_item(work, tiles_m, tiles_n, num_kb, it + work.workers, later) && fit >= 1) {
           depth = fit < 8 ? fit : 8;
           fence_proxy_async_smem();  // the ring was last used by TMA and the tensor core
-          for (int t = 0; t < depth && t < own_parts; ++t) issue(t);
         }
       }
-      const uint32_t row0 = mb * Cfg::TILE_M + rank * BM + q * 32;
-      const uint32_t my_row = row0 + lane;
-      for (int ko = 0; ko < own_chunks; ++ko) {
-        const int k = mine + ko * parts;  // this warp's chunk index
-        const uint32_t col0 = first_col + (uint32_t)(sub + 2 * k) * cw;
-        uint32_t outw[32];
+      const uint32_t pbuf = smem_u32(smem) + (uint32_t)ew * RING_SHARE;
+      bool item_ok = true;
+      for (int cls = 0; cls < parts && item_ok; ++cls) {
+        if (!(owned >> cls & 1u)) continue;
+        const int own_chunks = class_chunks(cls);
+        const int own_parts = own_chunks * per;
+        // accumulator column of this warp's t-th 32-column part of class cls
+        auto own_col = [&](int t) { return part_col((cls + (t / per) * parts) * per + t % per); };
+        int issued = 0;
+        auto issue = [&](int t) {
+          const uint32_t base = pbuf + (uint32_t)((t % depth) * n_contrib) * 4096u + lane * 16u;
+          const uint32_t pc = own_col(t) / 32;
+          for (uint32_t c = 0; c < n_contrib; ++c) {
+            const float *src = slot_rows(contrib_slot(c)) + (size_t)pc * BM * 32;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (h == 1 && !out16) break;
-          const int t = ko * per + h;           // this warp's owned-part index
-          const uint32_t cs = col0 + h * 32;    // first column of this 32-wide part
-          const uint32_t cc = cs - first_col;   // accumulator column
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + tq + acc * BN + cc, r);
-          tc_wait_ld(r);
-          float v[32];
+            for (int j = 0; j < 8; ++j) cp_async_16(base + c * 4096u + j * 512u, src + j * BM * 4);
+          }
+          cp_async_commit();
+          ++issued;
+        };
+        if (n_contrib) {
+          // the other parts have all arrived, so they are running: wait for
+          // their partials of this class to be written
+          bool ok = true;
+          if (lane == 0) ok = epoch_wait(counter_of(x.slot + cls) + 1, work.epoch, n_contrib, status);
+          if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+            item_ok = false;
+            break;
+          }
+          if (depth)
+            for (int t = 0; t < depth && t < own_parts; ++t) issue(t);
+        }
+        const uint32_t row0 = mb * Cfg::TILE_M + rank * BM + q * 32;
+        const uint32_t my_row = row0 + lane;
+        for (int ko = 0; ko < own_chunks; ++ko) {
+          const int k = cls + ko * parts;  // this warp's chunk index
+          const uint32_t col0 = first_col + (uint32_t)(sub + 2 * k) * cw;
+          uint32_t outw[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          if (n_contrib) {
-            const int pc = (int)(cc / 32);
-            if (depth) {
-              cp_async_wait_pending(issued - (t + 1));
-              const uint8_t *blk = smem + (size_t)ew * RING_SHARE +
-                                   (size_t)((t % depth) * n_contrib) * 4096u + lane * 16u;
-#pragma unroll 1
-              for (uint32_t c = 0; c < n_contrib; ++c) {
+          for (int h = 0; h < 2; ++h) {
+            if (h == 1 && !out16) break;
+            const int t = ko * per + h;           // this warp's owned-part index
+            const uint32_t cs = col0 + h * 32;    // first column of this 32-wide part
+            const uint32_t cc = cs - first_col;   // accumulator column
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + tq + acc * BN + cc, r);
+            tc_wait_ld(r);
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            if (n_contrib) {
+              const int pc = (int)(cc / 32);
+              // The tile's sum is the left fold p0 + p1 + ... in part order,
+              // this part's own accumulator taking its place, so the result
+              // does not depend on which part finished the class.
+              auto fold = [&](auto contrib) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                  const float4 pv = *reinterpret_cast<const float4 *>(blk + c * 4096u + j * 512u);
-                  v[4 * j] += pv.x;
-                  v[4 * j + 1] += pv.y;
-                  v[4 * j + 2] += pv.z;
-                  v[4 * j + 3] += pv.w;
-                }
-              }
-              if (t + depth < own_parts) issue(t + depth);  // into the block just read
-            } else {
+                  float4 sum = me == 0 ? make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                                                     v[4 * j + 3])
+                                       : contrib(0u, j);
 #pragma unroll 1
-              for (uint32_t c = 0; c < n_contrib; ++c) {
-                const float *src = slot_rows(contrib_slot(c)) + (size_t)pc * BM * 32;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const float4 pv = __ldcg(reinterpret_cast<const float4 *>(src + j * BM * 4));
-                  v[4 * j] += pv.x;
-                  v[4 * j + 1] += pv.y;
-                  v[4 * j + 2] += pv.z;
-                  v[4 * j + 3] += pv.w;
+                  for (int pq = 1; pq < parts; ++pq) {
+                    const float4 t4 = pq == me ? make_float4(v[4 * j], v[4 * j + 1],
+                                                             v[4 * j + 2], v[4 * j + 3])
+                                               : contrib((uint32_t)(pq < me ? pq : pq - 1), j);
+                    sum.x += t4.x;
+                    sum.y += t4.y;
+                    sum.z += t4.z;
+                    sum.w += t4.w;
+                  }
+                  v[4 * j] = sum.x;
+                  v[4 * j + 1] = sum.y;
+                  v[4 * j + 2] = sum.z;
+                  v[4 * j + 3] = sum.w;
                 }
+              };
+              if (depth) {
+                cp_async_wait_pending(issued - (t + 1));
+                const uint8_t *blk = smem + (size_t)ew * RING_SHARE +
+                                     (size_t)((t % depth) * n_contrib) * 4096u + lane * 16u;
+                fold([&](uint32_t c, int j) {
+                  return *reinterpret_cast<const float4 *>(blk + c * 4096u + j * 512u);
+                });
+                if (t + depth < own_parts) issue(t + depth);  // into the block just read
+              } else {
+                fold([&](uint32_t c, int j) {
+                  const float *src = slot_rows(contrib_slot(c)) + (size_t)pc * BM * 32;
+                  return __ldcg(reinterpret_cast<const float4 *>(src + j * BM * 4));
+                });
               }
             }
-          }
-          if (epi.bias) {
+            if (epi.bias) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              v[j] += __shfl_sync(0xffffffffu, breg[j & 7], (int)(cc >> 3) + (j >> 3));
-          }
-          if (epi.glu && my_row < M) {
-            // SwiGLU backward: with s = sigmoid(gate), d(gate) = v up s (1 +
-            // gate (1 - s)) replaces v; d(up) = v gate s is stored here
-            const uint16_t *gr = epi.glu + (size_t)my_row * epi.ldglu + cs;
-            const uint16_t *ur = gr + epi.glu_F;
-            uint16_t *dur = epi.glu_up_out + (size_t)my_row * epi.ldglu + cs;
-            if (cs + 32 <= N) {
-              uint32_t gw[16], uw[16], dw[16];
+              for (int j = 0; j < 32; ++j)
+                v[j] += __shfl_sync(0xffffffffu, breg[j & 7], (int)(cc >> 3) + (j >> 3));
+            }
+            if (epi.glu && my_row < M) {
+              // SwiGLU backward: with s = sigmoid(gate), d(gate) = v up s (1 +
+              // gate (1 - s)) replaces v; d(up) = v gate s is stored here
+              const uint16_t *gr = epi.glu + (size_t)my_row * epi.ldglu + cs;
+              const uint16_t *ur = gr + epi.glu_F;
+              uint16_t *dur = epi.glu_up_out + (size_t)my_row * epi.ldglu + cs;
+              if (cs + 32 <= N) {
+                uint32_t gw[16], uw[16], dw[16];
 #pragma unroll
-              for (int k4 = 0; k4 < 4; ++k4) {
-                const uint4 tg = *reinterpret_cast<const uint4 *>(gr + 8 * k4);
-                const uint4 tu = *reinterpret_cast<const uint4 *>(ur + 8 * k4);
-                gw[4 * k4] = tg.x; gw[4 * k4 + 1] = tg.y; gw[4 * k4 + 2] = tg.z; gw[4 * k4 + 3] = tg.w;
-                uw[4 * k4] = tu.x; uw[4 * k4 + 1] = tu.y; uw[4 * k4 + 2] = tu.z; uw[4 * k4 + 3] = tu.w;
-              }
+                for (int k4 = 0; k4 < 4; ++k4) {
+                  const uint4 tg = *reinterpret_cast<const uint4 *>(gr + 8 * k4);
+                  const uint4 tu = *reinterpret_cast<const uint4 *>(ur + 8 * k4);
+                  gw[4 * k4] = tg.x; gw[4 * k4 + 1] = tg.y; gw[4 * k4 + 2] = tg.z; gw[4 * k4 + 3] = tg.w;
+                  uw[4 * k4] = tu.x; uw[4 * k4 + 1] = tu.y; uw[4 * k4 + 2] = tu.z; uw[4 * k4 + 3] = tu.w;
+                }
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                float du[2];
+                for (int i = 0; i < 16; ++i) {
+                  float du[2];
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                  const float g = load16<false>((uint16_t)(gw[i] >> (16 * e)));
-                  const float u = load16<false>((uint16_t)(uw[i] >> (16 * e)));
+                  for (int e = 0; e < 2; ++e) {
+                    const float g = load16<false>((uint16_t)(gw[i] >> (16 * e)));
+                    const float u = load16<false>((uint16_t)(uw[i] >> (16 * e)));
+                    const float sg = __fdividef(1.0f, 1.0f + __expf(-g));
+                    const float d = v[2 * i + e];
+                    v[2 * i + e] = d * u * sg * (1.0f + g * (1.0f - sg));
+                    du[e] = d * g * sg;
+                  }
+                  dw[i] = pack2_16<false>(du[0], du[1]);
+                }
+#pragma unroll
+                for (int k4 = 0; k4 < 4; ++k4)
+                  *reinterpret_cast<uint4 *>(dur + 8 * k4) =
+                      make_uint4(dw[4 * k4], dw[4 * k4 + 1], dw[4 * k4 + 2], dw[4 * k4 + 3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  if (cs + j >= N) continue;
+                  const float g = load16<false>(gr[j]), u = load16<false>(ur[j]);
                   const float sg = __fdividef(1.0f, 1.0f + __expf(-g));
-                  const float d = v[2 * i + e];
-                  v[2 * i + e] = d * u * sg * (1.0f + g * (1.0f - sg));
-                  du[e] = d * g * sg;
-                }
-                dw[i] = pack2_16<false>(du[0], du[1]);
-              }
-#pragma unroll
-              for (int k4 = 0; k4 < 4; ++k4)
-                *reinterpret_cast<uint4 *>(dur + 8 * k4) =
-                    make_uint4(dw[4 * k4], dw[4 * k4 + 1], dw[4 * k4 + 2], dw[4 * k4 + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (cs + j >= N) continue;
-                const float g = load16<false>(gr[j]), u = load16<false>(ur[j]);
-                const float sg = __fdividef(1.0f, 1.0f + __expf(-g));
-                const float d = v[j];
-                v[j] = d * u * sg * (1.0f + g * (1.0f - sg));
-                dur[j] = (uint16_t)(pack2_16<false>(d * g * sg, 0.0f) & 0xFFFFu);
-              }
-            }
-          }
-          if (epi.silu) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = bwpp_silu_f(v[j]);
-          }
-          if (epi.residual && my_row < M && epi.res16) {
-            // 16-bit residual (read before this chunk is stored: may alias C)
-            const uint16_t *rr =
-                static_cast<const uint16_t *>(epi.residual) + (size_t)my_row * epi.ldr + cs;
-            const bool f16 = epi.res16 == 2;
-            if (cs + 32 <= N && (epi.ldr & 7) == 0 &&
-                (reinterpret_cast<uintptr_t>(epi.residual) & 15) == 0) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint4 t = *reinterpret_cast<const uint4 *>(rr + 8 * j);
-                const uint32_t w[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const uint16_t lo = (uint16_t)(w[e] & 0xFFFFu), hi = (uint16_t)(w[e] >> 16);
-                  v[8 * j + 2 * e] += f16 ? load16<true>(lo) : load16<false>(lo);
-                  v[8 * j + 2 * e + 1] += f16 ? load16<true>(hi) : load16<false>(hi);
+                  const float d = v[j];
+                  v[j] = d * u * sg * (1.0f + g * (1.0f - sg));
+                  dur[j] = (uint16_t)(pack2_16<false>(d * g * sg, 0.0f) & 0xFFFFu);
                 }
               }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (cs + j < N) v[j] += f16 ? load16<true>(rr[j]) : load16<false>(rr[j]);
             }
-          } else if (epi.residual && my_row < M) {
-            const float *rr = static_cast<const float *>(epi.residual) + (size_t)my_row * epi.ldr + cs;
-            if (cs + 32 <= N && (epi.ldr & 3) == 0 &&
-                (reinterpret_cast<uintptr_t>(epi.residual) & 15) == 0) {
+            if (epi.silu) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 t = *reinterpret_cast<const float4 *>(rr + 4 * j);
-                v[4 * j] += t.x;
-                v[4 * j + 1] += t.y;
-                v[4 * j + 2] += t.z;
-                v[4 * j + 3] += t.w;
+              for (int j = 0; j < 32; ++j) v[j] = bwpp_silu_f(v[j]);
+            }
+            if (epi.residual && my_row < M && epi.res16) {
+              // 16-bit residual (read before this chunk is stored: may alias C)
+              const uint16_t *rr =
+                  static_cast<const uint16_t *>(epi.residual) + (size_t)my_row * epi.ldr + cs;
+              const bool f16 = epi.res16 == 2;
+              if (cs + 32 <= N && (epi.ldr & 7) == 0 &&
+                  (reinterpret_cast<uintptr_t>(epi.residual) & 15) == 0) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const uint4 t = *reinterpret_cast<const uint4 *>(rr + 8 * j);
+                  const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const uint16_t lo = (uint16_t)(w[e] & 0xFFFFu), hi = (uint16_t)(w[e] >> 16);
+                    v[8 * j + 2 * e] += f16 ? load16<true>(lo) : load16<false>(lo);
+                    v[8 * j + 2 * e + 1] += f16 ? load16<true>(hi) : load16<false>(hi);
+                  }
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (cs + j < N) v[j] += f16 ? load16<true>(rr[j]) : load16<false>(rr[j]);
               }
+            } else if (epi.residual && my_row < M) {
+              const float *rr = static_cast<const float *>(epi.residual) + (size_t)my_row * epi.ldr + cs;
+              if (cs + 32 <= N && (epi.ldr & 3) == 0 &&
+                  (reinterpret_cast<uintptr_t>(epi.residual) & 15) == 0) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float4 t = *reinterpret_cast<const float4 *>(rr + 4 * j);
+                  v[4 * j] += t.x;
+                  v[4 * j + 1] += t.y;
+                  v[4 * j + 2] += t.z;
+                  v[4 * j + 3] += t.w;
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (cs + j < N) v[j] += rr[j];
+              }
+            }
+            if (out16) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                outw[h * 16 + j] = epi.out_f16 ? pack2_16<true>(v[2 * j], v[2 * j + 1])
+                                               : pack2_16<false>(v[2 * j], v[2 * j + 1]);
             } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (cs + j < N) v[j] += rr[j];
+              for (int j = 0; j < 32; ++j) outw[j] = __float_as_uint(v[j]);
             }
           }
-          if (out16) {
+          // the previous store from this warp's buffer has finished reading it
+          if (lane == 0) tma_store_wait_read<0>();
+          __syncwarp();
+          uint8_t *sc = stage_c;
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              outw[h * 16 + j] = epi.out_f16 ? pack2_16<true>(v[2 * j], v[2 * j + 1])
-                                             : pack2_16<false>(v[2 * j], v[2 * j + 1]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) outw[j] = __float_as_uint(v[j]);
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4 *>(sc + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                make_uint4(outw[4 * j], outw[4 * j + 1], outw[4 * j + 2], outw[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < M) {
+            tma_store_2d(&tmC, sc, (int32_t)col0, (int32_t)row0);
+            tma_store_commit();
           }
         }
-        // the previous store from this warp's buffer has finished reading it
-        if (lane == 0) tma_store_wait_read<0>();
-        __syncwarp();
-        uint8_t *sc = stage_c;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<uint4 *>(sc + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-              make_uint4(outw[4 * j], outw[4 * j + 1], outw[4 * j + 2], outw[4 * j + 3]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && row0 < M) {
-          tma_store_2d(&tmC, sc, (int32_t)col0, (int32_t)row0);
-          tma_store_commit();
-        }
+        if (depth) cp_async_wait_pending(0);  // the ring is reused by the next class
+      }  // classes
+      if (!item_ok) {
+        *abort_flag = 1;
+        break;
       }
-      if (depth) cp_async_wait_pending(0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -734,22 +821,23 @@ int g_pair_clusters[4][64] = {};  // resident CTA pairs per device (0: not queri
 inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Split-tail scratch of ctx: 2 * num_sms fp32 slots of BM x BN (a CTA-pair
-// slot takes two of them; a launch uses at most cap slots) and 16 flags
-// per slot (2 CTAs x 8 epilogue warps).  Allocated on first use; never when the caller owns the workspace
-// (then GEMMs use the half-tile tail).
+// slot takes two of them; a launch uses at most cap slots) and, per slot, an
+// (arrived, written) pair of 64-bit class counters for each of the 2 CTAs x
+// 8 epilogue warps.  Allocated on first use; never when the caller owns the
+// workspace (then GEMMs use the half-tile tail).
 bool gemm_scratch(BwppCudaCtx *ctx) {
   if (ctx->gemm_partials) return true;
   if (ctx->user_workspace || ctx->gemm_scratch_failed) return false;
   const size_t slots = 2 * (size_t)ctx->num_sms;
   const size_t part_bytes = slots * BM * BN * sizeof(float);
-  const size_t flag_bytes = slots * 2 * EPI_WARPS * sizeof(uint32_t);
+  const size_t counter_bytes = slots * 2 * EPI_WARPS * 2 * sizeof(unsigned long long);
   void *p = nullptr;
-  if (cudaMalloc(&p, part_bytes + flag_bytes) != cudaSuccess) {
+  if (cudaMalloc(&p, part_bytes + counter_bytes) != cudaSuccess) {
     (void)cudaGetLastError();
     ctx->gemm_scratch_failed = 1;
     return false;
   }
-  if (cudaMemsetAsync(static_cast<uint8_t *>(p) + part_bytes, 0, flag_bytes, ctx->stream) !=
+  if (cudaMemsetAsync(static_cast<uint8_t *>(p) + part_bytes, 0, counter_bytes, ctx->stream) !=
       cudaSuccess) {
     (void)cudaGetLastError();
     cudaFree(p);
@@ -757,7 +845,7 @@ bool gemm_scratch(BwppCudaCtx *ctx) {
     return false;
   }
   ctx->gemm_partials = static_cast<float *>(p);
-  ctx->gemm_flags = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(p) + part_bytes);
+  ctx->gemm_counters = reinterpret_cast<unsigned long long *>(static_cast<uint8_t *>(p) + part_bytes);
   ctx->gemm_epoch = 0;
   return true;
 }
@@ -849,9 +937,9 @@ int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
     w.sk_tiles = tail;
     w.sk_parts = parts;
     w.epoch = ++ctx->gemm_epoch;
-    if (w.epoch == 0) w.epoch = ++ctx->gemm_epoch;  // 0 is the flags' initial value
+    if (w.epoch == 0) w.epoch = ++ctx->gemm_epoch;  // 0 is the counters' initial tag
     w.partials = ctx->gemm_partials;
-    w.flags = ctx->gemm_flags;
+    w.counters = ctx->gemm_counters;
   } else {
     // whole tiles; a tail that fits twice into one round runs as N halves
     const bool halve = tail > 0 && tail * 2 <= cap;

@@ -13,6 +13,8 @@
 //
 // Reference: runtime/cpu/bwpp_cpu_ref.c:63-90 (rmsnorm fwd); backward rule
 // compiler/graph_ir.c:1735-1789; layernorm has no reference counterpart.
+#include <pthread.h>
+
 #include "bwpp_cuda_internal.cuh"
 #include "rowwise.cuh"
 
@@ -549,28 +551,67 @@ constexpr size_t kNoAllocScratchFloats = (size_t)1 << 20;  // 4 MiB
 // stand-in symbol); the device address comes from cudaGetSymbolAddress.
 static __device__ __align__(256) float g_norm_bwd_scratch[kNoAllocScratchFloats];
 
-float *g_noalloc_scratch[64];
-int g_noalloc_sms[64];
-int g_noalloc_ready[64];
+// Per-device cache of the array's device address, keyed on the CUDA context
+// that was current when it was looked up: a cudaDeviceReset (or anything else
+// that recreates the primary context) reloads the module at a new address, so
+// a changed context redoes the look-up instead of using a stale pointer.
+typedef int (*cu_ctx_get_current_fn)(void **);
 
-// Once per device, with that device current.
-int noalloc_setup(int dev) {
+struct NoAllocDev {
+  void *cu_ctx;
+  float *scratch;
+  int sms;
+};
+
+NoAllocDev g_noalloc[64];
+pthread_mutex_t g_noalloc_mu = PTHREAD_MUTEX_INITIALIZER;
+cu_ctx_get_current_fn g_ctx_get_current = nullptr;
+
+void *current_cu_ctx() {
+  cu_ctx_get_current_fn f = __atomic_load_n(&g_ctx_get_current, __ATOMIC_ACQUIRE);
+  if (!f) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    f = (cu_ctx_get_current_fn)fn;
+    __atomic_store_n(&g_ctx_get_current, f, __ATOMIC_RELEASE);
+  }
+  void *c = nullptr;
+  return f(&c) == 0 ? c : nullptr;
+}
+
+// With device `dev` current: the array's address and the SM count, looked up
+// again whenever the current context is not the one cached.
+int noalloc_setup(int dev, float **scratch, int *sms) {
   if (dev < 0 || dev >= 64) return BWPP_CUDA_ERR_ARG;
-  if (__atomic_load_n(&g_noalloc_ready[dev], __ATOMIC_ACQUIRE)) return BWPP_CUDA_OK;
+  // cudaGetSymbolAddress makes the primary context current if none is yet
   float *p = nullptr;
-  if (cudaGetSymbolAddress((void **)&p, g_norm_bwd_scratch) != cudaSuccess || !p) {
+  void *cc = current_cu_ctx();
+  pthread_mutex_lock(&g_noalloc_mu);
+  NoAllocDev &d = g_noalloc[dev];
+  if (cc && d.cu_ctx == cc && d.scratch) {
+    *scratch = d.scratch;
+    *sms = d.sms;
+    pthread_mutex_unlock(&g_noalloc_mu);
+    return BWPP_CUDA_OK;
+  }
+  int n = 0;
+  if (cudaGetSymbolAddress((void **)&p, g_norm_bwd_scratch) != cudaSuccess || !p ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
     cudaGetLastError();
+    pthread_mutex_unlock(&g_noalloc_mu);
     return BWPP_CUDA_ERR_CUDA;
   }
-  int sms = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-      sms <= 0) {
-    cudaGetLastError();
-    return BWPP_CUDA_ERR_CUDA;
-  }
-  g_noalloc_scratch[dev] = p;
-  g_noalloc_sms[dev] = sms;
-  __atomic_store_n(&g_noalloc_ready[dev], 1, __ATOMIC_RELEASE);
+  d.cu_ctx = cc ? cc : current_cu_ctx();
+  d.scratch = p;
+  d.sms = n;
+  *scratch = p;
+  *sms = n;
+  pthread_mutex_unlock(&g_noalloc_mu);
   return BWPP_CUDA_OK;
 }
 
@@ -584,23 +625,29 @@ extern "C" int bwpp_cuda_rmsnorm_bwd_f32_noalloc(
   const bool partials = dgamma || dbeta;
   // One CTA needs 2 * cols floats of partials: wider rows are rejected.
   if (partials && 2 * (size_t)cols > kNoAllocScratchFloats) return BWPP_CUDA_ERR_ARG;
+  // An error left pending by earlier work of the caller is not this call's:
+  // leave it in place for the caller and launch nothing.
+  if (cudaPeekAtLastError() != cudaSuccess) return BWPP_CUDA_ERR_CUDA;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
     return BWPP_CUDA_ERR_CUDA;
   }
-  int rc = noalloc_setup(dev);
+  float *scratch = nullptr;
+  int sms = 0;
+  int rc = noalloc_setup(dev, &scratch, &sms);
   if (rc) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   if (rows == 0) {
-    // dgamma = dbeta = 0 without a memset allocation: one tiny kernel
+    // dgamma = dbeta = 0 (sums over no rows) with one small kernel each; the
+    // kernel skips a NULL output
     if (partials) {
-      column_sum_kernel<<<(cols + 255) / 256, 256, 0, s>>>(g_noalloc_scratch[dev], dgamma, 0, cols);
-      column_sum_kernel<<<(cols + 255) / 256, 256, 0, s>>>(g_noalloc_scratch[dev], dbeta, 0, cols);
+      column_sum_kernel<<<(cols + 255) / 256, 256, 0, s>>>(scratch, dgamma, 0, cols);
+      column_sum_kernel<<<(cols + 255) / 256, 256, 0, s>>>(scratch, dbeta, 0, cols);
     }
     return cudaGetLastError() == cudaSuccess ? BWPP_CUDA_OK : BWPP_CUDA_ERR_CUDA;
   }
-  uint32_t grid = (uint32_t)g_noalloc_sms[dev] * 4;
+  uint32_t grid = (uint32_t)sms * 4;
   if (rows < grid) grid = rows;
   float *pg = nullptr, *pb = nullptr;
   if (partials) {
@@ -608,7 +655,7 @@ extern "C" int bwpp_cuda_rmsnorm_bwd_f32_noalloc(
     if (grid > fit) grid = (uint32_t)fit;
     // Each CTA overwrites its whole partial row before it is read, so nothing
     // left over from an earlier call leaks into this one.
-    pg = g_noalloc_scratch[dev];
+    pg = scratch;
     pb = pg + (size_t)grid * cols;
   }
   const bool v4 = cols % 4 == 0 && ld % 4 == 0 && aligned16(x) && aligned16(dy) &&

@@ -279,6 +279,19 @@ int bwpp_cuda_tiny_model_get(BwppCudaTinyModel *m, float *params_out, float *gra
   return bwpp_cuda_sync(m->ctx);
 }
 
+int bwpp_cuda_tiny_model_input_grad(BwppCudaTinyModel *m, float *dx_out) {
+  if (!m || !dx_out) return BWPP_CUDA_ERR_ARG;
+  int rc = bwpp_ctx_enter(m->ctx);
+  if (rc) return rc;
+  // after the backward of layer 0, dh holds d loss / d h_in(0) = d loss / d x
+  const size_t n = (size_t)m->cfg.batch * m->cfg.seq * m->cfg.d_model;
+  rc = bwpp_check_cuda(m->ctx, cudaMemcpyAsync(dx_out, m->dh, n * 4, cudaMemcpyDefault,
+                                               m->ctx->stream),
+                       "input grad out");
+  if (rc) return rc;
+  return bwpp_cuda_sync(m->ctx);
+}
+
 int bwpp_cuda_tiny_model_set_params(BwppCudaTinyModel *m, const float *params_in) {
   if (!m || !params_in) return BWPP_CUDA_ERR_ARG;
   int rc = bwpp_ctx_enter(m->ctx);

@@ -131,6 +131,14 @@ int bwpp_cuda_device_count(void);
  * the next bwpp_cuda_sync returns BWPP_CUDA_ERR_TIMEOUT and the context stays
  * usable.  Nothing faults or traps. */
 int bwpp_cuda_selftest_wait_timeout(BwppCudaCtx *ctx, uint32_t limit_ms);
+/* Co-residency self test (no reference counterpart): launches `ctas` CTAs on
+ * `stream` (a cudaStream_t other than the ctx's), each holding `smem_bytes`
+ * of shared memory (<= 227 KB) and an SM slot for `busy_ms` (1..3000) of
+ * %globaltimer, then returning.  A kernel launched meanwhile on the ctx's
+ * stream gets only the SMs left over, which tests that no kernel here waits
+ * on a CTA that has not started (the GEMM's split tail).  Nothing faults. */
+int bwpp_cuda_selftest_occupy(BwppCudaCtx *ctx, void *stream, uint32_t ctas,
+                              uint32_t smem_bytes, uint32_t busy_ms);
 
 /* ---- 1. ctx entry points (device pointers, async) ---------------------- */
 
@@ -230,7 +238,10 @@ int bwpp_cuda_rmsnorm_bwd_f32(BwppCudaCtx *ctx, const float *x,
  *     (1,048,576 floats) inside the library, held on every GPU that loads it
  *     until the process exits.  The first call on a device does the set-up:
  *     it looks up that array's device address (once per device, with the
- *     device current).  Make that first call before any stream capture.
+ *     device current).  Make that first call before any stream capture.  The
+ *     look-up is tied to the device's CUDA context: after a cudaDeviceReset
+ *     (or anything else that creates a new context) the next call looks the
+ *     address up again.
  *   - Limit: with dgamma or dbeta requested, cols may be at most 524,288
  *     (2 * cols floats per CTA); larger cols return BWPP_CUDA_ERR_ARG.  Wide
  *     rows run on fewer CTAs (the partials of all CTAs must fit).
@@ -238,9 +249,12 @@ int bwpp_cuda_rmsnorm_bwd_f32(BwppCudaCtx *ctx, const float *x,
  *     the GPU (different streams, or other host threads) race on it and give
  *     wrong dgamma / dbeta; serialize them.  Each call overwrites the part of
  *     the array it reads, so leftovers of earlier calls do not matter.
- *   - Calls no cudaMalloc, cudaFree or other allocating routine.  Returns a
- *     status code (BWPP_CUDA_ERR_CUDA on a launch error); device-side errors
- *     surface at the caller's next synchronization. */
+ *   - Calls no cudaMalloc, cudaFree or other allocating routine.
+ *   - Errors: BWPP_CUDA_ERR_ARG for bad arguments; BWPP_CUDA_ERR_CUDA when one
+ *     of its own launches fails, or, without launching anything, when a CUDA
+ *     error from earlier work on this thread is still pending (that error is
+ *     left in place for the caller to read).  Device-side errors surface at
+ *     the caller's next synchronization. */
 int bwpp_cuda_rmsnorm_bwd_f32_noalloc(const float *x, const float *gamma,
                                       const float *dy, float *dx, float *dgamma,
                                       float *dbeta, uint32_t rows, uint32_t cols,
@@ -357,6 +371,10 @@ size_t bwpp_cuda_tiny_model_param_count(const BwppCudaTinyModel *model);
  * (host or device destinations; NULL skips).  Synchronous. */
 int bwpp_cuda_tiny_model_get(BwppCudaTinyModel *model, float *params_out,
                              float *grads_out);
+/* Copies d loss / d x [batch*seq, d_model] fp32 of the last step (the
+ * gradient that reaches the input embeddings) to `dx_out` (host or device).
+ * Synchronous. */
+int bwpp_cuda_tiny_model_input_grad(BwppCudaTinyModel *model, float *dx_out);
 /* Replaces the fp32 parameters (host or device source) and re-derives the
  * bf16 compute copies.  Synchronous. */
 int bwpp_cuda_tiny_model_set_params(BwppCudaTinyModel *model,

@@ -56,3 +56,28 @@ def test_profile_traffic_is_recorded(name):
     """The roofline's `traffic` comes from the committed ncu summary of the kernel."""
     traffic = bench.profile_traffic(name)
     assert traffic is not None and traffic > 1e8
+
+
+def test_default_run_covers_every_baseline_config():
+    """The headline GEMM run also measures attention (both masks), the norms,
+    reduce_max, softmax and the tiny_model DP step; other workloads run alone."""
+    names = bench.suite_names("all", "gemm")
+    for n in ("attention", "attention_causal", "rmsnorm_fwd", "rmsnorm_bwd", "layernorm_fwd",
+              "layernorm_bwd", "reduce_max_fwd", "reduce_max_bwd", "softmax_fwd", "tiny_model"):
+        assert n in names
+    assert "gemm" not in names
+    assert bench.suite_names("none", "gemm") == []
+    assert bench.suite_names("attention,tiny_model", "tiny_model") == ["attention"]
+
+
+def test_reference_arm_default_reports_the_suite():
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
+                          "--steps", "1", "--warmup", "0"],
+                         capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads(out.stdout.strip().splitlines()[-1])
+    w = d["workloads"]
+    assert w["rmsnorm_fwd"]["unit"] == "GB/s" and w["rmsnorm_fwd"]["value"] > 0
+    assert w["attention_causal"]["unit"] == "TFLOP/s"
+    assert w["rmsnorm_fwd"]["cpu_baseline"]["repeats"] == 3
+    assert "unavailable" in w["tiny_model"] and "unavailable" in w["layernorm_bwd"]

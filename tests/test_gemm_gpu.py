@@ -268,6 +268,39 @@ def test_wave_tail_split_k(ctx):
     assert torch.equal(c, c2)
 
 
+def test_split_tail_with_half_the_sms_held_by_another_stream(ctx):
+    """The split tail must not need all of its CTAs resident at once: here
+    another stream holds half of the SMs (full shared memory each) for 2.5 s,
+    longer than the kernels' 2 s wait limit, while the 1024 x 4096 x 11008
+    GEMM runs on the rest.  Parts that start early count themselves in and
+    leave their partials; the parts that start after the hold ends finish
+    the tiles.  Status OK, and bit-identical to the same GEMM run alone (the
+    partial sums fold in part order whichever part finishes a tile)."""
+    import bwpp
+    M, K, N = 1024, 4096, 11008
+    g = torch.Generator(device="cuda").manual_seed(78)
+    x = (torch.randn(M, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    w = (torch.randn(K, N, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    b = torch.rand(N, device="cuda", generator=g) * 0.2 - 0.1
+    alone = torch.empty(M, N, device="cuda")
+    ctx.matmul_bf16(x, w, alone, M, N, K, K, N, N, b, 1, 1)
+    ctx.sync()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    other = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    held = torch.empty(M, N, device="cuda")
+    rc = ctx.lib.bwpp_cuda_selftest_occupy(ctx.handle, other.cuda_stream, sms // 2, 200 * 1024, 2500)
+    assert rc == bwpp.OK
+    ctx.matmul_bf16(x, w, held, M, N, K, K, N, N, b, 1, 1)
+    ctx.sync()  # raises on BWPP_CUDA_ERR_TIMEOUT
+    torch.cuda.synchronize()
+    assert torch.equal(held, alone)
+    rows = np.arange(0, M, 37)
+    ref = O.matmul(np.ascontiguousarray(x[rows].float().cpu().numpy()),
+                   np.ascontiguousarray(w.float().cpu().numpy()), b.cpu().numpy(), 1, 1)
+    assert rel_fro(held[rows].cpu().numpy(), ref) <= TIGHT
+
+
 # Split-tail cases: (M, N, K, a_mn, b_mn, out_bf16, residual)
 #  - 2 tiles: each tile's 128 K blocks cut into 8 parts (7 partials per owner)
 #  - M <= 128 (single-CTA kernel): 8 tiles cut into 8 parts each

@@ -1,11 +1,15 @@
 """Data-parallel training step on two GPUs (one process per GPU, NCCL).
 
-Both ranks step the same tiny_model on the same batch; the per-layer
-gradient buckets are summed over NCCL on a side stream, overlapped with the
-backward, and SGD applies lr / 2 to the sum.  With identical data the sum is
-exactly twice each rank's gradient and (lr / 2) * (2 g) == lr * g in fp32,
-so the parameters must equal a single-GPU step bit for bit.  Needs two GPUs
-(skipped otherwise)."""
+The per-layer gradient buckets are summed over NCCL on a side stream,
+overlapped with the backward, and SGD applies lr / 2 to the sum.
+  - Same batch on both ranks: the sum is exactly twice each rank's gradient
+    and (lr / 2) * (2 g) == lr * g in fp32, so the parameters must equal a
+    single-GPU step bit for bit.
+  - A different batch per rank: the summed gradient must equal g0 + g1
+    recomputed locally (an allreduce that only doubled the rank's own
+    gradient fails this), and the step must match a single-GPU step on the
+    concatenated batch of 2B sequences within fp32 reassociation.
+Needs two GPUs (skipped otherwise)."""
 import datetime
 import os
 import socket
@@ -58,6 +62,96 @@ def _rank(rank, world, port, q):
         q.put((rank, diff))
     except Exception as e:  # reported to the parent
         q.put((rank, repr(e)[:300]))
+
+
+def _rank_distinct(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    try:
+        import torch.distributed as dist
+        import bwpp
+        from bwpp.dist import comm_from_process_group
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        lib = bwpp.load()
+        ctx = bwpp.Ctx(rank)
+        L, D, H, F, B, S = 2, 256, 2, 512, 2, 256
+        comm = comm_from_process_group(lib, rank, world, rank, dist)
+        batches = []
+        for r in range(world):  # every rank can regenerate every rank's batch
+            g = torch.Generator(device="cuda").manual_seed(100 + r)
+            batches.append((torch.randn(B * S, D, device="cuda", generator=g),
+                            torch.randn(B * S, D, device="cuda", generator=g)))
+        x, tgt = batches[rank]
+        dp = bwpp.TinyModel(ctx, L, D, H, F, B, S, 1e-5, seed=3)
+        solo = bwpp.TinyModel(ctx, L, D, H, F, B, S, 1e-5, seed=3)
+        cat = bwpp.TinyModel(ctx, L, D, H, F, world * B, S, 1e-5, seed=3)
+        n = dp.count
+        # (1) the summed gradient against a local sum of both ranks' gradients
+        dp.step(x, tgt, lr=0.0, comm=comm)
+        g_dp = torch.empty(n, device="cuda")
+        dp.get(None, g_dp)
+        g_sum = torch.zeros(n, device="cuda")
+        for r in range(world):
+            solo.step(*batches[r], lr=0.0)
+            gr = torch.empty(n, device="cuda")
+            solo.get(None, gr)
+            g_sum += gr
+        ar_err = float(torch.linalg.norm((g_dp - g_sum).double()) / torch.linalg.norm(g_sum.double()))
+        own = torch.empty(n, device="cuda")
+        solo.step(x, tgt, lr=0.0)
+        solo.get(None, own)
+        own_err = float(torch.linalg.norm((g_dp - world * own).double()) / torch.linalg.norm(g_sum.double()))
+        # (2) one step with lr against a single-GPU step on the concatenated batch
+        p0 = torch.empty(n, device="cuda")
+        dp.get(p0, None)
+        dp.step(x, tgt, lr=0.1, comm=comm)
+        p_dp = torch.empty(n, device="cuda")
+        dp.get(p_dp, None)
+        cat.step(torch.cat([b[0] for b in batches]), torch.cat([b[1] for b in batches]), lr=0.1)
+        p_cat = torch.empty(n, device="cuda")
+        cat.get(p_cat, None)
+        d_dp, d_cat = (p_dp - p0).double(), (p_cat - p0).double()
+        step_err = float(torch.linalg.norm(d_dp - d_cat) / torch.linalg.norm(d_cat))
+        ctx.sync()
+        lib.bwpp_cuda_comm_destroy(comm)
+        for m in (dp, solo, cat):
+            m.close()
+        ctx.close()
+        dist.destroy_process_group()
+        q.put((rank, (ar_err, own_err, step_err)))
+    except Exception as e:  # reported to the parent
+        q.put((rank, repr(e)[:300]))
+
+
+def _run_two(target):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, out = q.get(timeout=300)
+        res[r] = out
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return res
+
+
+def test_two_gpu_data_parallel_step_distinct_batches():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    res = _run_two(_rank_distinct)
+    for r in range(2):
+        assert isinstance(res[r], tuple), res
+        ar_err, own_err, step_err = res[r]
+        assert ar_err <= 1e-6, res          # NCCL sum == g0 + g1 (two operands: exact)
+        assert own_err >= 1e-2, res         # and not world x the local gradient
+        assert step_err <= 1e-4, res        # fp32 reassociation only
 
 
 def test_two_gpu_data_parallel_step_matches_single_gpu():

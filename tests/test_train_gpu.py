@@ -169,3 +169,134 @@ def test_tiny_model_step_vs_float64():
     assert torch.equal(grads, g1)
     model.close()
     ctx.close()
+
+
+def test_gradient_of_concatenated_batch_is_mean_of_per_batch_gradients():
+    """The identity the data-parallel step rests on, on one GPU: the gradient
+    of the MSE loss over a batch of 2B sequences equals the mean of the
+    gradients over its two halves of B.  Per-sequence work is identical in
+    both runs (the MSE scale halves exactly), so the two sides differ only
+    by fp32 reassociation of the sums over tokens (dW, dgamma).  A step that
+    dropped or double-counted a half would be off by O(1)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    L, D, H, F, B, S, eps = 2, 256, 2, 512, 2, 256, 1e-5
+    ctx = bwpp.Ctx(0)
+    half = bwpp.TinyModel(ctx, L, D, H, F, B, S, eps, seed=3)
+    full = bwpp.TinyModel(ctx, L, D, H, F, 2 * B, S, eps, seed=3)
+    g = torch.Generator(device="cuda").manual_seed(21)
+    x = torch.randn(2 * B * S, D, device="cuda", generator=g)
+    tgt = torch.randn(2 * B * S, D, device="cuda", generator=g)
+    parts = []
+    for i in range(2):
+        rows = slice(i * B * S, (i + 1) * B * S)
+        half.step(x[rows].contiguous(), tgt[rows].contiguous(), lr=0.0)
+        gr = torch.empty(half.count, device="cuda")
+        half.get(None, gr)
+        parts.append(gr)
+    full.step(x, tgt, lr=0.0)
+    g_cat = torch.empty(full.count, device="cuda")
+    full.get(None, g_cat)
+    mean = (parts[0].double() + parts[1].double()) / 2
+    err = float(torch.linalg.norm(g_cat.double() - mean) / torch.linalg.norm(mean))
+    assert err <= 1e-4, err
+    # and one SGD step on the full batch moves the weights by lr * that mean
+    p0 = torch.empty(full.count, device="cuda")
+    full.get(p0, None)
+    full.step(x, tgt, lr=0.1)
+    p1 = torch.empty(full.count, device="cuda")
+    full.get(p1, None)
+    upd = (p1 - p0).double()
+    err = float(torch.linalg.norm(upd + 0.1 * mean) / torch.linalg.norm(0.1 * mean))
+    assert err <= 1e-4, err
+    half.close()
+    full.close()
+    ctx.close()
+
+
+def _ref_attention_dev(q, k, v, scale):
+    s = (q @ k.transpose(-1, -2)) * scale
+    S = s.shape[-1]
+    s = s.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool, device=s.device), 1), float("-inf"))
+    return torch.softmax(s, -1) @ v
+
+
+def ref_model_grads_chunked(flat, x, tgt, L, D, H, F, B, S, eps, chunk):
+    """float64 restatement of the step (same bf16 rounding points as
+    ref_model_step) on the GPU, over `chunk` sequences at a time: the loss is
+    the mean over all B sequences, so each chunk's backward adds its share of
+    the parameter gradient; returns (loss, d params, d x)."""
+    params = flat.clone().requires_grad_(True)
+    n_total = float(B * S * D)
+    scale = 1.0 / math.sqrt(128)
+    loss = 0.0
+    dx = torch.empty_like(x)
+
+    def rms(u, gam):
+        return u * torch.rsqrt((u * u).mean(-1, keepdim=True) + eps) * gam
+
+    for b0 in range(0, B, chunk):
+        cb = min(chunk, B - b0)
+        rows = slice(b0 * S, (b0 + cb) * S)
+        xb = x[rows].clone().requires_grad_(True)
+        P = split_params(params, L, D, F)
+        h = xb
+        for p in P:
+            w = {k_: st_bf16(v_) if v_.dim() == 2 else v_ for k_, v_ in p.items()}
+            n1 = st_bf16(rms(h, w["g1"]))
+            qkv = st_bf16(n1 @ w["wqkv"])
+            q, k, v = (heads(qkv[:, i * D:(i + 1) * D], cb, S, H) for i in range(3))
+            o = st_bf16(_ref_attention_dev(q, k, v, scale).permute(0, 2, 1, 3).reshape(cb * S, D))
+            h = h + o @ w["wo"]
+            n2 = st_bf16(rms(h, w["g2"]))
+            gu = st_bf16(n2 @ w["w13"])
+            a = st_bf16(torch.nn.functional.silu(gu[:, :F]) * gu[:, F:])
+            h = h + a @ w["w2"]
+        part = ((h - tgt[rows]) ** 2).sum() / n_total
+        part.backward()
+        loss += float(part.detach())
+        dx[rows] = xb.grad
+        del h, part, xb
+    return loss, params.grad, dx
+
+
+def test_tiny_model_step_config5_shape_vs_float64():
+    """configs[4] at its own shape (2 layers, d_model 2048, 16 x 128 heads,
+    causal, gated MLP 5632, seq 2048, batch 16): the loss, every layer's
+    weight gradients, the norm-gain gradients and 40 sampled rows of
+    d loss / d x against the float64 restatement (run on the GPU in chunks
+    of 4 sequences).  Tolerances as at the reduced shape."""
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    L, D, H, F, B, S, eps = 2, 2048, 16, 5632, 16, 2048, 1e-5
+    ctx = bwpp.Ctx(0)
+    model = bwpp.TinyModel(ctx, L, D, H, F, B, S, eps, seed=1)
+    g = torch.Generator(device="cuda").manual_seed(5000)
+    x = torch.randn(B * S, D, device="cuda", generator=g)
+    tgt = torch.randn(B * S, D, device="cuda", generator=g)
+    params = torch.empty(model.count, device="cuda")
+    grads = torch.empty(model.count, device="cuda")
+    dx = torch.empty(B * S, D, device="cuda")
+    loss = torch.empty(1, device="cuda")
+    model.get(params, None)
+    model.step(x, tgt, lr=0.0, loss_out=loss)
+    model.get(None, grads)
+    model.input_grad(dx)
+    model.close()
+    ctx.close()
+    rloss, rgrad, rdx = ref_model_grads_chunked(params.double(), x.double(), tgt.double(),
+                                                L, D, H, F, B, S, eps, chunk=4)
+    assert abs(float(loss) - rloss) <= 2e-3 * abs(rloss), (float(loss), rloss)
+    gp = split_params(grads.double(), L, D, F)
+    rp = split_params(rgrad, L, D, F)
+    for l in range(L):
+        for name in gp[l]:
+            a, b = gp[l][name], rp[l][name]
+            err = float(torch.linalg.norm(a - b) / torch.linalg.norm(b))
+            assert err <= 3e-2, (l, name, err)
+    rows = torch.tensor(sorted({0, 1, S - 1, S, B * S - 1} |
+                               set(np.random.default_rng(9).integers(0, B * S, 35).tolist())),
+                        device="cuda")
+    a, b = dx[rows].double(), rdx[rows]
+    err = float(torch.linalg.norm(a - b) / torch.linalg.norm(b))
+    assert err <= 3e-2, err
