@@ -91,7 +91,10 @@ struct GemmEpi {
   const uint16_t *glu;
   uint16_t *glu_up_out;
   uint32_t ldglu, glu_F;
-};
+  // 1: the residual operand multiplies instead of adding (the gate of a
+  // SwiGLU: silu(A B + bias) * R)
+  int res_mul;
+  };
 
 // Work of a launch, handed out round-robin to `workers` workers (CTA pairs,
 // or CTAs): worker w takes items w, w + workers, w + 2 workers, ...
@@ -671,14 +674,19 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                   for (int e = 0; e < 4; ++e) {
                     const uint16_t lo = (uint16_t)(w[e] & 0xFFFFu), hi = (uint16_t)(w[e] >> 16);
-                    v[8 * j + 2 * e] += f16 ? load16<true>(lo) : load16<false>(lo);
-                    v[8 * j + 2 * e + 1] += f16 ? load16<true>(hi) : load16<false>(hi);
+                    const float r0 = f16 ? load16<true>(lo) : load16<false>(lo);
+                    const float r1 = f16 ? load16<true>(hi) : load16<false>(hi);
+                    v[8 * j + 2 * e] = epi.res_mul ? v[8 * j + 2 * e] * r0 : v[8 * j + 2 * e] + r0;
+                    v[8 * j + 2 * e + 1] = epi.res_mul ? v[8 * j + 2 * e + 1] * r1 : v[8 * j + 2 * e + 1] + r1;
                   }
                 }
               } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                  if (cs + j < N) v[j] += f16 ? load16<true>(rr[j]) : load16<false>(rr[j]);
+                  if (cs + j < N) {
+                    const float r = f16 ? load16<true>(rr[j]) : load16<false>(rr[j]);
+                    v[j] = epi.res_mul ? v[j] * r : v[j] + r;
+                  }
               }
             } else if (epi.residual && my_row < M) {
               const float *rr = static_cast<const float *>(epi.residual) + (size_t)my_row * epi.ldr + cs;
@@ -687,15 +695,22 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                   const float4 t = *reinterpret_cast<const float4 *>(rr + 4 * j);
-                  v[4 * j] += t.x;
-                  v[4 * j + 1] += t.y;
-                  v[4 * j + 2] += t.z;
-                  v[4 * j + 3] += t.w;
+                  if (epi.res_mul) {
+                    v[4 * j] *= t.x;
+                    v[4 * j + 1] *= t.y;
+                    v[4 * j + 2] *= t.z;
+                    v[4 * j + 3] *= t.w;
+                  } else {
+                    v[4 * j] += t.x;
+                    v[4 * j + 1] += t.y;
+                    v[4 * j + 2] += t.z;
+                    v[4 * j + 3] += t.w;
+                  }
                 }
               } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                  if (cs + j < N) v[j] += rr[j];
+                  if (cs + j < N) v[j] = epi.res_mul ? v[j] * rr[j] : v[j] + rr[j];
               }
             }
             if (out16) {
@@ -784,8 +799,9 @@ __global__ void gemm_simt_kernel(const uint16_t *__restrict__ a,
     if (epi.residual) {
       const size_t ri = (size_t)row * epi.ldr + col;
       const uint16_t *r16 = static_cast<const uint16_t *>(epi.residual);
-      acc += epi.res16 == 0 ? static_cast<const float *>(epi.residual)[ri]
-             : epi.res16 == 2 ? load16<true>(r16[ri]) : load16<false>(r16[ri]);
+      const float r = epi.res16 == 0 ? static_cast<const float *>(epi.residual)[ri]
+                      : epi.res16 == 2 ? load16<true>(r16[ri]) : load16<false>(r16[ri]);
+      acc = epi.res_mul ? acc * r : acc + r;
     }
     if (epi.out_bf16) {
       const uint32_t w = epi.out_f16 ? pack2_16<true>(acc, 0.0f) : pack2_16<false>(acc, 0.0f);
@@ -973,7 +989,8 @@ int launch_tc_any(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb
 // step).  a_mn / b_mn select the operand layouts described at the top;
 // ab_f16 = 1 takes f16 A and B (else bf16); out_bf16 = 1 writes 16-bit C,
 // f16 when out_f16 = 1 (else bf16); out_bf16 = 0 writes fp32 C.  The
-// residual is fp32 (res16 = 0), bf16 (1) or f16 (2); it may alias C.
+// residual is fp32 (res16 = 0), bf16 (1) or f16 (2), added, or with 4 set in
+// res16 multiplied (SwiGLU gate); it may alias C.
 int bwpp_gemm_launch_dt(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t lda,
                         const uint16_t *b, int b_mn, uint32_t ldb, void *c,
                         uint32_t ldc, uint32_t M, uint32_t N, uint32_t K,
@@ -981,7 +998,10 @@ int bwpp_gemm_launch_dt(BwppCudaCtx *ctx, const uint16_t *a, int a_mn, uint32_t 
                         uint32_t ldr, int out_bf16, int force_simt, int ab_f16,
                         int out_f16, int res16) {
   if (M == 0 || N == 0) return BWPP_CUDA_OK;
-  GemmEpi epi{bias, residual, ldr, silu ? 1 : 0, out_bf16 ? 1 : 0, out_f16 ? 1 : 0, res16};
+  // res16: residual element type in bits 0-1 (0 fp32, 1 bf16, 2 f16); bit 2
+  // makes the residual a multiplier
+  GemmEpi epi{bias, residual, ldr, silu ? 1 : 0, out_bf16 ? 1 : 0, out_f16 ? 1 : 0, res16 & 3};
+  epi.res_mul = (res16 >> 2) & 1;
   const uint32_t out_es = out_bf16 ? 2 : 4;
   const bool tc_ok = !force_simt && K > 0 && al16(a) && al16(b) && al16(c) &&
                      (lda % 8) == 0 && (ldb % 8) == 0 && ((ldc * out_es) % 16) == 0 &&

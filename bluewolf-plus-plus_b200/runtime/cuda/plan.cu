@@ -67,6 +67,10 @@ int bwpp_plan_reduce_sum(BwppCudaCtx *ctx, int dt, const void *x, void *o, uint3
                          int axis);
 int bwpp_plan_transpose(BwppCudaCtx *ctx, int dt, const void *x, void *o, uint32_t batch,
                         uint32_t R, uint32_t C);
+int bwpp_plan_swiglu(BwppCudaCtx *ctx, int dt, const void *a, const void *b, void *o, size_t n);
+int bwpp_plan_add_rmsnorm(BwppCudaCtx *ctx, int dt, const void *a, const void *b,
+                          const void *gamma, const void *beta, void *h, void *y, uint32_t R,
+                          uint32_t C, float eps);
 
 namespace {
 
@@ -109,7 +113,7 @@ struct Node {
 
 enum Kind {
   K_GEMM, K_ATTN, K_SOFTMAX, K_RMSNORM, K_UNARY, K_BINARY, K_TRANSPOSE, K_SILU_GRAD,
-  K_SOFTMAX_GRAD, K_RMSNORM_GRAD, K_REDUCE
+  K_SOFTMAX_GRAD, K_RMSNORM_GRAD, K_REDUCE, K_SWIGLU, K_ADD_RMSNORM
 };
 
 struct Step {
@@ -117,6 +121,8 @@ struct Step {
   int pos = -1;                         // node position it runs at
   int a = -1, b = -1, c = -1, out = -1; // value ids
   int a_t = 0, b_t = 0, bias = -1, silu = 0;  // GEMM: operand read transposed
+  int res_mul = 0;                      // GEMM: c multiplies (SwiGLU gate) instead of adding
+  int d = -1, e = -1, out2 = -1;        // add+rmsnorm: gamma, beta, the stored sum (or -1)
   int op = 0, bmode = 0, axis = 1;
   size_t bias_off = 0;                  // fp32 bias scratch offset
   std::string what;
@@ -536,8 +542,28 @@ struct BwppCudaPlan {
               st.what += " +silu";
             }
           }
+          // SwiGLU gate: mul(silu(.), U) with U of the output's full shape
+          // multiplies in the epilogue (the spec's `swiglu` pattern)
+          if (st.silu && vals[cur].uses.size() == 1 && !vals[cur].output) {
+            const int mp = vals[cur].uses[0];
+            Node &Mu = nodes[mp];
+            if (Mu.op == "mul" && Mu.in.size() == 2 && !Mu.fused && Mu.in[0] != Mu.in[1]) {
+              const int other = Mu.in[0] == cur ? Mu.in[1] : Mu.in[0];
+              const Val &ov = vals[other];
+              if (ov.numel() == vals[cur].numel() && ov.last() == N && ov.dtype == vals[cur].dtype &&
+                  safe_to_defer({st.a, st.b, st.bias, other}, i, mp, {i, last, mp})) {
+                Mu.fused = true;
+                vals[cur].live = false;
+                cur = Mu.out;
+                last = mp;
+                st.c = other;
+                st.res_mul = 1;
+                st.what += " +swiglu";
+              }
+            }
+          }
           // residual: add(., R) with R of the output's full shape, added last
-          if (vals[cur].uses.size() == 1 && !vals[cur].output) {
+          if (!st.res_mul && vals[cur].uses.size() == 1 && !vals[cur].output) {
             const int rp = vals[cur].uses[0];
             Node &R = nodes[rp];
             if (R.op == "add" && R.in.size() == 2 && !R.fused && R.in[0] != R.in[1]) {
@@ -571,6 +597,27 @@ struct BwppCudaPlan {
         st.what = "rmsnorm";
       } else if (op == "silu") {
         st.kind = K_UNARY; st.a = n.in[0]; st.op = 1; st.what = "silu";
+        // swiglu: mul(silu(x), y) of one shape and dtype -> one pass
+        const int so = n.out;
+        if (fuse && vals[so].uses.size() == 1 && !vals[so].output) {
+          const int mp = vals[so].uses[0];
+          Node &Mu = nodes[mp];
+          if (Mu.op == "mul" && Mu.in.size() == 2 && !Mu.fused && Mu.in[0] != Mu.in[1]) {
+            const int other = Mu.in[0] == so ? Mu.in[1] : Mu.in[0];
+            const Val &xv = vals[n.in[0]], &ov = vals[other];
+            if (ov.numel() == vals[so].numel() && xv.numel() == ov.numel() &&
+                xv.dtype == ov.dtype && ov.dtype == vals[Mu.out].dtype &&
+                vals[so].dtype == xv.dtype && safe_to_defer({n.in[0], other}, i, mp, {i, mp})) {
+              Mu.fused = true;
+              vals[so].live = false;
+              st.kind = K_SWIGLU;
+              st.b = other;
+              st.out = Mu.out;
+              st.pos = mp;
+              st.what = "swiglu (fused silu, mul)";
+            }
+          }
+        }
       } else if (op == "reshape") {
         st.kind = K_UNARY; st.a = n.in[0]; st.op = 0; st.what = "reshape";
       } else if (op == "add" || op == "sub" || op == "mul" || op == "div") {
@@ -579,6 +626,41 @@ struct BwppCudaPlan {
         st.b = n.in.size() > 1 ? n.in[1] : n.in[0];
         st.op = op == "add" ? 0 : op == "sub" ? 1 : op == "mul" ? 2 : 3;
         st.what = op;
+        // residual + norm: rmsnorm(add(a, b)) with a, b of one shape runs as
+        // one row kernel at the norm's place; the sum is stored only when
+        // something besides the norm reads it (all such reads come after)
+        const int h = n.out;
+        int rp = -1;
+        bool later = true;
+        for (int u : vals[h].uses) {
+          if (nodes[u].op == "rmsnorm" && !nodes[u].fused && nodes[u].in[0] == h && rp < 0) rp = u;
+        }
+        for (int u : vals[h].uses)
+          if (u != rp && u <= rp) later = false;
+        if (fuse && op == "add" && n.in.size() == 2 && rp > i && later) {
+          const Node &Rn = nodes[rp];
+          const Val &av = vals[n.in[0]], &bv = vals[n.in[1]];
+          const int gm = Rn.in.size() > 1 ? Rn.in[1] : -1, bt = Rn.in.size() > 2 ? Rn.in[2] : -1;
+          const int C = (int)vals[h].last();
+          bool ok = av.numel() == bv.numel() && av.numel() == vals[h].numel() &&
+                    av.dtype == bv.dtype && av.dtype == vals[h].dtype &&
+                    vals[Rn.out].dtype == av.dtype;
+          for (int g : {gm, bt})
+            ok = ok && (g < 0 || (vals[g].numel() == C && vals[g].dtype == av.dtype));
+          if (ok && safe_to_defer({n.in[0], n.in[1], gm, bt}, i, rp, {i, rp})) {
+            nodes[rp].fused = true;
+            const bool keep_h = vals[h].output || vals[h].uses.size() > 1;
+            if (!keep_h) vals[h].live = false;
+            st.kind = K_ADD_RMSNORM;
+            st.d = gm;
+            st.e = bt;
+            st.out = Rn.out;
+            st.out2 = keep_h ? h : -1;
+            st.pos = rp;
+            st.what = keep_h ? "add+rmsnorm (fused residual add and norm, sum stored)"
+                             : "add+rmsnorm (fused residual add and norm)";
+          }
+        }
       } else if (op == "broadcast") {
         st.kind = K_BINARY; st.a = n.in[0]; st.b = n.in[0]; st.op = 4; st.what = "broadcast";
       } else if (op == "silu_grad") {
@@ -604,9 +686,10 @@ struct BwppCudaPlan {
     std::vector<char> need(vals.size(), 0), keep(steps.size(), 0);
     for (int i = (int)steps.size() - 1; i >= 0; --i) {
       const Step &st = steps[i];
-      if (!vals[st.out].output && !need[st.out]) continue;
+      const bool want2 = st.out2 >= 0 && (vals[st.out2].output || need[st.out2]);
+      if (!vals[st.out].output && !need[st.out] && !want2) continue;
       keep[i] = 1;
-      for (int x : {st.a, st.b, st.c, st.bias})
+      for (int x : {st.a, st.b, st.c, st.bias, st.d, st.e})
         if (x >= 0) need[x] = 1;
     }
     std::vector<Step> kept;
@@ -615,6 +698,7 @@ struct BwppCudaPlan {
         kept.push_back(steps[i]);
       } else {
         vals[steps[i].out].live = false;
+        if (steps[i].out2 >= 0) vals[steps[i].out2].live = false;
         nodes[steps[i].pos].fused = true;
       }
     }
@@ -797,7 +881,8 @@ struct BwppCudaPlan {
         const int64_t a_b = (A.numel() / (M * K) > 1) ? M * K : 0;
         const int64_t b_b = (B.numel() / (K * N) > 1) ? K * N : 0;
         const Val *R = st.c >= 0 ? &vals[st.c] : nullptr;
-        const int res16 = !R ? 0 : R->dtype == DT_F16 ? 2 : R->dtype == DT_BF16 ? 1 : 0;
+        const int res16 = (!R ? 0 : R->dtype == DT_F16 ? 2 : R->dtype == DT_BF16 ? 1 : 0) |
+                          (st.res_mul ? 4 : 0);
         for (int64_t i = 0; !rc && i < batch; ++i) {
           const void *res = R ? (const uint8_t *)R->ptr + (size_t)(i * M * N) * dt_size(R->dtype)
                               : nullptr;
@@ -896,6 +981,16 @@ struct BwppCudaPlan {
       case K_RMSNORM_GRAD:
         rc = bwpp_plan_rmsnorm_grad(c, o.dtype, vals[st.a].ptr, vals[st.b].ptr, vals[st.c].ptr, out,
                                     (uint32_t)o.rows(), (uint32_t)o.last(), eps);
+        ++launches;
+        break;
+      case K_SWIGLU:
+        rc = bwpp_plan_swiglu(c, o.dtype, vals[st.a].ptr, vals[st.b].ptr, out, o.numel());
+        ++launches;
+        break;
+      case K_ADD_RMSNORM:
+        rc = bwpp_plan_add_rmsnorm(c, o.dtype, vals[st.a].ptr, vals[st.b].ptr, P(st.d), P(st.e),
+                                   st.out2 >= 0 ? vals[st.out2].ptr : nullptr, out,
+                                   (uint32_t)o.rows(), (uint32_t)o.last(), eps);
         ++launches;
         break;
       case K_REDUCE: {

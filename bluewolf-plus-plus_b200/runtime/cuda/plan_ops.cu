@@ -11,6 +11,10 @@
 //            for dX), rmsnorm / softmax for f32 or bf16 storage
 //   reduce   reduce_sum over axis 0 or 1; broadcast back
 //   layout   batched 2-D transpose
+//   fused    swiglu: silu(a) * b in one pass (the `swiglu` pattern of
+//            spec/llm-primitives.md:17-22 when a is not a GEMM output);
+//            residual + norm: h = a + b and y = rmsnorm(h) per row in one
+//            kernel (h stored only when something else reads it)
 #include <math.h>
 
 #include "bwpp_cuda_internal.cuh"
@@ -234,6 +238,59 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// o = silu(a) * b, elementwise; a, b, o dense, same shape
+template <int DT>
+__global__ void swiglu_kernel(const void *a_, const void *b_, void *o_, size_t n) {
+  using S = St<DT>;
+  const auto *a = static_cast<const typename S::T *>(a_);
+  const auto *b = static_cast<const typename S::T *>(b_);
+  auto *o = static_cast<typename S::T *>(o_);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    S::st(o, i, silu1(S::ld(a, i)) * S::ld(b, i));
+}
+
+// Residual + RMSNorm, one CTA per row (grid-stride): h = a + b rounded to the
+// storage type (as the unfused add would store it), y = rmsnorm(h) * gamma +
+// beta; h is written when h_out != NULL.  The row's sum of squares is taken
+// over the rounded h, as the unfused add -> rmsnorm would read it.
+template <int DT>
+__global__ void __launch_bounds__(kThreads)
+    add_rmsnorm_kernel(const void *a_, const void *b_, const void *gamma_, const void *beta_,
+                       void *h_, void *y_, uint32_t R, uint32_t C, float eps) {
+  using S = St<DT>;
+  const auto *a = static_cast<const typename S::T *>(a_);
+  const auto *b = static_cast<const typename S::T *>(b_);
+  const auto *gm = static_cast<const typename S::T *>(gamma_);
+  const auto *bt = static_cast<const typename S::T *>(beta_);
+  auto *h = static_cast<typename S::T *>(h_);
+  auto *y = static_cast<typename S::T *>(y_);
+  __shared__ float sv[32];
+  // the rounded sum, as the storage type holds it
+  auto hsum = [&](size_t i) {
+    typename S::T t[1];
+    S::st(t, 0, S::ld(a, i) + S::ld(b, i));
+    return S::ld(t, 0);
+  };
+  for (uint32_t r = blockIdx.x; r < R; r += gridDim.x) {
+    const size_t o = (size_t)r * C;
+    float ss = 0.0f;
+    for (uint32_t c = threadIdx.x; c < C; c += kThreads) {
+      const float t = hsum(o + c);
+      ss = fmaf(t, t, ss);
+      if (h) S::st(h, o + c, t);
+    }
+    ss = block_sum(ss, sv);
+    const float inv = rsqrtf(ss / (float)C + eps);
+    // each thread re-reads only the elements it wrote (h may alias a or b)
+    for (uint32_t c = threadIdx.x; c < C; c += kThreads) {
+      const float g = gm ? S::ld(gm, c) : 1.0f, bb = bt ? S::ld(bt, c) : 0.0f;
+      const float t = h ? S::ld(h, o + c) : hsum(o + c);
+      S::st(y, o + c, t * inv * g + bb);
+    }
+  }
+}
+
 // axis 1: out[r] = sum_c x[r, c] (CTA per row); axis 0: out[c] = sum_r x[r, c]
 // (thread per column, rows in order: deterministic)
 template <int DT>
@@ -399,5 +456,24 @@ int bwpp_plan_transpose(BwppCudaCtx *ctx, int dt, const void *x, void *o, uint32
   dim3 grid((C + 31) / 32, (R + 31) / 32, batch);
   BWPP_PLAN_DT(dt, transpose_kernel, <<<grid, dim3(32, 8), 0, ctx->stream>>>(x, o, R, C));
   BWPP_LAUNCH_CHECK(ctx, "plan transpose");
+  return BWPP_CUDA_OK;
+}
+
+int bwpp_plan_swiglu(BwppCudaCtx *ctx, int dt, const void *a, const void *b, void *o, size_t n) {
+  if (n == 0) return BWPP_CUDA_OK;
+  const uint32_t g = grid_flat(ctx, n);
+  BWPP_PLAN_DT(dt, swiglu_kernel, <<<g, 256, 0, ctx->stream>>>(a, b, o, n));
+  BWPP_LAUNCH_CHECK(ctx, "plan swiglu");
+  return BWPP_CUDA_OK;
+}
+
+int bwpp_plan_add_rmsnorm(BwppCudaCtx *ctx, int dt, const void *a, const void *b,
+                          const void *gamma, const void *beta, void *h, void *y, uint32_t R,
+                          uint32_t C, float eps) {
+  if (!R || !C) return BWPP_CUDA_OK;
+  BWPP_PLAN_DT(dt, add_rmsnorm_kernel,
+               <<<grid_rows(ctx, R), kThreads, 0, ctx->stream>>>(a, b, gamma, beta, h, y, R, C,
+                                                                 eps));
+  BWPP_LAUNCH_CHECK(ctx, "plan add_rmsnorm");
   return BWPP_CUDA_OK;
 }

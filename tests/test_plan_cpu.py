@@ -90,3 +90,18 @@ def test_errors_are_reported():
     with pytest.raises(RuntimeError, match="inner dims"):
         lower("matmul", dict(M=8, K=16, N=32)).close() or bwpp.Plan(
             None, dump("matmul").replace("[K,N]", "[N,K]"), None, dict(M=8, K=16, N=32))
+
+
+def test_swiglu_and_residual_norm_patterns():
+    # spec/llm-primitives.md:17-22: swiglu (silu(x) * y) and residual + norm
+    assert kinds(lower("swiglu_ffn", dict(T=128, D=256, H=512))) == \
+        ["gemm", "gemm +silu +swiglu", "gemm"]
+    assert kinds(lower("swiglu_gate", dict(T=128, D=256))) == ["add", "swiglu (fused silu, mul)"]
+    assert kinds(lower("residual_norm", dict(T=64, D=256))) == \
+        ["add+rmsnorm (fused residual add and norm)"]
+    # the sum is read again after the norm: stored, in the attention output's buffer
+    k = kinds(lower("attn_residual_norm", dict(T=256, D=128)))
+    assert k == ["attention (fused transpose, matmul, softmax, matmul)",
+                 "add+rmsnorm (fused residual add and norm, sum stored)", "add"]
+    # unfused, each op is its own step
+    assert len(lower("swiglu_ffn", dict(T=128, D=256, H=512), options="fuse=0").steps()) == 5

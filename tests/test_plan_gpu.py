@@ -243,3 +243,80 @@ def test_graphs_in_other_storage_types(ctx, dtype):
     q, k, v = (f32(half(rng, Bh, H, T, D, scale=0.3)) for _ in range(3))
     out = run_dt("attention", dict(B=Bh, H=H, T=T, D=D), {"q": q, "k": k, "v": v})
     assert rel_fro(out, O.attention_bhsd(rb(q), rb(k), rb(v), 1.0, 0)) <= tol
+
+
+# ---- the swiglu and residual + norm patterns (spec/llm-primitives.md:17-22) --
+
+def _silu(x):
+    return x / (1 + np.exp(-x))
+
+
+@pytest.mark.parametrize("fuse", [1, 0])
+def test_swiglu_ffn_gate_in_the_gemm_epilogue(ctx, fuse):
+    """silu(x W1) * (x W3) then W2: the gate multiplies in the W1 GEMM's
+    epilogue (3 launches fused, 5 unfused)."""
+    T, D, H = 200, 256, 384
+    rng = np.random.default_rng(31)
+    x = half(rng, T, D, scale=0.5)
+    w1, w3 = half(rng, D, H, scale=0.1), half(rng, D, H, scale=0.1)
+    w2 = half(rng, H, D, scale=0.1)
+    outs, launches = run(ctx, "swiglu_ffn", dict(T=T, D=D, H=H), {"x": x, "w1": w1, "w3": w3, "w2": w2},
+                         options=f"fuse={fuse}")
+    g = O.matmul(f32(x), f32(w1))
+    u = O.matmul(f32(x), f32(w3)).astype(np.float16)  # the graph stores u as f16
+    a = (_silu(g) * f32(u)).astype(np.float16)
+    ref = O.matmul(f32(a), f32(w2))
+    (out,) = outs.values()
+    assert rel_fro(out, ref) <= 3e-3
+    assert launches == (3 if fuse else 5)
+
+
+@pytest.mark.parametrize("fuse", [1, 0])
+def test_swiglu_gate_standalone(ctx, fuse):
+    """mul(silu(add(x, r)), y): the silu and mul run as one pass."""
+    T, D = 300, 520
+    rng = np.random.default_rng(32)
+    x, r, y = half(rng, T, D), half(rng, T, D), half(rng, T, D)
+    outs, launches = run(ctx, "swiglu_gate", dict(T=T, D=D), {"x": x, "r": r, "y": y},
+                         options=f"fuse={fuse}")
+    s = (f32(x) + f32(r)).astype(np.float16)
+    ref = _silu(f32(s)) * f32(y)
+    (out,) = outs.values()
+    assert rel_fro(out, ref) <= 2e-3
+    assert launches == (2 if fuse else 3)
+
+
+@pytest.mark.parametrize("fuse", [1, 0])
+@pytest.mark.parametrize("T,D", [(64, 256), (130, 1000)])
+def test_residual_norm(ctx, fuse, T, D):
+    """rmsnorm(add(x, r), g): one row kernel, the sum never stored."""
+    rng = np.random.default_rng(33 + D)
+    x, r = half(rng, T, D), half(rng, T, D)
+    g = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    outs, launches = run(ctx, "residual_norm", dict(T=T, D=D), {"x": x, "r": r, "g": g},
+                         options=f"fuse={fuse}")
+    h = (f32(x) + f32(r)).astype(np.float16)
+    ref = O.rmsnorm(f32(h), f32(g), None, 1e-5)
+    (out,) = outs.values()
+    assert rel_fro(out, ref) <= 2e-3
+    assert launches == (1 if fuse else 2)
+
+
+@pytest.mark.parametrize("fuse", [1, 0])
+def test_attention_residual_norm_sum_stored(ctx, fuse):
+    """h = x + attention(q, k, v); out = h + rmsnorm(h, g): the fused residual
+    + norm stores h (read again by the last add), in the attention output's
+    buffer as the memory plan has it."""
+    T, D = 256, 128
+    rng = np.random.default_rng(34)
+    x, q, k, v = (half(rng, T, D, scale=0.3) for _ in range(4))
+    g = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    outs, launches = run(ctx, "attn_residual_norm", dict(T=T, D=D),
+                         {"x": x, "q": q, "k": k, "v": v, "g": g}, options=f"fuse={fuse}")
+    a = O.attention_bhsd(f32(q)[None, None], f32(k)[None, None], f32(v)[None, None], 1.0, 0)[0, 0]
+    h = (f32(x) + a.astype(np.float16)).astype(np.float16)
+    n = O.rmsnorm(f32(h), f32(g), None, 1e-5).astype(np.float16)
+    ref = f32(h) + f32(n)
+    (out,) = outs.values()
+    assert rel_fro(out, ref) <= 1e-2
+    assert launches == (3 if fuse else 7)
