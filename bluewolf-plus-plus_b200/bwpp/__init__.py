@@ -144,6 +144,7 @@ _SIGS = {
     "bwpp_cuda_dispatch_attention_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, AttentionParams, _cp]),
     # launch-plan executor
     "bwpp_cuda_plan_create": (_i32, [_vp, _cp, _cp, _cp, _cp, C.POINTER(_vp)]),
+    "bwpp_cuda_plan_create_launch": (_i32, [_vp, _cp, _cp, C.POINTER(_vp)]),
     "bwpp_cuda_plan_last_error": (_cp, []),
     "bwpp_cuda_plan_describe": (_i32, [_vp, C.c_char_p, C.c_size_t]),
     "bwpp_cuda_plan_find": (_i32, [_vp, _cp]),
@@ -340,8 +341,10 @@ class Ctx:
 
 
 class Plan:
-    """A graph of the reference compiler (its --dot / --grad-dot dump, and
-    optionally its --mem-plan dump) lowered onto the CUDA kernels.
+    """A graph of the reference compiler lowered onto the CUDA kernels: the
+    launch plan `bwppc --target cuda --dims ...` writes (pass its text as
+    graph_dot; mem_plan and dims are then unused), or its --dot / --grad-dot
+    dump and optionally its --mem-plan dump, lowered here.
 
         plan = Plan(ctx, open("g.dot").read(), open("m.txt").read(), {"T": 128, "D": 256})
         plan.bind("x", x_tensor); ...; plan.run(); y = plan.tensor("out")
@@ -356,9 +359,15 @@ class Plan:
         self.ctx = ctx
         spec = ",".join(f"{k}={int(v)}" for k, v in (dims or {}).items())
         h = C.c_void_p()
-        rc = self.lib.bwpp_cuda_plan_create(ctx.handle if ctx is not None else None, graph_dot.encode(),
-                                            mem_plan.encode() if mem_plan else None, spec.encode(),
-                                            options.encode() if options else None, C.byref(h))
+        if graph_dot.lstrip().startswith("// BW++ CUDA launch plan"):
+            # the output of `bwppc --target cuda` (dims are bound in it)
+            rc = self.lib.bwpp_cuda_plan_create_launch(ctx.handle if ctx is not None else None,
+                                                       graph_dot.encode(),
+                                                       options.encode() if options else None, C.byref(h))
+        else:
+            rc = self.lib.bwpp_cuda_plan_create(ctx.handle if ctx is not None else None, graph_dot.encode(),
+                                                mem_plan.encode() if mem_plan else None, spec.encode(),
+                                                options.encode() if options else None, C.byref(h))
         if rc != 0:
             raise RuntimeError(f"plan_create: {status_string(rc)}: "
                                f"{self.lib.bwpp_cuda_plan_last_error().decode()}")

@@ -1,5 +1,8 @@
 // Launch-plan executor: runs a graph built by the reference compiler on the
-// B200 kernels, from the compiler's own dumps:
+// B200 kernels, either from the launch plan that `bwppc --target cuda`
+// writes (compiler/codegen_cuda.c of this package: fusion decisions, operand
+// value ids and arena offsets all made by the compiler; parse_launch below),
+// or from the compiler's own dumps, lowered here:
 //   bwppc <in.bwpp> <out.metal> --entry <fn> --dot g.dot [--mem-plan m.txt]
 //   bwppc ... --grad-dot g.dot                     (the gradient graph)
 // The graph dump (compiler/graph_ir.c:1326-1358) lists every value (name,
@@ -94,6 +97,7 @@ struct Val {
   bool live = true;             // false: fused away, never materialised
   void *ptr = nullptr;
   bool bound = false;
+  size_t off = SIZE_MAX;        // arena offset given by a launch plan
   int64_t numel() const {
     int64_t n = 1;
     for (int64_t d : dims) n *= d;
@@ -123,6 +127,7 @@ struct Step {
   int a_t = 0, b_t = 0, bias = -1, silu = 0;  // GEMM: operand read transposed
   int res_mul = 0;                      // GEMM: c multiplies (SwiGLU gate) instead of adding
   int d = -1, e = -1, out2 = -1;        // add+rmsnorm: gamma, beta, the stored sum (or -1)
+  float eps = 1e-5f;                    // rmsnorm, rmsnorm_grad, add+rmsnorm
   int op = 0, bmode = 0, axis = 1;
   size_t bias_off = 0;                  // fp32 bias scratch offset
   std::string what;
@@ -171,6 +176,8 @@ struct BwppCudaPlan {
   int mp_buffers = 0;
   float eps = 1e-5f;
   int fuse = 1;
+  bool from_launch = false;             // built from a `bwppc --target cuda` plan
+  size_t graph_bytes = 0;               // its arena bytes (graph values)
   // device memory: one allocation
   uint8_t *arena = nullptr;
   size_t arena_bytes = 0;
@@ -263,6 +270,170 @@ struct BwppCudaPlan {
       for (int x : nodes[i].in)
         if (!vals[x].input && vals[x].producer >= (int)i)
           return fail(BWPP_CUDA_ERR_ARG, "nodes are not in dependency order at n%d", nodes[i].id);
+    return BWPP_CUDA_OK;
+  }
+
+  // ---------------------------------------------------- `--target cuda` plan
+  // The lines of compiler/codegen_cuda.c: bwpp.value (id, name, dtype, bound
+  // dims, flags, buffer, arena offset), bwpp.arena (bytes) and bwpp.launch
+  // (kernel, operands, epilogue), in launch order.  Nothing is re-lowered.
+  static std::map<std::string, std::string> kv_fields(const std::string &line, size_t from) {
+    std::map<std::string, std::string> kv;
+    size_t i = from;
+    while (i < line.size()) {
+      while (i < line.size() && isspace((unsigned char)line[i])) ++i;
+      size_t j = i;
+      while (j < line.size() && !isspace((unsigned char)line[j])) ++j;
+      const std::string tok = line.substr(i, j - i);
+      const size_t eq = tok.find('=');
+      if (eq != std::string::npos) kv[tok.substr(0, eq)] = tok.substr(eq + 1);
+      i = j;
+    }
+    return kv;
+  }
+
+  static int vref(const std::string &t) {  // "v12" -> 12, else -1
+    if (t.size() < 2 || t[0] != 'v' || !isdigit((unsigned char)t[1])) return -1;
+    return atoi(t.c_str() + 1);
+  }
+
+  int parse_launch(const char *text) {
+    from_launch = true;
+    bool have_arena = false;
+    std::vector<std::string> launches;
+    const char *p = text;
+    while (*p) {
+      const char *eol = strchr(p, '\n');
+      std::string line = trim(std::string(p, eol ? eol - p : strlen(p)));
+      p = eol ? eol + 1 : p + strlen(p);
+      if (starts_with(line.c_str(), "// bwpp.value: ")) {
+        const size_t at = strlen("// bwpp.value: ");
+        const size_t sp = line.find(' ', at);
+        Val v;
+        v.id = vref(line.substr(at, sp == std::string::npos ? std::string::npos : sp - at));
+        if (v.id < 0 || v.id > (1 << 20)) return fail(BWPP_CUDA_ERR_ARG, "launch plan: bad value line %s", line.c_str());
+        auto kv = kv_fields(line, sp == std::string::npos ? line.size() : sp);
+        v.name = kv["name"];
+        v.dtype = parse_dtype(kv["dtype"]);
+        if (v.dtype < 0) return fail(BWPP_CUDA_ERR_UNSUPPORTED, "launch plan: v%d dtype", v.id);
+        for (const auto &d : split_dims(kv["dims"])) {
+          const long long n = atoll(d.c_str());
+          if (n <= 0) return fail(BWPP_CUDA_ERR_ARG, "launch plan: v%d dims", v.id);
+          v.dims.push_back(n);
+        }
+        v.known = !v.dims.empty();
+        const std::string &fl = kv["flags"];
+        v.input = fl.find("input") != std::string::npos;
+        v.output = fl.find("output") != std::string::npos;
+        v.live = v.input || kv.count("offset");
+        if (kv.count("buffer") && kv["buffer"][0] == 'b') {
+          v.buffer = atoi(kv["buffer"].c_str() + 1);
+          mp_buffers = std::max(mp_buffers, v.buffer + 1);
+        }
+        if (kv.count("offset")) v.off = (size_t)strtoull(kv["offset"].c_str(), nullptr, 10);
+        if (v.id >= (int)vals.size()) vals.resize(v.id + 1);
+        vals[v.id] = v;
+      } else if (starts_with(line.c_str(), "// bwpp.arena: bytes=")) {
+        graph_bytes = (size_t)strtoull(line.c_str() + strlen("// bwpp.arena: bytes="), nullptr, 10);
+        have_arena = true;
+      } else if (starts_with(line.c_str(), "// bwpp.launch: ")) {
+        launches.push_back(line);
+      }
+    }
+    if (vals.empty() || !have_arena)
+      return fail(BWPP_CUDA_ERR_ARG, "not a launch plan (no bwpp.value / bwpp.arena lines)");
+    for (const std::string &line : launches) {
+      const size_t at = strlen("// bwpp.launch: ");
+      char kind[32] = {0};
+      int idx = -1;
+      if (sscanf(line.c_str() + at, "%d %31s", &idx, kind) != 2)
+        return fail(BWPP_CUDA_ERR_ARG, "launch plan: bad launch line %s", line.c_str());
+      auto kv = kv_fields(line, at);
+      auto V = [&](const char *key) { return kv.count(key) ? vref(kv[key]) : -1; };
+      Step st;
+      const std::string k = kind;
+      st.out = V("out");
+      st.pos = kv.count("node") ? atoi(kv["node"].c_str() + 1) : idx;
+      if (kv.count("eps")) st.eps = (float)atof(kv["eps"].c_str());
+      if (k == "gemm") {
+        st.kind = K_GEMM;
+        st.a = V("a");
+        st.b = V("b");
+        st.a_t = kv.count("a_t") ? atoi(kv["a_t"].c_str()) : 0;
+        st.b_t = kv.count("b_t") ? atoi(kv["b_t"].c_str()) : 0;
+        st.bias = V("bias");
+        st.silu = kv.count("silu") ? atoi(kv["silu"].c_str()) : 0;
+        st.c = kv.count("gate") ? V("gate") : V("residual");
+        st.res_mul = kv.count("gate") ? 1 : 0;
+        st.what = "gemm";
+        if (st.a_t) st.what += " A^T";
+        if (st.b_t) st.what += " B^T";
+        if (st.bias >= 0) st.what += " +bias";
+        if (st.silu) st.what += " +silu";
+        if (st.c >= 0) st.what += st.res_mul ? " +swiglu" : " +residual";
+      } else if (k == "attention") {
+        st.kind = K_ATTN;
+        st.a = V("q");
+        st.b = V("k");
+        st.c = V("v");
+        if ((kv.count("scale") && atof(kv["scale"].c_str()) != 1.0) ||
+            (kv.count("causal") && atoi(kv["causal"].c_str()) != 0))
+          return fail(BWPP_CUDA_ERR_UNSUPPORTED, "launch plan: scaled / causal graph attention");
+        st.what = "attention (fused transpose, matmul, softmax, matmul)";
+      } else if (k == "softmax") {
+        st.kind = K_SOFTMAX; st.a = V("x"); st.what = "softmax";
+      } else if (k == "rmsnorm") {
+        st.kind = K_RMSNORM; st.a = V("x"); st.b = V("gamma"); st.c = V("beta"); st.what = "rmsnorm";
+      } else if (k == "add_rmsnorm") {
+        st.kind = K_ADD_RMSNORM;
+        st.a = V("a"); st.b = V("b"); st.d = V("gamma"); st.e = V("beta"); st.out2 = V("sum");
+        st.what = st.out2 >= 0 ? "add+rmsnorm (fused residual add and norm, sum stored)"
+                               : "add+rmsnorm (fused residual add and norm)";
+      } else if (k == "swiglu") {
+        st.kind = K_SWIGLU; st.a = V("x"); st.b = V("y"); st.what = "swiglu (fused silu, mul)";
+      } else if (k == "unary") {
+        st.kind = K_UNARY;
+        st.a = V("x");
+        st.op = kv["op"] == "silu" ? 1 : 0;
+        st.what = st.op ? "silu" : "reshape";
+      } else if (k == "binary") {
+        static const char *ops[] = {"add", "sub", "mul", "div", "broadcast"};
+        st.kind = K_BINARY;
+        st.a = V("a");
+        st.b = V("b");
+        st.op = -1;
+        for (int o = 0; o < 5; ++o)
+          if (kv["op"] == ops[o]) st.op = o;
+        if (st.op < 0) return fail(BWPP_CUDA_ERR_ARG, "launch plan: binary op %s", kv["op"].c_str());
+        st.what = ops[st.op];
+      } else if (k == "transpose") {
+        st.kind = K_TRANSPOSE; st.a = V("x"); st.what = "transpose";
+      } else if (k == "silu_grad") {
+        st.kind = K_SILU_GRAD; st.a = V("x"); st.b = V("dy"); st.what = "silu_grad";
+      } else if (k == "softmax_grad") {
+        st.kind = K_SOFTMAX_GRAD; st.a = V("y"); st.b = V("dy"); st.what = "softmax_grad";
+      } else if (k == "rmsnorm_grad") {
+        st.kind = K_RMSNORM_GRAD; st.a = V("x"); st.b = V("gamma"); st.c = V("dy");
+        st.what = "rmsnorm_grad";
+      } else if (k == "reduce_sum") {
+        st.kind = K_REDUCE; st.a = V("x"); st.what = "reduce_sum";
+      } else {
+        return fail(BWPP_CUDA_ERR_UNSUPPORTED, "launch plan: unknown kernel %s", kind);
+      }
+      // every operand names a known value with a bound shape
+      const int need[] = {st.out, st.a};
+      for (int x : need)
+        if (!val(x) || !vals[x].known) return fail(BWPP_CUDA_ERR_ARG, "launch plan: %s", line.c_str());
+      for (int x : {st.b, st.c, st.bias, st.d, st.e, st.out2})
+        if (x != -1 && (!val(x) || !vals[x].known))
+          return fail(BWPP_CUDA_ERR_ARG, "launch plan: %s", line.c_str());
+      if (st.pos < 0 || st.pos > (1 << 20)) return fail(BWPP_CUDA_ERR_ARG, "launch plan: node");
+      if ((int)nodes.size() <= st.pos) nodes.resize(st.pos + 1);
+      for (int x : {st.a, st.b, st.c, st.bias, st.d, st.e})
+        if (x >= 0) vals[x].uses.push_back(st.pos);
+      steps.push_back(st);
+    }
+    for (size_t i = 0; i < nodes.size(); ++i) nodes[i].id = (int)i;
     return BWPP_CUDA_OK;
   }
 
@@ -703,7 +874,14 @@ struct BwppCudaPlan {
       }
     }
     steps = kept;
-    // 4. per-step shape checks, binary broadcast modes, reduction axes, aliasing
+    for (Step &st : steps)
+      if (st.kind == K_RMSNORM || st.kind == K_RMSNORM_GRAD || st.kind == K_ADD_RMSNORM) st.eps = eps;
+    return BWPP_CUDA_OK;
+  }
+
+  // 4. per-step shape checks, binary broadcast modes, reduction axes, aliasing
+  // (both plan sources)
+  int finish() {
     for (Step &st : steps) {
       Val &o = vals[st.out];
       if (st.kind == K_BINARY) {
@@ -810,6 +988,16 @@ struct BwppCudaPlan {
         own_off[v.id] = off;
         off += own[v.id];
       }
+    if (from_launch) {
+      // the compiler laid the graph's values out; check its offsets fit
+      for (auto &v : vals) {
+        if (v.id < 0 || v.input || !v.live) continue;
+        const size_t bytes = (size_t)v.numel() * dt_size(v.dtype);
+        if (v.off == SIZE_MAX || v.off + bytes > graph_bytes || (v.off & 255))
+          return fail(BWPP_CUDA_ERR_ARG, "launch plan: v%d has no valid arena offset", v.id);
+      }
+      off = graph_bytes;
+    }
     const size_t bias_off = off;
     off += bias_total;
     scratch_off = off;
@@ -827,7 +1015,7 @@ struct BwppCudaPlan {
     }
     for (auto &v : vals) {
       if (v.id < 0 || v.input || !v.live) continue;
-      v.ptr = arena + (v.buffer >= 0 ? buf_off[v.buffer] : own_off[v.id]);
+      v.ptr = arena + (from_launch ? v.off : v.buffer >= 0 ? buf_off[v.buffer] : own_off[v.id]);
     }
     return BWPP_CUDA_OK;
   }
@@ -943,11 +1131,11 @@ struct BwppCudaPlan {
         const uint32_t R = (uint32_t)x.rows(), C = (uint32_t)x.last();
         if (x.dtype == DT_F16)
           rc = bwpp_cuda_rmsnorm_f16(c, (const uint16_t *)x.ptr, (uint16_t *)out,
-                                     (const uint16_t *)P(st.b), (const uint16_t *)P(st.c), R, C, C, eps);
+                                     (const uint16_t *)P(st.b), (const uint16_t *)P(st.c), R, C, C, st.eps);
         else if (x.dtype == DT_F32)
           rc = bwpp_cuda_rmsnorm_fwd_f32(c, (const float *)x.ptr, (float *)out, (const float *)P(st.b),
-                                         (const float *)P(st.c), R, C, C, eps);
-        else rc = bwpp_plan_rmsnorm(c, x.dtype, x.ptr, P(st.b), P(st.c), out, R, C, eps);
+                                         (const float *)P(st.c), R, C, C, st.eps);
+        else rc = bwpp_plan_rmsnorm(c, x.dtype, x.ptr, P(st.b), P(st.c), out, R, C, st.eps);
         ++launches;
         break;
       }
@@ -980,7 +1168,7 @@ struct BwppCudaPlan {
         break;
       case K_RMSNORM_GRAD:
         rc = bwpp_plan_rmsnorm_grad(c, o.dtype, vals[st.a].ptr, vals[st.b].ptr, vals[st.c].ptr, out,
-                                    (uint32_t)o.rows(), (uint32_t)o.last(), eps);
+                                    (uint32_t)o.rows(), (uint32_t)o.last(), st.eps);
         ++launches;
         break;
       case K_SWIGLU:
@@ -990,7 +1178,7 @@ struct BwppCudaPlan {
       case K_ADD_RMSNORM:
         rc = bwpp_plan_add_rmsnorm(c, o.dtype, vals[st.a].ptr, vals[st.b].ptr, P(st.d), P(st.e),
                                    st.out2 >= 0 ? vals[st.out2].ptr : nullptr, out,
-                                   (uint32_t)o.rows(), (uint32_t)o.last(), eps);
+                                   (uint32_t)o.rows(), (uint32_t)o.last(), st.eps);
         ++launches;
         break;
       case K_REDUCE: {
@@ -1043,6 +1231,32 @@ int bwpp_cuda_plan_create(BwppCudaCtx *ctx, const char *graph_dot, const char *m
   for (auto &n : p->nodes)
     if (!rc) rc = p->infer(n);
   if (!rc) rc = p->lower();
+  if (!rc) rc = p->finish();
+  if (!rc) rc = p->allocate();
+  if (rc) {
+    if (p->arena) cudaFree(p->arena);
+    delete p;
+    return rc;
+  }
+  tl_err[0] = 0;
+  *out = p;
+  return BWPP_CUDA_OK;
+}
+
+int bwpp_cuda_plan_create_launch(BwppCudaCtx *ctx, const char *launch_plan, const char *options,
+                                 BwppCudaPlan **out) {
+  if (!out || !launch_plan) return BWPP_CUDA_ERR_ARG;
+  *out = nullptr;
+  if (ctx) {
+    int rc = bwpp_ctx_enter(ctx);
+    if (rc) return rc;
+  }
+  BwppCudaPlan *p = new (std::nothrow) BwppCudaPlan();
+  if (!p) return BWPP_CUDA_ERR_NOMEM;
+  p->ctx = ctx;
+  int rc = p->parse_options(options);
+  if (!rc) rc = p->parse_launch(launch_plan);
+  if (!rc) rc = p->finish();
   if (!rc) rc = p->allocate();
   if (rc) {
     if (p->arena) cudaFree(p->arena);

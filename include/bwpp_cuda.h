@@ -512,7 +512,9 @@ int bwpp_cuda_dispatch_attention_f16(BwppCudaCtx *ctx, const uint16_t *q, const 
                                      BwppCudaAttentionParams params, const char *source);
 
 /* ---- 5. launch-plan executor ----------------------------------------------
- * Runs a graph built by the reference compiler from its own dumps:
+ * Runs a graph built by the reference compiler, from the launch plan that
+ * `bwppc --target cuda` writes (bwpp_cuda_plan_create_launch below) or from
+ * the compiler's own dumps:
  *   bwppc in.bwpp out.metal --entry fn --dot graph.dot [--mem-plan plan.txt]
  *   (or --grad-dot for the gradient graph).
  * graph_dot: the text of the graph dump (compiler/graph_ir.c:1326-1358);
@@ -522,12 +524,24 @@ int bwpp_cuda_dispatch_attention_f16(BwppCudaCtx *ctx, const uint16_t *q, const 
  * With ctx == NULL the plan is parsed and lowered only (no device memory):
  * bwpp_cuda_plan_describe shows the lowered steps.  Fusions: matmul ->
  * softmax attention patterns into the attention kernel, transposes into GEMM
- * operand layouts, matmul -> add(bias by dataflow) -> silu into the GEMM
- * epilogue.  No counterpart in the reference (it has no executor for its
- * graphs); the op vocabulary is compiler/include/graph_ir.h:39-57. */
+ * operand layouts, matmul -> add(bias by dataflow) -> silu -> mul(gate) or
+ * add(residual) into the GEMM epilogue, mul(silu(x), y) into one swiglu pass,
+ * rmsnorm(add(a, b)) into one residual + norm pass.  No counterpart in the
+ * reference (it has no executor for its graphs); the op vocabulary is
+ * compiler/include/graph_ir.h:39-57. */
 typedef struct BwppCudaPlan BwppCudaPlan;
 int bwpp_cuda_plan_create(BwppCudaCtx *ctx, const char *graph_dot, const char *mem_plan,
                           const char *dims, const char *options, BwppCudaPlan **out);
+/* The same executor on the text of a launch plan written by
+ *   bwppc in.bwpp out.plan --entry fn --target cuda --dims T=128,D=256
+ * (this package's compiler/codegen_cuda.c, selected by the --target flag the
+ * patch compiler/main_target_cuda.patch adds to compiler/main.c:49-85,186).
+ * The plan carries the compiler's fusion decisions, operand value ids, bound
+ * shapes and arena offsets (one cudaMalloc, compiler/mem_plan.c's buffers
+ * sized in bytes); nothing is re-lowered.  options: NULL or "fuse=1" (eps
+ * comes from each launch line). */
+int bwpp_cuda_plan_create_launch(BwppCudaCtx *ctx, const char *launch_plan, const char *options,
+                                 BwppCudaPlan **out);
 /* Message of the last failed bwpp_cuda_plan_create on this thread. */
 const char *bwpp_cuda_plan_last_error(void);
 /* Writes the lowered steps as text; returns the bytes needed (incl. NUL). */

@@ -111,15 +111,17 @@ def _rank_distinct(rank, world, port, q):
         cat.step(torch.cat([b[0] for b in batches]), torch.cat([b[1] for b in batches]), lr=0.1)
         p_cat = torch.empty(n, device="cuda")
         cat.get(p_cat, None)
-        d_dp, d_cat = (p_dp - p0).double(), (p_cat - p0).double()
-        step_err = float(torch.linalg.norm(d_dp - d_cat) / torch.linalg.norm(d_cat))
+        # weights of magnitude ~0.1: one fp32 rounding is ~7e-9, far below
+        # what a wrong gradient sum would move them
+        step_err = float((p_dp - p_cat).abs().max())
+        moved = float((p_dp - p0).abs().max())
         ctx.sync()
         lib.bwpp_cuda_comm_destroy(comm)
         for m in (dp, solo, cat):
             m.close()
         ctx.close()
         dist.destroy_process_group()
-        q.put((rank, (ar_err, own_err, step_err)))
+        q.put((rank, (ar_err, own_err, step_err, moved)))
     except Exception as e:  # reported to the parent
         q.put((rank, repr(e)[:300]))
 
@@ -148,10 +150,11 @@ def test_two_gpu_data_parallel_step_distinct_batches():
     res = _run_two(_rank_distinct)
     for r in range(2):
         assert isinstance(res[r], tuple), res
-        ar_err, own_err, step_err = res[r]
+        ar_err, own_err, step_err, moved = res[r]
         assert ar_err <= 1e-6, res          # NCCL sum == g0 + g1 (two operands: exact)
         assert own_err >= 1e-2, res         # and not world x the local gradient
-        assert step_err <= 1e-4, res        # fp32 reassociation only
+        assert step_err <= 1e-6, res        # same weights as the concatenated-batch step
+        assert moved > 1e-5, res            # which did move them
 
 
 def test_two_gpu_data_parallel_step_matches_single_gpu():
