@@ -460,10 +460,10 @@ class AttentionF16Workload(AttentionWorkload):
 
 
 class PlanTinyModelWorkload(Workload):
-    """examples/tiny_model.bwpp through the launch-plan executor: the reference
-    compiler's own graph and memory-plan dumps (tests/golden/plans/), bound to
-    T=8192 tokens, D=1024, H=4096, V=32000, f16 as the graph declares; one
-    step = one forward pass of the graph (24 kernel steps)."""
+    """examples/tiny_model.bwpp through the launch-plan executor: the launch
+    plan `bwppc --target cuda --dims T=8192,D=1024,H=4096,V=32000` wrote
+    (tests/golden/plans/), f16 as the graph declares; one step = one forward
+    pass of the graph (24 kernel launches)."""
     T, D, H, V = 8192, 1024, 4096, 32000
     kernel = "plan (tiny_model graph)"
     profile = "plan_tiny_model"
@@ -473,10 +473,9 @@ class PlanTinyModelWorkload(Workload):
     def setup(self):
         t = self.torch
         here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden", "plans")
-        dot = open(os.path.join(here, "tiny_model.dot")).read()
-        mem = open(os.path.join(here, "tiny_model.mem.txt")).read()
-        dims = dict(T=self.T, D=self.D, H=self.H, V=self.V)
-        self.plan = self.bwpp.Plan(self.ctx, dot, mem, dims)
+        name = f"tiny_model@T{self.T}_D{self.D}_H{self.H}_V{self.V}.plan"
+        with open(os.path.join(here, name)) as f:
+            self.plan = self.bwpp.Plan(self.ctx, f.read())
         g = t.Generator(device="cuda").manual_seed(6000 + self.rank)
         self.inputs = {}
         x_id = self.plan.id("x")
@@ -510,8 +509,8 @@ class PlanTinyModelWorkload(Workload):
         return float(self.flops() * self.world)
 
     def config(self):
-        return {"workload": "examples/tiny_model.bwpp forward from the reference compiler's graph + "
-                            "memory-plan dumps, launch-plan executor",
+        return {"workload": "examples/tiny_model.bwpp forward from the compiler's launch plan "
+                            "(bwppc --target cuda), launch-plan executor",
                 "T": self.T, "D": self.D, "H": self.H, "V": self.V,
                 "parallelism": f"one replica per GPU ({self.world}), no collective",
                 "fusions": "silu and residual-add GEMM epilogues, transposes folded; attention "

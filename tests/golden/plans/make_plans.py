@@ -8,8 +8,13 @@ reference's own examples and on the test sources in src/ (written for this
 repository in the reference DSL: the swiglu and residual + norm patterns):
     bwppc <example>.bwpp <tmp>.metal --entry <fn> --dot <name>.dot
           --grad-dot <name>.grad.dot --mem-plan <name>.mem.txt
-The dumps are committed so the executor tests run where the reference tree
-is absent (the GPU box).  Run from anywhere: python tests/golden/plans/make_plans.py
+It also builds `bwppc` with this package's CUDA target
+(`make -C bluewolf-plus-plus_b200/compiler`, the reference sources with
+main.c patched) and writes launch plans, <name>@<dims>.plan, for the dims the
+executor tests use:
+    bwppc <example>.bwpp <name>@<dims>.plan --entry <fn> --target cuda --dims ...
+The dumps and plans are committed so the executor tests run where the
+reference tree is absent (the GPU box).  Run from anywhere: python tests/golden/plans/make_plans.py
 The reference checkout is taken from $BWPP_REFERENCE, else from a directory
 named `reference` beside this repository.
 """
@@ -42,8 +47,35 @@ CASES = [
 ]
 
 
+# launch plans: (dump name, dims) -- the dims of the executor's GPU tests
+LAUNCH = [
+    ("matmul_add_silu", dict(M=200, K=256, N=384)),
+    ("matmul_add_bias_reshape", dict(M=129, K=136, N=264)),
+    ("norms", dict(B=96, N=512)),
+    ("attention", dict(B=2, H=3, T=256, D=64)),
+    ("attention", dict(B=2, H=3, T=256, D=128)),
+    ("attention", dict(B=2, H=3, T=256, D=96)),
+    ("tiny_block", dict(T=128, D=256, H=512)),
+    ("tiny_model", dict(T=256, D=128, H=256, V=512)),
+    ("tiny_model", dict(T=128, D=256, H=512, V=1000)),
+    ("tiny_model", dict(T=8192, D=1024, H=4096, V=32000)),
+    ("swiglu_ffn", dict(T=200, D=256, H=384)),
+    ("swiglu_gate", dict(T=300, D=520)),
+    ("residual_norm", dict(T=64, D=256)),
+    ("residual_norm", dict(T=130, D=1000)),
+    ("attn_residual_norm", dict(T=256, D=128)),
+]
+CUDA_BWPPC = os.path.join(ROOT, "bluewolf-plus-plus_b200", "compiler", "_build", "bwppc")
+
+
+def tag(dims):
+    return "_".join(f"{k}{v}" for k, v in dims.items())
+
+
 def main():
     subprocess.run(["make", "-C", os.path.join(ROOT, "oracle"), "bwppc", f"REF={REF}"], check=True)
+    subprocess.run(["make", "-C", os.path.join(ROOT, "bluewolf-plus-plus_b200", "compiler"),
+                    f"REF={REF}"], check=True)
     if not os.path.exists(BWPPC):
         sys.exit("oracle/_ref/bwppc was not built (reference tree missing?)")
     with tempfile.TemporaryDirectory() as tmp:
@@ -55,6 +87,15 @@ def main():
                             "--dot", out(".dot"), "--grad-dot", out(".grad.dot"),
                             "--mem-plan", out(".mem.txt")], check=True)
             print("wrote", name)
+    srcs = {name: (example, entry) for name, example, entry in CASES}
+    for name, dims in LAUNCH:
+        example, entry = srcs[name]
+        src = (os.path.join(HERE, example + ".bwpp") if example.startswith("src/")
+               else os.path.join(REF, "examples", example + ".bwpp"))
+        out = os.path.join(HERE, f"{name}@{tag(dims)}.plan")
+        subprocess.run([CUDA_BWPPC, src, out, "--entry", entry, "--target", "cuda", "--dims",
+                        ",".join(f"{k}={v}" for k, v in dims.items())], check=True)
+        print("wrote", os.path.basename(out))
 
 
 if __name__ == "__main__":

@@ -105,3 +105,47 @@ def test_swiglu_and_residual_norm_patterns():
                  "add+rmsnorm (fused residual add and norm, sum stored)", "add"]
     # unfused, each op is its own step
     assert len(lower("swiglu_ffn", dict(T=128, D=256, H=512), options="fuse=0").steps()) == 5
+
+
+# ---- launch plans written by `bwppc --target cuda` (compiler/codegen_cuda.c) --
+
+def launch_fixtures():
+    out = []
+    for f in sorted(os.listdir(PLANS)):
+        if f.endswith(".plan"):
+            name, tag = f[:-5].split("@")
+            dims = {}
+            for part in tag.split("_"):
+                i = next(j for j, ch in enumerate(part) if ch.isdigit())
+                dims[part[:i]] = int(part[i:])
+            out.append((name, dims, f))
+    return out
+
+
+@pytest.mark.parametrize("name,dims,fname", launch_fixtures())
+def test_compiler_launch_plan_matches_executor_lowering(name, dims, fname):
+    """The compiler's fusion decisions, operand forms, memory layout and
+    arena size equal the executor's own lowering of the same graph's dumps."""
+    lp = bwpp.Plan(None, dump(fname, ""))
+    dp = lower(name, dims)
+    assert lp.describe() == dp.describe()
+
+
+def test_launch_plan_keeps_the_metal_meta_tags():
+    text = dump("tiny_model@T256_D128_H256_V512.plan", "")
+    assert "// bwpp.meta: kernel=attention_f16" in text and "// bwpp.meta: target=cuda" in text
+    text = dump("matmul_add_silu@M200_K256_N384.plan", "")
+    assert "// bwpp.meta: kernel=matmul_f16" in text
+    assert "// bwpp.meta: epilogue=add_silu" in text
+    assert "// bwpp.launch: 0 gemm node=n2 a=v0 b=v1 bias=v2 silu=1 out=v5" in text
+
+
+def test_launch_plan_errors():
+    with pytest.raises(RuntimeError, match="not a launch plan"):
+        bwpp.Plan(None, "// BW++ CUDA launch plan\n// bwpp.meta: target=cuda\n")
+    bad = dump("residual_norm@T64_D256.plan", "").replace("add_rmsnorm", "frobnicate")
+    with pytest.raises(RuntimeError, match="unknown kernel"):
+        bwpp.Plan(None, bad)
+    bad = dump("residual_norm@T64_D256.plan", "").replace("offset=0", "offset=7")
+    with pytest.raises(RuntimeError, match="arena offset"):
+        bwpp.Plan(None, bad)

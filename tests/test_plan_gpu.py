@@ -320,3 +320,86 @@ def test_attention_residual_norm_sum_stored(ctx, fuse):
     (out,) = outs.values()
     assert rel_fro(out, ref) <= 1e-2
     assert launches == (3 if fuse else 7)
+
+
+# ---- launch plans written by `bwppc --target cuda` ------------------------------
+
+def _launch_fixtures():
+    out = []
+    for f in sorted(os.listdir(PLANS)):
+        if f.endswith(".plan") and "V32000" not in f:  # the bench-size plan runs in bench.py
+            name, tag = f[:-5].split("@")
+            dims = {}
+            for part in tag.split("_"):
+                i = next(j for j, ch in enumerate(part) if ch.isdigit())
+                dims[part[:i]] = int(part[i:])
+            out.append((name, dims, f))
+    return out
+
+
+@pytest.mark.parametrize("name,dims,fname", _launch_fixtures())
+def test_compiler_launch_plan_runs_like_the_dump(ctx, name, dims, fname):
+    """The compiler's launch plan and the executor's lowering of the graph
+    dumps are the same program: on the same inputs every output is bit for
+    bit the same, with the same launches (their numerics against the oracle
+    are checked at these dims by the tests above)."""
+    with open(os.path.join(PLANS, fname)) as f:
+        launch = bwpp.Plan(ctx, f.read())
+    lowered = bwpp.Plan(ctx, dump(name), dump(name, ".mem.txt"), dims)
+    rng = np.random.default_rng(len(fname))
+    keep = []
+    for v in lowered.values():
+        if not v["input"]:
+            continue
+        shape = v["shape"]
+        scale = 1.0 if len(shape) == 1 else shape[-1] ** -0.5
+        arr = half(rng, *shape, scale=scale)
+        if len(shape) == 1:
+            arr = (1 + 0.1 * arr).astype(np.float16)
+        t = torch.from_numpy(arr).cuda()
+        keep.append(t)
+        lowered.bind(v["id"], t)
+        launch.bind(v["id"], t)
+    lowered.run()
+    launch.run()
+    ctx.sync()
+    outs = [v["id"] for v in lowered.values() if v["output"]]
+    assert outs
+    for vid in outs:
+        a = launch.tensor(vid).cpu()
+        b = lowered.tensor(vid).cpu()
+        assert torch.equal(a, b), (fname, vid)
+        assert bool(torch.isfinite(a.float()).all())
+    assert launch.launches == lowered.launches
+    launch.close()
+    lowered.close()
+
+
+def test_tiny_model_forward_from_the_compiler_launch_plan(ctx):
+    """examples/tiny_model.bwpp compiled with --target cuda, against the fp32
+    oracle composition."""
+    T, D, H, V = 256, 128, 256, 512
+    rng = np.random.default_rng(7)
+    p = {"x": half(rng, T, D)}
+    for pre in ("1", "2"):
+        for w in ("wq", "wk", "wv", "wo"):
+            p[w + pre] = half(rng, D, D, scale=D ** -0.5)
+        p["w1" + pre] = half(rng, D, H, scale=D ** -0.5)
+        p["w2" + pre] = half(rng, H, D, scale=H ** -0.5)
+        p["g1" + pre] = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+        p["g2" + pre] = (1 + 0.1 * rng.standard_normal(D)).astype(np.float16)
+    p["wcls"] = half(rng, D, V, scale=D ** -0.5)
+    with open(os.path.join(PLANS, "tiny_model@T256_D128_H256_V512.plan")) as f:
+        plan = bwpp.Plan(ctx, f.read())
+    keep = []
+    for key, arr in p.items():
+        t = torch.from_numpy(arr).cuda()
+        keep.append(t)
+        plan.bind(key, t)
+    plan.run()
+    ctx.sync()
+    (out,) = [plan.tensor(v["id"]).float().cpu().numpy() for v in plan.values() if v["output"]]
+    assert out.shape == (T, V)
+    assert rel_fro(out, tiny_forward_ref({k: f32(v) for k, v in p.items()})) <= 3e-2
+    assert plan.launches == 20
+    plan.close()
