@@ -109,6 +109,11 @@ _SIGS = {
     "bwpp_cuda_comm_create": (_i32, [C.POINTER(_vp), _vp, _i32, _i32, _i32]),
     "bwpp_cuda_comm_allreduce_sum_f32": (_i32, [_vp, _vp, _sz, _vp]),
     "bwpp_cuda_comm_destroy": (_i32, [_vp]),
+    "bwpp_cuda_comm_create_timeout": (_i32, [C.POINTER(_vp), _vp, _i32, _i32, _i32, _u32]),
+    "bwpp_cuda_comm_set_timeout": (_i32, [_vp, _u32]),
+    "bwpp_cuda_comm_wait": (_i32, [_vp]),
+    "bwpp_cuda_comm_aborted": (_i32, [_vp]),
+    "bwpp_cuda_comm_watch": (_i32, [_vp, _vp, _vp, _vp, _u32]),
     "bwpp_cuda_tiny_model_create": (_i32, [_vp, C.POINTER(TinyModelConfig), _u64, C.POINTER(_vp)]),
     "bwpp_cuda_tiny_model_destroy": (_i32, [_vp]),
     "bwpp_cuda_tiny_model_param_count": (_sz, [_vp]),

@@ -31,9 +31,10 @@ def broadcast_bytes(payload: bytes | None, dist, src: int = 0) -> bytes:
     return obj[0]
 
 
-def comm_from_process_group(lib, rank: int, world: int, device: int, dist):
+def comm_from_process_group(lib, rank: int, world: int, device: int, dist, timeout_ms: int = 120000):
     """Creates a BwppCudaComm for (rank, world): rank 0 makes the 128-byte
-    NCCL id, the process group broadcasts it, every rank joins."""
+    NCCL id, the process group broadcasts it, every rank joins (bounded by
+    timeout_ms, which also bounds every later wait on the communicator)."""
     uid = (C.c_ubyte * 128)()
     payload = None
     if rank == 0:
@@ -44,9 +45,9 @@ def comm_from_process_group(lib, rank: int, world: int, device: int, dist):
     payload = broadcast_bytes(payload, dist)
     uid = (C.c_ubyte * 128).from_buffer_copy(payload)
     handle = C.c_void_p()
-    rc = lib.bwpp_cuda_comm_create(C.byref(handle), uid, rank, world, device)
+    rc = lib.bwpp_cuda_comm_create_timeout(C.byref(handle), uid, rank, world, device, int(timeout_ms))
     if rc != 0:
-        raise RuntimeError(f"bwpp_cuda_comm_create failed ({rc})")
+        raise RuntimeError(f"bwpp_cuda_comm_create_timeout failed ({rc})")
     return handle
 
 

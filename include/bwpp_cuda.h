@@ -334,16 +334,46 @@ int bwpp_cuda_cast_f32_bf16(BwppCudaCtx *ctx, const float *src, uint16_t *dst,
 /* ---- data-parallel communicator (NCCL) ----------------------------------- */
 /* The gradient allreduce of the tiny_model training step (no reference
  * counterpart: the reference has no multi-device code).  NCCL is loaded at
- * run time (libnccl.so.2), sharing a copy the process already has. */
+ * run time (libnccl.so.2, or the file $BWPP_NCCL_LIBRARY names), sharing a
+ * copy the process already has.
+ * Every wait on a communicator is bounded by its timeout: it is created
+ * non-blocking, and before a collective is queued (and in
+ * bwpp_cuda_comm_wait) a host watchdog waits for the previous one.  A peer
+ * that stops taking part (a rank that left between steps) makes that wait
+ * expire: the watchdog aborts the communicator (ncclCommAbort ends the NCCL
+ * kernels waiting on the peer), and the call returns BWPP_CUDA_ERR_TIMEOUT
+ * (BWPP_CUDA_ERR for an asynchronous NCCL error).  An aborted communicator
+ * refuses further collectives; destroy it. */
 typedef struct BwppCudaComm BwppCudaComm;
 /* Rank 0 creates the 128-byte id and hands it to every rank. */
 int bwpp_cuda_comm_unique_id(unsigned char *id128);
+/* Creation waits (bounded by timeout_ms) for every rank to join. */
+int bwpp_cuda_comm_create_timeout(BwppCudaComm **out, const unsigned char *id128,
+                                  int rank, int nranks, int device,
+                                  uint32_t timeout_ms);
+/* bwpp_cuda_comm_create_timeout with a 120 s timeout. */
 int bwpp_cuda_comm_create(BwppCudaComm **out, const unsigned char *id128,
                           int rank, int nranks, int device);
-/* In-place sum over ranks, asynchronous on `stream`. */
+int bwpp_cuda_comm_set_timeout(BwppCudaComm *comm, uint32_t timeout_ms);
+/* In-place sum over ranks, asynchronous on `stream` (after a bounded wait
+ * for the communicator's previous collective). */
 int bwpp_cuda_comm_allreduce_sum_f32(BwppCudaComm *comm, float *buf,
                                      size_t count, void *stream);
+/* Waits (bounded) for the latest collective. */
+int bwpp_cuda_comm_wait(BwppCudaComm *comm);
+/* 1 once the communicator was aborted (then only destroy it). */
+int bwpp_cuda_comm_aborted(const BwppCudaComm *comm);
 int bwpp_cuda_comm_destroy(BwppCudaComm *comm);
+/* The host watchdog the communicator uses, driven by callbacks (a caller's
+ * own collectives, or tests with a fake communicator): polls done(user)
+ * (1 finished, 0 not yet, < 0 failed) and error(user) (0 fine, 1 in
+ * progress, else failed; may be NULL) with a growing interval (20 us to
+ * 1 ms) until done, a failure or timeout_ms.  On failure or timeout it calls
+ * abort_fn(user) once and returns BWPP_CUDA_ERR (error), BWPP_CUDA_ERR_CUDA
+ * (done < 0) or BWPP_CUDA_ERR_TIMEOUT; BWPP_CUDA_OK when done. */
+int bwpp_cuda_comm_watch(int (*done)(void *), int (*error)(void *),
+                         void (*abort_fn)(void *), void *user,
+                         uint32_t timeout_ms);
 
 /* ---- tiny_model training step ------------------------------------------- */
 /* The decoder block of examples/tiny_model.bwpp:4-58 in the shape of the

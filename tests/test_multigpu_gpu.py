@@ -9,6 +9,11 @@ overlapped with the backward, and SGD applies lr / 2 to the sum.
     recomputed locally (an allreduce that only doubled the rank's own
     gradient fails this), and the step must match a single-GPU step on the
     concatenated batch of 2B sequences within fp32 reassociation.
+  - A rank that leaves between steps: it takes no part in the next step
+    (none of its kernels or collectives in flight, its process alive); the
+    other rank's next step ends with BWPP_CUDA_ERR_TIMEOUT within the
+    communicator's 3 s bound (its watchdog aborts the NCCL communicator), and
+    its context stays usable.  NVLS is off (NCCL_NVLS_ENABLE=0).
 Needs two GPUs (skipped otherwise)."""
 import datetime
 import os
@@ -124,6 +129,91 @@ def _rank_distinct(rank, world, port, q):
         q.put((rank, (ar_err, own_err, step_err, moved)))
     except Exception as e:  # reported to the parent
         q.put((rank, repr(e)[:300]))
+
+
+def _rank_leaves(rank, world, port, q, handled):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    try:
+        import time
+
+        import torch.distributed as dist
+        import bwpp
+        from bwpp.dist import comm_from_process_group
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        lib = bwpp.load()
+        ctx = bwpp.Ctx(rank)
+        L, D, H, F, B, S = 2, 256, 2, 512, 2, 256
+        comm = comm_from_process_group(lib, rank, world, rank, dist, timeout_ms=3000)
+        g = torch.Generator(device="cuda").manual_seed(40 + rank)
+        x = torch.randn(B * S, D, device="cuda", generator=g)
+        tgt = torch.randn(B * S, D, device="cuda", generator=g)
+        model = bwpp.TinyModel(ctx, L, D, H, F, B, S, 1e-5, seed=3)
+        model.step(x, tgt, lr=0.1, comm=comm)  # step 1: both ranks
+        ctx.sync()
+        assert lib.bwpp_cuda_comm_wait(comm) == bwpp.OK
+        dist.barrier()
+        if rank == 1:
+            # leaves: no step 2; stays alive (its memory still mapped) until
+            # the other rank has dealt with it
+            handled.wait(timeout=120)
+            lib.bwpp_cuda_comm_destroy(comm)
+            model.close()
+            ctx.close()
+            q.put((rank, "left"))
+            return
+        t0 = time.monotonic()
+        status = bwpp.OK
+        try:
+            model.step(x, tgt, lr=0.1, comm=comm)  # step 2: the peer never joins
+            ctx.sync()
+            status = lib.bwpp_cuda_comm_wait(comm)
+        except bwpp.BwppError as e:
+            status = e.status
+        elapsed = time.monotonic() - t0
+        aborted = lib.bwpp_cuda_comm_aborted(comm)
+        ctx.sync()  # the NCCL kernels ended with the abort; the stream drains
+        # the context still runs kernels
+        a = torch.randn(256, 256, device="cuda").to(torch.bfloat16)
+        c = torch.empty(256, 256, device="cuda")
+        ctx.matmul_bf16(a, a, c, 256, 256, 256, 256, 256, 256, None, 0, 0)
+        ctx.sync()
+        ok = bool(torch.allclose(c, a.float() @ a.float(), rtol=1e-2, atol=1e-2))
+        handled.set()
+        lib.bwpp_cuda_comm_destroy(comm)
+        model.close()
+        ctx.close()
+        q.put((rank, (status, elapsed, aborted, ok)))
+    except Exception as e:  # reported to the parent
+        handled.set()
+        q.put((rank, repr(e)[:300]))
+
+
+def test_two_gpu_rank_leaving_between_steps_times_out_the_next_step():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    handled = ctx.Event()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_leaves, args=(r, 2, port, q, handled)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, out = q.get(timeout=300)
+        res[r] = out
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == "left", res
+    import bwpp
+    status, elapsed, aborted, ok = res[0]
+    assert status == bwpp.ERR_TIMEOUT, res
+    assert 2.5 <= elapsed <= 30.0, res  # the 3 s bound, not a hang
+    assert aborted == 1 and ok, res
 
 
 def _run_two(target):

@@ -72,11 +72,11 @@ def test_noalloc_partial_outputs_and_empty_rows(rows, want):
     stream = torch.cuda.current_stream().cuda_stream
     x, dy, gamma = _inputs(77, max(rows, 1), cols)
     x, dy = x[:rows].contiguous(), dy[:rows].contiguous()
-    ref_dx, ref_dg, ref_db = torch.empty_like(x), torch.empty(cols, device="cuda"), torch.empty(cols, device="cuda")
-    ctx.rmsnorm_bwd(x, gamma, dy, ref_dx, ref_dg, ref_db, rows, cols, cols, 1e-5)
-    ctx.sync()
-    if rows == 0:
-        assert float(ref_dg.abs().max()) == 0.0 and float(ref_db.abs().max()) == 0.0
+    ref_dx = torch.empty_like(x)
+    ref_dg, ref_db = torch.zeros(cols, device="cuda"), torch.zeros(cols, device="cuda")
+    if rows:  # sums over no rows are 0
+        ctx.rmsnorm_bwd(x, gamma, dy, ref_dx, ref_dg, ref_db, rows, cols, cols, 1e-5)
+        ctx.sync()
     for _ in range(2):
         dx = torch.full_like(x, float("nan"))
         dg = torch.full((cols,), float("nan"), device="cuda")
