@@ -190,7 +190,9 @@ class GemmWorkload(Workload):
                 "parallelism": f"rows of X over {self.world} GPU(s), W replicated, no collective",
                 "l2": "256 MiB written between timed steps (flush)"}
 
-    # e2e through the CPU-signature mirror with pinned host buffers
+    # e2e through the CPU-signature mirror with pinned host buffers; on N GPUs
+    # its multi-GPU form, where each rank uploads 1/N of W and NCCL
+    # all-gathers the bf16 W over NVLink
     def setup_e2e(self):
         t = self.torch
         self.ha = self.x.float().cpu().pin_memory()
@@ -199,8 +201,22 @@ class GemmWorkload(Workload):
         self.hc = t.empty(self.m, self.N, dtype=t.float32).pin_memory()
         self.h2d = (self.m * self.K + self.K * self.N + self.N) * 4
         self.d2h = self.m * self.N * 4
+        if self.world > 1:
+            import torch.distributed as dist
+            self.comm = comm_from_process_group(self.bwpp.load(), self.rank, self.world,
+                                                t.cuda.current_device(), dist)
+            kc = -(-self.K // self.world)
+            k0 = min(self.rank * kc, self.K)
+            k1 = min(k0 + kc, self.K)
+            self.h2d = (self.m * self.K + (k1 - k0) * self.N + self.N) * 4
+            self.e2e_api = ("bwpp_cuda_matmul_f32_dist (the f32 mirror across the ranks): pinned host "
+                            "A rows, 1/N of W's K rows and b in, NCCL all-gather of bf16 W, C rows out")
 
     def step_e2e(self):
+        if self.world > 1:
+            self.bwpp.matmul_f32_dist(self.comm, self.ha, self.hb, self.hc, self.m, self.N, self.K, self.K,
+                                      self.N, self.N, self.hbias, 1, 1)
+            return
         self.bwpp.matmul_f32(self.ha, self.hb, self.hc, self.m, self.N, self.K, self.K, self.N, self.N,
                              self.hbias, 1, 1)
 

@@ -114,6 +114,8 @@ _SIGS = {
     "bwpp_cuda_comm_wait": (_i32, [_vp]),
     "bwpp_cuda_comm_aborted": (_i32, [_vp]),
     "bwpp_cuda_comm_watch": (_i32, [_vp, _vp, _vp, _vp, _u32]),
+    "bwpp_cuda_matmul_f32_dist": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp,
+                                         _i32, _i32]),
     "bwpp_cuda_tiny_model_create": (_i32, [_vp, C.POINTER(TinyModelConfig), _u64, C.POINTER(_vp)]),
     "bwpp_cuda_tiny_model_destroy": (_i32, [_vp]),
     "bwpp_cuda_tiny_model_param_count": (_sz, [_vp]),
@@ -518,6 +520,14 @@ def matmul_f32(a, b, c, M, N, K, lda, ldb, ldc, bias, apply_silu, apply_bias):
     load().bwpp_cuda_matmul_f32(_ptr(a), _ptr(b), _ptr(c), M, N, K, lda, ldb, ldc, _ptr(bias),
                                 int(apply_silu), int(apply_bias))
     _mirror_check("bwpp_cuda_matmul_f32")
+
+
+def matmul_f32_dist(comm, a, b, c, M, N, K, lda, ldb, ldc, bias, apply_silu, apply_bias):
+    """bwpp_cuda_matmul_f32_dist: this rank's rows of a / c, all of b and bias (host memory)."""
+    rc = load().bwpp_cuda_matmul_f32_dist(comm, _ptr(a), _ptr(b), _ptr(c), M, N, K, lda, ldb, ldc,
+                                          _ptr(bias), int(apply_silu), int(apply_bias))
+    if rc != OK:
+        raise BwppError(rc, f"bwpp_cuda_matmul_f32_dist: {status_string(rc)}")
 
 
 def softmax_f32(x, y, rows, cols, ld):

@@ -30,6 +30,7 @@ typedef struct {
   char internal[128];
 } ncclUniqueId;
 typedef int ncclResult_t;  // 0 = ncclSuccess
+constexpr int kNcclUint8 = 1;
 constexpr int kNcclFloat32 = 7;
 constexpr int kNcclSum = 0;
 constexpr int kNcclInProgress = 7;
@@ -54,6 +55,8 @@ struct Nccl {
   ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*all_reduce)(const void *, void *, size_t, int, int, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void *, void *, size_t, int, ncclComm_t,
+                             cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t *) = nullptr;
@@ -76,6 +79,7 @@ int nccl_load() {
   n.get_unique_id = (decltype(n.get_unique_id))dlsym(h, "ncclGetUniqueId");
   n.comm_init_rank = (decltype(n.comm_init_rank))dlsym(h, "ncclCommInitRank");
   n.all_reduce = (decltype(n.all_reduce))dlsym(h, "ncclAllReduce");
+  n.all_gather = (decltype(n.all_gather))dlsym(h, "ncclAllGather");
   n.comm_destroy = (decltype(n.comm_destroy))dlsym(h, "ncclCommDestroy");
   n.comm_abort = (decltype(n.comm_abort))dlsym(h, "ncclCommAbort");
   n.get_async_error = (decltype(n.get_async_error))dlsym(h, "ncclCommGetAsyncError");
@@ -337,3 +341,32 @@ int bwpp_cuda_comm_destroy(BwppCudaComm *c) {
 
 // Ranks of the communicator (for the training step's gradient averaging).
 int bwpp_comm_nranks(const BwppCudaComm *c) { return c ? c->nranks : 1; }
+int bwpp_comm_rank(const BwppCudaComm *c) { return c ? c->rank : 0; }
+int bwpp_comm_device(const BwppCudaComm *c) { return c ? c->device : -1; }
+
+// In-place all-gather of `bytes` per rank on `stream`: rank r's part sits at
+// buf + r * bytes.  Same bounded hand-off as the allreduce.
+int bwpp_comm_allgather_bytes(BwppCudaComm *c, void *buf, size_t bytes, cudaStream_t stream) {
+  if (!c || (!buf && bytes)) return BWPP_CUDA_ERR_ARG;
+  if (c->aborted) return BWPP_CUDA_ERR;
+  if (!g_nccl.all_gather) return BWPP_CUDA_ERR_UNSUPPORTED;
+  if (bytes == 0) return BWPP_CUDA_OK;
+  int rc = comm_wait_last(c);
+  if (rc) return rc;
+  uint8_t *base = static_cast<uint8_t *>(buf);
+  const ncclResult_t r = g_nccl.all_gather(base + (size_t)c->rank * bytes, base, bytes, kNcclUint8,
+                                           c->comm, stream);
+  if (r == kNcclInProgress) {
+    rc = comm_settle(c);
+    if (rc) return rc;
+  } else if (r != 0) {
+    comm_abort(c);
+    return BWPP_CUDA_ERR;
+  }
+  if (cudaEventRecord(c->last, stream) != cudaSuccess) {
+    cudaGetLastError();
+    return BWPP_CUDA_ERR_CUDA;
+  }
+  c->pending = 1;
+  return BWPP_CUDA_OK;
+}

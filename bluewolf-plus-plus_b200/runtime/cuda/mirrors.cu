@@ -22,6 +22,10 @@ int bwpp_gemm_launch(BwppCudaCtx *ctx, const uint16_t *a, const uint16_t *b,
 int bwpp_cast_launch(BwppCudaCtx *ctx, const float *src, uint16_t *dst,
                      uint32_t rows, uint32_t cols, uint32_t ld_src,
                      uint32_t ld_dst);
+int bwpp_comm_nranks(const BwppCudaComm *c);
+int bwpp_comm_rank(const BwppCudaComm *c);
+int bwpp_comm_device(const BwppCudaComm *c);
+int bwpp_comm_allgather_bytes(BwppCudaComm *c, void *buf, size_t bytes, cudaStream_t stream);
 int bwpp_attention_launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k,
                           const uint16_t *v, void *o, uint32_t BH, uint32_t Sq,
                           uint32_t Skv, uint32_t Kd, uint32_t Dv, uint64_t q_bh,
@@ -386,9 +390,117 @@ int matmul_f32_host_pipelined(BwppCudaCtx *ctx, const float *a, const float *b, 
   return bwpp_check_cuda(ctx, e, "copy stream join");
 }
 
+// ---------------------------------------------------------------------------
+// The same host-operand matmul across the ranks of a communicator, each rank
+// holding its own rows of A and C and the whole B in host memory.  B is the
+// large shared operand (4096 x 11008 fp32 = 180 MB at the benchmark config),
+// so no rank copies all of it over PCIe: rank r uploads its 1/n of B's K rows,
+// rounds them to bf16 into its slot of the bf16 B, and one in-place NCCL
+// all-gather over NVLink assembles the whole bf16 B on every GPU.  Meanwhile
+// A's row chunks go up on the upload stream; each chunk's GEMM (on the ctx
+// stream, after the all-gather) sends its C rows back on the download stream.
+int matmul_f32_dist(BwppCudaCtx *ctx, BwppCudaComm *comm, const float *a, const float *b,
+                    float *c, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                    uint32_t ldc, const float *bias, int apply_silu, bool use_bias) {
+  if (N == 0 || K == 0) return BWPP_CUDA_OK;
+  if (lda < K || ldb < N || ldc < N) return BWPP_CUDA_ERR_ARG;
+  if (bwpp_comm_device(comm) != ctx->device) return BWPP_CUDA_ERR_ARG;
+  CopyLanes *l = nullptr;
+  int rc = lanes_for(ctx, &l);
+  if (rc) return rc;
+  const uint32_t n = (uint32_t)bwpp_comm_nranks(comm), r = (uint32_t)bwpp_comm_rank(comm);
+  const uint32_t K8 = round_up(K, 8), N8 = round_up(N, 8), ldC = round_up(N, 4);
+  const uint32_t kc = (K + n - 1) / n;                       // B rows per rank
+  const uint32_t k0 = r * kc < K ? r * kc : K, k1 = k0 + kc < K ? k0 + kc : K;
+  const size_t slot = (size_t)kc * N8 * 2;                   // bytes of one rank's bf16 rows
+  uint32_t nr = 1, mr = M ? M : 1;
+  if (M) chunking(M, 256, 128, &nr, &mr);
+  Carver cv;
+  const size_t off_b = cv.take(sizeof(float) * (size_t)kc * N);
+  const size_t off_b16 = cv.take(slot * n);
+  const size_t off_bias = cv.take(use_bias ? sizeof(float) * (size_t)N : 0);
+  const size_t off_a = cv.take(sizeof(float) * (size_t)M * K);
+  const size_t off_a16 = cv.take(2 * (size_t)M * K8);
+  const size_t off_c = cv.take(sizeof(float) * (size_t)M * ldC);
+  uint8_t *ws = (uint8_t *)bwpp_ctx_workspace(ctx, cv.total);
+  if (!ws) return BWPP_CUDA_ERR_NOMEM;
+  float *dB = reinterpret_cast<float *>(ws + off_b);
+  uint16_t *b16 = reinterpret_cast<uint16_t *>(ws + off_b16);
+  float *dBias = use_bias ? reinterpret_cast<float *>(ws + off_bias) : nullptr;
+  float *dA = reinterpret_cast<float *>(ws + off_a);
+  uint16_t *a16 = reinterpret_cast<uint16_t *>(ws + off_a16);
+  float *dC = reinterpret_cast<float *>(ws + off_c);
+  // this rank's K rows of B first (upload, then bf16 into its slot), then
+  // the all-gather; the copy streams start after the ctx stream's earlier work
+  rc = bwpp_check_cuda(ctx, cudaEventRecord(l->drained, ctx->stream), "event");
+  if (!rc) rc = bwpp_check_cuda(ctx, cudaStreamWaitEvent(l->in, l->drained, 0), "wait");
+  if (!rc) rc = bwpp_check_cuda(ctx, cudaStreamWaitEvent(l->out, l->drained, 0), "wait");
+  if (!rc && k1 > k0)
+    rc = bwpp_check_cuda(ctx,
+                         cudaMemcpy2DAsync(dB, sizeof(float) * N, b + (size_t)k0 * ldb,
+                                           sizeof(float) * ldb, sizeof(float) * N, k1 - k0,
+                                           cudaMemcpyHostToDevice, l->in),
+                         "B rows upload");
+  if (!rc && use_bias)
+    rc = bwpp_check_cuda(ctx, cudaMemcpyAsync(dBias, bias, sizeof(float) * N,
+                                              cudaMemcpyHostToDevice, l->in),
+                         "bias upload");
+  if (!rc) rc = bwpp_check_cuda(ctx, cudaEventRecord(l->uploaded[0], l->in), "event");
+  if (!rc) rc = bwpp_check_cuda(ctx, cudaStreamWaitEvent(ctx->stream, l->uploaded[0], 0), "wait");
+  if (!rc && k1 > k0)
+    rc = bwpp_cast_launch(ctx, dB, b16 + (size_t)r * kc * N8, k1 - k0, N, N, N8);
+  if (!rc) rc = bwpp_comm_allgather_bytes(comm, b16, slot, ctx->stream);
+  // A's row chunks: upload, cast, GEMM over all of N, download
+  for (uint32_t k = 0; k < nr && M && !rc; ++k) {
+    const uint32_t r0 = k * mr, rows = M - r0 < mr ? M - r0 : mr;
+    const int ev = 1 + (int)(k % (kMaxChunks - 1));
+    rc = bwpp_check_cuda(ctx,
+                         cudaMemcpy2DAsync(dA + (size_t)r0 * K, sizeof(float) * K,
+                                           a + (size_t)r0 * lda, sizeof(float) * lda,
+                                           sizeof(float) * K, rows, cudaMemcpyHostToDevice, l->in),
+                         "A chunk upload");
+    if (!rc) rc = bwpp_check_cuda(ctx, cudaEventRecord(l->uploaded[ev], l->in), "event");
+    if (!rc) rc = bwpp_check_cuda(ctx, cudaStreamWaitEvent(ctx->stream, l->uploaded[ev], 0), "wait");
+    if (!rc) rc = bwpp_cast_launch(ctx, dA + (size_t)r0 * K, a16 + (size_t)r0 * K8, rows, K, K, K8);
+    if (!rc)
+      rc = bwpp_gemm_launch(ctx, a16 + (size_t)r0 * K8, b16, dC + (size_t)r0 * ldC, rows, N, K,
+                            K8, N8, ldC, dBias, apply_silu, use_bias, 0);
+    if (!rc) rc = bwpp_check_cuda(ctx, cudaEventRecord(l->computed[ev], ctx->stream), "event");
+    if (!rc) rc = bwpp_check_cuda(ctx, cudaStreamWaitEvent(l->out, l->computed[ev], 0), "wait");
+    if (!rc)
+      rc = bwpp_check_cuda(ctx,
+                           cudaMemcpy2DAsync(c + (size_t)r0 * ldc, sizeof(float) * ldc,
+                                             dC + (size_t)r0 * ldC, sizeof(float) * ldC,
+                                             sizeof(float) * N, rows, cudaMemcpyDeviceToHost,
+                                             l->out),
+                           "C chunk download");
+  }
+  cudaError_t e = cudaEventRecord(l->drained, l->out);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->stream, l->drained, 0);
+  if (rc) {
+    cudaStreamSynchronize(l->in);
+    cudaStreamSynchronize(l->out);
+    return rc;
+  }
+  return bwpp_check_cuda(ctx, e, "copy stream join");
+}
+
 }  // namespace
 
 extern "C" {
+
+int bwpp_cuda_matmul_f32_dist(BwppCudaComm *comm, const float *a, const float *b, float *c,
+                              uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                              uint32_t ldc, const float *bias, int apply_silu, int apply_bias) {
+  tl_status = BWPP_CUDA_OK;
+  if (!comm || !b || (M && (!a || !c))) return tl_status = BWPP_CUDA_ERR_ARG;
+  BwppCudaCtx *ctx = mirror_ctx();
+  if (!ctx) return tl_status = BWPP_CUDA_ERR_CUDA;
+  if (is_device_ptr(a) || is_device_ptr(b) || is_device_ptr(c)) return tl_status = BWPP_CUDA_ERR_ARG;
+  const int rc = matmul_f32_dist(ctx, comm, a, b, c, M, N, K, lda, ldb, ldc, bias, apply_silu,
+                                 apply_bias && bias);
+  return finish(ctx, rc);
+}
 
 int bwpp_cuda_last_status(void) { return bwpp_cuda_last_status_impl(); }
 

@@ -364,6 +364,19 @@ int bwpp_cuda_comm_wait(BwppCudaComm *comm);
 /* 1 once the communicator was aborted (then only destroy it). */
 int bwpp_cuda_comm_aborted(const BwppCudaComm *comm);
 int bwpp_cuda_comm_destroy(BwppCudaComm *comm);
+/* Multi-GPU form of bwpp_cuda_matmul_f32 (no reference counterpart): a
+ * collective over the communicator's ranks (one process or thread per GPU,
+ * the communicator's device current).  Rank r passes its own M rows of A and
+ * C and the whole B and bias, all in HOST memory, with the argument meaning
+ * of bwpp_cpu_matmul_f32 (runtime/cpu/bwpp_cpu_ref.c:8-35).  Each rank uploads
+ * only its 1/n of B's K rows and rounds them to bf16; an NCCL all-gather
+ * over NVLink assembles the bf16 B on every GPU; A's row chunks go up, their
+ * GEMMs run and their C rows come back, copies overlapping the math.
+ * Synchronous; returns a status (also left in bwpp_cuda_last_status). */
+int bwpp_cuda_matmul_f32_dist(BwppCudaComm *comm, const float *a, const float *b,
+                              float *c, uint32_t M, uint32_t N, uint32_t K,
+                              uint32_t lda, uint32_t ldb, uint32_t ldc,
+                              const float *bias, int apply_silu, int apply_bias);
 /* The host watchdog the communicator uses, driven by callbacks (a caller's
  * own collectives, or tests with a fake communicator): polls done(user)
  * (1 finished, 0 not yet, < 0 failed) and error(user) (0 fine, 1 in

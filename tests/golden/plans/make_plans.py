@@ -13,6 +13,7 @@ It also builds `bwppc` with this package's CUDA target
 main.c patched) and writes launch plans, <name>@<dims>.plan, for the dims the
 executor tests use:
     bwppc <example>.bwpp <name>@<dims>.plan --entry <fn> --target cuda --dims ...
+and, for gradient graphs, <name>.grad@<dims>.plan with --grad-plan.
 The dumps and plans are committed so the executor tests run where the
 reference tree is absent (the GPU box).  Run from anywhere: python tests/golden/plans/make_plans.py
 The reference checkout is taken from $BWPP_REFERENCE, else from a directory
@@ -65,6 +66,11 @@ LAUNCH = [
     ("residual_norm", dict(T=130, D=1000)),
     ("attn_residual_norm", dict(T=256, D=128)),
 ]
+# gradient graphs (--grad-plan): <name>.grad@<dims>.plan
+GRAD_LAUNCH = [
+    ("matmul_add_silu", dict(M=192, K=128, N=256)),
+    ("norms", dict(B=64, N=256)),
+]
 CUDA_BWPPC = os.path.join(ROOT, "bluewolf-plus-plus_b200", "compiler", "_build", "bwppc")
 
 
@@ -96,6 +102,16 @@ def main():
         subprocess.run([CUDA_BWPPC, src, out, "--entry", entry, "--target", "cuda", "--dims",
                         ",".join(f"{k}={v}" for k, v in dims.items())], check=True)
         print("wrote", os.path.basename(out))
+    with tempfile.TemporaryDirectory() as tmp:
+        for name, dims in GRAD_LAUNCH:
+            example, entry = srcs[name]
+            src = (os.path.join(HERE, example + ".bwpp") if example.startswith("src/")
+                   else os.path.join(REF, "examples", example + ".bwpp"))
+            out = os.path.join(HERE, f"{name}.grad@{tag(dims)}.plan")
+            subprocess.run([CUDA_BWPPC, src, os.path.join(tmp, "fwd.plan"), "--entry", entry,
+                            "--target", "cuda", "--dims", ",".join(f"{k}={v}" for k, v in dims.items()),
+                            "--grad-plan", out], check=True)
+            print("wrote", os.path.basename(out))
 
 
 if __name__ == "__main__":

@@ -216,6 +216,54 @@ def test_two_gpu_rank_leaving_between_steps_times_out_the_next_step():
     assert aborted == 1 and ok, res
 
 
+def _rank_matmul_dist(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    try:
+        import numpy as np
+        import torch.distributed as dist
+        import bwpp
+        import oracle as O
+        from bwpp.dist import comm_from_process_group, split_rows
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        lib = bwpp.load()
+        comm = comm_from_process_group(lib, rank, world, rank, dist)
+        M, K, N = 700, 1000, 1032  # K split 500 / 500, M unevenly
+        rng = np.random.default_rng(5)
+        a = (0.1 * rng.standard_normal((M, K))).astype(np.float32)
+        b = (0.1 * rng.standard_normal((K, N))).astype(np.float32)
+        bias = rng.uniform(-0.1, 0.1, N).astype(np.float32)
+        r0, r1 = split_rows(M, rank, world)
+        ha = torch.from_numpy(np.ascontiguousarray(a[r0:r1])).pin_memory()
+        hb, hbias = torch.from_numpy(b).pin_memory(), torch.from_numpy(bias).pin_memory()
+        errs = []
+        for _ in range(2):
+            hc = torch.full((r1 - r0, N), float("nan")).pin_memory()
+            bwpp.matmul_f32_dist(comm, ha, hb, hc, r1 - r0, N, K, K, N, N, hbias, 1, 1)
+            ref = O.matmul(O.bf16_to_f32(O.f32_to_bf16(a[r0:r1])), O.bf16_to_f32(O.f32_to_bf16(b)),
+                           bias, 1, 1)
+            d = hc.numpy() - ref
+            errs.append(float(np.linalg.norm(d) / np.linalg.norm(ref)))
+        lib.bwpp_cuda_comm_destroy(comm)
+        dist.destroy_process_group()
+        q.put((rank, errs))
+    except Exception as e:  # reported to the parent
+        q.put((rank, repr(e)[:300]))
+
+
+def test_two_gpu_f32_matmul_mirror_with_all_gathered_w():
+    """bwpp_cuda_matmul_f32_dist: each rank uploads half of W's K rows, the
+    bf16 W is all-gathered over NCCL, each rank's C rows match the oracle on
+    the bf16-rounded operands (1e-2 north-star bound, 2e-4 bug detector)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    res = _run_two(_rank_matmul_dist)
+    for r in range(2):
+        assert isinstance(res[r], list), res
+        assert max(res[r]) <= 2e-4, res
+
+
 def _run_two(target):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

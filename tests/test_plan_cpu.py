@@ -125,8 +125,15 @@ def launch_fixtures():
 @pytest.mark.parametrize("name,dims,fname", launch_fixtures())
 def test_compiler_launch_plan_matches_executor_lowering(name, dims, fname):
     """The compiler's fusion decisions, operand forms, memory layout and
-    arena size equal the executor's own lowering of the same graph's dumps."""
+    arena size equal the executor's own lowering of the same graph's dumps.
+    (Gradient graphs: the same launches; the dumps carry no memory plan for
+    them, the compiler lays them out with its own.)"""
     lp = bwpp.Plan(None, dump(fname, ""))
+    if name.endswith(".grad"):
+        dp = lower(name[:-5], dims, grad=True)
+        strip = lambda p: [s.replace(" (own buffer)", "") for s in p.steps()]
+        assert strip(lp) == strip(dp)
+        return
     dp = lower(name, dims)
     assert lp.describe() == dp.describe()
 

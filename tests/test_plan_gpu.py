@@ -345,7 +345,10 @@ def test_compiler_launch_plan_runs_like_the_dump(ctx, name, dims, fname):
     are checked at these dims by the tests above)."""
     with open(os.path.join(PLANS, fname)) as f:
         launch = bwpp.Plan(ctx, f.read())
-    lowered = bwpp.Plan(ctx, dump(name), dump(name, ".mem.txt"), dims)
+    if name.endswith(".grad"):  # gradient graph: no memory-plan dump for it
+        lowered = bwpp.Plan(ctx, dump(name[:-5], ".grad.dot"), None, dims)
+    else:
+        lowered = bwpp.Plan(ctx, dump(name), dump(name, ".mem.txt"), dims)
     rng = np.random.default_rng(len(fname))
     keep = []
     for v in lowered.values():
