@@ -13,6 +13,8 @@
  *      mul(., U) (the SwiGLU gate) or add(., R) (a residual);
  *      mul(silu(x), y) becomes one swiglu pass; rmsnorm(add(a, b)) one
  *      residual + norm row pass (the sum stored only when read again);
+ *      every other node is one launch (permute carries its axes, reduce_max
+ *      and its mask their axis, from the graph's attributes);
  *   3. drop launches whose results nobody reads;
  *   4. lay out memory: the memory plan's buffers (only values that are
  *      still materialised count towards a buffer's size), values without a
@@ -36,7 +38,7 @@ enum { DT_F16 = 0, DT_BF16 = 1, DT_F32 = 2 };
 
 enum {
   K_GEMM, K_ATTN, K_SOFTMAX, K_RMSNORM, K_UNARY, K_BINARY, K_TRANSPOSE, K_SILU_GRAD,
-  K_SOFTMAX_GRAD, K_RMSNORM_GRAD, K_REDUCE, K_SWIGLU, K_ADD_RMSNORM
+  K_SOFTMAX_GRAD, K_RMSNORM_GRAD, K_REDUCE, K_SWIGLU, K_ADD_RMSNORM, K_PERMUTE, K_REDUCE_MAX
 };
 
 typedef struct {
@@ -56,6 +58,9 @@ typedef struct {
   int in[BWPP_GRAPH_MAX_INPUTS];
   int nin, out, fused;
   float eps;
+  int axis;                       /* reduce_max (-1: the last) */
+  int perm[BWPP_GRAPH_MAX_DIMS];  /* permute */
+  int perm_rank;
 } CgNode;
 
 typedef struct {
@@ -63,6 +68,8 @@ typedef struct {
   int a, b, c, out, bias, d, e, out2;
   int a_t, b_t, silu, res_mul, op;
   float eps;
+  int axis;
+  int perm[BWPP_GRAPH_MAX_DIMS];
   const char *what;
 } CgStep;
 
@@ -205,9 +212,20 @@ static BwppStatus infer(Cg *cg, int pos) {
       break;
     }
     case BWPP_GOP_SOFTMAX: case BWPP_GOP_SILU: case BWPP_GOP_RMSNORM: case BWPP_GOP_SILU_GRAD:
-    case BWPP_GOP_SOFTMAX_GRAD: case BWPP_GOP_RMSNORM_GRAD:
+    case BWPP_GOP_SOFTMAX_GRAD: case BWPP_GOP_RMSNORM_GRAD: case BWPP_GOP_REDUCE_MAX_MASK:
+    case BWPP_GOP_REDUCE_MAX_GRAD:
       rank = A->rank;
       memcpy(d, A->dims, sizeof(d));
+      break;
+    case BWPP_GOP_PERMUTE:
+      /* output dim i is input dim perm[i] (the gradient graph records an
+       * inverse permute's output unpermuted; this shape wins) */
+      if (n->perm_rank != A->rank) return cg_fail(cg, "n%d: permute of rank %d by %d axes", pos, A->rank, n->perm_rank);
+      rank = A->rank;
+      for (int i = 0; i < rank; ++i) {
+        if (n->perm[i] < 0 || n->perm[i] >= rank) return cg_fail(cg, "n%d: permute axis", pos);
+        d[i] = A->dims[n->perm[i]];
+      }
       break;
     case BWPP_GOP_ADD: case BWPP_GOP_SUB: case BWPP_GOP_MUL: case BWPP_GOP_DIV: {
       const CgVal *w = (!B || numel(A) >= numel(B)) ? A : B;
@@ -233,7 +251,7 @@ static BwppStatus infer(Cg *cg, int pos) {
                      op_name(n->op), n->out, (long long)numel(o), (long long)a);
     /* the graph records some outputs untransposed (rank-4 transpose): the
      * shape that follows from the operation wins */
-    if (n->op != BWPP_GOP_TRANSPOSE && !is_gemm(n->op)) return BWPP_OK;
+    if (n->op != BWPP_GOP_TRANSPOSE && n->op != BWPP_GOP_PERMUTE && !is_gemm(n->op)) return BWPP_OK;
   }
   o->rank = rank;
   memcpy(o->dims, d, sizeof(d));
@@ -567,6 +585,22 @@ static BwppStatus lower(Cg *cg) {
         st->eps = n->eps;
         break;
       case BWPP_GOP_REDUCE_SUM: st->kind = K_REDUCE; break;
+      case BWPP_GOP_PERMUTE:
+        st->kind = K_PERMUTE;
+        for (int k = 0; k < n->perm_rank; ++k) st->perm[k] = n->perm[k];
+        break;
+      case BWPP_GOP_REDUCE_MAX:
+      case BWPP_GOP_REDUCE_MAX_MASK:
+        st->kind = K_REDUCE_MAX;
+        st->op = n->op == BWPP_GOP_REDUCE_MAX ? 0 : 1;
+        st->axis = n->axis >= 0 ? n->axis : cg->v[n->in[0]].rank - 1;
+        break;
+      case BWPP_GOP_REDUCE_MAX_GRAD: /* mask * (dy broadcast to x's shape) */
+        st->kind = K_BINARY;
+        st->b = n->in[1];
+        st->op = 2;
+        st->what = "reduce_max_grad";
+        break;
       default:
         return cg_fail(cg, "op %s (n%d) has no CUDA kernel", op_name(n->op), i);
     }
@@ -604,7 +638,8 @@ static BwppStatus lower(Cg *cg) {
    * memory plan reuses an input's buffer for the output */
   for (int i = 0; i < cg->ns; ++i) {
     const CgStep *st = &cg->s[i];
-    if (st->kind != K_GEMM && st->kind != K_ATTN && st->kind != K_TRANSPOSE && st->kind != K_REDUCE)
+    if (st->kind != K_GEMM && st->kind != K_ATTN && st->kind != K_TRANSPOSE && st->kind != K_REDUCE &&
+        st->kind != K_PERMUTE && !(st->kind == K_REDUCE_MAX && st->op == 0))
       continue;
     CgVal *o = &cg->v[st->out];
     const int rd[4] = {st->a, st->b, st->kind == K_GEMM ? -1 : st->c, st->bias};
@@ -712,12 +747,21 @@ static void emit(Cg *cg, FILE *f, const BwppIrModule *ir) {
   fprintf(f, "// bwpp.arena: bytes=%zu\n", cg->arena);
   static const char *kname[] = {"gemm", "attention", "softmax", "rmsnorm", "unary", "binary",
                                 "transpose", "silu_grad", "softmax_grad", "rmsnorm_grad",
-                                "reduce_sum", "swiglu", "add_rmsnorm"};
+                                "reduce_sum", "swiglu", "add_rmsnorm", "permute", "reduce_max"};
   static const char *bop[] = {"add", "sub", "mul", "div", "broadcast"};
   for (int i = 0; i < cg->ns; ++i) {
     const CgStep *st = &cg->s[i];
-    fprintf(f, "// bwpp.launch: %d %s node=n%d", i, kname[st->kind], st->pos);
-    switch (st->kind) {
+    const int rmg = st->what && strcmp(st->what, "reduce_max_grad") == 0;
+    fprintf(f, "// bwpp.launch: %d %s node=n%d", i, rmg ? "reduce_max_grad" : kname[st->kind], st->pos);
+    switch (rmg ? -1 : st->kind) {
+      case -1: fprintf(f, " mask=v%d dy=v%d", st->a, st->b); break;
+      case K_PERMUTE:
+        fprintf(f, " x=v%d perm=", st->a);
+        for (int k = 0; k < cg->v[st->a].rank; ++k) fprintf(f, "%s%d", k ? "," : "", st->perm[k]);
+        break;
+      case K_REDUCE_MAX:
+        fprintf(f, " x=v%d axis=%d mode=%s", st->a, st->axis, st->op ? "mask" : "values");
+        break;
       case K_GEMM:
         fprintf(f, " a=v%d b=v%d", st->a, st->b);
         if (st->a_t) fputs(" a_t=1", f);
@@ -806,6 +850,9 @@ BwppStatus bwpp_codegen_cuda(const BwppIrModule *ir, const BwppGraph *graph, con
     n->nin = (int)gn->input_count;
     n->out = (int)gn->output;
     n->eps = gn->attr.has_epsilon ? gn->attr.epsilon : 1e-5f;
+    n->axis = gn->attr.has_axis ? gn->attr.axis : -1;
+    n->perm_rank = (int)gn->attr.perm_rank;
+    for (int k = 0; k < n->perm_rank && k < BWPP_GRAPH_MAX_DIMS; ++k) n->perm[k] = (int)gn->attr.perm[k];
     if (n->out < 0 || n->out >= cg.nv || cg.v[n->out].producer >= 0) {
       rc = cg_fail(&cg, "node n%d: bad or repeated output", i);
       break;

@@ -128,6 +128,8 @@ struct GemmWork {
   uint32_t sk_tile0;   // first split tile (= items)
   uint32_t sk_tiles;   // 0: no split tail
   uint32_t sk_parts;
+  uint32_t split_first;  // 1: the split parts are every worker's first item, so
+                         // their hand-off overlaps the whole tiles after them
   uint32_t epoch;      // tag of this launch's counts (counter high word)
   float *partials;     // [slot][TILE_M][BN] fp32, in TMEM chunk order
   unsigned long long *counters;  // [slot][2 CTAs][EPI_WARPS][arrived, written]
@@ -197,12 +199,17 @@ __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t tiles_m,
 // The item with round-robin index `it`; false past the last item.
 __device__ __forceinline__ bool get_item(const GemmWork &w, uint32_t tiles_m, uint32_t tiles_n,
                                          uint32_t num_kb, uint32_t it, GemmItem &x) {
-  if (it < w.items) {
-    uint32_t t = it, half = 0;
+  const uint32_t nsplit = w.sk_tiles * w.sk_parts;
+  // split parts come first (split_first) or after the whole tiles
+  const bool split = w.split_first ? it < nsplit : it >= w.items;
+  if (!split) {
+    const uint32_t wi = w.split_first ? it - nsplit : it;
+    if (wi >= w.items) return false;
+    uint32_t t = wi, half = 0;
     x.wn = BN;
-    if (it >= w.split_begin) {
-      t = w.split_begin + (it - w.split_begin) / 2;
-      half = (it - w.split_begin) & 1;
+    if (wi >= w.split_begin) {
+      t = w.split_begin + (wi - w.split_begin) / 2;
+      half = (wi - w.split_begin) & 1;
       x.wn = BN / 2;
     }
     tile_coords(t, tiles_m, tiles_n, x.mb, x.nb);
@@ -214,8 +221,8 @@ __device__ __forceinline__ bool get_item(const GemmWork &w, uint32_t tiles_m, ui
     x.slot = 0;
     return true;
   }
-  const uint32_t j = it - w.items;
-  if (j >= w.sk_tiles * w.sk_parts) return false;
+  const uint32_t j = w.split_first ? it : it - w.items;
+  if (j >= nsplit) return false;
   const uint32_t part = j / w.sk_tiles, tr = j - part * w.sk_tiles;
   tile_coords(w.sk_tile0 + tr, tiles_m, tiles_n, x.mb, x.nb);
   x.n_off = 0;
@@ -876,6 +883,15 @@ bool pairs_enabled() {
   return on != 0;
 }
 
+// Split parts run before the whole tiles unless BWPP_GEMM_SPLIT_FIRST=0.
+bool split_first_enabled() {
+  static const int on = [] {
+    const char *e = getenv("BWPP_GEMM_SPLIT_FIRST");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return on != 0;
+}
+
 // Launches the tensor-core kernel.  Returns BWPP_CUDA_ERR_UNSUPPORTED (with
 // nothing launched) when a CTA pair cannot be made resident, so the caller
 // can take the single-CTA kernel.
@@ -952,6 +968,7 @@ int launch_tc(BwppCudaCtx *ctx, const CUtensorMap &ta, const CUtensorMap &tb,
     w.sk_tile0 = w.items;
     w.sk_tiles = tail;
     w.sk_parts = parts;
+    w.split_first = split_first_enabled() ? 1u : 0u;
     w.epoch = ++ctx->gemm_epoch;
     if (w.epoch == 0) w.epoch = ++ctx->gemm_epoch;  // 0 is the counters' initial tag
     w.partials = ctx->gemm_partials;

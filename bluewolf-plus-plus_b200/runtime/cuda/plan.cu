@@ -22,8 +22,11 @@
 //     reshape(bias) form the reference's fusion pass misses
 //     (compiler/graph_ir.c:760-767, compiler/codegen_metal.c:17-123) fuses
 //     too;
+//   * mul(silu(x), y) becomes one swiglu pass and rmsnorm(add(a, b)) one
+//     residual + norm row pass;
 //   * everything else is one kernel per node (plan_ops.cu, half_ops.cu,
-//     norms.cu, reduce_max.cu).
+//     norms.cu, reduce_max.cu), permute and the reduce_max family included
+//     (from dumps, a permute's axes are read off the symbolic dims).
 // A fusion is skipped when the memory plan hands one of its inputs' buffers
 // to a value produced before the fused step runs.  A GEMM / attention /
 // transpose / reduction whose output the plan puts in one of its inputs'
@@ -71,6 +74,10 @@ int bwpp_plan_reduce_sum(BwppCudaCtx *ctx, int dt, const void *x, void *o, uint3
 int bwpp_plan_transpose(BwppCudaCtx *ctx, int dt, const void *x, void *o, uint32_t batch,
                         uint32_t R, uint32_t C);
 int bwpp_plan_swiglu(BwppCudaCtx *ctx, int dt, const void *a, const void *b, void *o, size_t n);
+int bwpp_plan_permute(BwppCudaCtx *ctx, int dt, const void *x, void *o, int rank,
+                      const int64_t *dims, const int *perm);
+int bwpp_plan_reduce_max(BwppCudaCtx *ctx, int dt, const void *x, void *o, uint32_t outer,
+                         uint32_t n, uint32_t inner, int mode);
 int bwpp_plan_add_rmsnorm(BwppCudaCtx *ctx, int dt, const void *a, const void *b,
                           const void *gamma, const void *beta, void *h, void *y, uint32_t R,
                           uint32_t C, float eps);
@@ -117,7 +124,7 @@ struct Node {
 
 enum Kind {
   K_GEMM, K_ATTN, K_SOFTMAX, K_RMSNORM, K_UNARY, K_BINARY, K_TRANSPOSE, K_SILU_GRAD,
-  K_SOFTMAX_GRAD, K_RMSNORM_GRAD, K_REDUCE, K_SWIGLU, K_ADD_RMSNORM
+  K_SOFTMAX_GRAD, K_RMSNORM_GRAD, K_REDUCE, K_SWIGLU, K_ADD_RMSNORM, K_PERMUTE, K_REDUCE_MAX
 };
 
 struct Step {
@@ -128,6 +135,7 @@ struct Step {
   int res_mul = 0;                      // GEMM: c multiplies (SwiGLU gate) instead of adding
   int d = -1, e = -1, out2 = -1;        // add+rmsnorm: gamma, beta, the stored sum (or -1)
   float eps = 1e-5f;                    // rmsnorm, rmsnorm_grad, add+rmsnorm
+  int perm[4] = {0, 1, 2, 3};           // permute: input dim of each output dim
   int op = 0, bmode = 0, axis = 1;
   size_t bias_off = 0;                  // fp32 bias scratch offset
   std::string what;
@@ -417,6 +425,21 @@ struct BwppCudaPlan {
         st.what = "rmsnorm_grad";
       } else if (k == "reduce_sum") {
         st.kind = K_REDUCE; st.a = V("x"); st.what = "reduce_sum";
+      } else if (k == "permute") {
+        st.kind = K_PERMUTE;
+        st.a = V("x");
+        st.what = "permute";
+        const auto p = split_dims(kv["perm"]);
+        if (p.empty() || p.size() > 4) return fail(BWPP_CUDA_ERR_ARG, "launch plan: permute perm");
+        for (size_t i = 0; i < p.size(); ++i) st.perm[i] = atoi(p[i].c_str());
+      } else if (k == "reduce_max") {
+        st.kind = K_REDUCE_MAX;
+        st.a = V("x");
+        st.axis = kv.count("axis") ? atoi(kv["axis"].c_str()) : -1;
+        st.op = kv["mode"] == "mask" ? 1 : 0;
+        st.what = st.op ? "reduce_max_mask" : "reduce_max";
+      } else if (k == "reduce_max_grad") {
+        st.kind = K_BINARY; st.a = V("mask"); st.b = V("dy"); st.op = 2; st.what = "reduce_max_grad";
       } else {
         return fail(BWPP_CUDA_ERR_UNSUPPORTED, "launch plan: unknown kernel %s", kind);
       }
@@ -533,7 +556,8 @@ struct BwppCudaPlan {
       d = in(0).dims;
       std::swap(d[d.size() - 1], d[d.size() - 2]);
     } else if (op == "softmax" || op == "silu" || op == "rmsnorm" || op == "silu_grad" ||
-               op == "softmax_grad" || op == "rmsnorm_grad") {
+               op == "softmax_grad" || op == "rmsnorm_grad" || op == "reduce_max_mask" ||
+               op == "reduce_max_grad") {
       d = in(0).dims;
     } else if (op == "add" || op == "sub" || op == "mul" || op == "div") {
       d = in(0).numel() >= in(1).numel() ? in(0).dims : in(1).dims;
@@ -843,6 +867,50 @@ struct BwppCudaPlan {
         st.what = "rmsnorm_grad";
       } else if (op == "reduce_sum") {
         st.kind = K_REDUCE; st.a = n.in[0]; st.what = "reduce_sum";
+      } else if (op == "permute") {
+        // the dump carries no permutation: it is read off the symbolic dims
+        // (each output dim names one input dim); the gradient graph records a
+        // permute's output unpermuted, which reads as the identity and is
+        // refused, as is any ambiguity (the launch plan carries the attribute)
+        const Val &x = vals[n.in[0]], &o = vals[n.out];
+        st.kind = K_PERMUTE;
+        st.a = n.in[0];
+        st.what = "permute";
+        bool ok = x.sdims.size() == o.sdims.size() && !x.sdims.empty() && x.sdims.size() <= 4;
+        bool ident = true;
+        for (size_t i = 0; ok && i < o.sdims.size(); ++i) {
+          int hit = -1, hits = 0;
+          for (size_t j = 0; j < x.sdims.size(); ++j)
+            if (x.sdims[j] == o.sdims[i]) {
+              hit = (int)j;
+              ++hits;
+            }
+          ok = hits == 1;
+          st.perm[i] = hit;
+          ident = ident && hit == (int)i;
+        }
+        if (!ok || ident)
+          return fail(BWPP_CUDA_ERR_UNSUPPORTED,
+                      "permute (n%d): the permutation cannot be read off the dump's shapes; run "
+                      "the compiler's launch plan (bwppc --target cuda)", n.id);
+      } else if (op == "reduce_max" || op == "reduce_max_mask") {
+        // axis: the dim the forward output keeps as 1 (the graph's default:
+        // the last); the mask has the input's shape, so it takes the last
+        st.kind = K_REDUCE_MAX;
+        st.a = n.in[0];
+        st.op = op == "reduce_max" ? 0 : 1;
+        st.what = op;
+        const auto &xd = vals[n.in[0]].dims, &od = vals[n.out].dims;
+        st.axis = (int)xd.size() - 1;
+        if (st.op == 0 && od.size() == xd.size())
+          for (size_t i = 0; i < xd.size(); ++i)
+            if (od[i] == 1 && xd[i] != 1) {
+              st.axis = (int)i;
+              break;
+            }
+      } else if (op == "reduce_max_grad") {
+        // mask * (dy broadcast to x's shape): elementwise
+        st.kind = K_BINARY; st.a = n.in[0]; st.b = n.in[1]; st.op = 2; st.what = "reduce_max_grad";
       } else {
         return fail(BWPP_CUDA_ERR_UNSUPPORTED, "op %s (n%d) is not supported by the executor",
                     op.c_str(), n.id);
@@ -883,6 +951,25 @@ struct BwppCudaPlan {
   // (both plan sources)
   int finish() {
     for (Step &st : steps) {
+      if (st.kind == K_PERMUTE) {
+        const auto &xd = vals[st.a].dims, &od = vals[st.out].dims;
+        bool ok = xd.size() == od.size() && !xd.empty() && xd.size() <= 4;
+        std::vector<int> seen(4, 0);
+        for (size_t i = 0; ok && i < xd.size(); ++i) {
+          const int p = st.perm[i];
+          ok = p >= 0 && p < (int)xd.size() && !seen[p]++ && od[i] == xd[p];
+        }
+        if (!ok) return fail(BWPP_CUDA_ERR_ARG, "permute at n%d: permutation and shapes", nodes[st.pos].id);
+      }
+      if (st.kind == K_REDUCE_MAX) {
+        const auto &xd = vals[st.a].dims;
+        if (st.axis < 0 || st.axis >= (int)xd.size())
+          return fail(BWPP_CUDA_ERR_ARG, "reduce_max at n%d: axis", nodes[st.pos].id);
+        int64_t expect = vals[st.a].numel();
+        if (st.op == 0) expect /= xd[st.axis];
+        if (vals[st.out].numel() != expect)
+          return fail(BWPP_CUDA_ERR_ARG, "reduce_max at n%d: output shape", nodes[st.pos].id);
+      }
       Val &o = vals[st.out];
       if (st.kind == K_BINARY) {
         Val *a = &vals[st.a], *b = &vals[st.b];
@@ -922,7 +1009,8 @@ struct BwppCudaPlan {
       // not, so their output gets a buffer of its own.
       // (A GEMM's residual is read before the same elements are stored, so
       // it may share the output's buffer.)
-      if (st.kind == K_GEMM || st.kind == K_ATTN || st.kind == K_TRANSPOSE || st.kind == K_REDUCE) {
+      if (st.kind == K_GEMM || st.kind == K_ATTN || st.kind == K_TRANSPOSE || st.kind == K_REDUCE ||
+          st.kind == K_PERMUTE || (st.kind == K_REDUCE_MAX && st.op == 0)) {
         for (int x : {st.a, st.b, st.kind == K_GEMM ? -1 : st.c, st.bias})
           if (x >= 0 && !vals[x].input && vals[x].buffer >= 0 && vals[x].buffer == o.buffer)
             o.buffer = -1;
@@ -1171,6 +1259,22 @@ struct BwppCudaPlan {
                                     (uint32_t)o.rows(), (uint32_t)o.last(), st.eps);
         ++launches;
         break;
+      case K_PERMUTE: {
+        const Val &x = vals[st.a];
+        rc = bwpp_plan_permute(c, x.dtype, x.ptr, out, (int)x.dims.size(), x.dims.data(), st.perm);
+        ++launches;
+        break;
+      }
+      case K_REDUCE_MAX: {
+        const Val &x = vals[st.a];
+        int64_t outer = 1, inner = 1;
+        for (int i = 0; i < st.axis; ++i) outer *= x.dims[i];
+        for (size_t i = st.axis + 1; i < x.dims.size(); ++i) inner *= x.dims[i];
+        rc = bwpp_plan_reduce_max(c, x.dtype, x.ptr, out, (uint32_t)outer, (uint32_t)x.dims[st.axis],
+                                  (uint32_t)inner, st.op);
+        ++launches;
+        break;
+      }
       case K_SWIGLU:
         rc = bwpp_plan_swiglu(c, o.dtype, vals[st.a].ptr, vals[st.b].ptr, out, o.numel());
         ++launches;

@@ -10,7 +10,10 @@
 //   row ops  softmax_grad, rmsnorm_grad (compiler/graph_ir.c:1735-1789 rule
 //            for dX), rmsnorm / softmax for f32 or bf16 storage
 //   reduce   reduce_sum over axis 0 or 1; broadcast back
-//   layout   batched 2-D transpose
+//   layout   batched 2-D transpose; permute of up to 4 dims
+//   max      reduce_max over one axis (values), and its mask (1 at every
+//            element equal to the max along the axis: all ties, as
+//            runtime/cpu/bwpp_cpu_ref.c:146-190 marks them)
 //   fused    swiglu: silu(a) * b in one pass (the `swiglu` pattern of
 //            spec/llm-primitives.md:17-22 when a is not a GEMM output);
 //            residual + norm: h = a + b and y = rmsnorm(h) per row in one
@@ -234,6 +237,85 @@ __global__ void __launch_bounds__(kThreads)
     for (uint32_t c = threadIdx.x; c < C; c += kThreads) {
       const float g = gm ? S::ld(gm, c) : 1.0f, b = bt ? S::ld(bt, c) : 0.0f;
       S::st(y, o + c, S::ld(x, o + c) * inv * g + b);
+    }
+  }
+}
+
+// o[i0, i1, i2, i3] = x[...] with output dim d taken from input dim perm[d]
+// (rank <= 4, dense row-major; unused dims are 1).  Thread per output element.
+struct PermDims {
+  uint32_t out[4];      // output dims
+  uint64_t in_stride[4];  // input stride of the input dim each output dim reads
+};
+
+template <int DT>
+__global__ void permute_kernel(const void *x_, void *o_, size_t n, const PermDims pd) {
+  using S = St<DT>;
+  const auto *x = static_cast<const typename S::T *>(x_);
+  auto *o = static_cast<typename S::T *>(o_);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    size_t r = i, src = 0;
+#pragma unroll
+    for (int d = 3; d >= 0; --d) {
+      const uint32_t c = (uint32_t)(r % pd.out[d]);
+      r /= pd.out[d];
+      src += (size_t)c * pd.in_stride[d];
+    }
+    o[i] = x[src];
+  }
+}
+
+// reduce_max over the middle dim of x viewed as [outer, n, inner]: mode 0
+// writes the maxima [outer, inner]; mode 1 the mask [outer, n, inner] (1 where
+// x equals its maximum, all ties).  Strict '>' scan from -INF.
+// inner == 1 (the last axis): one CTA per row, block reduction.
+template <int DT>
+__global__ void __launch_bounds__(kThreads)
+    max_rows_kernel(const void *x_, void *o_, uint32_t outer, uint32_t n, int mode) {
+  using S = St<DT>;
+  const auto *x = static_cast<const typename S::T *>(x_);
+  auto *o = static_cast<typename S::T *>(o_);
+  __shared__ float sv[32];
+  for (uint32_t r = blockIdx.x; r < outer; r += gridDim.x) {
+    const size_t base = (size_t)r * n;
+    float m = -INFINITY;
+    for (uint32_t c = threadIdx.x; c < n; c += kThreads) {
+      const float t = S::ld(x, base + c);
+      if (t > m) m = t;
+    }
+    m = block_max(m, sv);
+    if (mode == 0) {
+      if (threadIdx.x == 0) S::st(o, r, m);
+    } else {
+      for (uint32_t c = threadIdx.x; c < n; c += kThreads)
+        S::st(o, base + c, S::ld(x, base + c) == m ? 1.0f : 0.0f);
+    }
+  }
+}
+
+// inner > 1: thread per (outer, inner) column, coalesced over inner
+template <int DT>
+__global__ void max_cols_kernel(const void *x_, void *o_, uint32_t outer, uint32_t n,
+                                uint32_t inner, int mode) {
+  using S = St<DT>;
+  const auto *x = static_cast<const typename S::T *>(x_);
+  auto *o = static_cast<typename S::T *>(o_);
+  const size_t cols = (size_t)outer * inner;
+  for (size_t k = blockIdx.x * (size_t)blockDim.x + threadIdx.x; k < cols;
+       k += (size_t)gridDim.x * blockDim.x) {
+    const size_t ob = k / inner, ib = k % inner;
+    const size_t base = ob * (size_t)n * inner + ib;
+    float m = -INFINITY;
+    for (uint32_t c = 0; c < n; ++c) {
+      const float t = S::ld(x, base + (size_t)c * inner);
+      if (t > m) m = t;
+    }
+    if (mode == 0) {
+      S::st(o, k, m);
+    } else {
+      for (uint32_t c = 0; c < n; ++c)
+        S::st(o, base + (size_t)c * inner, S::ld(x, base + (size_t)c * inner) == m ? 1.0f : 0.0f);
     }
   }
 }
@@ -475,5 +557,51 @@ int bwpp_plan_add_rmsnorm(BwppCudaCtx *ctx, int dt, const void *a, const void *b
                <<<grid_rows(ctx, R), kThreads, 0, ctx->stream>>>(a, b, gamma, beta, h, y, R, C,
                                                                  eps));
   BWPP_LAUNCH_CHECK(ctx, "plan add_rmsnorm");
+  return BWPP_CUDA_OK;
+}
+
+// perm[d]: the input dim output dim d reads; dims: the input's dims (rank <= 4)
+int bwpp_plan_permute(BwppCudaCtx *ctx, int dt, const void *x, void *o, int rank,
+                      const int64_t *dims, const int *perm) {
+  if (rank < 1 || rank > 4) return bwpp_set_error(ctx, BWPP_CUDA_ERR_UNSUPPORTED, "plan permute: rank");
+  uint64_t stride[4];
+  uint64_t st = 1;
+  for (int d = rank - 1; d >= 0; --d) {
+    stride[d] = st;
+    st *= (uint64_t)dims[d];
+  }
+  PermDims pd;
+  const int pad = 4 - rank;  // leading unit dims
+  size_t n = 1;
+  for (int d = 0; d < 4; ++d) {
+    if (d < pad) {
+      pd.out[d] = 1;
+      pd.in_stride[d] = 0;
+    } else {
+      const int p = perm[d - pad];
+      pd.out[d] = (uint32_t)dims[p];
+      pd.in_stride[d] = stride[p];
+      n *= (size_t)dims[p];
+    }
+  }
+  if (n == 0) return BWPP_CUDA_OK;
+  BWPP_PLAN_DT(dt, permute_kernel, <<<grid_flat(ctx, n), 256, 0, ctx->stream>>>(x, o, n, pd));
+  BWPP_LAUNCH_CHECK(ctx, "plan permute");
+  return BWPP_CUDA_OK;
+}
+
+// x viewed as [outer, n, inner]; mode 0: maxima, 1: the tie mask
+int bwpp_plan_reduce_max(BwppCudaCtx *ctx, int dt, const void *x, void *o, uint32_t outer,
+                         uint32_t n, uint32_t inner, int mode) {
+  if (!outer || !n || !inner) return BWPP_CUDA_OK;
+  if (inner == 1) {
+    BWPP_PLAN_DT(dt, max_rows_kernel,
+                 <<<grid_rows(ctx, outer), kThreads, 0, ctx->stream>>>(x, o, outer, n, mode));
+  } else {
+    BWPP_PLAN_DT(dt, max_cols_kernel,
+                 <<<grid_flat(ctx, (size_t)outer * inner), 256, 0, ctx->stream>>>(x, o, outer, n,
+                                                                                  inner, mode));
+  }
+  BWPP_LAUNCH_CHECK(ctx, "plan reduce_max");
   return BWPP_CUDA_OK;
 }

@@ -569,7 +569,11 @@ int bwpp_cuda_dispatch_attention_f16(BwppCudaCtx *ctx, const uint16_t *q, const 
  * softmax attention patterns into the attention kernel, transposes into GEMM
  * operand layouts, matmul -> add(bias by dataflow) -> silu -> mul(gate) or
  * add(residual) into the GEMM epilogue, mul(silu(x), y) into one swiglu pass,
- * rmsnorm(add(a, b)) into one residual + norm pass.  No counterpart in the
+ * rmsnorm(add(a, b)) into one residual + norm pass; every other graph op
+ * (permute and the reduce_max family included) is one kernel.  A dump does
+ * not carry a permute's axes: they are read off the symbolic dims, and a
+ * permute they do not determine is refused (the launch plan carries them).
+ * No counterpart in the
  * reference (it has no executor for its graphs); the op vocabulary is
  * compiler/include/graph_ir.h:39-57. */
 typedef struct BwppCudaPlan BwppCudaPlan;

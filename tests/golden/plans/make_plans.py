@@ -5,7 +5,8 @@ reference compiler itself.
 The reference compiler is built unmodified from its sources by
 `make -C oracle bwppc` (into oracle/_ref/bwppc, git-ignored) and run on the
 reference's own examples and on the test sources in src/ (written for this
-repository in the reference DSL: the swiglu and residual + norm patterns):
+repository in the reference DSL: the swiglu and residual + norm patterns,
+permute and reduce_max):
     bwppc <example>.bwpp <tmp>.metal --entry <fn> --dot <name>.dot
           --grad-dot <name>.grad.dot --mem-plan <name>.mem.txt
 It also builds `bwppc` with this package's CUDA target
@@ -45,6 +46,8 @@ CASES = [
     ("swiglu_gate", "src/swiglu_ffn", "gate"),
     ("attn_residual_norm", "src/residual_norm", "attn_residual_norm"),
     ("residual_norm", "src/residual_norm", "residual_norm"),
+    ("permute_max", "src/permute_max", "permute_max"),
+    ("row_max", "src/permute_max", "row_max"),
 ]
 
 
@@ -65,11 +68,15 @@ LAUNCH = [
     ("residual_norm", dict(T=64, D=256)),
     ("residual_norm", dict(T=130, D=1000)),
     ("attn_residual_norm", dict(T=256, D=128)),
+    ("permute_max", dict(B=2, T=128, H=4, D=64)),
+    ("row_max", dict(R=300, C=1000)),
 ]
 # gradient graphs (--grad-plan): <name>.grad@<dims>.plan
 GRAD_LAUNCH = [
     ("matmul_add_silu", dict(M=192, K=128, N=256)),
     ("norms", dict(B=64, N=256)),
+    ("permute_max", dict(B=2, T=128, H=4, D=64)),
+    ("row_max", dict(R=300, C=1000)),
 ]
 CUDA_BWPPC = os.path.join(ROOT, "bluewolf-plus-plus_b200", "compiler", "_build", "bwppc")
 

@@ -343,6 +343,8 @@ def test_compiler_launch_plan_runs_like_the_dump(ctx, name, dims, fname):
     dumps are the same program: on the same inputs every output is bit for
     bit the same, with the same launches (their numerics against the oracle
     are checked at these dims by the tests above)."""
+    if name == "permute_max.grad":
+        pytest.skip("the dump cannot carry the permute's axes (its own test below)")
     with open(os.path.join(PLANS, fname)) as f:
         launch = bwpp.Plan(ctx, f.read())
     if name.endswith(".grad"):  # gradient graph: no memory-plan dump for it
@@ -406,3 +408,69 @@ def test_tiny_model_forward_from_the_compiler_launch_plan(ctx):
     assert rel_fro(out, tiny_forward_ref({k: f32(v) for k, v in p.items()})) <= 3e-2
     assert plan.launches == 20
     plan.close()
+
+
+# ---- permute and reduce_max (compiler/graph_ir.c:496-548, 663-695, 1672-1690, 1798-1821) --
+
+def _plan_from(ctx, fname, inputs):
+    with open(os.path.join(PLANS, fname)) as f:
+        plan = bwpp.Plan(ctx, f.read())
+    keep = []
+    ids = [v["id"] for v in plan.values() if v["input"]]
+    for vid, arr in zip(ids, inputs):
+        t = torch.from_numpy(np.ascontiguousarray(arr)).cuda()
+        keep.append(t)
+        plan.bind(vid, t)
+    plan.run()
+    ctx.sync()
+    outs = [plan.tensor(v["id"]).float().cpu().numpy() for v in plan.values() if v["output"]]
+    plan.close()
+    return outs
+
+
+def test_permute_and_reduce_max_forward(ctx):
+    """permute(x, [0,2,1,3]) then reduce_max over the last axis (f16), exact."""
+    B, T, H, D = 2, 128, 4, 64
+    x = half(np.random.default_rng(41), B, T, H, D)
+    (out,) = _plan_from(ctx, "permute_max@B2_T128_H4_D64.plan", [x])
+    ref = np.transpose(f32(x), (0, 2, 1, 3)).max(axis=3, keepdims=True)
+    assert out.shape == (B, H, T, 1) and np.array_equal(out, ref)
+    lowered = bwpp.Plan(ctx, dump("permute_max"), dump("permute_max", ".mem.txt"), dict(B=B, T=T, H=H, D=D))
+    lowered.bind("x", torch.from_numpy(x).cuda())
+    lowered.run()
+    ctx.sync()
+    (vid,) = [v["id"] for v in lowered.values() if v["output"]]
+    assert np.array_equal(lowered.tensor(vid).float().cpu().numpy(), ref)
+    lowered.close()
+
+
+def test_permute_and_reduce_max_gradient(ctx):
+    """The gradient graph (mask of every tied maximum, dy broadcast, their
+    product, the inverse permute) against the reference's mask / grad
+    semantics (oracle restatement of runtime/cpu/bwpp_cpu_ref.c:146-219)."""
+    B, T, H, D = 2, 128, 4, 64
+    rng = np.random.default_rng(42)
+    x = half(rng, B, T, H, D)
+    y = np.ascontiguousarray(np.transpose(x, (0, 2, 1, 3)))          # forward activation
+    dy = half(rng, B, H, T, 1)
+    # inputs in value order: x, the seed dY [B,H,T,1], the activation y
+    (dx,) = _plan_from(ctx, "permute_max.grad@B2_T128_H4_D64.plan", [x, dy, y])
+    rows = f32(y).reshape(-1, D)
+    mask = O.reduce_max_mask(rows, 1)
+    g = O.reduce_max_grad(mask, f32(dy).reshape(-1), 1).reshape(B, H, T, D)
+    ref = np.transpose(g.astype(np.float16), (0, 2, 1, 3)).astype(np.float32)
+    assert dx.shape == (B, T, H, D) and np.array_equal(dx, ref)
+
+
+def test_row_max_gradient_with_ties(ctx):
+    """f32 rows with many ties: every tied maximum takes the gradient, bit for
+    bit as the reference's reduce_max mask / grad pair."""
+    R, C = 300, 1000
+    rng = np.random.default_rng(43)
+    x = rng.integers(0, 5, (R, C)).astype(np.float32)  # ties everywhere
+    dy = rng.standard_normal((R, 1)).astype(np.float32)
+    (mx,) = _plan_from(ctx, "row_max@R300_C1000.plan", [x])
+    assert np.array_equal(mx, x.max(axis=1, keepdims=True))
+    (dx,) = _plan_from(ctx, "row_max.grad@R300_C1000.plan", [x, dy])
+    mask = O.reduce_max_mask(x, 1)
+    assert np.array_equal(dx, O.reduce_max_grad(mask, dy.reshape(-1), 1))
