@@ -92,8 +92,8 @@ import bwpp
 ctx = bwpp.Ctx(0)
 rng = np.random.default_rng(91)
 outs = {}
-for i, (B, H, S, D, causal) in enumerate([(2, 3, 700, 700, 128), (1, 4, 512, 512, 64),
-                                          (1, 2, 1024, 1024, 128), (1, 1, 300, 300, 128)]):
+for i, (B, H, S, D) in enumerate([(2, 3, 700, 128), (1, 4, 512, 64), (1, 2, 1024, 128),
+                                   (1, 1, 300, 128)]):
     q, k, v = (torch.from_numpy(rng.standard_normal((B, H, S, D)).astype(np.float32)).cuda()
                .to(torch.bfloat16) for _ in range(3))
     for c in (0, 1):
