@@ -28,8 +28,6 @@
 //
 // Every wait is bounded (BWPP_WAIT_LIMIT_NS); on expiry the kernel records
 // BWPP_CUDA_ERR_TIMEOUT, unwinds, frees TMEM and returns.
-#include <stdlib.h>
-
 #include "attention_common.cuh"
 
 namespace {
@@ -44,20 +42,14 @@ constexpr int W_PROD = 16, W_MMA = 17;
 // core, so part of the load moves to the otherwise idle FMA pipe.
 constexpr int kEmuPairsPer8 = 2;
 
-// SP (P in shared memory): the softmax writes P as a K-major 128-byte-swizzle
-// bf16 tile in shared memory (one per Q tile) instead of over S's TMEM
-// columns, so S is free as soon as the softmax has loaded it: S_X(j+1) is
-// issued while the softmax of block j still runs, and only PV_X(j) waits for
-// P_X(j).  V then needs one slot (its PV burst comes once per block).
-template <int D, bool F16 = false, bool SP = false>
+template <int D, bool F16 = false>
 struct Cfg {
   static constexpr int BOXES = D / 64;
   static constexpr int TILE = BOXES * BOX;  // Q / K / V tile bytes
   static constexpr int OFF_Q = 0;           // 2 tiles
   static constexpr int OFF_K = 2 * TILE;    // 2 stages
-  static constexpr int OFF_V = 4 * TILE;    // 2 stages (SP: 1)
-  static constexpr int OFF_P = (SP ? 5 : 6) * TILE;  // SP: 2 P tiles of P_TILE bytes
-  static constexpr int OFF_BAR = OFF_P + (SP ? 2 * P_TILE : 0);
+  static constexpr int OFF_V = 4 * TILE;    // 2 stages
+  static constexpr int OFF_BAR = 6 * TILE;
   static constexpr int SMEM = OFF_BAR + 512 + 1024;
   static constexpr uint32_t TMEM_S = 0;        // S_A at 0, S_B at 128
   static constexpr uint32_t TMEM_O = 2 * BN;   // O_A at 256, O_B at 256 + D
@@ -112,7 +104,7 @@ __device__ __forceinline__ Item decode_item(int w, uint32_t pairs, uint32_t Sq, 
 // S MMAs run while the softmax warps are still in the previous epilogue; its
 // first PV waits for that epilogue to read O (o_free).  All barrier phases
 // are running counters over the CTA's whole item sequence.
-template <int D, bool F16, bool SP>
+template <int D, bool F16>
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
@@ -120,7 +112,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const AttnIO io, uint32_t BH, uint32_t Sq,
                         uint32_t Skv, float scale_log2, int causal,
                         uint32_t pairs, int *sched, int *status) {
-  using C = Cfg<D, F16, SP>;
+  using C = Cfg<D, F16>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -199,9 +191,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 Skv, (j + 1) * BN);
             ++kc;
           }
-          const int vs = SP ? 0 : (int)(vc & 1);
-          const uint32_t vph = SP ? (vc & 1) : ((vc >> 1) & 1);
-          if (!mbar_wait(&bar->v_empty[vs], vph ^ 1, status)) { ok = false; break; }
+          const int vs = vc & 1;
+          if (!mbar_wait(&bar->v_empty[vs], ((vc >> 1) & 1) ^ 1, status)) { ok = false; break; }
           mbar_arrive_expect_tx(&bar->v_full[vs], C::TILE);
           load_rows<C::BOXES>(smem + C::OFF_V + vs * C::TILE, &tmV, &bar->v_full[vs], io, it.bh, Skv,
                               j * BN);
@@ -247,20 +238,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                         (!first || ks > 0) ? 1u : 0u);
         tc_commit(&bar->pv_done[X]);
       };
-      // SP: O_X (+)= P_X V with P_X from its shared-memory tile (K-major,
-      // 128-byte swizzle, two 64-key atoms like a Q tile)
-      const uint64_t dp = make_smem_desc(smem_u32(smem + C::OFF_P), 16, 1024, BWPP_SWIZZLE_128B);
-      auto issue_pv_sp = [&](int X, bool first) {
-        const uint64_t pd = desc_add(dp, (uint32_t)X * P_TILE);
-        const uint32_t d_tmem = tmem + C::TMEM_O + X * D;
-#pragma unroll
-        for (int ks = 0; ks < BN / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * BOX + (ks & 3) * 32;
-          tc_mma_f16_ss(d_tmem, desc_add(pd, off), desc_add(dv, ks * 2048), C::IDESC_PV,
-                        (!first || ks > 0) ? 1u : 0u);
-        }
-        tc_commit(&bar->pv_done[X]);
-      };
       uint32_t kc = 0, vc = 0;          // K / V blocks consumed
       uint32_t sc[2] = {0, 0};          // S MMAs issued per tile
       uint32_t pc[2] = {0, 0};          // P blocks consumed per tile
@@ -292,13 +269,22 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_commit(&bar->k_empty[kc & 1]);
           ++kc;
         }
-        if constexpr (SP) {
-          // per block: both tiles' S(j+1) as soon as the softmax has loaded
-          // S(j), then both PV(j) as P(j) lands in shared memory
-          for (int j = 0; j < it.n && ok && !*abort_flag; ++j) {
-            bool k_ready = false;
-            for (int X = 0; X < 2 && ok; ++X) {
-              if (j + 1 >= it.nblk[X]) continue;
+        for (int j = 0; j < it.n && ok && !*abort_flag; ++j) {
+          bool v_ready = false, k_ready = false;
+          for (int X = 0; X < 2 && ok; ++X) {
+            if (j < it.nblk[X]) {
+              ok = mbar_wait(&bar->p_full[X], pc[X] & 1, status);
+              ++pc[X];
+              // the first PV of an item overwrites O_X: the previous item's
+              // epilogue must have read it
+              if (ok && j == 0 && seq > 0) ok = mbar_wait(&bar->o_free[X], (seq - 1) & 1, status);
+              if (ok && !v_ready) v_ready = ok = mbar_wait(&bar->v_full[vc & 1], (vc >> 1) & 1, status);
+              if (!ok) break;
+              tc_fence_after();
+              issue_pv(X, vc & 1, j == 0);
+            }
+            if (X == 1) tc_commit(&bar->v_empty[vc & 1]);  // V free after PV_B(j)
+            if (j + 1 < it.nblk[X]) {
               if (!k_ready) k_ready = ok = mbar_wait(&bar->k_full[kc & 1], (kc >> 1) & 1, status);
               if (ok) ok = mbar_wait(&bar->s_free[X], (sc[X] - 1) & 1, status);
               if (!ok) break;
@@ -307,58 +293,11 @@ __global__ void __launch_bounds__(THREADS, 1)
               ++sc[X];
               if (j + 2 == it.nblk[X]) tc_commit(&bar->q_empty[X]);
             }
-            if (!ok) break;
-            if (j + 1 < it.n) {
-              tc_commit(&bar->k_empty[kc & 1]);
-              ++kc;
-            }
-            ok = mbar_wait(&bar->v_full[0], vc & 1, status);
-            for (int X = 0; X < 2 && ok; ++X) {
-              if (j >= it.nblk[X]) continue;
-              ok = mbar_wait(&bar->p_full[X], pc[X] & 1, status);
-              ++pc[X];
-              // the first PV of an item overwrites O_X: the previous item's
-              // epilogue must have read it
-              if (ok && j == 0 && seq > 0) ok = mbar_wait(&bar->o_free[X], (seq - 1) & 1, status);
-              if (!ok) break;
-              tc_fence_after();
-              issue_pv_sp(X, j == 0);
-            }
-            if (!ok) break;
-            tc_commit(&bar->v_empty[0]);  // V free after both PV(j)
-            ++vc;
           }
-        } else {
-          for (int j = 0; j < it.n && ok && !*abort_flag; ++j) {
-            bool v_ready = false, k_ready = false;
-            for (int X = 0; X < 2 && ok; ++X) {
-              if (j < it.nblk[X]) {
-                ok = mbar_wait(&bar->p_full[X], pc[X] & 1, status);
-                ++pc[X];
-                // the first PV of an item overwrites O_X: the previous item's
-                // epilogue must have read it
-                if (ok && j == 0 && seq > 0) ok = mbar_wait(&bar->o_free[X], (seq - 1) & 1, status);
-                if (ok && !v_ready) v_ready = ok = mbar_wait(&bar->v_full[vc & 1], (vc >> 1) & 1, status);
-                if (!ok) break;
-                tc_fence_after();
-                issue_pv(X, vc & 1, j == 0);
-              }
-              if (X == 1) tc_commit(&bar->v_empty[vc & 1]);  // V free after PV_B(j)
-              if (j + 1 < it.nblk[X]) {
-                if (!k_ready) k_ready = ok = mbar_wait(&bar->k_full[kc & 1], (kc >> 1) & 1, status);
-                if (ok) ok = mbar_wait(&bar->s_free[X], (sc[X] - 1) & 1, status);
-                if (!ok) break;
-                tc_fence_after();
-                issue_s(X, kc & 1);
-                ++sc[X];
-                if (j + 2 == it.nblk[X]) tc_commit(&bar->q_empty[X]);
-              }
-            }
-            ++vc;
-            if (ok && j + 1 < it.n) {
-              tc_commit(&bar->k_empty[kc & 1]);
-              ++kc;
-            }
+          ++vc;
+          if (ok && j + 1 < it.n) {
+            tc_commit(&bar->k_empty[kc & 1]);
+            ++kc;
           }
         }
         if (!ok) break;
@@ -430,12 +369,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld_16x256b_x8(s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tc_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-        if constexpr (SP) {
-          // S_X is in registers: the MMA warp may issue S_X(j+1) now
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bar->s_free[X]);
-        }
         const uint32_t n0 = (uint32_t)j * BN;
         if (n0 + BN - 1 > (lim_a < lim_b ? lim_a : lim_b)) {
           // visible iff n0 + column <= lim
@@ -446,8 +379,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (col > ((v & 2) ? rel_b : rel_a)) r[v] = __float_as_uint(-INFINITY);
           }
         }
-        uint32_t pkt[16];  // P of one half: to TMEM, or (SP) to the P tile
-        bool pv_ok = true;  // SP: PV_X(j-1) seen complete
         float mxa, mxb;
         {
           float a4[4], b4[4];
@@ -480,7 +411,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint64_t acc_a = f2pack(0.0f, 0.0f), acc_b = f2pack(0.0f, 0.0f);
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
-            uint32_t *pk = pkt;
+            uint32_t pk[16];
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const int v = hf * 32 + 4 * k;
@@ -502,29 +433,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               acc_a = f2add(acc_a, f2pack(p0, p1));
               acc_b = f2add(acc_b, f2pack(p2, p3));
             }
-            if constexpr (SP) {
-              // PV_X(j-1) must be done before P_X(j) overwrites its tile (and
-              // before O is rescaled below)
-              if (hf == 0 && j > 0) {
-                pv_ok = mbar_wait(&bar->pv_done[X], pvc & 1, status);
-                ++pvc;
-                tc_fence_after();
-              }
-              // P_X(j) into its K-major 128-byte-swizzle tile: row r at
-              // r * 128, 16-byte chunk k at (k ^ (r & 7)) * 16; this thread's
-              // column pair of chunk k sits 4 * (lane & 3) bytes in
-              // (conflict-free per warp)
-              uint8_t *pt = smem + C::OFF_P + X * P_TILE + hf * BOX;
-              const uint32_t wo = 4u * (uint32_t)(lane & 3);
-              const int rb = ra + 8;
-#pragma unroll
-              for (int k = 0; k < 8; ++k) {
-                *reinterpret_cast<uint32_t *>(pt + ra * 128 + ((k ^ (ra & 7)) << 4) + wo) = pkt[2 * k];
-                *reinterpret_cast<uint32_t *>(pt + rb * 128 + ((k ^ (rb & 7)) << 4) + wo) = pkt[2 * k + 1];
-              }
-            } else {
-              tmem_st_16x128b_x8(s_col + hf * 32, pkt);
-            }
+            tmem_st_16x128b_x8(s_col + hf * 32, pk);
           }
           float a0, a1, b0, b1;
           f2unpack(acc_a, a0, a1);
@@ -534,13 +443,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           m_a = ua;
           m_b = ub;
         }
-        if (!pv_ok) {
-          ok = false;
-          break;
-        }
         // Rescale O's rows whose max moved (after the exponentials, so S no
         // longer occupies registers).  PV_X(j-1) is complete: the commit
-        // that signalled S_X(j) was issued after it (SP: waited for above).
+        // that signalled S_X(j) was issued after it.
         if (j > 0 && __any_sync(0xffffffffu, mva || mvb)) {
 #pragma unroll 1
           for (int c = 0; c < D / 64; ++c) {
@@ -553,30 +458,18 @@ __global__ void __launch_bounds__(THREADS, 1)
             tmem_st_16x256b_x8(o_col + c * 64, ro);
           }
         }
-        if constexpr (SP) {
-          tc_wait_st();
-          fence_proxy_async_smem();  // the tensor core reads P through the async proxy
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bar->p_full[X]);  // P_X ready for PV_X(j)
-        } else {
-          tc_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&bar->s_free[X]);  // S_X may be overwritten
-            mbar_arrive(&bar->p_full[X]);  // P_X ready for PV_X(j)
-          }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bar->s_free[X]);  // S_X may be overwritten
+          mbar_arrive(&bar->p_full[X]);  // P_X ready for PV_X(j)
         }
       }
       if (!ok) break;
       // epilogue: O / l -> global, then hand O_X back to the MMA warp
       if (nb > 0) {
-        if constexpr (SP) {
-          ++pvc;  // the last block's PV (the earlier ones were waited for above)
-        } else {
-          pvc += (uint32_t)nb;
-        }
+        pvc += (uint32_t)nb;
         if (!mbar_wait(&bar->pv_done[X], (pvc - 1) & 1, status)) { ok = false; break; }
         tc_fence_after();
         const float la = quad_sum(l_a), lb = quad_sum(l_b);
@@ -664,32 +557,23 @@ int make_tmap_3d(BwppCudaCtx *ctx, CUtensorMap *map, const void *base, uint32_t 
   return BWPP_CUDA_OK;
 }
 
-bool g_attr_set[8][64] = {};
+bool g_attr_set[4][64] = {};
 
-// P through shared memory (SP) when BWPP_ATTN_SMEM_P=1.
-bool smem_p_enabled() {
-  static const int on = [] {
-    const char *e = getenv("BWPP_ATTN_SMEM_P");
-    return (e && e[0] == '1') ? 1 : 0;
-  }();
-  return on != 0;
-}
-
-template <int D, bool F16 = false, bool SP = false>
-int launch_v(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *v,
-             uint32_t ld_in, uint32_t BH, uint32_t H, uint32_t Sq, uint32_t Skv, float scale,
-             int causal, const AttnIO &io) {
+template <int D, bool F16 = false>
+int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *v,
+           uint32_t ld_in, uint32_t BH, uint32_t H, uint32_t Sq, uint32_t Skv, float scale,
+           int causal, const AttnIO &io) {
   CUtensorMap tq, tk, tv;
   int rc = make_tmap_3d(ctx, &tq, q, D, Sq, BH, H, ld_in, F16);
   if (!rc) rc = make_tmap_3d(ctx, &tk, k, D, Skv, BH, H, ld_in, F16);
   if (!rc) rc = make_tmap_3d(ctx, &tv, v, D, Skv, BH, H, ld_in, F16);
   if (rc) return rc;
-  const int di = (D == 128 ? 1 : 0) + (F16 ? 2 : 0) + (SP ? 4 : 0);
+  const int di = (D == 128 ? 1 : 0) + (F16 ? 2 : 0);
   if (ctx->device < 64 && !g_attr_set[di][ctx->device]) {
     rc = bwpp_check_cuda(ctx,
-                         cudaFuncSetAttribute(attention_tc_kernel<D, F16, SP>,
+                         cudaFuncSetAttribute(attention_tc_kernel<D, F16>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              Cfg<D, F16, SP>::SMEM),
+                                              Cfg<D, F16>::SMEM),
                          "attention smem attribute");
     if (rc) return rc;
     g_attr_set[di][ctx->device] = true;
@@ -704,20 +588,11 @@ int launch_v(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint1
   rc = bwpp_check_cuda(ctx, cudaMemsetAsync(ctx->sched_counter, 0, sizeof(int), ctx->stream),
                        "attention work counter");
   if (rc) return rc;
-  attention_tc_kernel<D, F16, SP><<<(unsigned)grid, THREADS, Cfg<D, F16, SP>::SMEM, ctx->stream>>>(
+  attention_tc_kernel<D, F16><<<(unsigned)grid, THREADS, Cfg<D, F16>::SMEM, ctx->stream>>>(
       tq, tk, tv, io, BH, Sq, Skv, scale * 1.4426950408889634f, causal, pairs,
       ctx->sched_counter, ctx->status_word);
   BWPP_LAUNCH_CHECK(ctx, "attention tcgen05");
   return BWPP_CUDA_OK;
-}
-
-template <int D, bool F16 = false>
-int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *v,
-           uint32_t ld_in, uint32_t BH, uint32_t H, uint32_t Sq, uint32_t Skv, float scale,
-           int causal, const AttnIO &io) {
-  return smem_p_enabled()
-             ? launch_v<D, F16, true>(ctx, q, k, v, ld_in, BH, H, Sq, Skv, scale, causal, io)
-             : launch_v<D, F16, false>(ctx, q, k, v, ld_in, BH, H, Sq, Skv, scale, causal, io);
 }
 
 }  // namespace
