@@ -23,10 +23,11 @@
 
 #include "bwpp_cuda.h"
 
-static double now_sec(void) {
-  struct timespec ts;
-  clock_gettime(CLOCK_MONOTONIC, &ts);
-  return (double)ts.tv_sec + (double)ts.tv_nsec * 1e-9;
+/* monotonic wall clock in seconds, for the timed loops */
+static double wall_seconds(void) {
+  struct timespec t;
+  if (clock_gettime(CLOCK_MONOTONIC, &t) != 0) return 0.0;
+  return 1e-9 * (double)t.tv_nsec + (double)t.tv_sec;
 }
 
 static void ramp(float *dst, uint32_t rows, uint32_t cols, float scale) {
@@ -34,16 +35,25 @@ static void ramp(float *dst, uint32_t rows, uint32_t cols, float scale) {
     for (uint32_t j = 0; j < cols; ++j) dst[(size_t)i * cols + j] = (float)(i * cols + j + 1) * scale;
 }
 
-static void print_meta(const char *path) {
-  FILE *f = fopen(path, "rb");
-  if (!f) {
-    fprintf(stderr, "bench: failed to read %s\n", path);
+/* Echoes the compiler output's tag lines (bwpp.meta / bwpp.plan / bwpp.launch)
+ * so a run records which kernels and epilogue the compiler chose. */
+static void echo_tags(const char *path) {
+  static const char *const tags[] = {"bwpp.meta:", "bwpp.plan:", "bwpp.launch:"};
+  FILE *src = fopen(path, "r");
+  if (src == NULL) {
+    fprintf(stderr, "bench: cannot open compiler output %s\n", path);
     return;
   }
-  char line[512];
-  while (fgets(line, sizeof(line), f))
-    if (strstr(line, "bwpp.meta:") || strstr(line, "bwpp.plan:")) fputs(line, stdout);
-  fclose(f);
+  char buf[1024];
+  while (fgets(buf, (int)sizeof(buf), src) != NULL) {
+    for (size_t t = 0; t < sizeof(tags) / sizeof(tags[0]); ++t) {
+      if (strstr(buf, tags[t]) != NULL) {
+        fputs(buf, stdout);
+        break;
+      }
+    }
+  }
+  fclose(src);
 }
 
 int main(int argc, char **argv) {
@@ -64,7 +74,7 @@ int main(int argc, char **argv) {
   }
   if (metal_path) {
     printf("== MSL metadata ==\n");
-    print_meta(metal_path);
+    echo_tags(metal_path);
   }
   const size_t na = (size_t)M * K, nb = (size_t)K * N, nc = (size_t)M * N, nx = (size_t)rows * cols;
   float *a = malloc(na * 4), *b = malloc(nb * 4), *c = malloc(nc * 4), *bias = calloc(N, 4);
@@ -112,21 +122,21 @@ int main(int argc, char **argv) {
     return 1;
   }
 
-  double t0 = now_sec();
+  double t0 = wall_seconds();
   for (uint32_t i = 0; i < iters; ++i) bwpp_cuda_matmul_f32(ta, tb, tc, M, N, K, K, N, N, tbias, 0, 0);
-  double t1 = now_sec();
+  double t1 = wall_seconds();
   const double matmul_secs = t1 - t0;
   const double gflops = 2.0 * M * N * K * iters / 1e9 / (matmul_secs > 0 ? matmul_secs : 1.0);
   printf("matmul: M=%u N=%u K=%u iters=%u time=%.6fs gflops=%.2f%s\n", M, N, K, iters, matmul_secs,
          gflops, use_cuda ? " (cuda)" : " (cuda, host buffers)");
-  t0 = now_sec();
+  t0 = wall_seconds();
   for (uint32_t i = 0; i < iters; ++i) bwpp_cuda_softmax_f32(tx, ty, rows, cols, cols);
-  t1 = now_sec();
+  t1 = wall_seconds();
   const double softmax_secs = t1 - t0;
   printf("softmax: rows=%u cols=%u iters=%u time=%.6fs\n", rows, cols, iters, softmax_secs);
-  t0 = now_sec();
+  t0 = wall_seconds();
   for (uint32_t i = 0; i < iters; ++i) bwpp_cuda_rmsnorm_f32(tx, ty, tg, NULL, rows, cols, cols, 1e-5f);
-  t1 = now_sec();
+  t1 = wall_seconds();
   const double rmsnorm_secs = t1 - t0;
   printf("rmsnorm: rows=%u cols=%u iters=%u time=%.6fs\n", rows, cols, iters, rmsnorm_secs);
   const int status = bwpp_cuda_last_status();
