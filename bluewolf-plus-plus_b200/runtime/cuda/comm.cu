@@ -181,7 +181,8 @@ int bwpp_cuda_comm_watch(int (*done)(void *), int (*error)(void *), void (*abort
                          void *user, uint32_t timeout_ms) {
   if (!done || !abort_fn) return BWPP_CUDA_ERR_ARG;
   const uint64_t t0 = now_ns(), limit = (uint64_t)timeout_ms * 1000000ull;
-  long nap = 20;  // polling interval: 20 us, growing to 1 ms
+  long nap = 10;  // polling interval: 10 us, growing to 160 us (a late wake-up only delays
+                  // queueing the next collective, which the GPU is usually still busy before)
   while (true) {
     const int e = error ? error(user) : 0;
     if (e != 0 && e != 1) {
@@ -199,7 +200,7 @@ int bwpp_cuda_comm_watch(int (*done)(void *), int (*error)(void *), void (*abort
       return BWPP_CUDA_ERR_TIMEOUT;
     }
     sleep_us(nap);
-    if (nap < 1000) nap *= 2;
+    if (nap < 160) nap *= 2;
   }
 }
 

@@ -380,8 +380,8 @@ int bwpp_cuda_matmul_f32_dist(BwppCudaComm *comm, const float *a, const float *b
 /* The host watchdog the communicator uses, driven by callbacks (a caller's
  * own collectives, or tests with a fake communicator): polls done(user)
  * (1 finished, 0 not yet, < 0 failed) and error(user) (0 fine, 1 in
- * progress, else failed; may be NULL) with a growing interval (20 us to
- * 1 ms) until done, a failure or timeout_ms.  On failure or timeout it calls
+ * progress, else failed; may be NULL) with a growing interval (10 us to
+ * 160 us) until done, a failure or timeout_ms.  On failure or timeout it calls
  * abort_fn(user) once and returns BWPP_CUDA_ERR (error), BWPP_CUDA_ERR_CUDA
  * (done < 0) or BWPP_CUDA_ERR_TIMEOUT; BWPP_CUDA_OK when done. */
 int bwpp_cuda_comm_watch(int (*done)(void *), int (*error)(void *),

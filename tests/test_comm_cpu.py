@@ -69,7 +69,7 @@ def test_peer_that_never_joins_times_out_and_aborts_once():
     rc, dt = f.watch(300)
     assert rc == bwpp.ERR_TIMEOUT
     assert f.aborts == 1
-    assert 0.3 <= dt < 1.5  # the bound holds (polls back off to 1 ms, no more)
+    assert 0.3 <= dt < 1.5  # the bound holds (polls back off to 160 us, no more)
 
 
 def test_async_nccl_error_aborts():
