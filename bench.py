@@ -1045,7 +1045,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--rows", type=int, default=0,
-                    help="row-workload rows (default 65536; smaller only for profiler captures)")
+                    help="row-workload rows (default 65536) or the GEMM's M (default 8192); "
+                         "other values only for profiler captures")
     args = ap.parse_args()
     if args.workloads is None:
         args.workloads = "all" if args.workload == "gemm" else "none"
@@ -1074,6 +1075,8 @@ def main():
     wl = make_workload(args.workload, rank, world, torch, bwpp, ctx)
     if args.rows and isinstance(wl, RowWorkload):
         wl.R = args.rows
+    if args.rows and isinstance(wl, GemmWorkload):
+        wl.M = args.rows  # e.g. the per-GPU share of an N-GPU run, for a profiler capture
     wl.setup()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
 
