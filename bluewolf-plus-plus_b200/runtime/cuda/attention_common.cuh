@@ -77,36 +77,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
-// Two fp32 lanes in one 64-bit register: Blackwell issues one FMA / ADD for
-// both (fma.rn.f32x2 / add.rn.f32x2).
-__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-
-__device__ __forceinline__ void f2unpack(uint64_t v, float &lo, float &hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-
-__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-
-__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
-__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
 // 2^x for two lanes on the FMA pipe, to take load off the MUFU unit
 // (ex2): x = n + f with n = round(x) (magic-constant add: 1.5 * 2^23 leaves
 // round(x) in the low mantissa bits), f in [-0.5, 0.5]; 2^f from a cubic

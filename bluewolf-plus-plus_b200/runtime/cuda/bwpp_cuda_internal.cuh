@@ -654,10 +654,57 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t cluster_bar) {
       : "memory");
 }
 
+// Two fp32 lanes in one 64-bit register: Blackwell issues one FMA / ADD for
+// both (fma.rn.f32x2 / add.rn.f32x2).
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f2unpack(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // x * sigmoid(x).  __fdividef (2 ulp, no special-case branch) instead of the
 // IEEE divide: the divide's slow-path branch serialises the 32 independent
 // columns an epilogue thread holds.  Limits are kept: for x -> -inf the
 // denominator overflows to inf (or exceeds 2^126) and the result is -0 / 0.
 __device__ __forceinline__ float bwpp_silu_f(float x) {
   return __fdividef(x, 1.0f + __expf(-x));
+}
+
+// SiLU of two columns at once, as x * (1 / (1 + 2^(-x log2 e))): the scaling,
+// the 1 + e and the final product are paired fp32 operations (one issue slot
+// for both columns), the power of two and the reciprocal are the MUFU
+// approximations (ex2.approx, rcp.approx; flush-to-zero, so x -> -inf gives
+// 1/inf = 0 and a result of -0).
+__device__ __forceinline__ uint64_t bwpp_silu_f2(uint64_t x) {
+  const uint64_t t = f2mul(x, f2pack(-1.44269504f, -1.44269504f));
+  float t0, t1, e0, e1, y0, y1, r0, r1;
+  f2unpack(t, t0, t1);
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(t0));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(t1));
+  f2unpack(f2add(f2pack(e0, e1), f2pack(1.0f, 1.0f)), y0, y1);
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(y0));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(y1));
+  return f2mul(x, f2pack(r0, r1));
 }
