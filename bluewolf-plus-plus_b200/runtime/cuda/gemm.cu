@@ -476,9 +476,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t owned = split ? 0u : 1u;  // bit c: this part finishes class c
       if (split) {
         float *dst = slot_rows(x.slot + x.part);
+        // Classes whose partials this part has stored but not yet counted
+        // written: one fence, then lane c counts class c (the counters'
+        // round trips to L2, slow while other tiles' main loops run, overlap).
+        uint32_t unsignalled = 0;
+        auto signal_written = [&]() {
+          if (!__any_sync(0xffffffffu, unsignalled != 0)) return;
+          __threadfence();
+          __syncwarp();
+          if (lane < parts && (unsignalled >> lane & 1u))
+            epoch_arrive(counter_of(x.slot + lane) + 1, work.epoch);
+          __syncwarp();
+          unsignalled = 0;
+        };
         for (int i = 1; i <= parts; ++i) {
           const int c = (me + i) % parts;  // this part's own class last
           if (class_chunks(c) == 0) continue;
+          // before the own class, let the owners of the others go on
+          if (i == parts) signal_written();
           unsigned long long *ctr = counter_of(x.slot + c);
           uint32_t before = 0;
           if (lane == 0) before = epoch_arrive(ctr, work.epoch);
@@ -488,7 +503,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             continue;
           }
           // others still to come: this part's partial sums of class c to its
-          // slot, then count them written (every lane's stores come first)
+          // slot (counted written by signal_written, every lane's stores first)
+          unsignalled |= 1u << c;
           for (int k = c; k < my_chunks; k += parts) {
             for (int h = 0; h < per; ++h) {
               const uint32_t cc = part_col(k * per + h);
@@ -502,10 +518,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                                    __uint_as_float(w[4 * j + 2]), __uint_as_float(w[4 * j + 3])));
             }
           }
-          __threadfence();
-          __syncwarp();
-          if (lane == 0) epoch_arrive(ctr + 1, work.epoch);
         }
+        signal_written();
       }
       // the other parts' slots, in part order
       auto contrib_slot = [&](uint32_t c) { return x.slot + (c < (uint32_t)me ? c : c + 1); };
@@ -610,6 +624,40 @@ __global__ void __launch_bounds__(THREADS, 1)
                   return *reinterpret_cast<const float4 *>(blk + c * 4096u + j * 512u);
                 });
                 if (t + depth < own_parts) issue(t + depth);  // into the block just read
+              } else if (n_contrib <= 2) {
+                // Straight from L2, each load a round trip that the next
+                // tile's running main loop makes slow: both contributors'
+                // float4s of half the part are requested before any is
+                // added (two round trips per part).  Same left fold in part
+                // order: (a + b) + c.
+                const float *src0 = slot_rows(contrib_slot(0)) + (size_t)pc * BM * 32;
+                const float *src1 = slot_rows(contrib_slot(n_contrib > 1 ? 1u : 0u)) + (size_t)pc * BM * 32;
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                  float4 pre[2][4];
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    pre[0][j] = __ldcg(reinterpret_cast<const float4 *>(src0 + (4 * hh + j) * BM * 4));
+                    if (n_contrib > 1)
+                      pre[1][j] = __ldcg(reinterpret_cast<const float4 *>(src1 + (4 * hh + j) * BM * 4));
+                  }
+#pragma unroll
+                  for (int jj = 0; jj < 4; ++jj) {
+                    const int j = 4 * hh + jj;
+                    const float4 own = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    const float4 a = me == 0 ? own : pre[0][jj];
+                    const float4 b = me == 0 ? pre[0][jj] : (me == 1 ? own : pre[1][jj]);
+                    float4 s = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+                    if (parts == 3) {
+                      const float4 c3 = me == 2 ? own : pre[1][jj];
+                      s = make_float4(s.x + c3.x, s.y + c3.y, s.z + c3.z, s.w + c3.w);
+                    }
+                    v[4 * j] = s.x;
+                    v[4 * j + 1] = s.y;
+                    v[4 * j + 2] = s.z;
+                    v[4 * j + 3] = s.w;
+                  }
+                }
               } else {
                 fold([&](uint32_t c, int j) {
                   const float *src = slot_rows(contrib_slot(c)) + (size_t)pc * BM * 32;
