@@ -15,8 +15,9 @@
 // max only moves when it grows by more than 2^8 (log2 domain), so O is
 // rescaled (tcgen05.ld / st) rarely; P <= 256 stays exact enough in bf16.
 // The softmax arithmetic uses paired fp32 lanes (fma/add .f32x2) and 3-input
-// max to halve its instruction count; CTAs are ordered head-major so one
-// head's K / V is read from DRAM once and shared through L2.
+// max to halve its instruction count; items go in groups of heads whose
+// K / V fit a share of L2 (read from DRAM once, shared through L2), heaviest
+// first inside a group.
 //
 // Warp roles (576 threads): warps 0-7 softmax of tile A, warps 8-15
 // softmax of tile B (warp w reads TMEM lanes 32*(w%4)..; the two warps of a
@@ -29,6 +30,8 @@
 // Every wait is bounded (BWPP_WAIT_LIMIT_NS); on expiry the kernel records
 // BWPP_CUDA_ERR_TIMEOUT, unwinds, frees TMEM and returns.
 #include "attention_common.cuh"
+
+#include <algorithm>
 
 namespace {
 
@@ -73,19 +76,29 @@ struct Bars {
 };
 static_assert(sizeof(Bars) <= 512, "barrier block");
 
-// Work item w (in the order CTAs take them): head bh = w / pairs, query
-// pair pairs - 1 - w % pairs of that head (the heaviest causal pair first),
-// i.e. rows q0 .. q0 + 255 as tiles A and B.
+// Work item w (in the order CTAs take them): the heads go in groups of
+// `group` (causal: as many as keep their K / V in a fraction of L2; else 1),
+// and inside a group the items go heaviest first across its heads: pair
+// pairs - 1 of every head of the group, then pair pairs - 2, ...  The CTAs
+// running together then share the group's K / V through L2, and, since the
+// work counter hands items out in this order, the last items of the launch
+// are the lightest (with causal items ordered head by head, a late heavy
+// item left most CTAs idle at the end when there are few heads per GPU).
+// Pair p is rows q0 .. q0 + 255 as tiles A and B, q0 = 2 p BM.
 struct Item {
   uint32_t bh, q0;
   int nblk[2], n;
 };
 
-__device__ __forceinline__ Item decode_item(int w, uint32_t pairs, uint32_t Sq, uint32_t Skv,
-                                            int causal) {
+__device__ __forceinline__ Item decode_item(int w, uint32_t pairs, uint32_t BH, uint32_t group,
+                                            uint32_t Sq, uint32_t Skv, int causal) {
   Item it;
-  it.bh = (uint32_t)w / pairs;
-  it.q0 = (pairs - 1 - (uint32_t)w % pairs) * 2 * BM;
+  const uint32_t per_group = group * pairs;
+  const uint32_t g0 = (uint32_t)w / per_group * group;  // first head of w's group
+  const uint32_t r = (uint32_t)w % per_group;
+  const uint32_t nh = min(group, BH - g0);              // heads in that group
+  it.bh = g0 + r % nh;
+  it.q0 = (pairs - 1 - r / nh) * 2 * BM;
   it.nblk[0] = blocks_for(it.q0, Sq, Skv, causal);
   it.nblk[1] = blocks_for(it.q0 + BM, Sq, Skv, causal);
   it.n = max(it.nblk[0], it.nblk[1]);
@@ -94,9 +107,9 @@ __device__ __forceinline__ Item decode_item(int w, uint32_t pairs, uint32_t Sq, 
 
 // Persistent: one CTA per SM takes work items (256 query rows of one head)
 // until none is left: its first item is blockIdx.x, the next ones come from
-// the context's work counter (items gridDim.x, gridDim.x + 1, ... in
-// head-major order, so the CTAs running together share a few heads' K / V in
-// L2, and a CTA that drew a short causal item simply draws again).  The
+// the context's work counter (items gridDim.x, gridDim.x + 1, ... in the
+// order of decode_item, so the CTAs running together share a group of heads'
+// K / V in L2, and a CTA that drew a short causal item simply draws again).  The
 // producer publishes each item id through a two-slot ring (sched_full /
 // sched_empty); every role walks the same item sequence.  Across items the
 // K / V ring keeps streaming, the next item's Q is loaded as soon as the
@@ -111,7 +124,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const __grid_constant__ CUtensorMap tmV,
                         const AttnIO io, uint32_t BH, uint32_t Sq,
                         uint32_t Skv, float scale_log2, int causal,
-                        uint32_t pairs, int *sched, int *status) {
+                        uint32_t pairs, uint32_t group, int *sched, int *status) {
   using C = Cfg<D, F16>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -165,7 +178,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         bar->item[slot] = w < total ? w : -1;
         mbar_arrive(&bar->sched_full[slot]);
         if (w >= total) break;
-        const Item it = decode_item(w, pairs, Sq, Skv, causal);
+        const Item it = decode_item(w, pairs, BH, group, Sq, Skv, causal);
         // K(0) first (its slot frees with the previous item's last S MMAs),
         // then both Q tiles.  Every item has at least one block (its first
         // row is below Sq and Skv >= 1).
@@ -248,7 +261,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int w = bar->item[slot];
         mbar_arrive(&bar->sched_empty[slot]);
         if (w < 0) break;
-        const Item it = decode_item(w, pairs, Sq, Skv, causal);
+        const Item it = decode_item(w, pairs, BH, group, Sq, Skv, causal);
         {
           // block 0: S_A(0), S_B(0)
           ok = mbar_wait(&bar->k_full[kc & 1], (kc >> 1) & 1, status);
@@ -346,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->sched_empty[slot]);
       if (w < 0) break;
-      const Item it = decode_item(w, pairs, Sq, Skv, causal);
+      const Item it = decode_item(w, pairs, BH, group, Sq, Skv, causal);
       const uint32_t bh = it.bh;
       const uint32_t qa = it.q0 + X * BM + ra, qb = qa + 8;  // query indices
       // last visible key of each row
@@ -585,11 +598,20 @@ int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_
   // persistent: one CTA per SM (at most one per item); the work counter
   // hands out the items after the first gridDim.x
   const uint64_t grid = items < (uint64_t)ctx->num_sms ? items : (uint64_t)ctx->num_sms;
+  // heads per item group: their K / V (2 Skv D 16-bit values each) within
+  // 32 MB.  Non-causal items are all alike, so there the order stays head by
+  // head (group 1): the CTAs of a head then read each K / V block together,
+  // 1.2% faster than the grouped order (which took causal at 32 heads per
+  // GPU from 808 to 1001 TFLOP/s).
+  const uint64_t kv_head = 4ull * Skv * D;
+  const uint32_t group =
+      causal ? (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(BH, (32ull << 20) / kv_head))
+             : 1u;
   rc = bwpp_check_cuda(ctx, cudaMemsetAsync(ctx->sched_counter, 0, sizeof(int), ctx->stream),
                        "attention work counter");
   if (rc) return rc;
   attention_tc_kernel<D, F16><<<(unsigned)grid, THREADS, Cfg<D, F16>::SMEM, ctx->stream>>>(
-      tq, tk, tv, io, BH, Sq, Skv, scale * 1.4426950408889634f, causal, pairs,
+      tq, tk, tv, io, BH, Sq, Skv, scale * 1.4426950408889634f, causal, pairs, group,
       ctx->sched_counter, ctx->status_word);
   BWPP_LAUNCH_CHECK(ctx, "attention tcgen05");
   return BWPP_CUDA_OK;
