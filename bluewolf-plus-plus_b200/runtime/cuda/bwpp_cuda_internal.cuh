@@ -183,6 +183,49 @@ __device__ __forceinline__ bool flag_wait(const uint32_t *p, uint32_t want, int 
   }
 }
 
+// ---- epoch-tagged counters in global memory (split work items) ----------
+
+// Counts one arrival on an epoch-tagged counter (high word: epoch, low word:
+// count; a word from an earlier launch reads as a count of 0) and returns the
+// count before it.  At most the parts of one split tile contend, so the loop
+// ends.
+__device__ __forceinline__ uint32_t epoch_arrive(unsigned long long *p, uint32_t epoch) {
+  unsigned long long cur = *reinterpret_cast<volatile unsigned long long *>(p);
+  while (true) {
+    const unsigned long long base =
+        (uint32_t)(cur >> 32) == epoch ? cur : ((unsigned long long)epoch << 32);
+    const unsigned long long prev = atomicCAS(p, cur, base + 1);
+    if (prev == cur) return (uint32_t)base;
+    cur = prev;
+  }
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits (bounded) until the counter reads `count` in this epoch; acquire, so
+// the counted writers' partials are then visible.
+__device__ __forceinline__ bool epoch_wait(const unsigned long long *p, uint32_t epoch,
+                                           uint32_t count, int *status) {
+  const unsigned long long want = ((unsigned long long)epoch << 32) | count;
+  if (ld_acquire_gpu_u64(p) == want) return true;
+  const uint64_t t0 = bwpp_globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      if (ld_acquire_gpu_u64(p) == want) return true;
+      __nanosleep(64);
+    }
+    if (bwpp_globaltimer() - t0 > BWPP_WAIT_LIMIT_NS) {
+      bwpp_report(status, BWPP_CUDA_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // ---- TMA: each copy targets the issuing CTA only --------------------------
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,

@@ -139,46 +139,6 @@ struct GemmWork {
   unsigned long long *counters;  // [slot][2 CTAs][EPI_WARPS][arrived, written]
 };
 
-// Counts one arrival on an epoch-tagged counter (high word: epoch, low word:
-// count; a word from an earlier launch reads as a count of 0) and returns the
-// count before it.  At most sk_parts warps contend, so the loop ends.
-__device__ __forceinline__ uint32_t epoch_arrive(unsigned long long *p, uint32_t epoch) {
-  unsigned long long cur = *reinterpret_cast<volatile unsigned long long *>(p);
-  while (true) {
-    const unsigned long long base =
-        (uint32_t)(cur >> 32) == epoch ? cur : ((unsigned long long)epoch << 32);
-    const unsigned long long prev = atomicCAS(p, cur, base + 1);
-    if (prev == cur) return (uint32_t)base;
-    cur = prev;
-  }
-}
-
-__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long *p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Waits (bounded) until the counter reads `count` in this epoch; acquire, so
-// the counted writers' partials are then visible.
-__device__ __forceinline__ bool epoch_wait(const unsigned long long *p, uint32_t epoch,
-                                           uint32_t count, int *status) {
-  const unsigned long long want = ((unsigned long long)epoch << 32) | count;
-  if (ld_acquire_gpu_u64(p) == want) return true;
-  const uint64_t t0 = bwpp_globaltimer();
-  while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 64; ++i) {
-      if (ld_acquire_gpu_u64(p) == want) return true;
-      __nanosleep(64);
-    }
-    if (bwpp_globaltimer() - t0 > BWPP_WAIT_LIMIT_NS) {
-      bwpp_report(status, BWPP_CUDA_ERR_TIMEOUT);
-      return false;
-    }
-  }
-}
-
 // One work item: a tile (or tile half) and the K blocks [kb0, kb1) of it.
 struct GemmItem {
   uint32_t mb, nb, n_off, wn, kb0, kb1;
@@ -568,6 +528,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             item_ok = false;
             break;
           }
+          __syncwarp();  // lane 0's acquire orders the whole warp's loads below
           if (depth)
             for (int t = 0; t < depth && t < own_parts; ++t) issue(t);
         }
