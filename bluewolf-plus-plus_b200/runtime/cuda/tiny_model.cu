@@ -97,12 +97,28 @@ struct BwppCudaTinyModel {
   void *arena;       // one cudaMalloc for everything above
   // gradient allreduce overlapped with the backward: one bucket per layer
   cudaStream_t comm_stream;
-  cudaEvent_t grad_ready[16], bucket_done[16];
+  // two gradient buckets per layer (FFN part, then attention part)
+  cudaEvent_t grad_ready[32], bucket_done[32];
 };
 
 namespace {
 
 size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Sums gradient bucket b (count floats at g) over the ranks on the comm
+// stream once the backward has produced it; every rank issues the buckets
+// in the same order.
+int allreduce_bucket(BwppCudaCtx *ctx, BwppCudaTinyModel *m, BwppCudaComm *comm, uint32_t b,
+                     float *g, size_t count) {
+  int rc = bwpp_check_cuda(ctx, cudaEventRecord(m->grad_ready[b], ctx->stream), "grad event");
+  if (!rc)
+    rc = bwpp_check_cuda(ctx, cudaStreamWaitEvent(m->comm_stream, m->grad_ready[b], 0),
+                         "comm wait");
+  if (!rc) rc = bwpp_cuda_comm_allreduce_sum_f32(comm, g, count, m->comm_stream);
+  if (!rc)
+    rc = bwpp_check_cuda(ctx, cudaEventRecord(m->bucket_done[b], m->comm_stream), "bucket event");
+  return rc;
+}
 
 // dh += rmsnorm_bwd(x, gamma, dtmp) and dgamma; dh16 = bf16(dh) when given.
 // One pass (the norm backward adds its dx into dh) when the row fits the
@@ -225,17 +241,17 @@ int bwpp_cuda_tiny_model_create(BwppCudaCtx *ctx, const BwppCudaTinyModelConfig 
   if (!rc)
     rc = bwpp_check_cuda(ctx, cudaStreamCreateWithFlags(&m->comm_stream, cudaStreamNonBlocking),
                          "comm stream");
-  for (uint32_t l = 0; l < c.layers && !rc; ++l) {
-    rc = bwpp_check_cuda(ctx, cudaEventCreateWithFlags(&m->grad_ready[l], cudaEventDisableTiming),
+  for (uint32_t b = 0; b < 2 * c.layers && !rc; ++b) {
+    rc = bwpp_check_cuda(ctx, cudaEventCreateWithFlags(&m->grad_ready[b], cudaEventDisableTiming),
                          "grad event");
     if (!rc)
-      rc = bwpp_check_cuda(ctx, cudaEventCreateWithFlags(&m->bucket_done[l], cudaEventDisableTiming),
+      rc = bwpp_check_cuda(ctx, cudaEventCreateWithFlags(&m->bucket_done[b], cudaEventDisableTiming),
                            "bucket event");
   }
   if (rc) {
-    for (uint32_t l = 0; l < c.layers; ++l) {
-      if (m->grad_ready[l]) cudaEventDestroy(m->grad_ready[l]);
-      if (m->bucket_done[l]) cudaEventDestroy(m->bucket_done[l]);
+    for (uint32_t b = 0; b < 2 * c.layers; ++b) {
+      if (m->grad_ready[b]) cudaEventDestroy(m->grad_ready[b]);
+      if (m->bucket_done[b]) cudaEventDestroy(m->bucket_done[b]);
     }
     if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
     cudaFree(m->arena);
@@ -251,9 +267,9 @@ int bwpp_cuda_tiny_model_destroy(BwppCudaTinyModel *m) {
   bwpp_ctx_enter(m->ctx);
   cudaStreamSynchronize(m->ctx->stream);
   cudaStreamSynchronize(m->comm_stream);
-  for (uint32_t l = 0; l < m->cfg.layers; ++l) {
-    cudaEventDestroy(m->grad_ready[l]);
-    cudaEventDestroy(m->bucket_done[l]);
+  for (uint32_t b = 0; b < 2 * m->cfg.layers; ++b) {
+    cudaEventDestroy(m->grad_ready[b]);
+    cudaEventDestroy(m->bucket_done[b]);
   }
   cudaStreamDestroy(m->comm_stream);
   cudaFree(m->arena);
@@ -373,6 +389,9 @@ int bwpp_cuda_tiny_model_step(BwppCudaTinyModel *m, const float *x, const float 
                             2 * F, nullptr, 0, nullptr, 0, 0, 0));  // dn2 = dgu W13^T
     // h_mid feeds rmsnorm(g2) and the residual: dh += rmsnorm_bwd(dn2), dh16 = bf16(dh)
     TRY(norm_bwd_into_dh(ctx, m, a.h_mid, P + p.g2, G + p.g2, T, D, c.eps, m->dh16));
+    // the FFN half of layer l's gradients (g2, w13, w2) is final: its sum over
+    // the ranks overlaps the attention backward of this layer
+    if (comm) TRY(allreduce_bucket(ctx, m, comm, 2 * l, G + p.g2, p.w2 + (size_t)F * D - p.g2));
     // h_mid = h_in + o Wo
     TRY(bwpp_gemm_launch_ex(ctx, a.o, 1, D, m->dh16, 1, D, G + p.wo, D, D, D, T, nullptr, 0,
                             nullptr, 0, 0, 0));  // dWo = o^T dh
@@ -390,25 +409,16 @@ int bwpp_cuda_tiny_model_step(BwppCudaTinyModel *m, const float *x, const float 
     // when a lower layer still reads it)
     TRY(norm_bwd_into_dh(ctx, m, a.h_in, P + p.g1, G + p.g1, T, D, c.eps,
                          l > 0 ? m->dh16 : nullptr));
-    // layer l's gradients are final: sum them over the ranks on the comm
-    // stream while the backward of layer l-1 runs (every rank issues the
-    // buckets in the same order, layers L-1 .. 0)
-    if (comm) {
-      const size_t begin = p.g1, count = p.w2 + (size_t)F * D - p.g1;
-      TRY(bwpp_check_cuda(ctx, cudaEventRecord(m->grad_ready[l], ctx->stream), "grad event"));
-      TRY(bwpp_check_cuda(ctx, cudaStreamWaitEvent(m->comm_stream, m->grad_ready[l], 0),
-                          "comm wait"));
-      TRY(bwpp_cuda_comm_allreduce_sum_f32(comm, G + begin, count, m->comm_stream));
-      TRY(bwpp_check_cuda(ctx, cudaEventRecord(m->bucket_done[l], m->comm_stream),
-                          "bucket event"));
-    }
+    // and the attention half (g1, wqkv, wo), overlapping the backward of
+    // layer l-1 (buckets in the same order on every rank)
+    if (comm) TRY(allreduce_bucket(ctx, m, comm, 2 * l + 1, G + p.g1, p.g2 - p.g1));
   }
   // ---------------- data-parallel gradient sum (overlapped above), SGD on
   // the mean gradient once every bucket has been summed
   const int nr = comm ? bwpp_comm_nranks(comm) : 1;
   if (comm)
-    for (uint32_t l = 0; l < c.layers; ++l)
-      TRY(bwpp_check_cuda(ctx, cudaStreamWaitEvent(ctx->stream, m->bucket_done[l], 0),
+    for (uint32_t b = 0; b < 2 * c.layers; ++b)
+      TRY(bwpp_check_cuda(ctx, cudaStreamWaitEvent(ctx->stream, m->bucket_done[b], 0),
                           "bucket wait"));
   if (lr != 0.0f) TRY(bwpp_sgd(ctx, P, G, P16, m->nparams, lr / (float)nr));
   if (loss_out)
