@@ -303,6 +303,31 @@ def test_residual_norm(ctx, fuse, T, D):
 
 
 @pytest.mark.parametrize("fuse", [1, 0])
+@pytest.mark.parametrize("T,D", [(64, 256), (130, 1000)])
+def test_residual_norm_in_f32_at_the_norm_tolerance(ctx, fuse, T, D):
+    """The same graph with every value declared f32: no storage rounding is
+    left, so the executor's residual + rmsnorm (fused, or add then norm)
+    meets the north-star norm bound, 1e-5 relative, against the fp32 oracle."""
+    rng = np.random.default_rng(35 + D)
+    x, r = (rng.standard_normal((T, D)).astype(np.float32) for _ in range(2))
+    g = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    dot = dump("residual_norm").replace("\\nf16 [", "\\nf32 [").replace('"f16 [', '"f32 [')
+    mem = dump("residual_norm", ".mem.txt").replace(" f16 ", " f32 ")
+    plan = bwpp.Plan(ctx, dot, mem, dict(T=T, D=D), f"fuse={fuse}")
+    assert all(v["dtype"] == "float32" for v in plan.values())
+    for key, arr in {"x": x, "r": r, "g": g}.items():
+        plan.bind(key, torch.from_numpy(arr).cuda())
+    plan.run()
+    ctx.sync()
+    (out,) = [plan.tensor(v["id"]).cpu().numpy() for v in plan.values() if v["output"]]
+    launches = plan.launches
+    plan.close()
+    ref = O.rmsnorm(x + r, g, None, 1e-5)
+    assert rel_fro(out, ref) <= 1e-5
+    assert launches == (1 if fuse else 2)
+
+
+@pytest.mark.parametrize("fuse", [1, 0])
 def test_attention_residual_norm_sum_stored(ctx, fuse):
     """h = x + attention(q, k, v); out = h + rmsnorm(h, g): the fused residual
     + norm stores h (read again by the last add), in the attention output's
