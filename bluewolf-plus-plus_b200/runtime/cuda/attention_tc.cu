@@ -57,6 +57,9 @@ struct Cfg {
   static constexpr uint32_t TMEM_S = 0;        // S_A at 0, S_B at 128
   static constexpr uint32_t TMEM_O = 2 * BN;   // O_A at 256, O_B at 256 + D
   static constexpr uint32_t TMEM_COLS = 512;
+  // split launches: per softmax warp, its O rows ([D/64][8][lane] float4)
+  // and one float4 (max a, max b, sum a, sum b) per lane
+  static constexpr int WARP_FLOATS = (D / 64) * 8 * 32 * 4 + 32 * 4;
   // Q, K, V and P are all bf16, or all f16 (the half ABI)
   static constexpr uint32_t IDESC_S = make_idesc_f32acc(BM, BN, 0, 0, F16 ? 1u : 0u);
   static constexpr uint32_t IDESC_PV = make_idesc_f32acc(BM, D, 0, 1, F16 ? 1u : 0u);
@@ -88,11 +91,38 @@ static_assert(sizeof(Bars) <= 512, "barrier block");
 struct Item {
   uint32_t bh, q0;
   int nblk[2], n;
+  uint32_t kb0;  // first key block (0 but in a split launch)
 };
 
+// Split tail of a non-causal launch whose last round of items would be at
+// most half full: the main launch takes the whole rounds, and a second,
+// split launch (the SPLIT instantiation of the kernel) runs each remaining
+// item as two halves over the key blocks [0, n/2) and [n/2, n), so that
+// round ends in half the time.  The two halves of an item merge through
+// global memory: every softmax warp of a half counts itself in on its
+// (item, warp) counter; the first to arrive stores its unnormalised O rows
+// and (max, sum) to the item's slot and counts them written; the second
+// waits for that (only for a half that has already arrived, so both need
+// not run at the same time), merges the two in half order and stores O.
+// The main launch's code is the kernel without any of this.
+struct AttnSplit {
+  uint32_t first;   // item index of split item 0
+  uint32_t epoch;   // tag of this launch's counts
+  float *partials;  // [split item][16 warps][WARP_FLOATS]
+  unsigned long long *counters;  // [split item][16 warps][arrived, written]
+};
+
+template <bool SPLIT>
 __device__ __forceinline__ Item decode_item(int w, uint32_t pairs, uint32_t BH, uint32_t group,
-                                            uint32_t Sq, uint32_t Skv, int causal) {
+                                            uint32_t Sq, uint32_t Skv, int causal,
+                                            const AttnSplit &sp) {
   Item it;
+  it.kb0 = 0;
+  uint32_t half = 0;
+  if constexpr (SPLIT) {  // work item w: half w & 1 of item first + w / 2
+    half = (uint32_t)w & 1u;
+    w = (int)(sp.first + ((uint32_t)w >> 1));
+  }
   const uint32_t per_group = group * pairs;
   const uint32_t g0 = (uint32_t)w / per_group * group;  // first head of w's group
   const uint32_t r = (uint32_t)w % per_group;
@@ -102,7 +132,125 @@ __device__ __forceinline__ Item decode_item(int w, uint32_t pairs, uint32_t BH, 
   it.nblk[0] = blocks_for(it.q0, Sq, Skv, causal);
   it.nblk[1] = blocks_for(it.q0 + BM, Sq, Skv, causal);
   it.n = max(it.nblk[0], it.nblk[1]);
+  if constexpr (SPLIT) {  // non-causal: a tile with rows sees all it.n blocks
+    const int h0 = it.n / 2;
+    const int cnt = half ? it.n - h0 : h0;
+    it.kb0 = half ? (uint32_t)h0 : 0u;
+    for (int X = 0; X < 2; ++X) it.nblk[X] = it.nblk[X] > 0 ? cnt : 0;
+    it.n = cnt;
+  }
   return it;
+}
+
+// Where a softmax thread's two rows of O live, for split_epilogue.
+struct SplitRows {
+  uint32_t o_col, bh, Sq, qa, qb;
+  int cpair, lane, warp;
+  float scale_log2;
+};
+
+// Epilogue of one softmax warp for half (w & 1) of split item w >> 1 (see
+// AttnSplit): the first half to arrive stores its unnormalised O rows and
+// (max, sum) and counts them written; the second merges the two and stores
+// O (and the log-sum-exp).  Weights, sums and the products' sum are rounded
+// in half order, so the result does not depend on which half came first.
+// False on a wait that ran out.
+template <int D, bool F16>
+__device__ __forceinline__ bool split_epilogue(const SplitRows &rw, const AttnIO &io,
+                                               const AttnSplit &sp, uint32_t w, float la,
+                                               float lb, float ma, float mb, int *status) {
+  constexpr int WF = (D / 64) * 8 * 32 * 4 + 32 * 4;
+  const int lane = rw.lane;
+  const bool h0 = (w & 1u) == 0;
+  float *slot = sp.partials + ((size_t)(w >> 1) * 16 + rw.warp) * WF;
+  unsigned long long *ctr = sp.counters + ((size_t)(w >> 1) * 16 + rw.warp) * 2;
+  uint32_t before = 0;
+  if (lane == 0) before = epoch_arrive(ctr, sp.epoch);
+  before = __shfl_sync(0xffffffffu, before, 0);
+  if (before == 0) {
+#pragma unroll 1
+    for (int c = 0; c < D / 64; ++c) {
+      uint32_t ro[32];
+      tmem_ld_16x256b_x8(rw.o_col + c * 64, ro);
+      tc_wait_ld(ro);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        __stcg(reinterpret_cast<float4 *>(slot + ((c * 8 + k) * 32 + lane) * 4),
+               make_float4(__uint_as_float(ro[4 * k]), __uint_as_float(ro[4 * k + 1]),
+                           __uint_as_float(ro[4 * k + 2]), __uint_as_float(ro[4 * k + 3])));
+    }
+    __stcg(reinterpret_cast<float4 *>(slot + ((D / 64) * 8 * 32 + lane) * 4),
+           make_float4(ma, mb, la, lb));
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) epoch_arrive(ctr + 1, sp.epoch);
+    return true;
+  }
+  bool okw = true;
+  if (lane == 0) okw = epoch_wait(ctr + 1, sp.epoch, 1, status);
+  if (!__shfl_sync(0xffffffffu, okw ? 1 : 0, 0)) return false;
+  __syncwarp();  // lane 0's acquire orders the whole warp's loads below
+  const float4 ml = __ldcg(reinterpret_cast<const float4 *>(slot + ((D / 64) * 8 * 32 + lane) * 4));
+  float wm[2], wo[2], l[2], m[2];
+  const float mine_m[2] = {ma, mb}, mine_l[2] = {la, lb}, oth_m[2] = {ml.x, ml.y},
+              oth_l[2] = {ml.z, ml.w};
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const float m0 = h0 ? mine_m[r] : oth_m[r], m1 = h0 ? oth_m[r] : mine_m[r];
+    const float l0 = h0 ? mine_l[r] : oth_l[r], l1 = h0 ? oth_l[r] : mine_l[r];
+    const float M = fmaxf(m0, m1);
+    const float e0 = m0 == -INFINITY ? 0.0f : fast_exp2((m0 - M) * rw.scale_log2);
+    const float e1 = m1 == -INFINITY ? 0.0f : fast_exp2((m1 - M) * rw.scale_log2);
+    wm[r] = h0 ? e0 : e1;
+    wo[r] = h0 ? e1 : e0;
+    m[r] = M;
+    l[r] = __fadd_rn(__fmul_rn(e0, l0), __fmul_rn(e1, l1));
+  }
+  const float inv_a = l[0] > 0.0f ? 1.0f / l[0] : 0.0f, inv_b = l[1] > 0.0f ? 1.0f / l[1] : 0.0f;
+  const bool va = rw.qa < rw.Sq, vb = rw.qb < rw.Sq;
+  if (io.lse && (lane & 3) == 0) {
+    if (va) io.lse[(size_t)rw.bh * rw.Sq + rw.qa] = l[0] > 0.0f ? m[0] * rw.scale_log2 + __log2f(l[0]) : -INFINITY;
+    if (vb) io.lse[(size_t)rw.bh * rw.Sq + rw.qb] = l[1] > 0.0f ? m[1] * rw.scale_log2 + __log2f(l[1]) : -INFINITY;
+  }
+#pragma unroll 1
+  for (int c = 0; c < D / 64; ++c) {
+    uint32_t ro[32];
+    tmem_ld_16x256b_x8(rw.o_col + c * 64, ro);
+    tc_wait_ld(ro);
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float4 t4 = __ldcg(reinterpret_cast<const float4 *>(slot + ((c * 8 + k) * 32 + lane) * 4));
+      const float ot[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = e >> 1;  // e < 2: row a, else row b
+        const float pm = __fmul_rn(__uint_as_float(ro[4 * k + e]), wm[r]);
+        const float po = __fmul_rn(ot[e], wo[r]);
+        v[4 * k + e] = (h0 ? __fadd_rn(pm, po) : __fadd_rn(po, pm)) * (r ? inv_b : inv_a);
+      }
+    }
+    if (io.out_f32) {
+      float *oa = io.out_f32 + ((size_t)rw.bh * rw.Sq + rw.qa) * D + c * 64 + rw.cpair;
+      float *ob = oa + 8 * (size_t)D;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (va) __stcs(reinterpret_cast<float2 *>(oa + 8 * k), make_float2(v[4 * k], v[4 * k + 1]));
+        if (vb) __stcs(reinterpret_cast<float2 *>(ob + 8 * k), make_float2(v[4 * k + 2], v[4 * k + 3]));
+      }
+    }
+    if (io.out_bf16) {
+      const size_t head_col = (size_t)(rw.bh % io.H) * D + c * 64 + rw.cpair;
+      uint16_t *oa = io.out_bf16 + ((size_t)(rw.bh / io.H) * rw.Sq + rw.qa) * io.ldo + head_col;
+      uint16_t *ob = oa + 8 * (size_t)io.ldo;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (va) *reinterpret_cast<uint32_t *>(oa + 8 * k) = pack2_16<F16>(v[4 * k], v[4 * k + 1]);
+        if (vb) *reinterpret_cast<uint32_t *>(ob + 8 * k) = pack2_16<F16>(v[4 * k + 2], v[4 * k + 3]);
+      }
+    }
+  }
+  return true;
 }
 
 // Persistent: one CTA per SM takes work items (256 query rows of one head)
@@ -117,21 +265,22 @@ __device__ __forceinline__ Item decode_item(int w, uint32_t pairs, uint32_t BH, 
 // S MMAs run while the softmax warps are still in the previous epilogue; its
 // first PV waits for that epilogue to read O (o_free).  All barrier phases
 // are running counters over the CTA's whole item sequence.
-template <int D, bool F16>
+template <int D, bool F16, bool SPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
                         const AttnIO io, uint32_t BH, uint32_t Sq,
                         uint32_t Skv, float scale_log2, int causal,
-                        uint32_t pairs, uint32_t group, int *sched, int *status) {
+                        uint32_t pairs, uint32_t group, uint32_t n_items, const AttnSplit sp,
+                        int *sched, int *status) {
   using C = Cfg<D, F16>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
   Bars *bar = reinterpret_cast<Bars *>(smem + C::OFF_BAR);
   volatile int *abort_flag = &bar->abort_flag;
-  const int total = (int)(pairs * BH);
+  const int total = (int)n_items;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -178,7 +327,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         bar->item[slot] = w < total ? w : -1;
         mbar_arrive(&bar->sched_full[slot]);
         if (w >= total) break;
-        const Item it = decode_item(w, pairs, BH, group, Sq, Skv, causal);
+        const Item it = decode_item<SPLIT>(w, pairs, BH, group, Sq, Skv, causal, sp);
         // K(0) first (its slot frees with the previous item's last S MMAs),
         // then both Q tiles.  Every item has at least one block (its first
         // row is below Sq and Skv >= 1).
@@ -186,7 +335,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int s = kc & 1;
           if (!mbar_wait(&bar->k_empty[s], ((kc >> 1) & 1) ^ 1, status)) { ok = false; break; }
           mbar_arrive_expect_tx(&bar->k_full[s], C::TILE);
-          load_rows<C::BOXES>(smem + C::OFF_K + s * C::TILE, &tmK, &bar->k_full[s], io, it.bh, Skv, 0);
+          load_rows<C::BOXES>(smem + C::OFF_K + s * C::TILE, &tmK, &bar->k_full[s], io, it.bh, Skv,
+                              it.kb0 * BN);
           ++kc;
         }
         for (int X = 0; X < 2 && ok; ++X) {
@@ -201,14 +351,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!mbar_wait(&bar->k_empty[s], ((kc >> 1) & 1) ^ 1, status)) { ok = false; break; }
             mbar_arrive_expect_tx(&bar->k_full[s], C::TILE);
             load_rows<C::BOXES>(smem + C::OFF_K + s * C::TILE, &tmK, &bar->k_full[s], io, it.bh,
-                                Skv, (j + 1) * BN);
+                                Skv, (it.kb0 + j + 1) * BN);
             ++kc;
           }
           const int vs = vc & 1;
           if (!mbar_wait(&bar->v_empty[vs], ((vc >> 1) & 1) ^ 1, status)) { ok = false; break; }
           mbar_arrive_expect_tx(&bar->v_full[vs], C::TILE);
           load_rows<C::BOXES>(smem + C::OFF_V + vs * C::TILE, &tmV, &bar->v_full[vs], io, it.bh, Skv,
-                              j * BN);
+                              (it.kb0 + j) * BN);
           ++vc;
         }
         w = (int)gridDim.x + atomicAdd(sched, 1);
@@ -261,7 +411,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int w = bar->item[slot];
         mbar_arrive(&bar->sched_empty[slot]);
         if (w < 0) break;
-        const Item it = decode_item(w, pairs, BH, group, Sq, Skv, causal);
+        const Item it = decode_item<SPLIT>(w, pairs, BH, group, Sq, Skv, causal, sp);
         {
           // block 0: S_A(0), S_B(0)
           ok = mbar_wait(&bar->k_full[kc & 1], (kc >> 1) & 1, status);
@@ -359,12 +509,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->sched_empty[slot]);
       if (w < 0) break;
-      const Item it = decode_item(w, pairs, BH, group, Sq, Skv, causal);
+      const Item it = decode_item<SPLIT>(w, pairs, BH, group, Sq, Skv, causal, sp);
       const uint32_t bh = it.bh;
       const uint32_t qa = it.q0 + X * BM + ra, qb = qa + 8;  // query indices
-      // last visible key of each row
-      const uint32_t lim_a = causal && qa < Skv - 1 ? qa : Skv - 1;
-      const uint32_t lim_b = causal && qb < Skv - 1 ? qb : Skv - 1;
+      // last visible key of each row, counted from the item's first key
+      // block (a split item's second half starts at it.kb0 and always holds
+      // a visible key, so the difference stays non-negative)
+      const uint32_t lim_a = (causal && qa < Skv - 1 ? qa : Skv - 1) - it.kb0 * BN;
+      const uint32_t lim_b = (causal && qb < Skv - 1 ? qb : Skv - 1) - it.kb0 * BN;
       const int nb = it.nblk[X];
       float m_a = -INFINITY, m_b = -INFINITY;  // reference maxima (scaled units)
       float l_a = 0.0f, l_b = 0.0f;            // this thread's share of the row sums
@@ -481,7 +633,19 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (!ok) break;
       // epilogue: O / l -> global, then hand O_X back to the MMA warp
-      if (nb > 0) {
+      if constexpr (SPLIT) {
+        if (nb > 0) {
+          pvc += (uint32_t)nb;
+          if (!mbar_wait(&bar->pv_done[X], (pvc - 1) & 1, status)) { ok = false; break; }
+          tc_fence_after();
+          const SplitRows rw{o_col, bh, Sq, qa, qb, cpair, lane, warp, scale_log2};
+          if (!split_epilogue<D, F16>(rw, io, sp, (uint32_t)w, quad_sum(l_a), quad_sum(l_b), m_a,
+                                      m_b, status)) {
+            ok = false;
+            break;
+          }
+        }
+      } else if (nb > 0) {
         pvc += (uint32_t)nb;
         if (!mbar_wait(&bar->pv_done[X], (pvc - 1) & 1, status)) { ok = false; break; }
         tc_fence_after();
@@ -570,7 +734,22 @@ int make_tmap_3d(BwppCudaCtx *ctx, CUtensorMap *map, const void *base, uint32_t 
   return BWPP_CUDA_OK;
 }
 
-bool g_attr_set[4][64] = {};
+bool g_attr_set[8][64] = {};
+
+template <int D, bool F16, bool SPLIT>
+int set_smem_attr(BwppCudaCtx *ctx) {
+  const int di = (D == 128 ? 1 : 0) + (F16 ? 2 : 0) + (SPLIT ? 4 : 0);
+  if (ctx->device < 64 && !g_attr_set[di][ctx->device]) {
+    const int rc = bwpp_check_cuda(ctx,
+                                   cudaFuncSetAttribute(attention_tc_kernel<D, F16, SPLIT>,
+                                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        Cfg<D, F16>::SMEM),
+                                   "attention smem attribute");
+    if (rc) return rc;
+    g_attr_set[di][ctx->device] = true;
+  }
+  return BWPP_CUDA_OK;
+}
 
 template <int D, bool F16 = false>
 int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_t *v,
@@ -580,17 +759,8 @@ int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_
   int rc = make_tmap_3d(ctx, &tq, q, D, Sq, BH, H, ld_in, F16);
   if (!rc) rc = make_tmap_3d(ctx, &tk, k, D, Skv, BH, H, ld_in, F16);
   if (!rc) rc = make_tmap_3d(ctx, &tv, v, D, Skv, BH, H, ld_in, F16);
+  if (!rc) rc = set_smem_attr<D, F16, false>(ctx);
   if (rc) return rc;
-  const int di = (D == 128 ? 1 : 0) + (F16 ? 2 : 0);
-  if (ctx->device < 64 && !g_attr_set[di][ctx->device]) {
-    rc = bwpp_check_cuda(ctx,
-                         cudaFuncSetAttribute(attention_tc_kernel<D, F16>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              Cfg<D, F16>::SMEM),
-                         "attention smem attribute");
-    if (rc) return rc;
-    g_attr_set[di][ctx->device] = true;
-  }
   const uint32_t pairs = (Sq + 2 * BM - 1) / (2 * BM);
   const uint64_t items = (uint64_t)pairs * BH;
   if (items > 0x7fffffffull)
@@ -607,13 +777,46 @@ int launch(BwppCudaCtx *ctx, const uint16_t *q, const uint16_t *k, const uint16_
   const uint32_t group =
       causal ? (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(BH, (32ull << 20) / kv_head))
              : 1u;
+  // Non-causal items are alike: a last round at most half full runs as a
+  // second, split launch (AttnSplit) after the whole rounds
+  AttnSplit sp{};
+  uint64_t whole = items;
+  {
+    const uint64_t rem = items % grid;
+    const uint32_t nkv = (Skv + BN - 1) / BN;
+    float *parts = nullptr;
+    size_t part_floats = 0, ncounters = 0;
+    unsigned long long *counters = nullptr;
+    uint32_t epoch = 0;
+    if (!causal && grid == (uint64_t)ctx->num_sms && rem > 0 && 2 * rem <= grid && nkv >= 2 &&
+        set_smem_attr<D, F16, true>(ctx) == BWPP_CUDA_OK &&
+        bwpp_split_scratch(ctx, &parts, &part_floats, &counters, &ncounters, &epoch) &&
+        rem * 16 * (uint64_t)Cfg<D, F16>::WARP_FLOATS <= part_floats && rem * 16 * 2 <= ncounters) {
+      whole = items - rem;
+      sp.first = (uint32_t)whole;
+      sp.epoch = epoch;
+      sp.partials = parts;
+      sp.counters = counters;
+    }
+  }
   rc = bwpp_check_cuda(ctx, cudaMemsetAsync(ctx->sched_counter, 0, sizeof(int), ctx->stream),
                        "attention work counter");
   if (rc) return rc;
-  attention_tc_kernel<D, F16><<<(unsigned)grid, THREADS, Cfg<D, F16>::SMEM, ctx->stream>>>(
+  attention_tc_kernel<D, F16, false><<<(unsigned)grid, THREADS, Cfg<D, F16>::SMEM, ctx->stream>>>(
       tq, tk, tv, io, BH, Sq, Skv, scale * 1.4426950408889634f, causal, pairs, group,
-      ctx->sched_counter, ctx->status_word);
+      (uint32_t)whole, sp, ctx->sched_counter, ctx->status_word);
   BWPP_LAUNCH_CHECK(ctx, "attention tcgen05");
+  if (whole < items) {
+    const uint32_t halves = (uint32_t)(2 * (items - whole));
+    rc = bwpp_check_cuda(ctx, cudaMemsetAsync(ctx->sched_counter, 0, sizeof(int), ctx->stream),
+                         "attention work counter");
+    if (rc) return rc;
+    const unsigned g2 = halves < (uint32_t)ctx->num_sms ? halves : (unsigned)ctx->num_sms;
+    attention_tc_kernel<D, F16, true><<<g2, THREADS, Cfg<D, F16>::SMEM, ctx->stream>>>(
+        tq, tk, tv, io, BH, Sq, Skv, scale * 1.4426950408889634f, causal, pairs, group, halves, sp,
+        ctx->sched_counter, ctx->status_word);
+    BWPP_LAUNCH_CHECK(ctx, "attention tcgen05 split tail");
+  }
   return BWPP_CUDA_OK;
 }
 

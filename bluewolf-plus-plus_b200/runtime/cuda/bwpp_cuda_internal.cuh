@@ -40,6 +40,11 @@ struct BwppCudaCtx {
   char last_error[256];
 };
 
+// Split-work scratch of ctx (gemm.cu): fp32 partials and epoch-tagged
+// counters shared by kernels that cut their last work items in two.
+bool bwpp_split_scratch(BwppCudaCtx *ctx, float **partials, size_t *partial_floats,
+                        unsigned long long **counters, size_t *ncounters, uint32_t *epoch);
+
 // Records a message in ctx->last_error (if ctx) and returns `code`.
 int bwpp_set_error(BwppCudaCtx *ctx, int code, const char *fmt, ...);
 

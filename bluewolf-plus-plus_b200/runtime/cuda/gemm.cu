@@ -1185,3 +1185,20 @@ int bwpp_cuda_cast_f32_bf16(BwppCudaCtx *ctx, const float *src, uint16_t *dst,
 }
 
 }  // extern "C"
+
+// The split-work scratch of ctx (the GEMM's split-tail partials and epoch
+// counters), for other kernels that cut a launch's last work items in two:
+// false when the caller owns the workspace or the allocation failed.  The
+// launch gets a fresh epoch tag; its counts from earlier launches read as 0.
+bool bwpp_split_scratch(BwppCudaCtx *ctx, float **partials, size_t *partial_floats,
+                        unsigned long long **counters, size_t *ncounters, uint32_t *epoch) {
+  if (!gemm_scratch(ctx)) return false;
+  const size_t slots = 2 * (size_t)ctx->num_sms;
+  *partials = ctx->gemm_partials;
+  *partial_floats = slots * BM * BN;
+  *counters = ctx->gemm_counters;
+  *ncounters = slots * 2 * EPI_WARPS * 2;
+  *epoch = ++ctx->gemm_epoch;
+  if (*epoch == 0) *epoch = ++ctx->gemm_epoch;  // 0 is the counters' initial tag
+  return true;
+}

@@ -82,3 +82,49 @@ def test_config4_sampled_rows(ctx):
         err = rel_fro(got, ref)
         assert err <= TOL and err <= TIGHT, (causal, err)
 
+
+
+# Non-causal launches whose last round of items (256 query rows of one head
+# each, one CTA per SM) would be at most half full run those items in a second
+# launch, as two halves over the key blocks merged in global memory: 160 items
+# leave 12 for it.  Checked against the oracle, with ragged Sq / Skv (the
+# second half holds the masked key edge) and in the half ABI, run to run
+# bit-identical (the merge is in half order), and against the same heads in a
+# launch of exactly 148 items (no split).
+SPLIT_SHAPES = [(40, 1024, 1024, 128), (40, 1000, 777, 128), (40, 1024, 1024, 64)]
+
+
+@pytest.mark.parametrize("BH,Sq,Skv,D", SPLIT_SHAPES)
+def test_attention_split_tail(ctx, BH, Sq, Skv, D):
+    pairs = -(-Sq // 256)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    if not (pairs * BH > sms and 0 < (pairs * BH) % sms <= sms // 2):
+        pytest.skip(f"{pairs * BH} items leave no split tail on {sms} SMs")
+    rng = np.random.default_rng(Sq + Skv + D)
+    q16, k16, v16 = qkv(rng, 1, BH, Sq, Skv, D)
+    scale = 1.0 / np.sqrt(D)
+    out = run(ctx, q16, k16, v16, 1, BH, Sq, Skv, D, scale, 0)
+    again = run(ctx, q16, k16, v16, 1, BH, Sq, Skv, D, scale, 0)
+    assert np.array_equal(out.view(np.uint32), again.view(np.uint32))
+    ref = O.attention_bhsd(*(O.bf16_to_f32(t) for t in (q16, k16, v16)), scale, 0)
+    err = rel_fro(out, ref)
+    assert err <= TOL and err <= TIGHT, err
+    # the halves round P to bf16 against their own running maxima, so a
+    # launch without the split agrees to about bf16 over the key sum
+    nh = sms // pairs
+    tail = run(ctx, q16[:, -nh:], k16[:, -nh:], v16[:, -nh:], 1, nh, Sq, Skv, D, scale, 0)
+    assert rel_fro(out[:, -nh:], tail) <= 1e-3
+
+
+def test_attention_split_tail_half_abi(ctx):
+    """The half ABI (f16 in, f16 out) through the same split tail."""
+    BH, S, D = 40, 1024, 128
+    rng = np.random.default_rng(77)
+    q, k, v = (rng.standard_normal((BH, S, D)).astype(np.float16) for _ in range(3))
+    qd, kd, vd = (torch.from_numpy(t).cuda() for t in (q, k, v))
+    od = torch.empty(BH, S, D, dtype=torch.float16, device="cuda")
+    ctx.attention_f16(qd, kd, vd, od, 1, BH, S, S, D, 1.0 / np.sqrt(D), 0)
+    ctx.sync()
+    ref = O.attention_bhsd(q.astype(np.float32)[None], k.astype(np.float32)[None],
+                           v.astype(np.float32)[None], 1.0 / np.sqrt(D), 0)[0]
+    assert rel_fro(od.float().cpu().numpy(), ref) <= TOL
