@@ -300,11 +300,18 @@ class AttentionWorkload(Workload):
         self.q, self.k, self.v = (t.randn(self.nh, self.S, self.D, device="cuda", generator=g).to(t.bfloat16)
                                   for _ in range(3))
         self.o = t.empty(self.nh, self.S, self.D, device="cuda")
+        # kernels per call: a non-causal launch whose last round of items (256
+        # query rows of one head, one CTA per SM) is at most half full runs
+        # that round as a second, split launch (attention_tc.cu)
+        sms = t.cuda.get_device_properties(t.cuda.current_device()).multi_processor_count
+        items = -(-self.S // 256) * self.nh
+        self.kernels = 2 if (not self.causal and items > sms and 0 < items % sms <= sms // 2
+                             and -(-self.S // 128) >= 2) else 1
 
     def step(self):
         self.ctx.attention_bf16(self.q, self.k, self.v, self.o, 1, self.nh, self.S, self.S, self.D,
                                 self.D ** -0.5, int(self.causal))
-        return 1
+        return self.kernels
 
     def flops_per_head(self):
         S, D = self.S, self.D
