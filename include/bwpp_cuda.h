@@ -110,8 +110,9 @@ int bwpp_cuda_ctx_set_stream(BwppCudaCtx *ctx, void *stream);
  * scratch.  (Without one, the first tensor-core GEMM whose last round is cut
  * into K parts allocates a fixed split-tail scratch, 2 x SM count tiles of
  * 128 x 256 fp32, about 38 MB on a B200, kept until the context is
- * destroyed; with one set beforehand, GEMMs run that round as whole tiles
- * or N halves instead.) */
+ * destroyed, which non-causal attention also uses for a half-empty last
+ * round of its items; with one set beforehand, GEMMs run that round as
+ * whole tiles or N halves and attention runs it whole instead.) */
 int bwpp_cuda_ctx_set_workspace(BwppCudaCtx *ctx, void *device_ptr,
                                 size_t bytes);
 /* Copies `bytes` between any two host / device buffers (e.g. filling arena
