@@ -1012,34 +1012,47 @@ def cpu_baseline_of(wl, repeats=3):
 
 
 def run_suite(names, args, rank, world, torch, bwpp, ctx, flush, barrier, dist):
+    """Each workload in turn, released before the next.  A workload that fails
+    is reported as {"error": ...} and ends the suite, so the headline line is
+    still printed (every rank runs the same steps, so a failure that is not
+    rank-local stops all ranks at the same point)."""
     out = {}
     for name in names:
-        wl = make_workload(name, rank, world, torch, bwpp, ctx)
-        if args.rows and isinstance(wl, RowWorkload):
-            wl.R = args.rows
-        wl.setup()
-        total_s, my_s, launches, _ = time_steps(wl, args.steps, args.warmup, torch, ctx, flush,
-                                                barrier, dist)
-        entry = {"value": wl.scale(wl.total_work_per_step() * args.steps, total_s), "unit": wl.unit,
-                 "ms_per_step": 1e3 * total_s / args.steps, "scaling": getattr(wl, "scaling", "strong"),
-                 "dtype": wl.dtype, "gpu_launches": launches, "roofline": roofline_of(wl, my_s),
-                 "config": wl.config()}
-        if hasattr(wl, "dp_check"):
-            entry["dp_check"] = wl.dp_check()
-        if rank == 0 and world == 1 and not args.no_cpu:
-            entry["cpu_baseline"] = cpu_baseline_of(wl)
-        if getattr(wl, "comm", None):
-            torch.cuda.synchronize()
-            bwpp.load().bwpp_cuda_comm_destroy(wl.comm)
-            wl.comm = None
-        if hasattr(wl, "model"):
-            wl.model.close()
-        out[name] = entry
-        del wl
-        torch.cuda.synchronize()
-        torch.cuda.empty_cache()
-        barrier()
+        try:
+            out[name] = run_workload(name, args, rank, world, torch, bwpp, ctx, flush, barrier, dist)
+        except Exception as e:  # noqa: BLE001 - reported in the JSON line
+            out[name] = {"error": f"{type(e).__name__}: {e}"[:400]}
+            print(f"bench: workload {name} failed: {e}", file=sys.stderr, flush=True)
+            break
     return out
+
+
+def run_workload(name, args, rank, world, torch, bwpp, ctx, flush, barrier, dist):
+    wl = make_workload(name, rank, world, torch, bwpp, ctx)
+    if args.rows and isinstance(wl, RowWorkload):
+        wl.R = args.rows
+    wl.setup()
+    total_s, my_s, launches, _ = time_steps(wl, args.steps, args.warmup, torch, ctx, flush,
+                                            barrier, dist)
+    entry = {"value": wl.scale(wl.total_work_per_step() * args.steps, total_s), "unit": wl.unit,
+             "ms_per_step": 1e3 * total_s / args.steps, "scaling": getattr(wl, "scaling", "strong"),
+             "dtype": wl.dtype, "gpu_launches": launches, "roofline": roofline_of(wl, my_s),
+             "config": wl.config()}
+    if hasattr(wl, "dp_check"):
+        entry["dp_check"] = wl.dp_check()
+    if rank == 0 and world == 1 and not args.no_cpu:
+        entry["cpu_baseline"] = cpu_baseline_of(wl)
+    if getattr(wl, "comm", None):
+        torch.cuda.synchronize()
+        bwpp.load().bwpp_cuda_comm_destroy(wl.comm)
+        wl.comm = None
+    if hasattr(wl, "model"):
+        wl.model.close()
+    del wl
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    barrier()
+    return entry
 
 
 def main():

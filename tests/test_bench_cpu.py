@@ -81,3 +81,23 @@ def test_reference_arm_default_reports_the_suite():
     assert w["attention_causal"]["unit"] == "TFLOP/s"
     assert w["rmsnorm_fwd"]["cpu_baseline"]["repeats"] == 3
     assert "unavailable" in w["tiny_model"] and "unavailable" in w["layernorm_bwd"]
+
+
+def test_a_failing_workload_is_reported_and_ends_the_suite(monkeypatch):
+    """A workload that raises is reported as {"error": ...}; the suite stops
+    there, so the headline JSON line is still printed."""
+    ran = []
+
+    def fake(name, *a, **k):
+        ran.append(name)
+        if name == "rmsnorm_fwd":
+            raise RuntimeError("boom")
+        return {"value": 1.0}
+
+    monkeypatch.setattr(bench, "run_workload", fake)
+    out = bench.run_suite(["attention", "rmsnorm_fwd", "softmax_fwd"], None, 0, 1, None, None, None,
+                          None, None, None)
+    assert ran == ["attention", "rmsnorm_fwd"]
+    assert out["attention"] == {"value": 1.0}
+    assert out["rmsnorm_fwd"]["error"].startswith("RuntimeError: boom")
+    assert "softmax_fwd" not in out
